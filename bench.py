@@ -1,0 +1,361 @@
+#!/usr/bin/env python
+"""Benchmark of the INT8 decode step on B200.
+
+Workload: Qwen3-ASR-0.6B decoder shapes (hidden
+1024, intermediate 3072, 28 layers, 16/8 heads x 128, vocab 151936), random
+N(0, 0.02) weights quantised per output channel to INT8, f32 embedding
+table, M independent sequences (default 8) each at KV length 1024.  One
+step = one greedy decode step of all M sequences: embedding gather, 28
+layers, final norm, lm head, argmax.  Metric: decode tokens/s (whole job).
+
+Data-parallel over GPUs with no collective on the data path: each rank runs
+its own M sequences on its own weight replica (weak scaling); the only
+collectives are the timing barrier and the max-over-ranks of the timings.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch M] [--impl ours|reference]
+
+Prints one JSON line on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode tokens/s (INT8 decode step, Qwen3-ASR-0.6B decoder shapes)"
+UNIT = "tokens/s"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--batch", type=int, default=8)
+    ap.add_argument("--kv-len", type=int, default=1024)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0, help="bounded CPU-baseline sample length")
+    ap.add_argument("--seed", type=int, default=1234)
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------------ clocks --
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML every few ms."""
+
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+               0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+    def __init__(self, index):
+        self.samples, self.reasons = [], 0
+        self.ok = False
+        self.max_mhz = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            pass
+        self._stop = threading.Event()
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                self.reasons |= int(self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h))
+            except Exception:
+                pass
+            time.sleep(0.002)
+
+    def __enter__(self):
+        if self.ok:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        if self.ok:
+            self._stop.set()
+            self.t.join()
+
+    def summary(self):
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"], "samples": 0}
+        names = [n for b, n in self.REASONS.items() if self.reasons & b and n != "gpu_idle"]
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+                "reasons": names, "samples": len(self.samples)}
+
+
+# --------------------------------------------------------- byte accounting --
+def class_bytes(cfg, M, kv_len):
+    """Algorithmic bytes per launch of each kernel class of the step (weights,
+    scales, activations in/out, K/V rows read)."""
+    H, I, hd = cfg["hidden"], cfg["inter"], cfg["head_dim"]
+    q, kv = cfg["n_heads"] * hd, cfg["n_kv_heads"] * hd
+    f = 4
+    return {
+        "embed": M * H * f * 2,
+        "norm": M * H * f * 2 + H * f,
+        "qkv": (q + 2 * kv) * H + (q + 2 * kv) * f + M * H * f + M * (q + 2 * kv) * f,
+        "qkv_post": M * (q + 2 * kv) * f * 2 + 2 * hd * f,
+        "attn": M * 2 * kv_len * kv * f + 2 * M * q * f,
+        "oproj": H * q + H * f + M * q * f + 2 * M * H * f,
+        "gateup": 2 * I * H + 2 * I * f + M * H * f + M * I * f,
+        "down": H * I + H * f + M * I * f + 2 * M * H * f,
+        "lmhead": cfg["vocab"] * H + cfg["vocab"] * f + M * H * f,
+    }
+
+
+# ---------------------------------------------------------- CPU baseline ----
+_CPU_STATE = {}
+
+
+def cpu_decoder(cfg, seed):
+    if "dec" not in _CPU_STATE:
+        from oracle import pyoracle
+        from qwenasr_b200 import synthetic
+        w = synthetic.decoder_weights_np(cfg, seed)
+        _CPU_STATE["w"] = w
+        _CPU_STATE["dec"] = pyoracle.OracleDecoder(w)
+        _CPU_STATE["orc"] = pyoracle
+    return _CPU_STATE["dec"], _CPU_STATE["w"], _CPU_STATE["orc"]
+
+
+def cpu_time_tokens(cfg, kv_len, n_tokens, seed, threads):
+    """decoder_forward_int8 of the oracle on the host: n_tokens single-sequence
+    steps at position kv_len-1.  Returns seconds per token."""
+    dec, w, orc = cpu_decoder(cfg, seed)
+    orc.set_threads(threads)
+    if "kv" not in _CPU_STATE:
+        k, v = dec.new_kv(kv_len)
+        rng = np.random.default_rng(seed + 1)
+        k[:, :kv_len - 1] = rng.standard_normal((k.shape[0], kv_len - 1, k.shape[2]), np.float32)
+        v[:, :kv_len - 1] = rng.standard_normal((v.shape[0], kv_len - 1, v.shape[2]), np.float32)
+        _CPU_STATE["kv"] = (k, v)
+    k, v = _CPU_STATE["kv"]
+    tok = 17
+    t0 = time.perf_counter()
+    for _ in range(n_tokens):
+        tok, _, _ = dec.forward(k, v, kv_len - 1, w["embed"][tok])
+    return (time.perf_counter() - t0) / n_tokens
+
+
+def cpu_threads():
+    return max(1, min(16, os.cpu_count() or 1))  # the reference pool caps at MAX_THREADS = 16 (mod.rs:177)
+
+
+def cpu_baseline(cfg, kv_len, seed, seconds):
+    th = cpu_threads()
+    per = cpu_time_tokens(cfg, kv_len, 1, seed, th)  # warm-up + estimate
+    n = max(2, int(seconds / max(per, 1e-3)))
+    per = cpu_time_tokens(cfg, kv_len, n, seed, th)
+    return {"value": 1.0 / per, "unit": UNIT, "cores": th, "kind": "port",
+            "sample": f"{n} single-sequence decode steps of the oracle restatement at KV length {kv_len} "
+                      f"(0.6B shapes, 28 layers, 151936-row lm head), {th} threads of {os.cpu_count()} host cores"}
+
+
+# ------------------------------------------------------------- reference ----
+def run_reference(a):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from qwenasr_b200 import synthetic
+    cfg = synthetic.DEC_0_6B
+    th = cpu_threads()
+    est = cpu_time_tokens(cfg, a.kv_len, 1, a.seed, th)
+    # one step = the M sequences decoded one after another (the reference has
+    # no batching); shrink to fewer sequences per step when K steps of the full
+    # batch would not finish within ~3 minutes
+    per_step_seqs = a.batch
+    budget = 180.0
+    while per_step_seqs > 1 and est * per_step_seqs * (a.steps + a.warmup) > budget:
+        per_step_seqs -= 1
+    for _ in range(a.warmup):
+        cpu_time_tokens(cfg, a.kv_len, per_step_seqs, a.seed, th)
+    times = [cpu_time_tokens(cfg, a.kv_len, per_step_seqs, a.seed, th) * per_step_seqs for _ in range(a.steps)]
+    step_s = sum(times) / len(times)
+    value = per_step_seqs / step_s
+    sample = (f"{per_step_seqs} of {a.batch} sequences per step, decoded sequentially like transcribe_segment; "
+              f"oracle restatement of decoder_forward_int8 on {th} threads of {os.cpu_count()} host cores")
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
+            "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8xf32", "data": "synthetic (seeded random-init weights, random KV history)",
+            "impl": "reference",
+            "config": {"workload": "INT8 decode step, 0.6B decoder shapes", "batch_per_gpu": a.batch,
+                       "kv_len": a.kv_len, "parallelism": f"replicas x{a.gpus}"},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": th, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------- ours ----
+def run_ours(a):
+    import torch
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device(f"cuda:{local}"))
+    from qwenasr_b200 import kernels as K
+    from qwenasr_b200 import synthetic
+    from qwenasr_b200.decoder import Decoder
+
+    cfg = synthetic.DEC_0_6B
+    M, L = a.batch, a.kv_len
+    dev = torch.device(f"cuda:{local}")
+    dec = Decoder(cfg, device=local, max_batch=M, max_seq=L)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(a.seed)
+
+    def qz(w):
+        q = torch.empty(w.shape, dtype=torch.int8, device=dev)
+        s = torch.empty(w.shape[0], dtype=torch.float32, device=dev)
+        K.quantize_f32_to_int8(w, w.shape[0], w.shape[1], q, s)
+        return q, s
+
+    for i in range(cfg["n_layers"]):
+        dec.set_layer(i, synthetic.layer_weights_gpu(cfg, gen, dev, qz))
+    emb = torch.randn(cfg["vocab"], cfg["hidden"], generator=gen, device=dev) * 0.02
+    lm, lms = qz(emb)
+    norm = 1.0 + 0.02 * torch.randn(cfg["hidden"], generator=gen, device=dev)
+    dec.set_globals(emb, norm, lm, lms)
+    del lm, lms
+    for m in range(M):
+        k, v = dec.kv(m)
+        k[:, :L - 1].normal_(generator=gen)
+        v[:, :L - 1].normal_(generator=gen)
+    torch.cuda.synchronize()
+
+    tokens0 = torch.randint(0, cfg["vocab"], (M,), generator=gen, device=dev, dtype=torch.int32)
+    positions = torch.full((M,), L - 1, dtype=torch.int32, device=dev)
+    tok = tokens0.clone()
+    st = dec.stream
+    for _ in range(max(a.warmup, 3)):
+        dec.step_device(tok, positions, tok)
+    st.synchronize()
+
+    def barrier():
+        if dist:
+            dist.barrier()
+
+    # ---- device-timed region: K steps, inputs resident, tokens fed back ----
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        ev0.record(st)
+        for _ in range(a.steps):
+            dec.step_device(tok, positions, tok)
+        ev1.record(st)
+        st.synchronize()
+    torch.cuda.synchronize()
+    barrier()
+    ms = ev0.elapsed_time(ev1) / a.steps
+    ms_t = torch.tensor([ms], device=dev)
+    if dist:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms = float(ms_t.item())
+
+    # ---- e2e: the public host-buffer API, H2D ids+positions, D2H next ids ----
+    host_tok = tokens0.cpu().numpy()
+    host_pos = positions.cpu().numpy()
+    for _ in range(max(a.warmup, 3)):
+        host_tok = dec.step(host_tok, host_pos)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        host_tok = dec.step(host_tok, host_pos)
+    e2e_s = (time.perf_counter() - t0) / a.steps
+    barrier()
+    e2e_t = torch.tensor([e2e_s], device=dev)
+    if dist:
+        dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
+    e2e_s = float(e2e_t.item())
+
+    # ---- live per-class kernel timing (eager step with events) ----
+    prof = None
+    for _ in range(3):
+        prof = dec.profile_step(host_tok, host_pos)
+    cb = class_bytes(cfg, M, L)
+    dom = max(prof, key=lambda k: prof[k][0])
+    dom_ms, dom_n = prof[dom]
+    per_launch_s = dom_ms / 1e3 / dom_n
+    peak, peak_kind = peaks()
+    achieved = cb[dom] / per_launch_s / 1e9
+    launches_per_step = sum(n for _, n in prof.values())
+    step_bytes = dec.step_bytes(host_pos)
+
+    line = None
+    if rank == 0:
+        value = world * M / (ms / 1e3)
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8xf32",
+            "data": "synthetic (seeded random-init weights, random KV history)",
+            "config": {"workload": "INT8 decode step, Qwen3-ASR-0.6B decoder shapes (BASELINE configs[2])",
+                       "batch_per_gpu": M, "kv_len": L, "layers": cfg["n_layers"], "vocab": cfg["vocab"],
+                       "parallelism": f"replicas x{world} (no collective)",
+                       "l2": f"inputs larger than L2: {step_bytes / 1e9:.2f} GB read per step"},
+            "e2e": {"value": world * M / e2e_s, "unit": UNIT, "h2d_bytes_per_step": 2 * 4 * M,
+                    "d2h_bytes_per_step": 4 * M + 4},
+            "gpu_launches": launches_per_step * a.steps,
+            "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None, "peak_kind": peak_kind,
+                         "bytes_per_launch": cb[dom], "us_per_launch": per_launch_s * 1e6},
+            "step_roofline": {"bytes": step_bytes, "achieved_gbs": step_bytes / (ms / 1e3) / 1e9,
+                              "frac": step_bytes / (ms / 1e3) / 1e9 / peak},
+            "kernel_ms_per_step": {k: round(v[0], 4) for k, v in prof.items()},
+            "clocks": clk.summary(),
+        }
+    if dist:
+        dist.barrier()
+    dec.close()
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(cfg, L, a.seed, a.cpu_seconds)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    a = parse()
+    if a.impl == "reference":
+        return run_reference(a)
+    return run_ours(a)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,293 @@
+/*
+ * qwenasr_cuda.h -- C ABI of the B200 (sm_100a) kernel library for the
+ * QwenASR per-layer hot path.
+ *
+ * Two layers of entry points:
+ *
+ *  1. Kernel level.  One function per function of the reference's kernel
+ *     module (crates/qwen-asr/src/kernels/mod.rs), same argument order and
+ *     meaning, with device pointers and an explicit CUDA stream appended
+ *     (`stream` is a cudaStream_t; NULL = the legacy default stream).  The
+ *     reference functions mutate slices in place where these do, and return
+ *     nothing; here every function returns a status (QASR_OK or a negative
+ *     QASR_ERR_*), with a message in qasr_last_error().  Fused entries
+ *     (qasr_pre_attn_block, qasr_ln_pe, ...) replace a sequence of reference
+ *     calls and name the sequence.
+ *
+ *  2. Decoder engine.  An opaque qasr_decoder owning INT8 decoder weights on
+ *     one GPU, KV caches for a batch of independent sequences and the
+ *     captured decode-step graph: the device counterpart of DecoderInt8 +
+ *     KvCache + RopeCache + decoder_forward_int8 (crates/qwen-asr/src/
+ *     decoder.rs:130-306, 652-965), driven by QwenCtx::decoder_forward_token
+ *     (context.rs:311) in the reference.
+ *
+ * Layouts are the reference's: row-major f32 activations [rows, cols]; INT8
+ * weights row-major [out, in] with f32 per-row scales [out]
+ * (quantize.rs:78-84); the fused gate/up weight with rows interleaved
+ * g0,u0,g1,u1,... (decoder.rs:699-719); KV cache per sequence
+ * [n_layers, max_seq, kv_dim] f32 with row (layer*max_seq + pos)
+ * (decoder.rs:194-202); RoPE tables [pos, head_dim] with duplicated halves
+ * (decoder.rs:253-289).
+ *
+ * Thread safety: entry points may be called from several host threads on
+ * distinct streams/engines; one qasr_decoder must not be driven from two
+ * threads at once.
+ */
+#ifndef QWENASR_CUDA_H
+#define QWENASR_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* The library is built with hidden default visibility; everything declared
+ * here is exported. */
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+#define QASR_OK 0
+#define QASR_ERR_INVALID (-1)     /* null pointer, bad shape or out-of-range id */
+#define QASR_ERR_CUDA (-2)        /* a CUDA call or kernel launch failed */
+#define QASR_ERR_ALLOC (-3)       /* device allocation failed */
+#define QASR_ERR_UNSUPPORTED (-4) /* shape outside what a specialised kernel handles */
+#define QASR_ERR_TIMEOUT (-5)     /* a bounded device-side wait gave up */
+
+/* Message of the last failing call on this host thread ("" if none). */
+const char *qasr_last_error(void);
+/* Library version string. */
+const char *qasr_version(void);
+
+/* ======================================================================
+ * Kernel level (device pointers)
+ * ==================================================================== */
+
+/* kernels::rms_norm (mod.rs:897-918; x86 row kernel avx::rms_norm_row,
+ * avx.rs:377-415).  out[s,:] = x[s,:] * (1/sqrt(sum(x^2)/hidden + eps)) * w.
+ * Bit-exact with the reference's x86_64 path (same summation tree). */
+int qasr_rms_norm(float *out, const float *x, const float *w, int seq, int hidden, float eps, void *stream);
+
+/* kernels::rms_norm_per_head (mod.rs:920-935), in place.  Bit-exact
+ * (sequential per-head sum, as in the reference). */
+int qasr_rms_norm_per_head(float *x, const float *w, int seq, int n_heads, int head_dim, float eps, void *stream);
+
+/* kernels::layer_norm (mod.rs:866-895; avx::layer_norm_row avx.rs:420-481).
+ * Bit-exact with the x86_64 path. */
+int qasr_layer_norm(float *out, const float *x, const float *w, const float *b, int seq, int hidden, float eps,
+                    void *stream);
+
+/* kernels::compute_rope_neox (mod.rs:1228-1245): cos/sin [seq, head_dim]
+ * for the given positions (halves duplicated). */
+int qasr_compute_rope_neox(float *cos_out, float *sin_out, const int32_t *positions, int seq, int head_dim,
+                           float theta, void *stream);
+
+/* RopeCache::ensure (decoder.rs:253-289): table rows 0..n_pos-1. */
+int qasr_rope_cache_table(float *cos_out, float *sin_out, int n_pos, int head_dim, float theta, void *stream);
+
+/* kernels::apply_rope_neox (mod.rs:1247-1267), in place; cos_v/sin_v are
+ * [seq, head_dim].  Bit-exact. */
+int qasr_apply_rope_neox(float *x, const float *cos_v, const float *sin_v, int seq, int n_heads, int head_dim,
+                         void *stream);
+
+/* KvCache::k_at / v_at copies (decoder.rs:194-202, calls at 805-810 and
+ * 894-895): rows k_new[s], v_new[s] -> cache row (layer*max_seq + start_pos + s).
+ * Bit-exact (a copy).  Fails with QASR_ERR_INVALID when start_pos+seq > max_seq. */
+int qasr_kv_append(float *k_cache, float *v_cache, const float *k_new, const float *v_new, int layer,
+                   int max_seq, int kv_dim, int start_pos, int seq, void *stream);
+
+/* kernels::sinusoidal_pe (mod.rs:1213-1226): pe [n_pos, d_model]. */
+int qasr_sinusoidal_pe(float *pe, int n_pos, int d_model, void *stream);
+
+/* kernels::gelu (mod.rs:948-963; avx::gelu_inplace avx.rs:536-563): the
+ * tanh form with the reference's fast exp, in place.  Bit-exact on the
+ * 8-aligned body; the last n%8 elements use tanhf like the reference tail. */
+int qasr_gelu(float *x, int64_t n, void *stream);
+
+/* Exact-erf GELU 0.5*x*(1+erf(x/sqrt(2))), in place: the encoder activation
+ * of the reference's Metal encoder (encoder_gpu.rs:470,480). */
+int qasr_gelu_erf(float *x, int64_t n, void *stream);
+
+/* kernels::silu (mod.rs:941-946), in place. */
+int qasr_silu(float *x, int64_t n, void *stream);
+
+/* kernels::swiglu_multiply (mod.rs:965-985; avx::swiglu_interleaved
+ * avx.rs:568-599): out[s,j] = silu(gu[s,2j]) * gu[s,2j+1].  Bit-exact on the
+ * 8-aligned body (reference fast exp); tail uses expf. */
+int qasr_swiglu_multiply(float *out, const float *gate_up, int seq, int inter, void *stream);
+
+/* kernels::add_inplace (mod.rs:482-484). */
+int qasr_add_inplace(float *a, const float *b, int64_t n, void *stream);
+
+/* kernels::linear_nobias_int8 (mod.rs:650-661; generic::int8_matvec_fused
+ * generic.rs:39-49): y[s,o] = scales[o] * sum_k w[o,k]*x[s,k].  Any seq
+ * (tokens are processed in groups of up to 8 per weight pass). */
+int qasr_linear_nobias_int8(float *y, const float *x, const int8_t *w, const float *scales, int seq, int in_dim,
+                            int out_dim, void *stream);
+
+/* kernels::linear_int8 (mod.rs:664-673): as above plus bias[o] (may be NULL). */
+int qasr_linear_int8(float *y, const float *x, const int8_t *w, const float *scales, const float *bias, int seq,
+                     int in_dim, int out_dim, void *stream);
+
+/* kernels::causal_attention (mod.rs:1124-1207): GQA causal attention of
+ * seq_q queries at global positions q_offset.. over k/v [seq_k, n_kv*hd].
+ * head_dim must be 64 or 128. */
+int qasr_causal_attention(float *out, const float *q, const float *k, const float *v, int seq_q, int seq_k,
+                          int n_heads, int n_kv_heads, int head_dim, float scale, int q_offset, void *stream);
+
+/* quantize_f32_to_int8 (quantize.rs:633-662): symmetric per-row INT8,
+ * scale = absmax/127, q = round-half-away(v*127/absmax) clamped.  Bit-exact. */
+int qasr_quantize_f32_to_int8(const float *data, int64_t out_dim, int64_t in_dim, int8_t *q, float *scales,
+                              void *stream);
+
+/* Embedding gather: dst[i,:] = table[ids[i],:] (f32 table, BASELINE decode
+ * config) -- bit-exact copy.  Ids outside [0,vocab) set *bad_id_flag (device
+ * int, may be NULL) and produce a zero row. */
+int qasr_embed_gather_f32(float *dst, const float *table, const int32_t *ids, int n, int dim, int64_t vocab,
+                          int *bad_id_flag, void *stream);
+
+/* tok_embed_int8_to_f32 (decoder.rs:639-646) for n ids: dst[i,d] =
+ * f32(table[id,d]) * scales[id].  Bit-exact. */
+int qasr_embed_gather_int8(float *dst, const int8_t *table, const float *scales, const int32_t *ids, int n, int dim,
+                           int64_t vocab, int *bad_id_flag, void *stream);
+
+/* ---------------------------------------------------------------- fused */
+
+/* The decoder pre-attention block of decoder_prefill_int8
+ * (decoder.rs:770-810) on given projections:
+ *   x_norm = rms_norm(x, w_in)                              (mod.rs:897)
+ *   q, k   = rms_norm_per_head(q|k, q_norm_w|k_norm_w)      (mod.rs:920)
+ *   q, k   = apply_rope_neox(q|k, cos/sin rows start_pos..) (mod.rs:1247)
+ *   cache rows start_pos.. of layer `layer` <- k, v         (decoder.rs:805-810)
+ * q is rotated in place; k_out (may be NULL) receives the rotated k.
+ * cos_tab/sin_tab are full RopeCache tables (row = position).  Bit-exact. */
+int qasr_pre_attn_block(float *x_norm, const float *x, const float *w_in, int seq, int hidden, float *q,
+                        const float *k, const float *v, float *k_out, const float *q_norm_w, const float *k_norm_w,
+                        int n_heads, int n_kv_heads, int head_dim, float eps, const float *cos_tab,
+                        const float *sin_tab, int start_pos, float *k_cache, float *v_cache, int layer,
+                        int max_seq, void *stream);
+
+/* Encoder LayerNorm + sinusoidal position add: out[r,:] =
+ * layer_norm(x[r,:]) + pe[r % n_pos, :]  (layer_norm mod.rs:866 bit-exact,
+ * then the add of encoder.rs:341-343).  pe is [n_pos, hidden]. */
+int qasr_ln_pe(float *out, const float *x, const float *w, const float *b, const float *pe, int rows, int hidden,
+               int n_pos, float eps, void *stream);
+
+/* Post-attention RMSNorm + fused gate/up INT8 matvec + SwiGLU for M tokens
+ * (decoder.rs:911-921): h[m,j] = silu(g)*u with g,u the interleaved rows
+ * 2j, 2j+1 of w_gate_up applied to rms_norm(x[m]).  M <= 8. */
+int qasr_int8_norm_gateup_swiglu(float *h, const float *x, const float *norm_w, const int8_t *w_gate_up,
+                                 const float *scales, int M, int hidden, int inter, float eps, void *stream);
+
+/* INT8 matvec with the residual add folded in (decoder.rs:907-908 and
+ * 922-924): x[m,o] += scales[o] * sum_k w[o,k]*a[m,k].  M <= 8. */
+int qasr_int8_matvec_residual(float *x, const float *a, const int8_t *w, const float *scales, int M, int in_dim,
+                              int out_dim, void *stream);
+
+/* Final RMSNorm + INT8 lm-head + first-max argmax (decoder.rs:929-964) for
+ * M tokens: ids_out[m] = argmax_o scales[o]*dot(w[o], rms_norm(x[m])).
+ * logits_out [M, vocab] may be NULL.  M <= 8. */
+int qasr_final_norm_lmhead_argmax(int32_t *ids_out, float *logits_out, const float *x, const float *norm_w,
+                                  const int8_t *w, const float *scales, int M, int hidden, int vocab, float eps,
+                                  void *stream);
+
+/* ======================================================================
+ * Decoder engine
+ * ==================================================================== */
+
+typedef struct qasr_decoder qasr_decoder;
+
+typedef struct {
+  int hidden;     /* 1024 (0.6B) / 2048 (1.7B) */
+  int inter;      /* 3072 / 6144 */
+  int n_layers;   /* 28 */
+  int n_heads;    /* 16 */
+  int n_kv_heads; /* 8 */
+  int head_dim;   /* 128 */
+  int vocab;      /* 151936 */
+  float eps;      /* 1e-6 */
+  float theta;    /* 1e6 */
+  int max_batch;  /* sequences decoded together, 1..8 */
+  int max_seq;    /* KV capacity per sequence */
+  int embed_is_int8; /* 1: INT8 token table + scales (qint8 V2), 0: f32 table */
+} qasr_decoder_config;
+
+/* One decoder layer's weights, host or device pointers (copied). */
+typedef struct {
+  const int8_t *wq; const float *wq_s;        /* [n_heads*hd, hidden] */
+  const int8_t *wk; const float *wk_s;        /* [n_kv*hd, hidden] */
+  const int8_t *wv; const float *wv_s;        /* [n_kv*hd, hidden] */
+  const int8_t *wo; const float *wo_s;        /* [hidden, n_heads*hd] */
+  const int8_t *gate_up; const float *gate_up_s; /* [2*inter, hidden], interleaved rows */
+  const int8_t *down; const float *down_s;    /* [hidden, inter] */
+  const float *q_norm; const float *k_norm;   /* [hd] */
+  const float *input_norm; const float *post_attn_norm; /* [hidden] */
+} qasr_dec_layer_weights;
+
+/* DecoderInt8 + KvCache allocation on `device` (decoder.rs:652-747,140-150).
+ * Returns NULL on failure (message in qasr_last_error()). */
+qasr_decoder *qasr_decoder_create(const qasr_decoder_config *cfg, int device);
+void qasr_decoder_free(qasr_decoder *dec);
+
+/* Upload weights (host or device pointers; copied). */
+int qasr_decoder_set_layer(qasr_decoder *dec, int layer, const qasr_dec_layer_weights *w);
+/* embed: f32 [vocab, hidden] or int8 [vocab, hidden] (+ embed_scales);
+ * final norm [hidden]; lm_head int8 [vocab, hidden] + scales.  When lm_head
+ * is NULL the lm head is tied to the INT8 embedding table (decoder.rs:950-963). */
+int qasr_decoder_set_globals(qasr_decoder *dec, const void *embed, const float *embed_scales, const float *norm,
+                             const int8_t *lm_head, const float *lm_head_s);
+
+/* Device pointers of sequence `slot`'s KV cache, [n_layers, max_seq, kv_dim]. */
+int qasr_decoder_kv(qasr_decoder *dec, int slot, float **k_cache, float **v_cache);
+
+/* One greedy decode step for sequences 0..M-1 (decoder_forward_int8,
+ * decoder.rs:845-965, per sequence): token ids and positions in, next ids
+ * out, all HOST buffers.  Sequence m embeds tokens[m], writes its K/V at
+ * row positions[m] of its cache and attends over rows 0..positions[m]. */
+int qasr_decoder_step(qasr_decoder *dec, const int32_t *tokens, const int32_t *positions, int M, int32_t *next_tokens);
+
+/* Same step on DEVICE buffers, enqueued on the engine's stream without a
+ * host synchronisation; next_tokens may alias tokens. */
+int qasr_decoder_step_device(qasr_decoder *dec, const int32_t *tokens, const int32_t *positions, int M,
+                             int32_t *next_tokens);
+
+/* The engine's CUDA stream (cudaStream_t) and, after a step, the device
+ * pointer of the last step's logits [M, vocab] (NULL unless enabled). */
+void *qasr_decoder_stream(qasr_decoder *dec);
+int qasr_decoder_keep_logits(qasr_decoder *dec, int enable);
+const float *qasr_decoder_logits(qasr_decoder *dec);
+
+/* Kernel classes of a decode step, for qasr_decoder_profile_step. */
+#define QASR_K_EMBED 0     /* token embedding gather */
+#define QASR_K_NORM 1      /* input / post-attention / final RMSNorm */
+#define QASR_K_QKV 2       /* fused q|k|v INT8 matvec */
+#define QASR_K_QKV_POST 3  /* q/k per-head norm + RoPE + KV append */
+#define QASR_K_ATTN 4      /* split-K decode attention */
+#define QASR_K_OPROJ 5     /* o-proj INT8 matvec + residual */
+#define QASR_K_GATEUP 6    /* gate/up INT8 matvec + SwiGLU */
+#define QASR_K_DOWN 7      /* down INT8 matvec + residual */
+#define QASR_K_LMHEAD 8    /* lm head INT8 matvec + argmax */
+#define QASR_K_COUNT 9
+
+/* Run one decode step eagerly (no graph) with CUDA events around every
+ * kernel; class_ms[c] receives the summed device time of class c and
+ * class_launches[c] (may be NULL) its launch count.  Same results as
+ * qasr_decoder_step; for profiling and rooflines. */
+int qasr_decoder_profile_step(qasr_decoder *dec, const int32_t *tokens, const int32_t *positions, int M,
+                              float *class_ms, int *class_launches, int n_classes);
+
+/* Bytes the decode step reads/writes per call, by the algorithmic model
+ * (weights + scales + norms + lm head + K/V rows attended); for rooflines. */
+int64_t qasr_decoder_step_bytes(const qasr_decoder *dec, const int32_t *positions, int M);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QWENASR_CUDA_H */

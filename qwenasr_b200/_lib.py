@@ -1,0 +1,130 @@
+"""ctypes binding of libqwenasr_b200.so (the C ABI in include/qwenasr_cuda.h).
+
+The shared library is built in-tree by qwenasr_b200/build.py.  Loading fails
+loudly when it is missing: there is no CPU fallback anywhere in this package.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libqwenasr_b200.so")
+HEADER = os.path.join(os.path.dirname(HERE), "include", "qwenasr_cuda.h")
+
+QASR_OK = 0
+QASR_ERR_INVALID = -1
+QASR_ERR_CUDA = -2
+QASR_ERR_ALLOC = -3
+QASR_ERR_UNSUPPORTED = -4
+QASR_ERR_TIMEOUT = -5
+
+
+class QasrError(RuntimeError):
+    def __init__(self, code: int, fn: str, msg: str):
+        super().__init__(f"{fn} failed with status {code}: {msg}")
+        self.code = code
+
+
+class DecoderConfig(C.Structure):
+    _fields_ = [("hidden", C.c_int), ("inter", C.c_int), ("n_layers", C.c_int), ("n_heads", C.c_int),
+                ("n_kv_heads", C.c_int), ("head_dim", C.c_int), ("vocab", C.c_int), ("eps", C.c_float),
+                ("theta", C.c_float), ("max_batch", C.c_int), ("max_seq", C.c_int), ("embed_is_int8", C.c_int)]
+
+
+class DecLayerWeights(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in (
+        "wq", "wq_s", "wk", "wk_s", "wv", "wv_s", "wo", "wo_s", "gate_up", "gate_up_s", "down", "down_s",
+        "q_norm", "k_norm", "input_norm", "post_attn_norm")]
+
+
+P = C.c_void_p
+I = C.c_int
+I64 = C.c_int64
+F = C.c_float
+
+# name -> (restype, argtypes); every function returning int is a status.
+_SIGS = {
+    "qasr_last_error": (C.c_char_p, []),
+    "qasr_version": (C.c_char_p, []),
+    "qasr_rms_norm": (I, [P, P, P, I, I, F, P]),
+    "qasr_rms_norm_per_head": (I, [P, P, I, I, I, F, P]),
+    "qasr_layer_norm": (I, [P, P, P, P, I, I, F, P]),
+    "qasr_compute_rope_neox": (I, [P, P, P, I, I, F, P]),
+    "qasr_rope_cache_table": (I, [P, P, I, I, F, P]),
+    "qasr_apply_rope_neox": (I, [P, P, P, I, I, I, P]),
+    "qasr_kv_append": (I, [P, P, P, P, I, I, I, I, I, P]),
+    "qasr_sinusoidal_pe": (I, [P, I, I, P]),
+    "qasr_gelu": (I, [P, I64, P]),
+    "qasr_gelu_erf": (I, [P, I64, P]),
+    "qasr_silu": (I, [P, I64, P]),
+    "qasr_swiglu_multiply": (I, [P, P, I, I, P]),
+    "qasr_add_inplace": (I, [P, P, I64, P]),
+    "qasr_linear_nobias_int8": (I, [P, P, P, P, I, I, I, P]),
+    "qasr_linear_int8": (I, [P, P, P, P, P, I, I, I, P]),
+    "qasr_causal_attention": (I, [P, P, P, P, I, I, I, I, I, F, I, P]),
+    "qasr_quantize_f32_to_int8": (I, [P, I64, I64, P, P, P]),
+    "qasr_embed_gather_f32": (I, [P, P, P, I, I, I64, P, P]),
+    "qasr_embed_gather_int8": (I, [P, P, P, P, I, I, I64, P, P]),
+    "qasr_pre_attn_block": (I, [P, P, P, I, I, P, P, P, P, P, P, I, I, I, F, P, P, I, P, P, I, I, P]),
+    "qasr_ln_pe": (I, [P, P, P, P, P, I, I, I, F, P]),
+    "qasr_int8_norm_gateup_swiglu": (I, [P, P, P, P, P, I, I, I, F, P]),
+    "qasr_int8_matvec_residual": (I, [P, P, P, P, I, I, I, P]),
+    "qasr_final_norm_lmhead_argmax": (I, [P, P, P, P, P, P, I, I, I, F, P]),
+    "qasr_decoder_create": (P, [C.POINTER(DecoderConfig), I]),
+    "qasr_decoder_free": (None, [P]),
+    "qasr_decoder_set_layer": (I, [P, I, C.POINTER(DecLayerWeights)]),
+    "qasr_decoder_set_globals": (I, [P, P, P, P, P, P]),
+    "qasr_decoder_kv": (I, [P, I, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p)]),
+    "qasr_decoder_step": (I, [P, P, P, I, P]),
+    "qasr_decoder_step_device": (I, [P, P, P, I, P]),
+    "qasr_decoder_stream": (P, [P]),
+    "qasr_decoder_keep_logits": (I, [P, I]),
+    "qasr_decoder_logits": (P, [P]),
+    "qasr_decoder_step_bytes": (I64, [P, P, I]),
+    "qasr_decoder_profile_step": (I, [P, P, P, I, P, P, I]),
+}
+
+KERNEL_CLASSES = ("embed", "norm", "qkv", "qkv_post", "attn", "oproj", "gateup", "down", "lmhead")
+
+_lib = None
+
+
+def header_functions() -> list[str]:
+    """Names of the functions declared in include/qwenasr_cuda.h."""
+    txt = open(HEADER).read()
+    txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
+    return sorted(set(re.findall(r"\b(qasr_[a-z0-9_]+)\s*\(", txt)))
+
+
+def load(path: str | None = None):
+    """Load the library (once).  Raises if the in-tree .so has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    path = path or LIB_PATH
+    if not os.path.exists(path):
+        raise RuntimeError(f"{path} is missing: build it with `python -m qwenasr_b200.build` "
+                           "(there is no CPU fallback)")
+    lib = C.CDLL(path)
+    for name, (res, args) in _SIGS.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def last_error() -> str:
+    return (load().qasr_last_error() or b"").decode()
+
+
+def check(code: int, fn: str) -> None:
+    if code != QASR_OK:
+        raise QasrError(code, fn, last_error())
+
+
+def call(name: str, *args) -> None:
+    """Call a status-returning entry point and raise QasrError on failure."""
+    check(getattr(load(), name)(*args), name)

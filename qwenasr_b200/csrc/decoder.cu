@@ -1,0 +1,581 @@
+// decoder.cu -- INT8 decoder engine: DecoderInt8 + KvCache + RopeCache +
+// decoder_forward_int8 (crates/qwen-asr/src/decoder.rs:130-306, 652-965) for
+// a batch of independent sequences on one GPU.
+//
+// Device layout (all allocated once in qasr_decoder_create):
+//   per layer  wqkv  int8 [q_dim + 2*kv_dim, hidden]  (q | k | v rows; one
+//                    matvec launch covers the three projections, like the
+//                    fused QKV range split of kernels::linear_nobias_bf16_qkv,
+//                    mod.rs:708-775), sqkv f32 scales; wo/so; gate_up/sgu
+//                    (interleaved rows, decoder.rs:699-719); down/sdown;
+//                    q/k/input/post norms f32.
+//   globals    embed (f32 or int8 + scales), final norm, lm head int8 + scales
+//   KV         k_cache/v_cache f32 [max_batch][n_layers][max_seq][kv_dim]:
+//              the reference's per-sequence KvCache layout, sequences stacked.
+//   RoPE       cos/sin [max_seq, head_dim], the RopeCache::ensure table.
+//   work       x, xn [B, hidden]; qkv [B, q+2kv]; q_out, attn [B, q_dim];
+//              h [B, inter]; attention partials/counters; argmax keys.
+//
+// One decode step = 2 + 7*n_layers kernels captured once per batch size in a
+// CUDA graph and replayed: embed gather; per layer rms_norm, QKV matvec,
+// q/k norm + RoPE + KV append, split-K attention, o-proj(+residual),
+// rms_norm, gate/up matvec(+SwiGLU), down matvec(+residual); final rms_norm
+// + lm head argmax.
+#include <algorithm>
+#include <cstring>
+#include <vector>
+
+#include "attention.cuh"
+#include "common.cuh"
+#include "matvec.cuh"
+
+namespace qasr {
+
+struct LayerDev {
+  int8_t *wqkv = nullptr, *wo = nullptr, *gate_up = nullptr, *down = nullptr;
+  float *sqkv = nullptr, *so = nullptr, *sgu = nullptr, *sdown = nullptr;
+  float *q_norm = nullptr, *k_norm = nullptr, *in_norm = nullptr, *post_norm = nullptr;
+};
+
+}  // namespace qasr
+
+struct qasr_decoder {
+  qasr_decoder_config cfg;
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  std::vector<qasr::LayerDev> layers;
+  void *embed = nullptr;
+  float *embed_s = nullptr, *norm = nullptr, *lm_s = nullptr;
+  int8_t *lm = nullptr;
+  bool lm_tied = false;
+  float *k_cache = nullptr, *v_cache = nullptr;
+  float *rope_cos = nullptr, *rope_sin = nullptr;
+  float *x = nullptr, *xn = nullptr, *qkv = nullptr, *q_out = nullptr, *attn = nullptr, *h = nullptr;
+  float *partials = nullptr, *logits = nullptr;
+  unsigned *attn_ctr = nullptr, *am_ctr = nullptr;
+  unsigned long long *am_keys = nullptr;
+  int32_t *tok = nullptr, *pos = nullptr, *next = nullptr;
+  int *err = nullptr;
+  int32_t *h_tok = nullptr, *h_pos = nullptr, *h_next = nullptr;  // pinned staging
+  int *h_err = nullptr;
+  int splits = 1;
+  bool keep_logits = false;
+  std::vector<cudaGraphExec_t> graphs;  // per M (index M), built lazily
+  std::vector<void *> allocs;
+  long seq_stride() const { return (long)cfg.n_layers * cfg.max_seq * cfg.n_kv_heads * cfg.head_dim; }
+};
+
+namespace qasr {
+
+// q/k per-head RMSNorm + NeoX RoPE at positions[m] + KV append, one warp per
+// (token, head) over the fused qkv row (decoder.rs:888-895).  head_dim 128:
+// lane L holds elements 4L..4L+3, the RoPE partner is lane^16.
+__global__ void __launch_bounds__(256)
+qkv_post_kernel(const float *__restrict__ qkv, int qkv_stride, float *__restrict__ q_out, float *__restrict__ k_cache,
+                float *__restrict__ v_cache, long seq_stride, int layer, int max_seq,
+                const int32_t *__restrict__ positions, const float *__restrict__ q_norm,
+                const float *__restrict__ k_norm, const float *__restrict__ cos_tab,
+                const float *__restrict__ sin_tab, int n_heads, int n_kv, float eps, int M, int *err) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int per_tok = n_heads + 2 * n_kv;
+  const int task = blockIdx.x * 8 + warp;
+  if (task >= M * per_tok) return;
+  const int m = task / per_tok, h = task % per_tok;
+  const int pos = positions[m];
+  if (pos < 0 || pos >= max_seq) {
+    if (lane == 0) atomicExch(err, 2);
+    return;
+  }
+  const int kv_dim = n_kv * 128;
+  float4 v = reinterpret_cast<const float4 *>(qkv + (size_t)m * qkv_stride + h * 128)[lane];
+  const size_t cache_row = (size_t)m * seq_stride + ((size_t)layer * max_seq + pos) * kv_dim;
+  if (h >= n_heads + n_kv) {  // V head: plain append
+    reinterpret_cast<float4 *>(v_cache + cache_row + (h - n_heads - n_kv) * 128)[lane] = v;
+    return;
+  }
+  const float *nw = h < n_heads ? q_norm : k_norm;
+  float ss = __fmul_rn(v.x, v.x);
+  ss = fmaf(v.y, v.y, ss);
+  ss = fmaf(v.z, v.z, ss);
+  ss = fmaf(v.w, v.w, ss);
+  ss = warp_sum(ss);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, 128.0f), eps)));
+  const float4 w4 = reinterpret_cast<const float4 *>(nw)[lane];
+  v.x = __fmul_rn(__fmul_rn(v.x, inv), w4.x);
+  v.y = __fmul_rn(__fmul_rn(v.y, inv), w4.y);
+  v.z = __fmul_rn(__fmul_rn(v.z, inv), w4.z);
+  v.w = __fmul_rn(__fmul_rn(v.w, inv), w4.w);
+  float4 p;
+  p.x = __shfl_xor_sync(0xffffffffu, v.x, 16);
+  p.y = __shfl_xor_sync(0xffffffffu, v.y, 16);
+  p.z = __shfl_xor_sync(0xffffffffu, v.z, 16);
+  p.w = __shfl_xor_sync(0xffffffffu, v.w, 16);
+  const float4 c = reinterpret_cast<const float4 *>(cos_tab + (size_t)pos * 128)[lane];
+  const float4 s = reinterpret_cast<const float4 *>(sin_tab + (size_t)pos * 128)[lane];
+  const float sg = lane < 16 ? -1.0f : 1.0f;  // first half: x1*c - x2*s; second: x2*c + x1*s
+  float4 o;
+  o.x = __fadd_rn(__fmul_rn(v.x, c.x), __fmul_rn(sg * p.x, s.x));
+  o.y = __fadd_rn(__fmul_rn(v.y, c.y), __fmul_rn(sg * p.y, s.y));
+  o.z = __fadd_rn(__fmul_rn(v.z, c.z), __fmul_rn(sg * p.z, s.z));
+  o.w = __fadd_rn(__fmul_rn(v.w, c.w), __fmul_rn(sg * p.w, s.w));
+  if (h < n_heads)
+    reinterpret_cast<float4 *>(q_out + (size_t)m * n_heads * 128 + h * 128)[lane] = o;
+  else
+    reinterpret_cast<float4 *>(k_cache + cache_row + (h - n_heads) * 128)[lane] = o;
+}
+
+// Embedding gather for the step's tokens (f32 or int8 table).
+__global__ void step_embed_kernel(float *__restrict__ x, const void *__restrict__ table,
+                                  const float *__restrict__ scales, int is_int8, const int32_t *__restrict__ ids,
+                                  int dim, int vocab, int *err) {
+  const int m = blockIdx.x;
+  int id = ids[m];
+  if (id < 0 || id >= vocab) {
+    if (threadIdx.x == 0) atomicExch(err, 1);
+    id = 0;
+  }
+  float4 *d = reinterpret_cast<float4 *>(x + (size_t)m * dim);
+  if (is_int8) {
+    const uint32_t *src = reinterpret_cast<const uint32_t *>(static_cast<const int8_t *>(table) + (size_t)id * dim);
+    const float s = scales[id];
+    for (int c = threadIdx.x; c < dim / 4; c += blockDim.x) {
+      float f[4];
+      i8x4_to_f32(src[c], f);
+      d[c] = make_float4(__fmul_rn(f[0], s), __fmul_rn(f[1], s), __fmul_rn(f[2], s), __fmul_rn(f[3], s));
+    }
+  } else {
+    const float4 *src = reinterpret_cast<const float4 *>(static_cast<const float *>(table) + (size_t)id * dim);
+    for (int c = threadIdx.x; c < dim / 4; c += blockDim.x) d[c] = src[c];
+  }
+}
+
+}  // namespace qasr
+
+using namespace qasr;
+
+// kernels launched by the decode step (the rope table kernel lives in norm_rope.cu)
+extern "C" int qasr_rms_norm(float *, const float *, const float *, int, int, float, void *);
+extern "C" int qasr_rope_cache_table(float *, float *, int, int, float, void *);
+
+static void *dalloc(qasr_decoder *d, size_t bytes, int *rc) {
+  void *p = nullptr;
+  if (*rc) return nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes ? bytes : 16);
+  if (e != cudaSuccess) {
+    *rc = cuda_status(e, "qasr_decoder: cudaMalloc");
+    return nullptr;
+  }
+  d->allocs.push_back(p);
+  return p;
+}
+
+extern "C" void qasr_decoder_free(qasr_decoder *d) {
+  if (!d) return;
+  cudaSetDevice(d->device);
+  if (d->stream) cudaStreamSynchronize(d->stream);
+  for (auto g : d->graphs)
+    if (g) cudaGraphExecDestroy(g);
+  for (void *p : d->allocs) cudaFree(p);
+  if (d->h_tok) cudaFreeHost(d->h_tok);
+  if (d->stream) cudaStreamDestroy(d->stream);
+  delete d;
+}
+
+extern "C" qasr_decoder *qasr_decoder_create(const qasr_decoder_config *cfg, int device) {
+  if (!cfg || cfg->hidden <= 0 || cfg->hidden % 128 || cfg->inter <= 0 || cfg->inter % 64 || cfg->n_layers <= 0 ||
+      cfg->n_heads <= 0 || cfg->n_kv_heads <= 0 || cfg->n_heads % cfg->n_kv_heads || cfg->vocab <= 0 ||
+      cfg->max_batch <= 0 || cfg->max_batch > 8 || cfg->max_seq <= 0) {
+    set_error("qasr_decoder_create: invalid config");
+    return nullptr;
+  }
+  if (cfg->head_dim != 128 || cfg->n_heads / cfg->n_kv_heads > 2) {
+    set_error("qasr_decoder_create: head_dim must be 128 and GQA group <= 2");
+    return nullptr;
+  }
+  if (cudaSetDevice(device) != cudaSuccess) {
+    set_error("qasr_decoder_create: cudaSetDevice(%d) failed", device);
+    return nullptr;
+  }
+  qasr_decoder *d = new qasr_decoder();
+  d->cfg = *cfg;
+  d->device = device;
+  int rc = cuda_status(cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking), "qasr_decoder_create");
+  const int H = cfg->hidden, I = cfg->inter, L = cfg->n_layers, hd = cfg->head_dim;
+  const int q_dim = cfg->n_heads * hd, kv_dim = cfg->n_kv_heads * hd, qkv_rows = q_dim + 2 * kv_dim;
+  const int B = cfg->max_batch;
+  d->layers.resize(L);
+  for (int l = 0; l < L; ++l) {
+    LayerDev &ld = d->layers[l];
+    ld.wqkv = (int8_t *)dalloc(d, (size_t)qkv_rows * H, &rc);
+    ld.sqkv = (float *)dalloc(d, (size_t)qkv_rows * 4, &rc);
+    ld.wo = (int8_t *)dalloc(d, (size_t)H * q_dim, &rc);
+    ld.so = (float *)dalloc(d, (size_t)H * 4, &rc);
+    ld.gate_up = (int8_t *)dalloc(d, (size_t)2 * I * H, &rc);
+    ld.sgu = (float *)dalloc(d, (size_t)2 * I * 4, &rc);
+    ld.down = (int8_t *)dalloc(d, (size_t)H * I, &rc);
+    ld.sdown = (float *)dalloc(d, (size_t)H * 4, &rc);
+    ld.q_norm = (float *)dalloc(d, (size_t)hd * 4, &rc);
+    ld.k_norm = (float *)dalloc(d, (size_t)hd * 4, &rc);
+    ld.in_norm = (float *)dalloc(d, (size_t)H * 4, &rc);
+    ld.post_norm = (float *)dalloc(d, (size_t)H * 4, &rc);
+  }
+  d->embed = dalloc(d, (size_t)cfg->vocab * H * (cfg->embed_is_int8 ? 1 : 4), &rc);
+  if (cfg->embed_is_int8) d->embed_s = (float *)dalloc(d, (size_t)cfg->vocab * 4, &rc);
+  d->norm = (float *)dalloc(d, (size_t)H * 4, &rc);
+  const size_t kv_elems = (size_t)B * d->seq_stride();
+  d->k_cache = (float *)dalloc(d, kv_elems * 4, &rc);
+  d->v_cache = (float *)dalloc(d, kv_elems * 4, &rc);
+  d->rope_cos = (float *)dalloc(d, (size_t)cfg->max_seq * hd * 4, &rc);
+  d->rope_sin = (float *)dalloc(d, (size_t)cfg->max_seq * hd * 4, &rc);
+  d->x = (float *)dalloc(d, (size_t)B * H * 4, &rc);
+  d->xn = (float *)dalloc(d, (size_t)B * H * 4, &rc);
+  d->qkv = (float *)dalloc(d, (size_t)B * qkv_rows * 4, &rc);
+  d->q_out = (float *)dalloc(d, (size_t)B * q_dim * 4, &rc);
+  d->attn = (float *)dalloc(d, (size_t)B * q_dim * 4, &rc);
+  d->h = (float *)dalloc(d, (size_t)B * I * 4, &rc);
+  d->splits = attn_pick_splits(B, cfg->n_kv_heads, cfg->max_seq);
+  const int G = cfg->n_heads / cfg->n_kv_heads;
+  d->partials = (float *)dalloc(d, (size_t)B * cfg->n_kv_heads * d->splits * G * kAttnPartStride * 4, &rc);
+  d->attn_ctr = (unsigned *)dalloc(d, (size_t)B * cfg->n_kv_heads * 4, &rc);
+  d->am_keys = (unsigned long long *)dalloc(d, 8 * 8, &rc);
+  d->am_ctr = (unsigned *)dalloc(d, 16, &rc);
+  d->tok = (int32_t *)dalloc(d, 8 * 4, &rc);
+  d->pos = (int32_t *)dalloc(d, 8 * 4, &rc);
+  d->next = (int32_t *)dalloc(d, 8 * 4, &rc);
+  d->err = (int *)dalloc(d, 16, &rc);
+  if (!rc) rc = cuda_status(cudaHostAlloc((void **)&d->h_tok, 4 * 64, cudaHostAllocDefault), "cudaHostAlloc");
+  if (rc) {
+    qasr_decoder_free(d);
+    return nullptr;
+  }
+  d->h_pos = d->h_tok + 16;
+  d->h_next = d->h_tok + 32;
+  d->h_err = reinterpret_cast<int *>(d->h_tok + 48);
+  cudaStream_t st = d->stream;
+  rc = cuda_status(cudaMemsetAsync(d->k_cache, 0, kv_elems * 4, st), "memset");
+  if (!rc) rc = cuda_status(cudaMemsetAsync(d->v_cache, 0, kv_elems * 4, st), "memset");
+  if (!rc) rc = cuda_status(cudaMemsetAsync(d->attn_ctr, 0, (size_t)B * cfg->n_kv_heads * 4, st), "memset");
+  if (!rc) rc = cuda_status(cudaMemsetAsync(d->am_keys, 0, 64, st), "memset");
+  if (!rc) rc = cuda_status(cudaMemsetAsync(d->am_ctr, 0, 16, st), "memset");
+  if (!rc) rc = cuda_status(cudaMemsetAsync(d->err, 0, 16, st), "memset");
+  if (!rc) rc = qasr_rope_cache_table(d->rope_cos, d->rope_sin, cfg->max_seq, hd, cfg->theta, st);
+  if (!rc) rc = cuda_status(cudaStreamSynchronize(st), "qasr_decoder_create");
+  if (rc) {
+    qasr_decoder_free(d);
+    return nullptr;
+  }
+  d->graphs.assign(9, nullptr);
+  return d;
+}
+
+static int copy_in(qasr_decoder *d, void *dst, const void *src, size_t bytes, const char *what) {
+  if (!src) {
+    set_error("qasr_decoder: %s is NULL", what);
+    return QASR_ERR_INVALID;
+  }
+  return cuda_status(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, d->stream), what);
+}
+
+extern "C" int qasr_decoder_set_layer(qasr_decoder *d, int layer, const qasr_dec_layer_weights *w) {
+  if (!d || !w || layer < 0 || layer >= d->cfg.n_layers) {
+    set_error("qasr_decoder_set_layer: invalid arguments");
+    return QASR_ERR_INVALID;
+  }
+  cudaSetDevice(d->device);
+  const qasr_decoder_config &c = d->cfg;
+  const size_t H = c.hidden, I = c.inter, q_dim = (size_t)c.n_heads * c.head_dim, kv = (size_t)c.n_kv_heads * c.head_dim;
+  LayerDev &ld = d->layers[layer];
+  int rc = 0;
+  if (!rc) rc = copy_in(d, ld.wqkv, w->wq, q_dim * H, "wq");
+  if (!rc) rc = copy_in(d, ld.wqkv + q_dim * H, w->wk, kv * H, "wk");
+  if (!rc) rc = copy_in(d, ld.wqkv + (q_dim + kv) * H, w->wv, kv * H, "wv");
+  if (!rc) rc = copy_in(d, ld.sqkv, w->wq_s, q_dim * 4, "wq_s");
+  if (!rc) rc = copy_in(d, ld.sqkv + q_dim, w->wk_s, kv * 4, "wk_s");
+  if (!rc) rc = copy_in(d, ld.sqkv + q_dim + kv, w->wv_s, kv * 4, "wv_s");
+  if (!rc) rc = copy_in(d, ld.wo, w->wo, H * q_dim, "wo");
+  if (!rc) rc = copy_in(d, ld.so, w->wo_s, H * 4, "wo_s");
+  if (!rc) rc = copy_in(d, ld.gate_up, w->gate_up, 2 * I * H, "gate_up");
+  if (!rc) rc = copy_in(d, ld.sgu, w->gate_up_s, 2 * I * 4, "gate_up_s");
+  if (!rc) rc = copy_in(d, ld.down, w->down, H * I, "down");
+  if (!rc) rc = copy_in(d, ld.sdown, w->down_s, H * 4, "down_s");
+  if (!rc) rc = copy_in(d, ld.q_norm, w->q_norm, c.head_dim * 4, "q_norm");
+  if (!rc) rc = copy_in(d, ld.k_norm, w->k_norm, c.head_dim * 4, "k_norm");
+  if (!rc) rc = copy_in(d, ld.in_norm, w->input_norm, H * 4, "input_norm");
+  if (!rc) rc = copy_in(d, ld.post_norm, w->post_attn_norm, H * 4, "post_attn_norm");
+  if (!rc) rc = cuda_status(cudaStreamSynchronize(d->stream), "qasr_decoder_set_layer");
+  return rc;
+}
+
+extern "C" int qasr_decoder_set_globals(qasr_decoder *d, const void *embed, const float *embed_scales,
+                                        const float *norm, const int8_t *lm_head, const float *lm_head_s) {
+  if (!d) {
+    set_error("qasr_decoder_set_globals: null decoder");
+    return QASR_ERR_INVALID;
+  }
+  cudaSetDevice(d->device);
+  const qasr_decoder_config &c = d->cfg;
+  const size_t VH = (size_t)c.vocab * c.hidden;
+  int rc = copy_in(d, d->embed, embed, VH * (c.embed_is_int8 ? 1 : 4), "embed");
+  if (!rc && c.embed_is_int8) rc = copy_in(d, d->embed_s, embed_scales, (size_t)c.vocab * 4, "embed_scales");
+  if (!rc) rc = copy_in(d, d->norm, norm, (size_t)c.hidden * 4, "norm");
+  if (!rc) {
+    if (lm_head) {
+      if (!d->lm) {
+        int arc = 0;
+        d->lm = (int8_t *)dalloc(d, VH, &arc);
+        d->lm_s = (float *)dalloc(d, (size_t)c.vocab * 4, &arc);
+        if (arc) return arc;
+      }
+      rc = copy_in(d, d->lm, lm_head, VH, "lm_head");
+      if (!rc) rc = copy_in(d, d->lm_s, lm_head_s, (size_t)c.vocab * 4, "lm_head_s");
+      d->lm_tied = false;
+    } else {
+      if (!c.embed_is_int8) {
+        set_error("qasr_decoder_set_globals: a tied lm head needs the INT8 embedding table");
+        return QASR_ERR_INVALID;
+      }
+      d->lm_tied = true;
+    }
+  }
+  if (!rc) rc = cuda_status(cudaStreamSynchronize(d->stream), "qasr_decoder_set_globals");
+  return rc;
+}
+
+extern "C" int qasr_decoder_kv(qasr_decoder *d, int slot, float **k, float **v) {
+  if (!d || !k || !v || slot < 0 || slot >= d->cfg.max_batch) {
+    set_error("qasr_decoder_kv: invalid arguments");
+    return QASR_ERR_INVALID;
+  }
+  *k = d->k_cache + (size_t)slot * d->seq_stride();
+  *v = d->v_cache + (size_t)slot * d->seq_stride();
+  return QASR_OK;
+}
+
+extern "C" void *qasr_decoder_stream(qasr_decoder *d) { return d ? (void *)d->stream : nullptr; }
+
+extern "C" int qasr_decoder_keep_logits(qasr_decoder *d, int enable) {
+  if (!d) return QASR_ERR_INVALID;
+  if (enable && !d->logits) {
+    int rc = 0;
+    cudaSetDevice(d->device);
+    d->logits = (float *)dalloc(d, (size_t)d->cfg.max_batch * d->cfg.vocab * 4, &rc);
+    if (rc) return rc;
+  }
+  if ((bool)enable != d->keep_logits) {
+    for (auto &g : d->graphs)
+      if (g) {
+        cudaGraphExecDestroy(g);
+        g = nullptr;
+      }
+  }
+  d->keep_logits = enable != 0;
+  return QASR_OK;
+}
+
+extern "C" const float *qasr_decoder_logits(qasr_decoder *d) { return d && d->keep_logits ? d->logits : nullptr; }
+
+// Optional per-kernel-class timing of an eager step: events recorded before
+// the first and after every kernel, durations summed per class.
+struct StepMarks {
+  std::vector<cudaEvent_t> ev;
+  std::vector<int> cls;
+  cudaStream_t st;
+  void mark(int c) {
+    cudaEvent_t e;
+    cudaEventCreate(&e);
+    cudaEventRecord(e, st);
+    ev.push_back(e);
+    cls.push_back(c);
+  }
+  ~StepMarks() {
+    for (auto e : ev) cudaEventDestroy(e);
+  }
+};
+#define MARK(c) \
+  if (marks) marks->mark(c)
+
+// Enqueue the kernels of one decode step for M sequences on d->stream.
+static int enqueue_step(qasr_decoder *d, int M, StepMarks *marks = nullptr) {
+  const qasr_decoder_config &c = d->cfg;
+  cudaStream_t st = d->stream;
+  MARK(-1);
+  const int H = c.hidden, I = c.inter, hd = c.head_dim;
+  const int q_dim = c.n_heads * hd, kv_dim = c.n_kv_heads * hd, qkv_rows = q_dim + 2 * kv_dim;
+  const int G = c.n_heads / c.n_kv_heads;
+  const void *emb_tab = d->embed;
+  step_embed_kernel<<<M, 256, 0, st>>>(d->x, emb_tab, d->embed_s, c.embed_is_int8, d->tok, H, c.vocab, d->err);
+  MARK(QASR_K_EMBED);
+  int rc = launch_status("decode step: embed");
+  for (int l = 0; l < c.n_layers && !rc; ++l) {
+    const LayerDev &L = d->layers[l];
+    rc = qasr_rms_norm(d->xn, d->x, L.in_norm, M, H, c.eps, st);
+    if (rc) break;
+    MARK(QASR_K_NORM);
+    MvParams p{};
+    p.x = d->xn; p.x_stride = H; p.w = L.wqkv; p.scales = L.sqkv; p.y = d->qkv; p.y_stride = qkv_rows;
+    p.M = M; p.K = H; p.N = qkv_rows;
+    mv_launch(p, MvEpi::Store, st, 0);
+    MARK(QASR_K_QKV);
+    const int tasks = M * (c.n_heads + 2 * c.n_kv_heads);
+    qkv_post_kernel<<<ceil_div(tasks, 8), 256, 0, st>>>(d->qkv, qkv_rows, d->q_out, d->k_cache, d->v_cache,
+                                                        d->seq_stride(), l, c.max_seq, d->pos, L.q_norm, L.k_norm,
+                                                        d->rope_cos, d->rope_sin, c.n_heads, c.n_kv_heads, c.eps, M,
+                                                        d->err);
+    MARK(QASR_K_QKV_POST);
+    AttnDecodeParams a{};
+    a.q = d->q_out; a.q_stride = q_dim; a.k_cache = d->k_cache; a.v_cache = d->v_cache;
+    a.seq_stride = d->seq_stride(); a.layer = l; a.max_seq = c.max_seq; a.kv_dim = kv_dim;
+    a.n_kv_heads = c.n_kv_heads; a.positions = d->pos; a.scale = 1.0f / sqrtf((float)hd); a.M = M;
+    a.splits = d->splits; a.partials = d->partials; a.counters = d->attn_ctr; a.out = d->attn; a.out_stride = q_dim;
+    if ((rc = attn_decode_launch(a, G, st))) break;
+    MARK(QASR_K_ATTN);
+    MvParams o{};
+    o.x = d->attn; o.x_stride = q_dim; o.w = L.wo; o.scales = L.so; o.y = d->x; o.y_stride = H;
+    o.M = M; o.K = q_dim; o.N = H;
+    mv_launch(o, MvEpi::Residual, st, 0);
+    MARK(QASR_K_OPROJ);
+    if ((rc = qasr_rms_norm(d->xn, d->x, L.post_norm, M, H, c.eps, st))) break;
+    MARK(QASR_K_NORM);
+    MvParams g{};
+    g.x = d->xn; g.x_stride = H; g.w = L.gate_up; g.scales = L.sgu; g.y = d->h; g.y_stride = I;
+    g.M = M; g.K = H; g.N = 2 * I;
+    mv_launch(g, MvEpi::SwiGLU, st, 0);
+    MARK(QASR_K_GATEUP);
+    MvParams dn{};
+    dn.x = d->h; dn.x_stride = I; dn.w = L.down; dn.scales = L.sdown; dn.y = d->x; dn.y_stride = H;
+    dn.M = M; dn.K = I; dn.N = H;
+    mv_launch(dn, MvEpi::Residual, st, 0);
+    MARK(QASR_K_DOWN);
+    rc = launch_status("decode step: layer");
+  }
+  if (rc) return rc;
+  if ((rc = qasr_rms_norm(d->xn, d->x, d->norm, M, H, c.eps, st))) return rc;
+  MARK(QASR_K_NORM);
+  MvParams lm{};
+  lm.x = d->xn; lm.x_stride = H;
+  lm.w = d->lm_tied ? static_cast<const int8_t *>(d->embed) : d->lm;
+  lm.scales = d->lm_tied ? d->embed_s : d->lm_s;
+  lm.y = d->keep_logits ? d->logits : nullptr; lm.y_stride = c.vocab;
+  lm.M = M; lm.K = H; lm.N = c.vocab; lm.keys = d->am_keys; lm.counter = d->am_ctr; lm.ids = d->next;
+  mv_launch(lm, MvEpi::Argmax, st, 4);
+  MARK(QASR_K_LMHEAD);
+  return launch_status("decode step: lm head");
+}
+
+static int run_graph(qasr_decoder *d, int M) {
+  if (!d->graphs[M]) {
+    cudaGraph_t graph = nullptr;
+    int rc = cuda_status(cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+    if (rc) return rc;
+    int erc = enqueue_step(d, M);
+    rc = cuda_status(cudaStreamEndCapture(d->stream, &graph), "end capture");
+    if (erc) {
+      if (graph) cudaGraphDestroy(graph);
+      return erc;
+    }
+    if (rc) return rc;
+    cudaGraphExec_t exec = nullptr;
+    rc = cuda_status(cudaGraphInstantiate(&exec, graph, 0), "graph instantiate");
+    cudaGraphDestroy(graph);
+    if (rc) return rc;
+    d->graphs[M] = exec;
+  }
+  return cuda_status(cudaGraphLaunch(d->graphs[M], d->stream), "graph launch");
+}
+
+extern "C" int qasr_decoder_step_device(qasr_decoder *d, const int32_t *tokens, const int32_t *positions, int M,
+                                        int32_t *next_tokens) {
+  if (!d || !tokens || !positions || !next_tokens || M <= 0 || M > d->cfg.max_batch) {
+    set_error("qasr_decoder_step_device: invalid arguments (M=%d)", M);
+    return QASR_ERR_INVALID;
+  }
+  cudaSetDevice(d->device);
+  int rc = cuda_status(cudaMemcpyAsync(d->tok, tokens, M * 4, cudaMemcpyDeviceToDevice, d->stream), "tokens");
+  if (!rc) rc = cuda_status(cudaMemcpyAsync(d->pos, positions, M * 4, cudaMemcpyDeviceToDevice, d->stream), "pos");
+  if (!rc) rc = run_graph(d, M);
+  if (!rc) rc = cuda_status(cudaMemcpyAsync(next_tokens, d->next, M * 4, cudaMemcpyDeviceToDevice, d->stream), "next");
+  return rc;
+}
+
+extern "C" int qasr_decoder_step(qasr_decoder *d, const int32_t *tokens, const int32_t *positions, int M,
+                                 int32_t *next_tokens) {
+  if (!d || !tokens || !positions || !next_tokens || M <= 0 || M > d->cfg.max_batch) {
+    set_error("qasr_decoder_step: invalid arguments (M=%d)", M);
+    return QASR_ERR_INVALID;
+  }
+  for (int m = 0; m < M; ++m) {
+    if (tokens[m] < 0 || tokens[m] >= d->cfg.vocab) {
+      set_error("qasr_decoder_step: token %d of sequence %d outside [0,%d)", tokens[m], m, d->cfg.vocab);
+      return QASR_ERR_INVALID;
+    }
+    if (positions[m] < 0 || positions[m] >= d->cfg.max_seq) {
+      set_error("qasr_decoder_step: position %d of sequence %d outside [0,%d)", positions[m], m, d->cfg.max_seq);
+      return QASR_ERR_INVALID;
+    }
+  }
+  cudaSetDevice(d->device);
+  std::memcpy(d->h_tok, tokens, M * 4);
+  std::memcpy(d->h_pos, positions, M * 4);
+  int rc = cuda_status(cudaMemcpyAsync(d->tok, d->h_tok, M * 4, cudaMemcpyHostToDevice, d->stream), "tokens H2D");
+  if (!rc) rc = cuda_status(cudaMemcpyAsync(d->pos, d->h_pos, M * 4, cudaMemcpyHostToDevice, d->stream), "pos H2D");
+  if (!rc) rc = run_graph(d, M);
+  if (!rc) rc = cuda_status(cudaMemcpyAsync(d->h_next, d->next, M * 4, cudaMemcpyDeviceToHost, d->stream), "D2H");
+  if (!rc) rc = cuda_status(cudaMemcpyAsync(d->h_err, d->err, 4, cudaMemcpyDeviceToHost, d->stream), "err D2H");
+  if (!rc) rc = cuda_status(cudaStreamSynchronize(d->stream), "qasr_decoder_step");
+  if (rc) return rc;
+  if (*d->h_err) {
+    set_error("qasr_decoder_step: device reported bad input (code %d)", *d->h_err);
+    cudaMemsetAsync(d->err, 0, 4, d->stream);
+    cudaStreamSynchronize(d->stream);
+    return QASR_ERR_INVALID;
+  }
+  std::memcpy(next_tokens, d->h_next, M * 4);
+  return QASR_OK;
+}
+
+extern "C" int64_t qasr_decoder_step_bytes(const qasr_decoder *d, const int32_t *positions, int M) {
+  if (!d || !positions || M <= 0) return 0;
+  const qasr_decoder_config &c = d->cfg;
+  const int64_t H = c.hidden, I = c.inter, q_dim = (int64_t)c.n_heads * c.head_dim,
+                kv = (int64_t)c.n_kv_heads * c.head_dim;
+  const int64_t w_layer = (q_dim + 2 * kv) * H + H * q_dim + 2 * I * H + H * I;
+  const int64_t s_layer = 4 * ((q_dim + 2 * kv) + H + 2 * I + H);
+  const int64_t n_layer = 4 * (2 * c.head_dim + 2 * H);
+  int64_t bytes = c.n_layers * (w_layer + s_layer + n_layer);
+  bytes += (int64_t)c.vocab * H + 4 * (int64_t)c.vocab;  // lm head + scales
+  for (int m = 0; m < M; ++m) bytes += (int64_t)c.n_layers * 2 * (positions[m] + 1) * kv * 4;
+  return bytes;
+}
+
+extern "C" int qasr_decoder_profile_step(qasr_decoder *d, const int32_t *tokens, const int32_t *positions, int M,
+                                         float *class_ms, int *class_launches, int n_classes) {
+  if (!d || !tokens || !positions || !class_ms || M <= 0 || M > d->cfg.max_batch || n_classes < QASR_K_COUNT) {
+    set_error("qasr_decoder_profile_step: invalid arguments");
+    return QASR_ERR_INVALID;
+  }
+  cudaSetDevice(d->device);
+  std::memcpy(d->h_tok, tokens, M * 4);
+  std::memcpy(d->h_pos, positions, M * 4);
+  int rc = cuda_status(cudaMemcpyAsync(d->tok, d->h_tok, M * 4, cudaMemcpyHostToDevice, d->stream), "tokens H2D");
+  if (!rc) rc = cuda_status(cudaMemcpyAsync(d->pos, d->h_pos, M * 4, cudaMemcpyHostToDevice, d->stream), "pos H2D");
+  if (rc) return rc;
+  StepMarks marks;
+  marks.st = d->stream;
+  rc = enqueue_step(d, M, &marks);
+  if (!rc) rc = cuda_status(cudaStreamSynchronize(d->stream), "qasr_decoder_profile_step");
+  if (rc) return rc;
+  for (int i = 0; i < n_classes; ++i) {
+    class_ms[i] = 0.0f;
+    if (class_launches) class_launches[i] = 0;
+  }
+  for (size_t i = 1; i < marks.ev.size(); ++i) {
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, marks.ev[i - 1], marks.ev[i]);
+    const int c = marks.cls[i];
+    if (c >= 0 && c < n_classes) {
+      class_ms[c] += ms;
+      if (class_launches) class_launches[c] += 1;
+    }
+  }
+  return QASR_OK;
+}

@@ -1,0 +1,415 @@
+// norm_rope.cu -- RMSNorm, LayerNorm(+PE), per-head norm, RoPE, KV append and
+// the fused decoder pre-attention block, reproducing the reference's f32
+// rounding sequence (crates/qwen-asr/src/kernels/avx.rs:377-481,
+// kernels/mod.rs:866-935 and 1213-1267, decoder.rs:194-202, 253-289).
+//
+// All of these are HBM-bound row kernels: each row is read once with 16-byte
+// vector loads into shared memory, reduced in the reference's order by one
+// warp, and written once.
+#include "common.cuh"
+#include "rowops.cuh"
+
+namespace qasr {
+
+constexpr int kRowWarps = 4;  // warps per CTA for one-warp-per-row kernels
+
+// ---------------------------------------------------------------- rms_norm
+__global__ void __launch_bounds__(kRowWarps * 32)
+rms_norm_kernel(float *__restrict__ out, const float *__restrict__ x, const float *__restrict__ w, int seq,
+                int hidden, float eps) {
+  extern __shared__ float smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kRowWarps + warp;
+  if (row >= seq) return;
+  float *xs = smem + (size_t)warp * hidden;
+  warp_load_row(xs, x + (size_t)row * hidden, hidden);
+  const float inv = rms_inv_ref(xs, hidden, eps);
+  float *o = out + (size_t)row * hidden;
+  for (int i = lane; i < hidden; i += 32) o[i] = __fmul_rn(__fmul_rn(xs[i], inv), w[i]);
+}
+
+// ------------------------------------------------------- rms_norm_per_head
+// One warp per (row, head).  The reference sums the head sequentially
+// (mod.rs:926-929), so lane 0 does exactly that; the scaling is parallel.
+__global__ void __launch_bounds__(256)
+rms_norm_per_head_kernel(float *__restrict__ x, const float *__restrict__ w, int seq, int n_heads, int head_dim,
+                         float eps) {
+  extern __shared__ float smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long task = (long)blockIdx.x * 8 + warp;
+  if (task >= (long)seq * n_heads) return;
+  float *hs = smem + (size_t)warp * head_dim;
+  float *v = x + task * head_dim;
+  warp_load_row(hs, v, head_dim);
+  float inv = 0.0f;
+  if (lane == 0) {
+    float s = 0.0f;
+    for (int d = 0; d < head_dim; ++d) s = __fadd_rn(s, __fmul_rn(hs[d], hs[d]));
+    inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)head_dim), eps)));
+  }
+  inv = __shfl_sync(0xffffffffu, inv, 0);
+  for (int d = lane; d < head_dim; d += 32) v[d] = __fmul_rn(__fmul_rn(hs[d], inv), w[d]);
+}
+
+// -------------------------------------------------------------- layer_norm
+// out = layer_norm(x) (+ pe[row % n_pos] when pe != nullptr).
+__global__ void __launch_bounds__(kRowWarps * 32)
+layer_norm_kernel(float *__restrict__ out, const float *__restrict__ x, const float *__restrict__ w,
+                  const float *__restrict__ b, const float *__restrict__ pe, int rows, int hidden, int n_pos,
+                  float eps) {
+  extern __shared__ float smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kRowWarps + warp;
+  if (row >= rows) return;
+  float *xs = smem + (size_t)warp * hidden;
+  warp_load_row(xs, x + (size_t)row * hidden, hidden);
+  float mean, inv;
+  ln_stats_ref(xs, hidden, eps, mean, inv);
+  // avx.rs:469-480: fma((x-mean)*inv, w, b) on the 8-aligned body, two
+  // roundings more on the scalar tail.
+  const int body = hidden - hidden % 8;
+  float *o = out + (size_t)row * hidden;
+  const float *p = pe ? pe + (size_t)(row % n_pos) * hidden : nullptr;
+  for (int i = lane; i < hidden; i += 32) {
+    float c = __fmul_rn(__fsub_rn(xs[i], mean), inv);
+    float y = i < body ? fmaf(c, w[i], b[i]) : __fadd_rn(__fmul_rn(c, w[i]), b[i]);
+    if (p) y = __fadd_rn(y, p[i]);
+    o[i] = y;
+  }
+}
+
+// ------------------------------------------------------------------- RoPE
+// cos/sin table rows.  The reference evaluates powf/cosf/sinf in f32 via
+// glibc (decoder.rs:258-281, mod.rs:1235-1240); here each transcendental is
+// evaluated in double and rounded once, i.e. the correctly rounded f32 value,
+// which is what glibc returns except in rare last-ulp cases.  The f32
+// operations around them (exponent, reciprocal, angle) are done in f32 in
+// the reference's order.  positions == nullptr means rows 0..seq-1.
+__global__ void rope_table_kernel(float *__restrict__ cos_out, float *__restrict__ sin_out,
+                                  const int32_t *__restrict__ positions, int seq, int head_dim, float theta) {
+  const int half = head_dim / 2;
+  const long t = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= (long)seq * half) return;
+  const int s = (int)(t / half), d = (int)(t % half);
+  const float pos = positions ? (float)positions[s] : (float)s;
+  const float expo = __fdiv_rn((float)(2 * d), (float)head_dim);
+  const float pw = (float)pow((double)theta, (double)expo);
+  const float inv_freq = __fdiv_rn(1.0f, pw);
+  const float angle = __fmul_rn(pos, inv_freq);
+  const float c = (float)cos((double)angle), sn = (float)sin((double)angle);
+  const size_t r = (size_t)s * head_dim;
+  cos_out[r + d] = c;
+  cos_out[r + half + d] = c;
+  sin_out[r + d] = sn;
+  sin_out[r + half + d] = sn;
+}
+
+// apply_rope_neox (mod.rs:1247-1267): one thread per (row, head, d < half).
+__global__ void apply_rope_kernel(float *__restrict__ x, const float *__restrict__ cos_v,
+                                  const float *__restrict__ sin_v, int seq, int n_heads, int head_dim) {
+  const int half = head_dim / 2;
+  const long t = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= (long)seq * n_heads * half) return;
+  const int d = (int)(t % half);
+  const long sh = t / half;
+  const int s = (int)(sh / n_heads);
+  float *vec = x + sh * head_dim;
+  const float *c = cos_v + (size_t)s * head_dim, *sn = sin_v + (size_t)s * head_dim;
+  const float x1 = vec[d], x2 = vec[half + d];
+  vec[d] = __fadd_rn(__fmul_rn(x1, c[d]), __fmul_rn(-x2, sn[d]));
+  vec[half + d] = __fadd_rn(__fmul_rn(x2, c[half + d]), __fmul_rn(x1, sn[half + d]));
+}
+
+// KvCache row copies (decoder.rs:194-202): one float4 per thread.
+__global__ void kv_append_kernel(float *__restrict__ k_cache, float *__restrict__ v_cache,
+                                 const float *__restrict__ k_new, const float *__restrict__ v_new, int layer,
+                                 int max_seq, int kv_dim, int start_pos, int seq) {
+  const long t = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  const int per_row = kv_dim / 4;
+  if (t >= (long)seq * per_row) return;
+  const int s = (int)(t / per_row), c = (int)(t % per_row);
+  const size_t dst = ((size_t)layer * max_seq + start_pos + s) * kv_dim;
+  reinterpret_cast<float4 *>(k_cache + dst)[c] = reinterpret_cast<const float4 *>(k_new + (size_t)s * kv_dim)[c];
+  reinterpret_cast<float4 *>(v_cache + dst)[c] = reinterpret_cast<const float4 *>(v_new + (size_t)s * kv_dim)[c];
+}
+
+// --------------------------------------------------- fused pre-attn block
+// One CTA per token row, 16 warps.  Work items: the rms_norm of x (item 0),
+// one item per Q/K head (per-head norm + RoPE, K also appended to the cache),
+// and 8 slices of the V row copy.  head_dim is 128: lane L holds elements
+// 4L..4L+3, lanes 0-15 the first half and lanes 16-31 the second, so the
+// RoPE partner of a lane is lane^16.
+constexpr int kPreWarps = 16;
+
+QASR_DEV void head_norm_rope_128(float *dst, float *dst2, const float *src,
+                                 const float *__restrict__ nw, const float *__restrict__ crow,
+                                 const float *__restrict__ srow, float eps, float *hs) {
+  const int lane = threadIdx.x & 31;
+  float4 v = reinterpret_cast<const float4 *>(src)[lane];
+  reinterpret_cast<float4 *>(hs)[lane] = v;
+  __syncwarp();
+  float inv = 0.0f;
+  if (lane == 0) {
+    float s = 0.0f;
+#pragma unroll 16
+    for (int d = 0; d < 128; ++d) s = __fadd_rn(s, __fmul_rn(hs[d], hs[d]));
+    inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, 128.0f), eps)));
+  }
+  inv = __shfl_sync(0xffffffffu, inv, 0);
+  const float4 w4 = reinterpret_cast<const float4 *>(nw)[lane];
+  v.x = __fmul_rn(__fmul_rn(v.x, inv), w4.x);
+  v.y = __fmul_rn(__fmul_rn(v.y, inv), w4.y);
+  v.z = __fmul_rn(__fmul_rn(v.z, inv), w4.z);
+  v.w = __fmul_rn(__fmul_rn(v.w, inv), w4.w);
+  float4 p;
+  p.x = __shfl_xor_sync(0xffffffffu, v.x, 16);
+  p.y = __shfl_xor_sync(0xffffffffu, v.y, 16);
+  p.z = __shfl_xor_sync(0xffffffffu, v.z, 16);
+  p.w = __shfl_xor_sync(0xffffffffu, v.w, 16);
+  const float4 c = reinterpret_cast<const float4 *>(crow)[lane];
+  const float4 s = reinterpret_cast<const float4 *>(srow)[lane];
+  float4 o;
+  if (lane < 16) {  // x1 = own, x2 = partner: x1*c + (-x2)*s
+    o.x = __fadd_rn(__fmul_rn(v.x, c.x), __fmul_rn(-p.x, s.x));
+    o.y = __fadd_rn(__fmul_rn(v.y, c.y), __fmul_rn(-p.y, s.y));
+    o.z = __fadd_rn(__fmul_rn(v.z, c.z), __fmul_rn(-p.z, s.z));
+    o.w = __fadd_rn(__fmul_rn(v.w, c.w), __fmul_rn(-p.w, s.w));
+  } else {          // x2 = own, x1 = partner: x2*c + x1*s
+    o.x = __fadd_rn(__fmul_rn(v.x, c.x), __fmul_rn(p.x, s.x));
+    o.y = __fadd_rn(__fmul_rn(v.y, c.y), __fmul_rn(p.y, s.y));
+    o.z = __fadd_rn(__fmul_rn(v.z, c.z), __fmul_rn(p.z, s.z));
+    o.w = __fadd_rn(__fmul_rn(v.w, c.w), __fmul_rn(p.w, s.w));
+  }
+  reinterpret_cast<float4 *>(dst)[lane] = o;
+  if (dst2) reinterpret_cast<float4 *>(dst2)[lane] = o;
+  __syncwarp();
+}
+
+__global__ void __launch_bounds__(kPreWarps * 32)
+pre_attn_block_kernel(float *__restrict__ x_norm, const float *__restrict__ x, const float *__restrict__ w_in,
+                      int hidden, float *__restrict__ q, const float *__restrict__ k, const float *__restrict__ v,
+                      float *__restrict__ k_out, const float *__restrict__ q_norm_w,
+                      const float *__restrict__ k_norm_w, int n_heads, int n_kv_heads, float eps,
+                      const float *__restrict__ cos_tab, const float *__restrict__ sin_tab, int start_pos,
+                      float *__restrict__ k_cache, float *__restrict__ v_cache, int layer, int max_seq) {
+  extern __shared__ float smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int s = blockIdx.x;
+  const int pos = start_pos + s;
+  const int q_dim = n_heads * 128, kv_dim = n_kv_heads * 128;
+  const float *crow = cos_tab + (size_t)pos * 128, *srow = sin_tab + (size_t)pos * 128;
+  float *cache_row_k = k_cache + ((size_t)layer * max_seq + pos) * kv_dim;
+  float *cache_row_v = v_cache + ((size_t)layer * max_seq + pos) * kv_dim;
+  float *hs = smem + hidden + warp * 128;
+  const int n_items = 1 + n_heads + n_kv_heads + 8;
+  for (int it = warp; it < n_items; it += kPreWarps) {
+    if (it == 0) {
+      warp_load_row(smem, x + (size_t)s * hidden, hidden);
+      const float inv = rms_inv_ref(smem, hidden, eps);
+      float *o = x_norm + (size_t)s * hidden;
+      for (int i = lane; i < hidden; i += 32) o[i] = __fmul_rn(__fmul_rn(smem[i], inv), w_in[i]);
+    } else if (it <= n_heads) {
+      const int h = it - 1;
+      float *qh = q + (size_t)s * q_dim + h * 128;
+      head_norm_rope_128(qh, nullptr, qh, q_norm_w, crow, srow, eps, hs);
+    } else if (it <= n_heads + n_kv_heads) {
+      const int h = it - 1 - n_heads;
+      const float *kh = k + (size_t)s * kv_dim + h * 128;
+      float *ko = k_out ? k_out + (size_t)s * kv_dim + h * 128 : nullptr;
+      head_norm_rope_128(cache_row_k + h * 128, ko, kh, k_norm_w, crow, srow, eps, hs);
+    } else {
+      const int part = it - 1 - n_heads - n_kv_heads;  // 8 slices of the V row
+      const int per = kv_dim / 8;                       // floats per slice (multiple of 4)
+      const float4 *src = reinterpret_cast<const float4 *>(v + (size_t)s * kv_dim + part * per);
+      float4 *dst = reinterpret_cast<float4 *>(cache_row_v + part * per);
+      for (int i = lane; i < per / 4; i += 32) dst[i] = src[i];
+    }
+  }
+}
+
+// ---------------------------------------------------------- sinusoidal PE
+// sinusoidal_pe (mod.rs:1213-1226): f32 steps in the reference's order, each
+// transcendental evaluated in double and rounded once (see rope_table_kernel).
+__global__ void sinusoidal_pe_kernel(float *__restrict__ pe, int n_pos, int d_model) {
+  const int half = d_model / 2;
+  const long t = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= (long)n_pos * half) return;
+  const int p = (int)(t / half), d = (int)(t % half);
+  const float ln10k = (float)log(10000.0);
+  const float log_ts = __fdiv_rn(ln10k, (float)(half - 1));
+  const float arg = __fmul_rn(-(float)d, log_ts);
+  const float inv_ts = (float)exp((double)arg);
+  const float angle = __fmul_rn((float)p, inv_ts);
+  pe[(size_t)p * d_model + d] = (float)sin((double)angle);
+  pe[(size_t)p * d_model + half + d] = (float)cos((double)angle);
+}
+
+}  // namespace qasr
+
+using namespace qasr;
+
+static inline cudaStream_t S(void *s) { return reinterpret_cast<cudaStream_t>(s); }
+static inline bool al16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+extern "C" int qasr_rms_norm(float *out, const float *x, const float *w, int seq, int hidden, float eps,
+                             void *stream) {
+  if (!out || !x || !w || seq < 0 || hidden <= 0) {
+    set_error("qasr_rms_norm: invalid arguments (seq=%d hidden=%d)", seq, hidden);
+    return QASR_ERR_INVALID;
+  }
+  if (seq == 0) return QASR_OK;
+  const size_t smem = (size_t)kRowWarps * hidden * sizeof(float);
+  if (smem > 200 * 1024) {
+    set_error("qasr_rms_norm: hidden=%d too large", hidden);
+    return QASR_ERR_UNSUPPORTED;
+  }
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(rms_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  rms_norm_kernel<<<ceil_div(seq, kRowWarps), kRowWarps * 32, smem, S(stream)>>>(out, x, w, seq, hidden, eps);
+  return launch_status("qasr_rms_norm");
+}
+
+extern "C" int qasr_rms_norm_per_head(float *x, const float *w, int seq, int n_heads, int head_dim, float eps,
+                                      void *stream) {
+  if (!x || !w || seq < 0 || n_heads <= 0 || head_dim <= 0 || head_dim > 4096) {
+    set_error("qasr_rms_norm_per_head: invalid arguments");
+    return QASR_ERR_INVALID;
+  }
+  if (seq == 0) return QASR_OK;
+  const long tasks = (long)seq * n_heads;
+  rms_norm_per_head_kernel<<<ceil_div(tasks, 8), 256, 8 * head_dim * sizeof(float), S(stream)>>>(
+      x, w, seq, n_heads, head_dim, eps);
+  return launch_status("qasr_rms_norm_per_head");
+}
+
+extern "C" int qasr_layer_norm(float *out, const float *x, const float *w, const float *b, int seq, int hidden,
+                               float eps, void *stream) {
+  if (!out || !x || !w || !b || seq < 0 || hidden <= 0) {
+    set_error("qasr_layer_norm: invalid arguments");
+    return QASR_ERR_INVALID;
+  }
+  if (seq == 0) return QASR_OK;
+  const size_t smem = (size_t)kRowWarps * hidden * sizeof(float);
+  if (smem > 200 * 1024) {
+    set_error("qasr_layer_norm: hidden=%d too large", hidden);
+    return QASR_ERR_UNSUPPORTED;
+  }
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(layer_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  layer_norm_kernel<<<ceil_div(seq, kRowWarps), kRowWarps * 32, smem, S(stream)>>>(out, x, w, b, nullptr, seq,
+                                                                                   hidden, 1, eps);
+  return launch_status("qasr_layer_norm");
+}
+
+extern "C" int qasr_ln_pe(float *out, const float *x, const float *w, const float *b, const float *pe, int rows,
+                          int hidden, int n_pos, float eps, void *stream) {
+  if (!out || !x || !w || !b || !pe || rows < 0 || hidden <= 0 || n_pos <= 0) {
+    set_error("qasr_ln_pe: invalid arguments");
+    return QASR_ERR_INVALID;
+  }
+  if (rows == 0) return QASR_OK;
+  const size_t smem = (size_t)kRowWarps * hidden * sizeof(float);
+  if (smem > 200 * 1024) {
+    set_error("qasr_ln_pe: hidden=%d too large", hidden);
+    return QASR_ERR_UNSUPPORTED;
+  }
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(layer_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  layer_norm_kernel<<<ceil_div(rows, kRowWarps), kRowWarps * 32, smem, S(stream)>>>(out, x, w, b, pe, rows, hidden,
+                                                                                    n_pos, eps);
+  return launch_status("qasr_ln_pe");
+}
+
+extern "C" int qasr_compute_rope_neox(float *cos_out, float *sin_out, const int32_t *positions, int seq,
+                                      int head_dim, float theta, void *stream) {
+  if (!cos_out || !sin_out || !positions || seq < 0 || head_dim <= 0 || (head_dim & 1)) {
+    set_error("qasr_compute_rope_neox: invalid arguments");
+    return QASR_ERR_INVALID;
+  }
+  if (seq == 0) return QASR_OK;
+  const long n = (long)seq * (head_dim / 2);
+  rope_table_kernel<<<ceil_div(n, 256), 256, 0, S(stream)>>>(cos_out, sin_out, positions, seq, head_dim, theta);
+  return launch_status("qasr_compute_rope_neox");
+}
+
+extern "C" int qasr_rope_cache_table(float *cos_out, float *sin_out, int n_pos, int head_dim, float theta,
+                                     void *stream) {
+  if (!cos_out || !sin_out || n_pos < 0 || head_dim <= 0 || (head_dim & 1)) {
+    set_error("qasr_rope_cache_table: invalid arguments");
+    return QASR_ERR_INVALID;
+  }
+  if (n_pos == 0) return QASR_OK;
+  const long n = (long)n_pos * (head_dim / 2);
+  rope_table_kernel<<<ceil_div(n, 256), 256, 0, S(stream)>>>(cos_out, sin_out, nullptr, n_pos, head_dim, theta);
+  return launch_status("qasr_rope_cache_table");
+}
+
+extern "C" int qasr_apply_rope_neox(float *x, const float *cos_v, const float *sin_v, int seq, int n_heads,
+                                    int head_dim, void *stream) {
+  if (!x || !cos_v || !sin_v || seq < 0 || n_heads <= 0 || head_dim <= 0 || (head_dim & 1)) {
+    set_error("qasr_apply_rope_neox: invalid arguments");
+    return QASR_ERR_INVALID;
+  }
+  if (seq == 0) return QASR_OK;
+  const long n = (long)seq * n_heads * (head_dim / 2);
+  apply_rope_kernel<<<ceil_div(n, 256), 256, 0, S(stream)>>>(x, cos_v, sin_v, seq, n_heads, head_dim);
+  return launch_status("qasr_apply_rope_neox");
+}
+
+extern "C" int qasr_kv_append(float *k_cache, float *v_cache, const float *k_new, const float *v_new, int layer,
+                              int max_seq, int kv_dim, int start_pos, int seq, void *stream) {
+  if (!k_cache || !v_cache || !k_new || !v_new || layer < 0 || max_seq <= 0 || kv_dim <= 0 || (kv_dim & 3) ||
+      start_pos < 0 || seq < 0 || start_pos + seq > max_seq || !al16(k_cache) || !al16(v_cache) || !al16(k_new) ||
+      !al16(v_new)) {
+    set_error("qasr_kv_append: invalid arguments (start_pos=%d seq=%d max_seq=%d kv_dim=%d, 16-byte aligned "
+              "pointers required)", start_pos, seq, max_seq, kv_dim);
+    return QASR_ERR_INVALID;
+  }
+  if (seq == 0) return QASR_OK;
+  const long n = (long)seq * (kv_dim / 4);
+  kv_append_kernel<<<ceil_div(n, 256), 256, 0, S(stream)>>>(k_cache, v_cache, k_new, v_new, layer, max_seq, kv_dim,
+                                                            start_pos, seq);
+  return launch_status("qasr_kv_append");
+}
+
+extern "C" int qasr_pre_attn_block(float *x_norm, const float *x, const float *w_in, int seq, int hidden, float *q,
+                                   const float *k, const float *v, float *k_out, const float *q_norm_w,
+                                   const float *k_norm_w, int n_heads, int n_kv_heads, int head_dim, float eps,
+                                   const float *cos_tab, const float *sin_tab, int start_pos, float *k_cache,
+                                   float *v_cache, int layer, int max_seq, void *stream) {
+  if (!x_norm || !x || !w_in || !q || !k || !v || !q_norm_w || !k_norm_w || !cos_tab || !sin_tab || !k_cache ||
+      !v_cache || seq < 0 || hidden <= 0 || n_heads <= 0 || n_kv_heads <= 0 || start_pos < 0 || layer < 0 ||
+      start_pos + seq > max_seq) {
+    set_error("qasr_pre_attn_block: invalid arguments");
+    return QASR_ERR_INVALID;
+  }
+  if (!al16(x) || !al16(q) || !al16(k) || !al16(v) || (k_out && !al16(k_out)) || !al16(q_norm_w) ||
+      !al16(k_norm_w) || !al16(cos_tab) || !al16(sin_tab) || !al16(k_cache) || !al16(v_cache)) {
+    set_error("qasr_pre_attn_block: all vector operands must be 16-byte aligned");
+    return QASR_ERR_INVALID;
+  }
+  if (head_dim != 128 || (hidden & 3) || ((n_kv_heads * 128 / 8) & 3)) {
+    set_error("qasr_pre_attn_block: head_dim must be 128 (got %d)", head_dim);
+    return QASR_ERR_UNSUPPORTED;
+  }
+  if (seq == 0) return QASR_OK;
+  const size_t smem = ((size_t)hidden + kPreWarps * 128) * sizeof(float);
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(pre_attn_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  pre_attn_block_kernel<<<seq, kPreWarps * 32, smem, S(stream)>>>(x_norm, x, w_in, hidden, q, k, v, k_out, q_norm_w,
+                                                                  k_norm_w, n_heads, n_kv_heads, eps, cos_tab,
+                                                                  sin_tab, start_pos, k_cache, v_cache, layer,
+                                                                  max_seq);
+  return launch_status("qasr_pre_attn_block");
+}
+
+extern "C" int qasr_sinusoidal_pe(float *pe, int n_pos, int d_model, void *stream) {
+  if (!pe || n_pos < 0 || d_model < 4 || (d_model & 1)) {
+    set_error("qasr_sinusoidal_pe: invalid arguments");
+    return QASR_ERR_INVALID;
+  }
+  if (n_pos == 0) return QASR_OK;
+  const long n = (long)n_pos * (d_model / 2);
+  sinusoidal_pe_kernel<<<ceil_div(n, 256), 256, 0, S(stream)>>>(pe, n_pos, d_model);
+  return launch_status("qasr_sinusoidal_pe");
+}

@@ -1,0 +1,63 @@
+// runtime.cu -- error reporting, version, per-device scratch of the
+// kernel-level fused entries.
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+
+#include "common.cuh"
+#include "matvec.cuh"
+
+namespace qasr {
+
+static thread_local char g_err[512] = "";
+
+void set_error(const char *fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+}
+
+int cuda_status(cudaError_t e, const char *what) {
+  if (e == cudaSuccess) return QASR_OK;
+  set_error("%s: %s", what, cudaGetErrorString(e));
+  return e == cudaErrorMemoryAllocation ? QASR_ERR_ALLOC : QASR_ERR_CUDA;
+}
+
+int launch_status(const char *what) { return cuda_status(cudaGetLastError(), what); }
+
+struct NormScratch {
+  float *buf = nullptr;
+  size_t cap = 0;
+};
+static NormScratch g_norm_scratch[64];
+static std::mutex g_scratch_mu;
+
+int mv_norm_scratch(float **buf, size_t n_floats) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return QASR_ERR_INVALID;
+  std::lock_guard<std::mutex> lk(g_scratch_mu);
+  NormScratch &s = g_norm_scratch[dev];
+  if (s.cap < n_floats) {
+    if (s.buf) {
+      cudaDeviceSynchronize();
+      cudaFree(s.buf);
+      s.buf = nullptr;
+      s.cap = 0;
+    }
+    size_t want = n_floats < 65536 ? 65536 : n_floats;
+    if (cudaMalloc(&s.buf, want * sizeof(float)) != cudaSuccess) {
+      set_error("kernel-level scratch: cudaMalloc(%zu) failed", want * sizeof(float));
+      return QASR_ERR_ALLOC;
+    }
+    s.cap = want;
+  }
+  *buf = s.buf;
+  return QASR_OK;
+}
+
+}  // namespace qasr
+
+extern "C" const char *qasr_last_error(void) { return qasr::g_err; }
+extern "C" const char *qasr_version(void) { return "qwenasr_b200 0.1.0 (sm_100a)"; }

@@ -1,0 +1,136 @@
+"""INT8 decoder engine on one B200: the host face of qasr_decoder.
+
+Mirrors DecoderInt8 + KvCache + decoder_forward_int8 of the reference
+(crates/qwen-asr/src/decoder.rs:130-228, 652-965) for a batch of up to 8
+independent sequences: weights are uploaded once, each sequence owns a KV
+cache slot, and one call advances every sequence by one greedy token.  All
+math runs in libqwenasr_b200.so; this module only owns handles and buffers.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+import torch
+
+from . import _lib
+
+LAYER_KEYS = ("wq", "wq_s", "wk", "wk_s", "wv", "wv_s", "wo", "wo_s", "gate_up", "gate_up_s", "down", "down_s",
+              "q_norm", "k_norm", "input_norm", "post_attn_norm")
+
+
+class _DevArray:
+    """__cuda_array_interface__ view of engine-owned device memory."""
+
+    def __init__(self, ptr, shape, typestr="<f4"):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (int(ptr), False),
+                                         "version": 3, "strides": None}
+
+
+def _host_or_dev_ptr(a, keep):
+    if isinstance(a, torch.Tensor):
+        if not a.is_contiguous():
+            a = a.contiguous()
+        keep.append(a)
+        return C.c_void_p(a.data_ptr())
+    arr = np.ascontiguousarray(a)
+    keep.append(arr)
+    return C.c_void_p(arr.ctypes.data)
+
+
+class Decoder:
+    """One qasr_decoder: config dict keys hidden, inter, n_layers, n_heads,
+    n_kv_heads, head_dim, vocab, eps, theta."""
+
+    def __init__(self, cfg: dict, device: int = 0, max_batch: int = 8, max_seq: int = 2048,
+                 embed_is_int8: bool = False):
+        self.cfg = dict(cfg)
+        self.device = device
+        self.max_batch = max_batch
+        self.max_seq = max_seq
+        c = _lib.DecoderConfig(cfg["hidden"], cfg["inter"], cfg["n_layers"], cfg["n_heads"], cfg["n_kv_heads"],
+                               cfg["head_dim"], cfg["vocab"], cfg["eps"], cfg["theta"], max_batch, max_seq,
+                               1 if embed_is_int8 else 0)
+        lib = _lib.load()
+        self._h = lib.qasr_decoder_create(C.byref(c), device)
+        if not self._h:
+            raise _lib.QasrError(_lib.QASR_ERR_INVALID, "qasr_decoder_create", _lib.last_error())
+        self.kv_dim = cfg["n_kv_heads"] * cfg["head_dim"]
+
+    # ---------------------------------------------------------------- weights
+    def set_layer(self, i: int, w: dict) -> None:
+        keep = []
+        s = _lib.DecLayerWeights(*[_host_or_dev_ptr(w[k], keep) for k in LAYER_KEYS])
+        _lib.call("qasr_decoder_set_layer", self._h, i, C.byref(s))
+
+    def set_globals(self, embed, norm, lm_head=None, lm_head_s=None, embed_scales=None) -> None:
+        keep = []
+        _lib.call("qasr_decoder_set_globals", self._h, _host_or_dev_ptr(embed, keep),
+                  _host_or_dev_ptr(embed_scales, keep) if embed_scales is not None else None,
+                  _host_or_dev_ptr(norm, keep), _host_or_dev_ptr(lm_head, keep) if lm_head is not None else None,
+                  _host_or_dev_ptr(lm_head_s, keep) if lm_head_s is not None else None)
+
+    # --------------------------------------------------------------- caches
+    def kv(self, slot: int):
+        """(k, v) torch views of sequence `slot`'s cache [n_layers, max_seq, kv_dim]."""
+        k = C.c_void_p()
+        v = C.c_void_p()
+        _lib.call("qasr_decoder_kv", self._h, slot, C.byref(k), C.byref(v))
+        shape = (self.cfg["n_layers"], self.max_seq, self.kv_dim)
+        with torch.cuda.device(self.device):
+            return (torch.as_tensor(_DevArray(k.value, shape), device=f"cuda:{self.device}"),
+                    torch.as_tensor(_DevArray(v.value, shape), device=f"cuda:{self.device}"))
+
+    @property
+    def stream(self) -> torch.cuda.ExternalStream:
+        return torch.cuda.ExternalStream(_lib.load().qasr_decoder_stream(self._h), device=f"cuda:{self.device}")
+
+    def keep_logits(self, enable: bool = True) -> None:
+        _lib.call("qasr_decoder_keep_logits", self._h, 1 if enable else 0)
+
+    def logits(self, M: int):
+        p = _lib.load().qasr_decoder_logits(self._h)
+        if not p:
+            return None
+        return torch.as_tensor(_DevArray(p, (M, self.cfg["vocab"])), device=f"cuda:{self.device}")
+
+    # ----------------------------------------------------------------- step
+    def step(self, tokens, positions) -> np.ndarray:
+        """decoder_forward_int8 for len(tokens) sequences (host buffers in/out)."""
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        p = np.ascontiguousarray(positions, dtype=np.int32)
+        out = np.empty_like(t)
+        _lib.call("qasr_decoder_step", self._h, t.ctypes.data_as(C.c_void_p), p.ctypes.data_as(C.c_void_p), t.size,
+                  out.ctypes.data_as(C.c_void_p))
+        return out
+
+    def step_device(self, tokens: torch.Tensor, positions: torch.Tensor, out: torch.Tensor) -> None:
+        """Same step on device int32 tensors, enqueued on the engine stream."""
+        _lib.call("qasr_decoder_step_device", self._h, C.c_void_p(tokens.data_ptr()),
+                  C.c_void_p(positions.data_ptr()), tokens.numel(), C.c_void_p(out.data_ptr()))
+
+    def profile_step(self, tokens, positions) -> dict:
+        """One eager step with CUDA events around each kernel: {class: (ms, launches)}."""
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        p = np.ascontiguousarray(positions, dtype=np.int32)
+        n = len(_lib.KERNEL_CLASSES)
+        ms = (C.c_float * n)()
+        cnt = (C.c_int * n)()
+        _lib.call("qasr_decoder_profile_step", self._h, t.ctypes.data_as(C.c_void_p), p.ctypes.data_as(C.c_void_p),
+                  t.size, ms, cnt, n)
+        return {k: (float(ms[i]), int(cnt[i])) for i, k in enumerate(_lib.KERNEL_CLASSES)}
+
+    def step_bytes(self, positions) -> int:
+        p = np.ascontiguousarray(positions, dtype=np.int32)
+        return int(_lib.load().qasr_decoder_step_bytes(self._h, p.ctypes.data_as(C.c_void_p), p.size))
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            _lib.load().qasr_decoder_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -1,0 +1,95 @@
+"""Seeded synthetic inputs and random-init weights of the benchmark configs.
+
+No model checkpoints exist on the build or GPU machines, so weights are
+random with the architecture's shapes (config.rs:56-82 defaults, 0.6B/1.7B
+shapes of config.rs:110-156):  matrices ~ N(0, 0.02) quantised per output
+channel to INT8 by the qwen-asr-quantize rule (quantize.rs:633-662), norm
+weights ~ N(1, 0.02), embedding table ~ N(0, 0.02).  The gate/up matrices
+are stored with rows interleaved g0,u0,g1,u1,... as DecoderInt8::load does
+(decoder.rs:699-719).
+
+Two generators with the same distributions:
+  * layer_weights_np: numpy on the host (parity tests, CPU baseline);
+  * layer_weights_gpu: torch on the GPU, quantised by the library's own
+    qasr_quantize_f32_to_int8 kernel (benchmarks at full size).
+"""
+from __future__ import annotations
+
+import numpy as np
+
+DEC_0_6B = dict(hidden=1024, inter=3072, n_layers=28, n_heads=16, n_kv_heads=8, head_dim=128, vocab=151936,
+                eps=1e-6, theta=1e6)
+DEC_1_7B = dict(DEC_0_6B, hidden=2048, inter=6144)
+
+
+def quantize_np(w: np.ndarray):
+    """quantize_f32_to_int8 (quantize.rs:633-662) in numpy: absmax/127 scales,
+    round half away from zero, clamp to [-128, 127]."""
+    w = np.asarray(w, np.float32)
+    absmax = np.abs(w).max(axis=1)
+    scales = (absmax / np.float32(127.0)).astype(np.float32)
+    with np.errstate(divide="ignore"):
+        inv = np.where(absmax > 0, np.float32(127.0) / absmax, np.float32(0.0)).astype(np.float32)
+    v = (w * inv[:, None]).astype(np.float32)
+    a = np.abs(v)
+    r = np.floor(a)
+    q = np.copysign(r + (a - r >= np.float32(0.5)), v)  # a - r is exact: half away from zero
+    return np.clip(q, -128, 127).astype(np.int8), scales
+
+
+def interleave_rows(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    out = np.empty((a.shape[0] * 2,) + a.shape[1:], a.dtype)
+    out[0::2] = a
+    out[1::2] = b
+    return out
+
+
+def layer_weights_np(cfg: dict, rng: np.random.Generator, quantize=quantize_np) -> dict:
+    """One decoder layer (DecLayerInt8, decoder.rs:652-663) as numpy arrays."""
+    H, I, hd = cfg["hidden"], cfg["inter"], cfg["head_dim"]
+    q_dim, kv = cfg["n_heads"] * hd, cfg["n_kv_heads"] * hd
+    out = {}
+    for name, shape in (("wq", (q_dim, H)), ("wk", (kv, H)), ("wv", (kv, H)), ("wo", (H, q_dim)),
+                        ("down", (H, I))):
+        out[name], out[name + "_s"] = quantize((rng.standard_normal(shape, np.float32) * np.float32(0.02)))
+    g, gs = quantize(rng.standard_normal((I, H), np.float32) * np.float32(0.02))
+    u, us = quantize(rng.standard_normal((I, H), np.float32) * np.float32(0.02))
+    out["gate_up"] = interleave_rows(g, u)
+    out["gate_up_s"] = interleave_rows(gs, us)
+    for name, n in (("q_norm", hd), ("k_norm", hd), ("input_norm", H), ("post_attn_norm", H)):
+        out[name] = (1.0 + 0.02 * rng.standard_normal(n)).astype(np.float32)
+    return out
+
+
+def decoder_weights_np(cfg: dict, seed: int, quantize=quantize_np) -> dict:
+    """Full random decoder: layers, f32 embedding table, final norm, INT8 lm head
+    (quantised from the embedding table, i.e. tied weights in INT8 form)."""
+    rng = np.random.default_rng(seed)
+    layers = [layer_weights_np(cfg, rng, quantize) for _ in range(cfg["n_layers"])]
+    emb = rng.standard_normal((cfg["vocab"], cfg["hidden"]), np.float32) * np.float32(0.02)
+    lm, lms = quantize(emb)
+    norm = (1.0 + 0.02 * rng.standard_normal(cfg["hidden"])).astype(np.float32)
+    return dict(cfg=dict(cfg), layers=layers, embed=emb, norm=norm, lm_head=lm, lm_head_s=lms)
+
+
+def layer_weights_gpu(cfg: dict, gen, device, quantize_gpu) -> dict:
+    """Same distributions on the GPU (torch.Generator `gen`); quantize_gpu(w)
+    -> (int8, scales) is the library's quantiser."""
+    import torch
+    H, I, hd = cfg["hidden"], cfg["inter"], cfg["head_dim"]
+    q_dim, kv = cfg["n_heads"] * hd, cfg["n_kv_heads"] * hd
+
+    def rn(*shape):
+        return torch.randn(*shape, generator=gen, device=device, dtype=torch.float32) * 0.02
+
+    out = {}
+    for name, shape in (("wq", (q_dim, H)), ("wk", (kv, H)), ("wv", (kv, H)), ("wo", (H, q_dim)),
+                        ("down", (H, I))):
+        out[name], out[name + "_s"] = quantize_gpu(rn(*shape))
+    g, gs = quantize_gpu(rn(I, H))
+    u, us = quantize_gpu(rn(I, H))
+    out["gate_up"] = torch.stack([g, u], 1).reshape(2 * I, H).contiguous()
+    out["gate_up_s"] = torch.stack([gs, us], 1).reshape(2 * I).contiguous()
+    for name, n in (("q_norm", hd), ("k_norm", hd), ("input_norm", H), ("post_attn_norm", H)):
+        out[name] = 1.0 + 0.02 * torch.randn(n, generator=gen, device=device, dtype=torch.float32)
+    return out
