@@ -10,8 +10,11 @@
 //    CTAs, each CTA serves both query heads of the GQA group so every K/V row
 //    is read from HBM exactly once, and the last CTA of a (sequence, kv head)
 //    merges the partial softmax states (counter + threadfence, no spin).
-#include "common.cuh"
+#include <cudaTypedefs.h>
+
 #include "attention.cuh"
+#include "common.cuh"
+#include "tma.cuh"
 
 namespace qasr {
 
@@ -62,51 +65,136 @@ causal_attention_kernel(float *__restrict__ out, const float *__restrict__ q, co
 }
 
 // ------------------------------------------------------------------- decode
-// grid = (splits, n_kv_heads, M), 4 warps.  head_dim 128, GQA group size G.
+// Persistent flash-decoding.  The keys of all (sequence, kv head) pairs are
+// laid end to end and cut into gridDim equal ranges, so every SM streams the
+// same number of K/V bytes whatever the batch and lengths.  A CTA walks its
+// range as segments (one per pair it touches) of 64-key tiles; thread 0 keeps
+// kAttnStages K+V tile pairs in flight with 2D TMA loads (box: 64 rows x one
+// 128-float head slice, no multicast).  Each of the 4 warps scores 16 keys of
+// a tile for both query heads of the GQA group (every K/V byte is read from
+// HBM once), keeps an online-softmax state, and the CTA merges its warps at
+// the end of a segment.  A pair split over several CTAs is merged by the last
+// one to finish (counter + threadfence, slots in CTA order: deterministic).
+struct AttnSmall {
+  uint64_t bar[kAttnStages];
+  int nseg;
+  int seg_pair[128], seg_a[128], seg_b[128];
+};
+
+QASR_DEV void tma_load_2d(float *dst, const CUtensorMap *tm, int x, int y, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(smem_u32(dst)),
+      "l"(tm), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
 template <int G>
-__global__ void __launch_bounds__(kAttnWarps * 32)
-attn_decode_kernel(AttnDecodeParams p) {
-  __shared__ float sp[kAttnWarps][G][32];          // per-warp softmax weights of a key group
+__global__ void __launch_bounds__(kAttnWarps * 32, 1)
+attn_decode_kernel(const __grid_constant__ AttnDecodeParams p) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  constexpr int TILE_F = kAttnTile * 128;  // floats per K (or V) tile
+  float *tiles = reinterpret_cast<float *>(smem_raw);
+  AttnSmall &sm = *reinterpret_cast<AttnSmall *>(smem_raw + (size_t)kAttnStages * 2 * TILE_F * 4);
+  __shared__ float sp[kAttnWarps][G][16];
   __shared__ float wm[kAttnWarps][G], wl[kAttnWarps][G];
   __shared__ float4 wo[kAttnWarps][G][32];
-  __shared__ bool last;
+  __shared__ int s_last;
+
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int split = blockIdx.x, kvh = blockIdx.y, m = blockIdx.z;
-  // positions outside [0, max_seq) were flagged by the append kernel; clamp so
-  // nothing here reads outside the cache
-  const int len = max(1, min(p.positions[m] + 1, p.max_seq));
-  const int chunk = ((len + p.splits - 1) / p.splits + 31) & ~31;
-  const int begin = split * chunk, end = min(len, begin + chunk);
-  const float *kc = p.k_cache + (size_t)m * p.seq_stride + (size_t)p.layer * p.max_seq * p.kv_dim + kvh * 128 + 4 * lane;
-  const float *vc = p.v_cache + (size_t)m * p.seq_stride + (size_t)p.layer * p.max_seq * p.kv_dim + kvh * 128 + 4 * lane;
+  const int n_kv = p.n_kv_heads, n_pairs = p.M * n_kv;
+  auto len_of = [&](int pair) { return max(1, min(p.positions[pair / n_kv] + 1, p.max_seq)); };
+  long long Tk = 0;
+  for (int pr = 0; pr < n_pairs; ++pr) Tk += len_of(pr);
+  const long long Gd = gridDim.x, c = blockIdx.x;
+  const long long t0 = c * Tk / Gd, t1 = (c + 1) * Tk / Gd;
 
-  float4 qv[G];
-#pragma unroll
-  for (int g = 0; g < G; ++g)
-    qv[g] = *reinterpret_cast<const float4 *>(p.q + (size_t)m * p.q_stride + (kvh * G + g) * 128 + 4 * lane);
-  float mx[G], sum[G];
-  float4 o[G];
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    mx[g] = -INFINITY;
-    sum[g] = 0.0f;
-    o[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (threadIdx.x == 0) {
+    int ns = 0;
+    long long off = 0;
+    for (int pr = 0; pr < n_pairs && ns < 128; ++pr) {
+      const long long len = len_of(pr);
+      const long long a = max(off, t0), b = min(off + len, t1);
+      if (a < b) {
+        sm.seg_pair[ns] = pr;
+        sm.seg_a[ns] = (int)(a - off);
+        sm.seg_b[ns] = (int)(b - off);
+        ++ns;
+      }
+      off += len;
+    }
+    sm.nseg = ns;
+    for (int st = 0; st < kAttnStages; ++st) mbar_init(&sm.bar[st], 1);
   }
+  mbar_fence_init();
+  __syncthreads();
+  const int nseg = sm.nseg;
 
-  for (int base = begin + warp * 32; base < end; base += kAttnWarps * 32) {
-    const int nkeys = min(32, end - base);
-    // Scores of this 32-key group: per half of 16 keys, each lane forms the
-    // G*16 partial dots of its 4 dims, a reduce-scatter leaves one full dot
-    // per lane group, and the owners park them in shared memory.
+  // tile cursor shared by producer and consumers (advanced in the same order)
+  auto tiles_of = [&](int sg) { return (sm.seg_b[sg] - sm.seg_a[sg] + kAttnTile - 1) / kAttnTile; };
+  int total = 0;
+  for (int sg = 0; sg < nseg; ++sg) total += tiles_of(sg);
+
+  int is = 0, it = 0;  // producer cursor (thread 0)
+  auto issue_next = [&](int item) {
+    while (it >= tiles_of(is)) {
+      it = 0;
+      ++is;
+    }
+    const int pr = sm.seg_pair[is], m = pr / n_kv, kvh = pr % n_kv;
+    const int row = (m * p.n_layers + p.layer) * p.max_seq + sm.seg_a[is] + it * kAttnTile;
+    const int st = item % kAttnStages;
+    mbar_arrive_expect_tx(&sm.bar[st], 2 * TILE_F * 4);
+    tma_load_2d(tiles + (size_t)(2 * st) * TILE_F, &p.tm_k, kvh * 128, row, &sm.bar[st]);
+    tma_load_2d(tiles + (size_t)(2 * st + 1) * TILE_F, &p.tm_v, kvh * 128, row, &sm.bar[st]);
+    ++it;
+  };
+  // q and the newest K/V row are written by the previous kernel: wait for it
+  // before the first tile load (the tile holding the newest row may be any)
+  pdl_wait();
+  pdl_launch_dependents();
+  if (threadIdx.x == 0)
+    for (int i = 0; i < total && i < kAttnStages; ++i) issue_next(i);
+
+  float mx[G], sum[G];
+  float4 o[G], qv[G];
+  int cs = 0, ct = 0;  // consumer cursor
+  int cur_pair = -1;
+  for (int i = 0; i < total; ++i) {
+    while (ct >= tiles_of(cs)) {
+      ct = 0;
+      ++cs;
+    }
+    const int pr = sm.seg_pair[cs], m = pr / n_kv, kvh = pr % n_kv;
+    if (pr != cur_pair) {  // new segment: load q, reset state
+      cur_pair = pr;
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
+      for (int g = 0; g < G; ++g) {
+        qv[g] = *reinterpret_cast<const float4 *>(p.q + (size_t)m * p.q_stride + (kvh * G + g) * 128 + 4 * lane);
+        mx[g] = -INFINITY;
+        sum[g] = 0.0f;
+        o[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    const int st = i % kAttnStages;
+    const bool ok = mbar_wait(&sm.bar[st], (unsigned)((i / kAttnStages) & 1));
+    if (__syncthreads_or(!ok)) {
+      if (threadIdx.x == 0 && p.err) atomicExch(p.err, -QASR_ERR_TIMEOUT);
+      for (int k2 = i; k2 < total && k2 < i + kAttnStages; ++k2)
+        mbar_wait(&sm.bar[k2 % kAttnStages], (unsigned)((k2 / kAttnStages) & 1));
+      return;
+    }
+    const float *kt = tiles + (size_t)(2 * st) * TILE_F;
+    const float *vt = tiles + (size_t)(2 * st + 1) * TILE_F;
+    const int nk = min(kAttnTile, sm.seg_b[cs] - sm.seg_a[cs] - ct * kAttnTile);
+    const int k0 = warp * 16;
+    const int nkw = max(0, min(16, nk - k0));  // keys of this warp in the tile
+    if (nkw > 0) {
       constexpr int V = G * 16;
       float part[V];
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
-        const int key = half * 16 + j;
-        float4 kv = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (key < nkeys) kv = *reinterpret_cast<const float4 *>(kc + (size_t)(base + key) * p.kv_dim);
+        const float4 kv = *reinterpret_cast<const float4 *>(kt + (size_t)(k0 + j) * 128 + 4 * lane);
 #pragma unroll
         for (int g = 0; g < G; ++g) {
           float d = __fmul_rn(qv[g].x, kv.x);
@@ -118,131 +206,209 @@ attn_decode_kernel(AttnDecodeParams p) {
       }
       const float tot = warp_reduce_scatter<V>(part);
       const int idx = reduce_index<V>(lane);
-      if ((lane & (32 / V - 1)) == 0) sp[warp][idx / 16][half * 16 + idx % 16] = __fmul_rn(tot, p.scale);
-    }
-    __syncwarp();
-    float score[G];
-#pragma unroll
-    for (int g = 0; g < G; ++g) score[g] = lane < nkeys ? sp[warp][g][lane] : -INFINITY;
-    __syncwarp();
-    // online softmax over the group
-    float corr[G];
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const float nmax = fmaxf(mx[g], warp_max(score[g]));
-      corr[g] = mx[g] == -INFINITY ? 0.0f : expf(__fsub_rn(mx[g], nmax));
-      const float pj = lane < nkeys ? expf(__fsub_rn(score[g], nmax)) : 0.0f;
-      sum[g] = __fadd_rn(__fmul_rn(sum[g], corr[g]), warp_sum(pj));
-      mx[g] = nmax;
-      sp[warp][g][lane] = pj;
-      o[g].x = __fmul_rn(o[g].x, corr[g]);
-      o[g].y = __fmul_rn(o[g].y, corr[g]);
-      o[g].z = __fmul_rn(o[g].z, corr[g]);
-      o[g].w = __fmul_rn(o[g].w, corr[g]);
-    }
-    __syncwarp();
-    for (int j = 0; j < nkeys; ++j) {
-      const float4 vv = *reinterpret_cast<const float4 *>(vc + (size_t)(base + j) * p.kv_dim);
+      if ((lane & (32 / V - 1)) == 0) sp[warp][idx / 16][idx % 16] = __fmul_rn(tot, p.scale);
+      __syncwarp();
+      float corr[G], pj[G];
 #pragma unroll
       for (int g = 0; g < G; ++g) {
-        const float w = sp[warp][g][j];
-        o[g].x = fmaf(w, vv.x, o[g].x);
-        o[g].y = fmaf(w, vv.y, o[g].y);
-        o[g].z = fmaf(w, vv.z, o[g].z);
-        o[g].w = fmaf(w, vv.w, o[g].w);
+        const float sc = lane < nkw ? sp[warp][g][lane & 15] : -INFINITY;
+        const float nmax = fmaxf(mx[g], warp_max(sc));
+        corr[g] = mx[g] == -INFINITY ? 0.0f : expf(__fsub_rn(mx[g], nmax));
+        pj[g] = lane < nkw ? expf(__fsub_rn(sc, nmax)) : 0.0f;
+        sum[g] = __fadd_rn(__fmul_rn(sum[g], corr[g]), warp_sum(pj[g]));
+        mx[g] = nmax;
+      }
+      __syncwarp();
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        if (lane < 16) sp[warp][g][lane] = pj[g];
+        o[g].x = __fmul_rn(o[g].x, corr[g]);
+        o[g].y = __fmul_rn(o[g].y, corr[g]);
+        o[g].z = __fmul_rn(o[g].z, corr[g]);
+        o[g].w = __fmul_rn(o[g].w, corr[g]);
+      }
+      __syncwarp();
+#pragma unroll 4
+      for (int j = 0; j < 16; ++j) {
+        if (j >= nkw) break;
+        const float4 vv = *reinterpret_cast<const float4 *>(vt + (size_t)(k0 + j) * 128 + 4 * lane);
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const float w = sp[warp][g][j];
+          o[g].x = fmaf(w, vv.x, o[g].x);
+          o[g].y = fmaf(w, vv.y, o[g].y);
+          o[g].z = fmaf(w, vv.z, o[g].z);
+          o[g].w = fmaf(w, vv.w, o[g].w);
+        }
       }
     }
-    __syncwarp();
-  }
+    __syncthreads();  // every warp is done with stage st
+    if (threadIdx.x == 0 && i + kAttnStages < total) {
+      fence_proxy_async();
+      issue_next(i + kAttnStages);
+    }
+    ++ct;
+    if (ct < tiles_of(cs)) continue;
 
-  // merge the warps of this CTA
+    // ---- end of segment: merge the warps ----
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    if (lane == 0) {
-      wm[warp][g] = mx[g];
-      wl[warp][g] = sum[g];
+    for (int g = 0; g < G; ++g) {
+      if (lane == 0) {
+        wm[warp][g] = mx[g];
+        wl[warp][g] = sum[g];
+      }
+      wo[warp][g][lane] = o[g];
     }
-    wo[warp][g][lane] = o[g];
-  }
-  __syncthreads();
-  float *part_base = p.partials + (((size_t)m * p.n_kv_heads + kvh) * p.splits + split) * (size_t)(G * kAttnPartStride);
-  if (warp < G) {
-    const int g = warp;
-    float M = -INFINITY;
-    for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, wm[w][g]);
-    float L = 0.0f;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int w = 0; w < kAttnWarps; ++w) {
-      const float f = wm[w][g] == -INFINITY ? 0.0f : expf(__fsub_rn(wm[w][g], M));
-      L = __fadd_rn(L, __fmul_rn(wl[w][g], f));
-      const float4 ov = wo[w][g][lane];
-      acc.x = fmaf(ov.x, f, acc.x);
-      acc.y = fmaf(ov.y, f, acc.y);
-      acc.z = fmaf(ov.z, f, acc.z);
-      acc.w = fmaf(ov.w, f, acc.w);
+    __syncthreads();
+    // CTAs covering this pair: c_of(t) = floor(((t+1)*Gd - 1) / Tk)
+    long long off = 0;
+    for (int q2 = 0; q2 < pr; ++q2) off += len_of(q2);
+    const long long len = len_of(pr);
+    const long long c_first = ((off + 1) * Gd - 1) / Tk, c_last = ((off + len) * Gd - 1) / Tk;
+    const bool alone = c_first == c_last;
+    if (warp < G) {
+      const int g = warp;
+      float Mx = -INFINITY;
+      for (int w = 0; w < kAttnWarps; ++w) Mx = fmaxf(Mx, wm[w][g]);
+      float L = 0.0f;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int w = 0; w < kAttnWarps; ++w) {
+        const float f = wm[w][g] == -INFINITY ? 0.0f : expf(__fsub_rn(wm[w][g], Mx));
+        L = __fadd_rn(L, __fmul_rn(wl[w][g], f));
+        const float4 ov = wo[w][g][lane];
+        acc.x = fmaf(ov.x, f, acc.x);
+        acc.y = fmaf(ov.y, f, acc.y);
+        acc.z = fmaf(ov.z, f, acc.z);
+        acc.w = fmaf(ov.w, f, acc.w);
+      }
+      float *dst_out = p.out + (size_t)m * p.out_stride + (kvh * G + g) * 128;
+      if (alone) {
+        const float inv = __fdiv_rn(1.0f, L);
+        reinterpret_cast<float4 *>(dst_out)[lane] =
+            make_float4(__fmul_rn(acc.x, inv), __fmul_rn(acc.y, inv), __fmul_rn(acc.z, inv), __fmul_rn(acc.w, inv));
+      } else {
+        float *slot = p.partials + ((size_t)(c + pr) * G + g) * kAttnPartStride;
+        reinterpret_cast<float4 *>(slot)[lane] = acc;
+        if (lane == 0) {
+          slot[128] = Mx;
+          slot[129] = L;
+        }
+      }
     }
-    float *pg = part_base + g * kAttnPartStride;
-    reinterpret_cast<float4 *>(pg)[lane] = acc;
-    if (lane == 0) {
-      pg[128] = M;
-      pg[129] = L;
+    if (!alone) {
+      __threadfence();
+      __syncthreads();
+      if (threadIdx.x == 0) s_last = atomicAdd(p.counters + pr, 1u) == (unsigned)(c_last - c_first);
+      __syncthreads();
+      if (s_last) {
+        __threadfence();
+        if (warp < G) {
+          const int g = warp;
+          float Mx = -INFINITY;
+          for (long long c2 = c_first; c2 <= c_last; ++c2)
+            Mx = fmaxf(Mx, __ldcg(p.partials + ((size_t)(c2 + pr) * G + g) * kAttnPartStride + 128));
+          float L = 0.0f;
+          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (long long c2 = c_first; c2 <= c_last; ++c2) {
+            const float *ps = p.partials + ((size_t)(c2 + pr) * G + g) * kAttnPartStride;
+            const float ms = __ldcg(ps + 128);
+            const float f = ms == -INFINITY ? 0.0f : expf(__fsub_rn(ms, Mx));
+            L = __fadd_rn(L, __fmul_rn(__ldcg(ps + 129), f));
+            const float4 ov = __ldcg(reinterpret_cast<const float4 *>(ps) + lane);
+            acc.x = fmaf(ov.x, f, acc.x);
+            acc.y = fmaf(ov.y, f, acc.y);
+            acc.z = fmaf(ov.z, f, acc.z);
+            acc.w = fmaf(ov.w, f, acc.w);
+          }
+          const float inv = __fdiv_rn(1.0f, L);
+          *reinterpret_cast<float4 *>(p.out + (size_t)m * p.out_stride + (kvh * G + g) * 128 + 4 * lane) =
+              make_float4(__fmul_rn(acc.x, inv), __fmul_rn(acc.y, inv), __fmul_rn(acc.z, inv),
+                          __fmul_rn(acc.w, inv));
+        }
+        if (threadIdx.x == 0) p.counters[pr] = 0u;
+      }
     }
+    __syncthreads();
   }
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    unsigned *ctr = p.counters + (size_t)m * p.n_kv_heads + kvh;
-    last = atomicAdd(ctr, 1u) == (unsigned)p.splits - 1;
-  }
-  __syncthreads();
-  if (!last) return;
-  __threadfence();
-  // last CTA of (m, kvh): merge all splits
-  if (warp < G) {
-    const int g = warp;
-    const float *pb = p.partials + (((size_t)m * p.n_kv_heads + kvh) * p.splits) * (size_t)(G * kAttnPartStride) + g * kAttnPartStride;
-    float M = -INFINITY;
-    for (int s = 0; s < p.splits; ++s) M = fmaxf(M, __ldcg(pb + (size_t)s * G * kAttnPartStride + 128));
-    float L = 0.0f;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int s = 0; s < p.splits; ++s) {
-      const float *ps = pb + (size_t)s * G * kAttnPartStride;
-      const float ms = __ldcg(ps + 128);
-      const float f = ms == -INFINITY ? 0.0f : expf(__fsub_rn(ms, M));
-      L = __fadd_rn(L, __fmul_rn(__ldcg(ps + 129), f));
-      const float4 ov = __ldcg(reinterpret_cast<const float4 *>(ps) + lane);
-      acc.x = fmaf(ov.x, f, acc.x);
-      acc.y = fmaf(ov.y, f, acc.y);
-      acc.z = fmaf(ov.z, f, acc.z);
-      acc.w = fmaf(ov.w, f, acc.w);
-    }
-    const float inv = __fdiv_rn(1.0f, L);
-    float4 r = make_float4(__fmul_rn(acc.x, inv), __fmul_rn(acc.y, inv), __fmul_rn(acc.z, inv), __fmul_rn(acc.w, inv));
-    *reinterpret_cast<float4 *>(p.out + (size_t)m * p.out_stride + (kvh * G + g) * 128 + 4 * lane) = r;
-  }
-  if (threadIdx.x == 0) p.counters[(size_t)m * p.n_kv_heads + kvh] = 0u;
 }
 
-int attn_pick_splits(int M, int n_kv_heads, int max_len) {
-  int sms = 148;
-  int dev = 0;
-  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  int splits = (2 * sms + M * n_kv_heads - 1) / (M * n_kv_heads);
-  const int max_splits = (max_len + 127) / 128;  // at least 128 keys per split
-  splits = std::max(1, std::min(splits, max_splits));
-  return std::min(splits, kAttnMaxSplits);
+int attn_grid() {
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  return sms;
 }
 
-int attn_decode_launch(const AttnDecodeParams &p, int group, cudaStream_t st) {
-  dim3 grid(p.splits, p.n_kv_heads, p.M);
+int attn_make_tensor_map(CUtensorMap *tm, const float *base, long rows, int kv_dim) {
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  if (!encode) {
+    cudaDriverEntryPointQueryResult q;
+    void *fn = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn) {
+      set_error("attention: cuTensorMapEncodeTiled unavailable");
+      return QASR_ERR_CUDA;
+    }
+    encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || kv_dim % 128 || rows <= 0) {
+    set_error("attention: KV cache must be 16-byte aligned with kv_dim a multiple of 128");
+    return QASR_ERR_INVALID;
+  }
+  const cuuint64_t dims[2] = {(cuuint64_t)kv_dim, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)kv_dim * 4};
+  const cuuint32_t box[2] = {128, (cuuint32_t)kAttnTile};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("attention: cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return QASR_ERR_CUDA;
+  }
+  return QASR_OK;
+}
+
+static size_t attn_smem() {
+  return (size_t)kAttnStages * 2 * kAttnTile * 128 * 4 + sizeof(AttnSmall);
+}
+
+template <int G>
+static int attn_launch_t(const AttnDecodeParams &p, cudaStream_t st, bool pdl) {
+  static bool attr_done = false;
+  if (!attr_done) {
+    cudaFuncSetAttribute(attn_decode_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_smem());
+    attr_done = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)attn_grid());
+  cfg.blockDim = dim3(kAttnWarps * 32);
+  cfg.dynamicSmemBytes = attn_smem();
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cuda_status(cudaLaunchKernelEx(&cfg, attn_decode_kernel<G>, p), "attention launch");
+}
+
+int attn_decode_launch(const AttnDecodeParams &p, int group, cudaStream_t st, bool pdl) {
+  if (p.M * p.n_kv_heads > 128) {
+    set_error("attention: M*n_kv_heads = %d > 128", p.M * p.n_kv_heads);
+    return QASR_ERR_UNSUPPORTED;
+  }
   switch (group) {
-    case 1: attn_decode_kernel<1><<<grid, kAttnWarps * 32, 0, st>>>(p); break;
-    case 2: attn_decode_kernel<2><<<grid, kAttnWarps * 32, 0, st>>>(p); break;
+    case 1: return attn_launch_t<1>(p, st, pdl);
+    case 2: return attn_launch_t<2>(p, st, pdl);
     default:
       set_error("attention: GQA group size %d unsupported (1 or 2)", group);
       return QASR_ERR_UNSUPPORTED;
   }
-  return QASR_OK;
 }
 
 }  // namespace qasr

@@ -1,30 +1,35 @@
 // attention.cuh -- host-side interface of the decode attention kernel.
 #pragma once
+#include <cuda.h>
+
 #include "common.cuh"
 
 namespace qasr {
 
 constexpr int kAttnWarps = 4;
-constexpr int kAttnPartStride = 132;  // floats per (split, head) partial: o[128], max, sum, pad
-constexpr int kAttnMaxSplits = 64;
+constexpr int kAttnTile = 64;         // keys per TMA tile
+constexpr int kAttnStages = 3;        // K+V tiles in flight per CTA
+constexpr int kAttnPartStride = 132;  // floats per (segment, head) partial: o[128], max, sum, pad
 
 struct AttnDecodeParams {
+  CUtensorMap tm_k;      // 2D tensor maps over the whole cache: [rows = B*L*max_seq, kv_dim] f32,
+  CUtensorMap tm_v;      // box [kAttnTile rows, 128 floats]
   const float *q;        // [M, n_heads*128] normalised + rotated queries
   long q_stride;
-  const float *k_cache;  // sequence m at k_cache + m*seq_stride, [n_layers, max_seq, kv_dim]
-  const float *v_cache;
-  long seq_stride;
-  int layer, max_seq, kv_dim, n_kv_heads;
+  int layer, n_layers, max_seq, n_kv_heads;
   const int32_t *positions;  // [M]: attend over rows 0..positions[m]
   float scale;
-  int M, splits;
-  float *partials;       // [M, n_kv, splits, G, kAttnPartStride]
-  unsigned *counters;    // [M, n_kv], zero on entry, re-armed by the kernel
+  int M;
+  float *partials;       // [gridDim + M*n_kv, G, kAttnPartStride]
+  unsigned *counters;    // [M*n_kv], zero on entry, re-armed by the kernel
   float *out;            // [M, n_heads*128]
   long out_stride;
+  int *err;              // -QASR_ERR_TIMEOUT on a bounded-wait timeout
 };
 
-int attn_pick_splits(int M, int n_kv_heads, int max_len);
-int attn_decode_launch(const AttnDecodeParams &p, int group, cudaStream_t st);
+// 2D tensor map over a KV cache [rows, kv_dim] f32 with box [kAttnTile, 128].
+int attn_make_tensor_map(CUtensorMap *tm, const float *base, long rows, int kv_dim);
+int attn_decode_launch(const AttnDecodeParams &p, int group, cudaStream_t st, bool pdl);
+int attn_grid();
 
 }  // namespace qasr

@@ -16,11 +16,11 @@
 //   work       x, xn [B, hidden]; qkv [B, q+2kv]; q_out, attn [B, q_dim];
 //              h [B, inter]; attention partials/counters; argmax keys.
 //
-// One decode step = 2 + 7*n_layers kernels captured once per batch size in a
-// CUDA graph and replayed: embed gather; per layer rms_norm, QKV matvec,
-// q/k norm + RoPE + KV append, split-K attention, o-proj(+residual),
-// rms_norm, gate/up matvec(+SwiGLU), down matvec(+residual); final rms_norm
-// + lm head argmax.
+// One decode step = 2 + 6*n_layers kernels captured once per batch size in a
+// CUDA graph (programmatic dependent launch between the streaming kernels)
+// and replayed: embed gather; per layer RMSNorm+QKV matvec, q/k norm + RoPE
+// + KV append, attention, o-proj(+residual), RMSNorm+gate/up matvec+SwiGLU,
+// down matvec(+residual); final RMSNorm + lm head + argmax.
 #include <algorithm>
 #include <cstring>
 #include <vector>
@@ -51,14 +51,15 @@ struct qasr_decoder {
   float *k_cache = nullptr, *v_cache = nullptr;
   float *rope_cos = nullptr, *rope_sin = nullptr;
   float *x = nullptr, *xn = nullptr, *qkv = nullptr, *q_out = nullptr, *attn = nullptr, *h = nullptr;
-  float *partials = nullptr, *logits = nullptr;
-  unsigned *attn_ctr = nullptr, *am_ctr = nullptr;
+  float *partials = nullptr, *logits = nullptr, *mv_partial = nullptr;
+  unsigned *attn_ctr = nullptr, *am_ctr = nullptr, *mv_ctr = nullptr;
+  CUtensorMap tm_k, tm_v;
+  int s_oproj = 1, s_down = 1;
   unsigned long long *am_keys = nullptr;
   int32_t *tok = nullptr, *pos = nullptr, *next = nullptr;
   int *err = nullptr;
   int32_t *h_tok = nullptr, *h_pos = nullptr, *h_next = nullptr;  // pinned staging
   int *h_err = nullptr;
-  int splits = 1;
   bool keep_logits = false;
   std::vector<cudaGraphExec_t> graphs;  // per M (index M), built lazily
   std::vector<void *> allocs;
@@ -233,10 +234,15 @@ extern "C" qasr_decoder *qasr_decoder_create(const qasr_decoder_config *cfg, int
   d->q_out = (float *)dalloc(d, (size_t)B * q_dim * 4, &rc);
   d->attn = (float *)dalloc(d, (size_t)B * q_dim * 4, &rc);
   d->h = (float *)dalloc(d, (size_t)B * I * 4, &rc);
-  d->splits = attn_pick_splits(B, cfg->n_kv_heads, cfg->max_seq);
   const int G = cfg->n_heads / cfg->n_kv_heads;
-  d->partials = (float *)dalloc(d, (size_t)B * cfg->n_kv_heads * d->splits * G * kAttnPartStride * 4, &rc);
+  d->partials = (float *)dalloc(d, (size_t)(attn_grid() + B * cfg->n_kv_heads) * G * kAttnPartStride * 4, &rc);
   d->attn_ctr = (unsigned *)dalloc(d, (size_t)B * cfg->n_kv_heads * 4, &rc);
+  // split-K of the two hidden-sized projections (o-proj K=q_dim, down K=inter)
+  d->s_oproj = mv2_pick_slices(H, q_dim, B, MvEpi::Residual);
+  d->s_down = mv2_pick_slices(H, I, B, MvEpi::Residual);
+  const int s_max = std::max(d->s_oproj, d->s_down);
+  d->mv_partial = (float *)dalloc(d, (size_t)s_max * B * H * 4, &rc);
+  d->mv_ctr = (unsigned *)dalloc(d, (size_t)(H / 4 + 16) * 4, &rc);
   d->am_keys = (unsigned long long *)dalloc(d, 8 * 8, &rc);
   d->am_ctr = (unsigned *)dalloc(d, 16, &rc);
   d->tok = (int32_t *)dalloc(d, 8 * 4, &rc);
@@ -255,6 +261,9 @@ extern "C" qasr_decoder *qasr_decoder_create(const qasr_decoder_config *cfg, int
   rc = cuda_status(cudaMemsetAsync(d->k_cache, 0, kv_elems * 4, st), "memset");
   if (!rc) rc = cuda_status(cudaMemsetAsync(d->v_cache, 0, kv_elems * 4, st), "memset");
   if (!rc) rc = cuda_status(cudaMemsetAsync(d->attn_ctr, 0, (size_t)B * cfg->n_kv_heads * 4, st), "memset");
+  if (!rc) rc = cuda_status(cudaMemsetAsync(d->mv_ctr, 0, (size_t)(H / 4 + 16) * 4, st), "memset");
+  if (!rc) rc = attn_make_tensor_map(&d->tm_k, d->k_cache, (long)B * L * cfg->max_seq, kv_dim);
+  if (!rc) rc = attn_make_tensor_map(&d->tm_v, d->v_cache, (long)B * L * cfg->max_seq, kv_dim);
   if (!rc) rc = cuda_status(cudaMemsetAsync(d->am_keys, 0, 64, st), "memset");
   if (!rc) rc = cuda_status(cudaMemsetAsync(d->am_ctr, 0, 16, st), "memset");
   if (!rc) rc = cuda_status(cudaMemsetAsync(d->err, 0, 16, st), "memset");
@@ -406,60 +415,49 @@ static int enqueue_step(qasr_decoder *d, int M, StepMarks *marks = nullptr) {
   step_embed_kernel<<<M, 256, 0, st>>>(d->x, emb_tab, d->embed_s, c.embed_is_int8, d->tok, H, c.vocab, d->err);
   MARK(QASR_K_EMBED);
   int rc = launch_status("decode step: embed");
+  auto mv = [&](const float *x, long xs, const float *nw, const int8_t *w, const float *sc, float *y, long ys, int K,
+                int N, int S, MvEpi e) {
+    Mv2Params p{};
+    p.x = x; p.x_stride = xs; p.norm_w = nw; p.eps = c.eps; p.w = w; p.scales = sc; p.y = y; p.y_stride = ys;
+    p.M = M; p.K = K; p.N = N; p.S = S; p.KS = K / S; p.KC = mv2_chunk(K / S);
+    p.partial = d->mv_partial; p.rg_counter = d->mv_ctr;
+    p.keys = d->am_keys; p.counter = d->am_ctr; p.ids = d->next; p.err = d->err;
+    return mv2_launch(p, e, st, true);
+  };
   for (int l = 0; l < c.n_layers && !rc; ++l) {
     const LayerDev &L = d->layers[l];
-    rc = qasr_rms_norm(d->xn, d->x, L.in_norm, M, H, c.eps, st);
-    if (rc) break;
-    MARK(QASR_K_NORM);
-    MvParams p{};
-    p.x = d->xn; p.x_stride = H; p.w = L.wqkv; p.scales = L.sqkv; p.y = d->qkv; p.y_stride = qkv_rows;
-    p.M = M; p.K = H; p.N = qkv_rows;
-    mv_launch(p, MvEpi::Store, st, 0);
+    // input RMSNorm fused into the q|k|v matvec
+    if ((rc = mv(d->x, H, L.in_norm, L.wqkv, L.sqkv, d->qkv, qkv_rows, H, qkv_rows, 1, MvEpi::Store))) break;
     MARK(QASR_K_QKV);
     const int tasks = M * (c.n_heads + 2 * c.n_kv_heads);
     qkv_post_kernel<<<ceil_div(tasks, 8), 256, 0, st>>>(d->qkv, qkv_rows, d->q_out, d->k_cache, d->v_cache,
                                                         d->seq_stride(), l, c.max_seq, d->pos, L.q_norm, L.k_norm,
                                                         d->rope_cos, d->rope_sin, c.n_heads, c.n_kv_heads, c.eps, M,
                                                         d->err);
+    if ((rc = launch_status("decode step: qkv post"))) break;
     MARK(QASR_K_QKV_POST);
     AttnDecodeParams a{};
-    a.q = d->q_out; a.q_stride = q_dim; a.k_cache = d->k_cache; a.v_cache = d->v_cache;
-    a.seq_stride = d->seq_stride(); a.layer = l; a.max_seq = c.max_seq; a.kv_dim = kv_dim;
+    a.tm_k = d->tm_k; a.tm_v = d->tm_v;
+    a.q = d->q_out; a.q_stride = q_dim; a.layer = l; a.n_layers = c.n_layers; a.max_seq = c.max_seq;
     a.n_kv_heads = c.n_kv_heads; a.positions = d->pos; a.scale = 1.0f / sqrtf((float)hd); a.M = M;
-    a.splits = d->splits; a.partials = d->partials; a.counters = d->attn_ctr; a.out = d->attn; a.out_stride = q_dim;
-    if ((rc = attn_decode_launch(a, G, st))) break;
+    a.partials = d->partials; a.counters = d->attn_ctr; a.out = d->attn; a.out_stride = q_dim; a.err = d->err;
+    if ((rc = attn_decode_launch(a, G, st, true))) break;
     MARK(QASR_K_ATTN);
-    MvParams o{};
-    o.x = d->attn; o.x_stride = q_dim; o.w = L.wo; o.scales = L.so; o.y = d->x; o.y_stride = H;
-    o.M = M; o.K = q_dim; o.N = H;
-    mv_launch(o, MvEpi::Residual, st, 0);
+    if ((rc = mv(d->attn, q_dim, nullptr, L.wo, L.so, d->x, H, q_dim, H, d->s_oproj, MvEpi::Residual))) break;
     MARK(QASR_K_OPROJ);
-    if ((rc = qasr_rms_norm(d->xn, d->x, L.post_norm, M, H, c.eps, st))) break;
-    MARK(QASR_K_NORM);
-    MvParams g{};
-    g.x = d->xn; g.x_stride = H; g.w = L.gate_up; g.scales = L.sgu; g.y = d->h; g.y_stride = I;
-    g.M = M; g.K = H; g.N = 2 * I;
-    mv_launch(g, MvEpi::SwiGLU, st, 0);
+    // post-attention RMSNorm fused into the gate/up matvec, SwiGLU in its epilogue
+    if ((rc = mv(d->x, H, L.post_norm, L.gate_up, L.sgu, d->h, I, H, 2 * I, 1, MvEpi::SwiGLU))) break;
     MARK(QASR_K_GATEUP);
-    MvParams dn{};
-    dn.x = d->h; dn.x_stride = I; dn.w = L.down; dn.scales = L.sdown; dn.y = d->x; dn.y_stride = H;
-    dn.M = M; dn.K = I; dn.N = H;
-    mv_launch(dn, MvEpi::Residual, st, 0);
+    if ((rc = mv(d->h, I, nullptr, L.down, L.sdown, d->x, H, I, H, d->s_down, MvEpi::Residual))) break;
     MARK(QASR_K_DOWN);
-    rc = launch_status("decode step: layer");
   }
   if (rc) return rc;
-  if ((rc = qasr_rms_norm(d->xn, d->x, d->norm, M, H, c.eps, st))) return rc;
-  MARK(QASR_K_NORM);
-  MvParams lm{};
-  lm.x = d->xn; lm.x_stride = H;
-  lm.w = d->lm_tied ? static_cast<const int8_t *>(d->embed) : d->lm;
-  lm.scales = d->lm_tied ? d->embed_s : d->lm_s;
-  lm.y = d->keep_logits ? d->logits : nullptr; lm.y_stride = c.vocab;
-  lm.M = M; lm.K = H; lm.N = c.vocab; lm.keys = d->am_keys; lm.counter = d->am_ctr; lm.ids = d->next;
-  mv_launch(lm, MvEpi::Argmax, st, 4);
+  // final RMSNorm fused into the lm head, argmax in its epilogue
+  rc = mv(d->x, H, d->norm, d->lm_tied ? static_cast<const int8_t *>(d->embed) : d->lm,
+          d->lm_tied ? d->embed_s : d->lm_s, d->keep_logits ? d->logits : nullptr, c.vocab, H, c.vocab, 1,
+          MvEpi::Argmax);
   MARK(QASR_K_LMHEAD);
-  return launch_status("decode step: lm head");
+  return rc;
 }
 
 static int run_graph(qasr_decoder *d, int M) {

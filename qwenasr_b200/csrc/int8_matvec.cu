@@ -244,23 +244,60 @@ static int check_mv(const char *fn, const float *y, const float *x, const int8_t
   return QASR_OK;
 }
 
+// Try the weight-streaming kernel (matvec2.cu) for M <= 8 tokens; returns
+// QASR_ERR_UNSUPPORTED (nothing launched) for shapes it does not cover.
+static int try_mv2(const float *x, long xs, const float *nw, float eps, const int8_t *w, const float *scales,
+                   const float *bias, float *y, long ys, int M, int K, int N, MvEpi e, int32_t *ids, cudaStream_t st) {
+  if (K % 512 || (reinterpret_cast<uintptr_t>(w) & 15) || (reinterpret_cast<uintptr_t>(x) & 15) || (xs & 3) ||
+      (reinterpret_cast<uintptr_t>(nw) & 15) ||
+      M < 1 || M > 8)
+    return QASR_ERR_UNSUPPORTED;
+  Mv2Params p{};
+  p.x = x; p.x_stride = xs; p.norm_w = nw; p.eps = eps; p.w = w; p.scales = scales; p.bias = bias;
+  p.y = y; p.y_stride = ys; p.M = M; p.K = K; p.N = N;
+  p.S = nw ? 1 : mv2_pick_slices(N, K, M, e);
+  p.KS = K / p.S;
+  p.KC = mv2_chunk(p.KS);
+  if (p.S == 1 && (size_t)8 * K * 4 > 96 * 1024) return QASR_ERR_UNSUPPORTED;
+  int rc;
+  if (p.S > 1) {
+    void *part, *ctr;
+    if ((rc = dev_scratch(kScratchPartial, (size_t)p.S * M * N * 4, &part))) return rc;
+    if ((rc = dev_scratch(kScratchCounter, (size_t)(N / 4 + 16) * 4, &ctr))) return rc;
+    p.partial = static_cast<float *>(part);
+    p.rg_counter = static_cast<unsigned *>(ctr);
+  }
+  if (e == MvEpi::Argmax) {
+    if ((rc = argmax_scratch(&p.keys, &p.counter))) return rc;
+    p.ids = ids;
+  }
+  return mv2_launch(p, e, st, false);
+}
+
 static int linear_int8_impl(const char *fn, float *y, const float *x, const int8_t *w, const float *scales,
                             const float *bias, int seq, int in_dim, int out_dim, void *stream) {
   int rc = check_mv(fn, y, x, w, scales, seq, in_dim, out_dim);
   if (rc) return rc;
   for (int s0 = 0; s0 < seq; s0 += 8) {
-    MvParams p{};
-    p.x = x + (size_t)s0 * in_dim;
-    p.x_stride = in_dim;
-    p.w = w;
-    p.scales = scales;
-    p.bias = bias;
-    p.y = y + (size_t)s0 * out_dim;
-    p.y_stride = out_dim;
-    p.M = std::min(8, seq - s0);
-    p.K = in_dim;
-    p.N = out_dim;
-    mv_launch(p, bias ? MvEpi::StoreBias : MvEpi::Store, S(stream), 0);
+    const int m = std::min(8, seq - s0);
+    rc = try_mv2(x + (size_t)s0 * in_dim, in_dim, nullptr, 0.f, w, scales, bias, y + (size_t)s0 * out_dim, out_dim,
+                 m, in_dim, out_dim, bias ? MvEpi::StoreBias : MvEpi::Store, nullptr, S(stream));
+    if (rc == QASR_ERR_UNSUPPORTED) {
+      MvParams p{};
+      p.x = x + (size_t)s0 * in_dim;
+      p.x_stride = in_dim;
+      p.w = w;
+      p.scales = scales;
+      p.bias = bias;
+      p.y = y + (size_t)s0 * out_dim;
+      p.y_stride = out_dim;
+      p.M = m;
+      p.K = in_dim;
+      p.N = out_dim;
+      mv_launch(p, bias ? MvEpi::StoreBias : MvEpi::Store, S(stream), 0);
+    } else if (rc) {
+      return rc;
+    }
   }
   return launch_status(fn);
 }
@@ -284,6 +321,9 @@ extern "C" int qasr_int8_matvec_residual(float *x, const float *a, const int8_t 
     return QASR_ERR_UNSUPPORTED;
   }
   if (M == 0) return QASR_OK;
+  rc = try_mv2(a, in_dim, nullptr, 0.f, w, scales, nullptr, x, out_dim, M, in_dim, out_dim, MvEpi::Residual, nullptr,
+               S(stream));
+  if (rc != QASR_ERR_UNSUPPORTED) return rc ? rc : launch_status("qasr_int8_matvec_residual");
   MvParams p{};
   p.x = a;
   p.x_stride = in_dim;
@@ -308,6 +348,9 @@ extern "C" int qasr_int8_norm_gateup_swiglu(float *h, const float *x, const floa
     return QASR_ERR_INVALID;
   }
   if (M == 0) return QASR_OK;
+  rc = try_mv2(x, hidden, norm_w, eps, w_gate_up, scales, nullptr, h, inter, M, hidden, 2 * inter, MvEpi::SwiGLU,
+               nullptr, S(stream));
+  if (rc != QASR_ERR_UNSUPPORTED) return rc ? rc : launch_status("qasr_int8_norm_gateup_swiglu");
   float *xn = nullptr;
   if ((rc = mv_norm_scratch(&xn, (size_t)M * hidden))) return rc;
   if ((rc = qasr_rms_norm(xn, x, norm_w, M, hidden, eps, stream))) return rc;
@@ -336,6 +379,9 @@ extern "C" int qasr_final_norm_lmhead_argmax(int32_t *ids_out, float *logits_out
     return QASR_ERR_INVALID;
   }
   if (M == 0) return QASR_OK;
+  rc = try_mv2(x, hidden, norm_w, eps, w, scales, nullptr, logits_out, vocab, M, hidden, vocab, MvEpi::Argmax,
+               ids_out, S(stream));
+  if (rc != QASR_ERR_UNSUPPORTED) return rc ? rc : launch_status("qasr_final_norm_lmhead_argmax");
   float *xn = nullptr;
   if ((rc = mv_norm_scratch(&xn, (size_t)M * hidden))) return rc;
   if ((rc = qasr_rms_norm(xn, x, norm_w, M, hidden, eps, stream))) return rc;

@@ -21,6 +21,31 @@ struct MvParams {
   int32_t *ids;              // Argmax: [M] result
 };
 
+// Weight-streaming matvec (matvec2.cu).
+struct Mv2Params {
+  const float *x;        // [M, K] activations, row stride x_stride (16-byte aligned rows)
+  long x_stride;
+  const float *norm_w;   // RMSNorm weights [K] applied to x while staging (S must be 1), or null
+  float eps;
+  const int8_t *w;       // [N, K] row-major int8, 16-byte aligned
+  const float *scales;   // [N]
+  const float *bias;     // [N] (StoreBias)
+  float *y;              // as MvParams::y
+  long y_stride;
+  int M, K, N;
+  int S, KS, KC;         // K slices, slice width, bytes of a row per pipeline stage
+  float *partial;        // [S, M, N] split-K partial sums (S > 1)
+  unsigned *rg_counter;  // [ceil(N/4)] split-K counters, zero on entry, re-armed by the kernel
+  unsigned long long *keys;
+  unsigned *counter;
+  int32_t *ids;
+  int *err;              // set to -QASR_ERR_TIMEOUT if a bounded wait gives up (may be null)
+};
+
+int mv2_launch(const Mv2Params &p, MvEpi e, cudaStream_t st, bool pdl);
+int mv2_pick_slices(int N, int K, int M, MvEpi e);
+inline int mv2_chunk(int KS) { return KS % 1024 == 0 ? 1024 : 512; }
+
 // Enqueue one matvec.  R = rows per warp (1, 2, 4), 0 = automatic.
 void mv_launch(const MvParams &p, MvEpi e, cudaStream_t st, int R);
 int mv_pick_rows(int N, MvEpi e);
@@ -29,5 +54,8 @@ int mv_pick_rows(int N, MvEpi e);
 // re-entrant across concurrently running streams of one device).
 int argmax_scratch(unsigned long long **keys, unsigned **counter);
 int mv_norm_scratch(float **buf, size_t n_floats);
+
+constexpr int kScratchPartial = 0, kScratchCounter = 1, kScratchSlots = 4;
+int dev_scratch(int slot, size_t bytes, void **out);
 
 }  // namespace qasr

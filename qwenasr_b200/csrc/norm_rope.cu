@@ -79,29 +79,40 @@ layer_norm_kernel(float *__restrict__ out, const float *__restrict__ x, const fl
 }
 
 // ------------------------------------------------------------------- RoPE
-// cos/sin table rows.  The reference evaluates powf/cosf/sinf in f32 via
-// glibc (decoder.rs:258-281, mod.rs:1235-1240); here each transcendental is
-// evaluated in double and rounded once, i.e. the correctly rounded f32 value,
-// which is what glibc returns except in rare last-ulp cases.  The f32
-// operations around them (exponent, reciprocal, angle) are done in f32 in
-// the reference's order.  positions == nullptr means rows 0..seq-1.
+// cos/sin table rows.  The reference computes inv_freq[d] = 1/theta^(2d/D)
+// once on the host with f32 powf (RopeCache::ensure, decoder.rs:258-262;
+// compute_rope_neox mod.rs:1236) and then angle = pos*inv_freq in f32; the
+// launchers below compute inv_freq the same way on the host (the same libm
+// powf the Rust code calls) and pass it in.  cos/sin of the f32 angle are
+// evaluated in double and rounded once (the correctly rounded f32 value).
+// positions == nullptr means rows 0..seq-1.
+struct InvFreq {
+  float v[128];
+};
+
 __global__ void rope_table_kernel(float *__restrict__ cos_out, float *__restrict__ sin_out,
-                                  const int32_t *__restrict__ positions, int seq, int head_dim, float theta) {
+                                  const int32_t *__restrict__ positions, int seq, int head_dim,
+                                  const __grid_constant__ InvFreq inv) {
   const int half = head_dim / 2;
   const long t = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= (long)seq * half) return;
   const int s = (int)(t / half), d = (int)(t % half);
   const float pos = positions ? (float)positions[s] : (float)s;
-  const float expo = __fdiv_rn((float)(2 * d), (float)head_dim);
-  const float pw = (float)pow((double)theta, (double)expo);
-  const float inv_freq = __fdiv_rn(1.0f, pw);
-  const float angle = __fmul_rn(pos, inv_freq);
+  const float angle = __fmul_rn(pos, inv.v[d]);
   const float c = (float)cos((double)angle), sn = (float)sin((double)angle);
   const size_t r = (size_t)s * head_dim;
   cos_out[r + d] = c;
   cos_out[r + half + d] = c;
   sin_out[r + d] = sn;
   sin_out[r + half + d] = sn;
+}
+
+// Host: inv_freq of RopeCache::ensure (f32 powf, f32 reciprocal).
+static InvFreq host_inv_freq(int head_dim, float theta) {
+  InvFreq f{};
+  const int half = head_dim / 2;
+  for (int d = 0; d < half && d < 128; ++d) f.v[d] = 1.0f / powf(theta, (float)(2 * d) / (float)head_dim);
+  return f;
 }
 
 // apply_rope_neox (mod.rs:1247-1267): one thread per (row, head, d < half).
@@ -322,25 +333,27 @@ extern "C" int qasr_ln_pe(float *out, const float *x, const float *w, const floa
 
 extern "C" int qasr_compute_rope_neox(float *cos_out, float *sin_out, const int32_t *positions, int seq,
                                       int head_dim, float theta, void *stream) {
-  if (!cos_out || !sin_out || !positions || seq < 0 || head_dim <= 0 || (head_dim & 1)) {
+  if (!cos_out || !sin_out || !positions || seq < 0 || head_dim <= 0 || (head_dim & 1) || head_dim > 256) {
     set_error("qasr_compute_rope_neox: invalid arguments");
     return QASR_ERR_INVALID;
   }
   if (seq == 0) return QASR_OK;
   const long n = (long)seq * (head_dim / 2);
-  rope_table_kernel<<<ceil_div(n, 256), 256, 0, S(stream)>>>(cos_out, sin_out, positions, seq, head_dim, theta);
+  rope_table_kernel<<<ceil_div(n, 256), 256, 0, S(stream)>>>(cos_out, sin_out, positions, seq, head_dim,
+                                                              host_inv_freq(head_dim, theta));
   return launch_status("qasr_compute_rope_neox");
 }
 
 extern "C" int qasr_rope_cache_table(float *cos_out, float *sin_out, int n_pos, int head_dim, float theta,
                                      void *stream) {
-  if (!cos_out || !sin_out || n_pos < 0 || head_dim <= 0 || (head_dim & 1)) {
+  if (!cos_out || !sin_out || n_pos < 0 || head_dim <= 0 || (head_dim & 1) || head_dim > 256) {
     set_error("qasr_rope_cache_table: invalid arguments");
     return QASR_ERR_INVALID;
   }
   if (n_pos == 0) return QASR_OK;
   const long n = (long)n_pos * (head_dim / 2);
-  rope_table_kernel<<<ceil_div(n, 256), 256, 0, S(stream)>>>(cos_out, sin_out, nullptr, n_pos, head_dim, theta);
+  rope_table_kernel<<<ceil_div(n, 256), 256, 0, S(stream)>>>(cos_out, sin_out, nullptr, n_pos, head_dim,
+                                                              host_inv_freq(head_dim, theta));
   return launch_status("qasr_rope_cache_table");
 }
 

@@ -57,6 +57,43 @@ int mv_norm_scratch(float **buf, size_t n_floats) {
   return QASR_OK;
 }
 
+// Per-device, per-purpose scratch for the kernel-level entries: grown on
+// demand, zero-filled when (re)allocated.  Kernels that use counters in it
+// leave them at zero again when they finish.
+struct DevScratch {
+  void *buf = nullptr;
+  size_t cap = 0;
+};
+static DevScratch g_dev_scratch[64][kScratchSlots];
+
+int dev_scratch(int slot, size_t bytes, void **out) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || slot < 0 || slot >= kScratchSlots) return QASR_ERR_INVALID;
+  std::lock_guard<std::mutex> lk(g_scratch_mu);
+  DevScratch &s = g_dev_scratch[dev][slot];
+  if (s.cap < bytes) {
+    if (s.buf) {
+      cudaDeviceSynchronize();
+      cudaFree(s.buf);
+      s.buf = nullptr;
+      s.cap = 0;
+    }
+    size_t want = bytes < 4096 ? 4096 : bytes;
+    if (cudaMalloc(&s.buf, want) != cudaSuccess) {
+      set_error("kernel-level scratch: cudaMalloc(%zu) failed", want);
+      return QASR_ERR_ALLOC;
+    }
+    if (cudaMemset(s.buf, 0, want) != cudaSuccess) {
+      set_error("kernel-level scratch: cudaMemset failed");
+      return QASR_ERR_CUDA;
+    }
+    s.cap = want;
+  }
+  *out = s.buf;
+  return QASR_OK;
+}
+
 }  // namespace qasr
 
 extern "C" const char *qasr_last_error(void) { return qasr::g_err; }
