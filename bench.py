@@ -57,6 +57,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="bounded CPU-baseline sample length")
     ap.add_argument("--seed", type=int, default=1234)
+    ap.add_argument("--layers", type=int, default=28,
+                    help="decoder layers (28 = the configured workload; fewer only for profiler captures)")
     return ap.parse_args()
 
 
@@ -231,7 +233,7 @@ def run_ours(a):
     from qwenasr_b200 import synthetic
     from qwenasr_b200.decoder import Decoder
 
-    cfg = synthetic.DEC_0_6B
+    cfg = dict(synthetic.DEC_0_6B, n_layers=a.layers)
     M, L = a.batch, a.kv_len
     dev = torch.device(f"cuda:{local}")
     dec = Decoder(cfg, device=local, max_batch=M, max_seq=L)

@@ -106,7 +106,11 @@ attn_decode_kernel(const __grid_constant__ AttnDecodeParams p) {
   auto len_of = [&](int pair) { return max(1, min(p.positions[pair / n_kv] + 1, p.max_seq)); };
   long long Tk = 0;
   for (int pr = 0; pr < n_pairs; ++pr) Tk += len_of(pr);
-  const long long Gd = gridDim.x, c = blockIdx.x;
+  // Virtual grid: with fewer keys than CTAs, only the first Tk CTAs take part,
+  // so every participating CTA owns at least one key and the CTAs covering a
+  // pair are exactly c_of(first key) .. c_of(last key).
+  const long long Gd = min((long long)gridDim.x, Tk), c = blockIdx.x;
+  if (c >= Gd) return;
   const long long t0 = c * Tk / Gd, t1 = (c + 1) * Tk / Gd;
 
   if (threadIdx.x == 0) {
@@ -381,7 +385,10 @@ template <int G>
 static int attn_launch_t(const AttnDecodeParams &p, cudaStream_t st, bool pdl) {
   static bool attr_done = false;
   if (!attr_done) {
-    cudaFuncSetAttribute(attn_decode_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_smem());
+    int rc = cuda_status(cudaFuncSetAttribute(attn_decode_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              (int)attn_smem()),
+                         "attention: shared memory opt-in");
+    if (rc) return rc;
     attr_done = true;
   }
   cudaLaunchConfig_t cfg = {};

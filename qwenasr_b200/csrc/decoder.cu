@@ -467,11 +467,11 @@ static int run_graph(qasr_decoder *d, int M) {
     if (rc) return rc;
     int erc = enqueue_step(d, M);
     rc = cuda_status(cudaStreamEndCapture(d->stream, &graph), "end capture");
-    if (erc) {
+    if (erc || rc) {
       if (graph) cudaGraphDestroy(graph);
-      return erc;
+      cudaGetLastError();  // do not leave the capture error sticky for later calls
+      return erc ? erc : rc;
     }
-    if (rc) return rc;
     cudaGraphExec_t exec = nullptr;
     rc = cuda_status(cudaGraphInstantiate(&exec, graph, 0), "graph instantiate");
     cudaGraphDestroy(graph);

@@ -50,6 +50,7 @@ struct Mv2Smem {
   uint64_t bar[kMv2Warps][kMv2Stages];
   float inv[8];
   int err;
+  int last;
   unsigned long long best[kMv2Warps * 32];
 };
 
@@ -282,7 +283,7 @@ int8_mv2_kernel(const __grid_constant__ Mv2Params p) {
   }
 
   if constexpr (E == MvEpi::Argmax) {
-    __shared__ bool last;
+    int &last = sm.last;
     sm.best[threadIdx.x] = best;
     __syncthreads();
     if (threadIdx.x < M) {
@@ -352,7 +353,10 @@ static int launch_t(const Mv2Params &p, cudaStream_t st, bool pdl) {
   const size_t smem = mv2_smem_bytes(MT, p.KS, p.KC, nsl);
   static bool attr_done = false;
   if (!attr_done) {
-    cudaFuncSetAttribute(int8_mv2_kernel<MT, E, NORM>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    int rc = cuda_status(cudaFuncSetAttribute(int8_mv2_kernel<MT, E, NORM>,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024),
+                         "int8 matvec: shared memory opt-in");
+    if (rc) return rc;
     attr_done = true;
   }
   cudaLaunchConfig_t cfg = {};
