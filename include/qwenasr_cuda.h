@@ -262,8 +262,8 @@ const float *qasr_decoder_logits(qasr_decoder *dec);
 /* Kernel classes of a decode step, for qasr_decoder_profile_step. */
 #define QASR_K_EMBED 0     /* token embedding gather */
 #define QASR_K_NORM 1      /* input / post-attention / final RMSNorm */
-#define QASR_K_QKV 2       /* fused q|k|v INT8 matvec */
-#define QASR_K_QKV_POST 3  /* q/k per-head norm + RoPE + KV append */
+#define QASR_K_QKV 2       /* RMSNorm + q|k|v INT8 matvec + q/k norm, RoPE, KV append */
+#define QASR_K_QKV_POST 3  /* (fused into QASR_K_QKV; no separate launch) */
 #define QASR_K_ATTN 4      /* split-K decode attention */
 #define QASR_K_OPROJ 5     /* o-proj INT8 matvec + residual */
 #define QASR_K_GATEUP 6    /* gate/up INT8 matvec + SwiGLU */

@@ -96,9 +96,12 @@ attn_decode_kernel(const __grid_constant__ AttnDecodeParams p) {
   constexpr int TILE_F = kAttnTile * 128;  // floats per K (or V) tile
   float *tiles = reinterpret_cast<float *>(smem_raw);
   AttnSmall &sm = *reinterpret_cast<AttnSmall *>(smem_raw + (size_t)kAttnStages * 2 * TILE_F * 4);
-  __shared__ float sp[kAttnWarps][G][16];
-  __shared__ float wm[kAttnWarps][G], wl[kAttnWarps][G];
-  __shared__ float4 wo[kAttnWarps][G][32];
+  // warp w serves query head (w % G) of the group on key group (w / G) of
+  // each tile: KPW keys per warp
+  constexpr int KPW = kAttnTile * G / kAttnWarps;
+  __shared__ float sp[kAttnWarps][KPW];
+  __shared__ float wm[kAttnWarps], wl[kAttnWarps];
+  __shared__ float4 wo[kAttnWarps][32];
   __shared__ int s_last;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -160,10 +163,13 @@ attn_decode_kernel(const __grid_constant__ AttnDecodeParams p) {
   if (threadIdx.x == 0)
     for (int i = 0; i < total && i < kAttnStages; ++i) issue_next(i);
 
-  float mx[G], sum[G];
-  float4 o[G], qv[G];
+  const int hg = warp % G, kgrp = warp / G;  // this warp's head in the group, key group
+  float mx = -INFINITY, sum = 0.0f;
+  float4 o = make_float4(0.f, 0.f, 0.f, 0.f), qv = o;
   int cs = 0, ct = 0;  // consumer cursor
   int cur_pair = -1;
+  const int my_key = reduce_index<KPW>(lane);
+  const bool writer = (lane & (32 / KPW - 1)) == 0;
   for (int i = 0; i < total; ++i) {
     while (ct >= tiles_of(cs)) {
       ct = 0;
@@ -172,13 +178,10 @@ attn_decode_kernel(const __grid_constant__ AttnDecodeParams p) {
     const int pr = sm.seg_pair[cs], m = pr / n_kv, kvh = pr % n_kv;
     if (pr != cur_pair) {  // new segment: load q, reset state
       cur_pair = pr;
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        qv[g] = *reinterpret_cast<const float4 *>(p.q + (size_t)m * p.q_stride + (kvh * G + g) * 128 + 4 * lane);
-        mx[g] = -INFINITY;
-        sum[g] = 0.0f;
-        o[g] = make_float4(0.f, 0.f, 0.f, 0.f);
-      }
+      qv = *reinterpret_cast<const float4 *>(p.q + (size_t)m * p.q_stride + (kvh * G + hg) * 128 + 4 * lane);
+      mx = -INFINITY;
+      sum = 0.0f;
+      o = make_float4(0.f, 0.f, 0.f, 0.f);
     }
     const int st = i % kAttnStages;
     const bool ok = mbar_wait(&sm.bar[st], (unsigned)((i / kAttnStages) & 1));
@@ -191,60 +194,45 @@ attn_decode_kernel(const __grid_constant__ AttnDecodeParams p) {
     const float *kt = tiles + (size_t)(2 * st) * TILE_F;
     const float *vt = tiles + (size_t)(2 * st + 1) * TILE_F;
     const int nk = min(kAttnTile, sm.seg_b[cs] - sm.seg_a[cs] - ct * kAttnTile);
-    const int k0 = warp * 16;
-    const int nkw = max(0, min(16, nk - k0));  // keys of this warp in the tile
+    const int k0 = kgrp * KPW;
+    const int nkw = max(0, min(KPW, nk - k0));  // keys of this warp in the tile
     if (nkw > 0) {
-      constexpr int V = G * 16;
-      float part[V];
+      float part[KPW];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
+      for (int j = 0; j < KPW; ++j) {
         const float4 kv = *reinterpret_cast<const float4 *>(kt + (size_t)(k0 + j) * 128 + 4 * lane);
+        float d = __fmul_rn(qv.x, kv.x);
+        d = fmaf(qv.y, kv.y, d);
+        d = fmaf(qv.z, kv.z, d);
+        d = fmaf(qv.w, kv.w, d);
+        part[j] = d;
+      }
+      const float tot = warp_reduce_scatter<KPW>(part);
+      const bool live = my_key < nkw;
+      const float sc = live ? __fmul_rn(tot, p.scale) : -INFINITY;
+      const float nmax = fmaxf(mx, warp_max(sc));
+      const float corr = mx == -INFINITY ? 0.0f : expf(__fsub_rn(mx, nmax));
+      const float pj = live ? expf(__fsub_rn(sc, nmax)) : 0.0f;
+      sum = __fadd_rn(__fmul_rn(sum, corr), warp_sum(writer ? pj : 0.0f));
+      mx = nmax;
+      if (writer) sp[warp][my_key] = pj;
+      __syncwarp();
+      o.x = __fmul_rn(o.x, corr);
+      o.y = __fmul_rn(o.y, corr);
+      o.z = __fmul_rn(o.z, corr);
+      o.w = __fmul_rn(o.w, corr);
 #pragma unroll
-        for (int g = 0; g < G; ++g) {
-          float d = __fmul_rn(qv[g].x, kv.x);
-          d = fmaf(qv[g].y, kv.y, d);
-          d = fmaf(qv[g].z, kv.z, d);
-          d = fmaf(qv[g].w, kv.w, d);
-          part[g * 16 + j] = d;
+      for (int j = 0; j < KPW; ++j) {
+        if (j < nkw) {
+          const float4 vv = *reinterpret_cast<const float4 *>(vt + (size_t)(k0 + j) * 128 + 4 * lane);
+          const float w = sp[warp][j];
+          o.x = fmaf(w, vv.x, o.x);
+          o.y = fmaf(w, vv.y, o.y);
+          o.z = fmaf(w, vv.z, o.z);
+          o.w = fmaf(w, vv.w, o.w);
         }
       }
-      const float tot = warp_reduce_scatter<V>(part);
-      const int idx = reduce_index<V>(lane);
-      if ((lane & (32 / V - 1)) == 0) sp[warp][idx / 16][idx % 16] = __fmul_rn(tot, p.scale);
       __syncwarp();
-      float corr[G], pj[G];
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        const float sc = lane < nkw ? sp[warp][g][lane & 15] : -INFINITY;
-        const float nmax = fmaxf(mx[g], warp_max(sc));
-        corr[g] = mx[g] == -INFINITY ? 0.0f : expf(__fsub_rn(mx[g], nmax));
-        pj[g] = lane < nkw ? expf(__fsub_rn(sc, nmax)) : 0.0f;
-        sum[g] = __fadd_rn(__fmul_rn(sum[g], corr[g]), warp_sum(pj[g]));
-        mx[g] = nmax;
-      }
-      __syncwarp();
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        if (lane < 16) sp[warp][g][lane] = pj[g];
-        o[g].x = __fmul_rn(o[g].x, corr[g]);
-        o[g].y = __fmul_rn(o[g].y, corr[g]);
-        o[g].z = __fmul_rn(o[g].z, corr[g]);
-        o[g].w = __fmul_rn(o[g].w, corr[g]);
-      }
-      __syncwarp();
-#pragma unroll 4
-      for (int j = 0; j < 16; ++j) {
-        if (j >= nkw) break;
-        const float4 vv = *reinterpret_cast<const float4 *>(vt + (size_t)(k0 + j) * 128 + 4 * lane);
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-          const float w = sp[warp][g][j];
-          o[g].x = fmaf(w, vv.x, o[g].x);
-          o[g].y = fmaf(w, vv.y, o[g].y);
-          o[g].z = fmaf(w, vv.z, o[g].z);
-          o[g].w = fmaf(w, vv.w, o[g].w);
-        }
-      }
     }
     __syncthreads();  // every warp is done with stage st
     if (threadIdx.x == 0 && i + kAttnStages < total) {
@@ -254,15 +242,12 @@ attn_decode_kernel(const __grid_constant__ AttnDecodeParams p) {
     ++ct;
     if (ct < tiles_of(cs)) continue;
 
-    // ---- end of segment: merge the warps ----
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      if (lane == 0) {
-        wm[warp][g] = mx[g];
-        wl[warp][g] = sum[g];
-      }
-      wo[warp][g][lane] = o[g];
+    // ---- end of segment: merge the warps of each head ----
+    if (lane == 0) {
+      wm[warp] = mx;
+      wl[warp] = sum;
     }
+    wo[warp][lane] = o;
     __syncthreads();
     // CTAs covering this pair: c_of(t) = floor(((t+1)*Gd - 1) / Tk)
     long long off = 0;
@@ -273,13 +258,13 @@ attn_decode_kernel(const __grid_constant__ AttnDecodeParams p) {
     if (warp < G) {
       const int g = warp;
       float Mx = -INFINITY;
-      for (int w = 0; w < kAttnWarps; ++w) Mx = fmaxf(Mx, wm[w][g]);
+      for (int w = g; w < kAttnWarps; w += G) Mx = fmaxf(Mx, wm[w]);
       float L = 0.0f;
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int w = 0; w < kAttnWarps; ++w) {
-        const float f = wm[w][g] == -INFINITY ? 0.0f : expf(__fsub_rn(wm[w][g], Mx));
-        L = __fadd_rn(L, __fmul_rn(wl[w][g], f));
-        const float4 ov = wo[w][g][lane];
+      for (int w = g; w < kAttnWarps; w += G) {
+        const float f = wm[w] == -INFINITY ? 0.0f : expf(__fsub_rn(wm[w], Mx));
+        L = __fadd_rn(L, __fmul_rn(wl[w], f));
+        const float4 ov = wo[w][lane];
         acc.x = fmaf(ov.x, f, acc.x);
         acc.y = fmaf(ov.y, f, acc.y);
         acc.z = fmaf(ov.z, f, acc.z);

@@ -6,7 +6,7 @@
 
 namespace qasr {
 
-constexpr int kAttnWarps = 4;
+constexpr int kAttnWarps = 16;
 constexpr int kAttnTile = 64;         // keys per TMA tile
 constexpr int kAttnStages = 3;        // K+V tiles in flight per CTA
 constexpr int kAttnPartStride = 132;  // floats per (segment, head) partial: o[128], max, sum, pad

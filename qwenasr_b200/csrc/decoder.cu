@@ -16,11 +16,12 @@
 //   work       x, xn [B, hidden]; qkv [B, q+2kv]; q_out, attn [B, q_dim];
 //              h [B, inter]; attention partials/counters; argmax keys.
 //
-// One decode step = 2 + 6*n_layers kernels captured once per batch size in a
+// One decode step = 2 + 5*n_layers kernels captured once per batch size in a
 // CUDA graph (programmatic dependent launch between the streaming kernels)
-// and replayed: embed gather; per layer RMSNorm+QKV matvec, q/k norm + RoPE
-// + KV append, attention, o-proj(+residual), RMSNorm+gate/up matvec+SwiGLU,
-// down matvec(+residual); final RMSNorm + lm head + argmax.
+// and replayed: embed gather; per layer RMSNorm+QKV matvec with the q/k
+// per-head norm + RoPE + KV append in its epilogue, attention, o-proj
+// (+residual), RMSNorm+gate/up matvec+SwiGLU, down matvec(+residual); final
+// RMSNorm + lm head + argmax.
 #include <algorithm>
 #include <cstring>
 #include <vector>
@@ -52,7 +53,7 @@ struct qasr_decoder {
   float *rope_cos = nullptr, *rope_sin = nullptr;
   float *x = nullptr, *xn = nullptr, *qkv = nullptr, *q_out = nullptr, *attn = nullptr, *h = nullptr;
   float *partials = nullptr, *logits = nullptr, *mv_partial = nullptr;
-  unsigned *attn_ctr = nullptr, *am_ctr = nullptr, *mv_ctr = nullptr;
+  unsigned *attn_ctr = nullptr, *am_ctr = nullptr, *mv_ctr = nullptr, *head_ctr = nullptr;
   CUtensorMap tm_k, tm_v;
   int s_oproj = 1, s_down = 1;
   unsigned long long *am_keys = nullptr;
@@ -67,63 +68,6 @@ struct qasr_decoder {
 };
 
 namespace qasr {
-
-// q/k per-head RMSNorm + NeoX RoPE at positions[m] + KV append, one warp per
-// (token, head) over the fused qkv row (decoder.rs:888-895).  head_dim 128:
-// lane L holds elements 4L..4L+3, the RoPE partner is lane^16.
-__global__ void __launch_bounds__(256)
-qkv_post_kernel(const float *__restrict__ qkv, int qkv_stride, float *__restrict__ q_out, float *__restrict__ k_cache,
-                float *__restrict__ v_cache, long seq_stride, int layer, int max_seq,
-                const int32_t *__restrict__ positions, const float *__restrict__ q_norm,
-                const float *__restrict__ k_norm, const float *__restrict__ cos_tab,
-                const float *__restrict__ sin_tab, int n_heads, int n_kv, float eps, int M, int *err) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int per_tok = n_heads + 2 * n_kv;
-  const int task = blockIdx.x * 8 + warp;
-  if (task >= M * per_tok) return;
-  const int m = task / per_tok, h = task % per_tok;
-  const int pos = positions[m];
-  if (pos < 0 || pos >= max_seq) {
-    if (lane == 0) atomicExch(err, 2);
-    return;
-  }
-  const int kv_dim = n_kv * 128;
-  float4 v = reinterpret_cast<const float4 *>(qkv + (size_t)m * qkv_stride + h * 128)[lane];
-  const size_t cache_row = (size_t)m * seq_stride + ((size_t)layer * max_seq + pos) * kv_dim;
-  if (h >= n_heads + n_kv) {  // V head: plain append
-    reinterpret_cast<float4 *>(v_cache + cache_row + (h - n_heads - n_kv) * 128)[lane] = v;
-    return;
-  }
-  const float *nw = h < n_heads ? q_norm : k_norm;
-  float ss = __fmul_rn(v.x, v.x);
-  ss = fmaf(v.y, v.y, ss);
-  ss = fmaf(v.z, v.z, ss);
-  ss = fmaf(v.w, v.w, ss);
-  ss = warp_sum(ss);
-  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, 128.0f), eps)));
-  const float4 w4 = reinterpret_cast<const float4 *>(nw)[lane];
-  v.x = __fmul_rn(__fmul_rn(v.x, inv), w4.x);
-  v.y = __fmul_rn(__fmul_rn(v.y, inv), w4.y);
-  v.z = __fmul_rn(__fmul_rn(v.z, inv), w4.z);
-  v.w = __fmul_rn(__fmul_rn(v.w, inv), w4.w);
-  float4 p;
-  p.x = __shfl_xor_sync(0xffffffffu, v.x, 16);
-  p.y = __shfl_xor_sync(0xffffffffu, v.y, 16);
-  p.z = __shfl_xor_sync(0xffffffffu, v.z, 16);
-  p.w = __shfl_xor_sync(0xffffffffu, v.w, 16);
-  const float4 c = reinterpret_cast<const float4 *>(cos_tab + (size_t)pos * 128)[lane];
-  const float4 s = reinterpret_cast<const float4 *>(sin_tab + (size_t)pos * 128)[lane];
-  const float sg = lane < 16 ? -1.0f : 1.0f;  // first half: x1*c - x2*s; second: x2*c + x1*s
-  float4 o;
-  o.x = __fadd_rn(__fmul_rn(v.x, c.x), __fmul_rn(sg * p.x, s.x));
-  o.y = __fadd_rn(__fmul_rn(v.y, c.y), __fmul_rn(sg * p.y, s.y));
-  o.z = __fadd_rn(__fmul_rn(v.z, c.z), __fmul_rn(sg * p.z, s.z));
-  o.w = __fadd_rn(__fmul_rn(v.w, c.w), __fmul_rn(sg * p.w, s.w));
-  if (h < n_heads)
-    reinterpret_cast<float4 *>(q_out + (size_t)m * n_heads * 128 + h * 128)[lane] = o;
-  else
-    reinterpret_cast<float4 *>(k_cache + cache_row + (h - n_heads) * 128)[lane] = o;
-}
 
 // Embedding gather for the step's tokens (f32 or int8 table).
 __global__ void step_embed_kernel(float *__restrict__ x, const void *__restrict__ table,
@@ -242,7 +186,8 @@ extern "C" qasr_decoder *qasr_decoder_create(const qasr_decoder_config *cfg, int
   d->s_down = mv2_pick_slices(H, I, B, MvEpi::Residual);
   const int s_max = std::max(d->s_oproj, d->s_down);
   d->mv_partial = (float *)dalloc(d, (size_t)s_max * B * H * 4, &rc);
-  d->mv_ctr = (unsigned *)dalloc(d, (size_t)(H / 4 + 16) * 4, &rc);
+  d->mv_ctr = (unsigned *)dalloc(d, (size_t)(H / 2 + 16) * 4, &rc);
+  d->head_ctr = (unsigned *)dalloc(d, (size_t)(cfg->n_heads + 2 * cfg->n_kv_heads) * 4, &rc);
   d->am_keys = (unsigned long long *)dalloc(d, 8 * 8, &rc);
   d->am_ctr = (unsigned *)dalloc(d, 16, &rc);
   d->tok = (int32_t *)dalloc(d, 8 * 4, &rc);
@@ -261,7 +206,9 @@ extern "C" qasr_decoder *qasr_decoder_create(const qasr_decoder_config *cfg, int
   rc = cuda_status(cudaMemsetAsync(d->k_cache, 0, kv_elems * 4, st), "memset");
   if (!rc) rc = cuda_status(cudaMemsetAsync(d->v_cache, 0, kv_elems * 4, st), "memset");
   if (!rc) rc = cuda_status(cudaMemsetAsync(d->attn_ctr, 0, (size_t)B * cfg->n_kv_heads * 4, st), "memset");
-  if (!rc) rc = cuda_status(cudaMemsetAsync(d->mv_ctr, 0, (size_t)(H / 4 + 16) * 4, st), "memset");
+  if (!rc) rc = cuda_status(cudaMemsetAsync(d->mv_ctr, 0, (size_t)(H / 2 + 16) * 4, st), "memset");
+  if (!rc)
+    rc = cuda_status(cudaMemsetAsync(d->head_ctr, 0, (size_t)(cfg->n_heads + 2 * cfg->n_kv_heads) * 4, st), "memset");
   if (!rc) rc = attn_make_tensor_map(&d->tm_k, d->k_cache, (long)B * L * cfg->max_seq, kv_dim);
   if (!rc) rc = attn_make_tensor_map(&d->tm_v, d->v_cache, (long)B * L * cfg->max_seq, kv_dim);
   if (!rc) rc = cuda_status(cudaMemsetAsync(d->am_keys, 0, 64, st), "memset");
@@ -415,27 +362,31 @@ static int enqueue_step(qasr_decoder *d, int M, StepMarks *marks = nullptr) {
   step_embed_kernel<<<M, 256, 0, st>>>(d->x, emb_tab, d->embed_s, c.embed_is_int8, d->tok, H, c.vocab, d->err);
   MARK(QASR_K_EMBED);
   int rc = launch_status("decode step: embed");
-  auto mv = [&](const float *x, long xs, const float *nw, const int8_t *w, const float *sc, float *y, long ys, int K,
-                int N, int S, MvEpi e) {
+  auto mvp = [&](const float *x, long xs, const float *nw, const int8_t *w, const float *sc, float *y, long ys, int K,
+                 int N, int S) {
     Mv2Params p{};
     p.x = x; p.x_stride = xs; p.norm_w = nw; p.eps = c.eps; p.w = w; p.scales = sc; p.y = y; p.y_stride = ys;
     p.M = M; p.K = K; p.N = N; p.S = S; p.KS = K / S; p.KC = mv2_chunk(K / S);
     p.partial = d->mv_partial; p.rg_counter = d->mv_ctr;
     p.keys = d->am_keys; p.counter = d->am_ctr; p.ids = d->next; p.err = d->err;
-    return mv2_launch(p, e, st, true);
+    return p;
   };
+  auto mv = [&](const float *x, long xs, const float *nw, const int8_t *w, const float *sc, float *y, long ys, int K,
+                int N, int S, MvEpi e) { return mv2_launch(mvp(x, xs, nw, w, sc, y, ys, K, N, S), e, st, true); };
   for (int l = 0; l < c.n_layers && !rc; ++l) {
     const LayerDev &L = d->layers[l];
-    // input RMSNorm fused into the q|k|v matvec
-    if ((rc = mv(d->x, H, L.in_norm, L.wqkv, L.sqkv, d->qkv, qkv_rows, H, qkv_rows, 1, MvEpi::Store))) break;
+    // input RMSNorm fused into the q|k|v matvec; its epilogue applies the q/k
+    // per-head norm + RoPE and appends K/V (one launch)
+    {
+      Mv2Params p = mvp(d->x, H, L.in_norm, L.wqkv, L.sqkv, d->qkv, qkv_rows, H, qkv_rows, 1);
+      p.post.q_out = d->q_out; p.post.k_cache = d->k_cache; p.post.v_cache = d->v_cache;
+      p.post.seq_stride = d->seq_stride(); p.post.layer = l; p.post.max_seq = c.max_seq;
+      p.post.n_heads = c.n_heads; p.post.n_kv = c.n_kv_heads; p.post.positions = d->pos;
+      p.post.q_norm = L.q_norm; p.post.k_norm = L.k_norm; p.post.cos_tab = d->rope_cos; p.post.sin_tab = d->rope_sin;
+      p.post.head_ctr = d->head_ctr;
+      if ((rc = mv2_launch(p, MvEpi::QkvPost, st, true))) break;
+    }
     MARK(QASR_K_QKV);
-    const int tasks = M * (c.n_heads + 2 * c.n_kv_heads);
-    qkv_post_kernel<<<ceil_div(tasks, 8), 256, 0, st>>>(d->qkv, qkv_rows, d->q_out, d->k_cache, d->v_cache,
-                                                        d->seq_stride(), l, c.max_seq, d->pos, L.q_norm, L.k_norm,
-                                                        d->rope_cos, d->rope_sin, c.n_heads, c.n_kv_heads, c.eps, M,
-                                                        d->err);
-    if ((rc = launch_status("decode step: qkv post"))) break;
-    MARK(QASR_K_QKV_POST);
     AttnDecodeParams a{};
     a.tm_k = d->tm_k; a.tm_v = d->tm_v;
     a.q = d->q_out; a.q_stride = q_dim; a.layer = l; a.n_layers = c.n_layers; a.max_seq = c.max_seq;

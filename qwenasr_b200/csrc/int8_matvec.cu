@@ -263,7 +263,7 @@ static int try_mv2(const float *x, long xs, const float *nw, float eps, const in
   if (p.S > 1) {
     void *part, *ctr;
     if ((rc = dev_scratch(kScratchPartial, (size_t)p.S * M * N * 4, &part))) return rc;
-    if ((rc = dev_scratch(kScratchCounter, (size_t)(N / 4 + 16) * 4, &ctr))) return rc;
+    if ((rc = dev_scratch(kScratchCounter, (size_t)(N / 2 + 16) * 4, &ctr))) return rc;
     p.partial = static_cast<float *>(part);
     p.rg_counter = static_cast<unsigned *>(ctr);
   }

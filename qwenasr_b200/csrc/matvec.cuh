@@ -6,7 +6,21 @@ namespace qasr {
 
 constexpr int kMvWarps = 4;  // warps per CTA
 
-enum class MvEpi { Store, StoreBias, Residual, SwiGLU, Argmax };
+enum class MvEpi { Store, StoreBias, Residual, SwiGLU, Argmax, QkvPost };
+
+// Per-head epilogue of the fused q|k|v projection (decoder.rs:888-895): when the
+// last rows of a 128-wide head are written, that warp applies the q/k
+// per-head RMSNorm and NeoX RoPE at positions[m] and appends K/V to the cache.
+struct QkvPostParams {
+  float *q_out;              // [M, n_heads*128]
+  float *k_cache, *v_cache;  // per sequence m at + m*seq_stride, [n_layers, max_seq, kv_dim]
+  long seq_stride;
+  int layer, max_seq, n_heads, n_kv;
+  const int32_t *positions;  // [M]
+  const float *q_norm, *k_norm;      // [128]
+  const float *cos_tab, *sin_tab;    // [max_seq, 128]
+  unsigned *head_ctr;        // [n_heads + 2*n_kv], zero on entry, re-armed by the kernel
+};
 
 struct MvParams {
   const float *x;        // [M, K] activations, row stride x_stride
@@ -40,11 +54,13 @@ struct Mv2Params {
   unsigned *counter;
   int32_t *ids;
   int *err;              // set to -QASR_ERR_TIMEOUT if a bounded wait gives up (may be null)
+  QkvPostParams post;    // MvEpi::QkvPost only
 };
 
 int mv2_launch(const Mv2Params &p, MvEpi e, cudaStream_t st, bool pdl);
 int mv2_pick_slices(int N, int K, int M, MvEpi e);
-inline int mv2_chunk(int KS) { return KS % 1024 == 0 ? 1024 : 512; }
+inline int mv2_chunk(int KS) { return 512; }
+inline int mv2_rows(int M) { return M >= 4 ? 2 : 4; }  // rows per warp unit for M tokens
 
 // Enqueue one matvec.  R = rows per warp (1, 2, 4), 0 = automatic.
 void mv_launch(const MvParams &p, MvEpi e, cudaStream_t st, int R);

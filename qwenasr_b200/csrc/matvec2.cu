@@ -3,12 +3,15 @@
 // (generic::int8_matvec_fused, crates/qwen-asr/src/kernels/generic.rs:39-49).
 //
 // Design (HBM-bound: every weight byte is read exactly once per call):
-//  * persistent grid, one 8-warp CTA per SM; the N x K weight matrix is cut
-//    into units of R=4 rows x one K-slice (KS columns), numbered slice-major
-//    and handed out to CTAs in contiguous ranges, warps round-robin;
-//  * each warp streams its units' rows through its own 4-stage shared-memory
-//    ring with 1D bulk copies (cp.async.bulk, completion on an mbarrier), so
-//    up to 128 KB of weights per SM are in flight;
+//  * persistent grid, one 8-warp CTA per SM, sized (<= 128 registers, about
+//    100 KB of shared memory) so that a CTA of the next kernel in the stream
+//    fits beside it: under programmatic dependent launch the next kernel's
+//    weight prefetch overlaps this kernel;
+//  * the N x K weight matrix is cut into units of R rows x one K-slice (KS
+//    columns), numbered slice-major and handed out to CTAs in contiguous
+//    ranges, warps round-robin;
+//  * each warp streams its units' rows through its own 8 KB shared-memory ring
+//    with 1D bulk copies (cp.async.bulk, completion on an mbarrier);
 //  * x (<= 2 K-slices of all M tokens) is staged once per CTA in a permuted
 //    layout in which both the 16-byte weight reads and the 16-byte x reads of
 //    a warp are bank-conflict free; an optional RMSNorm (the reference's
@@ -18,9 +21,10 @@
 //    a row group (atomic counter) sums slices 0..S-1 in order, so results are
 //    deterministic;
 //  * epilogues: store, +bias, residual add, SwiGLU of interleaved gate/up rows
-//    (decoder.rs:916-921), first-max argmax (decoder.rs:942-947);
-//  * the weight prefetch is issued before griddepcontrol.wait, so under
-//    programmatic dependent launch it overlaps the previous kernel.
+//    (decoder.rs:916-921), first-max argmax (decoder.rs:942-947), and the
+//    q/k per-head norm + RoPE + KV append of the fused QKV projection
+//    (decoder.rs:888-895), run by the warp that completes a head;
+//  * the weight prefetch is issued before griddepcontrol.wait.
 // Every mbarrier wait is bounded (tma.cuh); a timeout sets *err and the kernel
 // drains its copies and returns.
 #include "common.cuh"
@@ -31,9 +35,9 @@
 namespace qasr {
 
 constexpr int kMv2Warps = 8;
-constexpr int kMv2Stages = 4;
-constexpr int kMv2R = 4;
-constexpr int kMv2KCMax = 1024;  // largest bytes of one row per pipeline stage
+constexpr int kMv2KC = 512;          // bytes of one row per pipeline stage
+constexpr int kMv2RingBytes = 8192;  // per-warp weight ring
+constexpr int kMv2MaxStages = 8;
 
 // Position of element k (within a slice) in the permuted x layout.
 QASR_DEV int xperm(int k) {
@@ -47,24 +51,71 @@ QASR_DEV int xperm_inv(int idx) {
 }
 
 struct Mv2Smem {
-  uint64_t bar[kMv2Warps][kMv2Stages];
+  uint64_t bar[kMv2Warps][kMv2MaxStages];
   float inv[8];
-  int err;
   int last;
   unsigned long long best[kMv2Warps * 32];
 };
 
-template <int MT, MvEpi E, bool NORM>
-__global__ void __launch_bounds__(kMv2Warps * 32, 1)
+// q/k per-head RMSNorm (tree-order sum) + NeoX RoPE at positions[m], or the V
+// copy, for one 128-wide head held as a float4 per lane (lane L = elements
+// 4L..4L+3; the RoPE partner of a lane is lane^16).
+QASR_DEV void qkv_head_post(const QkvPostParams &q, float eps, int h, int m, float4 v, int *err) {
+  const int lane = threadIdx.x & 31;
+  const int pos = q.positions[m];
+  if (pos < 0 || pos >= q.max_seq) {
+    if (lane == 0 && err) atomicExch(err, 2);
+    return;
+  }
+  const int kv_dim = q.n_kv * 128;
+  const size_t cache_row = (size_t)m * q.seq_stride + ((size_t)q.layer * q.max_seq + pos) * kv_dim;
+  if (h >= q.n_heads + q.n_kv) {
+    reinterpret_cast<float4 *>(q.v_cache + cache_row + (h - q.n_heads - q.n_kv) * 128)[lane] = v;
+    return;
+  }
+  const float *nw = h < q.n_heads ? q.q_norm : q.k_norm;
+  float ss = __fmul_rn(v.x, v.x);
+  ss = fmaf(v.y, v.y, ss);
+  ss = fmaf(v.z, v.z, ss);
+  ss = fmaf(v.w, v.w, ss);
+  ss = warp_sum(ss);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, 128.0f), eps)));
+  const float4 w4 = reinterpret_cast<const float4 *>(nw)[lane];
+  v.x = __fmul_rn(__fmul_rn(v.x, inv), w4.x);
+  v.y = __fmul_rn(__fmul_rn(v.y, inv), w4.y);
+  v.z = __fmul_rn(__fmul_rn(v.z, inv), w4.z);
+  v.w = __fmul_rn(__fmul_rn(v.w, inv), w4.w);
+  float4 pr;
+  pr.x = __shfl_xor_sync(0xffffffffu, v.x, 16);
+  pr.y = __shfl_xor_sync(0xffffffffu, v.y, 16);
+  pr.z = __shfl_xor_sync(0xffffffffu, v.z, 16);
+  pr.w = __shfl_xor_sync(0xffffffffu, v.w, 16);
+  const float4 c = reinterpret_cast<const float4 *>(q.cos_tab + (size_t)pos * 128)[lane];
+  const float4 s = reinterpret_cast<const float4 *>(q.sin_tab + (size_t)pos * 128)[lane];
+  const float sg = lane < 16 ? -1.0f : 1.0f;  // first half: x1*c - x2*s; second: x2*c + x1*s
+  float4 o;
+  o.x = __fadd_rn(__fmul_rn(v.x, c.x), __fmul_rn(sg * pr.x, s.x));
+  o.y = __fadd_rn(__fmul_rn(v.y, c.y), __fmul_rn(sg * pr.y, s.y));
+  o.z = __fadd_rn(__fmul_rn(v.z, c.z), __fmul_rn(sg * pr.z, s.z));
+  o.w = __fadd_rn(__fmul_rn(v.w, c.w), __fmul_rn(sg * pr.w, s.w));
+  if (h < q.n_heads)
+    reinterpret_cast<float4 *>(q.q_out + (size_t)m * q.n_heads * 128 + h * 128)[lane] = o;
+  else
+    reinterpret_cast<float4 *>(q.k_cache + cache_row + (h - q.n_heads) * 128)[lane] = o;
+}
+
+template <int MT, int R, MvEpi E, bool NORM>
+__global__ void __launch_bounds__(kMv2Warps * 32, 2)
 int8_mv2_kernel(const __grid_constant__ Mv2Params p) {
+  constexpr int STAGES = kMv2RingBytes / (R * kMv2KC);
+  static_assert(STAGES <= kMv2MaxStages, "ring");
   extern __shared__ __align__(128) unsigned char smem_raw[];
   Mv2Smem &sm = *reinterpret_cast<Mv2Smem *>(smem_raw);
-  const int KC = p.KC;
+  constexpr int KC = kMv2KC;
   int8_t *wbuf = reinterpret_cast<int8_t *>(smem_raw + ((sizeof(Mv2Smem) + 127) & ~size_t(127)));
-  float *xs = reinterpret_cast<float *>(wbuf + (size_t)kMv2Warps * kMv2Stages * kMv2R * KC);
+  float *xs = reinterpret_cast<float *>(wbuf + (size_t)kMv2Warps * kMv2RingBytes);
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  constexpr int R = kMv2R;
   constexpr int V = R * MT;
   const int M = p.M, K = p.K, N = p.N, S = p.S, KS = p.KS;
   const int n_rg = (N + R - 1) / R;
@@ -75,18 +126,17 @@ int8_mv2_kernel(const __grid_constant__ Mv2Params p) {
   const long my_units = u1 - u0 > warp ? (u1 - u0 - warp + kMv2Warps - 1) / kMv2Warps : 0;
   const long T = my_units * nchunk;  // pipeline items of this warp
 
-  if (threadIdx.x < kMv2Warps * kMv2Stages) mbar_init(&sm.bar[threadIdx.x / kMv2Stages][threadIdx.x % kMv2Stages], 1);
-  if (threadIdx.x == 0) sm.err = 0;
+  if (threadIdx.x < kMv2Warps * STAGES) mbar_init(&sm.bar[threadIdx.x / STAGES][threadIdx.x % STAGES], 1);
   mbar_fence_init();
   __syncthreads();
 
-  int8_t *mybuf = wbuf + (size_t)warp * kMv2Stages * R * KC;
+  int8_t *mybuf = wbuf + (size_t)warp * kMv2RingBytes;
   auto issue = [&](long i) {  // lane 0 only
     const long j = i / nchunk;
     const int c = (int)(i % nchunk);
     const long u = u0 + warp + j * kMv2Warps;
     const int slice = (int)(u / n_rg), rg = (int)(u % n_rg);
-    const int st = (int)(i % kMv2Stages);
+    const int st = (int)(i % STAGES);
     mbar_arrive_expect_tx(&sm.bar[warp][st], R * KC);
 #pragma unroll
     for (int r = 0; r < R; ++r) {
@@ -96,7 +146,7 @@ int8_mv2_kernel(const __grid_constant__ Mv2Params p) {
     }
   };
   if (lane == 0)
-    for (long i = 0; i < T && i < kMv2Stages; ++i) issue(i);
+    for (long i = 0; i < T && i < STAGES; ++i) issue(i);
 
   // activations come from the previous kernel: wait for it only now
   pdl_wait();
@@ -108,7 +158,8 @@ int8_mv2_kernel(const __grid_constant__ Mv2Params p) {
     const int n4 = M * KS / 4;
     for (int t = threadIdx.x; t < n4; t += blockDim.x) {
       const int m = t / (KS / 4), k = (t % (KS / 4)) * 4;
-      const float4 v = *reinterpret_cast<const float4 *>(p.x + (size_t)m * p.x_stride + (size_t)(slice_lo + sl) * KS + k);
+      const float4 v =
+          *reinterpret_cast<const float4 *>(p.x + (size_t)m * p.x_stride + (size_t)(slice_lo + sl) * KS + k);
       *reinterpret_cast<float4 *>(xs + ((size_t)sl * MT + m) * KS + xperm(k)) = v;
     }
   }
@@ -116,15 +167,15 @@ int8_mv2_kernel(const __grid_constant__ Mv2Params p) {
     __syncthreads();
     if (warp < M) {
       const float *xr = xs + (size_t)warp * KS;
-      const int n = K, n16 = n / 16, lane16 = lane;
+      const int n = K, n16 = n / 16;
       float acc = 0.0f;
-      if (lane16 < 16) {
+      if (lane < 16) {
         for (int j = 0; j < n16; ++j) {
-          const float v = xr[xperm(16 * j + lane16)];
+          const float v = xr[xperm(16 * j + lane)];
           acc = fmaf(v, v, acc);
         }
-        if ((n & 15) >= 8 && lane16 < 8) {
-          const float v = xr[xperm(16 * n16 + lane16)];
+        if ((n & 15) >= 8 && lane < 8) {
+          const float v = xr[xperm(16 * n16 + lane)];
           acc = fmaf(v, v, acc);
         }
       }
@@ -160,6 +211,7 @@ int8_mv2_kernel(const __grid_constant__ Mv2Params p) {
   const bool writer = (lane & ((32 / V) - 1)) == 0;
   unsigned long long best = 0ull;
   bool failed = false;
+  long fail_item = -1;
 
   float acc[R][MT];
 #pragma unroll
@@ -167,10 +219,9 @@ int8_mv2_kernel(const __grid_constant__ Mv2Params p) {
 #pragma unroll
     for (int m = 0; m < MT; ++m) acc[r][m] = 0.0f;
 
-  long fail_item = -1;
-  for (long i = 0; i < T && !failed; ++i) {
-    const int st = (int)(i % kMv2Stages);
-    if (!mbar_wait(&sm.bar[warp][st], (unsigned)((i / kMv2Stages) & 1))) {
+  for (long i = 0; i < T; ++i) {
+    const int st = (int)(i % STAGES);
+    if (!mbar_wait(&sm.bar[warp][st], (unsigned)((i / STAGES) & 1))) {
       failed = true;
       fail_item = i;
       break;
@@ -181,16 +232,16 @@ int8_mv2_kernel(const __grid_constant__ Mv2Params p) {
     const int slice = (int)(u / n_rg), rg = (int)(u % n_rg);
     const int8_t *wb = mybuf + (size_t)st * R * KC;
     const float *xb = xs + (size_t)(slice - slice_lo) * MT * KS + (size_t)c * KC + 4 * lane;
-    for (int blk = 0; blk < KC; blk += 512) {
+    {
       uint4 wv[R];
 #pragma unroll
-      for (int r = 0; r < R; ++r) wv[r] = *reinterpret_cast<const uint4 *>(wb + (size_t)r * KC + blk + 16 * lane);
+      for (int r = 0; r < R; ++r) wv[r] = *reinterpret_cast<const uint4 *>(wb + (size_t)r * KC + 16 * lane);
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         float4 xv[MT];
 #pragma unroll
         for (int m = 0; m < MT; ++m)
-          xv[m] = m < M ? *reinterpret_cast<const float4 *>(xb + (size_t)m * KS + blk + 128 * q)
+          xv[m] = m < M ? *reinterpret_cast<const float4 *>(xb + (size_t)m * KS + 128 * q)
                         : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
         for (int r = 0; r < R; ++r) {
@@ -208,9 +259,9 @@ int8_mv2_kernel(const __grid_constant__ Mv2Params p) {
       }
     }
     __syncwarp();
-    if (lane == 0 && i + kMv2Stages < T) {
+    if (lane == 0 && i + STAGES < T) {
       fence_proxy_async();
-      issue(i + kMv2Stages);
+      issue(i + STAGES);
     }
     if (c != nchunk - 1) continue;
 
@@ -267,19 +318,31 @@ int8_mv2_kernel(const __grid_constant__ Mv2Params p) {
         if constexpr (E == MvEpi::Residual) v = __fadd_rn(*dst, v);
         *dst = v;
       }
+      if constexpr (E == MvEpi::QkvPost) {
+        // the warp completing the last rows of a head finishes the head
+        const int head = (rg * R) / 128;
+        __threadfence();
+        __syncwarp();
+        unsigned done = 0;
+        if (lane == 0) done = atomicAdd(p.post.head_ctr + head, 1u);
+        done = __shfl_sync(0xffffffffu, done, 0);
+        if (done == 128 / R - 1) {
+          __threadfence();
+          for (int m = 0; m < M; ++m) {
+            const float4 hv = __ldcg(reinterpret_cast<const float4 *>(p.y + (size_t)m * p.y_stride + head * 128) + lane);
+            qkv_head_post(p.post, p.eps, head, m, hv, p.err);
+          }
+          if (lane == 0) p.post.head_ctr[head] = 0u;
+        }
+      }
     }
   }
 
   if (failed) {
     // report, then let every copy this warp issued land before the CTA exits
-    if (lane == 0) {
-      sm.err = 1;
-      if (p.err) atomicExch(p.err, -QASR_ERR_TIMEOUT);
-    }
-    // items fail_item .. fail_item+kMv2Stages-1 (those < T) were issued and
-    // not yet consumed: wait (bounded) for each of them
-    for (long k = fail_item; k < T && k < fail_item + kMv2Stages; ++k)
-      mbar_wait(&sm.bar[warp][k % kMv2Stages], (unsigned)((k / kMv2Stages) & 1));
+    if (lane == 0 && p.err) atomicExch(p.err, -QASR_ERR_TIMEOUT);
+    for (long k = fail_item; k < T && k < fail_item + STAGES; ++k)
+      mbar_wait(&sm.bar[warp][k % STAGES], (unsigned)((k / STAGES) & 1));
   }
 
   if constexpr (E == MvEpi::Argmax) {
@@ -317,43 +380,43 @@ static int mv2_sms() {
   return sms;
 }
 
-size_t mv2_smem_bytes(int MT, int KS, int KC, int nsl) {
-  return ((sizeof(Mv2Smem) + 127) & ~size_t(127)) + (size_t)kMv2Warps * kMv2Stages * kMv2R * KC +
+static size_t mv2_smem_bytes(int MT, int KS, int nsl) {
+  return ((sizeof(Mv2Smem) + 127) & ~size_t(127)) + (size_t)kMv2Warps * kMv2RingBytes +
          (size_t)nsl * MT * KS * sizeof(float);
 }
 
 // Pick the K split: the fewest slices (each a multiple of 512 columns,
 // <= 1024 unless S = 1) giving about one unit per warp of the grid.
 int mv2_pick_slices(int N, int K, int M, MvEpi e) {
-  if (e == MvEpi::Argmax || K % 512) return 1;
-  const long n_rg = (N + kMv2R - 1) / kMv2R;
+  if (e == MvEpi::Argmax || e == MvEpi::QkvPost || K % 512) return 1;
+  const long n_rg = (N + mv2_rows(M) - 1) / mv2_rows(M);
   const long want = (long)mv2_sms() * kMv2Warps;
   int best = 1;
   for (int S = 1; S <= K / 512; ++S) {
     if (K % S || (K / S) % 512) continue;
     if (S > 1 && K / S > 1024) continue;
     best = S;
-    if (n_rg * S >= want && (S > 1 || (size_t)M * K * 4 <= 96 * 1024)) break;
+    if (n_rg * S >= want && (S > 1 || (size_t)8 * K * 4 <= 48 * 1024)) break;
   }
-  if (best == 1 && (size_t)8 * K * 4 > 96 * 1024) {
+  if (best == 1 && (size_t)8 * K * 4 > 48 * 1024) {
     for (int S = 2; S <= K / 512; ++S)
       if (K % S == 0 && (K / S) % 512 == 0 && K / S <= 1024) return S;
   }
   return best;
 }
 
-template <int MT, MvEpi E, bool NORM>
+template <int MT, int R, MvEpi E, bool NORM>
 static int launch_t(const Mv2Params &p, cudaStream_t st, bool pdl) {
-  const long n_rg = (p.N + kMv2R - 1) / kMv2R;
+  const long n_rg = (p.N + R - 1) / R;
   const long U = n_rg * p.S;
   long G = std::min<long>(mv2_sms(), U);
   // each CTA must touch at most two K slices
   while (G > 1 && (U + G - 1) / G > n_rg) --G;
   const int nsl = p.S == 1 ? 1 : 2;
-  const size_t smem = mv2_smem_bytes(MT, p.KS, p.KC, nsl);
+  const size_t smem = mv2_smem_bytes(MT, p.KS, nsl);
   static bool attr_done = false;
   if (!attr_done) {
-    int rc = cuda_status(cudaFuncSetAttribute(int8_mv2_kernel<MT, E, NORM>,
+    int rc = cuda_status(cudaFuncSetAttribute(int8_mv2_kernel<MT, R, E, NORM>,
                                               cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024),
                          "int8 matvec: shared memory opt-in");
     if (rc) return rc;
@@ -369,22 +432,23 @@ static int launch_t(const Mv2Params &p, cudaStream_t st, bool pdl) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cuda_status(cudaLaunchKernelEx(&cfg, int8_mv2_kernel<MT, E, NORM>, p), "int8 matvec launch");
+  return cuda_status(cudaLaunchKernelEx(&cfg, int8_mv2_kernel<MT, R, E, NORM>, p), "int8 matvec launch");
 }
 
 template <MvEpi E, bool NORM>
 static int launch_e(const Mv2Params &p, cudaStream_t st, bool pdl) {
-  if (p.M <= 1) return launch_t<1, E, NORM>(p, st, pdl);
-  if (p.M <= 2) return launch_t<2, E, NORM>(p, st, pdl);
-  if (p.M <= 4) return launch_t<4, E, NORM>(p, st, pdl);
-  return launch_t<8, E, NORM>(p, st, pdl);
+  if (p.M <= 1) return launch_t<1, 4, E, NORM>(p, st, pdl);
+  if (p.M <= 2) return launch_t<2, 4, E, NORM>(p, st, pdl);
+  if (p.M <= 4) return launch_t<4, 2, E, NORM>(p, st, pdl);
+  return launch_t<8, 2, E, NORM>(p, st, pdl);
 }
 
 int mv2_launch(const Mv2Params &p, MvEpi e, cudaStream_t st, bool pdl) {
-  if (p.M < 1 || p.M > 8 || p.K % 512 || p.KS * p.S != p.K || (p.KC != 512 && p.KC != kMv2KCMax) || p.KS % p.KC ||
+  if (p.M < 1 || p.M > 8 || p.K % 512 || p.KS * p.S != p.K || p.KC != kMv2KC || p.KS % p.KC ||
       (p.S > 1 && (!p.partial || !p.rg_counter)) || (p.norm_w && p.S != 1) ||
       (e == MvEpi::Argmax && (p.S != 1 || !p.keys || !p.counter || !p.ids)) ||
-      mv2_smem_bytes(8, p.KS, p.KC, p.S == 1 ? 1 : 2) > 227 * 1024 || (reinterpret_cast<uintptr_t>(p.w) & 15) ||
+      (e == MvEpi::QkvPost && (p.S != 1 || !p.post.head_ctr || !p.post.positions)) ||
+      mv2_smem_bytes(8, p.KS, p.S == 1 ? 1 : 2) > 227 * 1024 || (reinterpret_cast<uintptr_t>(p.w) & 15) ||
       (reinterpret_cast<uintptr_t>(p.x) & 15) || (p.x_stride & 3)) {
     set_error("int8 matvec: unsupported configuration (M=%d K=%d N=%d S=%d)", p.M, p.K, p.N, p.S);
     return QASR_ERR_UNSUPPORTED;
@@ -396,6 +460,7 @@ int mv2_launch(const Mv2Params &p, MvEpi e, cudaStream_t st, bool pdl) {
     case MvEpi::Residual: return launch_e<MvEpi::Residual, false>(p, st, pdl);
     case MvEpi::SwiGLU: return norm ? launch_e<MvEpi::SwiGLU, true>(p, st, pdl) : launch_e<MvEpi::SwiGLU, false>(p, st, pdl);
     case MvEpi::Argmax: return norm ? launch_e<MvEpi::Argmax, true>(p, st, pdl) : launch_e<MvEpi::Argmax, false>(p, st, pdl);
+    case MvEpi::QkvPost: return norm ? launch_e<MvEpi::QkvPost, true>(p, st, pdl) : launch_e<MvEpi::QkvPost, false>(p, st, pdl);
   }
   return QASR_ERR_INVALID;
 }
