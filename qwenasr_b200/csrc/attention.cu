@@ -66,17 +66,19 @@ causal_attention_kernel(float *__restrict__ out, const float *__restrict__ q, co
 
 // ------------------------------------------------------------------- decode
 // Persistent flash-decoding.  The keys of all (sequence, kv head) pairs are
-// laid end to end and cut into gridDim equal ranges, so every SM streams the
-// same number of K/V bytes whatever the batch and lengths.  A CTA walks its
-// range as segments (one per pair it touches) of 64-key tiles; thread 0 keeps
-// kAttnStages K+V tile pairs in flight with 2D TMA loads (box: 64 rows x one
-// 128-float head slice, no multicast).  Each of the 4 warps scores 16 keys of
-// a tile for both query heads of the GQA group (every K/V byte is read from
-// HBM once), keeps an online-softmax state, and the CTA merges its warps at
-// the end of a segment.  A pair split over several CTAs is merged by the last
-// one to finish (counter + threadfence, slots in CTA order: deterministic).
+// laid end to end and cut into equal ranges, one per CTA, so every SM streams
+// the same number of K/V bytes whatever the batch and lengths.  A CTA walks
+// its range as segments (one per pair it touches); each segment is split
+// evenly over the 8 warps, and every warp streams its keys through its own
+// 3-stage ring of 8-key K and V tiles with 2D TMA loads (box: 8 rows x one
+// 128-float head slice; no multicast), so warps never wait for each other
+// inside a segment.  A warp scores its keys for both query heads of the GQA
+// group (each K/V byte is read from HBM once and used twice), keeps an
+// online-softmax state per head, and the CTA merges its warps at the end of
+// the segment.  A pair split over several CTAs is merged by the last one to
+// finish (counter + threadfence, slots in CTA order: deterministic).
 struct AttnSmall {
-  uint64_t bar[kAttnStages];
+  uint64_t bar[kAttnWarps][kAttnStages];
   int nseg;
   int seg_pair[128], seg_a[128], seg_b[128];
 };
@@ -94,14 +96,12 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
 attn_decode_kernel(const __grid_constant__ AttnDecodeParams p) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   constexpr int TILE_F = kAttnTile * 128;  // floats per K (or V) tile
+  constexpr int KPW = kAttnTile;           // keys per tile (per warp)
   float *tiles = reinterpret_cast<float *>(smem_raw);
-  AttnSmall &sm = *reinterpret_cast<AttnSmall *>(smem_raw + (size_t)kAttnStages * 2 * TILE_F * 4);
-  // warp w serves query head (w % G) of the group on key group (w / G) of
-  // each tile: KPW keys per warp
-  constexpr int KPW = kAttnTile * G / kAttnWarps;
-  __shared__ float sp[kAttnWarps][KPW];
-  __shared__ float wm[kAttnWarps], wl[kAttnWarps];
-  __shared__ float4 wo[kAttnWarps][32];
+  AttnSmall &sm = *reinterpret_cast<AttnSmall *>(smem_raw + (size_t)kAttnWarps * kAttnStages * 2 * TILE_F * 4);
+  __shared__ float sp[kAttnWarps][G][KPW];
+  __shared__ float wm[kAttnWarps][G], wl[kAttnWarps][G];
+  __shared__ float4 wo[kAttnWarps][G][32];
   __shared__ int s_last;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -131,123 +131,142 @@ attn_decode_kernel(const __grid_constant__ AttnDecodeParams p) {
       off += len;
     }
     sm.nseg = ns;
-    for (int st = 0; st < kAttnStages; ++st) mbar_init(&sm.bar[st], 1);
   }
+  if (lane < kAttnStages) mbar_init(&sm.bar[warp][lane], 1);
   mbar_fence_init();
   __syncthreads();
   const int nseg = sm.nseg;
 
-  // tile cursor shared by producer and consumers (advanced in the same order)
-  auto tiles_of = [&](int sg) { return (sm.seg_b[sg] - sm.seg_a[sg] + kAttnTile - 1) / kAttnTile; };
-  int total = 0;
-  for (int sg = 0; sg < nseg; ++sg) total += tiles_of(sg);
-
-  int is = 0, it = 0;  // producer cursor (thread 0)
+  // this warp's key sub-range of segment sg
+  auto wrange = [&](int sg, int &wa, int &wb) {
+    const int a = sm.seg_a[sg], n = sm.seg_b[sg] - a;
+    wa = a + (int)((long)n * warp / kAttnWarps);
+    wb = a + (int)((long)n * (warp + 1) / kAttnWarps);
+  };
+  int T = 0;  // pipeline items (tiles) of this warp
+  for (int sg = 0; sg < nseg; ++sg) {
+    int wa, wb;
+    wrange(sg, wa, wb);
+    T += (wb - wa + KPW - 1) / KPW;
+  }
+  float *mytiles = tiles + (size_t)warp * kAttnStages * 2 * TILE_F;
+  int ps = 0, pt = 0;  // producer cursor (lane 0): segment, tile within the warp's sub-range
   auto issue_next = [&](int item) {
-    while (it >= tiles_of(is)) {
-      it = 0;
-      ++is;
+    int wa, wb;
+    wrange(ps, wa, wb);
+    while (pt * KPW >= wb - wa) {
+      pt = 0;
+      ++ps;
+      wrange(ps, wa, wb);
     }
-    const int pr = sm.seg_pair[is], m = pr / n_kv, kvh = pr % n_kv;
-    const int row = (m * p.n_layers + p.layer) * p.max_seq + sm.seg_a[is] + it * kAttnTile;
+    const int pr = sm.seg_pair[ps], m = pr / n_kv, kvh = pr % n_kv;
+    const int row = (m * p.n_layers + p.layer) * p.max_seq + wa + pt * KPW;
     const int st = item % kAttnStages;
-    mbar_arrive_expect_tx(&sm.bar[st], 2 * TILE_F * 4);
-    tma_load_2d(tiles + (size_t)(2 * st) * TILE_F, &p.tm_k, kvh * 128, row, &sm.bar[st]);
-    tma_load_2d(tiles + (size_t)(2 * st + 1) * TILE_F, &p.tm_v, kvh * 128, row, &sm.bar[st]);
-    ++it;
+    mbar_arrive_expect_tx(&sm.bar[warp][st], 2 * TILE_F * 4);
+    tma_load_2d(mytiles + (size_t)(2 * st) * TILE_F, &p.tm_k, kvh * 128, row, &sm.bar[warp][st]);
+    tma_load_2d(mytiles + (size_t)(2 * st + 1) * TILE_F, &p.tm_v, kvh * 128, row, &sm.bar[warp][st]);
+    ++pt;
   };
   // q and the newest K/V row are written by the previous kernel: wait for it
   // before the first tile load (the tile holding the newest row may be any)
   pdl_wait();
   pdl_launch_dependents();
-  if (threadIdx.x == 0)
-    for (int i = 0; i < total && i < kAttnStages; ++i) issue_next(i);
+  if (lane == 0)
+    for (int i = 0; i < T && i < kAttnStages; ++i) issue_next(i);
+  __syncwarp();
 
-  const int hg = warp % G, kgrp = warp / G;  // this warp's head in the group, key group
-  float mx = -INFINITY, sum = 0.0f;
-  float4 o = make_float4(0.f, 0.f, 0.f, 0.f), qv = o;
-  int cs = 0, ct = 0;  // consumer cursor
-  int cur_pair = -1;
-  const int my_key = reduce_index<KPW>(lane);
-  const bool writer = (lane & (32 / KPW - 1)) == 0;
-  for (int i = 0; i < total; ++i) {
-    while (ct >= tiles_of(cs)) {
-      ct = 0;
-      ++cs;
-    }
-    const int pr = sm.seg_pair[cs], m = pr / n_kv, kvh = pr % n_kv;
-    if (pr != cur_pair) {  // new segment: load q, reset state
-      cur_pair = pr;
-      qv = *reinterpret_cast<const float4 *>(p.q + (size_t)m * p.q_stride + (kvh * G + hg) * 128 + 4 * lane);
-      mx = -INFINITY;
-      sum = 0.0f;
-      o = make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-    const int st = i % kAttnStages;
-    const bool ok = mbar_wait(&sm.bar[st], (unsigned)((i / kAttnStages) & 1));
-    if (__syncthreads_or(!ok)) {
-      if (threadIdx.x == 0 && p.err) atomicExch(p.err, -QASR_ERR_TIMEOUT);
-      for (int k2 = i; k2 < total && k2 < i + kAttnStages; ++k2)
-        mbar_wait(&sm.bar[k2 % kAttnStages], (unsigned)((k2 / kAttnStages) & 1));
-      return;
-    }
-    const float *kt = tiles + (size_t)(2 * st) * TILE_F;
-    const float *vt = tiles + (size_t)(2 * st + 1) * TILE_F;
-    const int nk = min(kAttnTile, sm.seg_b[cs] - sm.seg_a[cs] - ct * kAttnTile);
-    const int k0 = kgrp * KPW;
-    const int nkw = max(0, min(KPW, nk - k0));  // keys of this warp in the tile
-    if (nkw > 0) {
-      float part[KPW];
+  constexpr int V = G * KPW;
+  const int my_idx = reduce_index<V>(lane);  // value (head my_idx/KPW, key my_idx%KPW)
+  const bool writer = (lane & (32 / V - 1)) == 0;
+  int item = 0;
+  bool failed = false;
+  int fail_item = -1;
+  for (int sg = 0; sg < nseg; ++sg) {
+    const int pr = sm.seg_pair[sg], m = pr / n_kv, kvh = pr % n_kv;
+    int wa, wb;
+    wrange(sg, wa, wb);
+    float mx[G], sum[G];
+    float4 o[G], qv[G];
 #pragma unroll
-      for (int j = 0; j < KPW; ++j) {
-        const float4 kv = *reinterpret_cast<const float4 *>(kt + (size_t)(k0 + j) * 128 + 4 * lane);
-        float d = __fmul_rn(qv.x, kv.x);
-        d = fmaf(qv.y, kv.y, d);
-        d = fmaf(qv.z, kv.z, d);
-        d = fmaf(qv.w, kv.w, d);
-        part[j] = d;
+    for (int g = 0; g < G; ++g) {
+      qv[g] = *reinterpret_cast<const float4 *>(p.q + (size_t)m * p.q_stride + (kvh * G + g) * 128 + 4 * lane);
+      mx[g] = -INFINITY;
+      sum[g] = 0.0f;
+      o[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    for (int k0 = wa; k0 < wb; k0 += KPW, ++item) {
+      const int st = item % kAttnStages;
+      if (!failed && !mbar_wait(&sm.bar[warp][st], (unsigned)((item / kAttnStages) & 1))) {
+        failed = true;
+        fail_item = item;
       }
-      const float tot = warp_reduce_scatter<KPW>(part);
-      const bool live = my_key < nkw;
-      const float sc = live ? __fmul_rn(tot, p.scale) : -INFINITY;
-      const float nmax = fmaxf(mx, warp_max(sc));
-      const float corr = mx == -INFINITY ? 0.0f : expf(__fsub_rn(mx, nmax));
-      const float pj = live ? expf(__fsub_rn(sc, nmax)) : 0.0f;
-      sum = __fadd_rn(__fmul_rn(sum, corr), warp_sum(writer ? pj : 0.0f));
-      mx = nmax;
-      if (writer) sp[warp][my_key] = pj;
-      __syncwarp();
-      o.x = __fmul_rn(o.x, corr);
-      o.y = __fmul_rn(o.y, corr);
-      o.z = __fmul_rn(o.z, corr);
-      o.w = __fmul_rn(o.w, corr);
+      if (failed) continue;
+      const float *kt = mytiles + (size_t)(2 * st) * TILE_F;
+      const float *vt = mytiles + (size_t)(2 * st + 1) * TILE_F;
+      const int nk = min(KPW, wb - k0);
+      float part[V];
 #pragma unroll
       for (int j = 0; j < KPW; ++j) {
-        if (j < nkw) {
-          const float4 vv = *reinterpret_cast<const float4 *>(vt + (size_t)(k0 + j) * 128 + 4 * lane);
-          const float w = sp[warp][j];
-          o.x = fmaf(w, vv.x, o.x);
-          o.y = fmaf(w, vv.y, o.y);
-          o.z = fmaf(w, vv.z, o.z);
-          o.w = fmaf(w, vv.w, o.w);
+        const float4 kv = *reinterpret_cast<const float4 *>(kt + (size_t)j * 128 + 4 * lane);
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          float d = __fmul_rn(qv[g].x, kv.x);
+          d = fmaf(qv[g].y, kv.y, d);
+          d = fmaf(qv[g].z, kv.z, d);
+          d = fmaf(qv[g].w, kv.w, d);
+          part[g * KPW + j] = d;
         }
       }
+      const float tot = warp_reduce_scatter<V>(part);
+      const int my_g = my_idx / KPW, my_key = my_idx % KPW;
+      const bool live = my_key < nk;
+      const float sc = live ? __fmul_rn(tot, p.scale) : -INFINITY;
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        // lanes of head g carry its scores; the rest contribute neutral values
+        const float scg = my_g == g ? sc : -INFINITY;
+        const float nmax = fmaxf(mx[g], warp_max(scg));
+        const float corr = mx[g] == -INFINITY ? 0.0f : expf(__fsub_rn(mx[g], nmax));
+        const float pj = (my_g == g && live) ? expf(__fsub_rn(sc, nmax)) : 0.0f;
+        sum[g] = __fadd_rn(__fmul_rn(sum[g], corr), warp_sum(writer ? pj : 0.0f));
+        mx[g] = nmax;
+        if (writer && my_g == g) sp[warp][g][my_key] = pj;
+        o[g].x = __fmul_rn(o[g].x, corr);
+        o[g].y = __fmul_rn(o[g].y, corr);
+        o[g].z = __fmul_rn(o[g].z, corr);
+        o[g].w = __fmul_rn(o[g].w, corr);
+      }
       __syncwarp();
+#pragma unroll
+      for (int j = 0; j < KPW; ++j) {
+        if (j < nk) {
+          const float4 vv = *reinterpret_cast<const float4 *>(vt + (size_t)j * 128 + 4 * lane);
+#pragma unroll
+          for (int g = 0; g < G; ++g) {
+            const float w = sp[warp][g][j];
+            o[g].x = fmaf(w, vv.x, o[g].x);
+            o[g].y = fmaf(w, vv.y, o[g].y);
+            o[g].z = fmaf(w, vv.z, o[g].z);
+            o[g].w = fmaf(w, vv.w, o[g].w);
+          }
+        }
+      }
+      __syncwarp();  // every lane is done with stage st and with sp
+      if (lane == 0 && item + kAttnStages < T) {
+        fence_proxy_async();
+        issue_next(item + kAttnStages);
+      }
     }
-    __syncthreads();  // every warp is done with stage st
-    if (threadIdx.x == 0 && i + kAttnStages < total) {
-      fence_proxy_async();
-      issue_next(i + kAttnStages);
-    }
-    ++ct;
-    if (ct < tiles_of(cs)) continue;
 
     // ---- end of segment: merge the warps of each head ----
-    if (lane == 0) {
-      wm[warp] = mx;
-      wl[warp] = sum;
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      if (lane == 0) {
+        wm[warp][g] = mx[g];
+        wl[warp][g] = sum[g];
+      }
+      wo[warp][g][lane] = o[g];
     }
-    wo[warp][lane] = o;
     __syncthreads();
     // CTAs covering this pair: c_of(t) = floor(((t+1)*Gd - 1) / Tk)
     long long off = 0;
@@ -258,13 +277,13 @@ attn_decode_kernel(const __grid_constant__ AttnDecodeParams p) {
     if (warp < G) {
       const int g = warp;
       float Mx = -INFINITY;
-      for (int w = g; w < kAttnWarps; w += G) Mx = fmaxf(Mx, wm[w]);
+      for (int w = 0; w < kAttnWarps; ++w) Mx = fmaxf(Mx, wm[w][g]);
       float L = 0.0f;
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int w = g; w < kAttnWarps; w += G) {
-        const float f = wm[w] == -INFINITY ? 0.0f : expf(__fsub_rn(wm[w], Mx));
-        L = __fadd_rn(L, __fmul_rn(wl[w], f));
-        const float4 ov = wo[w][lane];
+      for (int w = 0; w < kAttnWarps; ++w) {
+        const float f = wm[w][g] == -INFINITY ? 0.0f : expf(__fsub_rn(wm[w][g], Mx));
+        L = __fadd_rn(L, __fmul_rn(wl[w][g], f));
+        const float4 ov = wo[w][g][lane];
         acc.x = fmaf(ov.x, f, acc.x);
         acc.y = fmaf(ov.y, f, acc.y);
         acc.z = fmaf(ov.z, f, acc.z);
@@ -299,11 +318,11 @@ attn_decode_kernel(const __grid_constant__ AttnDecodeParams p) {
           float L = 0.0f;
           float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
           for (long long c2 = c_first; c2 <= c_last; ++c2) {
-            const float *ps = p.partials + ((size_t)(c2 + pr) * G + g) * kAttnPartStride;
-            const float ms = __ldcg(ps + 128);
+            const float *ps2 = p.partials + ((size_t)(c2 + pr) * G + g) * kAttnPartStride;
+            const float ms = __ldcg(ps2 + 128);
             const float f = ms == -INFINITY ? 0.0f : expf(__fsub_rn(ms, Mx));
-            L = __fadd_rn(L, __fmul_rn(__ldcg(ps + 129), f));
-            const float4 ov = __ldcg(reinterpret_cast<const float4 *>(ps) + lane);
+            L = __fadd_rn(L, __fmul_rn(__ldcg(ps2 + 129), f));
+            const float4 ov = __ldcg(reinterpret_cast<const float4 *>(ps2) + lane);
             acc.x = fmaf(ov.x, f, acc.x);
             acc.y = fmaf(ov.y, f, acc.y);
             acc.z = fmaf(ov.z, f, acc.z);
@@ -318,6 +337,11 @@ attn_decode_kernel(const __grid_constant__ AttnDecodeParams p) {
       }
     }
     __syncthreads();
+  }
+  if (failed) {
+    if (lane == 0 && p.err) atomicExch(p.err, -QASR_ERR_TIMEOUT);
+    for (int k2 = fail_item; k2 < T && k2 < fail_item + kAttnStages; ++k2)
+      mbar_wait(&sm.bar[warp][k2 % kAttnStages], (unsigned)((k2 / kAttnStages) & 1));
   }
 }
 
@@ -363,7 +387,7 @@ int attn_make_tensor_map(CUtensorMap *tm, const float *base, long rows, int kv_d
 }
 
 static size_t attn_smem() {
-  return (size_t)kAttnStages * 2 * kAttnTile * 128 * 4 + sizeof(AttnSmall);
+  return (size_t)kAttnWarps * kAttnStages * 2 * kAttnTile * 128 * 4 + sizeof(AttnSmall);
 }
 
 template <int G>

@@ -60,7 +60,7 @@ struct Mv2Params {
 int mv2_launch(const Mv2Params &p, MvEpi e, cudaStream_t st, bool pdl);
 int mv2_pick_slices(int N, int K, int M, MvEpi e);
 inline int mv2_chunk(int KS) { return 512; }
-inline int mv2_rows(int M) { return M >= 4 ? 2 : 4; }  // rows per warp unit for M tokens
+inline int mv2_rows(int M) { return 4; }  // rows per warp unit
 
 // Enqueue one matvec.  R = rows per warp (1, 2, 4), 0 = automatic.
 void mv_launch(const MvParams &p, MvEpi e, cudaStream_t st, int R);

@@ -231,6 +231,15 @@ int8_mv2_kernel(const __grid_constant__ Mv2Params p) {
     const long u = u0 + warp + j * kMv2Warps;
     const int slice = (int)(u / n_rg), rg = (int)(u % n_rg);
     const int8_t *wb = mybuf + (size_t)st * R * KC;
+    // epilogue operands of this lane's (row, token), loaded now so their
+    // latency hides under the unit's arithmetic
+    const int pre_row = min(rg * R + my_r, N - 1);
+    const float pre_scale = p.scales[pre_row];
+    float pre_aux = 0.0f;
+    if constexpr (E == MvEpi::SwiGLU) pre_aux = p.scales[min(pre_row + 1, N - 1)];
+    if constexpr (E == MvEpi::StoreBias) pre_aux = p.bias[pre_row];
+    if constexpr (E == MvEpi::Residual)
+      if (S == 1 && my_m < M) pre_aux = p.y[(size_t)my_m * p.y_stride + pre_row];
     const float *xb = xs + (size_t)(slice - slice_lo) * MT * KS + (size_t)c * KC + 4 * lane;
     {
       uint4 wv[R];
@@ -298,24 +307,24 @@ int8_mv2_kernel(const __grid_constant__ Mv2Params p) {
     if constexpr (E == MvEpi::SwiGLU) {
       const float other = __shfl_xor_sync(0xffffffffu, sum, 32 / R);
       if (writer && valid && (my_r & 1) == 0) {
-        const float g = __fmul_rn(sum, p.scales[row]);
-        const float uu = __fmul_rn(other, p.scales[row + 1]);
+        const float g = __fmul_rn(sum, pre_scale);
+        const float uu = __fmul_rn(other, pre_aux);
         const float silu = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
         p.y[(size_t)my_m * p.y_stride + row / 2] = __fmul_rn(silu, uu);
       }
     } else if constexpr (E == MvEpi::Argmax) {
       if (valid) {
-        const float logit = __fmul_rn(sum, p.scales[row]);
+        const float logit = __fmul_rn(sum, pre_scale);
         if (writer && p.y) p.y[(size_t)my_m * p.y_stride + row] = logit;
         const unsigned long long key = argmax_key(logit, (uint32_t)row);
         best = key > best ? key : best;
       }
     } else {
       if (writer && valid) {
-        float v = __fmul_rn(sum, p.scales[row]);
-        if constexpr (E == MvEpi::StoreBias) v = __fadd_rn(v, p.bias[row]);
+        float v = __fmul_rn(sum, pre_scale);
+        if constexpr (E == MvEpi::StoreBias) v = __fadd_rn(v, pre_aux);
         float *dst = p.y + (size_t)my_m * p.y_stride + row;
-        if constexpr (E == MvEpi::Residual) v = __fadd_rn(*dst, v);
+        if constexpr (E == MvEpi::Residual) v = __fadd_rn(S == 1 ? pre_aux : *dst, v);
         *dst = v;
       }
       if constexpr (E == MvEpi::QkvPost) {
@@ -439,8 +448,8 @@ template <MvEpi E, bool NORM>
 static int launch_e(const Mv2Params &p, cudaStream_t st, bool pdl) {
   if (p.M <= 1) return launch_t<1, 4, E, NORM>(p, st, pdl);
   if (p.M <= 2) return launch_t<2, 4, E, NORM>(p, st, pdl);
-  if (p.M <= 4) return launch_t<4, 2, E, NORM>(p, st, pdl);
-  return launch_t<8, 2, E, NORM>(p, st, pdl);
+  if (p.M <= 4) return launch_t<4, 4, E, NORM>(p, st, pdl);
+  return launch_t<8, 4, E, NORM>(p, st, pdl);
 }
 
 int mv2_launch(const Mv2Params &p, MvEpi e, cudaStream_t st, bool pdl) {
