@@ -81,6 +81,7 @@ struct AttnSmall {
   uint64_t bar[kAttnWarps][kAttnStages];
   int nseg;
   int seg_pair[128], seg_a[128], seg_b[128];
+  long long off[129];  // prefix sums of the pair lengths (off[n_pairs] = total keys)
 };
 
 QASR_DEV void tma_load_2d(float *dst, const CUtensorMap *tm, int x, int y, uint64_t *bar) {
@@ -106,9 +107,24 @@ attn_decode_kernel(const __grid_constant__ AttnDecodeParams p) {
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_kv = p.n_kv_heads, n_pairs = p.M * n_kv;
-  auto len_of = [&](int pair) { return max(1, min(p.positions[pair / n_kv] + 1, p.max_seq)); };
-  long long Tk = 0;
-  for (int pr = 0; pr < n_pairs; ++pr) Tk += len_of(pr);
+  // pair lengths -> prefix offsets, one warp-parallel scan (<= 128 pairs)
+  if (warp == 0) {
+    long long carry = 0;
+    for (int base = 0; base < n_pairs; base += 32) {
+      const int pr = base + lane;
+      long long v = pr < n_pairs ? (long long)max(1, min(p.positions[pr / n_kv] + 1, p.max_seq)) : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const long long t = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += t;
+      }
+      if (pr < n_pairs) sm.off[pr + 1] = carry + v;
+      carry += __shfl_sync(0xffffffffu, v, 31);
+    }
+    if (lane == 0) sm.off[0] = 0;
+  }
+  __syncthreads();
+  const long long Tk = sm.off[n_pairs];
   // Virtual grid: with fewer keys than CTAs, only the first Tk CTAs take part,
   // so every participating CTA owns at least one key and the CTAs covering a
   // pair are exactly c_of(first key) .. c_of(last key).
@@ -118,9 +134,8 @@ attn_decode_kernel(const __grid_constant__ AttnDecodeParams p) {
 
   if (threadIdx.x == 0) {
     int ns = 0;
-    long long off = 0;
     for (int pr = 0; pr < n_pairs && ns < 128; ++pr) {
-      const long long len = len_of(pr);
+      const long long off = sm.off[pr], len = sm.off[pr + 1] - off;
       const long long a = max(off, t0), b = min(off + len, t1);
       if (a < b) {
         sm.seg_pair[ns] = pr;
@@ -128,7 +143,6 @@ attn_decode_kernel(const __grid_constant__ AttnDecodeParams p) {
         sm.seg_b[ns] = (int)(b - off);
         ++ns;
       }
-      off += len;
     }
     sm.nseg = ns;
   }
@@ -226,8 +240,8 @@ attn_decode_kernel(const __grid_constant__ AttnDecodeParams p) {
         // lanes of head g carry its scores; the rest contribute neutral values
         const float scg = my_g == g ? sc : -INFINITY;
         const float nmax = fmaxf(mx[g], warp_max(scg));
-        const float corr = mx[g] == -INFINITY ? 0.0f : expf(__fsub_rn(mx[g], nmax));
-        const float pj = (my_g == g && live) ? expf(__fsub_rn(sc, nmax)) : 0.0f;
+        const float corr = mx[g] == -INFINITY ? 0.0f : __expf(__fsub_rn(mx[g], nmax));
+        const float pj = (my_g == g && live) ? __expf(__fsub_rn(sc, nmax)) : 0.0f;
         sum[g] = __fadd_rn(__fmul_rn(sum[g], corr), warp_sum(writer ? pj : 0.0f));
         mx[g] = nmax;
         if (writer && my_g == g) sp[warp][g][my_key] = pj;
@@ -269,9 +283,7 @@ attn_decode_kernel(const __grid_constant__ AttnDecodeParams p) {
     }
     __syncthreads();
     // CTAs covering this pair: c_of(t) = floor(((t+1)*Gd - 1) / Tk)
-    long long off = 0;
-    for (int q2 = 0; q2 < pr; ++q2) off += len_of(q2);
-    const long long len = len_of(pr);
+    const long long off = sm.off[pr], len = sm.off[pr + 1] - off;
     const long long c_first = ((off + 1) * Gd - 1) / Tk, c_last = ((off + len) * Gd - 1) / Tk;
     const bool alone = c_first == c_last;
     if (warp < G) {
