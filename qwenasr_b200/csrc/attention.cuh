@@ -6,7 +6,7 @@
 
 namespace qasr {
 
-constexpr int kAttnWarps = 12;
+constexpr int kAttnWarps = 8;
 constexpr int kAttnTile = 8;          // keys per TMA tile (one warp's pipeline stage)
 constexpr int kAttnStages = 2;        // K+V tiles in flight per warp
 constexpr int kAttnPartStride = 132;  // floats per (segment, head) partial: o[128], max, sum, pad

@@ -4,13 +4,13 @@
 //
 // Design (HBM-bound: every weight byte is read exactly once per call):
 //  * persistent grid, one 8-warp CTA per SM, sized (<= 128 registers, about
-//    100 KB of shared memory) so that a CTA of the next kernel in the stream
+//    70 KB of shared memory) so that a CTA of the next kernel in the stream
 //    fits beside it: under programmatic dependent launch the next kernel's
 //    weight prefetch overlaps this kernel;
 //  * the N x K weight matrix is cut into units of R rows x one K-slice (KS
 //    columns), numbered slice-major and handed out to CTAs in contiguous
 //    ranges, warps round-robin;
-//  * each warp streams its units' rows through its own 8 KB shared-memory ring
+//  * each warp streams its units' rows through its own 4 KB shared-memory ring
 //    with 1D bulk copies (cp.async.bulk, completion on an mbarrier);
 //  * x (<= 2 K-slices of all M tokens) is staged once per CTA in a permuted
 //    layout in which both the 16-byte weight reads and the 16-byte x reads of
@@ -36,7 +36,7 @@ namespace qasr {
 
 constexpr int kMv2Warps = 8;
 constexpr int kMv2KC = 512;          // bytes of one row per pipeline stage
-constexpr int kMv2RingBytes = 8192;  // per-warp weight ring
+constexpr int kMv2RingBytes = 4096;  // per-warp weight ring
 constexpr int kMv2MaxStages = 8;
 
 // Position of element k (within a slice) in the permuted x layout.
@@ -170,7 +170,17 @@ int8_mv2_kernel(const __grid_constant__ Mv2Params p) {
       const int n = K, n16 = n / 16;
       float acc = 0.0f;
       if (lane < 16) {
-        for (int j = 0; j < n16; ++j) {
+        // the chain must run in order; its operands are fetched 16 at a time
+        // ahead of it so only the FMA latency is serial
+        int j = 0;
+        for (; j + 16 <= n16; j += 16) {
+          float v[16];
+#pragma unroll
+          for (int t = 0; t < 16; ++t) v[t] = xr[xperm(16 * (j + t) + lane)];
+#pragma unroll
+          for (int t = 0; t < 16; ++t) acc = fmaf(v[t], v[t], acc);
+        }
+        for (; j < n16; ++j) {
           const float v = xr[xperm(16 * j + lane)];
           acc = fmaf(v, v, acc);
         }
@@ -337,10 +347,13 @@ int8_mv2_kernel(const __grid_constant__ Mv2Params p) {
         done = __shfl_sync(0xffffffffu, done, 0);
         if (done == 128 / R - 1) {
           __threadfence();
-          for (int m = 0; m < M; ++m) {
-            const float4 hv = __ldcg(reinterpret_cast<const float4 *>(p.y + (size_t)m * p.y_stride + head * 128) + lane);
-            qkv_head_post(p.post, p.eps, head, m, hv, p.err);
-          }
+          float4 hv[MT];  // every token's head row in flight at once
+#pragma unroll
+          for (int m = 0; m < MT; ++m)
+            if (m < M) hv[m] = __ldcg(reinterpret_cast<const float4 *>(p.y + (size_t)m * p.y_stride + head * 128) + lane);
+#pragma unroll
+          for (int m = 0; m < MT; ++m)
+            if (m < M) qkv_head_post(p.post, p.eps, head, m, hv[m], p.err);
           if (lane == 0) p.post.head_ctr[head] = 0u;
         }
       }
