@@ -38,6 +38,7 @@ constexpr int kMv2Warps = 8;
 constexpr int kMv2KC = 512;          // bytes of one row per pipeline stage
 constexpr int kMv2RingBytes = 4096;  // per-warp weight ring
 constexpr int kMv2MaxStages = 8;
+constexpr int kMv2MaxSlices = 12;  // largest split-K factor
 
 // Position of element k (within a slice) in the permuted x layout.
 QASR_DEV int xperm(int k) {
@@ -52,6 +53,7 @@ QASR_DEV int xperm_inv(int idx) {
 
 struct Mv2Smem {
   uint64_t bar[kMv2Warps][kMv2MaxStages];
+  uint64_t nbar;  // norm weights copy
   float inv[8];
   int last;
   unsigned long long best[kMv2Warps * 32];
@@ -114,6 +116,7 @@ int8_mv2_kernel(const __grid_constant__ Mv2Params p) {
   constexpr int KC = kMv2KC;
   int8_t *wbuf = reinterpret_cast<int8_t *>(smem_raw + ((sizeof(Mv2Smem) + 127) & ~size_t(127)));
   float *xs = reinterpret_cast<float *>(wbuf + (size_t)kMv2Warps * kMv2RingBytes);
+  float *nws = xs + (size_t)(p.S == 1 ? 1 : 2) * MT * p.KS;  // NORM: norm weights [K]
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   constexpr int V = R * MT;
@@ -127,8 +130,15 @@ int8_mv2_kernel(const __grid_constant__ Mv2Params p) {
   const long T = my_units * nchunk;  // pipeline items of this warp
 
   if (threadIdx.x < kMv2Warps * STAGES) mbar_init(&sm.bar[threadIdx.x / STAGES][threadIdx.x % STAGES], 1);
+  if (threadIdx.x == kMv2Warps * STAGES) mbar_init(&sm.nbar, 1);
   mbar_fence_init();
   __syncthreads();
+  if constexpr (NORM) {  // constant operand: fetch it before waiting for the previous kernel
+    if (threadIdx.x == 0) {
+      mbar_arrive_expect_tx(&sm.nbar, (unsigned)K * 4);
+      bulk_g2s(nws, p.norm_w, (unsigned)K * 4, &sm.nbar);
+    }
+  }
 
   int8_t *mybuf = wbuf + (size_t)warp * kMv2RingBytes;
   auto issue = [&](long i) {  // lane 0 only
@@ -156,11 +166,25 @@ int8_mv2_kernel(const __grid_constant__ Mv2Params p) {
   const int nsl = (u1 > u0) ? (int)((u1 - 1) / n_rg) - slice_lo + 1 : 0;
   for (int sl = 0; sl < nsl; ++sl) {
     const int n4 = M * KS / 4;
-    for (int t = threadIdx.x; t < n4; t += blockDim.x) {
-      const int m = t / (KS / 4), k = (t % (KS / 4)) * 4;
-      const float4 v =
-          *reinterpret_cast<const float4 *>(p.x + (size_t)m * p.x_stride + (size_t)(slice_lo + sl) * KS + k);
-      *reinterpret_cast<float4 *>(xs + ((size_t)sl * MT + m) * KS + xperm(k)) = v;
+    // four independent 16-byte loads in flight per thread
+    for (int t0 = threadIdx.x; t0 < n4; t0 += 4 * blockDim.x) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int t = t0 + u * blockDim.x;
+        if (t < n4) {
+          const int m = t / (KS / 4), k = (t % (KS / 4)) * 4;
+          v[u] = *reinterpret_cast<const float4 *>(p.x + (size_t)m * p.x_stride + (size_t)(slice_lo + sl) * KS + k);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int t = t0 + u * blockDim.x;
+        if (t < n4) {
+          const int m = t / (KS / 4), k = (t % (KS / 4)) * 4;
+          *reinterpret_cast<float4 *>(xs + ((size_t)sl * MT + m) * KS + xperm(k)) = v[u];
+        }
+      }
     }
   }
   if constexpr (NORM) {  // S == 1: the slice is the whole row
@@ -197,6 +221,7 @@ int8_mv2_kernel(const __grid_constant__ Mv2Params p) {
         }
       if (lane == 0) sm.inv[warp] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)n), p.eps)));
     }
+    if (!mbar_wait(&sm.nbar, 0) && threadIdx.x == 0 && p.err) atomicExch(p.err, -QASR_ERR_TIMEOUT);
     __syncthreads();
     const int n4 = M * KS / 4;
     for (int t = threadIdx.x; t < n4; t += blockDim.x) {
@@ -204,7 +229,7 @@ int8_mv2_kernel(const __grid_constant__ Mv2Params p) {
       float4 *v4 = reinterpret_cast<float4 *>(xs + (size_t)m * KS + slot);
       const int k = xperm_inv(slot);
       const float inv = sm.inv[m];
-      const float4 wn = *reinterpret_cast<const float4 *>(p.norm_w + k);
+      const float4 wn = *reinterpret_cast<const float4 *>(nws + k);
       float4 v = *v4;
       v.x = __fmul_rn(__fmul_rn(v.x, inv), wn.x);
       v.y = __fmul_rn(__fmul_rn(v.y, inv), wn.y);
@@ -308,8 +333,16 @@ int8_mv2_kernel(const __grid_constant__ Mv2Params p) {
       if (finish) {
         __threadfence();
         sum = 0.0f;
-        if (valid)
-          for (int s2 = 0; s2 < S; ++s2) sum = __fadd_rn(sum, __ldcg(p.partial + ((size_t)s2 * M + my_m) * N + row));
+        if (valid) {
+          // all slice partials in flight at once, summed in slice order
+          float part[kMv2MaxSlices];
+#pragma unroll
+          for (int s2 = 0; s2 < kMv2MaxSlices; ++s2)
+            part[s2] = s2 < S ? __ldcg(p.partial + ((size_t)s2 * M + my_m) * N + row) : 0.0f;
+#pragma unroll
+          for (int s2 = 0; s2 < kMv2MaxSlices; ++s2)
+            if (s2 < S) sum = __fadd_rn(sum, part[s2]);
+        }
         if (lane == 0) p.rg_counter[rg] = 0u;
       }
     }
@@ -402,9 +435,9 @@ static int mv2_sms() {
   return sms;
 }
 
-static size_t mv2_smem_bytes(int MT, int KS, int nsl) {
+static size_t mv2_smem_bytes(int MT, int KS, int nsl, int K) {
   return ((sizeof(Mv2Smem) + 127) & ~size_t(127)) + (size_t)kMv2Warps * kMv2RingBytes +
-         (size_t)nsl * MT * KS * sizeof(float);
+         (size_t)nsl * MT * KS * sizeof(float) + (size_t)K * sizeof(float);
 }
 
 // Pick the K split: the fewest slices (each a multiple of 512 columns,
@@ -414,7 +447,7 @@ int mv2_pick_slices(int N, int K, int M, MvEpi e) {
   const long n_rg = (N + mv2_rows(M) - 1) / mv2_rows(M);
   const long want = (long)mv2_sms() * kMv2Warps;
   int best = 1;
-  for (int S = 1; S <= K / 512; ++S) {
+  for (int S = 1; S <= K / 512 && S <= kMv2MaxSlices; ++S) {
     if (K % S || (K / S) % 512) continue;
     if (S > 1 && K / S > 1024) continue;
     best = S;
@@ -435,7 +468,7 @@ static int launch_t(const Mv2Params &p, cudaStream_t st, bool pdl) {
   // each CTA must touch at most two K slices
   while (G > 1 && (U + G - 1) / G > n_rg) --G;
   const int nsl = p.S == 1 ? 1 : 2;
-  const size_t smem = mv2_smem_bytes(MT, p.KS, nsl);
+  const size_t smem = mv2_smem_bytes(MT, p.KS, nsl, NORM ? p.K : 0);
   static bool attr_done = false;
   if (!attr_done) {
     int rc = cuda_status(cudaFuncSetAttribute(int8_mv2_kernel<MT, R, E, NORM>,
@@ -470,7 +503,8 @@ int mv2_launch(const Mv2Params &p, MvEpi e, cudaStream_t st, bool pdl) {
       (p.S > 1 && (!p.partial || !p.rg_counter)) || (p.norm_w && p.S != 1) ||
       (e == MvEpi::Argmax && (p.S != 1 || !p.keys || !p.counter || !p.ids)) ||
       (e == MvEpi::QkvPost && (p.S != 1 || !p.post.head_ctr || !p.post.positions)) ||
-      mv2_smem_bytes(8, p.KS, p.S == 1 ? 1 : 2) > 227 * 1024 || (reinterpret_cast<uintptr_t>(p.w) & 15) ||
+      mv2_smem_bytes(8, p.KS, p.S == 1 ? 1 : 2, p.K) > 227 * 1024 || (reinterpret_cast<uintptr_t>(p.w) & 15) ||
+      (p.norm_w && (reinterpret_cast<uintptr_t>(p.norm_w) & 15)) || p.S > kMv2MaxSlices ||
       (reinterpret_cast<uintptr_t>(p.x) & 15) || (p.x_stride & 3)) {
     set_error("int8 matvec: unsupported configuration (M=%d K=%d N=%d S=%d)", p.M, p.K, p.N, p.S);
     return QASR_ERR_UNSUPPORTED;
