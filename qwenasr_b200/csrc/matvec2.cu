@@ -122,12 +122,12 @@ int8_mv2_kernel(const __grid_constant__ Mv2Params p) {
   constexpr int V = R * MT;
   const int M = p.M, K = p.K, N = p.N, S = p.S, KS = p.KS;
   const int n_rg = (N + R - 1) / R;
-  const long U = (long)n_rg * S;
-  const long u0 = U * blockIdx.x / gridDim.x, u1 = U * (blockIdx.x + 1) / gridDim.x;
-  const int slice_lo = (int)(u0 / n_rg);
+  const int U = n_rg * S;  // < 2^31 for every supported shape (checked on the host)
+  const int u0 = (int)((long long)U * blockIdx.x / gridDim.x), u1 = (int)((long long)U * (blockIdx.x + 1) / gridDim.x);
+  const int slice_lo = u0 / n_rg;
   const int nchunk = KS / KC;
-  const long my_units = u1 - u0 > warp ? (u1 - u0 - warp + kMv2Warps - 1) / kMv2Warps : 0;
-  const long T = my_units * nchunk;  // pipeline items of this warp
+  const int my_units = u1 - u0 > warp ? (u1 - u0 - warp + kMv2Warps - 1) / kMv2Warps : 0;
+  const int T = my_units * nchunk;  // pipeline items of this warp
 
   if (threadIdx.x < kMv2Warps * STAGES) mbar_init(&sm.bar[threadIdx.x / STAGES][threadIdx.x % STAGES], 1);
   if (threadIdx.x == kMv2Warps * STAGES) mbar_init(&sm.nbar, 1);
@@ -141,12 +141,19 @@ int8_mv2_kernel(const __grid_constant__ Mv2Params p) {
   }
 
   int8_t *mybuf = wbuf + (size_t)warp * kMv2RingBytes;
-  auto issue = [&](long i) {  // lane 0 only
-    const long j = i / nchunk;
-    const int c = (int)(i % nchunk);
-    const long u = u0 + warp + j * kMv2Warps;
-    const int slice = (int)(u / n_rg), rg = (int)(u % n_rg);
-    const int st = (int)(i % STAGES);
+  // producer cursor (lane 0): unit (slice, row group) and chunk of the next item
+  int pc = 0, pslice = (u0 + warp) / n_rg, prg = (u0 + warp) % n_rg;
+  auto issue = [&](int i) {  // lane 0 only, called for i = 0, 1, 2, ... in order
+    const int c = pc, slice = pslice, rg = prg;
+    if (++pc == nchunk) {  // next unit of this warp: u += kMv2Warps
+      pc = 0;
+      prg += kMv2Warps;
+      while (prg >= n_rg) {
+        prg -= n_rg;
+        ++pslice;
+      }
+    }
+    const int st = i % STAGES;
     mbar_arrive_expect_tx(&sm.bar[warp][st], R * KC);
 #pragma unroll
     for (int r = 0; r < R; ++r) {
@@ -156,7 +163,7 @@ int8_mv2_kernel(const __grid_constant__ Mv2Params p) {
     }
   };
   if (lane == 0)
-    for (long i = 0; i < T && i < STAGES; ++i) issue(i);
+    for (int i = 0; i < T && i < STAGES; ++i) issue(i);
 
   // activations come from the previous kernel: wait for it only now
   pdl_wait();
@@ -165,24 +172,21 @@ int8_mv2_kernel(const __grid_constant__ Mv2Params p) {
   // ---- stage x (slices slice_lo, slice_lo+1) in the permuted layout ----
   const int nsl = (u1 > u0) ? (int)((u1 - 1) / n_rg) - slice_lo + 1 : 0;
   for (int sl = 0; sl < nsl; ++sl) {
-    const int n4 = M * KS / 4;
-    // four independent 16-byte loads in flight per thread
-    for (int t0 = threadIdx.x; t0 < n4; t0 += 4 * blockDim.x) {
-      float4 v[4];
+    // per token: KS/4 float4s, four independent 16-byte loads in flight per thread
+    for (int m = 0; m < M; ++m) {
+      const float *src = p.x + (size_t)m * p.x_stride + (size_t)(slice_lo + sl) * KS;
+      float *dst = xs + ((size_t)sl * MT + m) * KS;
+      for (int k0 = 4 * threadIdx.x; k0 < KS; k0 += 16 * blockDim.x) {
+        float4 v[4];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int t = t0 + u * blockDim.x;
-        if (t < n4) {
-          const int m = t / (KS / 4), k = (t % (KS / 4)) * 4;
-          v[u] = *reinterpret_cast<const float4 *>(p.x + (size_t)m * p.x_stride + (size_t)(slice_lo + sl) * KS + k);
+        for (int u = 0; u < 4; ++u) {
+          const int k = k0 + 4 * u * blockDim.x;
+          if (k < KS) v[u] = *reinterpret_cast<const float4 *>(src + k);
         }
-      }
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int t = t0 + u * blockDim.x;
-        if (t < n4) {
-          const int m = t / (KS / 4), k = (t % (KS / 4)) * 4;
-          *reinterpret_cast<float4 *>(xs + ((size_t)sl * MT + m) * KS + xperm(k)) = v[u];
+        for (int u = 0; u < 4; ++u) {
+          const int k = k0 + 4 * u * blockDim.x;
+          if (k < KS) *reinterpret_cast<float4 *>(dst + xperm(k)) = v[u];
         }
       }
     }
@@ -223,19 +227,19 @@ int8_mv2_kernel(const __grid_constant__ Mv2Params p) {
     }
     if (!mbar_wait(&sm.nbar, 0) && threadIdx.x == 0 && p.err) atomicExch(p.err, -QASR_ERR_TIMEOUT);
     __syncthreads();
-    const int n4 = M * KS / 4;
-    for (int t = threadIdx.x; t < n4; t += blockDim.x) {
-      const int m = t / (KS / 4), slot = (t % (KS / 4)) * 4;
-      float4 *v4 = reinterpret_cast<float4 *>(xs + (size_t)m * KS + slot);
+    for (int slot = 4 * threadIdx.x; slot < KS; slot += 4 * blockDim.x) {
       const int k = xperm_inv(slot);
-      const float inv = sm.inv[m];
       const float4 wn = *reinterpret_cast<const float4 *>(nws + k);
-      float4 v = *v4;
-      v.x = __fmul_rn(__fmul_rn(v.x, inv), wn.x);
-      v.y = __fmul_rn(__fmul_rn(v.y, inv), wn.y);
-      v.z = __fmul_rn(__fmul_rn(v.z, inv), wn.z);
-      v.w = __fmul_rn(__fmul_rn(v.w, inv), wn.w);
-      *v4 = v;
+      for (int m = 0; m < M; ++m) {
+        float4 *v4 = reinterpret_cast<float4 *>(xs + (size_t)m * KS + slot);
+        const float inv = sm.inv[m];
+        float4 v = *v4;
+        v.x = __fmul_rn(__fmul_rn(v.x, inv), wn.x);
+        v.y = __fmul_rn(__fmul_rn(v.y, inv), wn.y);
+        v.z = __fmul_rn(__fmul_rn(v.z, inv), wn.z);
+        v.w = __fmul_rn(__fmul_rn(v.w, inv), wn.w);
+        *v4 = v;
+      }
     }
   }
   // rows m >= M of the staged x are never read (token loops stop at M)
@@ -246,7 +250,8 @@ int8_mv2_kernel(const __grid_constant__ Mv2Params p) {
   const bool writer = (lane & ((32 / V) - 1)) == 0;
   unsigned long long best = 0ull;
   bool failed = false;
-  long fail_item = -1;
+  int fail_item = -1;
+  int cc = 0, cslice = (u0 + warp) / n_rg, crg = (u0 + warp) % n_rg;  // consumer cursor
 
   float acc[R][MT];
 #pragma unroll
@@ -254,17 +259,22 @@ int8_mv2_kernel(const __grid_constant__ Mv2Params p) {
 #pragma unroll
     for (int m = 0; m < MT; ++m) acc[r][m] = 0.0f;
 
-  for (long i = 0; i < T; ++i) {
-    const int st = (int)(i % STAGES);
+  for (int i = 0; i < T; ++i) {
+    const int st = i % STAGES;
     if (!mbar_wait(&sm.bar[warp][st], (unsigned)((i / STAGES) & 1))) {
       failed = true;
       fail_item = i;
       break;
     }
-    const long j = i / nchunk;
-    const int c = (int)(i % nchunk);
-    const long u = u0 + warp + j * kMv2Warps;
-    const int slice = (int)(u / n_rg), rg = (int)(u % n_rg);
+    const int c = cc, slice = cslice, rg = crg;
+    if (++cc == nchunk) {
+      cc = 0;
+      crg += kMv2Warps;
+      while (crg >= n_rg) {
+        crg -= n_rg;
+        ++cslice;
+      }
+    }
     const int8_t *wb = mybuf + (size_t)st * R * KC;
     // epilogue operands of this lane's (row, token), loaded now so their
     // latency hides under the unit's arithmetic
@@ -396,7 +406,7 @@ int8_mv2_kernel(const __grid_constant__ Mv2Params p) {
   if (failed) {
     // report, then let every copy this warp issued land before the CTA exits
     if (lane == 0 && p.err) atomicExch(p.err, -QASR_ERR_TIMEOUT);
-    for (long k = fail_item; k < T && k < fail_item + STAGES; ++k)
+    for (int k = fail_item; k < T && k < fail_item + STAGES; ++k)
       mbar_wait(&sm.bar[warp][k % STAGES], (unsigned)((k / STAGES) & 1));
   }
 
