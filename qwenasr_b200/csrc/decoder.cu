@@ -58,6 +58,7 @@ struct qasr_decoder {
   int s_oproj = 1, s_down = 1;
   unsigned long long *am_keys = nullptr;
   int32_t *tok = nullptr, *pos = nullptr, *next = nullptr;
+  int8_t *tile_tmp = nullptr;  // natural-layout staging for weight uploads
   int *err = nullptr;
   int32_t *h_tok = nullptr, *h_pos = nullptr, *h_next = nullptr;  // pinned staging
   int *h_err = nullptr;
@@ -70,9 +71,11 @@ struct qasr_decoder {
 namespace qasr {
 
 // Embedding gather for the step's tokens (f32 or int8 table).
+// A tied INT8 table is stored only in the lm head's tiled layout; the
+// gather then reads it through mv2_tiled_offset.
 __global__ void step_embed_kernel(float *__restrict__ x, const void *__restrict__ table,
                                   const float *__restrict__ scales, int is_int8, const int32_t *__restrict__ ids,
-                                  int dim, int vocab, int *err) {
+                                  int dim, int vocab, int *err, int tiled) {
   const int m = blockIdx.x;
   int id = ids[m];
   if (id < 0 || id >= vocab) {
@@ -81,11 +84,15 @@ __global__ void step_embed_kernel(float *__restrict__ x, const void *__restrict_
   }
   float4 *d = reinterpret_cast<float4 *>(x + (size_t)m * dim);
   if (is_int8) {
-    const uint32_t *src = reinterpret_cast<const uint32_t *>(static_cast<const int8_t *>(table) + (size_t)id * dim);
+    const int8_t *tab = static_cast<const int8_t *>(table);
+    const uint32_t *src = reinterpret_cast<const uint32_t *>(tab + (size_t)id * dim);
     const float s = scales[id];
+    const int kc = mv2_chunk(dim);
     for (int c = threadIdx.x; c < dim / 4; c += blockDim.x) {
       float f[4];
-      i8x4_to_f32(src[c], f);
+      const uint32_t wv = tiled ? *reinterpret_cast<const uint32_t *>(tab + mv2_tiled_offset(id, 4 * c, dim, kc, vocab / 4))
+                                : src[c];
+      i8x4_to_f32(wv, f);
       d[c] = make_float4(__fmul_rn(f[0], s), __fmul_rn(f[1], s), __fmul_rn(f[2], s), __fmul_rn(f[3], s));
     }
   } else {
@@ -164,6 +171,8 @@ extern "C" qasr_decoder *qasr_decoder_create(const qasr_decoder_config *cfg, int
     ld.in_norm = (float *)dalloc(d, (size_t)H * 4, &rc);
     ld.post_norm = (float *)dalloc(d, (size_t)H * 4, &rc);
   }
+  d->tile_tmp = (int8_t *)dalloc(
+      d, std::max(std::max((size_t)qkv_rows * H, (size_t)2 * I * H), std::max((size_t)H * q_dim, (size_t)H * I)), &rc);
   d->embed = dalloc(d, (size_t)cfg->vocab * H * (cfg->embed_is_int8 ? 1 : 4), &rc);
   if (cfg->embed_is_int8) d->embed_s = (float *)dalloc(d, (size_t)cfg->vocab * 4, &rc);
   d->norm = (float *)dalloc(d, (size_t)H * 4, &rc);
@@ -241,18 +250,23 @@ extern "C" int qasr_decoder_set_layer(qasr_decoder *d, int layer, const qasr_dec
   const qasr_decoder_config &c = d->cfg;
   const size_t H = c.hidden, I = c.inter, q_dim = (size_t)c.n_heads * c.head_dim, kv = (size_t)c.n_kv_heads * c.head_dim;
   LayerDev &ld = d->layers[layer];
+  int8_t *tmp = d->tile_tmp;  // natural layout staging, re-tiled into the engine copy
   int rc = 0;
-  if (!rc) rc = copy_in(d, ld.wqkv, w->wq, q_dim * H, "wq");
-  if (!rc) rc = copy_in(d, ld.wqkv + q_dim * H, w->wk, kv * H, "wk");
-  if (!rc) rc = copy_in(d, ld.wqkv + (q_dim + kv) * H, w->wv, kv * H, "wv");
+  if (!rc) rc = copy_in(d, tmp, w->wq, q_dim * H, "wq");
+  if (!rc) rc = copy_in(d, tmp + q_dim * H, w->wk, kv * H, "wk");
+  if (!rc) rc = copy_in(d, tmp + (q_dim + kv) * H, w->wv, kv * H, "wv");
+  if (!rc) rc = mv2_tile_weights(ld.wqkv, tmp, (int)(q_dim + 2 * kv), (int)H, 1, d->stream);
   if (!rc) rc = copy_in(d, ld.sqkv, w->wq_s, q_dim * 4, "wq_s");
   if (!rc) rc = copy_in(d, ld.sqkv + q_dim, w->wk_s, kv * 4, "wk_s");
   if (!rc) rc = copy_in(d, ld.sqkv + q_dim + kv, w->wv_s, kv * 4, "wv_s");
-  if (!rc) rc = copy_in(d, ld.wo, w->wo, H * q_dim, "wo");
+  if (!rc) rc = copy_in(d, tmp, w->wo, H * q_dim, "wo");
+  if (!rc) rc = mv2_tile_weights(ld.wo, tmp, (int)H, (int)q_dim, d->s_oproj, d->stream);
   if (!rc) rc = copy_in(d, ld.so, w->wo_s, H * 4, "wo_s");
-  if (!rc) rc = copy_in(d, ld.gate_up, w->gate_up, 2 * I * H, "gate_up");
+  if (!rc) rc = copy_in(d, tmp, w->gate_up, 2 * I * H, "gate_up");
+  if (!rc) rc = mv2_tile_weights(ld.gate_up, tmp, (int)(2 * I), (int)H, 1, d->stream);
   if (!rc) rc = copy_in(d, ld.sgu, w->gate_up_s, 2 * I * 4, "gate_up_s");
-  if (!rc) rc = copy_in(d, ld.down, w->down, H * I, "down");
+  if (!rc) rc = copy_in(d, tmp, w->down, H * I, "down");
+  if (!rc) rc = mv2_tile_weights(ld.down, tmp, (int)H, (int)I, d->s_down, d->stream);
   if (!rc) rc = copy_in(d, ld.sdown, w->down_s, H * 4, "down_s");
   if (!rc) rc = copy_in(d, ld.q_norm, w->q_norm, c.head_dim * 4, "q_norm");
   if (!rc) rc = copy_in(d, ld.k_norm, w->k_norm, c.head_dim * 4, "k_norm");
@@ -271,27 +285,39 @@ extern "C" int qasr_decoder_set_globals(qasr_decoder *d, const void *embed, cons
   cudaSetDevice(d->device);
   const qasr_decoder_config &c = d->cfg;
   const size_t VH = (size_t)c.vocab * c.hidden;
-  int rc = copy_in(d, d->embed, embed, VH * (c.embed_is_int8 ? 1 : 4), "embed");
+  // INT8 tables are used by the lm head, which reads them in the tiled layout
+  auto upload_tiled = [&](int8_t *dst, const void *src, const char *what) {
+    void *tmp = nullptr;
+    int r = cuda_status(cudaMalloc(&tmp, VH), "qasr_decoder_set_globals: staging");
+    if (!r) r = copy_in(d, tmp, src, VH, what);
+    if (!r) r = mv2_tile_weights(dst, static_cast<const int8_t *>(tmp), c.vocab, c.hidden, 1, d->stream);
+    if (!r) r = cuda_status(cudaStreamSynchronize(d->stream), what);
+    if (tmp) cudaFree(tmp);
+    return r;
+  };
+  int rc = QASR_OK;
+  if (!lm_head && !c.embed_is_int8) {
+    set_error("qasr_decoder_set_globals: a tied lm head needs the INT8 embedding table");
+    return QASR_ERR_INVALID;
+  }
+  if (c.embed_is_int8 && !lm_head) {
+    rc = upload_tiled(static_cast<int8_t *>(d->embed), embed, "embed");  // tied: one tiled copy serves both
+    d->lm_tied = true;
+  } else {
+    rc = copy_in(d, d->embed, embed, VH * (c.embed_is_int8 ? 1 : 4), "embed");
+    d->lm_tied = false;
+  }
   if (!rc && c.embed_is_int8) rc = copy_in(d, d->embed_s, embed_scales, (size_t)c.vocab * 4, "embed_scales");
   if (!rc) rc = copy_in(d, d->norm, norm, (size_t)c.hidden * 4, "norm");
-  if (!rc) {
-    if (lm_head) {
-      if (!d->lm) {
-        int arc = 0;
-        d->lm = (int8_t *)dalloc(d, VH, &arc);
-        d->lm_s = (float *)dalloc(d, (size_t)c.vocab * 4, &arc);
-        if (arc) return arc;
-      }
-      rc = copy_in(d, d->lm, lm_head, VH, "lm_head");
-      if (!rc) rc = copy_in(d, d->lm_s, lm_head_s, (size_t)c.vocab * 4, "lm_head_s");
-      d->lm_tied = false;
-    } else {
-      if (!c.embed_is_int8) {
-        set_error("qasr_decoder_set_globals: a tied lm head needs the INT8 embedding table");
-        return QASR_ERR_INVALID;
-      }
-      d->lm_tied = true;
+  if (!rc && lm_head) {
+    if (!d->lm) {
+      int arc = 0;
+      d->lm = (int8_t *)dalloc(d, VH, &arc);
+      d->lm_s = (float *)dalloc(d, (size_t)c.vocab * 4, &arc);
+      if (arc) return arc;
     }
+    rc = upload_tiled(d->lm, lm_head, "lm_head");
+    if (!rc) rc = copy_in(d, d->lm_s, lm_head_s, (size_t)c.vocab * 4, "lm_head_s");
   }
   if (!rc) rc = cuda_status(cudaStreamSynchronize(d->stream), "qasr_decoder_set_globals");
   return rc;
@@ -359,7 +385,8 @@ static int enqueue_step(qasr_decoder *d, int M, StepMarks *marks = nullptr) {
   const int q_dim = c.n_heads * hd, kv_dim = c.n_kv_heads * hd, qkv_rows = q_dim + 2 * kv_dim;
   const int G = c.n_heads / c.n_kv_heads;
   const void *emb_tab = d->embed;
-  step_embed_kernel<<<M, 256, 0, st>>>(d->x, emb_tab, d->embed_s, c.embed_is_int8, d->tok, H, c.vocab, d->err);
+  step_embed_kernel<<<M, 256, 0, st>>>(d->x, emb_tab, d->embed_s, c.embed_is_int8, d->tok, H, c.vocab, d->err,
+                                       d->lm_tied ? 1 : 0);
   MARK(QASR_K_EMBED);
   int rc = launch_status("decode step: embed");
   auto mvp = [&](const float *x, long xs, const float *nw, const int8_t *w, const float *sc, float *y, long ys, int K,
@@ -369,6 +396,7 @@ static int enqueue_step(qasr_decoder *d, int M, StepMarks *marks = nullptr) {
     p.M = M; p.K = K; p.N = N; p.S = S; p.KS = K / S; p.KC = mv2_chunk(K / S);
     p.partial = d->mv_partial; p.rg_counter = d->mv_ctr;
     p.keys = d->am_keys; p.counter = d->am_ctr; p.ids = d->next; p.err = d->err;
+    p.tiled = true;
     return p;
   };
   auto mv = [&](const float *x, long xs, const float *nw, const int8_t *w, const float *sc, float *y, long ys, int K,

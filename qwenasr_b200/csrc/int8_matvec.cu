@@ -257,7 +257,7 @@ static int try_mv2(const float *x, long xs, const float *nw, float eps, const in
   p.y = y; p.y_stride = ys; p.M = M; p.K = K; p.N = N;
   p.S = nw ? 1 : mv2_pick_slices(N, K, M, e);
   p.KS = K / p.S;
-  p.KC = mv2_chunk(p.KS);
+  p.KC = 512;  // row-major weights: one copy per 512-byte row segment
   if (p.S == 1 && (size_t)8 * K * 4 > 96 * 1024) return QASR_ERR_UNSUPPORTED;
   int rc;
   if (p.S > 1) {

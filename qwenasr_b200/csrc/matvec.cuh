@@ -55,11 +55,30 @@ struct Mv2Params {
   int32_t *ids;
   int *err;              // set to -QASR_ERR_TIMEOUT if a bounded wait gives up (may be null)
   QkvPostParams post;    // MvEpi::QkvPost only
+  bool tiled;            // w is in the tiled layout of mv2_tile_weights (same S, KC)
 };
 
 int mv2_launch(const Mv2Params &p, MvEpi e, cudaStream_t st, bool pdl);
 int mv2_pick_slices(int N, int K, int M, MvEpi e);
-inline int mv2_chunk(int KS) { return 512; }
+__host__ __device__ inline int mv2_chunk(int KS) { return KS % 1024 == 0 ? 1024 : 512; }  // tiled layout
+
+// Tiled layout of an [N, K] INT8 matrix for a split into S slices of KS
+// columns with pipeline chunks of KC columns and R = 4 rows per unit: items
+// (slice, row group, chunk) stored one after another, each item the 4 row
+// segments of KC bytes; inside every 512-byte block of a segment, byte
+// 16L + 4q + e holds column 4L + 128q + e (L < 32, q < 4, e < 4), so that a
+// warp's 16-byte weight reads and its 16-byte natural-layout x reads are both
+// bank-conflict free.  The same bytes as the row-major matrix, permuted.
+// Byte offset of element (row, k); n_rg = N / 4.
+__host__ __device__ inline size_t mv2_tiled_offset(int row, int k, int KS, int KC, int n_rg) {
+  const int slice = k / KS, ks = k % KS, c = ks / KC, kc = ks % KC;
+  const int blk = kc >> 9, kk = kc & 511;
+  const int pos = (blk << 9) + ((kk & 127) >> 2) * 16 + (kk >> 7) * 4 + (kk & 3);
+  const int rg = row >> 2, r = row & 3;
+  return ((((size_t)slice * n_rg + rg) * (KS / KC) + c) * 4 + r) * KC + pos;
+}
+// Re-tile an [N, K] row-major INT8 matrix for split S (device to device).
+int mv2_tile_weights(int8_t *dst, const int8_t *src, int N, int K, int S, cudaStream_t st);
 inline int mv2_rows(int M) { return 4; }  // rows per warp unit
 
 // Enqueue one matvec.  R = rows per warp (1, 2, 4), 0 = automatic.

@@ -35,8 +35,9 @@
 namespace qasr {
 
 constexpr int kMv2Warps = 8;
+constexpr int kMv2R = 4;  // rows per unit (the engine tiles weights for it)
 constexpr int kMv2KC = 512;          // bytes of one row per pipeline stage
-constexpr int kMv2RingBytes = 4096;  // per-warp weight ring
+constexpr int kMv2RingBytes = 8192;  // per-warp weight ring
 constexpr int kMv2MaxStages = 8;
 constexpr int kMv2MaxSlices = 12;  // largest split-K factor
 
@@ -54,6 +55,7 @@ QASR_DEV int xperm_inv(int idx) {
 struct Mv2Smem {
   uint64_t bar[kMv2Warps][kMv2MaxStages];
   uint64_t nbar;  // norm weights copy
+  uint64_t xbar;  // x staging copies (tiled layout)
   float inv[8];
   int last;
   unsigned long long best[kMv2Warps * 32];
@@ -106,14 +108,18 @@ QASR_DEV void qkv_head_post(const QkvPostParams &q, float eps, int h, int m, flo
     reinterpret_cast<float4 *>(q.k_cache + cache_row + (h - q.n_heads) * 128)[lane] = o;
 }
 
-template <int MT, int R, MvEpi E, bool NORM>
+// TILED: the weights are in the engine's tiled layout (mv2_tile_weights):
+// every pipeline item is one contiguous bulk copy, and x is used in its
+// natural layout (staged with one bulk copy per token row).  Otherwise the
+// weights are the reference's row-major layout (one copy per row segment)
+// and x is staged through registers into the permuted layout.
+template <int MT, int R, MvEpi E, bool NORM, bool TILED>
 __global__ void __launch_bounds__(kMv2Warps * 32, 2)
 int8_mv2_kernel(const __grid_constant__ Mv2Params p) {
-  constexpr int STAGES = kMv2RingBytes / (R * kMv2KC);
-  static_assert(STAGES <= kMv2MaxStages, "ring");
   extern __shared__ __align__(128) unsigned char smem_raw[];
   Mv2Smem &sm = *reinterpret_cast<Mv2Smem *>(smem_raw);
-  constexpr int KC = kMv2KC;
+  const int KC = p.KC;
+  const int STAGES = kMv2RingBytes / (R * KC);
   int8_t *wbuf = reinterpret_cast<int8_t *>(smem_raw + ((sizeof(Mv2Smem) + 127) & ~size_t(127)));
   float *xs = reinterpret_cast<float *>(wbuf + (size_t)kMv2Warps * kMv2RingBytes);
   float *nws = xs + (size_t)(p.S == 1 ? 1 : 2) * MT * p.KS;  // NORM: norm weights [K]
@@ -131,6 +137,7 @@ int8_mv2_kernel(const __grid_constant__ Mv2Params p) {
 
   if (threadIdx.x < kMv2Warps * STAGES) mbar_init(&sm.bar[threadIdx.x / STAGES][threadIdx.x % STAGES], 1);
   if (threadIdx.x == kMv2Warps * STAGES) mbar_init(&sm.nbar, 1);
+  if (threadIdx.x == kMv2Warps * STAGES + 1) mbar_init(&sm.xbar, 1);
   mbar_fence_init();
   __syncthreads();
   if constexpr (NORM) {  // constant operand: fetch it before waiting for the previous kernel
@@ -155,11 +162,16 @@ int8_mv2_kernel(const __grid_constant__ Mv2Params p) {
     }
     const int st = i % STAGES;
     mbar_arrive_expect_tx(&sm.bar[warp][st], R * KC);
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      const int row = min(rg * R + r, N - 1);
-      bulk_g2s(mybuf + ((size_t)st * R + r) * KC, p.w + (size_t)row * K + (size_t)slice * KS + (size_t)c * KC, KC,
+    if constexpr (TILED) {
+      bulk_g2s(mybuf + (size_t)st * R * KC, p.w + (((size_t)slice * n_rg + rg) * nchunk + c) * R * KC, R * KC,
                &sm.bar[warp][st]);
+    } else {
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const int row = min(rg * R + r, N - 1);
+        bulk_g2s(mybuf + ((size_t)st * R + r) * KC, p.w + (size_t)row * K + (size_t)slice * KS + (size_t)c * KC, KC,
+                 &sm.bar[warp][st]);
+      }
     }
   };
   if (lane == 0)
@@ -171,7 +183,17 @@ int8_mv2_kernel(const __grid_constant__ Mv2Params p) {
 
   // ---- stage x (slices slice_lo, slice_lo+1) in the permuted layout ----
   const int nsl = (u1 > u0) ? (int)((u1 - 1) / n_rg) - slice_lo + 1 : 0;
-  for (int sl = 0; sl < nsl; ++sl) {
+  if constexpr (TILED) {  // natural layout: one bulk copy per (slice, token) row
+    if (threadIdx.x == 0 && nsl > 0) {
+      mbar_arrive_expect_tx(&sm.xbar, (unsigned)(nsl * M * KS * 4));
+      for (int sl = 0; sl < nsl; ++sl)
+        for (int m = 0; m < M; ++m)
+          bulk_g2s(xs + ((size_t)sl * MT + m) * KS, p.x + (size_t)m * p.x_stride + (size_t)(slice_lo + sl) * KS,
+                   (unsigned)KS * 4, &sm.xbar);
+    }
+    if (nsl > 0 && !mbar_wait(&sm.xbar, 0) && p.err) atomicExch(p.err, -QASR_ERR_TIMEOUT);
+  }
+  for (int sl = 0; sl < (TILED ? 0 : nsl); ++sl) {
     // per token: KS/4 float4s, four independent 16-byte loads in flight per thread
     for (int m = 0; m < M; ++m) {
       const float *src = p.x + (size_t)m * p.x_stride + (size_t)(slice_lo + sl) * KS;
@@ -204,23 +226,23 @@ int8_mv2_kernel(const __grid_constant__ Mv2Params p) {
         for (; j + 16 <= n16; j += 16) {
           float v[16];
 #pragma unroll
-          for (int t = 0; t < 16; ++t) v[t] = xr[xperm(16 * (j + t) + lane)];
+          for (int t = 0; t < 16; ++t) v[t] = xr[TILED ? 16 * (j + t) + lane : xperm(16 * (j + t) + lane)];
 #pragma unroll
           for (int t = 0; t < 16; ++t) acc = fmaf(v[t], v[t], acc);
         }
         for (; j < n16; ++j) {
-          const float v = xr[xperm(16 * j + lane)];
+          const float v = xr[TILED ? 16 * j + lane : xperm(16 * j + lane)];
           acc = fmaf(v, v, acc);
         }
         if ((n & 15) >= 8 && lane < 8) {
-          const float v = xr[xperm(16 * n16 + lane)];
+          const float v = xr[TILED ? 16 * n16 + lane : xperm(16 * n16 + lane)];
           acc = fmaf(v, v, acc);
         }
       }
       float sum = hsum16_avx_order(acc);
       if (lane == 0)
         for (int i = avx_vector_extent(n); i < n; ++i) {
-          const float v = xr[xperm(i)];
+          const float v = xr[TILED ? i : xperm(i)];
           sum = __fadd_rn(sum, __fmul_rn(v, v));
         }
       if (lane == 0) sm.inv[warp] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)n), p.eps)));
@@ -228,7 +250,7 @@ int8_mv2_kernel(const __grid_constant__ Mv2Params p) {
     if (!mbar_wait(&sm.nbar, 0) && threadIdx.x == 0 && p.err) atomicExch(p.err, -QASR_ERR_TIMEOUT);
     __syncthreads();
     for (int slot = 4 * threadIdx.x; slot < KS; slot += 4 * blockDim.x) {
-      const int k = xperm_inv(slot);
+      const int k = TILED ? slot : xperm_inv(slot);
       const float4 wn = *reinterpret_cast<const float4 *>(nws + k);
       for (int m = 0; m < M; ++m) {
         float4 *v4 = reinterpret_cast<float4 *>(xs + (size_t)m * KS + slot);
@@ -433,6 +455,27 @@ int8_mv2_kernel(const __grid_constant__ Mv2Params p) {
   }
 }
 
+// ------------------------------------------------------------ weight tiling --
+__global__ void tile_weights_kernel(int8_t *__restrict__ dst, const int8_t *__restrict__ src, int N, int K, int KS,
+                                    int KC) {
+  const long t = (long)blockIdx.x * blockDim.x + threadIdx.x;  // one 4-byte group
+  if (t >= (long)N * K / 4) return;
+  const int row = (int)(t / (K / 4)), k = (int)(t % (K / 4)) * 4;
+  const uint32_t v = *reinterpret_cast<const uint32_t *>(src + (size_t)row * K + k);
+  *reinterpret_cast<uint32_t *>(dst + mv2_tiled_offset(row, k, KS, KC, N / 4)) = v;
+}
+
+int mv2_tile_weights(int8_t *dst, const int8_t *src, int N, int K, int S, cudaStream_t st) {
+  if (N % kMv2R || K % 512 || K % S || (K / S) % 512 || !dst || !src || dst == src) {
+    set_error("mv2_tile_weights: unsupported shape N=%d K=%d S=%d", N, K, S);
+    return QASR_ERR_INVALID;
+  }
+  const int KS = K / S, KC = mv2_chunk(KS);
+  const long n = (long)N * K / 4;
+  tile_weights_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(dst, src, N, K, KS, KC);
+  return launch_status("mv2_tile_weights");
+}
+
 // ------------------------------------------------------------------- host --
 static int mv2_sms() {
   static int sms = 0;
@@ -446,6 +489,7 @@ static int mv2_sms() {
 }
 
 static size_t mv2_smem_bytes(int MT, int KS, int nsl, int K) {
+  (void)0;
   return ((sizeof(Mv2Smem) + 127) & ~size_t(127)) + (size_t)kMv2Warps * kMv2RingBytes +
          (size_t)nsl * MT * KS * sizeof(float) + (size_t)K * sizeof(float);
 }
@@ -470,7 +514,7 @@ int mv2_pick_slices(int N, int K, int M, MvEpi e) {
   return best;
 }
 
-template <int MT, int R, MvEpi E, bool NORM>
+template <int MT, int R, MvEpi E, bool NORM, bool TILED>
 static int launch_t(const Mv2Params &p, cudaStream_t st, bool pdl) {
   const long n_rg = (p.N + R - 1) / R;
   const long U = n_rg * p.S;
@@ -481,7 +525,7 @@ static int launch_t(const Mv2Params &p, cudaStream_t st, bool pdl) {
   const size_t smem = mv2_smem_bytes(MT, p.KS, nsl, NORM ? p.K : 0);
   static bool attr_done = false;
   if (!attr_done) {
-    int rc = cuda_status(cudaFuncSetAttribute(int8_mv2_kernel<MT, R, E, NORM>,
+    int rc = cuda_status(cudaFuncSetAttribute(int8_mv2_kernel<MT, R, E, NORM, TILED>,
                                               cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024),
                          "int8 matvec: shared memory opt-in");
     if (rc) return rc;
@@ -497,19 +541,24 @@ static int launch_t(const Mv2Params &p, cudaStream_t st, bool pdl) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cuda_status(cudaLaunchKernelEx(&cfg, int8_mv2_kernel<MT, R, E, NORM>, p), "int8 matvec launch");
+  return cuda_status(cudaLaunchKernelEx(&cfg, int8_mv2_kernel<MT, R, E, NORM, TILED>, p), "int8 matvec launch");
 }
 
+template <MvEpi E, bool NORM, bool TILED>
+static int launch_m(const Mv2Params &p, cudaStream_t st, bool pdl) {
+  if (p.M <= 1) return launch_t<1, 4, E, NORM, TILED>(p, st, pdl);
+  if (p.M <= 2) return launch_t<2, 4, E, NORM, TILED>(p, st, pdl);
+  if (p.M <= 4) return launch_t<4, 4, E, NORM, TILED>(p, st, pdl);
+  return launch_t<8, 4, E, NORM, TILED>(p, st, pdl);
+}
 template <MvEpi E, bool NORM>
 static int launch_e(const Mv2Params &p, cudaStream_t st, bool pdl) {
-  if (p.M <= 1) return launch_t<1, 4, E, NORM>(p, st, pdl);
-  if (p.M <= 2) return launch_t<2, 4, E, NORM>(p, st, pdl);
-  if (p.M <= 4) return launch_t<4, 4, E, NORM>(p, st, pdl);
-  return launch_t<8, 4, E, NORM>(p, st, pdl);
+  return p.tiled ? launch_m<E, NORM, true>(p, st, pdl) : launch_m<E, NORM, false>(p, st, pdl);
 }
 
 int mv2_launch(const Mv2Params &p, MvEpi e, cudaStream_t st, bool pdl) {
-  if (p.M < 1 || p.M > 8 || p.K % 512 || p.KS * p.S != p.K || p.KC != kMv2KC || p.KS % p.KC ||
+  if (p.M < 1 || p.M > 8 || p.K % 512 || p.KS * p.S != p.K || (p.KC != 512 && p.KC != 1024) || p.KS % p.KC ||
+      (!p.tiled && p.KC != kMv2KC) || (p.tiled && p.N % kMv2R) ||
       (p.S > 1 && (!p.partial || !p.rg_counter)) || (p.norm_w && p.S != 1) ||
       (e == MvEpi::Argmax && (p.S != 1 || !p.keys || !p.counter || !p.ids)) ||
       (e == MvEpi::QkvPost && (p.S != 1 || !p.post.head_ctr || !p.post.positions)) ||
