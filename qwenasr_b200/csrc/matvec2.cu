@@ -308,16 +308,17 @@ int8_mv2_kernel(const __grid_constant__ Mv2Params p) {
     if constexpr (E == MvEpi::Residual)
       if (S == 1 && my_m < M) pre_aux = p.y[(size_t)my_m * p.y_stride + pre_row];
     const float *xb = xs + (size_t)(slice - slice_lo) * MT * KS + (size_t)c * KC + 4 * lane;
-    {
+#pragma unroll 1
+    for (int blk = 0; blk < KC; blk += 512) {  // 512-byte blocks of the chunk
       uint4 wv[R];
 #pragma unroll
-      for (int r = 0; r < R; ++r) wv[r] = *reinterpret_cast<const uint4 *>(wb + (size_t)r * KC + 16 * lane);
+      for (int r = 0; r < R; ++r) wv[r] = *reinterpret_cast<const uint4 *>(wb + (size_t)r * KC + blk + 16 * lane);
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         float4 xv[MT];
 #pragma unroll
         for (int m = 0; m < MT; ++m)
-          xv[m] = m < M ? *reinterpret_cast<const float4 *>(xb + (size_t)m * KS + 128 * q)
+          xv[m] = m < M ? *reinterpret_cast<const float4 *>(xb + (size_t)m * KS + blk + 128 * q)
                         : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
         for (int r = 0; r < R; ++r) {
