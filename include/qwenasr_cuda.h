@@ -193,6 +193,21 @@ int qasr_final_norm_lmhead_argmax(int32_t *ids_out, float *logits_out, const flo
                                   const int8_t *w, const float *scales, int M, int hidden, int vocab, float eps,
                                   void *stream);
 
+/* Same result as qasr_final_norm_lmhead_argmax, but the call allocates no
+ * device memory.  No counterpart in the reference (its CPU path has no device
+ * allocations to avoid).  For hosts that may not allocate once serving has
+ * started: a runtime with its own pool or a hard memory budget.  The argmax
+ * scratch is a fixed 256-byte array in the library; its device address is
+ * looked up on the first call on each device (make that first call before any
+ * stream capture).  Limits: M <= 8, hidden a multiple of 512 and <= 3072,
+ * x / w / norm_w 16-byte aligned; larger M returns QASR_ERR_INVALID, other
+ * shapes QASR_ERR_UNSUPPORTED.  The scratch is shared by all calls on one
+ * device, so calls that overlap in time on one device race and must be
+ * serialised. */
+int qasr_final_norm_lmhead_argmax_noalloc(int32_t *ids_out, float *logits_out, const float *x, const float *norm_w,
+                                          const int8_t *w, const float *scales, int M, int hidden, int vocab,
+                                          float eps, void *stream);
+
 /* ======================================================================
  * Decoder engine
  * ==================================================================== */

@@ -72,6 +72,7 @@ _SIGS = {
     "qasr_int8_norm_gateup_swiglu": (I, [P, P, P, P, P, I, I, I, F, P]),
     "qasr_int8_matvec_residual": (I, [P, P, P, P, I, I, I, P]),
     "qasr_final_norm_lmhead_argmax": (I, [P, P, P, P, P, P, I, I, I, F, P]),
+    "qasr_final_norm_lmhead_argmax_noalloc": (I, [P, P, P, P, P, P, I, I, I, F, P]),
     "qasr_decoder_create": (P, [C.POINTER(DecoderConfig), I]),
     "qasr_decoder_free": (None, [P]),
     "qasr_decoder_set_layer": (I, [P, I, C.POINTER(DecLayerWeights)]),
