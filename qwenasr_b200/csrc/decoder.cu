@@ -13,15 +13,19 @@
 //   KV         k_cache/v_cache f32 [max_batch][n_layers][max_seq][kv_dim]:
 //              the reference's per-sequence KvCache layout, sequences stacked.
 //   RoPE       cos/sin [max_seq, head_dim], the RopeCache::ensure table.
-//   work       x, xn [B, hidden]; qkv [B, q+2kv]; q_out, attn [B, q_dim];
-//              h [B, inter]; attention partials/counters; argmax keys.
+//   work       x [B, hidden]; q_out, attn [B, q_dim]; h [B, inter];
+//              attention partials/counters; split accumulators of the INT8
+//              contractions; argmax keys.
+// Every INT8 matrix keeps the reference's row-major [out, in] layout and is
+// read by TMA through one tensor map (umma_weight_map) built at creation.
 //
 // One decode step = 2 + 5*n_layers kernels captured once per batch size in a
 // CUDA graph (programmatic dependent launch between the streaming kernels)
-// and replayed: embed gather; per layer RMSNorm+QKV matvec with the q/k
+// and replayed: embed gather; per layer RMSNorm+QKV contraction with the q/k
 // per-head norm + RoPE + KV append in its epilogue, attention, o-proj
-// (+residual), RMSNorm+gate/up matvec+SwiGLU, down matvec(+residual); final
-// RMSNorm + lm head + argmax.
+// (+residual), RMSNorm+gate/up contraction+SwiGLU, down contraction
+// (+residual); final RMSNorm + lm head + argmax.  The INT8 contractions run
+// on the tensor cores (umma_matvec.cu).
 #include <algorithm>
 #include <cstring>
 #include <vector>
@@ -29,11 +33,13 @@
 #include "attention.cuh"
 #include "common.cuh"
 #include "matvec.cuh"
+#include "umma.cuh"
 
 namespace qasr {
 
 struct LayerDev {
   int8_t *wqkv = nullptr, *wo = nullptr, *gate_up = nullptr, *down = nullptr;
+  CUtensorMap tm_qkv, tm_o, tm_gu, tm_down;
   float *sqkv = nullptr, *so = nullptr, *sgu = nullptr, *sdown = nullptr;
   float *q_norm = nullptr, *k_norm = nullptr, *in_norm = nullptr, *post_norm = nullptr;
 };
@@ -49,16 +55,16 @@ struct qasr_decoder {
   float *embed_s = nullptr, *norm = nullptr, *lm_s = nullptr;
   int8_t *lm = nullptr;
   bool lm_tied = false;
+  bool globals_ready = false;  // set_globals succeeded (the lm head tensor map exists)
   float *k_cache = nullptr, *v_cache = nullptr;
   float *rope_cos = nullptr, *rope_sin = nullptr;
-  float *x = nullptr, *xn = nullptr, *qkv = nullptr, *q_out = nullptr, *attn = nullptr, *h = nullptr;
-  float *partials = nullptr, *logits = nullptr, *mv_partial = nullptr;
-  unsigned *attn_ctr = nullptr, *am_ctr = nullptr, *mv_ctr = nullptr, *head_ctr = nullptr;
-  CUtensorMap tm_k, tm_v;
-  int s_oproj = 1, s_down = 1;
+  float *x = nullptr, *q_out = nullptr, *attn = nullptr, *h = nullptr;
+  float *partials = nullptr, *logits = nullptr;
+  unsigned *attn_ctr = nullptr, *am_ctr = nullptr, *u_ctr = nullptr;
+  unsigned long long *u_acc = nullptr;
+  CUtensorMap tm_k, tm_v, tm_lm;
   unsigned long long *am_keys = nullptr;
   int32_t *tok = nullptr, *pos = nullptr, *next = nullptr;
-  int8_t *tile_tmp = nullptr;  // natural-layout staging for weight uploads
   int *err = nullptr;
   int32_t *h_tok = nullptr, *h_pos = nullptr, *h_next = nullptr;  // pinned staging
   int *h_err = nullptr;
@@ -71,11 +77,9 @@ struct qasr_decoder {
 namespace qasr {
 
 // Embedding gather for the step's tokens (f32 or int8 table).
-// A tied INT8 table is stored only in the lm head's tiled layout; the
-// gather then reads it through mv2_tiled_offset.
 __global__ void step_embed_kernel(float *__restrict__ x, const void *__restrict__ table,
                                   const float *__restrict__ scales, int is_int8, const int32_t *__restrict__ ids,
-                                  int dim, int vocab, int *err, int tiled) {
+                                  int dim, int vocab, int *err) {
   const int m = blockIdx.x;
   int id = ids[m];
   if (id < 0 || id >= vocab) {
@@ -87,12 +91,9 @@ __global__ void step_embed_kernel(float *__restrict__ x, const void *__restrict_
     const int8_t *tab = static_cast<const int8_t *>(table);
     const uint32_t *src = reinterpret_cast<const uint32_t *>(tab + (size_t)id * dim);
     const float s = scales[id];
-    const int kc = mv2_chunk(dim);
     for (int c = threadIdx.x; c < dim / 4; c += blockDim.x) {
       float f[4];
-      const uint32_t wv = tiled ? *reinterpret_cast<const uint32_t *>(tab + mv2_tiled_offset(id, 4 * c, dim, kc, vocab / 4))
-                                : src[c];
-      i8x4_to_f32(wv, f);
+      i8x4_to_f32(src[c], f);
       d[c] = make_float4(__fmul_rn(f[0], s), __fmul_rn(f[1], s), __fmul_rn(f[2], s), __fmul_rn(f[3], s));
     }
   } else {
@@ -170,9 +171,11 @@ extern "C" qasr_decoder *qasr_decoder_create(const qasr_decoder_config *cfg, int
     ld.k_norm = (float *)dalloc(d, (size_t)hd * 4, &rc);
     ld.in_norm = (float *)dalloc(d, (size_t)H * 4, &rc);
     ld.post_norm = (float *)dalloc(d, (size_t)H * 4, &rc);
+    if (!rc) rc = umma_weight_map(&ld.tm_qkv, ld.wqkv, qkv_rows, H);
+    if (!rc) rc = umma_weight_map(&ld.tm_o, ld.wo, H, q_dim);
+    if (!rc) rc = umma_weight_map(&ld.tm_gu, ld.gate_up, 2 * I, H);
+    if (!rc) rc = umma_weight_map(&ld.tm_down, ld.down, H, I);
   }
-  d->tile_tmp = (int8_t *)dalloc(
-      d, std::max(std::max((size_t)qkv_rows * H, (size_t)2 * I * H), std::max((size_t)H * q_dim, (size_t)H * I)), &rc);
   d->embed = dalloc(d, (size_t)cfg->vocab * H * (cfg->embed_is_int8 ? 1 : 4), &rc);
   if (cfg->embed_is_int8) d->embed_s = (float *)dalloc(d, (size_t)cfg->vocab * 4, &rc);
   d->norm = (float *)dalloc(d, (size_t)H * 4, &rc);
@@ -182,21 +185,16 @@ extern "C" qasr_decoder *qasr_decoder_create(const qasr_decoder_config *cfg, int
   d->rope_cos = (float *)dalloc(d, (size_t)cfg->max_seq * hd * 4, &rc);
   d->rope_sin = (float *)dalloc(d, (size_t)cfg->max_seq * hd * 4, &rc);
   d->x = (float *)dalloc(d, (size_t)B * H * 4, &rc);
-  d->xn = (float *)dalloc(d, (size_t)B * H * 4, &rc);
-  d->qkv = (float *)dalloc(d, (size_t)B * qkv_rows * 4, &rc);
   d->q_out = (float *)dalloc(d, (size_t)B * q_dim * 4, &rc);
   d->attn = (float *)dalloc(d, (size_t)B * q_dim * 4, &rc);
   d->h = (float *)dalloc(d, (size_t)B * I * 4, &rc);
   const int G = cfg->n_heads / cfg->n_kv_heads;
   d->partials = (float *)dalloc(d, (size_t)(attn_grid() + B * cfg->n_kv_heads) * G * kAttnPartStride * 4, &rc);
   d->attn_ctr = (unsigned *)dalloc(d, (size_t)B * cfg->n_kv_heads * 4, &rc);
-  // split-K of the two hidden-sized projections (o-proj K=q_dim, down K=inter)
-  d->s_oproj = mv2_pick_slices(H, q_dim, B, MvEpi::Residual);
-  d->s_down = mv2_pick_slices(H, I, B, MvEpi::Residual);
-  const int s_max = std::max(d->s_oproj, d->s_down);
-  d->mv_partial = (float *)dalloc(d, (size_t)s_max * B * H * 4, &rc);
-  d->mv_ctr = (unsigned *)dalloc(d, (size_t)(H / 2 + 16) * 4, &rc);
-  d->head_ctr = (unsigned *)dalloc(d, (size_t)(cfg->n_heads + 2 * cfg->n_kv_heads) * 4, &rc);
+  // split accumulators of the INT8 contractions, sized for the widest one
+  const int n_max = std::max(std::max(qkv_rows, 2 * I), std::max(H, cfg->vocab));
+  d->u_acc = (unsigned long long *)dalloc(d, umma_acc_words(n_max) * 8, &rc);
+  d->u_ctr = (unsigned *)dalloc(d, umma_ctr_words(n_max) * 4, &rc);
   d->am_keys = (unsigned long long *)dalloc(d, 8 * 8, &rc);
   d->am_ctr = (unsigned *)dalloc(d, 16, &rc);
   d->tok = (int32_t *)dalloc(d, 8 * 4, &rc);
@@ -215,9 +213,8 @@ extern "C" qasr_decoder *qasr_decoder_create(const qasr_decoder_config *cfg, int
   rc = cuda_status(cudaMemsetAsync(d->k_cache, 0, kv_elems * 4, st), "memset");
   if (!rc) rc = cuda_status(cudaMemsetAsync(d->v_cache, 0, kv_elems * 4, st), "memset");
   if (!rc) rc = cuda_status(cudaMemsetAsync(d->attn_ctr, 0, (size_t)B * cfg->n_kv_heads * 4, st), "memset");
-  if (!rc) rc = cuda_status(cudaMemsetAsync(d->mv_ctr, 0, (size_t)(H / 2 + 16) * 4, st), "memset");
-  if (!rc)
-    rc = cuda_status(cudaMemsetAsync(d->head_ctr, 0, (size_t)(cfg->n_heads + 2 * cfg->n_kv_heads) * 4, st), "memset");
+  if (!rc) rc = cuda_status(cudaMemsetAsync(d->u_acc, 0, umma_acc_words(n_max) * 8, st), "memset");
+  if (!rc) rc = cuda_status(cudaMemsetAsync(d->u_ctr, 0, umma_ctr_words(n_max) * 4, st), "memset");
   if (!rc) rc = attn_make_tensor_map(&d->tm_k, d->k_cache, (long)B * L * cfg->max_seq, kv_dim);
   if (!rc) rc = attn_make_tensor_map(&d->tm_v, d->v_cache, (long)B * L * cfg->max_seq, kv_dim);
   if (!rc) rc = cuda_status(cudaMemsetAsync(d->am_keys, 0, 64, st), "memset");
@@ -250,23 +247,18 @@ extern "C" int qasr_decoder_set_layer(qasr_decoder *d, int layer, const qasr_dec
   const qasr_decoder_config &c = d->cfg;
   const size_t H = c.hidden, I = c.inter, q_dim = (size_t)c.n_heads * c.head_dim, kv = (size_t)c.n_kv_heads * c.head_dim;
   LayerDev &ld = d->layers[layer];
-  int8_t *tmp = d->tile_tmp;  // natural layout staging, re-tiled into the engine copy
   int rc = 0;
-  if (!rc) rc = copy_in(d, tmp, w->wq, q_dim * H, "wq");
-  if (!rc) rc = copy_in(d, tmp + q_dim * H, w->wk, kv * H, "wk");
-  if (!rc) rc = copy_in(d, tmp + (q_dim + kv) * H, w->wv, kv * H, "wv");
-  if (!rc) rc = mv2_tile_weights(ld.wqkv, tmp, (int)(q_dim + 2 * kv), (int)H, 1, d->stream);
+  if (!rc) rc = copy_in(d, ld.wqkv, w->wq, q_dim * H, "wq");
+  if (!rc) rc = copy_in(d, ld.wqkv + q_dim * H, w->wk, kv * H, "wk");
+  if (!rc) rc = copy_in(d, ld.wqkv + (q_dim + kv) * H, w->wv, kv * H, "wv");
   if (!rc) rc = copy_in(d, ld.sqkv, w->wq_s, q_dim * 4, "wq_s");
   if (!rc) rc = copy_in(d, ld.sqkv + q_dim, w->wk_s, kv * 4, "wk_s");
   if (!rc) rc = copy_in(d, ld.sqkv + q_dim + kv, w->wv_s, kv * 4, "wv_s");
-  if (!rc) rc = copy_in(d, tmp, w->wo, H * q_dim, "wo");
-  if (!rc) rc = mv2_tile_weights(ld.wo, tmp, (int)H, (int)q_dim, d->s_oproj, d->stream);
+  if (!rc) rc = copy_in(d, ld.wo, w->wo, H * q_dim, "wo");
   if (!rc) rc = copy_in(d, ld.so, w->wo_s, H * 4, "wo_s");
-  if (!rc) rc = copy_in(d, tmp, w->gate_up, 2 * I * H, "gate_up");
-  if (!rc) rc = mv2_tile_weights(ld.gate_up, tmp, (int)(2 * I), (int)H, 1, d->stream);
+  if (!rc) rc = copy_in(d, ld.gate_up, w->gate_up, 2 * I * H, "gate_up");
   if (!rc) rc = copy_in(d, ld.sgu, w->gate_up_s, 2 * I * 4, "gate_up_s");
-  if (!rc) rc = copy_in(d, tmp, w->down, H * I, "down");
-  if (!rc) rc = mv2_tile_weights(ld.down, tmp, (int)H, (int)I, d->s_down, d->stream);
+  if (!rc) rc = copy_in(d, ld.down, w->down, H * I, "down");
   if (!rc) rc = copy_in(d, ld.sdown, w->down_s, H * 4, "down_s");
   if (!rc) rc = copy_in(d, ld.q_norm, w->q_norm, c.head_dim * 4, "q_norm");
   if (!rc) rc = copy_in(d, ld.k_norm, w->k_norm, c.head_dim * 4, "k_norm");
@@ -285,23 +277,13 @@ extern "C" int qasr_decoder_set_globals(qasr_decoder *d, const void *embed, cons
   cudaSetDevice(d->device);
   const qasr_decoder_config &c = d->cfg;
   const size_t VH = (size_t)c.vocab * c.hidden;
-  // INT8 tables are used by the lm head, which reads them in the tiled layout
-  auto upload_tiled = [&](int8_t *dst, const void *src, const char *what) {
-    void *tmp = nullptr;
-    int r = cuda_status(cudaMalloc(&tmp, VH), "qasr_decoder_set_globals: staging");
-    if (!r) r = copy_in(d, tmp, src, VH, what);
-    if (!r) r = mv2_tile_weights(dst, static_cast<const int8_t *>(tmp), c.vocab, c.hidden, 1, d->stream);
-    if (!r) r = cuda_status(cudaStreamSynchronize(d->stream), what);
-    if (tmp) cudaFree(tmp);
-    return r;
-  };
   int rc = QASR_OK;
   if (!lm_head && !c.embed_is_int8) {
     set_error("qasr_decoder_set_globals: a tied lm head needs the INT8 embedding table");
     return QASR_ERR_INVALID;
   }
   if (c.embed_is_int8 && !lm_head) {
-    rc = upload_tiled(static_cast<int8_t *>(d->embed), embed, "embed");  // tied: one tiled copy serves both
+    rc = copy_in(d, d->embed, embed, VH, "embed");  // tied: one copy serves the gather and the lm head
     d->lm_tied = true;
   } else {
     rc = copy_in(d, d->embed, embed, VH * (c.embed_is_int8 ? 1 : 4), "embed");
@@ -316,10 +298,13 @@ extern "C" int qasr_decoder_set_globals(qasr_decoder *d, const void *embed, cons
       d->lm_s = (float *)dalloc(d, (size_t)c.vocab * 4, &arc);
       if (arc) return arc;
     }
-    rc = upload_tiled(d->lm, lm_head, "lm_head");
+    rc = copy_in(d, d->lm, lm_head, VH, "lm_head");
     if (!rc) rc = copy_in(d, d->lm_s, lm_head_s, (size_t)c.vocab * 4, "lm_head_s");
   }
+  if (!rc)
+    rc = umma_weight_map(&d->tm_lm, d->lm_tied ? static_cast<const int8_t *>(d->embed) : d->lm, c.vocab, c.hidden);
   if (!rc) rc = cuda_status(cudaStreamSynchronize(d->stream), "qasr_decoder_set_globals");
+  d->globals_ready = rc == QASR_OK;
   return rc;
 }
 
@@ -379,40 +364,42 @@ struct StepMarks {
 // Enqueue the kernels of one decode step for M sequences on d->stream.
 static int enqueue_step(qasr_decoder *d, int M, StepMarks *marks = nullptr) {
   const qasr_decoder_config &c = d->cfg;
+  if (!d->globals_ready) {
+    set_error("qasr_decoder: qasr_decoder_set_globals must succeed before a step");
+    return QASR_ERR_INVALID;
+  }
   cudaStream_t st = d->stream;
   MARK(-1);
   const int H = c.hidden, I = c.inter, hd = c.head_dim;
   const int q_dim = c.n_heads * hd, kv_dim = c.n_kv_heads * hd, qkv_rows = q_dim + 2 * kv_dim;
   const int G = c.n_heads / c.n_kv_heads;
   const void *emb_tab = d->embed;
-  step_embed_kernel<<<M, 256, 0, st>>>(d->x, emb_tab, d->embed_s, c.embed_is_int8, d->tok, H, c.vocab, d->err,
-                                       d->lm_tied ? 1 : 0);
+  step_embed_kernel<<<M, 256, 0, st>>>(d->x, emb_tab, d->embed_s, c.embed_is_int8, d->tok, H, c.vocab, d->err);
   MARK(QASR_K_EMBED);
   int rc = launch_status("decode step: embed");
-  auto mvp = [&](const float *x, long xs, const float *nw, const int8_t *w, const float *sc, float *y, long ys, int K,
-                 int N, int S) {
-    Mv2Params p{};
-    p.x = x; p.x_stride = xs; p.norm_w = nw; p.eps = c.eps; p.w = w; p.scales = sc; p.y = y; p.y_stride = ys;
-    p.M = M; p.K = K; p.N = N; p.S = S; p.KS = K / S; p.KC = mv2_chunk(K / S);
-    p.partial = d->mv_partial; p.rg_counter = d->mv_ctr;
+  auto mvp = [&](const CUtensorMap &tm, const float *x, long xs, const float *nw, const float *sc, float *y, long ys,
+                 int K, int N) {
+    UmmaParams p{};
+    p.tmap = tm;
+    p.x = x; p.x_stride = xs; p.norm_w = nw; p.eps = c.eps; p.scales = sc; p.y = y; p.y_stride = ys;
+    p.M = M; p.K = K; p.N = N;
+    p.acc = d->u_acc; p.tile_ctr = d->u_ctr;
     p.keys = d->am_keys; p.counter = d->am_ctr; p.ids = d->next; p.err = d->err;
-    p.tiled = true;
     return p;
   };
-  auto mv = [&](const float *x, long xs, const float *nw, const int8_t *w, const float *sc, float *y, long ys, int K,
-                int N, int S, MvEpi e) { return mv2_launch(mvp(x, xs, nw, w, sc, y, ys, K, N, S), e, st, true); };
+  auto mv = [&](const CUtensorMap &tm, const float *x, long xs, const float *nw, const float *sc, float *y, long ys,
+                int K, int N, MvEpi e) { return umma_launch(mvp(tm, x, xs, nw, sc, y, ys, K, N), e, st, true); };
   for (int l = 0; l < c.n_layers && !rc; ++l) {
     const LayerDev &L = d->layers[l];
     // input RMSNorm fused into the q|k|v matvec; its epilogue applies the q/k
     // per-head norm + RoPE and appends K/V (one launch)
     {
-      Mv2Params p = mvp(d->x, H, L.in_norm, L.wqkv, L.sqkv, d->qkv, qkv_rows, H, qkv_rows, 1);
+      UmmaParams p = mvp(L.tm_qkv, d->x, H, L.in_norm, L.sqkv, nullptr, 0, H, qkv_rows);
       p.post.q_out = d->q_out; p.post.k_cache = d->k_cache; p.post.v_cache = d->v_cache;
       p.post.seq_stride = d->seq_stride(); p.post.layer = l; p.post.max_seq = c.max_seq;
       p.post.n_heads = c.n_heads; p.post.n_kv = c.n_kv_heads; p.post.positions = d->pos;
       p.post.q_norm = L.q_norm; p.post.k_norm = L.k_norm; p.post.cos_tab = d->rope_cos; p.post.sin_tab = d->rope_sin;
-      p.post.head_ctr = d->head_ctr;
-      if ((rc = mv2_launch(p, MvEpi::QkvPost, st, true))) break;
+      if ((rc = umma_launch(p, MvEpi::QkvPost, st, true))) break;
     }
     MARK(QASR_K_QKV);
     AttnDecodeParams a{};
@@ -422,19 +409,18 @@ static int enqueue_step(qasr_decoder *d, int M, StepMarks *marks = nullptr) {
     a.partials = d->partials; a.counters = d->attn_ctr; a.out = d->attn; a.out_stride = q_dim; a.err = d->err;
     if ((rc = attn_decode_launch(a, G, st, true))) break;
     MARK(QASR_K_ATTN);
-    if ((rc = mv(d->attn, q_dim, nullptr, L.wo, L.so, d->x, H, q_dim, H, d->s_oproj, MvEpi::Residual))) break;
+    if ((rc = mv(L.tm_o, d->attn, q_dim, nullptr, L.so, d->x, H, q_dim, H, MvEpi::Residual))) break;
     MARK(QASR_K_OPROJ);
     // post-attention RMSNorm fused into the gate/up matvec, SwiGLU in its epilogue
-    if ((rc = mv(d->x, H, L.post_norm, L.gate_up, L.sgu, d->h, I, H, 2 * I, 1, MvEpi::SwiGLU))) break;
+    if ((rc = mv(L.tm_gu, d->x, H, L.post_norm, L.sgu, d->h, I, H, 2 * I, MvEpi::SwiGLU))) break;
     MARK(QASR_K_GATEUP);
-    if ((rc = mv(d->h, I, nullptr, L.down, L.sdown, d->x, H, I, H, d->s_down, MvEpi::Residual))) break;
+    if ((rc = mv(L.tm_down, d->h, I, nullptr, L.sdown, d->x, H, I, H, MvEpi::Residual))) break;
     MARK(QASR_K_DOWN);
   }
   if (rc) return rc;
   // final RMSNorm fused into the lm head, argmax in its epilogue
-  rc = mv(d->x, H, d->norm, d->lm_tied ? static_cast<const int8_t *>(d->embed) : d->lm,
-          d->lm_tied ? d->embed_s : d->lm_s, d->keep_logits ? d->logits : nullptr, c.vocab, H, c.vocab, 1,
-          MvEpi::Argmax);
+  rc = mv(d->tm_lm, d->x, H, d->norm, d->lm_tied ? d->embed_s : d->lm_s, d->keep_logits ? d->logits : nullptr, c.vocab,
+          H, c.vocab, MvEpi::Argmax);
   MARK(QASR_K_LMHEAD);
   return rc;
 }

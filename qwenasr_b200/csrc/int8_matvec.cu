@@ -17,6 +17,7 @@
 // (decoder.rs:936-947).
 #include "common.cuh"
 #include "matvec.cuh"
+#include "umma.cuh"
 
 namespace qasr {
 
@@ -244,6 +245,30 @@ static int check_mv(const char *fn, const float *y, const float *x, const int8_t
   return QASR_OK;
 }
 
+// Try the tensor-core kernel (umma_matvec.cu) for M <= 8 tokens; returns
+// QASR_ERR_UNSUPPORTED (nothing launched) for shapes it does not cover.
+static int try_umma(const float *x, long xs, const float *nw, float eps, const int8_t *w, const float *scales,
+                    const float *bias, float *y, long ys, int M, int K, int N, MvEpi e, int32_t *ids, cudaStream_t st) {
+  if (K % 128 || (reinterpret_cast<uintptr_t>(w) & 15) || (reinterpret_cast<uintptr_t>(x) & 15) || (xs & 3) ||
+      (reinterpret_cast<uintptr_t>(nw) & 15) || M < 1 || M > 8 || (e == MvEpi::SwiGLU && (N & 1)))
+    return QASR_ERR_UNSUPPORTED;
+  UmmaParams p{};
+  int rc = umma_weight_map(&p.tmap, w, N, K);
+  if (rc) return rc;
+  p.x = x; p.x_stride = xs; p.norm_w = nw; p.eps = eps; p.scales = scales; p.bias = bias;
+  p.y = y; p.y_stride = ys; p.M = M; p.K = K; p.N = N;
+  void *acc, *ctr;
+  if ((rc = dev_scratch(kScratchUmmaAcc, umma_acc_words(N) * 8, &acc))) return rc;
+  if ((rc = dev_scratch(kScratchUmmaCtr, umma_ctr_words(N) * 4, &ctr))) return rc;
+  p.acc = static_cast<unsigned long long *>(acc);
+  p.tile_ctr = static_cast<unsigned *>(ctr);
+  if (e == MvEpi::Argmax) {
+    if ((rc = argmax_scratch(&p.keys, &p.counter))) return rc;
+    p.ids = ids;
+  }
+  return umma_launch(p, e, st, false);
+}
+
 // Try the weight-streaming kernel (matvec2.cu) for M <= 8 tokens; returns
 // QASR_ERR_UNSUPPORTED (nothing launched) for shapes it does not cover.
 static int try_mv2(const float *x, long xs, const float *nw, float eps, const int8_t *w, const float *scales,
@@ -280,8 +305,11 @@ static int linear_int8_impl(const char *fn, float *y, const float *x, const int8
   if (rc) return rc;
   for (int s0 = 0; s0 < seq; s0 += 8) {
     const int m = std::min(8, seq - s0);
-    rc = try_mv2(x + (size_t)s0 * in_dim, in_dim, nullptr, 0.f, w, scales, bias, y + (size_t)s0 * out_dim, out_dim,
-                 m, in_dim, out_dim, bias ? MvEpi::StoreBias : MvEpi::Store, nullptr, S(stream));
+    rc = try_umma(x + (size_t)s0 * in_dim, in_dim, nullptr, 0.f, w, scales, bias, y + (size_t)s0 * out_dim, out_dim,
+                  m, in_dim, out_dim, bias ? MvEpi::StoreBias : MvEpi::Store, nullptr, S(stream));
+    if (rc == QASR_ERR_UNSUPPORTED)
+      rc = try_mv2(x + (size_t)s0 * in_dim, in_dim, nullptr, 0.f, w, scales, bias, y + (size_t)s0 * out_dim, out_dim,
+                   m, in_dim, out_dim, bias ? MvEpi::StoreBias : MvEpi::Store, nullptr, S(stream));
     if (rc == QASR_ERR_UNSUPPORTED) {
       MvParams p{};
       p.x = x + (size_t)s0 * in_dim;
@@ -321,8 +349,11 @@ extern "C" int qasr_int8_matvec_residual(float *x, const float *a, const int8_t 
     return QASR_ERR_UNSUPPORTED;
   }
   if (M == 0) return QASR_OK;
-  rc = try_mv2(a, in_dim, nullptr, 0.f, w, scales, nullptr, x, out_dim, M, in_dim, out_dim, MvEpi::Residual, nullptr,
-               S(stream));
+  rc = try_umma(a, in_dim, nullptr, 0.f, w, scales, nullptr, x, out_dim, M, in_dim, out_dim, MvEpi::Residual, nullptr,
+                S(stream));
+  if (rc == QASR_ERR_UNSUPPORTED)
+    rc = try_mv2(a, in_dim, nullptr, 0.f, w, scales, nullptr, x, out_dim, M, in_dim, out_dim, MvEpi::Residual, nullptr,
+                 S(stream));
   if (rc != QASR_ERR_UNSUPPORTED) return rc ? rc : launch_status("qasr_int8_matvec_residual");
   MvParams p{};
   p.x = a;
@@ -348,8 +379,11 @@ extern "C" int qasr_int8_norm_gateup_swiglu(float *h, const float *x, const floa
     return QASR_ERR_INVALID;
   }
   if (M == 0) return QASR_OK;
-  rc = try_mv2(x, hidden, norm_w, eps, w_gate_up, scales, nullptr, h, inter, M, hidden, 2 * inter, MvEpi::SwiGLU,
-               nullptr, S(stream));
+  rc = try_umma(x, hidden, norm_w, eps, w_gate_up, scales, nullptr, h, inter, M, hidden, 2 * inter, MvEpi::SwiGLU,
+                nullptr, S(stream));
+  if (rc == QASR_ERR_UNSUPPORTED)
+    rc = try_mv2(x, hidden, norm_w, eps, w_gate_up, scales, nullptr, h, inter, M, hidden, 2 * inter, MvEpi::SwiGLU,
+                 nullptr, S(stream));
   if (rc != QASR_ERR_UNSUPPORTED) return rc ? rc : launch_status("qasr_int8_norm_gateup_swiglu");
   float *xn = nullptr;
   if ((rc = mv_norm_scratch(&xn, (size_t)M * hidden))) return rc;
@@ -379,8 +413,11 @@ extern "C" int qasr_final_norm_lmhead_argmax(int32_t *ids_out, float *logits_out
     return QASR_ERR_INVALID;
   }
   if (M == 0) return QASR_OK;
-  rc = try_mv2(x, hidden, norm_w, eps, w, scales, nullptr, logits_out, vocab, M, hidden, vocab, MvEpi::Argmax,
-               ids_out, S(stream));
+  rc = try_umma(x, hidden, norm_w, eps, w, scales, nullptr, logits_out, vocab, M, hidden, vocab, MvEpi::Argmax,
+                ids_out, S(stream));
+  if (rc == QASR_ERR_UNSUPPORTED)
+    rc = try_mv2(x, hidden, norm_w, eps, w, scales, nullptr, logits_out, vocab, M, hidden, vocab, MvEpi::Argmax,
+                 ids_out, S(stream));
   if (rc != QASR_ERR_UNSUPPORTED) return rc ? rc : launch_status("qasr_final_norm_lmhead_argmax");
   float *xn = nullptr;
   if ((rc = mv_norm_scratch(&xn, (size_t)M * hidden))) return rc;
