@@ -14,8 +14,7 @@
 //              the reference's per-sequence KvCache layout, sequences stacked.
 //   RoPE       cos/sin [max_seq, head_dim], the RopeCache::ensure table.
 //   work       x [B, hidden]; q_out, attn [B, q_dim]; h [B, inter];
-//              attention partials/counters; split accumulators of the INT8
-//              contractions; argmax keys.
+//              attention partials/counters; argmax keys.
 // Every INT8 matrix keeps the reference's row-major [out, in] layout and is
 // read by TMA through one tensor map (umma_weight_map) built at creation.
 //
@@ -60,8 +59,7 @@ struct qasr_decoder {
   float *rope_cos = nullptr, *rope_sin = nullptr;
   float *x = nullptr, *q_out = nullptr, *attn = nullptr, *h = nullptr;
   float *partials = nullptr, *logits = nullptr;
-  unsigned *attn_ctr = nullptr, *am_ctr = nullptr, *u_ctr = nullptr;
-  unsigned long long *u_acc = nullptr;
+  unsigned *attn_ctr = nullptr, *am_ctr = nullptr;
   CUtensorMap tm_k, tm_v, tm_lm;
   unsigned long long *am_keys = nullptr;
   int32_t *tok = nullptr, *pos = nullptr, *next = nullptr;
@@ -191,10 +189,6 @@ extern "C" qasr_decoder *qasr_decoder_create(const qasr_decoder_config *cfg, int
   const int G = cfg->n_heads / cfg->n_kv_heads;
   d->partials = (float *)dalloc(d, (size_t)(attn_grid() + B * cfg->n_kv_heads) * G * kAttnPartStride * 4, &rc);
   d->attn_ctr = (unsigned *)dalloc(d, (size_t)B * cfg->n_kv_heads * 4, &rc);
-  // split accumulators of the INT8 contractions, sized for the widest one
-  const int n_max = std::max(std::max(qkv_rows, 2 * I), std::max(H, cfg->vocab));
-  d->u_acc = (unsigned long long *)dalloc(d, umma_acc_words(n_max) * 8, &rc);
-  d->u_ctr = (unsigned *)dalloc(d, umma_ctr_words(n_max) * 4, &rc);
   d->am_keys = (unsigned long long *)dalloc(d, 8 * 8, &rc);
   d->am_ctr = (unsigned *)dalloc(d, 16, &rc);
   d->tok = (int32_t *)dalloc(d, 8 * 4, &rc);
@@ -213,8 +207,6 @@ extern "C" qasr_decoder *qasr_decoder_create(const qasr_decoder_config *cfg, int
   rc = cuda_status(cudaMemsetAsync(d->k_cache, 0, kv_elems * 4, st), "memset");
   if (!rc) rc = cuda_status(cudaMemsetAsync(d->v_cache, 0, kv_elems * 4, st), "memset");
   if (!rc) rc = cuda_status(cudaMemsetAsync(d->attn_ctr, 0, (size_t)B * cfg->n_kv_heads * 4, st), "memset");
-  if (!rc) rc = cuda_status(cudaMemsetAsync(d->u_acc, 0, umma_acc_words(n_max) * 8, st), "memset");
-  if (!rc) rc = cuda_status(cudaMemsetAsync(d->u_ctr, 0, umma_ctr_words(n_max) * 4, st), "memset");
   if (!rc) rc = attn_make_tensor_map(&d->tm_k, d->k_cache, (long)B * L * cfg->max_seq, kv_dim);
   if (!rc) rc = attn_make_tensor_map(&d->tm_v, d->v_cache, (long)B * L * cfg->max_seq, kv_dim);
   if (!rc) rc = cuda_status(cudaMemsetAsync(d->am_keys, 0, 64, st), "memset");
@@ -383,7 +375,6 @@ static int enqueue_step(qasr_decoder *d, int M, StepMarks *marks = nullptr) {
     p.tmap = tm;
     p.x = x; p.x_stride = xs; p.norm_w = nw; p.eps = c.eps; p.scales = sc; p.y = y; p.y_stride = ys;
     p.M = M; p.K = K; p.N = N;
-    p.acc = d->u_acc; p.tile_ctr = d->u_ctr;
     p.keys = d->am_keys; p.counter = d->am_ctr; p.ids = d->next; p.err = d->err;
     return p;
   };

@@ -257,11 +257,6 @@ static int try_umma(const float *x, long xs, const float *nw, float eps, const i
   if (rc) return rc;
   p.x = x; p.x_stride = xs; p.norm_w = nw; p.eps = eps; p.scales = scales; p.bias = bias;
   p.y = y; p.y_stride = ys; p.M = M; p.K = K; p.N = N;
-  void *acc, *ctr;
-  if ((rc = dev_scratch(kScratchUmmaAcc, umma_acc_words(N) * 8, &acc))) return rc;
-  if ((rc = dev_scratch(kScratchUmmaCtr, umma_ctr_words(N) * 4, &ctr))) return rc;
-  p.acc = static_cast<unsigned long long *>(acc);
-  p.tile_ctr = static_cast<unsigned *>(ctr);
   if (e == MvEpi::Argmax) {
     if ((rc = argmax_scratch(&p.keys, &p.counter))) return rc;
     p.ids = ids;

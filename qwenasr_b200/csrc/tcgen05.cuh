@@ -93,3 +93,69 @@ QASR_DEV void tma_load_2d_u8(void *dst, const CUtensorMap *tm, int x, int y, uin
 QASR_DEV void named_bar(int id, int count) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory"); }
 
 }  // namespace qasr
+
+// ------------------------------------------------------------ clusters --
+namespace qasr {
+
+QASR_DEV uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+QASR_DEV uint32_t cluster_id_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+QASR_DEV uint32_t cluster_count_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+// All threads of every CTA of the cluster (also a CTA-wide barrier).
+QASR_DEV void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Shared::cluster address of `local` (a shared::cta address) in CTA `rank`.
+QASR_DEV uint32_t cluster_map(uint32_t local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+  return r;
+}
+// Arrive (release at cluster scope) on an mbarrier of another CTA of the cluster.
+QASR_DEV void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+QASR_DEV unsigned long long ld_cluster_u64(uint32_t cluster_addr) {
+  unsigned long long v;
+  asm volatile("ld.shared::cluster.u64 %0, [%1];" : "=l"(v) : "r"(cluster_addr) : "memory");
+  return v;
+}
+QASR_DEV void ld_cluster_u64x2(uint32_t cluster_addr, unsigned long long &a, unsigned long long &b) {
+  asm volatile("ld.shared::cluster.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "r"(cluster_addr) : "memory");
+}
+// Split cluster barrier, per thread (no warp convergence needed): every
+// thread of the cluster arrives once, then waits before leaving.
+QASR_DEV void cluster_arrive_all() { asm volatile("barrier.cluster.arrive.release;" ::: "memory"); }
+QASR_DEV void cluster_wait_all() { asm volatile("barrier.cluster.wait.acquire;" ::: "memory"); }
+QASR_DEV bool mbar_try_wait_cluster(uint64_t *bar, unsigned parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait with cluster-scope acquire (remote arrivals); false on timeout.
+QASR_DEV bool mbar_wait_cluster(uint64_t *bar, unsigned parity) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  while (!mbar_try_wait_cluster(bar, parity))
+    if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+  return true;
+}
+
+}  // namespace qasr

@@ -10,9 +10,8 @@ namespace qasr {
 // y[m, o] = scales[o] * sum_k w[o, k] * x[m, k] for M <= 8 token rows, with
 // the epilogues of the matvec family (MvEpi).  The weights are the
 // reference's row-major [N, K] int8 matrix, read by TMA through `tmap`
-// (umma_weight_map).  Split accumulators `acc` ([ceil(N/128)*128, 8] 64-bit)
-// and `tile_ctr` ([ceil(N/128)]) must be zero on entry; the kernel leaves them
-// at zero.
+// (umma_weight_map).  No scratch: split-K partials are reduced inside a
+// thread-block cluster.
 struct UmmaParams {
   CUtensorMap tmap;
   const float *x;       // [M, K], rows 16-byte aligned (x_stride % 4 == 0)
@@ -24,24 +23,19 @@ struct UmmaParams {
   float *y;             // as MvParams::y
   long y_stride;
   int M, K, N;
-  unsigned long long *acc;
-  unsigned *tile_ctr;
   unsigned long long *keys;  // Argmax: [M], zero on entry, re-armed
   unsigned *counter;         // Argmax: CTA counter, zero on entry, re-armed
   int32_t *ids;              // Argmax: [M]
   int *err;                  // -QASR_ERR_TIMEOUT if a bounded wait gives up (may be null)
   QkvPostParams post;        // MvEpi::QkvPost (head_ctr unused)
   // filled in by umma_launch
-  int stages, nb;
+  int stages, csize;
 };
 
 // Tensor map of an [N, K] int8 matrix: box 128 rows x 128 bytes, 128-byte swizzle.
 int umma_weight_map(CUtensorMap *tm, const int8_t *w, int N, int K);
 // QASR_ERR_UNSUPPORTED (nothing launched) for shapes it does not cover.
 int umma_launch(UmmaParams p, MvEpi e, cudaStream_t st, bool pdl);
-// 64-bit words of split accumulators / counters needed for N output rows.
-inline size_t umma_acc_words(int N) { return (size_t)((N + 127) / 128) * 128 * 8; }
-inline size_t umma_ctr_words(int N) { return (size_t)((N + 127) / 128); }
 
 // Driver entry point cuTensorMapEncodeTiled (resolved once).
 void *tensor_map_encoder();

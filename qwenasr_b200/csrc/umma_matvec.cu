@@ -36,6 +36,9 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <map>
+#include <mutex>
+#include <tuple>
 
 #include "common.cuh"
 #include "matvec.cuh"
@@ -48,9 +51,11 @@
 namespace qasr {
 
 constexpr int kUWarps = 8;
-constexpr int kUMaxStages = 6;
+constexpr int kUMaxStages = 8;
+constexpr int kUMaxCluster = 16;
 constexpr int kUTile = 128 * 128;        // bytes of one weight tile
 constexpr int kUBSlot = 32 * 128;        // bytes of the digit rows of one K tile
+constexpr int kURed = 128 * 8 * 8;       // one tile's 64-bit partials [row][token]
 constexpr int kUTmemCols = 64;           // two 32-column accumulators
 constexpr int kUEpiThreads = 128;        // warps 0..3
 constexpr int kUProducerWarp = 4, kUMmaWarp = 5;
@@ -59,12 +64,12 @@ constexpr uint32_t kUIdesc = umma_idesc_s8(128, 32);
 struct alignas(16) USmem {
   uint64_t full[kUMaxStages], empty[kUMaxStages];
   uint64_t accfull[2], accempty[2];
+  uint64_t redfull[2], redempty[2];  // cluster reduction of a tile's partials
   uint64_t xbar, nbar, done;
   uint32_t tmem;
   int abort;
-  int fin;
   int last;
-  float inv[8], qmul[8], dq[8];
+  float dq[8];
   unsigned long long best[4][8];
   alignas(16) float hs[8][128];  // QkvPost: one head of every token (read as float4)
 };
@@ -80,26 +85,34 @@ QASR_DEV float pow2f(int e) {  // 2^e for -126 <= e <= 127
   return __int_as_float((127 + e) << 23);
 }
 
+// Grid: clusters of C CTAs (C divides K/128).  Cluster c owns row tiles
+// c, c + n_clusters, ...; CTA rank r of the cluster contracts K tiles
+// [r*KC, (r+1)*KC) (KC = K/128/C) of each of them.  With C > 1 each rank
+// parks its 64-bit partials in shared memory and finishes a share of the
+// tile's rows by summing the partials of all ranks over distributed shared
+// memory, in rank order.
 template <MvEpi E, bool NORM>
 __global__ void __launch_bounds__(kUWarps * 32, 1) int8_umma_kernel(const __grid_constant__ UmmaParams p) {
   extern __shared__ unsigned char smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   unsigned char *base = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
-  const int STAGES = p.stages, NB = p.nb;
+  const int STAGES = p.stages, C = p.csize;
+  const int M = p.M, K = p.K, N = p.N;
+  const int KT = K / 128, NT = (N + 127) / 128, KC = KT / C;
   unsigned char *a_ring = base;
   unsigned char *b_tiles = a_ring + (size_t)STAGES * kUTile;
-  float *xs = reinterpret_cast<float *>(b_tiles + (size_t)NB * kUBSlot);  // NORM: [M, K]
-  float *nws = xs + (NORM ? (size_t)p.M * p.K : 0);                         // NORM: [K]
-  USmem &sm = *reinterpret_cast<USmem *>(nws + (NORM ? p.K : 0));
+  unsigned long long *red = reinterpret_cast<unsigned long long *>(b_tiles + (size_t)KC * kUBSlot);  // [2][128][8]
+  float *xs = reinterpret_cast<float *>(reinterpret_cast<unsigned char *>(red) + (C > 1 ? 2 * kURed : 0));
+  float *nws = xs + (NORM ? (size_t)M * K : 0);  // NORM: x rows [M, K], norm weights [K]
+  USmem &sm = *reinterpret_cast<USmem *>(nws + (NORM ? K : 0));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int M = p.M, K = p.K, N = p.N;
-  const int KT = K / 128, NT = (N + 127) / 128;
-  const long long U = (long long)NT * KT;
-  const int u0 = (int)(U * blockIdx.x / gridDim.x), u1 = (int)(U * (blockIdx.x + 1) / gridDim.x);
-  const int nu = u1 - u0;
-  const int kt_base = u0 % KT;
-  auto slot_of = [&](int kt) { return nu >= KT ? kt : (kt - kt_base + KT) % KT; };
+  const int rank = C > 1 ? (int)cluster_ctarank() : 0;
+  const int cid = C > 1 ? (int)cluster_id_x() : blockIdx.x;
+  const int ncl = C > 1 ? (int)cluster_count_x() : gridDim.x;
+  const int kt0 = rank * KC;
+  const int ntiles = cid < NT ? (NT - 1 - cid) / ncl + 1 : 0;
+  const int nu = ntiles * KC;  // pipeline items: (tile j, K tile kt0 + i % KC)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kUMaxStages; ++s) {
@@ -109,6 +122,8 @@ __global__ void __launch_bounds__(kUWarps * 32, 1) int8_umma_kernel(const __grid
     for (int b = 0; b < 2; ++b) {
       mbar_init(&sm.accfull[b], 1);
       mbar_init(&sm.accempty[b], 4);
+      mbar_init(&sm.redfull[b], C);
+      mbar_init(&sm.redempty[b], C);
     }
     mbar_init(&sm.xbar, 1);
     mbar_init(&sm.nbar, 1);
@@ -118,16 +133,20 @@ __global__ void __launch_bounds__(kUWarps * 32, 1) int8_umma_kernel(const __grid
   }
   if (warp == kUMmaWarp) tmem_alloc(&sm.tmem, kUTmemCols);
   tc_fence_before();
-  __syncthreads();
+  __syncwarp();
+  if (C > 1)
+    cluster_sync_all();  // every rank's barriers exist before any remote arrival
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem;
 
   // ---- weight prefetch: constant operand, issued before waiting on the previous kernel
   int produced = 0;  // producer thread only
   auto produce = [&](int i) {
-    const int u = u0 + i, st = i % STAGES;
+    const int st = i % STAGES, t = cid + (i / KC) * ncl, kt = kt0 + i % KC;
     mbar_arrive_expect_tx(&sm.full[st], kUTile);
-    tma_load_2d_u8(a_ring + (size_t)st * kUTile, &p.tmap, (u % KT) * 128, (u / KT) * 128, &sm.full[st]);
+    tma_load_2d_u8(a_ring + (size_t)st * kUTile, &p.tmap, kt * 128, t * 128, &sm.full[st]);
   };
   const bool producer = warp == kUProducerWarp && lane == 0;
   if (producer) {
@@ -143,124 +162,123 @@ __global__ void __launch_bounds__(kUWarps * 32, 1) int8_umma_kernel(const __grid
   pdl_wait();
   pdl_launch_dependents();
 
-  // ---- stage x: per-row exponent (and RMSNorm), then the digit rows
+  // ---- stage x.  Warp m owns token row m: its exponent (after the RMSNorm
+  // when NORM), then its three digit rows for every K tile this CTA uses.
+  // Lane l covers floats 4l..4l+3 of a 128-float K tile, so every shared
+  // access of the pass is a conflict-free 16-byte (or 4-byte) vector.
   if constexpr (NORM) {
     if (threadIdx.x == 0) {
       mbar_arrive_expect_tx(&sm.xbar, (unsigned)(M * K * 4));
       for (int m = 0; m < M; ++m) bulk_g2s(xs + (size_t)m * K, p.x + (size_t)m * p.x_stride, (unsigned)K * 4, &sm.xbar);
     }
   }
-  if (warp < M) {
-    const int m = warp;
-    float bound;
-    if constexpr (NORM) {
-      bool ok = mbar_wait(&sm.xbar, 0);
-      ok = mbar_wait(&sm.nbar, 0) && ok;
-      if (!ok && lane == 0) u_fail(sm, p.err);
-      const float *xr = xs + (size_t)m * K;
-      // sum of squares in the reference's order (rowops.cuh): lanes 0..15 run
-      // the sequential chains, operands fetched 16 at a time ahead of them
-      const int n16 = K / 16;
-      float acc = 0.0f;
-      if (lane < 16) {
-        int j = 0;
-        for (; j + 16 <= n16; j += 16) {
-          float v[16];
-#pragma unroll
-          for (int t = 0; t < 16; ++t) v[t] = xr[16 * (j + t) + lane];
-#pragma unroll
-          for (int t = 0; t < 16; ++t) acc = fmaf(v[t], v[t], acc);
-        }
-        for (; j < n16; ++j) {
-          const float v = xr[16 * j + lane];
-          acc = fmaf(v, v, acc);
-        }
-      }
-      const float sum = hsum16_avx_order(acc);  // K % 128 == 0: no 8-block, no scalar tail
-      const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)K), p.eps)));
-      float mx = 0.0f, mw = 0.0f;
-      for (int k = lane; k < K; k += 32) {
-        mx = fmaxf(mx, fabsf(xr[k]));
-        mw = fmaxf(mw, fabsf(nws[k]));
-      }
-      mx = warp_max(mx);
-      mw = warp_max(mw);
-      // rounding is monotonic, so this bounds every |rn(rn(x*inv)*w)|
-      bound = __fmul_rn(__fmul_rn(mx, inv), mw);
-      if (lane == 0) sm.inv[m] = inv;
-    } else {
-      const float4 *xr = reinterpret_cast<const float4 *>(p.x + (size_t)m * p.x_stride);
-      float mx = 0.0f;
-      for (int k4 = lane; k4 < K / 4; k4 += 32) {
-        const float4 v = xr[k4];
-        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-      }
-      bound = warp_max(mx);
-    }
-    if (lane == 0) {
-      int e = 0;
-      if (bound > 0.0f && bound <= 3.0e38f) frexpf(bound, &e);  // bound < 2^e
-      e = max(-100, min(e, 127));
-      sm.qmul[m] = pow2f(22 - e);
-      sm.dq[m] = pow2f(e - 22);
-    }
-  }
-  __syncthreads();
   {
-    const int nbu = min(KT, nu);
-    // items: (slot, token row m in 0..7, 16-byte chunk c) -> digit rows m, 8+m, 16+m;
-    // then the zero rows 24..31
-    const int n_tok = nbu * 8 * 8;
-    for (int it = threadIdx.x; it < 2 * n_tok; it += blockDim.x) {
-      const int item = it < n_tok ? it : it - n_tok;
-      const int slot = item >> 6, m = (item >> 3) & 7, c = item & 7;
+    const int m = warp;  // 8 warps: one per token row (rows m >= M are zero)
+    const int nbu = KC;
+    auto kt_of = [&](int slot) { return kt0 + slot; };
+    auto row_off = [&](int n) {  // byte offset of this lane's 4 bytes of digit row n in a slot
+      return (n >> 3) * 1024 + (n & 7) * 128 + (((lane >> 2) ^ (n & 7)) << 4) + (lane & 3) * 4;
+    };
+    auto put_digits = [&](int slot, float4 v, float qm) {
+      // X = rint(v * qm), |X| <= 2^22: v*qm is exact (power of two), and adding
+      // 1.5*2^23 leaves X in the low mantissa bits, rounded to nearest even.
+      // Balanced base-256 digits: d2 = low byte of X (as signed), X1 = (X+128)>>8,
+      // d1 = low byte of X1, d0 = (X1+128)>>8 (|d0| <= 64).
+      int X[4] = {__float_as_int(fmaf(v.x, qm, 12582912.0f)) - 0x4B400000,
+                  __float_as_int(fmaf(v.y, qm, 12582912.0f)) - 0x4B400000,
+                  __float_as_int(fmaf(v.z, qm, 12582912.0f)) - 0x4B400000,
+                  __float_as_int(fmaf(v.w, qm, 12582912.0f)) - 0x4B400000};
+      const uint32_t w2 = __byte_perm(__byte_perm(X[0], X[1], 0x0040), __byte_perm(X[2], X[3], 0x0040), 0x5410);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) X[q] = (X[q] + 128) >> 8;
+      const uint32_t w1 = __byte_perm(__byte_perm(X[0], X[1], 0x0040), __byte_perm(X[2], X[3], 0x0040), 0x5410);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) X[q] = (X[q] + 128) >> 8;
+      const uint32_t w0 = __byte_perm(__byte_perm(X[0], X[1], 0x0040), __byte_perm(X[2], X[3], 0x0040), 0x5410);
       unsigned char *tile = b_tiles + (size_t)slot * kUBSlot;
-      if (it >= n_tok) {  // padding row 24 + m
-        const int n = 24 + m;
-        *reinterpret_cast<uint4 *>(tile + (n >> 3) * 1024 + (n & 7) * 128 + ((c ^ (n & 7)) << 4)) =
-            make_uint4(0u, 0u, 0u, 0u);
-        continue;
-      }
-      uint32_t dg[3][4] = {{0u, 0u, 0u, 0u}, {0u, 0u, 0u, 0u}, {0u, 0u, 0u, 0u}};
-      if (m < M) {
-        const int kt = nu >= KT ? slot : (kt_base + slot) % KT;
-        const int k0 = kt * 128 + c * 16;
-        const float qm = sm.qmul[m];
-        float v[16];
-        if constexpr (NORM) {
-          const float inv = sm.inv[m];
+      *reinterpret_cast<uint32_t *>(tile + row_off(m)) = w0;
+      *reinterpret_cast<uint32_t *>(tile + row_off(8 + m)) = w1;
+      *reinterpret_cast<uint32_t *>(tile + row_off(16 + m)) = w2;
+    };
+    auto exponent = [&](float bound) {  // 2^e > bound (bound >= every |x| of the row)
+      int e = 0;
+      if (bound > 0.0f && bound <= 3.0e38f) frexpf(bound, &e);
+      e = max(-100, min(e, 127));
+      if (lane == 0) sm.dq[m] = pow2f(e - 22);
+      return pow2f(22 - e);
+    };
+    if (m < M) {
+      if constexpr (NORM) {
+        bool ok = mbar_wait(&sm.xbar, 0);
+        ok = mbar_wait(&sm.nbar, 0) && ok;
+        if (!ok && lane == 0) u_fail(sm, p.err);
+        const float *xr = xs + (size_t)m * K;
+        // sum of squares in the reference's order (rowops.cuh): lanes 0..15 run
+        // the sequential chains, operands fetched 16 at a time ahead of them
+        const int n16 = K / 16;
+        float acc = 0.0f, mx = 0.0f, mw = 0.0f;
+        if (lane < 16) {
+          for (int j = 0; j < n16; j += 16) {
+            float v[16];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) v[j] = __fmul_rn(__fmul_rn(xs[(size_t)m * K + k0 + j], inv), nws[k0 + j]);
+            for (int t = 0; t < 16; ++t) v[t] = j + t < n16 ? xr[16 * (j + t) + lane] : 0.0f;
+#pragma unroll
+            for (int t = 0; t < 16; ++t) {
+              acc = j + t < n16 ? fmaf(v[t], v[t], acc) : acc;
+              mx = fmaxf(mx, fabsf(v[t]));
+            }
+          }
         } else {
-          const float4 *src = reinterpret_cast<const float4 *>(p.x + (size_t)m * p.x_stride + k0);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float4 t = src[j];
-            v[4 * j] = t.x;
-            v[4 * j + 1] = t.y;
-            v[4 * j + 2] = t.z;
-            v[4 * j + 3] = t.w;
+          for (int k4 = lane - 16; k4 < K / 4; k4 += 16) {
+            const float4 b = reinterpret_cast<const float4 *>(nws)[k4];
+            mw = fmaxf(mw, fmaxf(fmaxf(fabsf(b.x), fabsf(b.y)), fmaxf(fabsf(b.z), fabsf(b.w))));
           }
         }
+        const float sum = hsum16_avx_order(acc);  // K % 128 == 0: no 8-block, no scalar tail
+        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)K), p.eps)));
+        mx = warp_max(mx);
+        mw = warp_max(mw);
+        // rounding is monotonic, so this bounds every |rn(rn(x*inv)*w)|
+        const float qm = exponent(__fmul_rn(__fmul_rn(mx, inv), mw));
+        for (int slot = 0; slot < nbu; ++slot) {
+          const int k = kt_of(slot) * 128 + 4 * lane;
+          const float4 a = *reinterpret_cast<const float4 *>(xr + k);
+          const float4 b = *reinterpret_cast<const float4 *>(nws + k);
+          const float4 v = make_float4(__fmul_rn(__fmul_rn(a.x, inv), b.x), __fmul_rn(__fmul_rn(a.y, inv), b.y),
+                                       __fmul_rn(__fmul_rn(a.z, inv), b.z), __fmul_rn(__fmul_rn(a.w, inv), b.w));
+          put_digits(slot, v, qm);
+        }
+      } else {
+        const float4 *xr = reinterpret_cast<const float4 *>(p.x + (size_t)m * p.x_stride);
+        constexpr int kRegTiles = 24;
+        if (KT <= kRegTiles) {  // the whole row in flight at once: one L2 round trip
+          float4 v[kRegTiles];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int X = __float2int_rn(__fmul_rn(v[j], qm));
-          const int d2 = ((X + 128) & 255) - 128;
-          const int t1 = (X - d2) >> 8;
-          const int d1 = ((t1 + 128) & 255) - 128;
-          const int d0 = (t1 - d1) >> 8;
-          dg[0][j >> 2] |= (uint32_t)(d0 & 255) << (8 * (j & 3));
-          dg[1][j >> 2] |= (uint32_t)(d1 & 255) << (8 * (j & 3));
-          dg[2][j >> 2] |= (uint32_t)(d2 & 255) << (8 * (j & 3));
+          for (int i = 0; i < kRegTiles; ++i)
+            if (i < KT) v[i] = xr[i * 32 + lane];
+          float mx = 0.0f;
+#pragma unroll
+          for (int i = 0; i < kRegTiles; ++i)
+            if (i < KT) mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
+          const float qm = exponent(warp_max(mx));
+          for (int slot = 0; slot < nbu; ++slot) put_digits(slot, xr[kt_of(slot) * 32 + lane], qm);
+        } else {
+          float mx = 0.0f;
+          for (int k4 = lane; k4 < K / 4; k4 += 32) {
+            const float4 a = xr[k4];
+            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))));
+          }
+          const float qm = exponent(warp_max(mx));
+          for (int slot = 0; slot < nbu; ++slot) put_digits(slot, xr[kt_of(slot) * 32 + lane], qm);
         }
       }
-#pragma unroll
-      for (int d = 0; d < 3; ++d) {
-        const int n = 8 * d + m;
-        *reinterpret_cast<uint4 *>(tile + (n >> 3) * 1024 + (n & 7) * 128 + ((c ^ (n & 7)) << 4)) =
-            make_uint4(dg[d][0], dg[d][1], dg[d][2], dg[d][3]);
-      }
+    } else {
+      for (int slot = 0; slot < nbu; ++slot)
+        for (int d = 0; d < 3; ++d)
+          *reinterpret_cast<uint32_t *>(b_tiles + (size_t)slot * kUBSlot + row_off(8 * d + m)) = 0u;
     }
+    for (int slot = 0; slot < nbu; ++slot)  // padding row 24 + warp
+      *reinterpret_cast<uint32_t *>(b_tiles + (size_t)slot * kUBSlot + row_off(24 + warp)) = 0u;
   }
   fence_proxy_async();  // digit rows written by threads -> visible to the tensor cores
   __syncthreads();
@@ -281,13 +299,11 @@ __global__ void __launch_bounds__(kUWarps * 32, 1) int8_umma_kernel(const __grid
       produce(produced);
     }
   } else if (warp == kUMmaWarp) {
-    // ---- MMA issuer (one thread)
+    // ---- MMA issuer (one thread): one accumulator per tile, double-buffered
     if (lane == 0) {
-      int pc = 0;
-      bool first = true;
       for (int i = 0; i < nu; ++i) {
-        const int u = u0 + i, kt = u % KT, st = i % STAGES, buf = pc & 1;
-        if (first && pc >= 2 && !mbar_wait(&sm.accempty[buf], (unsigned)(((pc >> 1) - 1) & 1))) {
+        const int j = i / KC, kk = i % KC, st = i % STAGES, buf = j & 1;
+        if (kk == 0 && j >= 2 && !mbar_wait(&sm.accempty[buf], (unsigned)(((j >> 1) - 1) & 1))) {
           u_fail(sm, p.err);
           break;
         }
@@ -298,35 +314,28 @@ __global__ void __launch_bounds__(kUWarps * 32, 1) int8_umma_kernel(const __grid
         if (u_aborted(sm)) break;
         tc_fence_after();
         const uint32_t a_addr = smem_u32(a_ring + (size_t)st * kUTile);
-        const uint32_t b_addr = smem_u32(b_tiles + (size_t)slot_of(kt) * kUBSlot);
+        const uint32_t b_addr = smem_u32(b_tiles + (size_t)kk * kUBSlot);
         const uint32_t d_addr = tmem + (uint32_t)(buf * 32);
 #pragma unroll
         for (int s = 0; s < 4; ++s)
           umma_s8(d_addr, umma_desc_sw128(a_addr + 32 * s), umma_desc_sw128(b_addr + 32 * s), kUIdesc,
-                  (first && s == 0) ? 0u : 1u);
+                  (kk == 0 && s == 0) ? 0u : 1u);
         umma_commit(&sm.empty[st]);
-        first = false;
-        if (i == nu - 1 || kt == KT - 1) {  // piece (row tile within this CTA) complete
-          umma_commit(&sm.accfull[buf]);
-          ++pc;
-          first = true;
-        }
+        if (kk == KC - 1) umma_commit(&sm.accfull[buf]);
       }
       // every MMA issued so far has completed once `done` flips
       umma_commit(&sm.done);
       if (!mbar_wait(&sm.done, 0)) u_fail(sm, p.err);
     }
   } else if (warp < 4) {
-    // ---- epilogue: thread = output row of the tile
-    const int r_in_tile = warp * 32 + lane;
-    int pc = 0;
-    for (int i = 0; i < nu;) {
-      const int u = u0 + i, t = u / KT, ka = u % KT;
-      const int kb = min(KT, ka + (nu - i));  // this piece covers K tiles ka .. kb-1
-      i += kb - ka;
-      const int buf = pc & 1;
-      if (!u_aborted(sm) && !mbar_wait(&sm.accfull[buf], (unsigned)((pc >> 1) & 1))) u_fail(sm, p.err);
-      ++pc;
+    // ---- epilogue: thread = row of the tile
+    const int ri = warp * 32 + lane;
+    // rows this rank finishes: a contiguous share (even-sized, so SwiGLU
+    // pairs stay together), or the whole tile for the per-head QkvPost
+    const int share = 128 / C;
+    for (int j = 0; j < ntiles; ++j) {
+      const int t = cid + j * ncl, buf = j & 1;
+      if (!u_aborted(sm) && !mbar_wait(&sm.accfull[buf], (unsigned)((j >> 1) & 1))) u_fail(sm, p.err);
       named_bar(1, kUEpiThreads);  // the four epilogue warps decide together
       if (u_aborted(sm)) break;
       tc_fence_after();
@@ -336,31 +345,45 @@ __global__ void __launch_bounds__(kUWarps * 32, 1) int8_umma_kernel(const __grid
       __syncwarp();
       if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&sm.accempty[buf])) : "memory");
 
-      const int row = t * 128 + r_in_tile;
-      const bool valid = row < N;
       long long V[8];
 #pragma unroll
       for (int m = 0; m < 8; ++m)
         V[m] = ((long long)(int)r[m] << 16) + ((long long)(int)r[8 + m] << 8) + (long long)(int)r[16 + m];
-      if (kb - ka != KT) {
-        // row tile shared with other CTAs: exact 64-bit integer sum, last contributor finishes
+      const int fin_rank = E == MvEpi::QkvPost ? t % C : ri / share;
+      bool mine = fin_rank == rank;
+      if (C > 1) {
+        unsigned long long *rb = red + (size_t)buf * 128 * 8;
+        // the ranks finished reading this buffer two tiles ago
+        bool ok = j < 2 || mbar_wait_cluster(&sm.redempty[buf], (unsigned)(((j >> 1) - 1) & 1));
 #pragma unroll
-        for (int m = 0; m < 8; ++m)
-          if (valid && m < M) atomicAdd(p.acc + (size_t)row * 8 + m, (unsigned long long)V[m]);
-        __threadfence();
+        for (int m = 0; m < 8; ++m) rb[ri * 8 + m] = (unsigned long long)V[m];
         named_bar(1, kUEpiThreads);
         if (threadIdx.x == 0) {
-          const unsigned old = atomicAdd(p.tile_ctr + t, (unsigned)(kb - ka));
-          sm.fin = old + (unsigned)(kb - ka) == (unsigned)KT;
+          asm volatile("fence.acq_rel.cluster;" ::: "memory");
+          for (int q = 0; q < C; ++q) mbar_arrive_remote(cluster_map(smem_u32(&sm.redfull[buf]), (uint32_t)q));
+        }
+        ok = mbar_wait_cluster(&sm.redfull[buf], (unsigned)((j >> 1) & 1)) && ok;
+        if (!ok) u_fail(sm, p.err);
+        if (mine) {
+          const uint32_t local = smem_u32(rb + ri * 8);
+#pragma unroll
+          for (int m = 0; m < 8; ++m) V[m] = 0;
+          for (int q = 0; q < C; ++q) {
+            const uint32_t ra = cluster_map(local, (uint32_t)q);
+            unsigned long long part[8];
+#pragma unroll
+            for (int h = 0; h < 4; ++h) ld_cluster_u64x2(ra + 16 * h, part[2 * h], part[2 * h + 1]);
+#pragma unroll
+            for (int m = 0; m < 8; ++m) V[m] += (long long)part[m];
+          }
         }
         named_bar(1, kUEpiThreads);
-        if (!sm.fin) continue;
-        __threadfence();
-#pragma unroll
-        for (int m = 0; m < 8; ++m)
-          if (valid && m < M) V[m] = (long long)atomicExch(p.acc + (size_t)row * 8 + m, 0ull);
-        if (threadIdx.x == 0) atomicExch(p.tile_ctr + t, 0u);
+        if (threadIdx.x == 0)
+          for (int q = 0; q < C; ++q) mbar_arrive_remote(cluster_map(smem_u32(&sm.redempty[buf]), (uint32_t)q));
       }
+
+      const int row = t * 128 + ri;
+      const bool valid = mine && row < N;
       const float sc = valid ? p.scales[row] : 0.0f;
       float yv[8];
 #pragma unroll
@@ -397,18 +420,21 @@ __global__ void __launch_bounds__(kUWarps * 32, 1) int8_umma_kernel(const __grid
             best[m] = key > best[m] ? key : best[m];
           }
       } else if constexpr (E == MvEpi::QkvPost) {
-        // the tile is one 128-wide head: finish it here
+        // the tile is one 128-wide head: its finishing rank completes it here
+        if (fin_rank == rank) {
 #pragma unroll
-        for (int m = 0; m < 8; ++m) sm.hs[m][r_in_tile] = yv[m];
-        named_bar(2, kUEpiThreads);
-        for (int m = warp; m < M; m += 4) {
-          const float4 hv = reinterpret_cast<const float4 *>(sm.hs[m])[lane];
-          qkv_head_post(p.post, p.eps, t, m, hv, p.err);
+          for (int m = 0; m < 8; ++m) sm.hs[m][ri] = yv[m];
+          named_bar(2, kUEpiThreads);
+          for (int m = warp; m < M; m += 4) {
+            const float4 hv = reinterpret_cast<const float4 *>(sm.hs[m])[lane];
+            qkv_head_post(p.post, p.eps, t, m, hv, p.err);
+          }
+          named_bar(2, kUEpiThreads);
         }
-        named_bar(2, kUEpiThreads);
       }
     }
   }
+  if (C > 1) cluster_arrive_all();  // this thread touches no other rank's memory from here on
   __syncthreads();
 
   if constexpr (E == MvEpi::Argmax) {
@@ -442,12 +468,15 @@ __global__ void __launch_bounds__(kUWarps * 32, 1) int8_umma_kernel(const __grid
     if (sm.last && threadIdx.x == 0) atomicExch(p.counter, 0u);
   }
 
-  // ---- teardown: copies in flight land, then TMEM is released
+  // ---- teardown: copies in flight land, no rank leaves while a peer may
+  // still read its partials or arrive on its barriers, then TMEM is released
   if (producer) {
     for (int i = max(0, produced - STAGES); i < produced; ++i)
       mbar_wait(&sm.full[i % STAGES], (unsigned)((i / STAGES) & 1));
   }
   tc_fence_before();
+  __syncwarp();
+  if (C > 1) cluster_wait_all();  // arrived after the role loops
   __syncthreads();
   if (warp == kUMmaWarp) {
     __syncwarp();
@@ -509,78 +538,160 @@ static int umma_sms() {
   return sms[dev];
 }
 
-static size_t umma_smem_bytes(int stages, int nb, bool norm, int M, int K) {
-  return 1024 + (size_t)stages * kUTile + (size_t)nb * kUBSlot + (norm ? (size_t)(M + 1) * K * 4 : 0) +
-         sizeof(USmem);
+static size_t umma_smem_bytes(int stages, int C, bool norm, int M, int K) {
+  const int KC = K / 128 / C;
+  return 1024 + (size_t)stages * kUTile + (size_t)KC * kUBSlot + (C > 1 ? 2 * kURed : 0) +
+         (norm ? (size_t)(M + 1) * K * 4 : 0) + sizeof(USmem);
+}
+
+struct UmmaPlan {
+  int C = 0, clusters = 0, stages = 0;
+  size_t smem = 0;
+};
+
+// Shared-memory opt-in (and, for clusters above 8, the non-portable size) of
+// one kernel instance on the current device; -1 if unavailable.
+template <MvEpi E, bool NORM>
+static int umma_prepare(int dev) {
+  static int state[64] = {0};  // 0 unknown, 1 portable clusters only, 2 up to 16
+  if (dev < 0 || dev >= 64) return -1;
+  if (!state[dev]) {
+    if (cudaFuncSetAttribute(int8_umma_kernel<E, NORM>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) !=
+        cudaSuccess) {
+      cudaGetLastError();
+      return -1;
+    }
+    state[dev] = cudaFuncSetAttribute(int8_umma_kernel<E, NORM>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==
+                         cudaSuccess
+                     ? 2
+                     : 1;
+    cudaGetLastError();
+  }
+  return state[dev];
+}
+
+// How many clusters of C CTAs with `smem` bytes each can be resident at once.
+template <MvEpi E, bool NORM>
+static int umma_max_clusters(int dev, int C, size_t smem) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, size_t>, int> cache;
+  std::lock_guard<std::mutex> lk(mu);
+  const auto key = std::make_tuple(dev, C, smem);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)C);
+  cfg.blockDim = dim3(kUWarps * 32);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)C;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, int8_umma_kernel<E, NORM>, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    n = 0;
+  }
+  cache[key] = n;
+  return n;
+}
+
+// Pick the cluster size: the K tiles of a row tile are split over the C
+// ranks of a cluster.  Cost model in units of one 16 KB weight tile streamed
+// by one SM: the busiest cluster's row tiles x K tiles per rank, plus the
+// exchange of partials when C > 1 (about three tiles' time, then one per
+// further row tile).
+template <MvEpi E, bool NORM>
+static UmmaPlan umma_plan(const UmmaParams &p, bool norm) {
+  UmmaPlan best;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int state = umma_prepare<E, NORM>(dev);
+  if (state < 0) return best;
+  const int KT = p.K / 128, NT = (p.N + 127) / 128;
+  double best_cost = 1e30;
+  for (int C = 1; C <= kUMaxCluster && C <= KT; ++C) {
+    if (KT % C || (C > 8 && state < 2) || 128 % (2 * C) && C > 1) continue;  // even row shares
+    int stages = kUMaxStages;
+    while (stages > 2 && umma_smem_bytes(stages, C, norm, p.M, p.K) > 227 * 1024) --stages;
+    const size_t smem = umma_smem_bytes(stages, C, norm, p.M, p.K);
+    if (smem > 227 * 1024) continue;
+    const int resident = C == 1 ? umma_max_clusters<E, NORM>(dev, 1, smem) * 1 : umma_max_clusters<E, NORM>(dev, C, smem);
+    if (resident < 1) continue;
+    const int clusters = std::min(NT, resident);
+    const int tiles = (NT + clusters - 1) / clusters;
+    const double cost = (double)tiles * (KT / C) + (C > 1 ? 3.0 + tiles : 0.0);
+    if (cost < best_cost - 1e-9) {
+      best_cost = cost;
+      best.C = C;
+      best.clusters = clusters;
+      best.smem = smem;
+      best.stages = std::max(2, std::min(stages, tiles * (KT / C)));
+    }
+  }
+  return best;
 }
 
 template <MvEpi E, bool NORM>
-static int umma_launch_t(const UmmaParams &p, int grid, size_t smem, cudaStream_t st, bool pdl) {
-  static int attr_dev_mask = 0;  // devices on which the shared-memory opt-in was done
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 31 && !(attr_dev_mask & (1 << dev))) {
-    int rc = cuda_status(cudaFuncSetAttribute(int8_umma_kernel<E, NORM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              227 * 1024),
-                         "int8 tensor-core matvec: shared memory opt-in");
-    if (rc) return rc;
-    attr_dev_mask |= 1 << dev;
+static int umma_launch_t(UmmaParams p, cudaStream_t st, bool pdl) {
+  const UmmaPlan plan = umma_plan<E, NORM>(p, NORM);
+  if (!plan.C) {
+    set_error("int8 tensor-core matvec: no launch configuration fits (M=%d K=%d N=%d)", p.M, p.K, p.N);
+    return QASR_ERR_UNSUPPORTED;
   }
+  p.csize = plan.C;
+  p.stages = plan.stages;
+  const size_t smem = umma_smem_bytes(p.stages, plan.C, NORM, p.M, p.K);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)grid);
+  cfg.gridDim = dim3((unsigned)(plan.clusters * plan.C));
   cfg.blockDim = dim3(kUWarps * 32);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (plan.C > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = (unsigned)plan.C;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  if (pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
+  cfg.numAttrs = na;
   return cuda_status(cudaLaunchKernelEx(&cfg, int8_umma_kernel<E, NORM>, p), "int8 tensor-core matvec launch");
 }
 
 int umma_launch(UmmaParams p, MvEpi e, cudaStream_t st, bool pdl) {
   const bool norm = p.norm_w != nullptr;
-  if (p.M < 1 || p.M > 8 || p.K <= 0 || p.K % 128 || p.N <= 0 || !p.x || !p.scales || !p.acc || !p.tile_ctr ||
+  if (p.M < 1 || p.M > 8 || p.K <= 0 || p.K % 128 || p.N <= 0 || !p.x || !p.scales ||
       (reinterpret_cast<uintptr_t>(p.x) & 15) || (p.x_stride & 3) ||
       (norm && (reinterpret_cast<uintptr_t>(p.norm_w) & 15)) ||
       (e == MvEpi::Argmax && (!p.keys || !p.counter || !p.ids)) || (e == MvEpi::SwiGLU && (p.N & 1)) ||
       (e == MvEpi::QkvPost && (!p.post.positions || p.N != (p.post.n_heads + 2 * p.post.n_kv) * 128)) ||
-      (e != MvEpi::Argmax && e != MvEpi::QkvPost && !p.y) || (e == MvEpi::StoreBias && !p.bias)) {
+      (e != MvEpi::Argmax && e != MvEpi::QkvPost && !p.y) || (e == MvEpi::StoreBias && !p.bias) ||
+      (long long)((p.N + 127) / 128) * (p.K / 128) >= (1ll << 30)) {
     set_error("int8 tensor-core matvec: unsupported configuration (M=%d K=%d N=%d)", p.M, p.K, p.N);
-    return QASR_ERR_UNSUPPORTED;
-  }
-  const int KT = p.K / 128, NT = (p.N + 127) / 128;
-  const long long U = (long long)NT * KT;
-  if (U >= (1ll << 30)) {
-    set_error("int8 tensor-core matvec: matrix too large");
-    return QASR_ERR_UNSUPPORTED;
-  }
-  const int grid = (int)std::min<long long>(umma_sms(), U);
-  const int nu_max = (int)((U + grid - 1) / grid);
-  p.nb = std::min(KT, nu_max);
-  p.stages = std::max(2, std::min(kUMaxStages, nu_max));
-  while (p.stages > 2 && umma_smem_bytes(p.stages, p.nb, norm, p.M, p.K) > 227 * 1024) --p.stages;
-  const size_t smem = umma_smem_bytes(p.stages, p.nb, norm, p.M, p.K);
-  if (smem > 227 * 1024) {
-    set_error("int8 tensor-core matvec: shared memory %zu too large (M=%d K=%d)", smem, p.M, p.K);
     return QASR_ERR_UNSUPPORTED;
   }
   switch (e) {
     case MvEpi::Store:
-      return norm ? umma_launch_t<MvEpi::Store, true>(p, grid, smem, st, pdl)
-                  : umma_launch_t<MvEpi::Store, false>(p, grid, smem, st, pdl);
-    case MvEpi::StoreBias: return umma_launch_t<MvEpi::StoreBias, false>(p, grid, smem, st, pdl);
-    case MvEpi::Residual: return umma_launch_t<MvEpi::Residual, false>(p, grid, smem, st, pdl);
+      return norm ? umma_launch_t<MvEpi::Store, true>(p, st, pdl) : umma_launch_t<MvEpi::Store, false>(p, st, pdl);
+    case MvEpi::StoreBias: return umma_launch_t<MvEpi::StoreBias, false>(p, st, pdl);
+    case MvEpi::Residual: return umma_launch_t<MvEpi::Residual, false>(p, st, pdl);
     case MvEpi::SwiGLU:
-      return norm ? umma_launch_t<MvEpi::SwiGLU, true>(p, grid, smem, st, pdl)
-                  : umma_launch_t<MvEpi::SwiGLU, false>(p, grid, smem, st, pdl);
+      return norm ? umma_launch_t<MvEpi::SwiGLU, true>(p, st, pdl) : umma_launch_t<MvEpi::SwiGLU, false>(p, st, pdl);
     case MvEpi::Argmax:
-      return norm ? umma_launch_t<MvEpi::Argmax, true>(p, grid, smem, st, pdl)
-                  : umma_launch_t<MvEpi::Argmax, false>(p, grid, smem, st, pdl);
+      return norm ? umma_launch_t<MvEpi::Argmax, true>(p, st, pdl) : umma_launch_t<MvEpi::Argmax, false>(p, st, pdl);
     case MvEpi::QkvPost:
-      return norm ? umma_launch_t<MvEpi::QkvPost, true>(p, grid, smem, st, pdl)
-                  : umma_launch_t<MvEpi::QkvPost, false>(p, grid, smem, st, pdl);
+      return norm ? umma_launch_t<MvEpi::QkvPost, true>(p, st, pdl) : umma_launch_t<MvEpi::QkvPost, false>(p, st, pdl);
   }
   return QASR_ERR_INVALID;
 }
