@@ -7,6 +7,8 @@
 // c ^ (r & 7), atoms 1024 bytes apart along M/N.  Atom bases must be
 // 1024-byte aligned; a K step inside the atom advances the start address.
 #pragma once
+#include <cuda.h>
+
 #include "common.cuh"
 #include "tma.cuh"
 
