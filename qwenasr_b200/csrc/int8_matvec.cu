@@ -298,6 +298,10 @@ static int linear_int8_impl(const char *fn, float *y, const float *x, const int8
                             const float *bias, int seq, int in_dim, int out_dim, void *stream) {
   int rc = check_mv(fn, y, x, w, scales, seq, in_dim, out_dim);
   if (rc) return rc;
+  if (seq > 8) {  // prefill / encoder shapes: one tensor-core GEMM over all rows
+    rc = int8_gemm(y, out_dim, x, in_dim, w, scales, bias, seq, in_dim, out_dim, S(stream));
+    if (rc != QASR_ERR_UNSUPPORTED) return rc;
+  }
   for (int s0 = 0; s0 < seq; s0 += 8) {
     const int m = std::min(8, seq - s0);
     rc = try_umma(x + (size_t)s0 * in_dim, in_dim, nullptr, 0.f, w, scales, bias, y + (size_t)s0 * out_dim, out_dim,

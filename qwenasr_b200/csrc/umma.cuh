@@ -37,6 +37,12 @@ int umma_weight_map(CUtensorMap *tm, const int8_t *w, int N, int K);
 // QASR_ERR_UNSUPPORTED (nothing launched) for shapes it does not cover.
 int umma_launch(UmmaParams p, MvEpi e, cudaStream_t st, bool pdl);
 
+// y[t, o] = scales[o] * sum_k w[o, k] * x[t, k] (+ bias[o]) for T token rows on
+// the tensor cores (umma_gemm.cu); QASR_ERR_UNSUPPORTED (nothing launched)
+// for shapes it does not cover.
+int int8_gemm(float *y, long y_stride, const float *x, long x_stride, const int8_t *w, const float *scales,
+              const float *bias, int T, int K, int N, cudaStream_t st);
+
 // Driver entry point cuTensorMapEncodeTiled (resolved once).
 void *tensor_map_encoder();
 

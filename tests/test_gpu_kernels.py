@@ -294,6 +294,35 @@ def test_linear_int8_bias(orc):
     assert ok and err < 5e-5, err
 
 
+@pytest.mark.parametrize("seq,out_dim,in_dim,bias", [
+    (33, 1024, 1024, False),    # just past one 32-token block
+    (200, 4096, 1024, False),   # decoder prefill q|k|v rows
+    (390, 896, 896, True),      # encoder projection, one 30 s window of tokens
+    (100, 1000, 3072, True),    # rows not a multiple of the 128-row tile
+])
+def test_int8_gemm_prefill_shapes(orc, seq, out_dim, in_dim, bias):
+    """seq_len > 8 runs as one tensor-core GEMM (the reference: seq_len matvecs,
+    mod.rs:650-673); same 2e-3 bar as the matvecs."""
+    rng = np.random.default_rng(seq + out_dim)
+    w, s = orc.quantize_f32_to_int8((rng.standard_normal((out_dim, in_dim)) * 0.02).astype(np.float32))
+    x = (rng.standard_normal((seq, in_dim)) * rng.uniform(0.01, 10.0, (seq, 1))).astype(np.float32)
+    y = torch.empty(seq, out_dim, device=DEV)
+    if bias:
+        b = (rng.standard_normal(out_dim) * 0.1).astype(np.float32)
+        K.linear_int8(y, T(x), T(w), T(s), T(b), seq, in_dim, out_dim)
+        ref = orc.linear_int8(x, w, s, b)
+    else:
+        K.linear_nobias_int8(y, T(x), T(w), T(s), seq, in_dim, out_dim)
+        ref = orc.linear_nobias_int8(x, w, s)
+    ok, err = rel_close(H(y), ref, 2e-3)
+    assert ok and err < 5e-5, err
+    # a second call with fewer rows reuses the digit scratch: stale rows must not leak
+    y2 = torch.full((seq // 2, out_dim), float("nan"), device=DEV)
+    K.linear_nobias_int8(y2, T(x[: seq // 2]), T(w), T(s), seq // 2, in_dim, out_dim)
+    ok, err = rel_close(H(y2), orc.linear_nobias_int8(x[: seq // 2], w, s), 2e-3)
+    assert ok and err < 5e-5, err
+
+
 @pytest.mark.parametrize("M", [1, 5, 8])
 def test_matvec_residual_and_gateup_swiglu(orc, M):
     rng = np.random.default_rng(M)
