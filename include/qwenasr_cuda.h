@@ -122,8 +122,9 @@ int qasr_swiglu_multiply(float *out, const float *gate_up, int seq, int inter, v
 int qasr_add_inplace(float *a, const float *b, int64_t n, void *stream);
 
 /* kernels::linear_nobias_int8 (mod.rs:650-661; generic::int8_matvec_fused
- * generic.rs:39-49): y[s,o] = scales[o] * sum_k w[o,k]*x[s,k].  Any seq
- * (tokens are processed in groups of up to 8 per weight pass). */
+ * generic.rs:39-49): y[s,o] = scales[o] * sum_k w[o,k]*x[s,k].  Any seq: up
+ * to 8 rows as a weight-streaming tensor-core contraction, more as one
+ * tensor-core GEMM over all rows (the reference runs seq matvecs). */
 int qasr_linear_nobias_int8(float *y, const float *x, const int8_t *w, const float *scales, int seq, int in_dim,
                             int out_dim, void *stream);
 
@@ -262,6 +263,17 @@ int qasr_decoder_kv(qasr_decoder *dec, int slot, float **k_cache, float **v_cach
  * out, all HOST buffers.  Sequence m embeds tokens[m], writes its K/V at
  * row positions[m] of its cache and attends over rows 0..positions[m]. */
 int qasr_decoder_step(qasr_decoder *dec, const int32_t *tokens, const int32_t *positions, int M, int32_t *next_tokens);
+
+/* decoder_prefill_int8 (decoder.rs:751-842) for sequence `slot`: the prompt
+ * rows embeds [seq, hidden] f32 (host or device pointer) at positions
+ * start_pos .. start_pos+seq-1 run through every layer and their K/V rows
+ * are written to the slot's cache (KvCache with len = start_pos).  The next
+ * decode step for the slot is at position start_pos + seq.  Synchronous. */
+int qasr_decoder_prefill(qasr_decoder *dec, int slot, const float *embeds, int seq, int start_pos);
+
+/* Device pointer to the residual stream [seq, hidden] left by the last
+ * prefill (the reference's bufs.pref_x); NULL before the first prefill. */
+const float *qasr_decoder_prefill_hidden(qasr_decoder *dec);
 
 /* Same step on DEVICE buffers, enqueued on the engine's stream without a
  * host synchronisation; next_tokens may alias tokens. */

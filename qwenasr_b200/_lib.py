@@ -79,6 +79,8 @@ _SIGS = {
     "qasr_decoder_set_globals": (I, [P, P, P, P, P, P]),
     "qasr_decoder_kv": (I, [P, I, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p)]),
     "qasr_decoder_step": (I, [P, P, P, I, P]),
+    "qasr_decoder_prefill": (I, [P, I, P, I, I]),
+    "qasr_decoder_prefill_hidden": (P, [P]),
     "qasr_decoder_step_device": (I, [P, P, P, I, P]),
     "qasr_decoder_stream": (P, [P]),
     "qasr_decoder_keep_logits": (I, [P, I]),

@@ -67,6 +67,11 @@ struct qasr_decoder {
   int32_t *h_tok = nullptr, *h_pos = nullptr, *h_next = nullptr;  // pinned staging
   int *h_err = nullptr;
   bool keep_logits = false;
+  // prefill work buffers (decoder_prefill_int8's DecoderBuffers), grown on demand
+  int pf_cap = 0;
+  float *pf_x = nullptr, *pf_xn = nullptr, *pf_q = nullptr, *pf_k = nullptr, *pf_v = nullptr, *pf_attn = nullptr,
+        *pf_proj = nullptr, *pf_gu = nullptr, *pf_h = nullptr;
+  void *pf_block = nullptr;
   std::vector<cudaGraphExec_t> graphs;  // per M (index M), built lazily
   std::vector<void *> allocs;
   long seq_stride() const { return (long)cfg.n_layers * cfg.max_seq * cfg.n_kv_heads * cfg.head_dim; }
@@ -127,6 +132,7 @@ extern "C" void qasr_decoder_free(qasr_decoder *d) {
   for (auto g : d->graphs)
     if (g) cudaGraphExecDestroy(g);
   for (void *p : d->allocs) cudaFree(p);
+  if (d->pf_block) cudaFree(d->pf_block);
   if (d->h_tok) cudaFreeHost(d->h_tok);
   if (d->stream) cudaStreamDestroy(d->stream);
   delete d;
@@ -533,3 +539,88 @@ extern "C" int qasr_decoder_profile_step(qasr_decoder *d, const int32_t *tokens,
   }
   return QASR_OK;
 }
+
+// decoder_prefill_int8 (decoder.rs:751-842) for sequence `slot`: the prompt
+// rows embeds[0..seq) (host or device, [seq, hidden] f32) at positions
+// start_pos.. go through every layer; their K/V rows are written to the
+// slot's cache.  The projections run as tensor-core GEMMs over all rows
+// (the reference: seq_len matvecs), the norms, RoPE, attention and SwiGLU
+// are the kernel-level entries, in the reference's order.
+extern "C" int qasr_decoder_prefill(qasr_decoder *d, int slot, const float *embeds, int seq, int start_pos) {
+  if (!d || !embeds || slot < 0 || slot >= (d ? d->cfg.max_batch : 0) || seq <= 0 || start_pos < 0) {
+    set_error("qasr_decoder_prefill: invalid arguments");
+    return QASR_ERR_INVALID;
+  }
+  const qasr_decoder_config &c = d->cfg;
+  if (start_pos + seq > c.max_seq) {
+    set_error("qasr_decoder_prefill: positions %d..%d outside the cache (max_seq %d)", start_pos,
+              start_pos + seq - 1, c.max_seq);
+    return QASR_ERR_INVALID;
+  }
+  cudaSetDevice(d->device);
+  cudaStream_t st = d->stream;
+  const int H = c.hidden, I = c.inter, hd = c.head_dim;
+  const int q_dim = c.n_heads * hd, kv_dim = c.n_kv_heads * hd;
+  int rc = QASR_OK;
+  if (seq > d->pf_cap) {
+    const int cap = std::max(seq, 64);
+    const size_t per_row = (size_t)2 * H + 2 * q_dim + 2 * kv_dim + H + 2 * I + I;
+    void *blk = nullptr;
+    if ((rc = cuda_status(cudaStreamSynchronize(st), "qasr_decoder_prefill"))) return rc;
+    if ((rc = cuda_status(cudaMalloc(&blk, per_row * cap * 4), "qasr_decoder_prefill: buffers"))) return rc;
+    if (d->pf_block) cudaFree(d->pf_block);
+    d->pf_block = blk;
+    float *f = static_cast<float *>(blk);
+    auto take = [&](size_t n) { float *r = f; f += n * cap; return r; };
+    d->pf_x = take(H);
+    d->pf_xn = take(H);
+    d->pf_q = take(q_dim);
+    d->pf_attn = take(q_dim);
+    d->pf_k = take(kv_dim);
+    d->pf_v = take(kv_dim);
+    d->pf_proj = take(H);
+    d->pf_gu = take(2 * I);
+    d->pf_h = take(I);
+    d->pf_cap = cap;
+  }
+  if ((rc = cuda_status(cudaMemcpyAsync(d->pf_x, embeds, (size_t)seq * H * 4, cudaMemcpyDefault, st), "prefill embeds")))
+    return rc;
+  const float *cos_r = d->rope_cos + (size_t)start_pos * hd, *sin_r = d->rope_sin + (size_t)start_pos * hd;
+  float *kc = d->k_cache + (size_t)slot * d->seq_stride(), *vc = d->v_cache + (size_t)slot * d->seq_stride();
+  const float scale = 1.0f / sqrtf((float)hd);
+  const int total = start_pos + seq;
+  for (int l = 0; l < c.n_layers && !rc; ++l) {
+    const LayerDev &L = d->layers[l];
+    const size_t kv_rows = (size_t)kv_dim * H;
+    if ((rc = qasr_rms_norm(d->pf_xn, d->pf_x, L.in_norm, seq, H, c.eps, st))) break;
+    // q, k, v: the three row ranges of the fused q|k|v matrix
+    if ((rc = qasr_linear_nobias_int8(d->pf_q, d->pf_xn, L.wqkv, L.sqkv, seq, H, q_dim, st))) break;
+    if ((rc = qasr_linear_nobias_int8(d->pf_k, d->pf_xn, L.wqkv + (size_t)q_dim * H, L.sqkv + q_dim, seq, H, kv_dim,
+                                      st)))
+      break;
+    if ((rc = qasr_linear_nobias_int8(d->pf_v, d->pf_xn, L.wqkv + (size_t)q_dim * H + kv_rows, L.sqkv + q_dim + kv_dim,
+                                      seq, H, kv_dim, st)))
+      break;
+    if ((rc = qasr_rms_norm_per_head(d->pf_q, L.q_norm, seq, c.n_heads, hd, c.eps, st))) break;
+    if ((rc = qasr_rms_norm_per_head(d->pf_k, L.k_norm, seq, c.n_kv_heads, hd, c.eps, st))) break;
+    if ((rc = qasr_apply_rope_neox(d->pf_q, cos_r, sin_r, seq, c.n_heads, hd, st))) break;
+    if ((rc = qasr_apply_rope_neox(d->pf_k, cos_r, sin_r, seq, c.n_kv_heads, hd, st))) break;
+    if ((rc = qasr_kv_append(kc, vc, d->pf_k, d->pf_v, l, c.max_seq, kv_dim, start_pos, seq, st))) break;
+    const size_t lay = (size_t)l * c.max_seq * kv_dim;
+    if ((rc = qasr_causal_attention(d->pf_attn, d->pf_q, kc + lay, vc + lay, seq, total, c.n_heads, c.n_kv_heads, hd,
+                                    scale, start_pos, st)))
+      break;
+    if ((rc = qasr_linear_nobias_int8(d->pf_proj, d->pf_attn, L.wo, L.so, seq, q_dim, H, st))) break;
+    if ((rc = qasr_add_inplace(d->pf_x, d->pf_proj, (int64_t)seq * H, st))) break;
+    if ((rc = qasr_rms_norm(d->pf_xn, d->pf_x, L.post_norm, seq, H, c.eps, st))) break;
+    if ((rc = qasr_linear_nobias_int8(d->pf_gu, d->pf_xn, L.gate_up, L.sgu, seq, H, 2 * I, st))) break;
+    if ((rc = qasr_swiglu_multiply(d->pf_h, d->pf_gu, seq, I, st))) break;
+    if ((rc = qasr_linear_nobias_int8(d->pf_proj, d->pf_h, L.down, L.sdown, seq, I, H, st))) break;
+    if ((rc = qasr_add_inplace(d->pf_x, d->pf_proj, (int64_t)seq * H, st))) break;
+  }
+  if (!rc) rc = cuda_status(cudaStreamSynchronize(st), "qasr_decoder_prefill");
+  return rc;
+}
+
+// Residual stream after the last prefill (device, [seq, hidden]); NULL before one.
+extern "C" const float *qasr_decoder_prefill_hidden(qasr_decoder *d) { return d ? d->pf_x : nullptr; }

@@ -104,6 +104,26 @@ class Decoder:
                   out.ctypes.data_as(C.c_void_p))
         return out
 
+    def prefill(self, slot: int, embeds, start_pos: int = 0) -> None:
+        """decoder_prefill_int8 for one sequence: embeds [seq, hidden] f32
+        (numpy or a CUDA tensor) at positions start_pos..; fills its K/V rows."""
+        if isinstance(embeds, torch.Tensor):
+            e = embeds.detach().float().contiguous()
+            ptr, seq = e.data_ptr(), e.shape[0]
+        else:
+            e = np.ascontiguousarray(embeds, dtype=np.float32)
+            ptr, seq = e.ctypes.data, e.shape[0]
+        _lib.call("qasr_decoder_prefill", self._h, int(slot), C.c_void_p(ptr), int(seq), int(start_pos))
+
+    def prefill_hidden(self, seq: int) -> torch.Tensor:
+        """Residual stream [seq, hidden] left by the last prefill (a copy)."""
+        ptr = _lib.load().qasr_decoder_prefill_hidden(self._h)
+        if not ptr:
+            raise RuntimeError("no prefill has run")
+        with torch.cuda.device(self.device):
+            view = torch.as_tensor(_DevArray(ptr, (seq, self.cfg["hidden"])), device=f"cuda:{self.device}")
+            return view.clone()
+
     def step_device(self, tokens: torch.Tensor, positions: torch.Tensor, out: torch.Tensor) -> None:
         """Same step on device int32 tensors, enqueued on the engine stream."""
         _lib.call("qasr_decoder_step_device", self._h, C.c_void_p(tokens.data_ptr()),

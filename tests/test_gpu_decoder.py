@@ -144,3 +144,34 @@ def test_decode_step_full_0_6b(orc):
         assert int(nxt[m]) == tok
         assert rel_err(logits[m], ref_logits) < 2e-3
     dec.close()
+
+
+@pytest.mark.parametrize("P", [1, 37, 129])
+def test_prefill_then_decode_matches_oracle(orc, P):
+    """decoder_prefill_int8 (decoder.rs:751-842) in two chunks, then one decode
+    step at position P: K/V rows, residual stream, logits and the greedy id
+    against the oracle's prefill + forward."""
+    orc.set_threads(8)
+    w, od, dec = build_pair(orc, SMALL, seed=50 + P, max_seq=256, max_batch=1)
+    rng = np.random.default_rng(P)
+    ids = rng.integers(0, SMALL["vocab"], P + 1).astype(np.int32)
+    emb = w["embed"][ids[:P]]
+    kh, vh = od.new_kv(256)
+    ref_x = od.prefill(kh, vh, 0, emb)
+    cut = P // 2
+    if cut:
+        dec.prefill(0, emb[:cut], 0)
+    dec.prefill(0, torch.from_numpy(emb[cut:]).to(DEV), cut)  # host and device prompt rows
+    kg, vg = dec.kv(0)
+    assert rel_err(kg[:, :P].cpu().numpy(), kh[:, :P]) < 2e-3
+    assert rel_err(vg[:, :P].cpu().numpy(), vh[:, :P]) < 2e-3
+    assert not kg[:, P:].cpu().numpy().any()
+    assert rel_err(dec.prefill_hidden(P - cut).cpu().numpy(), ref_x[cut:]) < 2e-3
+    dec.keep_logits(True)
+    nxt = dec.step(ids[P:P + 1], [P])
+    tok, ref_logits, _ = od.forward(kh, vh, P, w["embed"][ids[P]], want_logits=True)
+    assert int(nxt[0]) == tok
+    assert rel_err(dec.logits(1).cpu().numpy()[0], ref_logits) < 2e-3
+    with pytest.raises(Exception, match="outside"):
+        dec.prefill(0, emb[:1], 256)
+    dec.close()
