@@ -175,3 +175,27 @@ def test_prefill_then_decode_matches_oracle(orc, P):
     with pytest.raises(Exception, match="outside"):
         dec.prefill(0, emb[:1], 256)
     dec.close()
+
+
+def test_segment_batch_greedy_matches_oracle(orc):
+    """segments.decode_batch (the per-rank work of the batched-segment mode):
+    prompts of different lengths prefilled into their own slots, then greedy
+    steps at per-sequence positions; ids equal the oracle's prefill + forward."""
+    from qwenasr_b200 import segments
+    orc.set_threads(8)
+    w, od, dec = build_pair(orc, SMALL, seed=9, max_seq=96, max_batch=3)
+    rng = np.random.default_rng(5)
+    lens = [5, 0, 23]
+    prompts = [w["embed"][rng.integers(0, SMALL["vocab"], n)] for n in lens]
+    first = rng.integers(0, SMALL["vocab"], 3).astype(np.int32)
+    got = segments.decode_batch(dec, prompts, first, 4)
+    for i, n in enumerate(lens):
+        kh, vh = od.new_kv(96)
+        if n:
+            od.prefill(kh, vh, 0, prompts[i])
+        tok, ids = int(first[i]), []
+        for k in range(4):
+            tok, _, _ = od.forward(kh, vh, n + k, w["embed"][tok])
+            ids.append(tok)
+        assert got[i] == ids, (i, got[i], ids)
+    dec.close()
