@@ -132,6 +132,19 @@ int qasr_linear_nobias_int8(float *y, const float *x, const int8_t *w, const flo
 int qasr_linear_int8(float *y, const float *x, const int8_t *w, const float *scales, const float *bias, int seq,
                      int in_dim, int out_dim, void *stream);
 
+/* kernels::linear (mod.rs:531-565; cblas_sgemm in the reference):
+ * y[s,o] = sum_k x[s,k]*w[o,k] + b[o] (b may be NULL), f32 weights [out, in].
+ * Tensor cores for in_dim % 16 == 0, in_dim >= 128, out_dim >= 128 (each
+ * operand as three exact int8 digit planes); a CUDA-core kernel otherwise. */
+int qasr_linear(float *y, const float *x, const float *w, const float *b, int seq, int in_dim, int out_dim,
+                void *stream);
+
+/* kernels::linear_nobias (mod.rs:567-568). */
+int qasr_linear_nobias(float *y, const float *x, const float *w, int seq, int in_dim, int out_dim, void *stream);
+
+/* kernels::matmul_t (mod.rs:503-528): c[m,n] = sum_k a[m,k]*b[n,k]. */
+int qasr_matmul_t(float *c, const float *a, const float *b, int m, int k, int n, void *stream);
+
 /* kernels::causal_attention (mod.rs:1124-1207): GQA causal attention of
  * seq_q queries at global positions q_offset.. over k/v [seq_k, n_kv*hd].
  * head_dim must be 64 or 128. */

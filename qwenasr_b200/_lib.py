@@ -64,6 +64,9 @@ _SIGS = {
     "qasr_linear_nobias_int8": (I, [P, P, P, P, I, I, I, P]),
     "qasr_linear_int8": (I, [P, P, P, P, P, I, I, I, P]),
     "qasr_causal_attention": (I, [P, P, P, P, I, I, I, I, I, F, I, P]),
+    "qasr_linear": (I, [P, P, P, P, I, I, I, P]),
+    "qasr_linear_nobias": (I, [P, P, P, I, I, I, P]),
+    "qasr_matmul_t": (I, [P, P, P, I, I, I, P]),
     "qasr_quantize_f32_to_int8": (I, [P, I64, I64, P, P, P]),
     "qasr_embed_gather_f32": (I, [P, P, P, I, I, I64, P, P]),
     "qasr_embed_gather_int8": (I, [P, P, P, P, I, I, I64, P, P]),

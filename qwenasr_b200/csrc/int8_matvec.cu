@@ -249,8 +249,8 @@ static int check_mv(const char *fn, const float *y, const float *x, const int8_t
 // QASR_ERR_UNSUPPORTED (nothing launched) for shapes it does not cover.
 static int try_umma(const float *x, long xs, const float *nw, float eps, const int8_t *w, const float *scales,
                     const float *bias, float *y, long ys, int M, int K, int N, MvEpi e, int32_t *ids, cudaStream_t st) {
-  if (K % 128 || (reinterpret_cast<uintptr_t>(w) & 15) || (reinterpret_cast<uintptr_t>(x) & 15) || (xs & 3) ||
-      (reinterpret_cast<uintptr_t>(nw) & 15) || M < 1 || M > 8 || (e == MvEpi::SwiGLU && (N & 1)))
+  if (K % 128 || N < 128 || (reinterpret_cast<uintptr_t>(w) & 15) || (reinterpret_cast<uintptr_t>(x) & 15) ||
+      (xs & 3) || (reinterpret_cast<uintptr_t>(nw) & 15) || M < 1 || M > 8 || (e == MvEpi::SwiGLU && (N & 1)))
     return QASR_ERR_UNSUPPORTED;
   UmmaParams p{};
   int rc = umma_weight_map(&p.tmap, w, N, K);

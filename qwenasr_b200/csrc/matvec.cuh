@@ -90,7 +90,8 @@ int mv_pick_rows(int N, MvEpi e);
 int argmax_scratch(unsigned long long **keys, unsigned **counter);
 int mv_norm_scratch(float **buf, size_t n_floats);
 
-constexpr int kScratchPartial = 0, kScratchCounter = 1, kScratchDigits = 2, kScratchDigitScale = 3, kScratchSlots = 4;
+constexpr int kScratchPartial = 0, kScratchCounter = 1, kScratchDigits = 2, kScratchDigitScale = 3,
+              kScratchWeightDigits = 4, kScratchWeightScale = 5, kScratchSlots = 6;
 int dev_scratch(int slot, size_t bytes, void **out);
 
 }  // namespace qasr

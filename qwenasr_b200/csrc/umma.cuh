@@ -43,6 +43,14 @@ int umma_launch(UmmaParams p, MvEpi e, cudaStream_t st, bool pdl);
 int int8_gemm(float *y, long y_stride, const float *x, long x_stride, const int8_t *w, const float *scales,
               const float *bias, int T, int K, int N, cudaStream_t st);
 
+// y[t, o] = sum_k w[o, k] * x[t, k] (+ bias[o]) with f32 weights on the tensor
+// cores (three digit planes per operand); QASR_ERR_UNSUPPORTED as above.
+int f32_gemm(float *y, long y_stride, const float *x, long x_stride, const float *w, const float *bias, int T, int K,
+             int N, cudaStream_t st);
+// The same on CUDA cores, any shape.
+int f32_gemm_fallback(float *y, const float *x, const float *w, const float *bias, int T, int K, int N,
+                      cudaStream_t st);
+
 // Driver entry point cuTensorMapEncodeTiled (resolved once).
 void *tensor_map_encoder();
 

@@ -1,28 +1,37 @@
-// umma_gemm.cu -- INT8-weight GEMM for many token rows on the tcgen05 tensor
-// cores: the prefill and encoder projections, kernels::linear_nobias_int8 /
-// linear_int8 with seq_len > 8 (crates/qwen-asr/src/kernels/mod.rs:650-673,
-// which the reference runs as seq_len sequential matvecs of
-// generic::int8_matvec_fused, generic.rs:39-49).
+// umma_gemm.cu -- GEMMs for many token rows on the tcgen05 tensor cores:
+//  * INT8 weights: the prefill and encoder projections,
+//    kernels::linear_nobias_int8 / linear_int8 with seq_len > 8
+//    (crates/qwen-asr/src/kernels/mod.rs:650-673; the reference runs seq_len
+//    sequential matvecs of generic::int8_matvec_fused, generic.rs:39-49);
+//  * f32 weights: kernels::linear / linear_nobias / matmul_t (mod.rs:503-568,
+//    cblas_sgemm in the reference), the encoder projections of an f32 model.
 //
-// Same exact integer formulation as the decode contraction (umma_matvec.cu):
+// Exact integer formulation (as the decode contraction, umma_matvec.cu):
 // every activation row t is scaled by 2^(22-E_t) (2^E_t bounds its largest
 // magnitude), rounded to an integer X with |X| <= 2^22 and split into three
-// balanced signed bytes X = 65536*d0 + 256*d1 + d2.  The tensor cores contract
-// the int8 weights with the digit rows exactly in 32-bit integers; the
-// epilogue recombines the digits in 64 bits and rounds once.
+// balanced signed bytes X = 65536*d0 + 256*d1 + d2 ("digit rows").  INT8
+// weights are used as they are.  f32 weights get the same treatment per
+// weight row, giving three int8 "digit planes" W_a and a per-row factor; the
+// product of two digit expansions is then sum_a sum_b 2^(8(2-a)) 2^(8(2-b))
+// W_a . X_b.  The tensor cores compute every W_a . X_b exactly in 32-bit
+// integers; the epilogue recombines them exactly in 64 bits and rounds once.
+// The only approximation is the 23-bit rounding of each operand relative to
+// its row maximum -- below the f32 summation error of the reference.
 //
-//  * digit_rows_kernel: one warp per token row writes its three digit rows
-//    into token blocks of 32: block b holds rows d*32 + t (d = digit, t =
-//    token in block), 96 rows of K bytes, plus the row's dequantisation
-//    factor 2^(E-22).
-//  * int8_gemm_kernel: persistent; output tiles of 128 weight rows x one token
-//    block, taken row-tile-major with the token block fastest so the CTAs
-//    sharing a weight tile run together and the tile is read from HBM once.
-//    One thread streams the weight tile and the digit tile of every 128-byte
-//    K step with 2D TMA loads (128-byte swizzle, no multicast) into a 4-stage
-//    ring; one thread issues tcgen05.mma kind::i8 (M=128, N=96, K=32) into a
-//    double-buffered TMEM accumulator; four epilogue warps read it with
-//    tcgen05.ld (thread = output row) and write y (+bias), coalesced over rows.
+//  * digit_rows_kernel: one warp per row writes its three digit rows and its
+//    dequantisation factor 2^(E-22).  Row r of digit d goes to
+//    (r / B) * 3B + d * B + r % B: token blocks of B = 32 rows for
+//    activations, one block of B = N rows (three planes) for weights.
+//  * gemm_kernel<PLANES>: persistent; output tiles of 128 weight rows x one
+//    32-token block, taken row-tile-major with the token block fastest so the
+//    CTAs sharing a weight tile run together and it is read from HBM once.
+//    One thread streams, for every 128-byte K step (and weight plane), the
+//    weight tile and the digit tile with 2D TMA loads (128-byte swizzle, no
+//    multicast) into a 4-stage ring; one thread issues tcgen05.mma kind::i8
+//    (M=128, N=96, K=32) into a double-buffered TMEM accumulator (one per
+//    weight plane); four epilogue warps read it with tcgen05.ld (thread =
+//    output row), add the planes in 64-bit registers and write y (+bias),
+//    coalesced over rows.
 // Every wait is bounded; a timeout sets *err, stops the roles, drains the
 // copies and MMAs in flight and frees TMEM.
 #include <cuda.h>
@@ -47,15 +56,14 @@ constexpr uint32_t kGIdesc = umma_idesc_s8(128, kGRows);
 
 // ---------------------------------------------------------------- digits --
 __global__ void __launch_bounds__(256) digit_rows_kernel(int8_t *__restrict__ D, float *__restrict__ dq,
-                                                         const float *__restrict__ x, long x_stride, int T, int K,
-                                                         int T_pad) {
+                                                         const float *__restrict__ x, long x_stride, int rows, int K,
+                                                         int rows_pad, int B) {
   const int lane = threadIdx.x & 31;
   const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
-  if (t >= T_pad) return;
-  const int b = t / kGTok, tl = t % kGTok;
-  int8_t *row0 = D + ((size_t)b * kGRows + tl) * K;  // digit d at row0 + d*kGTok*K
-  const size_t dstep = (size_t)kGTok * K;
-  if (t >= T) {  // tokens past the end of the last block: zero digits
+  if (t >= rows_pad) return;
+  int8_t *row0 = D + ((size_t)(t / B) * 3 * B + t % B) * K;  // digit d at row0 + d*B*K
+  const size_t dstep = (size_t)B * K;
+  if (t >= rows) {  // rows past the end of the last block: zero digits
     for (int k = 4 * lane; k < K; k += 128)
       for (int d = 0; d < 3; ++d) *reinterpret_cast<uint32_t *>(row0 + d * dstep + k) = 0u;
     if (lane == 0) dq[t] = 0.0f;
@@ -95,10 +103,10 @@ __global__ void __launch_bounds__(256) digit_rows_kernel(int8_t *__restrict__ D,
 
 // ------------------------------------------------------------------ GEMM --
 struct GemmParams {
-  CUtensorMap tm_w;  // [N, K] int8, box 128 x 128, SW128
+  CUtensorMap tm_w;  // [PLANES*N, K] int8, box 128 x 128, SW128 (plane a at rows a*N..)
   CUtensorMap tm_d;  // [blocks*96, K] int8 digit rows, box 96 x 128, SW128
-  const float *dq;   // [blocks*32]
-  const float *scales, *bias;
+  const float *dq;   // [blocks*32] per token row
+  const float *scales, *bias;  // per weight row: INT8 scales, or the f32 weights' factors
   float *y;          // [T, N], row stride y_stride
   long y_stride;
   int T, K, N;
@@ -119,7 +127,8 @@ QASR_DEV void g_fail(GSmem &sm, int *err) {
   if (err) atomicExch(err, -QASR_ERR_TIMEOUT);
 }
 
-__global__ void __launch_bounds__(256, 1) int8_gemm_kernel(const __grid_constant__ GemmParams p) {
+template <int PLANES>
+__global__ void __launch_bounds__(256, 1) gemm_kernel(const __grid_constant__ GemmParams p) {
   extern __shared__ unsigned char smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   unsigned char *base = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
@@ -128,10 +137,12 @@ __global__ void __launch_bounds__(256, 1) int8_gemm_kernel(const __grid_constant
   GSmem &sm = *reinterpret_cast<GSmem *>(b_ring + (size_t)kGStages * kGBTile);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int KT = p.K / 128, NT = (p.N + 127) / 128, NB = (p.T + kGTok - 1) / kGTok;
+  const int KT = (p.K + 127) / 128, NT = (p.N + 127) / 128, NB = (p.T + kGTok - 1) / kGTok;
   const int tiles = NT * NB;
   const int my_tiles = (int)blockIdx.x < tiles ? (tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-  const int nu = my_tiles * KT;  // pipeline items (tile j, K step kt)
+  // pipeline items: (output tile j, weight plane a, K step kt); one accumulator per (j, a) "piece"
+  const int per_tile = PLANES * KT;
+  const int nu = my_tiles * per_tile;
   auto tile_of = [&](int j) { return (int)blockIdx.x + j * (int)gridDim.x; };
 
   if (threadIdx.x == 0) {
@@ -157,10 +168,10 @@ __global__ void __launch_bounds__(256, 1) int8_gemm_kernel(const __grid_constant
 
   int produced = 0;
   auto produce = [&](int i) {
-    const int st = i % kGStages, tile = tile_of(i / KT), kt = i % KT;
+    const int st = i % kGStages, tile = tile_of(i / per_tile), a = (i / KT) % PLANES, kt = i % KT;
     const int rt = tile / NB, tb = tile % NB;
     mbar_arrive_expect_tx(&sm.full[st], kGATile + kGBTile);
-    tma_load_2d_u8(a_ring + (size_t)st * kGATile, &p.tm_w, kt * 128, rt * 128, &sm.full[st]);
+    tma_load_2d_u8(a_ring + (size_t)st * kGATile, &p.tm_w, kt * 128, a * p.N + rt * 128, &sm.full[st]);
     tma_load_2d_u8(b_ring + (size_t)st * kGBTile, &p.tm_d, kt * 128, tb * kGRows, &sm.full[st]);
   };
   const bool producer = warp == 4 && lane == 0;
@@ -177,8 +188,8 @@ __global__ void __launch_bounds__(256, 1) int8_gemm_kernel(const __grid_constant
   } else if (warp == 5) {
     if (lane == 0) {
       for (int i = 0; i < nu; ++i) {
-        const int j = i / KT, kt = i % KT, st = i % kGStages, buf = j & 1;
-        if (kt == 0 && j >= 2 && !mbar_wait(&sm.accempty[buf], (unsigned)(((j >> 1) - 1) & 1))) {
+        const int piece = i / KT, kt = i % KT, st = i % kGStages, buf = piece & 1;
+        if (kt == 0 && piece >= 2 && !mbar_wait(&sm.accempty[buf], (unsigned)(((piece >> 1) - 1) & 1))) {
           g_fail(sm, p.err);
           break;
         }
@@ -203,10 +214,13 @@ __global__ void __launch_bounds__(256, 1) int8_gemm_kernel(const __grid_constant
     }
   } else if (warp < 4) {
     const int ri = warp * 32 + lane;
-    for (int j = 0; j < my_tiles; ++j) {
-      const int tile = tile_of(j), buf = j & 1;
-      const int rt = tile / NB, tb = tile % NB;
-      if (!g_aborted(sm) && !mbar_wait(&sm.accfull[buf], (unsigned)((j >> 1) & 1))) g_fail(sm, p.err);
+    long long V[kGTok];
+#pragma unroll
+    for (int t = 0; t < kGTok; ++t) V[t] = 0;
+    for (int piece = 0; piece < my_tiles * PLANES; ++piece) {
+      const int j = piece / PLANES, a = piece % PLANES, buf = piece & 1;
+      const int tile = tile_of(j), rt = tile / NB, tb = tile % NB;
+      if (!g_aborted(sm) && !mbar_wait(&sm.accfull[buf], (unsigned)((piece >> 1) & 1))) g_fail(sm, p.err);
       named_bar(1, 128);  // the four epilogue warps decide together
       if (g_aborted(sm)) break;
       tc_fence_after();
@@ -218,6 +232,12 @@ __global__ void __launch_bounds__(256, 1) int8_gemm_kernel(const __grid_constant
       tc_fence_before();
       __syncwarp();
       if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&sm.accempty[buf])) : "memory");
+      // plane a carries weight digit a: weight 2^(8*(PLANES-1-a)) within the plane sum
+      const int wshift = 8 * (PLANES - 1 - a);
+#pragma unroll
+      for (int tl = 0; tl < kGTok; ++tl)
+        V[tl] += (((long long)(int)a0[tl] << 16) + ((long long)(int)a1[tl] << 8) + (long long)(int)a2[tl]) << wshift;
+      if (a != PLANES - 1) continue;
       const int row = rt * 128 + ri;
       if (row < p.N) {
         const float sc = p.scales[row];
@@ -227,13 +247,14 @@ __global__ void __launch_bounds__(256, 1) int8_gemm_kernel(const __grid_constant
         for (int tl = 0; tl < kGTok; ++tl) {
           const int t = t0 + tl;
           if (t < p.T) {
-            const long long V = ((long long)(int)a0[tl] << 16) + ((long long)(int)a1[tl] << 8) + (long long)(int)a2[tl];
-            float v = __fmul_rn(__fmul_rn(__ll2float_rn(V), __ldg(p.dq + t)), sc);
+            float v = __fmul_rn(__fmul_rn(__ll2float_rn(V[tl]), __ldg(p.dq + t)), sc);
             if (p.bias) v = __fadd_rn(v, b);
             p.y[(size_t)t * p.y_stride + row] = v;
           }
         }
       }
+#pragma unroll
+      for (int t = 0; t < kGTok; ++t) V[t] = 0;
     }
   }
   __syncthreads();
@@ -262,44 +283,74 @@ static int gemm_sms() {
   return sms[dev];
 }
 
-static int digit_map(CUtensorMap *tm, const int8_t *D, int rows, int K) {
+// 2D map over an int8 [rows, K] matrix, box `box_rows` x 128 bytes, 128-byte swizzle.
+static int int8_map(CUtensorMap *tm, const int8_t *base, long rows, int K, int box_rows) {
   using Encode = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                               const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
                               CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
   auto encode = reinterpret_cast<Encode>(tensor_map_encoder());
   if (!encode) {
-    set_error("int8 tensor-core GEMM: cuTensorMapEncodeTiled unavailable");
+    set_error("tensor-core GEMM: cuTensorMapEncodeTiled unavailable");
     return QASR_ERR_CUDA;
   }
   const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)K};
-  const cuuint32_t box[2] = {128, (cuuint32_t)kGRows};
+  const cuuint32_t box[2] = {128, (cuuint32_t)box_rows};
   const cuuint32_t estr[2] = {1, 1};
-  CUresult r = encode(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t *>(D), dims, strides, box, estr,
+  CUresult r = encode(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t *>(base), dims, strides, box, estr,
                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
-    set_error("int8 tensor-core GEMM: cuTensorMapEncodeTiled failed (%d)", (int)r);
+    set_error("tensor-core GEMM: cuTensorMapEncodeTiled failed (%d)", (int)r);
     return QASR_ERR_CUDA;
   }
   return QASR_OK;
 }
 
-// y[t, o] = scales[o] * sum_k w[o, k] * x[t, k] (+ bias[o]) for T token rows.
-// QASR_ERR_UNSUPPORTED (nothing launched) for shapes it does not cover.
+static int digit_rows(int8_t *D, float *dq, const float *x, long x_stride, int rows, int rows_pad, int K, int B,
+                      cudaStream_t st) {
+  digit_rows_kernel<<<(rows_pad + 7) / 8, 256, 0, st>>>(D, dq, x, x_stride, rows, K, rows_pad, B);
+  return launch_status("tensor-core GEMM: digit rows");
+}
+
+template <int PLANES>
+static int gemm_launch(GemmParams &p, cudaStream_t st) {
+  static int attr_mask = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const size_t smem = 1024 + (size_t)kGStages * (kGATile + kGBTile) + sizeof(GSmem);
+  if (dev < 31 && !(attr_mask & (1 << dev))) {
+    int rc = cuda_status(cudaFuncSetAttribute(gemm_kernel<PLANES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              (int)smem),
+                         "tensor-core GEMM: shared memory opt-in");
+    if (rc) return rc;
+    attr_mask |= 1 << dev;
+  }
+  const long tiles = (long)((p.N + 127) / 128) * ((p.T + kGTok - 1) / kGTok);
+  const int grid = (int)std::min<long>(gemm_sms(), tiles);
+  gemm_kernel<PLANES><<<grid, 256, smem, st>>>(p);
+  return launch_status("tensor-core GEMM");
+}
+
+// Shapes the tensor-core GEMMs take: K a multiple of 16 (TMA row pitch) and
+// at least one 128-byte tile, at least one 128-row weight tile, 16-byte
+// aligned rows.
+static bool gemm_shape_ok(const float *x, long x_stride, int T, int K, int N) {
+  return T > 0 && K >= 128 && K % 16 == 0 && N >= 128 && !(reinterpret_cast<uintptr_t>(x) & 15) && !(x_stride & 3) &&
+         (long)((N + 127) / 128) * ((T + kGTok - 1) / kGTok) < (1l << 30);
+}
+
 int int8_gemm(float *y, long y_stride, const float *x, long x_stride, const int8_t *w, const float *scales,
               const float *bias, int T, int K, int N, cudaStream_t st) {
-  if (T <= 0 || K <= 0 || K % 128 || N <= 0 || (reinterpret_cast<uintptr_t>(x) & 15) || (x_stride & 3) ||
-      (reinterpret_cast<uintptr_t>(w) & 15))
-    return QASR_ERR_UNSUPPORTED;
+  if (!gemm_shape_ok(x, x_stride, T, K, N) || (reinterpret_cast<uintptr_t>(w) & 15)) return QASR_ERR_UNSUPPORTED;
   const int NB = (T + kGTok - 1) / kGTok, T_pad = NB * kGTok;
   void *dbuf = nullptr, *qbuf = nullptr;
   int rc;
   if ((rc = dev_scratch(kScratchDigits, (size_t)NB * kGRows * K, &dbuf))) return rc;
   if ((rc = dev_scratch(kScratchDigitScale, (size_t)T_pad * 4, &qbuf))) return rc;
   GemmParams p{};
-  if ((rc = umma_weight_map(&p.tm_w, w, N, K))) return rc;
-  if ((rc = digit_map(&p.tm_d, static_cast<int8_t *>(dbuf), NB * kGRows, K))) return rc;
+  if ((rc = int8_map(&p.tm_w, w, N, K, 128))) return rc;
+  if ((rc = int8_map(&p.tm_d, static_cast<int8_t *>(dbuf), (long)NB * kGRows, K, kGRows))) return rc;
   p.dq = static_cast<float *>(qbuf);
   p.scales = scales;
   p.bias = bias;
@@ -308,23 +359,102 @@ int int8_gemm(float *y, long y_stride, const float *x, long x_stride, const int8
   p.T = T;
   p.K = K;
   p.N = N;
-  digit_rows_kernel<<<(T_pad + 7) / 8, 256, 0, st>>>(static_cast<int8_t *>(dbuf), static_cast<float *>(qbuf), x,
-                                                      x_stride, T, K, T_pad);
-  if ((rc = launch_status("int8 tensor-core GEMM: digit rows"))) return rc;
-  static int attr_mask = 0;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const size_t smem = 1024 + (size_t)kGStages * (kGATile + kGBTile) + sizeof(GSmem);
-  if (dev < 31 && !(attr_mask & (1 << dev))) {
-    if ((rc = cuda_status(cudaFuncSetAttribute(int8_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-                          "int8 tensor-core GEMM: shared memory opt-in")))
-      return rc;
-    attr_mask |= 1 << dev;
+  if ((rc = digit_rows(static_cast<int8_t *>(dbuf), static_cast<float *>(qbuf), x, x_stride, T, T_pad, K, kGTok, st)))
+    return rc;
+  return gemm_launch<1>(p, st);
+}
+
+int f32_gemm(float *y, long y_stride, const float *x, long x_stride, const float *w, const float *bias, int T, int K,
+             int N, cudaStream_t st) {
+  if (!gemm_shape_ok(x, x_stride, T, K, N) || (reinterpret_cast<uintptr_t>(w) & 15)) return QASR_ERR_UNSUPPORTED;
+  const int NB = (T + kGTok - 1) / kGTok, T_pad = NB * kGTok;
+  void *dbuf = nullptr, *qbuf = nullptr, *wbuf = nullptr, *wq = nullptr;
+  int rc;
+  if ((rc = dev_scratch(kScratchDigits, (size_t)NB * kGRows * K, &dbuf))) return rc;
+  if ((rc = dev_scratch(kScratchDigitScale, (size_t)T_pad * 4, &qbuf))) return rc;
+  if ((rc = dev_scratch(kScratchWeightDigits, (size_t)3 * N * K, &wbuf))) return rc;
+  if ((rc = dev_scratch(kScratchWeightScale, (size_t)N * 4, &wq))) return rc;
+  GemmParams p{};
+  if ((rc = int8_map(&p.tm_w, static_cast<int8_t *>(wbuf), 3l * N, K, 128))) return rc;
+  if ((rc = int8_map(&p.tm_d, static_cast<int8_t *>(dbuf), (long)NB * kGRows, K, kGRows))) return rc;
+  p.dq = static_cast<float *>(qbuf);
+  p.scales = static_cast<float *>(wq);
+  p.bias = bias;
+  p.y = y;
+  p.y_stride = y_stride;
+  p.T = T;
+  p.K = K;
+  p.N = N;
+  // weight digit planes: rows of plane a at a*N (one block of N rows)
+  if ((rc = digit_rows(static_cast<int8_t *>(wbuf), static_cast<float *>(wq), w, K, N, N, K, N, st))) return rc;
+  if ((rc = digit_rows(static_cast<int8_t *>(dbuf), static_cast<float *>(qbuf), x, x_stride, T, T_pad, K, kGTok, st)))
+    return rc;
+  return gemm_launch<3>(p, st);
+}
+
+// ------------------------------------------------- CUDA-core fallback SGEMM --
+// y[t, o] = sum_k x[t, k] w[o, k] (+ b[o]) for shapes the tensor-core GEMM
+// does not take (K not a multiple of 16, unaligned rows): 32x32 output tiles,
+// K staged through shared memory, f32 accumulation in k order.
+__global__ void __launch_bounds__(256) sgemm_nt_kernel(float *__restrict__ y, const float *__restrict__ x,
+                                                       const float *__restrict__ w, const float *__restrict__ b,
+                                                       int T, int K, int N) {
+  __shared__ float xs[32][33], ws[32][33];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 8 rows of 4 outputs per thread
+  const int t0 = blockIdx.y * 32, o0 = blockIdx.x * 32;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int k0 = 0; k0 < K; k0 += 32) {
+    for (int i = ty; i < 32; i += 8) {
+      xs[i][tx] = (t0 + i < T && k0 + tx < K) ? x[(size_t)(t0 + i) * K + k0 + tx] : 0.0f;
+      ws[i][tx] = (o0 + i < N && k0 + tx < K) ? w[(size_t)(o0 + i) * K + k0 + tx] : 0.0f;
+    }
+    __syncthreads();
+    for (int kk = 0; kk < 32; ++kk)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) acc[r] = fmaf(xs[ty + 8 * r][kk], ws[tx][kk], acc[r]);
+    __syncthreads();
   }
-  const long tiles = (long)((N + 127) / 128) * NB;
-  const int grid = (int)std::min<long>(gemm_sms(), tiles);
-  int8_gemm_kernel<<<grid, 256, smem, st>>>(p);
-  return launch_status("int8 tensor-core GEMM");
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int t = t0 + ty + 8 * r, o = o0 + tx;
+    if (t < T && o < N) y[(size_t)t * N + o] = b ? __fadd_rn(acc[r], b[o]) : acc[r];
+  }
+}
+
+int f32_gemm_fallback(float *y, const float *x, const float *w, const float *bias, int T, int K, int N,
+                      cudaStream_t st) {
+  dim3 grid((N + 31) / 32, (T + 31) / 32);
+  sgemm_nt_kernel<<<grid, 256, 0, st>>>(y, x, w, bias, T, K, N);
+  return launch_status("f32 GEMM (CUDA cores)");
 }
 
 }  // namespace qasr
+
+using namespace qasr;
+
+static int linear_f32_impl(const char *fn, float *y, const float *x, const float *w, const float *b, int seq,
+                           int in_dim, int out_dim, void *stream) {
+  if (!y || !x || !w || seq < 0 || in_dim <= 0 || out_dim <= 0) {
+    set_error("%s: invalid arguments", fn);
+    return QASR_ERR_INVALID;
+  }
+  if (seq == 0) return QASR_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  int rc = f32_gemm(y, out_dim, x, in_dim, w, b, seq, in_dim, out_dim, st);
+  if (rc != QASR_ERR_UNSUPPORTED) return rc;
+  return f32_gemm_fallback(y, x, w, b, seq, in_dim, out_dim, st);
+}
+
+extern "C" int qasr_linear(float *y, const float *x, const float *w, const float *b, int seq, int in_dim,
+                           int out_dim, void *stream) {
+  return linear_f32_impl("qasr_linear", y, x, w, b, seq, in_dim, out_dim, stream);
+}
+
+extern "C" int qasr_linear_nobias(float *y, const float *x, const float *w, int seq, int in_dim, int out_dim,
+                                  void *stream) {
+  return linear_f32_impl("qasr_linear_nobias", y, x, w, nullptr, seq, in_dim, out_dim, stream);
+}
+
+extern "C" int qasr_matmul_t(float *c, const float *a, const float *b, int m, int k, int n, void *stream) {
+  return linear_f32_impl("qasr_matmul_t", c, a, b, nullptr, m, k, n, stream);
+}

@@ -138,6 +138,24 @@ def linear_int8(y, x, w_int8, scales, bias, seq_len, in_dim, out_dim):
               _ptr(bias, f32, "bias", out_dim), seq_len, in_dim, out_dim, _stream())
 
 
+def linear(y, x, w, b, seq_len, in_dim, out_dim):
+    """kernels::linear (mod.rs:531): y = x @ w^T + b, f32 weights; b may be None."""
+    _lib.call("qasr_linear", _ptr(y, f32, "y", seq_len * out_dim), _ptr(x, f32, "x", seq_len * in_dim),
+              _ptr(w, f32, "w", out_dim * in_dim), _ptr(b, f32, "b", out_dim), seq_len, in_dim, out_dim, _stream())
+
+
+def linear_nobias(y, x, w, seq_len, in_dim, out_dim):
+    """kernels::linear_nobias (mod.rs:567)."""
+    _lib.call("qasr_linear_nobias", _ptr(y, f32, "y", seq_len * out_dim), _ptr(x, f32, "x", seq_len * in_dim),
+              _ptr(w, f32, "w", out_dim * in_dim), seq_len, in_dim, out_dim, _stream())
+
+
+def matmul_t(c, a, b, m, k, n):
+    """kernels::matmul_t (mod.rs:503): c = a @ b^T."""
+    _lib.call("qasr_matmul_t", _ptr(c, f32, "c", m * n), _ptr(a, f32, "a", m * k), _ptr(b, f32, "b", n * k), m, k, n,
+              _stream())
+
+
 def causal_attention(out, q, k, v, seq_q, seq_k, n_heads, n_kv_heads, head_dim, scale, q_offset):
     """kernels::causal_attention (mod.rs:1174)."""
     _lib.call("qasr_causal_attention", _ptr(out, f32, "out", seq_q * n_heads * head_dim),

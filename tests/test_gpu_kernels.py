@@ -323,6 +323,41 @@ def test_int8_gemm_prefill_shapes(orc, seq, out_dim, in_dim, bias):
     assert ok and err < 5e-5, err
 
 
+@pytest.mark.parametrize("seq,out_dim,in_dim,bias", [
+    (1, 896, 896, True),        # one row
+    (390, 3584, 896, True),     # encoder fc1 over a window of tokens
+    (390, 896, 3584, True),     # encoder fc2
+    (13, 896, 7680, False),     # conv_out-like K
+    (70, 200, 1008, True),      # K not a multiple of 128 (tail tile zero-filled), N < 256
+    (5, 50, 100, True),         # K % 16 != 0: CUDA-core fallback
+    (3, 64, 64, False),         # below one tile: CUDA-core fallback
+])
+def test_linear_f32(orc, seq, out_dim, in_dim, bias):
+    """kernels::linear (mod.rs:531, cblas_sgemm in the reference) against an
+    fp64-accumulated oracle; both operands become exact int8 digit planes."""
+    rng = np.random.default_rng(seq * 3 + out_dim + in_dim)
+    w = (rng.standard_normal((out_dim, in_dim)) * rng.uniform(0.001, 0.2, (out_dim, 1))).astype(np.float32)
+    x = (rng.standard_normal((seq, in_dim)) * rng.uniform(0.01, 5.0, (seq, 1))).astype(np.float32)
+    b = (rng.standard_normal(out_dim) * 0.1).astype(np.float32) if bias else None
+    y = torch.empty(seq, out_dim, device=DEV)
+    if bias:
+        K.linear(y, T(x), T(w), T(b), seq, in_dim, out_dim)
+    else:
+        K.linear_nobias(y, T(x), T(w), seq, in_dim, out_dim)
+    ok, err = rel_close(H(y), orc.linear(x, w, b), 1e-5)
+    assert ok, err
+
+
+def test_matmul_t(orc):
+    rng = np.random.default_rng(3)
+    a = rng.standard_normal((17, 256)).astype(np.float32)
+    b = rng.standard_normal((130, 256)).astype(np.float32)
+    c = torch.empty(17, 130, device=DEV)
+    K.matmul_t(c, T(a), T(b), 17, 256, 130)
+    ok, err = rel_close(H(c), a.astype(np.float64) @ b.astype(np.float64).T, 1e-5)
+    assert ok, err
+
+
 @pytest.mark.parametrize("M", [1, 5, 8])
 def test_matvec_residual_and_gateup_swiglu(orc, M):
     rng = np.random.default_rng(M)
