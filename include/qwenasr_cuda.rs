@@ -1,0 +1,93 @@
+// qwenasr_cuda.rs -- Rust declarations of the C ABI in qwenasr_cuda.h, for a
+// crate of the reference (crates/qwen-asr) that links libqwenasr_b200.so.
+// No Rust toolchain exists where this library is built, so this file is not
+// compiled here; tests/test_abi.py checks that it declares every function of
+// the header with the same number of arguments.
+#![allow(non_camel_case_types, dead_code)]
+use std::os::raw::{c_char, c_int, c_void};
+
+pub const QASR_OK: c_int = 0;
+pub const QASR_ERR_INVALID: c_int = -1;
+pub const QASR_ERR_CUDA: c_int = -2;
+pub const QASR_ERR_ALLOC: c_int = -3;
+pub const QASR_ERR_UNSUPPORTED: c_int = -4;
+pub const QASR_ERR_TIMEOUT: c_int = -5;
+
+#[repr(C)]
+pub struct QasrDecoder {
+    _private: [u8; 0],
+}
+
+#[repr(C)]
+#[derive(Clone, Copy)]
+pub struct QasrDecoderConfig {
+    pub hidden: c_int,
+    pub inter: c_int,
+    pub n_layers: c_int,
+    pub n_heads: c_int,
+    pub n_kv_heads: c_int,
+    pub head_dim: c_int,
+    pub vocab: c_int,
+    pub eps: f32,
+    pub theta: f32,
+    pub max_batch: c_int,
+    pub max_seq: c_int,
+    pub embed_is_int8: c_int,
+}
+
+#[repr(C)]
+#[derive(Clone, Copy)]
+pub struct QasrDecLayerWeights {
+    pub wq: *const i8, pub wq_s: *const f32, pub wk: *const i8, pub wk_s: *const f32,
+    pub wv: *const i8, pub wv_s: *const f32, pub wo: *const i8, pub wo_s: *const f32,
+    pub gate_up: *const i8, pub gate_up_s: *const f32, pub down: *const i8, pub down_s: *const f32,
+    pub q_norm: *const f32, pub k_norm: *const f32, pub input_norm: *const f32, pub post_attn_norm: *const f32,
+}
+
+#[link(name = "qwenasr_b200")]
+extern "C" {
+    pub fn qasr_last_error() -> *const c_char;
+    pub fn qasr_version() -> *const c_char;
+    pub fn qasr_rms_norm(out: *mut f32, x: *const f32, w: *const f32, seq: c_int, hidden: c_int, eps: f32, stream: *mut c_void) -> c_int;
+    pub fn qasr_rms_norm_per_head(x: *mut f32, w: *const f32, seq: c_int, n_heads: c_int, head_dim: c_int, eps: f32, stream: *mut c_void) -> c_int;
+    pub fn qasr_layer_norm(out: *mut f32, x: *const f32, w: *const f32, b: *const f32, seq: c_int, hidden: c_int, eps: f32, stream: *mut c_void) -> c_int;
+    pub fn qasr_compute_rope_neox(cos_out: *mut f32, sin_out: *mut f32, positions: *const i32, seq: c_int, head_dim: c_int, theta: f32, stream: *mut c_void) -> c_int;
+    pub fn qasr_rope_cache_table(cos_out: *mut f32, sin_out: *mut f32, n_pos: c_int, head_dim: c_int, theta: f32, stream: *mut c_void) -> c_int;
+    pub fn qasr_apply_rope_neox(x: *mut f32, cos_v: *const f32, sin_v: *const f32, seq: c_int, n_heads: c_int, head_dim: c_int, stream: *mut c_void) -> c_int;
+    pub fn qasr_kv_append(k_cache: *mut f32, v_cache: *mut f32, k_new: *const f32, v_new: *const f32, layer: c_int, max_seq: c_int, kv_dim: c_int, start_pos: c_int, seq: c_int, stream: *mut c_void) -> c_int;
+    pub fn qasr_sinusoidal_pe(pe: *mut f32, n_pos: c_int, d_model: c_int, stream: *mut c_void) -> c_int;
+    pub fn qasr_gelu(x: *mut f32, n: i64, stream: *mut c_void) -> c_int;
+    pub fn qasr_gelu_erf(x: *mut f32, n: i64, stream: *mut c_void) -> c_int;
+    pub fn qasr_silu(x: *mut f32, n: i64, stream: *mut c_void) -> c_int;
+    pub fn qasr_swiglu_multiply(out: *mut f32, gate_up: *const f32, seq: c_int, inter: c_int, stream: *mut c_void) -> c_int;
+    pub fn qasr_add_inplace(a: *mut f32, b: *const f32, n: i64, stream: *mut c_void) -> c_int;
+    pub fn qasr_linear_nobias_int8(y: *mut f32, x: *const f32, w: *const i8, scales: *const f32, seq: c_int, in_dim: c_int, out_dim: c_int, stream: *mut c_void) -> c_int;
+    pub fn qasr_linear_int8(y: *mut f32, x: *const f32, w: *const i8, scales: *const f32, bias: *const f32, seq: c_int, in_dim: c_int, out_dim: c_int, stream: *mut c_void) -> c_int;
+    pub fn qasr_linear(y: *mut f32, x: *const f32, w: *const f32, b: *const f32, seq: c_int, in_dim: c_int, out_dim: c_int, stream: *mut c_void) -> c_int;
+    pub fn qasr_linear_nobias(y: *mut f32, x: *const f32, w: *const f32, seq: c_int, in_dim: c_int, out_dim: c_int, stream: *mut c_void) -> c_int;
+    pub fn qasr_matmul_t(c: *mut f32, a: *const f32, b: *const f32, m: c_int, k: c_int, n: c_int, stream: *mut c_void) -> c_int;
+    pub fn qasr_causal_attention(out: *mut f32, q: *const f32, k: *const f32, v: *const f32, seq_q: c_int, seq_k: c_int, n_heads: c_int, n_kv_heads: c_int, head_dim: c_int, scale: f32, q_offset: c_int, stream: *mut c_void) -> c_int;
+    pub fn qasr_quantize_f32_to_int8(data: *const f32, out_dim: i64, in_dim: i64, q: *mut i8, scales: *mut f32, stream: *mut c_void) -> c_int;
+    pub fn qasr_embed_gather_f32(dst: *mut f32, table: *const f32, ids: *const i32, n: c_int, dim: c_int, vocab: i64, bad_id_flag: *mut c_int, stream: *mut c_void) -> c_int;
+    pub fn qasr_embed_gather_int8(dst: *mut f32, table: *const i8, scales: *const f32, ids: *const i32, n: c_int, dim: c_int, vocab: i64, bad_id_flag: *mut c_int, stream: *mut c_void) -> c_int;
+    pub fn qasr_pre_attn_block(x_norm: *mut f32, x: *const f32, w_in: *const f32, seq: c_int, hidden: c_int, q: *mut f32, k: *const f32, v: *const f32, k_out: *mut f32, q_norm_w: *const f32, k_norm_w: *const f32, n_heads: c_int, n_kv_heads: c_int, head_dim: c_int, eps: f32, cos_tab: *const f32, sin_tab: *const f32, start_pos: c_int, k_cache: *mut f32, v_cache: *mut f32, layer: c_int, max_seq: c_int, stream: *mut c_void) -> c_int;
+    pub fn qasr_ln_pe(out: *mut f32, x: *const f32, w: *const f32, b: *const f32, pe: *const f32, rows: c_int, hidden: c_int, n_pos: c_int, eps: f32, stream: *mut c_void) -> c_int;
+    pub fn qasr_int8_norm_gateup_swiglu(h: *mut f32, x: *const f32, norm_w: *const f32, w_gate_up: *const i8, scales: *const f32, M: c_int, hidden: c_int, inter: c_int, eps: f32, stream: *mut c_void) -> c_int;
+    pub fn qasr_int8_matvec_residual(x: *mut f32, a: *const f32, w: *const i8, scales: *const f32, M: c_int, in_dim: c_int, out_dim: c_int, stream: *mut c_void) -> c_int;
+    pub fn qasr_final_norm_lmhead_argmax(ids_out: *mut i32, logits_out: *mut f32, x: *const f32, norm_w: *const f32, w: *const i8, scales: *const f32, M: c_int, hidden: c_int, vocab: c_int, eps: f32, stream: *mut c_void) -> c_int;
+    pub fn qasr_final_norm_lmhead_argmax_noalloc(ids_out: *mut i32, logits_out: *mut f32, x: *const f32, norm_w: *const f32, w: *const i8, scales: *const f32, M: c_int, hidden: c_int, vocab: c_int, eps: f32, stream: *mut c_void) -> c_int;
+    pub fn qasr_decoder_create(cfg: *const QasrDecoderConfig, device: c_int) -> *mut QasrDecoder;
+    pub fn qasr_decoder_free(dec: *mut QasrDecoder);
+    pub fn qasr_decoder_set_layer(dec: *mut QasrDecoder, layer: c_int, w: *const QasrDecLayerWeights) -> c_int;
+    pub fn qasr_decoder_set_globals(dec: *mut QasrDecoder, embed: *const c_void, embed_scales: *const f32, norm: *const f32, lm_head: *const i8, lm_head_s: *const f32) -> c_int;
+    pub fn qasr_decoder_kv(dec: *mut QasrDecoder, slot: c_int, k_cache: *mut *mut f32, v_cache: *mut *mut f32) -> c_int;
+    pub fn qasr_decoder_step(dec: *mut QasrDecoder, tokens: *const i32, positions: *const i32, M: c_int, next_tokens: *mut i32) -> c_int;
+    pub fn qasr_decoder_prefill(dec: *mut QasrDecoder, slot: c_int, embeds: *const f32, seq: c_int, start_pos: c_int) -> c_int;
+    pub fn qasr_decoder_prefill_hidden(dec: *mut QasrDecoder) -> *const f32;
+    pub fn qasr_decoder_step_device(dec: *mut QasrDecoder, tokens: *const i32, positions: *const i32, M: c_int, next_tokens: *mut i32) -> c_int;
+    pub fn qasr_decoder_stream(dec: *mut QasrDecoder) -> *mut c_void;
+    pub fn qasr_decoder_keep_logits(dec: *mut QasrDecoder, enable: c_int) -> c_int;
+    pub fn qasr_decoder_logits(dec: *mut QasrDecoder) -> *const f32;
+    pub fn qasr_decoder_profile_step(dec: *mut QasrDecoder, tokens: *const i32, positions: *const i32, M: c_int, class_ms: *mut f32, class_launches: *mut c_int, n_classes: c_int) -> c_int;
+    pub fn qasr_decoder_step_bytes(dec: *const QasrDecoder, positions: *const i32, M: c_int) -> i64;
+}

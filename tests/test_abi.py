@@ -79,3 +79,23 @@ def test_missing_library_fails_loudly(tmp_path):
             _lib.load(str(tmp_path / "nope.so"))
         finally:
             _lib._lib = saved
+
+
+def _header_arg_counts():
+    import re
+    txt = re.sub(r"/\*.*?\*/", "", open(_lib.HEADER).read(), flags=re.S)
+    out = {}
+    for name, args in re.findall(r"\b(qasr_\w+)\s*\(([^;]*?)\);", txt, flags=re.S):
+        a = [x for x in " ".join(args.split()).split(",") if x.strip() and x.strip() != "void"]
+        out[name] = len(a)
+    return out
+
+
+def test_rust_binding_matches_header():
+    """include/qwenasr_cuda.rs (the untested Rust extern block for the
+    reference crate) declares every header function with the same arity."""
+    import os
+    import re
+    rs = open(os.path.join(os.path.dirname(_lib.HEADER), "qwenasr_cuda.rs")).read()
+    decl = {n: len([x for x in a.split(",") if x.strip()]) for n, a in re.findall(r"pub fn (qasr_\w+)\((.*?)\)", rs)}
+    assert decl == _header_arg_counts()
