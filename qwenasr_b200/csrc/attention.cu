@@ -67,21 +67,26 @@ causal_attention_kernel(float *__restrict__ out, const float *__restrict__ q, co
 // ------------------------------------------------------------------- decode
 // Persistent flash-decoding.  The keys of all (sequence, kv head) pairs are
 // laid end to end and cut into equal ranges, one per CTA, so every SM streams
-// the same number of K/V bytes whatever the batch and lengths.  A CTA walks
-// its range as segments (one per pair it touches); each segment is split
-// evenly over the 8 warps, and every warp streams its keys through its own
-// 3-stage ring of 8-key K and V tiles with 2D TMA loads (box: 8 rows x one
-// 128-float head slice; no multicast), so warps never wait for each other
-// inside a segment.  A warp scores its keys for both query heads of the GQA
-// group (each K/V byte is read from HBM once and used twice), keeps an
-// online-softmax state per head, and the CTA merges its warps at the end of
-// the segment.  A pair split over several CTAs is merged by the last one to
-// finish (counter + threadfence, slots in CTA order: deterministic).
+// the same number of K/V bytes whatever the batch and lengths.  The pairs a
+// CTA touches ("segments", usually one or two) share its 8 warps in
+// proportion to their key counts, so they stream at the same time; each warp
+// streams its contiguous key range of one segment through its own 2-stage
+// ring of 8-key K and V tiles (2D TMA, box 8 rows x one 128-float head slice,
+// no multicast), scores its keys for both query heads of the GQA group (each
+// K/V byte is read from HBM once and used twice) and keeps an online-softmax
+// state.  The CTA then merges the warps of each segment; a pair split over
+// several CTAs is merged by the last one to finish (counter + threadfence,
+// partials in CTA order: deterministic).  History tiles are fetched before
+// griddepcontrol.wait; only a tile holding the pair's newest row (appended by
+// the previous kernel) waits for it.  More than 8 segments (very short
+// pairs) are taken 8 at a time.
 struct AttnSmall {
   uint64_t bar[kAttnWarps][kAttnStages];
   int nseg;
   int seg_pair[128], seg_a[128], seg_b[128];
   long long off[129];  // prefix sums of the pair lengths (off[n_pairs] = total keys)
+  int wseg[kAttnWarps], wa[kAttnWarps], wb[kAttnWarps];  // per group: warp -> segment, key range
+  int last[kAttnWarps];
 };
 
 QASR_DEV void tma_load_2d(float *dst, const CUtensorMap *tm, int x, int y, uint64_t *bar) {
@@ -97,13 +102,12 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
 attn_decode_kernel(const __grid_constant__ AttnDecodeParams p) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   constexpr int TILE_F = kAttnTile * 128;  // floats per K (or V) tile
-  constexpr int KPW = kAttnTile;           // keys per tile (per warp)
+  constexpr int KPW = kAttnTile;           // keys per tile
+  constexpr int W = kAttnWarps;
   float *tiles = reinterpret_cast<float *>(smem_raw);
-  AttnSmall &sm = *reinterpret_cast<AttnSmall *>(smem_raw + (size_t)kAttnWarps * kAttnStages * 2 * TILE_F * 4);
-  __shared__ float sp[kAttnWarps][G][KPW];
-  __shared__ float wm[kAttnWarps][G], wl[kAttnWarps][G];
-  __shared__ float4 wo[kAttnWarps][G][32];
-  __shared__ int s_last;
+  float *slots = tiles + (size_t)W * kAttnStages * 2 * TILE_F;  // [warp][G][kAttnPartStride]
+  AttnSmall &sm = *reinterpret_cast<AttnSmall *>(slots + (size_t)W * G * kAttnPartStride);
+  __shared__ float sp[W][G][KPW];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_kv = p.n_kv_heads, n_pairs = p.M * n_kv;
@@ -150,55 +154,73 @@ attn_decode_kernel(const __grid_constant__ AttnDecodeParams p) {
   mbar_fence_init();
   __syncthreads();
   const int nseg = sm.nseg;
-
-  // this warp's key sub-range of segment sg
-  auto wrange = [&](int sg, int &wa, int &wb) {
-    const int a = sm.seg_a[sg], n = sm.seg_b[sg] - a;
-    wa = a + (int)((long)n * warp / kAttnWarps);
-    wb = a + (int)((long)n * (warp + 1) / kAttnWarps);
-  };
-  int T = 0;  // pipeline items (tiles) of this warp
-  for (int sg = 0; sg < nseg; ++sg) {
-    int wa, wb;
-    wrange(sg, wa, wb);
-    T += (wb - wa + KPW - 1) / KPW;
-  }
   float *mytiles = tiles + (size_t)warp * kAttnStages * 2 * TILE_F;
-  int ps = 0, pt = 0;  // producer cursor (lane 0): segment, tile within the warp's sub-range
-  auto issue_next = [&](int item) {
-    int wa, wb;
-    wrange(ps, wa, wb);
-    while (pt * KPW >= wb - wa) {
-      pt = 0;
-      ++ps;
-      wrange(ps, wa, wb);
-    }
-    const int pr = sm.seg_pair[ps], m = pr / n_kv, kvh = pr % n_kv;
-    const int row = (m * p.n_layers + p.layer) * p.max_seq + wa + pt * KPW;
-    const int st = item % kAttnStages;
-    mbar_arrive_expect_tx(&sm.bar[warp][st], 2 * TILE_F * 4);
-    tma_load_2d(mytiles + (size_t)(2 * st) * TILE_F, &p.tm_k, kvh * 128, row, &sm.bar[warp][st]);
-    tma_load_2d(mytiles + (size_t)(2 * st + 1) * TILE_F, &p.tm_v, kvh * 128, row, &sm.bar[warp][st]);
-    ++pt;
-  };
-  // q and the newest K/V row are written by the previous kernel: wait for it
-  // before the first tile load (the tile holding the newest row may be any)
-  pdl_wait();
-  pdl_launch_dependents();
-  if (lane == 0)
-    for (int i = 0; i < T && i < kAttnStages; ++i) issue_next(i);
-  __syncwarp();
+  // CTAs covering a pair: c_of(t) = floor(((t+1)*Gd - 1) / Tk) of its first and last key
+  auto c_first = [&](int s) { return ((sm.off[sm.seg_pair[s]] + 1) * Gd - 1) / Tk; };
+  auto c_last = [&](int s) { return (sm.off[sm.seg_pair[s] + 1] * Gd - 1) / Tk; };
 
+  int issued = 0, waited = 0;  // this warp's ring items, over all groups
+  bool failed = false;
   constexpr int V = G * KPW;
   const int my_idx = reduce_index<V>(lane);  // value (head my_idx/KPW, key my_idx%KPW)
   const bool writer = (lane & (32 / V - 1)) == 0;
-  int item = 0;
-  bool failed = false;
-  int fail_item = -1;
-  for (int sg = 0; sg < nseg; ++sg) {
+  const int my_g = my_idx / KPW, my_key = my_idx % KPW;
+
+  for (int g0 = 0; g0 < nseg; g0 += W) {
+    const int gn = min(W, nseg - g0);
+    if (threadIdx.x == 0) {
+      // warps per segment in proportion to its keys (each segment gets >= 1)
+      int cnt[W];
+      long long len[W];
+      for (int s = 0; s < gn; ++s) {
+        cnt[s] = 1;
+        len[s] = sm.seg_b[g0 + s] - sm.seg_a[g0 + s];
+      }
+      for (int extra = W - gn; extra > 0; --extra) {
+        int best = 0;
+        for (int s = 1; s < gn; ++s)  // largest keys per warp gets the next warp
+          if (len[s] * cnt[best] > len[best] * cnt[s]) best = s;
+        ++cnt[best];
+      }
+      int w = 0;
+      for (int s = 0; s < gn; ++s) {
+        const int a = sm.seg_a[g0 + s], n = sm.seg_b[g0 + s] - a;
+        for (int i = 0; i < cnt[s]; ++i, ++w) {
+          sm.wseg[w] = g0 + s;
+          sm.wa[w] = a + (int)((long long)n * i / cnt[s]);
+          sm.wb[w] = a + (int)((long long)n * (i + 1) / cnt[s]);
+        }
+      }
+    }
+    __syncthreads();
+    const int sg = sm.wseg[warp], wa = sm.wa[warp], wb = sm.wb[warp];
     const int pr = sm.seg_pair[sg], m = pr / n_kv, kvh = pr % n_kv;
-    int wa, wb;
-    wrange(sg, wa, wb);
+    const int T = (wb - wa + KPW - 1) / KPW;  // tiles of this warp in this group
+    const int newest = p.positions[m];         // row appended by the previous kernel
+    const int row0 = (m * p.n_layers + p.layer) * p.max_seq;
+    const int first_item = issued;             // ring index of this group's tile 0
+    auto issue = [&](int i) {  // lane 0: tile i of this group
+      const int st = issued % kAttnStages;
+      mbar_arrive_expect_tx(&sm.bar[warp][st], 2 * TILE_F * 4);
+      tma_load_2d(mytiles + (size_t)(2 * st) * TILE_F, &p.tm_k, kvh * 128, row0 + wa + i * KPW, &sm.bar[warp][st]);
+      tma_load_2d(mytiles + (size_t)(2 * st + 1) * TILE_F, &p.tm_v, kvh * 128, row0 + wa + i * KPW, &sm.bar[warp][st]);
+      ++issued;
+    };
+    int next_issue = 0;  // next tile of this group to issue (lane 0)
+    if (g0 == 0) {
+      // history tiles before the dependency wait, in order, up to the first
+      // tile that holds the newest row
+      if (lane == 0)
+        while (next_issue < T && next_issue < kAttnStages && wa + next_issue * KPW + KPW - 1 < newest) issue(next_issue++);
+      // q and the newest K/V rows come from the previous kernel
+      pdl_wait();
+      pdl_launch_dependents();
+    }
+    if (lane == 0)
+      while (next_issue < T && next_issue < kAttnStages) issue(next_issue++);
+    issued = __shfl_sync(0xffffffffu, issued, 0);
+    __syncwarp();
+
     float mx[G], sum[G];
     float4 o[G], qv[G];
 #pragma unroll
@@ -208,106 +230,112 @@ attn_decode_kernel(const __grid_constant__ AttnDecodeParams p) {
       sum[g] = 0.0f;
       o[g] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    for (int k0 = wa; k0 < wb; k0 += KPW, ++item) {
-      const int st = item % kAttnStages;
-      if (!failed && !mbar_wait(&sm.bar[warp][st], (unsigned)((item / kAttnStages) & 1))) {
-        failed = true;
-        fail_item = item;
+    for (int i = 0; i < T; ++i) {
+      const int item = first_item + i, st = item % kAttnStages;
+      if (!failed) {  // warp-uniform outcome: the tile math below is warp-collective
+        if (__all_sync(0xffffffffu, mbar_wait(&sm.bar[warp][st], (unsigned)((item / kAttnStages) & 1))))
+          ++waited;
+        else
+          failed = true;
       }
-      if (failed) continue;
-      const float *kt = mytiles + (size_t)(2 * st) * TILE_F;
-      const float *vt = mytiles + (size_t)(2 * st + 1) * TILE_F;
-      const int nk = min(KPW, wb - k0);
-      float part[V];
+      if (!failed) {
+        const float *kt = mytiles + (size_t)(2 * st) * TILE_F;
+        const float *vt = mytiles + (size_t)(2 * st + 1) * TILE_F;
+        const int nk = min(KPW, wb - wa - i * KPW);
+        float part[V];
 #pragma unroll
-      for (int j = 0; j < KPW; ++j) {
-        const float4 kv = *reinterpret_cast<const float4 *>(kt + (size_t)j * 128 + 4 * lane);
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-          float d = __fmul_rn(qv[g].x, kv.x);
-          d = fmaf(qv[g].y, kv.y, d);
-          d = fmaf(qv[g].z, kv.z, d);
-          d = fmaf(qv[g].w, kv.w, d);
-          part[g * KPW + j] = d;
-        }
-      }
-      const float tot = warp_reduce_scatter<V>(part);
-      const int my_g = my_idx / KPW, my_key = my_idx % KPW;
-      const bool live = my_key < nk;
-      const float sc = live ? __fmul_rn(tot, p.scale) : -INFINITY;
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        // lanes of head g carry its scores; the rest contribute neutral values
-        const float scg = my_g == g ? sc : -INFINITY;
-        const float nmax = fmaxf(mx[g], warp_max(scg));
-        const float corr = mx[g] == -INFINITY ? 0.0f : __expf(__fsub_rn(mx[g], nmax));
-        const float pj = (my_g == g && live) ? __expf(__fsub_rn(sc, nmax)) : 0.0f;
-        sum[g] = __fadd_rn(__fmul_rn(sum[g], corr), warp_sum(writer ? pj : 0.0f));
-        mx[g] = nmax;
-        if (writer && my_g == g) sp[warp][g][my_key] = pj;
-        o[g].x = __fmul_rn(o[g].x, corr);
-        o[g].y = __fmul_rn(o[g].y, corr);
-        o[g].z = __fmul_rn(o[g].z, corr);
-        o[g].w = __fmul_rn(o[g].w, corr);
-      }
-      __syncwarp();
-#pragma unroll
-      for (int j = 0; j < KPW; ++j) {
-        if (j < nk) {
-          const float4 vv = *reinterpret_cast<const float4 *>(vt + (size_t)j * 128 + 4 * lane);
+        for (int j = 0; j < KPW; ++j) {
+          const float4 kv = *reinterpret_cast<const float4 *>(kt + (size_t)j * 128 + 4 * lane);
 #pragma unroll
           for (int g = 0; g < G; ++g) {
-            const float w = sp[warp][g][j];
-            o[g].x = fmaf(w, vv.x, o[g].x);
-            o[g].y = fmaf(w, vv.y, o[g].y);
-            o[g].z = fmaf(w, vv.z, o[g].z);
-            o[g].w = fmaf(w, vv.w, o[g].w);
+            float d = __fmul_rn(qv[g].x, kv.x);
+            d = fmaf(qv[g].y, kv.y, d);
+            d = fmaf(qv[g].z, kv.z, d);
+            d = fmaf(qv[g].w, kv.w, d);
+            part[g * KPW + j] = d;
+          }
+        }
+        const float tot = warp_reduce_scatter<V>(part);
+        const bool live = my_key < nk;
+        const float sc = live ? __fmul_rn(tot, p.scale) : -INFINITY;
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          // lanes of head g carry its scores; the rest contribute neutral values
+          const float scg = my_g == g ? sc : -INFINITY;
+          const float nmax = fmaxf(mx[g], warp_max(scg));
+          const float corr = mx[g] == -INFINITY ? 0.0f : __expf(__fsub_rn(mx[g], nmax));
+          const float pj = (my_g == g && live) ? __expf(__fsub_rn(sc, nmax)) : 0.0f;
+          sum[g] = __fadd_rn(__fmul_rn(sum[g], corr), warp_sum(writer ? pj : 0.0f));
+          mx[g] = nmax;
+          if (writer && my_g == g) sp[warp][g][my_key] = pj;
+          o[g].x = __fmul_rn(o[g].x, corr);
+          o[g].y = __fmul_rn(o[g].y, corr);
+          o[g].z = __fmul_rn(o[g].z, corr);
+          o[g].w = __fmul_rn(o[g].w, corr);
+        }
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < KPW; ++j) {
+          if (j < nk) {
+            const float4 vv = *reinterpret_cast<const float4 *>(vt + (size_t)j * 128 + 4 * lane);
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+              const float w = sp[warp][g][j];
+              o[g].x = fmaf(w, vv.x, o[g].x);
+              o[g].y = fmaf(w, vv.y, o[g].y);
+              o[g].z = fmaf(w, vv.z, o[g].z);
+              o[g].w = fmaf(w, vv.w, o[g].w);
+            }
           }
         }
       }
       __syncwarp();  // every lane is done with stage st and with sp
-      if (lane == 0 && item + kAttnStages < T) {
+      if (lane == 0 && !failed && next_issue < T) {
         fence_proxy_async();
-        issue_next(item + kAttnStages);
+        issue(next_issue++);
       }
+      issued = __shfl_sync(0xffffffffu, issued, 0);
     }
-
-    // ---- end of segment: merge the warps of each head ----
+    // park this warp's state (an empty range leaves max = -inf, sum = 0)
+    float *sl = slots + (size_t)warp * G * kAttnPartStride;
 #pragma unroll
     for (int g = 0; g < G; ++g) {
+      reinterpret_cast<float4 *>(sl + g * kAttnPartStride)[lane] = o[g];
       if (lane == 0) {
-        wm[warp][g] = mx[g];
-        wl[warp][g] = sum[g];
+        sl[g * kAttnPartStride + 128] = mx[g];
+        sl[g * kAttnPartStride + 129] = sum[g];
       }
-      wo[warp][g][lane] = o[g];
     }
     __syncthreads();
-    // CTAs covering this pair: c_of(t) = floor(((t+1)*Gd - 1) / Tk)
-    const long long off = sm.off[pr], len = sm.off[pr + 1] - off;
-    const long long c_first = ((off + 1) * Gd - 1) / Tk, c_last = ((off + len) * Gd - 1) / Tk;
-    const bool alone = c_first == c_last;
-    if (warp < G) {
-      const int g = warp;
+
+    // ---- merge the warps of each segment of the group (task s*G+g: segment s, head g)
+    bool any_split = false;
+    for (int s = g0; s < g0 + gn; ++s) any_split |= c_first(s) != c_last(s);
+    for (int task = warp; task < gn * G; task += W) {
+      const int s = g0 + task / G, g = task % G;
+      const int prs = sm.seg_pair[s], ms = prs / n_kv, kvs = prs % n_kv;
       float Mx = -INFINITY;
-      for (int w = 0; w < kAttnWarps; ++w) Mx = fmaxf(Mx, wm[w][g]);
+      for (int w = 0; w < W; ++w)
+        if (sm.wseg[w] == s) Mx = fmaxf(Mx, slots[((size_t)w * G + g) * kAttnPartStride + 128]);
       float L = 0.0f;
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int w = 0; w < kAttnWarps; ++w) {
-        const float f = wm[w][g] == -INFINITY ? 0.0f : expf(__fsub_rn(wm[w][g], Mx));
-        L = __fadd_rn(L, __fmul_rn(wl[w][g], f));
-        const float4 ov = wo[w][g][lane];
+      for (int w = 0; w < W; ++w) {
+        if (sm.wseg[w] != s) continue;
+        const float *ws = slots + ((size_t)w * G + g) * kAttnPartStride;
+        const float f = ws[128] == -INFINITY ? 0.0f : expf(__fsub_rn(ws[128], Mx));
+        L = __fadd_rn(L, __fmul_rn(ws[129], f));
+        const float4 ov = reinterpret_cast<const float4 *>(ws)[lane];
         acc.x = fmaf(ov.x, f, acc.x);
         acc.y = fmaf(ov.y, f, acc.y);
         acc.z = fmaf(ov.z, f, acc.z);
         acc.w = fmaf(ov.w, f, acc.w);
       }
-      float *dst_out = p.out + (size_t)m * p.out_stride + (kvh * G + g) * 128;
-      if (alone) {
+      if (c_first(s) == c_last(s)) {
         const float inv = __fdiv_rn(1.0f, L);
-        reinterpret_cast<float4 *>(dst_out)[lane] =
+        reinterpret_cast<float4 *>(p.out + (size_t)ms * p.out_stride + (kvs * G + g) * 128)[lane] =
             make_float4(__fmul_rn(acc.x, inv), __fmul_rn(acc.y, inv), __fmul_rn(acc.z, inv), __fmul_rn(acc.w, inv));
       } else {
-        float *slot = p.partials + ((size_t)(c + pr) * G + g) * kAttnPartStride;
+        float *slot = p.partials + ((size_t)(c + prs) * G + g) * kAttnPartStride;
         reinterpret_cast<float4 *>(slot)[lane] = acc;
         if (lane == 0) {
           slot[128] = Mx;
@@ -315,46 +343,49 @@ attn_decode_kernel(const __grid_constant__ AttnDecodeParams p) {
         }
       }
     }
-    if (!alone) {
+    if (any_split) {
       __threadfence();
       __syncthreads();
-      if (threadIdx.x == 0) s_last = atomicAdd(p.counters + pr, 1u) == (unsigned)(c_last - c_first);
+      if (threadIdx.x < gn) {
+        const int s = g0 + threadIdx.x;
+        const long long cf = c_first(s), cl = c_last(s);
+        sm.last[threadIdx.x] = cf != cl && atomicAdd(p.counters + sm.seg_pair[s], 1u) == (unsigned)(cl - cf);
+      }
       __syncthreads();
-      if (s_last) {
+      for (int task = warp; task < gn * G; task += W) {
+        if (!sm.last[task / G]) continue;
         __threadfence();
-        if (warp < G) {
-          const int g = warp;
-          float Mx = -INFINITY;
-          for (long long c2 = c_first; c2 <= c_last; ++c2)
-            Mx = fmaxf(Mx, __ldcg(p.partials + ((size_t)(c2 + pr) * G + g) * kAttnPartStride + 128));
-          float L = 0.0f;
-          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-          for (long long c2 = c_first; c2 <= c_last; ++c2) {
-            const float *ps2 = p.partials + ((size_t)(c2 + pr) * G + g) * kAttnPartStride;
-            const float ms = __ldcg(ps2 + 128);
-            const float f = ms == -INFINITY ? 0.0f : expf(__fsub_rn(ms, Mx));
-            L = __fadd_rn(L, __fmul_rn(__ldcg(ps2 + 129), f));
-            const float4 ov = __ldcg(reinterpret_cast<const float4 *>(ps2) + lane);
-            acc.x = fmaf(ov.x, f, acc.x);
-            acc.y = fmaf(ov.y, f, acc.y);
-            acc.z = fmaf(ov.z, f, acc.z);
-            acc.w = fmaf(ov.w, f, acc.w);
-          }
-          const float inv = __fdiv_rn(1.0f, L);
-          *reinterpret_cast<float4 *>(p.out + (size_t)m * p.out_stride + (kvh * G + g) * 128 + 4 * lane) =
-              make_float4(__fmul_rn(acc.x, inv), __fmul_rn(acc.y, inv), __fmul_rn(acc.z, inv),
-                          __fmul_rn(acc.w, inv));
+        const int s = g0 + task / G, g = task % G;
+        const int prs = sm.seg_pair[s], ms = prs / n_kv, kvs = prs % n_kv;
+        const long long cf = c_first(s), cl = c_last(s);
+        float Mx = -INFINITY;
+        for (long long c2 = cf; c2 <= cl; ++c2)
+          Mx = fmaxf(Mx, __ldcg(p.partials + ((size_t)(c2 + prs) * G + g) * kAttnPartStride + 128));
+        float L = 0.0f;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (long long c2 = cf; c2 <= cl; ++c2) {
+          const float *ps2 = p.partials + ((size_t)(c2 + prs) * G + g) * kAttnPartStride;
+          const float ms2 = __ldcg(ps2 + 128);
+          const float f = ms2 == -INFINITY ? 0.0f : expf(__fsub_rn(ms2, Mx));
+          L = __fadd_rn(L, __fmul_rn(__ldcg(ps2 + 129), f));
+          const float4 ov = __ldcg(reinterpret_cast<const float4 *>(ps2) + lane);
+          acc.x = fmaf(ov.x, f, acc.x);
+          acc.y = fmaf(ov.y, f, acc.y);
+          acc.z = fmaf(ov.z, f, acc.z);
+          acc.w = fmaf(ov.w, f, acc.w);
         }
-        if (threadIdx.x == 0) p.counters[pr] = 0u;
+        const float inv = __fdiv_rn(1.0f, L);
+        *reinterpret_cast<float4 *>(p.out + (size_t)ms * p.out_stride + (kvs * G + g) * 128 + 4 * lane) =
+            make_float4(__fmul_rn(acc.x, inv), __fmul_rn(acc.y, inv), __fmul_rn(acc.z, inv), __fmul_rn(acc.w, inv));
+        if (lane == 0 && g == 0) p.counters[prs] = 0u;
       }
     }
-    __syncthreads();
+    __syncthreads();  // slots and the warp map are rewritten by the next group
   }
-  if (failed) {
-    if (lane == 0 && p.err) atomicExch(p.err, -QASR_ERR_TIMEOUT);
-    for (int k2 = fail_item; k2 < T && k2 < fail_item + kAttnStages; ++k2)
-      mbar_wait(&sm.bar[warp][k2 % kAttnStages], (unsigned)((k2 / kAttnStages) & 1));
-  }
+  if (failed && lane == 0 && p.err) atomicExch(p.err, -QASR_ERR_TIMEOUT);
+  // copies still in flight (only after a timeout) land before the CTA exits
+  for (int k2 = waited; k2 < issued; ++k2)
+    mbar_wait(&sm.bar[warp][k2 % kAttnStages], (unsigned)((k2 / kAttnStages) & 1));
 }
 
 int attn_grid() {
@@ -398,8 +429,9 @@ int attn_make_tensor_map(CUtensorMap *tm, const float *base, long rows, int kv_d
   return QASR_OK;
 }
 
-static size_t attn_smem() {
-  return (size_t)kAttnWarps * kAttnStages * 2 * kAttnTile * 128 * 4 + sizeof(AttnSmall);
+static size_t attn_smem(int G) {
+  return (size_t)kAttnWarps * kAttnStages * 2 * kAttnTile * 128 * 4 + (size_t)kAttnWarps * G * kAttnPartStride * 4 +
+         sizeof(AttnSmall);
 }
 
 template <int G>
@@ -407,7 +439,7 @@ static int attn_launch_t(const AttnDecodeParams &p, cudaStream_t st, bool pdl) {
   static bool attr_done = false;
   if (!attr_done) {
     int rc = cuda_status(cudaFuncSetAttribute(attn_decode_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              (int)attn_smem()),
+                                              (int)attn_smem(G)),
                          "attention: shared memory opt-in");
     if (rc) return rc;
     attr_done = true;
@@ -415,7 +447,7 @@ static int attn_launch_t(const AttnDecodeParams &p, cudaStream_t st, bool pdl) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)attn_grid());
   cfg.blockDim = dim3(kAttnWarps * 32);
-  cfg.dynamicSmemBytes = attn_smem();
+  cfg.dynamicSmemBytes = attn_smem(G);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
