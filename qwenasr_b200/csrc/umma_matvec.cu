@@ -358,9 +358,9 @@ __global__ void __launch_bounds__(kUWarps * 32, 1) int8_umma_kernel(const __grid
 #pragma unroll
         for (int m = 0; m < 8; ++m) rb[ri * 8 + m] = (unsigned long long)V[m];
         named_bar(1, kUEpiThreads);
-        if (threadIdx.x == 0) {
+        if (threadIdx.x < C) {  // one arrival per rank, issued in parallel
           asm volatile("fence.acq_rel.cluster;" ::: "memory");
-          for (int q = 0; q < C; ++q) mbar_arrive_remote(cluster_map(smem_u32(&sm.redfull[buf]), (uint32_t)q));
+          mbar_arrive_remote(cluster_map(smem_u32(&sm.redfull[buf]), (uint32_t)threadIdx.x));
         }
         ok = mbar_wait_cluster(&sm.redfull[buf], (unsigned)((j >> 1) & 1)) && ok;
         if (!ok) u_fail(sm, p.err);
@@ -378,8 +378,8 @@ __global__ void __launch_bounds__(kUWarps * 32, 1) int8_umma_kernel(const __grid
           }
         }
         named_bar(1, kUEpiThreads);
-        if (threadIdx.x == 0)
-          for (int q = 0; q < C; ++q) mbar_arrive_remote(cluster_map(smem_u32(&sm.redempty[buf]), (uint32_t)q));
+        if (threadIdx.x < C)  // this rank is done reading every rank's partials
+          mbar_arrive_remote(cluster_map(smem_u32(&sm.redempty[buf]), (uint32_t)threadIdx.x));
       }
 
       const int row = t * 128 + ri;
