@@ -122,6 +122,14 @@ class ClockSampler:
 
 
 # --------------------------------------------------------- byte accounting --
+# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of each
+# kernel class from one ncu capture of the 0.6B, M=8, KV-1024 step; see
+# profiles/attn_decode_0p6b_m8_kv1024.md and
+# profiles/int8_contraction_tcgen05_decode_0p6b_m8.md for the commands.
+NCU_TRAFFIC_M8 = {"attn": 67643904 + 1371392, "qkv": 4309504, "oproj": 2244608, "gateup": 6413824,
+                  "down": 3325952, "lmhead": 156296448 + 4083456}
+
+
 def class_bytes(cfg, M, kv_len):
     """Algorithmic bytes per launch of each kernel class of the step (weights,
     scales, activations in/out, K/V rows read)."""
@@ -341,7 +349,9 @@ def run_ours(a):
                     "d2h_bytes_per_step": 4 * M + 4},
             "gpu_launches": launches_per_step * a.steps,
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None, "peak_kind": peak_kind,
+                         "frac": achieved / peak,
+                         "traffic": NCU_TRAFFIC_M8.get(dom) if (M, L, cfg["n_layers"]) == (8, 1024, 28) else None,
+                         "traffic_source": "ncu capture of this workload (profiles/)", "peak_kind": peak_kind,
                          "bytes_per_launch": cb[dom], "us_per_launch": per_launch_s * 1e6},
             "step_roofline": {"bytes": step_bytes, "achieved_gbs": step_bytes / (ms / 1e3) / 1e9,
                               "frac": step_bytes / (ms / 1e3) / 1e9 / peak},
