@@ -145,6 +145,22 @@ int qasr_linear_nobias(float *y, const float *x, const float *w, int seq, int in
 /* kernels::matmul_t (mod.rs:503-528): c[m,n] = sum_k a[m,k]*b[n,k]. */
 int qasr_matmul_t(float *c, const float *a, const float *b, int m, int k, int n, void *stream);
 
+/* kernels::conv2d (mod.rs:790-860): out [c_out, h_out*w_out] = weight
+ * [c_out, c_in*kh*kw] x im2col(input [c_in, h_in, w_in]) + bias[c_out] (bias
+ * may be NULL); h_out = (h_in + 2*padding - kh)/stride + 1, same for w.  The
+ * product runs as the tensor-core f32 GEMM when c_in*kh*kw and the output
+ * size allow (see qasr_linear), on CUDA cores otherwise. */
+int qasr_conv2d(float *out, const float *input, const float *weight, const float *bias, int c_in, int c_out,
+                int h_in, int w_in, int kh, int kw, int stride, int padding, void *stream);
+
+/* kernels::bidirectional_attention (mod.rs:1038-1122): full attention inside
+ * windows [window_starts[w], window_starts[w+1]) (device int32 array of
+ * n_windows+1 increasing entries, the last = seq), q/k/v/out [seq,
+ * n_heads*head_dim]; head_dim 64 or 128. */
+int qasr_bidirectional_attention(float *out, const float *q, const float *k, const float *v, int seq, int n_heads,
+                                 int head_dim, float scale, const int32_t *window_starts, int n_windows,
+                                 void *stream);
+
 /* kernels::causal_attention (mod.rs:1124-1207): GQA causal attention of
  * seq_q queries at global positions q_offset.. over k/v [seq_k, n_kv*hd].
  * head_dim must be 64 or 128. */

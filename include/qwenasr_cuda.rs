@@ -66,6 +66,8 @@ extern "C" {
     pub fn qasr_linear(y: *mut f32, x: *const f32, w: *const f32, b: *const f32, seq: c_int, in_dim: c_int, out_dim: c_int, stream: *mut c_void) -> c_int;
     pub fn qasr_linear_nobias(y: *mut f32, x: *const f32, w: *const f32, seq: c_int, in_dim: c_int, out_dim: c_int, stream: *mut c_void) -> c_int;
     pub fn qasr_matmul_t(c: *mut f32, a: *const f32, b: *const f32, m: c_int, k: c_int, n: c_int, stream: *mut c_void) -> c_int;
+    pub fn qasr_conv2d(out: *mut f32, input: *const f32, weight: *const f32, bias: *const f32, c_in: c_int, c_out: c_int, h_in: c_int, w_in: c_int, kh: c_int, kw: c_int, stride: c_int, padding: c_int, stream: *mut c_void) -> c_int;
+    pub fn qasr_bidirectional_attention(out: *mut f32, q: *const f32, k: *const f32, v: *const f32, seq: c_int, n_heads: c_int, head_dim: c_int, scale: f32, window_starts: *const i32, n_windows: c_int, stream: *mut c_void) -> c_int;
     pub fn qasr_causal_attention(out: *mut f32, q: *const f32, k: *const f32, v: *const f32, seq_q: c_int, seq_k: c_int, n_heads: c_int, n_kv_heads: c_int, head_dim: c_int, scale: f32, q_offset: c_int, stream: *mut c_void) -> c_int;
     pub fn qasr_quantize_f32_to_int8(data: *const f32, out_dim: i64, in_dim: i64, q: *mut i8, scales: *mut f32, stream: *mut c_void) -> c_int;
     pub fn qasr_embed_gather_f32(dst: *mut f32, table: *const f32, ids: *const i32, n: c_int, dim: c_int, vocab: i64, bad_id_flag: *mut c_int, stream: *mut c_void) -> c_int;

@@ -67,6 +67,8 @@ _SIGS = {
     "qasr_linear": (I, [P, P, P, P, I, I, I, P]),
     "qasr_linear_nobias": (I, [P, P, P, I, I, I, P]),
     "qasr_matmul_t": (I, [P, P, P, I, I, I, P]),
+    "qasr_conv2d": (I, [P, P, P, P, I, I, I, I, I, I, I, I, P]),
+    "qasr_bidirectional_attention": (I, [P, P, P, P, I, I, I, F, P, I, P]),
     "qasr_quantize_f32_to_int8": (I, [P, I64, I64, P, P, P]),
     "qasr_embed_gather_f32": (I, [P, P, P, I, I, I64, P, P]),
     "qasr_embed_gather_int8": (I, [P, P, P, P, I, I, I64, P, P]),

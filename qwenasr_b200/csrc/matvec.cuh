@@ -91,7 +91,7 @@ int argmax_scratch(unsigned long long **keys, unsigned **counter);
 int mv_norm_scratch(float **buf, size_t n_floats);
 
 constexpr int kScratchPartial = 0, kScratchCounter = 1, kScratchDigits = 2, kScratchDigitScale = 3,
-              kScratchWeightDigits = 4, kScratchWeightScale = 5, kScratchSlots = 6;
+              kScratchWeightDigits = 4, kScratchWeightScale = 5, kScratchIm2col = 6, kScratchSlots = 7;
 int dev_scratch(int slot, size_t bytes, void **out);
 
 }  // namespace qasr

@@ -156,6 +156,23 @@ def matmul_t(c, a, b, m, k, n):
               _stream())
 
 
+def conv2d(out, inp, weight, bias, c_in, c_out, h_in, w_in, kh, kw, stride, padding):
+    """kernels::conv2d (mod.rs:815): out [c_out, h_out*w_out]; bias may be None."""
+    h_out = (h_in + 2 * padding - kh) // stride + 1
+    w_out = (w_in + 2 * padding - kw) // stride + 1
+    _lib.call("qasr_conv2d", _ptr(out, f32, "out", c_out * h_out * w_out), _ptr(inp, f32, "input", c_in * h_in * w_in),
+              _ptr(weight, f32, "weight", c_out * c_in * kh * kw), _ptr(bias, f32, "bias", c_out), c_in, c_out, h_in,
+              w_in, kh, kw, stride, padding, _stream())
+
+
+def bidirectional_attention(out, q, k, v, seq, n_heads, head_dim, scale, window_starts, n_windows):
+    """kernels::bidirectional_attention (mod.rs:1094); window_starts int32 [n_windows+1] on the device."""
+    _lib.call("qasr_bidirectional_attention", _ptr(out, f32, "out", seq * n_heads * head_dim),
+              _ptr(q, f32, "q", seq * n_heads * head_dim), _ptr(k, f32, "k", seq * n_heads * head_dim),
+              _ptr(v, f32, "v", seq * n_heads * head_dim), seq, n_heads, head_dim, C.c_float(scale),
+              _ptr(window_starts, i32, "window_starts", n_windows + 1), n_windows, _stream())
+
+
 def causal_attention(out, q, k, v, seq_q, seq_k, n_heads, n_kv_heads, head_dim, scale, q_offset):
     """kernels::causal_attention (mod.rs:1174)."""
     _lib.call("qasr_causal_attention", _ptr(out, f32, "out", seq_q * n_heads * head_dim),

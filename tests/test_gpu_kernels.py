@@ -430,3 +430,47 @@ def test_causal_attention(orc, seq_q, seq_k, off):
     K.causal_attention(out, T(q), T(k), T(v), seq_q, seq_k, nh, nkv, hd, scale, off)
     ref = orc.causal_attention(q, k, v, seq_q, seq_k, nh, nkv, hd, off, np.float32(scale))
     assert np.max(np.abs(H(out) - ref)) < 2e-5
+
+
+# -------------------------------------------------------- encoder kernels --
+def _conv2d_ref(x, w, b, c_in, c_out, h, wd, kh, kw, stride, pad):
+    """fp64 im2col + GEMM (conv2d, mod.rs:790-860, cblas_sgemm in the reference)."""
+    ho, wo = (h + 2 * pad - kh) // stride + 1, (wd + 2 * pad - kw) // stride + 1
+    xp = np.zeros((c_in, h + 2 * pad, wd + 2 * pad))
+    xp[:, pad:pad + h, pad:pad + wd] = x.reshape(c_in, h, wd)
+    cols = np.empty((c_in * kh * kw, ho * wo))
+    for ic in range(c_in):
+        for ki in range(kh):
+            for kj in range(kw):
+                cols[(ic * kh + ki) * kw + kj] = xp[ic, ki:ki + stride * ho:stride, kj:kj + stride * wo:stride].ravel()
+    out = w.reshape(c_out, -1).astype(np.float64) @ cols
+    return out + (b[:, None] if b is not None else 0.0)
+
+
+@pytest.mark.parametrize("c_in,c_out,h,w,bias", [
+    (1, 480, 128, 100, True),    # encoder conv1: [1,128,chunk] -> [480,64,50] (patch 9: CUDA cores)
+    (480, 480, 64, 50, True),    # conv2 -> [480,32,25] (patch 4320: tensor cores)
+    (480, 480, 32, 25, False),   # conv3 -> [480,16,13]
+])
+def test_conv2d_encoder_stem(c_in, c_out, h, w, bias):
+    rng = np.random.default_rng(c_in + h)
+    x = rng.standard_normal((c_in, h, w)).astype(np.float32)
+    wt = (rng.standard_normal((c_out, c_in, 3, 3)) * 0.05).astype(np.float32)
+    b = (rng.standard_normal(c_out) * 0.1).astype(np.float32) if bias else None
+    ho, wo = (h - 1) // 2 + 1, (w - 1) // 2 + 1
+    out = torch.empty(c_out, ho * wo, device=DEV)
+    K.conv2d(out, T(x), T(wt), T(b) if bias else None, c_in, c_out, h, w, 3, 3, 2, 1)
+    ok, err = rel_close(H(out), _conv2d_ref(x, wt, b, c_in, c_out, h, w, 3, 3, 2, 1), 1e-5)
+    assert ok, err
+
+
+@pytest.mark.parametrize("seq,n_heads,hd,win", [(390, 14, 64, 104), (37, 2, 128, 37), (50, 3, 64, 7)])
+def test_bidirectional_attention(orc, seq, n_heads, hd, win):
+    rng = np.random.default_rng(seq + win)
+    q, k, v = (rng.standard_normal((seq, n_heads * hd)).astype(np.float32) for _ in range(3))
+    starts = np.array(list(range(0, seq, win)) + [seq], np.int32)
+    scale = 1.0 / math.sqrt(hd)
+    out = torch.empty(seq, n_heads * hd, device=DEV)
+    K.bidirectional_attention(out, T(q), T(k), T(v), seq, n_heads, hd, scale, T(starts), len(starts) - 1)
+    ref = orc.bidirectional_attention(q, k, v, seq, n_heads, hd, starts, np.float32(scale))
+    assert np.max(np.abs(H(out) - ref)) < 2e-5
