@@ -338,6 +338,55 @@ int qasr_decoder_profile_step(qasr_decoder *dec, const int32_t *tokens, const in
  * (weights + scales + norms + lm head + K/V rows attended); for rooflines. */
 int64_t qasr_decoder_step_bytes(const qasr_decoder *dec, const int32_t *positions, int M);
 
+/* ======================================================================
+ * Audio encoder engine (f32 weights)
+ * ==================================================================== */
+
+typedef struct qasr_encoder qasr_encoder;
+
+typedef struct {
+  int d_model;        /* 896 (0.6B) / 1024 (1.7B) */
+  int n_layers;       /* 18 / 24 */
+  int n_heads;        /* 14 / 16 */
+  int head_dim;       /* 64 */
+  int ffn_dim;        /* 3584 / 4096 */
+  int output_dim;     /* the decoder hidden size: 1024 / 2048 */
+  int chunk_size;     /* mel frames per conv chunk: 2 * n_window = 100 */
+  int n_window_infer; /* 800: attention windows of chunk tokens * (n_window_infer / chunk_size) */
+} qasr_encoder_config;
+
+typedef struct {
+  const float *attn_norm_w, *attn_norm_b;        /* [d_model] */
+  const float *wq, *bq, *wk, *bk, *wv, *bv;      /* [d_model, d_model], [d_model] */
+  const float *wo, *bo;
+  const float *ffn_norm_w, *ffn_norm_b;          /* [d_model] */
+  const float *fc1_w, *fc1_b;                    /* [ffn, d_model], [ffn] */
+  const float *fc2_w, *fc2_b;                    /* [d_model, ffn], [d_model] */
+} qasr_enc_layer_weights;
+
+/* Encoder (encoder.rs:20-240) on `device`: weight buffers allocated, values
+ * set by the calls below (host or device pointers, copied).  NULL on failure. */
+qasr_encoder *qasr_encoder_create(const qasr_encoder_config *cfg, int device);
+void qasr_encoder_free(qasr_encoder *enc);
+
+/* Conv stem: conv1 [480, 1, 3, 3], conv2/conv3 [480, 480, 3, 3] with biases
+ * [480], conv_out [d_model, 480*16] (no bias). */
+int qasr_encoder_set_conv(qasr_encoder *enc, const float *conv1_w, const float *conv1_b, const float *conv2_w,
+                          const float *conv2_b, const float *conv3_w, const float *conv3_b, const float *conv_out_w);
+int qasr_encoder_set_layer(qasr_encoder *enc, int layer, const qasr_enc_layer_weights *w);
+/* ln_post [d_model], proj1 [d_model, d_model] + bias, proj2 [output_dim, d_model] + bias. */
+int qasr_encoder_set_post(qasr_encoder *enc, const float *ln_post_w, const float *ln_post_b, const float *proj1_w,
+                          const float *proj1_b, const float *proj2_w, const float *proj2_b);
+
+/* Encoder tokens produced for mel_frames frames (13 per full 100-frame chunk). */
+int qasr_encoder_tokens(const qasr_encoder *enc, int mel_frames);
+
+/* Encoder::forward (encoder.rs:243-415): mel [128, mel_frames] f32 (host or
+ * device) -> out [n_tokens, output_dim] (host or device, out_rows >= n_tokens).
+ * Synchronous. */
+int qasr_encoder_forward(qasr_encoder *enc, const float *mel, int mel_frames, float *out, int out_rows,
+                         int *n_tokens);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

@@ -44,6 +44,34 @@ pub struct QasrDecLayerWeights {
     pub q_norm: *const f32, pub k_norm: *const f32, pub input_norm: *const f32, pub post_attn_norm: *const f32,
 }
 
+#[repr(C)]
+pub struct QasrEncoder {
+    _private: [u8; 0],
+}
+
+#[repr(C)]
+#[derive(Clone, Copy)]
+pub struct QasrEncoderConfig {
+    pub d_model: c_int,
+    pub n_layers: c_int,
+    pub n_heads: c_int,
+    pub head_dim: c_int,
+    pub ffn_dim: c_int,
+    pub output_dim: c_int,
+    pub chunk_size: c_int,
+    pub n_window_infer: c_int,
+}
+
+#[repr(C)]
+#[derive(Clone, Copy)]
+pub struct QasrEncLayerWeights {
+    pub attn_norm_w: *const f32, pub attn_norm_b: *const f32,
+    pub wq: *const f32, pub bq: *const f32, pub wk: *const f32, pub bk: *const f32,
+    pub wv: *const f32, pub bv: *const f32, pub wo: *const f32, pub bo: *const f32,
+    pub ffn_norm_w: *const f32, pub ffn_norm_b: *const f32,
+    pub fc1_w: *const f32, pub fc1_b: *const f32, pub fc2_w: *const f32, pub fc2_b: *const f32,
+}
+
 #[link(name = "qwenasr_b200")]
 extern "C" {
     pub fn qasr_last_error() -> *const c_char;
@@ -92,4 +120,11 @@ extern "C" {
     pub fn qasr_decoder_logits(dec: *mut QasrDecoder) -> *const f32;
     pub fn qasr_decoder_profile_step(dec: *mut QasrDecoder, tokens: *const i32, positions: *const i32, M: c_int, class_ms: *mut f32, class_launches: *mut c_int, n_classes: c_int) -> c_int;
     pub fn qasr_decoder_step_bytes(dec: *const QasrDecoder, positions: *const i32, M: c_int) -> i64;
+    pub fn qasr_encoder_create(cfg: *const QasrEncoderConfig, device: c_int) -> *mut QasrEncoder;
+    pub fn qasr_encoder_free(enc: *mut QasrEncoder);
+    pub fn qasr_encoder_set_conv(enc: *mut QasrEncoder, conv1_w: *const f32, conv1_b: *const f32, conv2_w: *const f32, conv2_b: *const f32, conv3_w: *const f32, conv3_b: *const f32, conv_out_w: *const f32) -> c_int;
+    pub fn qasr_encoder_set_layer(enc: *mut QasrEncoder, layer: c_int, w: *const QasrEncLayerWeights) -> c_int;
+    pub fn qasr_encoder_set_post(enc: *mut QasrEncoder, ln_post_w: *const f32, ln_post_b: *const f32, proj1_w: *const f32, proj1_b: *const f32, proj2_w: *const f32, proj2_b: *const f32) -> c_int;
+    pub fn qasr_encoder_tokens(enc: *const QasrEncoder, mel_frames: c_int) -> c_int;
+    pub fn qasr_encoder_forward(enc: *mut QasrEncoder, mel: *const f32, mel_frames: c_int, out: *mut f32, out_rows: c_int, n_tokens: *mut c_int) -> c_int;
 }

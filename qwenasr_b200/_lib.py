@@ -94,6 +94,27 @@ _SIGS = {
     "qasr_decoder_profile_step": (I, [P, P, P, I, P, P, I]),
 }
 
+class EncoderConfig(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("d_model", "n_layers", "n_heads", "head_dim", "ffn_dim", "output_dim",
+                                       "chunk_size", "n_window_infer")]
+
+
+class EncLayerWeights(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in (
+        "attn_norm_w", "attn_norm_b", "wq", "bq", "wk", "bk", "wv", "bv", "wo", "bo", "ffn_norm_w", "ffn_norm_b",
+        "fc1_w", "fc1_b", "fc2_w", "fc2_b")]
+
+
+_SIGS.update({
+    "qasr_encoder_create": (P, [C.POINTER(EncoderConfig), I]),
+    "qasr_encoder_free": (None, [P]),
+    "qasr_encoder_set_conv": (I, [P, P, P, P, P, P, P, P]),
+    "qasr_encoder_set_layer": (I, [P, I, C.POINTER(EncLayerWeights)]),
+    "qasr_encoder_set_post": (I, [P, P, P, P, P, P, P]),
+    "qasr_encoder_tokens": (I, [P, I]),
+    "qasr_encoder_forward": (I, [P, P, I, P, I, C.POINTER(C.c_int)]),
+})
+
 KERNEL_CLASSES = ("embed", "norm", "qkv", "qkv_post", "attn", "oproj", "gateup", "down", "lmhead")
 
 _lib = None

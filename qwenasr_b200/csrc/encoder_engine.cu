@@ -1,0 +1,350 @@
+// encoder_engine.cu -- the audio encoder on one GPU: Encoder::forward
+// (crates/qwen-asr/src/encoder.rs:243-415) for f32 weights, composed from
+// the kernel-level entries in the reference's order.
+//
+// Per mel chunk of chunk_size frames (encoder.rs:281-348): three stride-2
+// 3x3 convolutions (480 channels) each followed by the tanh GELU, the
+// [480, h3, w3] -> [w3, 480*h3] reshape, the conv-out projection and the
+// sinusoidal position rows of the chunk.  Then per layer (encoder.rs:368-403):
+// LayerNorm, q/k/v projections with bias, bidirectional attention inside
+// windows of tokens_per_chunk * (n_window_infer / chunk_size) tokens, output
+// projection + residual, LayerNorm, fc1 + GELU, fc2 + residual.  Finally the
+// post LayerNorm and proj1 + GELU + proj2 (encoder.rs:405-415).
+//
+// Device layout: every weight is a device copy owned by the engine; the
+// activation buffers are sized for the largest mel length seen so far.
+#include <algorithm>
+#include <cstring>
+#include <vector>
+
+#include "common.cuh"
+
+namespace qasr {
+
+constexpr int kConvHidden = 480;  // CONV_HIDDEN (config.rs:23)
+constexpr int kMelBins = 128;
+
+// reshaped[t, ch*h3 + f] = c3[ch, f, t]
+__global__ void __launch_bounds__(256) conv_reshape_kernel(float *__restrict__ out, const float *__restrict__ c3,
+                                                           int ch_f, int w3) {
+  const long total = (long)ch_f * w3;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const int t = (int)(i / ch_f), cf = (int)(i % ch_f);
+    out[i] = c3[(long)cf * w3 + t];
+  }
+}
+
+struct EncLayerDev {
+  float *attn_norm_w, *attn_norm_b, *wq, *bq, *wk, *bk, *wv, *bv, *wo, *bo;
+  float *ffn_norm_w, *ffn_norm_b, *fc1_w, *fc1_b, *fc2_w, *fc2_b;
+};
+
+}  // namespace qasr
+
+struct qasr_encoder {
+  qasr_encoder_config cfg;
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  std::vector<qasr::EncLayerDev> layers;
+  float *conv_w[3] = {nullptr, nullptr, nullptr}, *conv_b[3] = {nullptr, nullptr, nullptr}, *conv_out_w = nullptr;
+  float *ln_post_w = nullptr, *ln_post_b = nullptr, *proj1_w = nullptr, *proj1_b = nullptr, *proj2_w = nullptr,
+        *proj2_b = nullptr;
+  std::vector<void *> allocs;
+  // activations, grown on demand
+  int tok_cap = 0, frames_cap = 0;
+  void *act = nullptr;
+  float *x = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr, *proj = nullptr,
+        *mid = nullptr, *out = nullptr, *pe = nullptr;
+  void *conv_buf = nullptr;
+  float *mel_chunk = nullptr, *c1 = nullptr, *c2 = nullptr, *c3 = nullptr, *reshaped = nullptr;
+  int32_t *win = nullptr;
+  int win_cap = 0;
+};
+
+using namespace qasr;
+
+static int enc_alloc(qasr_encoder *e, float **p, size_t n) {
+  void *q = nullptr;
+  int rc = cuda_status(cudaMalloc(&q, n * 4), "qasr_encoder: cudaMalloc");
+  if (rc) return rc;
+  e->allocs.push_back(q);
+  *p = static_cast<float *>(q);
+  return QASR_OK;
+}
+
+static int enc_copy(qasr_encoder *e, float *dst, const float *src, size_t n, const char *what) {
+  if (!src) {
+    set_error("qasr_encoder: %s is NULL", what);
+    return QASR_ERR_INVALID;
+  }
+  return cuda_status(cudaMemcpyAsync(dst, src, n * 4, cudaMemcpyDefault, e->stream), what);
+}
+
+extern "C" void qasr_encoder_free(qasr_encoder *e) {
+  if (!e) return;
+  cudaSetDevice(e->device);
+  if (e->stream) cudaStreamSynchronize(e->stream);
+  for (void *p : e->allocs) cudaFree(p);
+  if (e->act) cudaFree(e->act);
+  if (e->conv_buf) cudaFree(e->conv_buf);
+  if (e->win) cudaFree(e->win);
+  if (e->stream) cudaStreamDestroy(e->stream);
+  delete e;
+}
+
+static int chunk_tokens(int w) {  // three stride-2 3x3 convolutions with padding 1
+  const int w1 = (w + 2 - 3) / 2 + 1, w2 = (w1 + 2 - 3) / 2 + 1;
+  return (w2 + 2 - 3) / 2 + 1;
+}
+
+extern "C" qasr_encoder *qasr_encoder_create(const qasr_encoder_config *cfg, int device) {
+  if (!cfg || cfg->d_model <= 0 || cfg->n_layers <= 0 || cfg->n_heads <= 0 || cfg->ffn_dim <= 0 ||
+      cfg->output_dim <= 0 || cfg->chunk_size <= 0 || cfg->n_window_infer < cfg->chunk_size ||
+      cfg->head_dim * cfg->n_heads != cfg->d_model) {
+    set_error("qasr_encoder_create: invalid config");
+    return nullptr;
+  }
+  if (cfg->head_dim != 64 && cfg->head_dim != 128) {
+    set_error("qasr_encoder_create: head_dim must be 64 or 128");
+    return nullptr;
+  }
+  if (cudaSetDevice(device) != cudaSuccess) {
+    set_error("qasr_encoder_create: cudaSetDevice(%d) failed", device);
+    return nullptr;
+  }
+  qasr_encoder *e = new qasr_encoder();
+  e->cfg = *cfg;
+  e->device = device;
+  int rc = cuda_status(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking), "qasr_encoder_create");
+  const int D = cfg->d_model, F = cfg->ffn_dim, O = cfg->output_dim, CH = kConvHidden;
+  const int h3 = chunk_tokens(kMelBins);  // frequency rows after the stem: 16
+  e->layers.resize(cfg->n_layers);
+  const int cin[3] = {1, CH, CH};
+  for (int i = 0; i < 3 && !rc; ++i) {
+    rc = enc_alloc(e, &e->conv_w[i], (size_t)CH * cin[i] * 9);
+    if (!rc) rc = enc_alloc(e, &e->conv_b[i], CH);
+  }
+  if (!rc) rc = enc_alloc(e, &e->conv_out_w, (size_t)D * CH * h3);
+  for (auto &L : e->layers) {
+    float **pp[] = {&L.attn_norm_w, &L.attn_norm_b, &L.bq, &L.bk, &L.bv, &L.bo, &L.ffn_norm_w, &L.ffn_norm_b,
+                    &L.fc2_b};
+    for (float **p : pp)
+      if (!rc) rc = enc_alloc(e, p, D);
+    float **mm[] = {&L.wq, &L.wk, &L.wv, &L.wo};
+    for (float **p : mm)
+      if (!rc) rc = enc_alloc(e, p, (size_t)D * D);
+    if (!rc) rc = enc_alloc(e, &L.fc1_w, (size_t)F * D);
+    if (!rc) rc = enc_alloc(e, &L.fc1_b, F);
+    if (!rc) rc = enc_alloc(e, &L.fc2_w, (size_t)D * F);
+  }
+  if (!rc) rc = enc_alloc(e, &e->ln_post_w, D);
+  if (!rc) rc = enc_alloc(e, &e->ln_post_b, D);
+  if (!rc) rc = enc_alloc(e, &e->proj1_w, (size_t)D * D);
+  if (!rc) rc = enc_alloc(e, &e->proj1_b, D);
+  if (!rc) rc = enc_alloc(e, &e->proj2_w, (size_t)O * D);
+  if (!rc) rc = enc_alloc(e, &e->proj2_b, O);
+  if (rc) {
+    qasr_encoder_free(e);
+    return nullptr;
+  }
+  return e;
+}
+
+extern "C" int qasr_encoder_set_conv(qasr_encoder *e, const float *conv1_w, const float *conv1_b,
+                                     const float *conv2_w, const float *conv2_b, const float *conv3_w,
+                                     const float *conv3_b, const float *conv_out_w) {
+  if (!e) {
+    set_error("qasr_encoder_set_conv: null encoder");
+    return QASR_ERR_INVALID;
+  }
+  cudaSetDevice(e->device);
+  const int CH = kConvHidden, h3 = chunk_tokens(kMelBins);
+  const float *w[3] = {conv1_w, conv2_w, conv3_w}, *b[3] = {conv1_b, conv2_b, conv3_b};
+  const int cin[3] = {1, CH, CH};
+  int rc = QASR_OK;
+  for (int i = 0; i < 3 && !rc; ++i) {
+    rc = enc_copy(e, e->conv_w[i], w[i], (size_t)CH * cin[i] * 9, "conv weight");
+    if (!rc) rc = enc_copy(e, e->conv_b[i], b[i], CH, "conv bias");
+  }
+  if (!rc) rc = enc_copy(e, e->conv_out_w, conv_out_w, (size_t)e->cfg.d_model * CH * h3, "conv_out weight");
+  if (!rc) rc = cuda_status(cudaStreamSynchronize(e->stream), "qasr_encoder_set_conv");
+  return rc;
+}
+
+extern "C" int qasr_encoder_set_layer(qasr_encoder *e, int layer, const qasr_enc_layer_weights *w) {
+  if (!e || !w || layer < 0 || layer >= e->cfg.n_layers) {
+    set_error("qasr_encoder_set_layer: invalid arguments");
+    return QASR_ERR_INVALID;
+  }
+  cudaSetDevice(e->device);
+  const size_t D = e->cfg.d_model, F = e->cfg.ffn_dim;
+  EncLayerDev &L = e->layers[layer];
+  int rc = QASR_OK;
+  struct {
+    float *dst;
+    const float *src;
+    size_t n;
+    const char *what;
+  } items[] = {{L.attn_norm_w, w->attn_norm_w, D, "attn_norm_w"}, {L.attn_norm_b, w->attn_norm_b, D, "attn_norm_b"},
+               {L.wq, w->wq, D * D, "wq"}, {L.bq, w->bq, D, "bq"}, {L.wk, w->wk, D * D, "wk"},
+               {L.bk, w->bk, D, "bk"}, {L.wv, w->wv, D * D, "wv"}, {L.bv, w->bv, D, "bv"},
+               {L.wo, w->wo, D * D, "wo"}, {L.bo, w->bo, D, "bo"}, {L.ffn_norm_w, w->ffn_norm_w, D, "ffn_norm_w"},
+               {L.ffn_norm_b, w->ffn_norm_b, D, "ffn_norm_b"}, {L.fc1_w, w->fc1_w, F * D, "fc1_w"},
+               {L.fc1_b, w->fc1_b, F, "fc1_b"}, {L.fc2_w, w->fc2_w, D * F, "fc2_w"}, {L.fc2_b, w->fc2_b, D, "fc2_b"}};
+  for (auto &it : items)
+    if (!rc) rc = enc_copy(e, it.dst, it.src, it.n, it.what);
+  if (!rc) rc = cuda_status(cudaStreamSynchronize(e->stream), "qasr_encoder_set_layer");
+  return rc;
+}
+
+extern "C" int qasr_encoder_set_post(qasr_encoder *e, const float *ln_post_w, const float *ln_post_b,
+                                     const float *proj1_w, const float *proj1_b, const float *proj2_w,
+                                     const float *proj2_b) {
+  if (!e) {
+    set_error("qasr_encoder_set_post: null encoder");
+    return QASR_ERR_INVALID;
+  }
+  cudaSetDevice(e->device);
+  const size_t D = e->cfg.d_model, O = e->cfg.output_dim;
+  int rc = enc_copy(e, e->ln_post_w, ln_post_w, D, "ln_post_w");
+  if (!rc) rc = enc_copy(e, e->ln_post_b, ln_post_b, D, "ln_post_b");
+  if (!rc) rc = enc_copy(e, e->proj1_w, proj1_w, D * D, "proj1_w");
+  if (!rc) rc = enc_copy(e, e->proj1_b, proj1_b, D, "proj1_b");
+  if (!rc) rc = enc_copy(e, e->proj2_w, proj2_w, O * D, "proj2_w");
+  if (!rc) rc = enc_copy(e, e->proj2_b, proj2_b, O, "proj2_b");
+  if (!rc) rc = cuda_status(cudaStreamSynchronize(e->stream), "qasr_encoder_set_post");
+  return rc;
+}
+
+extern "C" int qasr_encoder_tokens(const qasr_encoder *e, int mel_frames) {
+  if (!e || mel_frames <= 0) return 0;
+  const int cs = e->cfg.chunk_size;
+  int total = 0;
+  for (int s = 0; s < mel_frames; s += cs) total += chunk_tokens(std::min(cs, mel_frames - s));
+  return total;
+}
+
+extern "C" int qasr_encoder_forward(qasr_encoder *e, const float *mel, int mel_frames, float *out, int out_rows,
+                                    int *n_tokens) {
+  if (!e || !mel || !out || mel_frames <= 0) {
+    set_error("qasr_encoder_forward: invalid arguments");
+    return QASR_ERR_INVALID;
+  }
+  cudaSetDevice(e->device);
+  const qasr_encoder_config &c = e->cfg;
+  const int D = c.d_model, F = c.ffn_dim, O = c.output_dim, CH = kConvHidden, cs = c.chunk_size;
+  const int T = qasr_encoder_tokens(e, mel_frames);
+  if (out_rows < T) {
+    set_error("qasr_encoder_forward: output has %d rows, %d tokens needed", out_rows, T);
+    return QASR_ERR_INVALID;
+  }
+  cudaStream_t st = e->stream;
+  int rc = QASR_OK;
+  // buffers
+  const int h1 = (kMelBins + 2 - 3) / 2 + 1, h2 = (h1 + 2 - 3) / 2 + 1, h3 = (h2 + 2 - 3) / 2 + 1;
+  const int w1m = (cs + 2 - 3) / 2 + 1, w2m = (w1m + 2 - 3) / 2 + 1, w3m = (w2m + 2 - 3) / 2 + 1;
+  if (T > e->tok_cap || mel_frames > e->frames_cap) {
+    if ((rc = cuda_status(cudaStreamSynchronize(st), "qasr_encoder_forward"))) return rc;
+    if (e->act) cudaFree(e->act);
+    if (e->conv_buf) cudaFree(e->conv_buf);
+    e->act = e->conv_buf = nullptr;
+    const size_t per_tok = (size_t)7 * D + F + O + D;  // x xn q k v attn proj | mid | out | pe
+    if ((rc = cuda_status(cudaMalloc(&e->act, per_tok * T * 4), "qasr_encoder_forward: buffers"))) return rc;
+    float *f = static_cast<float *>(e->act);
+    auto take = [&](size_t n) { float *r = f; f += n * T; return r; };
+    e->x = take(D);
+    e->xn = take(D);
+    e->q = take(D);
+    e->k = take(D);
+    e->v = take(D);
+    e->attn = take(D);
+    e->proj = take(D);
+    e->mid = take(F);
+    e->out = take(O);
+    e->pe = take(D);
+    const size_t conv_elems = (size_t)kMelBins * cs + (size_t)CH * h1 * w1m + (size_t)CH * h2 * w2m +
+                              (size_t)CH * h3 * w3m + (size_t)w3m * CH * h3;
+    if ((rc = cuda_status(cudaMalloc(&e->conv_buf, conv_elems * 4), "qasr_encoder_forward: conv buffers"))) return rc;
+    f = static_cast<float *>(e->conv_buf);
+    e->mel_chunk = f;
+    f += (size_t)kMelBins * cs;
+    e->c1 = f;
+    f += (size_t)CH * h1 * w1m;
+    e->c2 = f;
+    f += (size_t)CH * h2 * w2m;
+    e->c3 = f;
+    f += (size_t)CH * h3 * w3m;
+    e->reshaped = f;
+    e->tok_cap = T;
+    e->frames_cap = mel_frames;
+  }
+  // ---- conv stem per chunk (encoder.rs:281-348)
+  int tok = 0;
+  for (int s = 0; s < mel_frames && !rc; s += cs) {
+    const int cw = std::min(cs, mel_frames - s);
+    const int w1 = (cw + 2 - 3) / 2 + 1, w2 = (w1 + 2 - 3) / 2 + 1, w3 = (w2 + 2 - 3) / 2 + 1;
+    // chunk_mel [128, cw] from mel [128, mel_frames]
+    rc = cuda_status(cudaMemcpy2DAsync(e->mel_chunk, (size_t)cw * 4, mel + s, (size_t)mel_frames * 4, (size_t)cw * 4,
+                                       kMelBins, cudaMemcpyDefault, st),
+                     "qasr_encoder_forward: mel chunk");
+    if (!rc) rc = qasr_conv2d(e->c1, e->mel_chunk, e->conv_w[0], e->conv_b[0], 1, CH, kMelBins, cw, 3, 3, 2, 1, st);
+    if (!rc) rc = qasr_gelu(e->c1, (int64_t)CH * h1 * w1, st);
+    if (!rc) rc = qasr_conv2d(e->c2, e->c1, e->conv_w[1], e->conv_b[1], CH, CH, h1, w1, 3, 3, 2, 1, st);
+    if (!rc) rc = qasr_gelu(e->c2, (int64_t)CH * h2 * w2, st);
+    if (!rc) rc = qasr_conv2d(e->c3, e->c2, e->conv_w[2], e->conv_b[2], CH, CH, h2, w2, 3, 3, 2, 1, st);
+    if (!rc) rc = qasr_gelu(e->c3, (int64_t)CH * h3 * w3, st);
+    if (!rc) {
+      const long n = (long)CH * h3 * w3;
+      conv_reshape_kernel<<<(int)std::min((n + 255) / 256, 4096l), 256, 0, st>>>(e->reshaped, e->c3, CH * h3, w3);
+      rc = launch_status("qasr_encoder_forward: reshape");
+    }
+    if (!rc) rc = qasr_linear_nobias(e->x + (size_t)tok * D, e->reshaped, e->conv_out_w, w3, CH * h3, D, st);
+    if (!rc) rc = qasr_sinusoidal_pe(e->pe, w3, D, st);
+    if (!rc) rc = qasr_add_inplace(e->x + (size_t)tok * D, e->pe, (int64_t)w3 * D, st);
+    tok += w3;
+  }
+  if (rc) return rc;
+  // ---- attention windows (encoder.rs:350-357)
+  const int tpc = chunk_tokens(cs);
+  const int wsize = tpc * (c.n_window_infer / cs);
+  const int nw = (T + wsize - 1) / wsize;
+  std::vector<int32_t> starts(nw + 1);
+  for (int w = 0; w < nw; ++w) starts[w] = w * wsize;
+  starts[nw] = T;
+  if (nw + 1 > e->win_cap) {
+    if (e->win) cudaFree(e->win);
+    e->win = nullptr;
+    if ((rc = cuda_status(cudaMalloc(&e->win, (nw + 1) * 4), "qasr_encoder_forward: windows"))) return rc;
+    e->win_cap = nw + 1;
+  }
+  if ((rc = cuda_status(cudaMemcpyAsync(e->win, starts.data(), (nw + 1) * 4, cudaMemcpyHostToDevice, st), "windows")))
+    return rc;
+  // the host vector must outlive the copy
+  if ((rc = cuda_status(cudaStreamSynchronize(st), "qasr_encoder_forward"))) return rc;
+  const float scale = 1.0f / sqrtf((float)c.head_dim);
+  const int64_t td = (int64_t)T * D;
+  for (int l = 0; l < c.n_layers && !rc; ++l) {
+    const EncLayerDev &L = e->layers[l];
+    rc = qasr_layer_norm(e->xn, e->x, L.attn_norm_w, L.attn_norm_b, T, D, 1e-5f, st);
+    if (!rc) rc = qasr_linear(e->q, e->xn, L.wq, L.bq, T, D, D, st);
+    if (!rc) rc = qasr_linear(e->k, e->xn, L.wk, L.bk, T, D, D, st);
+    if (!rc) rc = qasr_linear(e->v, e->xn, L.wv, L.bv, T, D, D, st);
+    if (!rc) rc = qasr_bidirectional_attention(e->attn, e->q, e->k, e->v, T, c.n_heads, c.head_dim, scale, e->win, nw, st);
+    if (!rc) rc = qasr_linear(e->proj, e->attn, L.wo, L.bo, T, D, D, st);
+    if (!rc) rc = qasr_add_inplace(e->x, e->proj, td, st);
+    if (!rc) rc = qasr_layer_norm(e->xn, e->x, L.ffn_norm_w, L.ffn_norm_b, T, D, 1e-5f, st);
+    if (!rc) rc = qasr_linear(e->mid, e->xn, L.fc1_w, L.fc1_b, T, D, F, st);
+    if (!rc) rc = qasr_gelu(e->mid, (int64_t)T * F, st);
+    if (!rc) rc = qasr_linear(e->proj, e->mid, L.fc2_w, L.fc2_b, T, F, D, st);
+    if (!rc) rc = qasr_add_inplace(e->x, e->proj, td, st);
+  }
+  // ---- post LayerNorm and projections (encoder.rs:405-415)
+  if (!rc) rc = qasr_layer_norm(e->xn, e->x, e->ln_post_w, e->ln_post_b, T, D, 1e-5f, st);
+  if (!rc) rc = qasr_linear(e->q, e->xn, e->proj1_w, e->proj1_b, T, D, D, st);
+  if (!rc) rc = qasr_gelu(e->q, td, st);
+  if (!rc) rc = qasr_linear(e->out, e->q, e->proj2_w, e->proj2_b, T, D, O, st);
+  if (!rc) rc = cuda_status(cudaMemcpyAsync(out, e->out, (size_t)T * O * 4, cudaMemcpyDefault, st), "encoder output");
+  if (!rc) rc = cuda_status(cudaStreamSynchronize(st), "qasr_encoder_forward");
+  if (!rc && n_tokens) *n_tokens = T;
+  return rc;
+}

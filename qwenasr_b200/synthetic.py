@@ -93,3 +93,34 @@ def layer_weights_gpu(cfg: dict, gen, device, quantize_gpu) -> dict:
     for name, n in (("q_norm", hd), ("k_norm", hd), ("input_norm", H), ("post_attn_norm", H)):
         out[name] = 1.0 + 0.02 * torch.randn(n, generator=gen, device=device, dtype=torch.float32)
     return out
+
+
+# Audio encoder (encoder.rs; 0.6B config: d_model 896, 18 layers, 14 x 64
+# heads, ffn 3584, output = decoder hidden 1024, chunk 100 frames, window 800).
+ENC_0_6B = dict(d_model=896, n_layers=18, n_heads=14, head_dim=64, ffn_dim=3584, output_dim=1024, chunk_size=100,
+                n_window_infer=800)
+CONV_HIDDEN = 480
+
+
+def encoder_weights_np(cfg: dict, seed: int) -> dict:
+    """f32 encoder weights: matrices ~ N(0, 0.02) (conv kernels N(0, 0.05)),
+    LayerNorm weights ~ N(1, 0.02), biases ~ N(0, 0.02)."""
+    rng = np.random.default_rng(seed)
+    D, F, O, CH = cfg["d_model"], cfg["ffn_dim"], cfg["output_dim"], CONV_HIDDEN
+
+    def mat(*shape, s=0.02):
+        return (rng.standard_normal(shape) * s).astype(np.float32)
+
+    def ones(n):
+        return (1 + 0.02 * rng.standard_normal(n)).astype(np.float32)
+
+    w = {"conv1_w": mat(CH, 1, 3, 3, s=0.05), "conv1_b": mat(CH), "conv2_w": mat(CH, CH, 3, 3, s=0.05),
+         "conv2_b": mat(CH), "conv3_w": mat(CH, CH, 3, 3, s=0.05), "conv3_b": mat(CH), "conv_out_w": mat(D, CH * 16),
+         "ln_post_w": ones(D), "ln_post_b": mat(D), "proj1_w": mat(D, D), "proj1_b": mat(D), "proj2_w": mat(O, D),
+         "proj2_b": mat(O), "layers": []}
+    for _ in range(cfg["n_layers"]):
+        w["layers"].append({"attn_norm_w": ones(D), "attn_norm_b": mat(D), "wq": mat(D, D), "bq": mat(D),
+                            "wk": mat(D, D), "bk": mat(D), "wv": mat(D, D), "bv": mat(D), "wo": mat(D, D),
+                            "bo": mat(D), "ffn_norm_w": ones(D), "ffn_norm_b": mat(D), "fc1_w": mat(F, D),
+                            "fc1_b": mat(F), "fc2_w": mat(D, F), "fc2_b": mat(D)})
+    return w
