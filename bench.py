@@ -64,7 +64,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="bounded CPU-baseline sample length")
     ap.add_argument("--seed", type=int, default=1234)
-    ap.add_argument("--workload", choices=("decode", "gemm"), default="decode")
+    ap.add_argument("--workload", choices=("decode", "gemm", "encoder"), default="decode")
     ap.add_argument("--layers", type=int, default=28,
                     help="decoder layers (28 = the configured workload; fewer only for profiler captures)")
     return ap.parse_args()
@@ -480,12 +480,75 @@ def run_gemm(a):
     return 0
 
 
+# ---------------------------------------------------------------- encoder --
+def encoder_flops(cfg, frames):
+    """f32-equivalent multiply-adds x 2 of Encoder::forward for `frames` mel frames."""
+    CH, D, F, O, cs = 480, cfg["d_model"], cfg["ffn_dim"], cfg["output_dim"], cfg["chunk_size"]
+    fl, T = 0.0, 0
+    for s0 in range(0, frames, cs):
+        w = min(cs, frames - s0)
+        h1, w1 = 64, (w - 1) // 2 + 1
+        h2, w2 = 32, (w1 - 1) // 2 + 1
+        h3, w3 = 16, (w2 - 1) // 2 + 1
+        fl += 2.0 * CH * 9 * h1 * w1 + 2.0 * CH * CH * 9 * (h2 * w2 + h3 * w3) + 2.0 * w3 * CH * h3 * D
+        T += w3
+    wsize = 13 * (cfg["n_window_infer"] // cs)
+    att = sum(2.0 * 2 * min(wsize, T - s0) ** 2 * D for s0 in range(0, T, wsize))
+    fl += cfg["n_layers"] * (2.0 * T * (4 * D * D + 2 * D * F) + att) + 2.0 * T * (D * D + D * O)
+    return fl, T
+
+
+def run_encoder(a):
+    import torch
+    from qwenasr_b200 import synthetic
+    from qwenasr_b200.encoder import Encoder
+    torch.cuda.set_device(0)
+    cfg = synthetic.ENC_0_6B
+    frames = 3000  # one 30 s segment: 100 mel frames per second
+    enc = Encoder(cfg, device=0)
+    enc.set_weights(synthetic.encoder_weights_np(cfg, a.seed))
+    mel_h = np.random.default_rng(a.seed).standard_normal((128, frames)).astype(np.float32)
+    mel = torch.from_numpy(mel_h).cuda()
+    for _ in range(max(a.warmup, 3)):
+        enc.forward(mel)
+    torch.cuda.synchronize()
+    times = []
+    with ClockSampler(0) as clk:
+        for _ in range(a.steps):
+            t0 = time.perf_counter()
+            enc.forward(mel)  # synchronous: the engine waits for its stream
+            times.append(time.perf_counter() - t0)
+    # e2e: host mel in, host encoder rows out
+    e2e = []
+    for _ in range(a.steps):
+        t0 = time.perf_counter()
+        enc.forward(mel_h).cpu()
+        e2e.append(time.perf_counter() - t0)
+    s = statistics.median(times)
+    fl, T = encoder_flops(cfg, frames)
+    line = {"metric": "encoder audio seconds per second (Encoder::forward, Qwen3-ASR-0.6B encoder shapes)",
+            "value": 30.0 / s, "unit": "audio-s/s", "n_gpus": 1, "steps": a.steps, "warmup": a.warmup,
+            "ms_per_step": s * 1e3, "higher_is_better": True, "scaling": "none", "vs_baseline": None,
+            "dtype": "f32 (int8 digit planes on tcgen05)", "data": "synthetic (seeded weights, N(0,1) log-mel)",
+            "config": {"workload": "one 30 s segment: 3000 mel frames -> %d tokens, 18 layers" % T},
+            "tflops_f32_equivalent": fl / s / 1e12, "flops_per_step": fl,
+            "e2e": {"value": 30.0 / statistics.median(e2e), "unit": "audio-s/s",
+                    "h2d_bytes_per_step": 128 * frames * 4, "d2h_bytes_per_step": T * cfg["output_dim"] * 4},
+            "timing": "host wall clock around the synchronous forward (median of steps)",
+            "clocks": clk.summary()}
+    enc.close()
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     a = parse()
     if a.impl == "reference":
         return run_reference(a)
     if a.workload == "gemm":
         return run_gemm(a)
+    if a.workload == "encoder":
+        return run_encoder(a)
     return run_ours(a)
 
 
