@@ -16,6 +16,15 @@ collectives are the timing barrier and the max-over-ranks of the timings.
 
 Prints one JSON line on rank 0.
 
+    python bench.py --workload e2e [--gpus N]
+    python bench.py --workload segments [--gpus N]
+
+run the whole transcription path through qasr_transcribe_batch: 30 s of
+synthetic audio per segment -> log-mel -> encoder -> prompt -> prefill ->
+greedy decode (e2e: Qwen3-ASR-0.6B shapes, one segment per GPU, 256 tokens;
+segments: 1.7B shapes, 64 segments split evenly over the GPUs and decoded 8
+at a time, 128 tokens each).  Metric: audio seconds per second (whole job).
+
     python bench.py --workload gemm [--steps K] [--warmup W]
 
 measures the INT8 prefill/encoder projections instead (one GPU): one step =
@@ -56,18 +65,24 @@ def peaks():
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=None, help="timed steps (default 50; 5 for e2e, 3 for segments)")
+    ap.add_argument("--warmup", type=int, default=None, help="warm-up steps (default 5; 3 for e2e / segments)")
     ap.add_argument("--batch", type=int, default=8)
     ap.add_argument("--kv-len", type=int, default=1024)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="bounded CPU-baseline sample length")
     ap.add_argument("--seed", type=int, default=1234)
-    ap.add_argument("--workload", choices=("decode", "gemm", "encoder"), default="decode")
+    ap.add_argument("--workload", choices=("decode", "gemm", "encoder", "e2e", "segments"), default="decode")
     ap.add_argument("--layers", type=int, default=28,
                     help="decoder layers (28 = the configured workload; fewer only for profiler captures)")
-    return ap.parse_args()
+    a = ap.parse_args()
+    long_run = a.workload in ("e2e", "segments")
+    if a.steps is None:
+        a.steps = {"e2e": 5, "segments": 3}.get(a.workload, 50)
+    if a.warmup is None:
+        a.warmup = 3 if long_run else 5
+    return a
 
 
 # ------------------------------------------------------------------ clocks --
@@ -541,6 +556,203 @@ def run_encoder(a):
     return 0
 
 
+# ----------------------------------------------------------- transcription --
+TRANSCRIBE = {
+    "e2e": dict(dec="DEC_0_6B", enc="ENC_0_6B", segments_per_rank=1, seconds=30.0, new=256, batch=1,
+                scaling="weak", desc="BASELINE configs[3]: one 30 s segment per GPU, Qwen3-ASR-0.6B shapes "
+                                     "(INT8 decoder, f32 encoder), 256 greedy tokens"),
+    "segments": dict(dec="DEC_1_7B", enc="ENC_1_7B", segments=64, seconds=30.0, new=128, batch=8,
+                     scaling="strong", desc="BASELINE configs[4]: 64 segments of 30 s split evenly over the GPUs, "
+                                            "Qwen3-ASR-1.7B shapes (INT8 decoder, f32 encoder), 128 greedy tokens "
+                                            "each, 8 segments per decode batch"),
+}
+
+
+def cpu_transcribe_baseline(dcfg, ecfg, seconds, new, seed, budget_s):
+    """The oracle on the host cores, per segment: log-mel and encoder over the
+    whole segment, prefill and decode on a sample of the positions, scaled to
+    the segment's prompt and token counts."""
+    from oracle import pyoracle as orc
+    from qwenasr_b200 import synthetic
+    th = cpu_threads()
+    orc.set_threads(th)
+    audio = synthetic.synthetic_audio(seconds, seed)
+    t0 = time.perf_counter()
+    mel = orc.mel_spectrogram(audio)
+    t_mel = time.perf_counter() - t0
+    we = synthetic.encoder_weights_np(ecfg, seed)
+    t0 = time.perf_counter()
+    rows = orc.encoder_forward(we, ecfg, mel)
+    t_enc = time.perf_counter() - t0
+    del we
+    wd = synthetic.decoder_weights_np(dcfg, seed)
+    od = orc.OracleDecoder(wd)
+    prompt = 15 + rows.shape[0]
+    k, v = od.new_kv(prompt + 8)
+    n_pre = max(1, min(prompt - 1, int(budget_s / 4 / 0.05)))
+    t0 = time.perf_counter()
+    od.prefill(k, v, 0, rows[:n_pre])
+    t_pre = (time.perf_counter() - t0) / n_pre * (prompt - 1)
+    n_dec = 3
+    t0 = time.perf_counter()
+    tok = 198
+    for i in range(n_dec):
+        tok, _, _ = od.forward(k, v, n_pre + i, wd["embed"][tok])
+    t_dec = (time.perf_counter() - t0) / n_dec * new
+    total = t_mel + t_enc + t_pre + t_dec
+    return {"value": seconds / total, "unit": "audio-s/s", "cores": th, "kind": "port",
+            "sample": f"one {seconds:.0f} s segment: oracle log-mel and encoder over all of it "
+                      f"({t_mel:.2f} s + {t_enc:.2f} s), prefill timed on {n_pre} of {prompt - 1} rows and "
+                      f"decode on {n_dec} of {new} steps, both scaled linearly; {th} threads of "
+                      f"{os.cpu_count()} host cores",
+            "phase_s": {"mel": t_mel, "encoder": t_enc, "prefill_est": t_pre, "decode_est": t_dec}}
+
+
+def run_transcribe(a):
+    import torch
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device(f"cuda:{local}"))
+    from qwenasr_b200 import kernels as K
+    from qwenasr_b200 import synthetic
+    from qwenasr_b200.decoder import Decoder
+    from qwenasr_b200.encoder import Encoder
+    from qwenasr_b200.segments import segment_range
+    from qwenasr_b200.transcribe import prompt_len, transcribe_ids
+
+    spec = TRANSCRIBE[a.workload]
+    dcfg = dict(getattr(synthetic, spec["dec"]), n_layers=a.layers)
+    ecfg = getattr(synthetic, spec["enc"])
+    n_seg = spec.get("segments", spec.get("segments_per_rank", 1) * world)
+    mine = list(segment_range(n_seg, rank, world))
+    new, batch, secs = spec["new"], spec["batch"], spec["seconds"]
+    dev = torch.device(f"cuda:{local}")
+    enc = Encoder(ecfg, device=local)
+    enc_tokens = enc.tokens(K.mel_frames(int(secs * 16000)))
+    max_seq = ((prompt_len(enc_tokens) - 1 + new + 63) // 64) * 64
+    dec = Decoder(dcfg, device=local, max_batch=batch, max_seq=max_seq)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(a.seed + 17 * rank)
+
+    def qz(w):
+        q = torch.empty(w.shape, dtype=torch.int8, device=dev)
+        s = torch.empty(w.shape[0], dtype=torch.float32, device=dev)
+        K.quantize_f32_to_int8(w, w.shape[0], w.shape[1], q, s)
+        return q, s
+
+    for i in range(dcfg["n_layers"]):
+        dec.set_layer(i, synthetic.layer_weights_gpu(dcfg, gen, dev, qz))
+    emb = torch.randn(dcfg["vocab"], dcfg["hidden"], generator=gen, device=dev) * 0.02
+    lm, lms = qz(emb)
+    norm = 1.0 + 0.02 * torch.randn(dcfg["hidden"], generator=gen, device=dev)
+    dec.set_globals(emb, norm, lm, lms)
+    del lm, lms, emb
+    enc.set_weights(synthetic.encoder_weights_gpu(ecfg, gen, dev))
+    torch.cuda.synchronize()
+    audio_h = [synthetic.synthetic_audio(secs, a.seed + s) for s in mine]
+    audio_d = [torch.from_numpy(x).to(dev) for x in audio_h]
+    torch.cuda.synchronize()
+
+    def one_pass(src):
+        out = []
+        for b in range(0, len(src), batch):
+            out += transcribe_ids(dec, enc, src[b:b + batch], new)
+        return out
+
+    def barrier():
+        if dist:
+            dist.barrier()
+
+    for _ in range(max(a.warmup, 3)):
+        one_pass(audio_d)
+    st = dec.stream
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        ev0.record(st)
+        for _ in range(a.steps):
+            ids = one_pass(audio_d)
+        ev1.record(st)
+        st.synchronize()
+    torch.cuda.synchronize()
+    barrier()
+    ms = ev0.elapsed_time(ev1) / a.steps
+    # e2e: host samples in (H2D inside the call), host ids out
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        one_pass(audio_h)
+    e2e_ms = (time.perf_counter() - t0) / a.steps * 1e3
+    barrier()
+    # phase split on this rank: everything but the decode loop (one token)
+    t0 = time.perf_counter()
+    for b in range(0, len(audio_d), batch):
+        transcribe_ids(dec, enc, audio_d[b:b + batch], 1)
+    front_ms = (time.perf_counter() - t0) * 1e3
+    t = torch.tensor([ms, e2e_ms], device=dev)
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, e2e_ms = float(t[0]), float(t[1])
+    n_batches = (len(mine) + batch - 1) // batch
+    dec_step_ms = max(ms - front_ms, 1e-6) / max(1, n_batches * (new - 1))
+    mid_pos = np.full(min(batch, len(mine)), prompt_len(enc_tokens) - 1 + new // 2, np.int32)
+    step_bytes = dec.step_bytes(mid_pos)
+    prof = None
+    for _ in range(2):
+        prof = dec.profile_step(np.full(len(mid_pos), 198, np.int32), mid_pos)
+    launches = sum(n for _, n in prof.values()) * n_batches * new * a.steps
+    peak, peak_kind = peaks()
+    line = None
+    if rank == 0:
+        audio_s = n_seg * secs
+        line = {
+            "metric": "audio seconds per second (transcription: log-mel, encoder, prefill, greedy decode)",
+            "value": audio_s / (ms / 1e3), "unit": "audio-s/s", "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": spec["scaling"],
+            "vs_baseline": None, "dtype": "int8xf32 decoder, f32 encoder (int8 digit planes on tcgen05)",
+            "data": "synthetic (pink noise + 3 sinusoids at 16 kHz; seeded random-init weights)",
+            "config": {"workload": spec["desc"], "segments": n_seg, "seconds_per_segment": secs,
+                       "tokens_per_segment": new, "decode_batch": batch, "decoder_layers": dcfg["n_layers"],
+                       "hidden": dcfg["hidden"], "encoder_layers": ecfg["n_layers"],
+                       "parallelism": f"segments split over {world} GPU(s), no collective",
+                       "l2": "decode steps read weights + KV above L2 size; no flush"},
+            "decode_tokens_per_s": n_seg * new / (ms / 1e3),
+            "phase_ms_rank0": {"audio_encoder_prefill_first_token": front_ms,
+                               "decode_rest": ms - front_ms},
+            "e2e": {"value": audio_s / (e2e_ms / 1e3), "unit": "audio-s/s",
+                    "h2d_bytes_per_step": int(sum(x.nbytes for x in audio_h)) * world,
+                    "d2h_bytes_per_step": n_seg * new * 4},
+            "roofline": {"bound": "hbm", "kernel": "decode step (whole graph), estimated from the phase split",
+                         "achieved": step_bytes / (dec_step_ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                         "frac": step_bytes / (dec_step_ms / 1e3) / 1e9 / peak, "traffic": None,
+                         "peak_kind": peak_kind, "bytes_per_step": step_bytes, "ms_per_decode_step": dec_step_ms},
+            "gpu_launches": launches,
+            "gpu_launches_note": "decode-step kernels of rank 0 only; mel, encoder and prefill launches come on top",
+            "timing": "CUDA events on the decoder stream around whole passes (the call is synchronous)",
+            "clocks": clk.summary(),
+            "sample_ids": ids[0][:8],
+        }
+    if dist:
+        dist.barrier()
+    dec.close()
+    enc.close()
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_transcribe_baseline(dcfg, ecfg, secs, new, a.seed, a.cpu_seconds)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     a = parse()
     if a.impl == "reference":
@@ -549,6 +761,8 @@ def main():
         return run_gemm(a)
     if a.workload == "encoder":
         return run_encoder(a)
+    if a.workload in TRANSCRIBE:
+        return run_transcribe(a)
     return run_ours(a)
 
 

@@ -161,6 +161,19 @@ int qasr_bidirectional_attention(float *out, const float *q, const float *k, con
                                  int head_dim, float scale, const int32_t *window_starts, int n_windows,
                                  void *stream);
 
+/* audio::mel_spectrogram (audio.rs:271-385): frames for n_samples 16 kHz
+ * samples (n_samples / 160; 0 = too short, where the reference returns None). */
+int qasr_mel_frames(int n_samples);
+/* mel [128, n_frames] (device) = normalised log-mel of samples [n_samples]
+ * (device): reflect padding of 200, periodic Hann window, 400-point DFT, hop
+ * 160, last frame dropped, 128 Slaney mel bins, log10 with a 1e-10 floor,
+ * clamped at the global max - 8, then (v + 4) / 4.  The power spectrum and
+ * the mel sums follow the reference's f32 operation order exactly; log10 is
+ * correctly rounded (glibc's log10f is within one ulp of it).  The constant
+ * tables are uploaded on the first call per device (do not make that call
+ * under stream capture). */
+int qasr_mel_spectrogram(float *mel, const float *samples, int n_samples, void *stream);
+
 /* kernels::causal_attention (mod.rs:1124-1207): GQA causal attention of
  * seq_q queries at global positions q_offset.. over k/v [seq_k, n_kv*hd].
  * head_dim must be 64 or 128. */
@@ -312,6 +325,13 @@ int qasr_decoder_step_device(qasr_decoder *dec, const int32_t *tokens, const int
 /* The engine's CUDA stream (cudaStream_t) and, after a step, the device
  * pointer of the last step's logits [M, vocab] (NULL unless enabled). */
 void *qasr_decoder_stream(qasr_decoder *dec);
+/* The configuration and device the engine was created with (NULL / -1 for NULL). */
+const qasr_decoder_config *qasr_decoder_get_config(const qasr_decoder *dec);
+int qasr_decoder_device(const qasr_decoder *dec);
+/* QwenCtx::tok_embed_to_f32 (context.rs:115-124) for n host ids: rows of
+ * the engine's embedding table (dequantised when INT8) into out [n, hidden]
+ * (device).  Ids outside [0, vocab) are rejected.  Synchronous. */
+int qasr_decoder_embed(qasr_decoder *dec, const int32_t *ids, int n, float *out);
 int qasr_decoder_keep_logits(qasr_decoder *dec, int enable);
 const float *qasr_decoder_logits(qasr_decoder *dec);
 
@@ -380,12 +400,37 @@ int qasr_encoder_set_post(qasr_encoder *enc, const float *ln_post_w, const float
 
 /* Encoder tokens produced for mel_frames frames (13 per full 100-frame chunk). */
 int qasr_encoder_tokens(const qasr_encoder *enc, int mel_frames);
+const qasr_encoder_config *qasr_encoder_get_config(const qasr_encoder *enc);
+int qasr_encoder_device(const qasr_encoder *enc);
 
 /* Encoder::forward (encoder.rs:243-415): mel [128, mel_frames] f32 (host or
  * device) -> out [n_tokens, output_dim] (host or device, out_rows >= n_tokens).
  * Synchronous. */
 int qasr_encoder_forward(qasr_encoder *enc, const float *mel, int mel_frames, float *out, int out_rows,
                          int *n_tokens);
+
+/* ======================================================================
+ * Transcription (transcribe.rs), token ids out
+ * ==================================================================== */
+
+/* Prompt rows of a segment with n_audio_tokens encoder rows: PREFIX_HEAD (3)
+ * + n_prompt + PREFIX_TAIL (6) + audio + SUFFIX_BASE (6) + n_force. */
+int qasr_transcribe_prompt_len(int n_audio_tokens, int n_prompt, int n_force);
+
+/* transcribe_segment (transcribe.rs:67-244) for n_segments (<= the decoder's
+ * max_batch) independent segments at once, decoded as one batch (the
+ * segmented mode, transcribe.rs:354-420, without past-text conditioning):
+ * samples[i] (host or device, 16 kHz f32, n_samples[i] >= 160) -> log-mel ->
+ * encoder -> prompt embeddings with the reference's special tokens and the
+ * optional prompt / forced-language ids -> prefill into KV slot i -> greedy
+ * decode.  ids[i * ids_stride + j] (host) receives generated token j of
+ * segment i, n_ids[i] how many: max_new, or when stop_at_eos is set up to and
+ * including the first <|endoftext|> / <|im_end|>.  The encoder's output size
+ * must equal the decoder's hidden size and both engines must be on one
+ * device.  Synchronous. */
+int qasr_transcribe_batch(qasr_decoder *dec, qasr_encoder *enc, const float *const *samples, const int *n_samples,
+                          int n_segments, const int32_t *prompt_tokens, int n_prompt, const int32_t *force_tokens,
+                          int n_force, int max_new, int stop_at_eos, int32_t *ids, int ids_stride, int *n_ids);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

@@ -96,6 +96,8 @@ extern "C" {
     pub fn qasr_matmul_t(c: *mut f32, a: *const f32, b: *const f32, m: c_int, k: c_int, n: c_int, stream: *mut c_void) -> c_int;
     pub fn qasr_conv2d(out: *mut f32, input: *const f32, weight: *const f32, bias: *const f32, c_in: c_int, c_out: c_int, h_in: c_int, w_in: c_int, kh: c_int, kw: c_int, stride: c_int, padding: c_int, stream: *mut c_void) -> c_int;
     pub fn qasr_bidirectional_attention(out: *mut f32, q: *const f32, k: *const f32, v: *const f32, seq: c_int, n_heads: c_int, head_dim: c_int, scale: f32, window_starts: *const i32, n_windows: c_int, stream: *mut c_void) -> c_int;
+    pub fn qasr_mel_frames(n_samples: c_int) -> c_int;
+    pub fn qasr_mel_spectrogram(mel: *mut f32, samples: *const f32, n_samples: c_int, stream: *mut c_void) -> c_int;
     pub fn qasr_causal_attention(out: *mut f32, q: *const f32, k: *const f32, v: *const f32, seq_q: c_int, seq_k: c_int, n_heads: c_int, n_kv_heads: c_int, head_dim: c_int, scale: f32, q_offset: c_int, stream: *mut c_void) -> c_int;
     pub fn qasr_quantize_f32_to_int8(data: *const f32, out_dim: i64, in_dim: i64, q: *mut i8, scales: *mut f32, stream: *mut c_void) -> c_int;
     pub fn qasr_embed_gather_f32(dst: *mut f32, table: *const f32, ids: *const i32, n: c_int, dim: c_int, vocab: i64, bad_id_flag: *mut c_int, stream: *mut c_void) -> c_int;
@@ -116,6 +118,9 @@ extern "C" {
     pub fn qasr_decoder_prefill_hidden(dec: *mut QasrDecoder) -> *const f32;
     pub fn qasr_decoder_step_device(dec: *mut QasrDecoder, tokens: *const i32, positions: *const i32, M: c_int, next_tokens: *mut i32) -> c_int;
     pub fn qasr_decoder_stream(dec: *mut QasrDecoder) -> *mut c_void;
+    pub fn qasr_decoder_get_config(dec: *const QasrDecoder) -> *const QasrDecoderConfig;
+    pub fn qasr_decoder_device(dec: *const QasrDecoder) -> c_int;
+    pub fn qasr_decoder_embed(dec: *mut QasrDecoder, ids: *const i32, n: c_int, out: *mut f32) -> c_int;
     pub fn qasr_decoder_keep_logits(dec: *mut QasrDecoder, enable: c_int) -> c_int;
     pub fn qasr_decoder_logits(dec: *mut QasrDecoder) -> *const f32;
     pub fn qasr_decoder_profile_step(dec: *mut QasrDecoder, tokens: *const i32, positions: *const i32, M: c_int, class_ms: *mut f32, class_launches: *mut c_int, n_classes: c_int) -> c_int;
@@ -126,5 +131,9 @@ extern "C" {
     pub fn qasr_encoder_set_layer(enc: *mut QasrEncoder, layer: c_int, w: *const QasrEncLayerWeights) -> c_int;
     pub fn qasr_encoder_set_post(enc: *mut QasrEncoder, ln_post_w: *const f32, ln_post_b: *const f32, proj1_w: *const f32, proj1_b: *const f32, proj2_w: *const f32, proj2_b: *const f32) -> c_int;
     pub fn qasr_encoder_tokens(enc: *const QasrEncoder, mel_frames: c_int) -> c_int;
+    pub fn qasr_encoder_get_config(enc: *const QasrEncoder) -> *const QasrEncoderConfig;
+    pub fn qasr_encoder_device(enc: *const QasrEncoder) -> c_int;
     pub fn qasr_encoder_forward(enc: *mut QasrEncoder, mel: *const f32, mel_frames: c_int, out: *mut f32, out_rows: c_int, n_tokens: *mut c_int) -> c_int;
+    pub fn qasr_transcribe_prompt_len(n_audio_tokens: c_int, n_prompt: c_int, n_force: c_int) -> c_int;
+    pub fn qasr_transcribe_batch(dec: *mut QasrDecoder, enc: *mut QasrEncoder, samples: *mut *const f32, n_samples: *const c_int, n_segments: c_int, prompt_tokens: *const i32, n_prompt: c_int, force_tokens: *const i32, n_force: c_int, max_new: c_int, stop_at_eos: c_int, ids: *mut i32, ids_stride: c_int, n_ids: *mut c_int) -> c_int;
 }

@@ -786,4 +786,112 @@ void orc_pre_attn_block(float *x_norm, const float *x, const float *w_in, int se
   }
 }
 
+// --------------------------------------------------------------------------
+// Log-mel front end (audio.rs:202-385).  Every table is built with the same
+// f32 expression order and the same libm calls (logf, expf, cosf, sinf,
+// log10f) as the reference; sums are sequential (Rust does not reassociate
+// or contract them).
+// --------------------------------------------------------------------------
+static float orc_hz_to_mel(float hz) {  // audio.rs:202-213 (Slaney scale)
+  const float log_step = 27.0f / logf(6.4f);
+  if (hz >= 1000.0f) return 15.0f + logf(hz / 1000.0f) * log_step;
+  return 3.0f * hz / 200.0f;
+}
+
+static float orc_mel_to_hz(float mel) {  // audio.rs:215-224
+  const float log_step = logf(6.4f) / 27.0f;
+  if (mel >= 15.0f) return 1000.0f * expf(log_step * (mel - 15.0f));
+  return 200.0f * mel / 3.0f;
+}
+
+// filters [128, 201]: triangular Slaney-normalised filters (audio.rs:226-263).
+void orc_mel_filters(float *filters) {
+  const int nf = ORC_MEL_FREQS, nm = ORC_MEL_BINS;
+  std::vector<float> bin_hz(nf), edge_hz(nm + 2), width(nm + 1);
+  for (int f = 0; f < nf; ++f) bin_hz[f] = (float)f * (16000.0f / 2.0f) / (float)(nf - 1);
+  const float lo = orc_hz_to_mel(0.0f), hi = orc_hz_to_mel(8000.0f);
+  for (int i = 0; i < nm + 2; ++i) edge_hz[i] = orc_mel_to_hz(lo + (hi - lo) * (float)i / (float)(nm + 1));
+  for (int i = 0; i < nm + 1; ++i) {
+    width[i] = edge_hz[i + 1] - edge_hz[i];
+    if (width[i] == 0.0f) width[i] = 1e-6f;
+  }
+  for (int m = 0; m < nm; ++m) {
+    const float norm = 2.0f / (edge_hz[m + 2] - edge_hz[m]);
+    for (int f = 0; f < nf; ++f) {
+      const float rise = (bin_hz[f] - edge_hz[m]) / width[m];
+      const float fall = (edge_hz[m + 2] - bin_hz[f]) / width[m + 1];
+      filters[(size_t)m * nf + f] = std::max(std::min(rise, fall), 0.0f) * norm;
+    }
+  }
+}
+
+// window [400] (periodic Hann), cos_t / sin_t [201, 400] DFT rows (audio.rs:303-325).
+void orc_mel_tables(float *window, float *cos_t, float *sin_t) {
+  const float two_pi = 2.0f * 3.14159265358979323846f;
+  for (int i = 0; i < ORC_MEL_NFFT; ++i) window[i] = 0.5f * (1.0f - cosf(two_pi * (float)i / (float)ORC_MEL_NFFT));
+  for (int k = 0; k < ORC_MEL_FREQS; ++k)
+    for (int n = 0; n < ORC_MEL_NFFT; ++n) {
+      const float angle = two_pi * (float)k * (float)n / (float)ORC_MEL_NFFT;
+      cos_t[(size_t)k * ORC_MEL_NFFT + n] = cosf(angle);
+      sin_t[(size_t)k * ORC_MEL_NFFT + n] = sinf(angle);
+    }
+}
+
+int orc_mel_frames(int n_samples) { return n_samples > 0 ? n_samples / ORC_MEL_HOP : 0; }
+
+// Sample g of the reflect-padded signal (audio.rs:277-287): 200 samples
+// mirrored about samples[0] in front, 200 mirrored about samples[n-1] behind,
+// zero where the mirror runs off a short input.
+static float orc_padded_sample(const float *s, int n, long g) {
+  const int pad = ORC_MEL_NFFT / 2;
+  if (g < pad) {
+    const long src = pad - g;
+    return src < n ? s[src] : 0.0f;
+  }
+  if (g < pad + n) return s[g - pad];
+  const long src = (long)n - 2 - (g - pad - n);
+  return src >= 0 ? s[src] : 0.0f;
+}
+
+// mel [128, n_frames] = (max(log10(mel power), global max - 8) + 4) / 4.
+// Returns n_frames, 0 if the input is too short for one frame.
+int orc_mel_spectrogram(float *mel, const float *samples, int n_samples) {
+  const int n_frames = orc_mel_frames(n_samples);
+  if (n_frames <= 0) return 0;
+  const int NF = ORC_MEL_NFFT, NK = ORC_MEL_FREQS, NM = ORC_MEL_BINS;
+  std::vector<float> filt((size_t)NM * NK), win(NF), ct((size_t)NK * NF), st((size_t)NK * NF);
+  orc_mel_filters(filt.data());
+  orc_mel_tables(win.data(), ct.data(), st.data());
+  std::vector<float> logmel((size_t)n_frames * NM), frame(NF), power(NK);
+  float top = -1e30f;
+  for (int t = 0; t < n_frames; ++t) {
+    for (int i = 0; i < NF; ++i) frame[i] = orc_padded_sample(samples, n_samples, (long)t * ORC_MEL_HOP + i) * win[i];
+    for (int k = 0; k < NK; ++k) {
+      float re = 0.0f, im = 0.0f;
+      const float *c = &ct[(size_t)k * NF], *s = &st[(size_t)k * NF];
+      for (int i = 0; i < NF; ++i) {
+        re += frame[i] * c[i];
+        im += frame[i] * s[i];
+      }
+      power[k] = re * re + im * im;
+    }
+    for (int m = 0; m < NM; ++m) {
+      const float *f = &filt[(size_t)m * NK];
+      float acc = 0.0f;
+      for (int k = 0; k < NK; ++k) acc += f[k] * power[k];
+      if (acc < 1e-10f) acc = 1e-10f;
+      const float v = log10f(acc);
+      logmel[(size_t)t * NM + m] = v;
+      if (v > top) top = v;
+    }
+  }
+  const float floor_v = top - 8.0f;
+  for (int t = 0; t < n_frames; ++t)
+    for (int m = 0; m < NM; ++m) {
+      const float v = std::max(logmel[(size_t)t * NM + m], floor_v);
+      mel[(size_t)m * n_frames + t] = (v + 4.0f) / 4.0f;
+    }
+  return n_frames;
+}
+
 }  // extern "C"

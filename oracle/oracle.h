@@ -125,6 +125,16 @@ void orc_pre_attn_block(float *x_norm, const float *x, const float *w_in, int se
                         const float *cos_tab, const float *sin_tab, int start_pos,
                         float *k_cache, float *v_cache);
 
+/* ---- log-mel front end (audio.rs:202-385): 16 kHz, 400-point DFT, hop 160, 128 Slaney bins ---- */
+#define ORC_MEL_NFFT 400
+#define ORC_MEL_FREQS 201
+#define ORC_MEL_HOP 160
+#define ORC_MEL_BINS 128
+void orc_mel_filters(float *filters);                              /* [128, 201] */
+void orc_mel_tables(float *window, float *cos_t, float *sin_t);     /* [400], [201, 400] x2 */
+int orc_mel_frames(int n_samples);
+int orc_mel_spectrogram(float *mel, const float *samples, int n_samples);  /* mel [128, n_frames] */
+
 #ifdef __cplusplus
 }
 #endif

@@ -12,6 +12,7 @@ where noted).
 from __future__ import annotations
 
 import ctypes as C
+import math
 import os
 import subprocess
 
@@ -384,3 +385,92 @@ def pre_attn_block(x, w_in, q, k, v, q_norm_w, k_norm_w, n_heads, n_kv_heads, he
                              C.c_float(eps), _p(_f32(cos_tab)), _p(_f32(sin_tab)), start_pos,
                              _p(k_cache), _p(v_cache))
     return xn, q, k
+
+
+MEL_BINS, MEL_FREQS, MEL_NFFT, MEL_HOP = 128, 201, 400, 160
+
+
+def mel_filters():
+    """build_mel_filters (audio.rs:226-263): Slaney filters [128, 201]."""
+    f = np.empty((MEL_BINS, MEL_FREQS), np.float32)
+    lib().orc_mel_filters(_p(f))
+    return f
+
+
+def mel_tables():
+    """The periodic Hann window [400] and DFT cos/sin rows [201, 400] (audio.rs:303-325)."""
+    w = np.empty(MEL_NFFT, np.float32)
+    c = np.empty((MEL_FREQS, MEL_NFFT), np.float32)
+    s = np.empty((MEL_FREQS, MEL_NFFT), np.float32)
+    lib().orc_mel_tables(_p(w), _p(c), _p(s))
+    return w, c, s
+
+
+def mel_spectrogram(samples):
+    """audio::mel_spectrogram (audio.rs:271-385): [128, n_frames] log-mel of
+    16 kHz samples, or None when the input is too short for one frame."""
+    x = _f32(samples).ravel()
+    n_frames = len(x) // MEL_HOP
+    if n_frames == 0:
+        return None
+    mel = np.empty((MEL_BINS, n_frames), np.float32)
+    got = lib().orc_mel_spectrogram(_p(mel), _p(x), len(x))
+    assert got == n_frames
+    return mel
+
+
+# ------------------------------------------------------------ encoder --
+_CONV_HIDDEN = 480
+
+
+def _conv3x3s2(x, w, b, c_in, c_out, h, wd):
+    """kernels::conv2d (mod.rs:790-860) with a 3x3 kernel, stride 2, padding 1:
+    an im2col product in float64 (cblas_sgemm's stand-in)."""
+    ho, wo = (h - 1) // 2 + 1, (wd - 1) // 2 + 1
+    xp = np.zeros((c_in, h + 2, wd + 2))
+    xp[:, 1:1 + h, 1:1 + wd] = x.reshape(c_in, h, wd)
+    cols = np.empty((c_in * 9, ho * wo))
+    for ic in range(c_in):
+        for ki in range(3):
+            for kj in range(3):
+                cols[(ic * 3 + ki) * 3 + kj] = xp[ic, ki:ki + 2 * ho:2, kj:kj + 2 * wo:2].ravel()
+    return ((w.reshape(c_out, -1).astype(np.float64) @ cols) + b[:, None]).astype(np.float32), ho, wo
+
+
+def encoder_forward(w, cfg, mel):
+    """Encoder::forward (encoder.rs:243-415) composed from the restated
+    kernels: per 100-frame chunk the conv stem (3 x conv + GELU), conv_out
+    and the sinusoidal positions; windowed layers; post LayerNorm and the two
+    projections.  mel [128, frames] -> [tokens, output_dim]."""
+    D, CH, cs = cfg["d_model"], _CONV_HIDDEN, cfg["chunk_size"]
+    frames = mel.shape[1]
+    xs = []
+    for s in range(0, frames, cs):
+        chunk = mel[:, s:s + cs]
+        c1, h1, w1 = _conv3x3s2(chunk, w["conv1_w"], w["conv1_b"], 1, CH, 128, chunk.shape[1])
+        c1 = gelu(c1.ravel()).reshape(c1.shape)
+        c2, h2, w2 = _conv3x3s2(c1, w["conv2_w"], w["conv2_b"], CH, CH, h1, w1)
+        c2 = gelu(c2.ravel()).reshape(c2.shape)
+        c3, h3, w3 = _conv3x3s2(c2, w["conv3_w"], w["conv3_b"], CH, CH, h2, w2)
+        c3 = gelu(c3.ravel()).reshape(CH, h3, w3)
+        reshaped = np.ascontiguousarray(c3.transpose(2, 0, 1).reshape(w3, CH * h3))
+        xs.append(linear(reshaped, w["conv_out_w"]) + sinusoidal_pe(w3, D))
+    x = np.concatenate(xs).astype(np.float32)
+    T = x.shape[0]
+    tpc = 13
+    wsize = tpc * (cfg["n_window_infer"] // cs)
+    starts = np.array(list(range(0, T, wsize)) + [T], np.int32)
+    scale = np.float32(1.0 / math.sqrt(cfg["head_dim"]))
+    for L in w["layers"]:
+        xn = layer_norm(x, L["attn_norm_w"], L["attn_norm_b"], 1e-5)
+        q = linear(xn, L["wq"], L["bq"])
+        k = linear(xn, L["wk"], L["bk"])
+        v = linear(xn, L["wv"], L["bv"])
+        a = bidirectional_attention(q, k, v, T, cfg["n_heads"], cfg["head_dim"], starts, scale)
+        x = (x + linear(a, L["wo"], L["bo"])).astype(np.float32)
+        xn = layer_norm(x, L["ffn_norm_w"], L["ffn_norm_b"], 1e-5)
+        mid = gelu(linear(xn, L["fc1_w"], L["fc1_b"]).ravel()).reshape(T, -1)
+        x = (x + linear(mid, L["fc2_w"], L["fc2_b"])).astype(np.float32)
+    xn = layer_norm(x, w["ln_post_w"], w["ln_post_b"], 1e-5)
+    p1 = gelu(linear(xn, w["proj1_w"], w["proj1_b"]).ravel()).reshape(T, -1)
+    return linear(p1, w["proj2_w"], w["proj2_b"])

@@ -69,6 +69,8 @@ _SIGS = {
     "qasr_matmul_t": (I, [P, P, P, I, I, I, P]),
     "qasr_conv2d": (I, [P, P, P, P, I, I, I, I, I, I, I, I, P]),
     "qasr_bidirectional_attention": (I, [P, P, P, P, I, I, I, F, P, I, P]),
+    "qasr_mel_frames": (I, [I]),
+    "qasr_mel_spectrogram": (I, [P, P, I, P]),
     "qasr_quantize_f32_to_int8": (I, [P, I64, I64, P, P, P]),
     "qasr_embed_gather_f32": (I, [P, P, P, I, I, I64, P, P]),
     "qasr_embed_gather_int8": (I, [P, P, P, P, I, I, I64, P, P]),
@@ -88,6 +90,9 @@ _SIGS = {
     "qasr_decoder_prefill_hidden": (P, [P]),
     "qasr_decoder_step_device": (I, [P, P, P, I, P]),
     "qasr_decoder_stream": (P, [P]),
+    "qasr_decoder_get_config": (P, [P]),
+    "qasr_decoder_device": (I, [P]),
+    "qasr_decoder_embed": (I, [P, P, I, P]),
     "qasr_decoder_keep_logits": (I, [P, I]),
     "qasr_decoder_logits": (P, [P]),
     "qasr_decoder_step_bytes": (I64, [P, P, I]),
@@ -113,6 +118,10 @@ _SIGS.update({
     "qasr_encoder_set_post": (I, [P, P, P, P, P, P, P]),
     "qasr_encoder_tokens": (I, [P, I]),
     "qasr_encoder_forward": (I, [P, P, I, P, I, C.POINTER(C.c_int)]),
+    "qasr_encoder_get_config": (P, [P]),
+    "qasr_encoder_device": (I, [P]),
+    "qasr_transcribe_prompt_len": (I, [I, I, I]),
+    "qasr_transcribe_batch": (I, [P, P, P, P, I, P, I, P, I, I, I, P, I, P]),
 })
 
 KERNEL_CLASSES = ("embed", "norm", "qkv", "qkv_post", "attn", "oproj", "gateup", "down", "lmhead")

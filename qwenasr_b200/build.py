@@ -5,7 +5,9 @@
 Each .cu under csrc/ is compiled to an object in csrc/_build/ (in parallel),
 then linked into qwenasr_b200/libqwenasr_b200.so.  --fmad=false keeps nvcc
 from contracting a*b+c into FMAs the source did not ask for (the kernels
-reproduce the reference's rounding sequence).  No GPU is needed to build.
+reproduce the reference's rounding sequence); -ffp-contract=off does the same
+for host code (the log-mel tables are built on the host).  No GPU is needed
+to build.
 """
 from __future__ import annotations
 
@@ -25,7 +27,7 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "--fmad=false", "-std=c++17", "-Xcompiler", "-fPIC",
-                     "-Xcompiler", "-fvisibility=hidden", "--expt-relaxed-constexpr", f"-I{INCLUDE}"]
+                     "-Xcompiler", "-fvisibility=hidden", "-Xcompiler", "-ffp-contract=off", "--expt-relaxed-constexpr", f"-I{INCLUDE}"]
 
 
 def _sources():

@@ -72,6 +72,8 @@ struct qasr_decoder {
   float *pf_x = nullptr, *pf_xn = nullptr, *pf_q = nullptr, *pf_k = nullptr, *pf_v = nullptr, *pf_attn = nullptr,
         *pf_proj = nullptr, *pf_gu = nullptr, *pf_h = nullptr;
   void *pf_block = nullptr;
+  int32_t *emb_ids = nullptr;  // device ids of qasr_decoder_embed, grown on demand
+  int emb_cap = 0;
   std::vector<cudaGraphExec_t> graphs;  // per M (index M), built lazily
   std::vector<void *> allocs;
   long seq_stride() const { return (long)cfg.n_layers * cfg.max_seq * cfg.n_kv_heads * cfg.head_dim; }
@@ -133,6 +135,7 @@ extern "C" void qasr_decoder_free(qasr_decoder *d) {
     if (g) cudaGraphExecDestroy(g);
   for (void *p : d->allocs) cudaFree(p);
   if (d->pf_block) cudaFree(d->pf_block);
+  if (d->emb_ids) cudaFree(d->emb_ids);
   if (d->h_tok) cudaFreeHost(d->h_tok);
   if (d->stream) cudaStreamDestroy(d->stream);
   delete d;
@@ -620,6 +623,45 @@ extern "C" int qasr_decoder_prefill(qasr_decoder *d, int slot, const float *embe
   }
   if (!rc) rc = cuda_status(cudaStreamSynchronize(st), "qasr_decoder_prefill");
   return rc;
+}
+
+extern "C" const qasr_decoder_config *qasr_decoder_get_config(const qasr_decoder *d) { return d ? &d->cfg : nullptr; }
+extern "C" int qasr_decoder_device(const qasr_decoder *d) { return d ? d->device : -1; }
+
+// QwenCtx::tok_embed_to_f32 (context.rs:115-124) for n host ids: rows of the
+// engine's embedding table (dequantised when INT8) into out [n, hidden].
+extern "C" int qasr_decoder_embed(qasr_decoder *d, const int32_t *ids, int n, float *out) {
+  if (!d || !ids || !out || n <= 0) {
+    set_error("qasr_decoder_embed: invalid arguments");
+    return QASR_ERR_INVALID;
+  }
+  if (!d->globals_ready) {
+    set_error("qasr_decoder_embed: qasr_decoder_set_globals has not succeeded");
+    return QASR_ERR_INVALID;
+  }
+  const qasr_decoder_config &c = d->cfg;
+  for (int i = 0; i < n; ++i)
+    if (ids[i] < 0 || ids[i] >= c.vocab) {
+      set_error("qasr_decoder_embed: id %d (index %d) outside [0,%d)", ids[i], i, c.vocab);
+      return QASR_ERR_INVALID;
+    }
+  cudaSetDevice(d->device);
+  cudaStream_t st = d->stream;
+  int rc = QASR_OK;
+  if (n > d->emb_cap) {
+    if ((rc = cuda_status(cudaStreamSynchronize(st), "qasr_decoder_embed"))) return rc;
+    if (d->emb_ids) cudaFree(d->emb_ids);
+    d->emb_ids = nullptr;
+    d->emb_cap = 0;
+    if ((rc = cuda_status(cudaMalloc(&d->emb_ids, (size_t)std::max(n, 64) * 4), "qasr_decoder_embed: ids"))) return rc;
+    d->emb_cap = std::max(n, 64);
+  }
+  if ((rc = cuda_status(cudaMemcpyAsync(d->emb_ids, ids, (size_t)n * 4, cudaMemcpyHostToDevice, st), "embed ids")))
+    return rc;
+  step_embed_kernel<<<n, 256, 0, st>>>(out, d->embed, d->embed_s, c.embed_is_int8, d->emb_ids, c.hidden, c.vocab,
+                                       d->err);
+  if ((rc = launch_status("qasr_decoder_embed"))) return rc;
+  return cuda_status(cudaStreamSynchronize(st), "qasr_decoder_embed");
 }
 
 // Residual stream after the last prefill (device, [seq, hidden]); NULL before one.

@@ -216,6 +216,9 @@ extern "C" int qasr_encoder_set_post(qasr_encoder *e, const float *ln_post_w, co
   return rc;
 }
 
+extern "C" const qasr_encoder_config *qasr_encoder_get_config(const qasr_encoder *e) { return e ? &e->cfg : nullptr; }
+extern "C" int qasr_encoder_device(const qasr_encoder *e) { return e ? e->device : -1; }
+
 extern "C" int qasr_encoder_tokens(const qasr_encoder *e, int mel_frames) {
   if (!e || mel_frames <= 0) return 0;
   const int cs = e->cfg.chunk_size;

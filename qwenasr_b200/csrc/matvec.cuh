@@ -91,7 +91,9 @@ int argmax_scratch(unsigned long long **keys, unsigned **counter);
 int mv_norm_scratch(float **buf, size_t n_floats);
 
 constexpr int kScratchPartial = 0, kScratchCounter = 1, kScratchDigits = 2, kScratchDigitScale = 3,
-              kScratchWeightDigits = 4, kScratchWeightScale = 5, kScratchIm2col = 6, kScratchSlots = 7;
+              kScratchWeightDigits = 4, kScratchWeightScale = 5, kScratchIm2col = 6, kScratchMelPower = 7,
+              kScratchMelMax = 8, kScratchAudio = 9, kScratchMelOut = 10, kScratchEncOut = 11,
+              kScratchPrompt = 12, kScratchDecode = 13, kScratchSlots = 14;
 int dev_scratch(int slot, size_t bytes, void **out);
 
 }  // namespace qasr

@@ -1,0 +1,170 @@
+// transcribe.cu -- transcribe_segment (crates/qwen-asr/src/transcribe.rs:67-244)
+// on the device, token ids out (the host keeps its tokenizer):
+//
+//   samples -> qasr_mel_spectrogram -> qasr_encoder_forward -> prompt
+//   embeddings (PREFIX_HEAD, prompt, PREFIX_TAIL, audio rows, SUFFIX_BASE,
+//   forced tokens; transcribe.rs:11-13, 98-170) -> qasr_decoder_prefill of
+//   all but the last prompt row -> greedy decode from the last prompt token.
+//
+// Up to max_batch independent segments run together (the segmented mode,
+// transcribe.rs:354-420, with past_text_conditioning off): each is encoded
+// and prefilled into its own KV slot, then all decode in one batched step.
+// The decode loop keeps the ids on the device: step s reads step s-1's
+// argmax as its tokens and a precomputed position row, so consecutive steps
+// are enqueued back to back with no host round trip; the host looks at the
+// ids only every kCheckEvery steps, when stopping at end-of-text.
+#include <algorithm>
+#include <cstring>
+#include <vector>
+
+#include "common.cuh"
+#include "matvec.cuh"
+#include "qwenasr_cuda.h"
+
+namespace qasr {
+namespace {
+
+// transcribe.rs:11-13
+const int32_t kPrefixHead[] = {151644, 8948, 198};
+const int32_t kPrefixTail[] = {151645, 198, 151644, 872, 198, 151669};
+const int32_t kSuffixBase[] = {151670, 151645, 198, 151644, 77091, 198};
+constexpr int32_t kEndOfText = 151643, kImEnd = 151645;  // config.rs:14-15
+constexpr int kHead = 3, kTail = 6, kSuffix = 6;
+constexpr int kCheckEvery = 32;
+
+bool is_stop(int32_t t) { return t == kEndOfText || t == kImEnd; }
+
+}  // namespace
+}  // namespace qasr
+
+using namespace qasr;
+
+extern "C" int qasr_transcribe_prompt_len(int n_audio_tokens, int n_prompt, int n_force) {
+  if (n_audio_tokens < 0 || n_prompt < 0 || n_force < 0) return 0;
+  return kHead + n_prompt + kTail + n_audio_tokens + kSuffix + n_force;
+}
+
+extern "C" int qasr_transcribe_batch(qasr_decoder *dec, qasr_encoder *enc, const float *const *samples,
+                                     const int *n_samples, int n_segments, const int32_t *prompt_tokens, int n_prompt,
+                                     const int32_t *force_tokens, int n_force, int max_new, int stop_at_eos,
+                                     int32_t *ids, int ids_stride, int *n_ids) {
+  const qasr_decoder_config *dc = qasr_decoder_get_config(dec);
+  const qasr_encoder_config *ec = qasr_encoder_get_config(enc);
+  if (!dc || !ec || !samples || !n_samples || !ids || !n_ids || n_segments <= 0 || n_segments > dc->max_batch ||
+      max_new <= 0 || ids_stride < max_new || n_prompt < 0 || n_force < 0 || (n_prompt && !prompt_tokens) ||
+      (n_force && !force_tokens)) {
+    set_error("qasr_transcribe_batch: invalid arguments (%d segments, max_new %d)", n_segments, max_new);
+    return QASR_ERR_INVALID;
+  }
+  if (ec->output_dim != dc->hidden) {
+    set_error("qasr_transcribe_batch: encoder output %d != decoder hidden %d", ec->output_dim, dc->hidden);
+    return QASR_ERR_INVALID;
+  }
+  const int dev = qasr_decoder_device(dec);
+  if (qasr_encoder_device(enc) != dev) {
+    set_error("qasr_transcribe_batch: encoder on device %d, decoder on device %d", qasr_encoder_device(enc), dev);
+    return QASR_ERR_INVALID;
+  }
+  if (int rc = cuda_status(cudaSetDevice(dev), "qasr_transcribe_batch")) return rc;
+  const int H = dc->hidden, M = n_segments;
+  int max_samples = 0, max_tokens = 0;
+  for (int i = 0; i < M; ++i) {
+    const int frames = qasr_mel_frames(n_samples[i]);
+    if (!samples[i] || frames <= 0) {
+      set_error("qasr_transcribe_batch: segment %d has %d samples (at least 160 needed)", i, n_samples[i]);
+      return QASR_ERR_INVALID;
+    }
+    max_samples = std::max(max_samples, n_samples[i]);
+    max_tokens = std::max(max_tokens, qasr_encoder_tokens(enc, frames));
+    const int total = qasr_transcribe_prompt_len(qasr_encoder_tokens(enc, frames), n_prompt, n_force);
+    if (total - 1 + max_new > dc->max_seq) {
+      set_error("qasr_transcribe_batch: segment %d needs %d positions, the cache holds %d", i, total - 1 + max_new,
+                dc->max_seq);
+      return QASR_ERR_INVALID;
+    }
+  }
+  const int max_prompt = qasr_transcribe_prompt_len(max_tokens, n_prompt, n_force);
+  const int max_frames = qasr_mel_frames(max_samples);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(qasr_decoder_stream(dec));
+  void *audio = nullptr, *mel = nullptr, *enc_out = nullptr, *prompt = nullptr, *steps = nullptr;
+  int rc;
+  if ((rc = dev_scratch(kScratchAudio, (size_t)max_samples * 4, &audio))) return rc;
+  if ((rc = dev_scratch(kScratchMelOut, (size_t)128 * max_frames * 4, &mel))) return rc;
+  if ((rc = dev_scratch(kScratchEncOut, (size_t)max_tokens * H * 4, &enc_out))) return rc;
+  if ((rc = dev_scratch(kScratchPrompt, (size_t)max_prompt * H * 4, &prompt))) return rc;
+  // decode rows: tokens of step 0, then positions and ids of every step
+  if ((rc = dev_scratch(kScratchDecode, (size_t)(M + 2 * (size_t)max_new * M) * 4, &steps))) return rc;
+  int32_t *d_tok0 = static_cast<int32_t *>(steps), *d_pos = d_tok0 + M, *d_ids = d_pos + (size_t)max_new * M;
+
+  std::vector<int32_t> tok0(M), pos((size_t)max_new * M), pre;
+  float *embeds = static_cast<float *>(prompt);
+  for (int i = 0; i < M; ++i) {
+    // mel + encoder (transcribe.rs:78-96)
+    const int frames = qasr_mel_frames(n_samples[i]);
+    if ((rc = cuda_status(cudaMemcpyAsync(audio, samples[i], (size_t)n_samples[i] * 4, cudaMemcpyDefault, st),
+                          "qasr_transcribe_batch: samples")))
+      return rc;
+    if ((rc = qasr_mel_spectrogram(static_cast<float *>(mel), static_cast<const float *>(audio), n_samples[i], st)))
+      return rc;
+    if ((rc = cuda_status(cudaStreamSynchronize(st), "qasr_transcribe_batch: mel"))) return rc;
+    int T = 0;
+    if ((rc = qasr_encoder_forward(enc, static_cast<const float *>(mel), frames, static_cast<float *>(enc_out),
+                                   max_tokens, &T)))
+      return rc;
+    cudaSetDevice(dev);
+    // prompt embeddings (transcribe.rs:98-170): token rows around the audio rows
+    pre.assign(kPrefixHead, kPrefixHead + kHead);
+    pre.insert(pre.end(), prompt_tokens, prompt_tokens + n_prompt);
+    pre.insert(pre.end(), kPrefixTail, kPrefixTail + kTail);
+    const int prefix_len = (int)pre.size();
+    std::vector<int32_t> post(kSuffixBase, kSuffixBase + kSuffix);
+    post.insert(post.end(), force_tokens, force_tokens + n_force);
+    const int total = prefix_len + T + (int)post.size();
+    if ((rc = qasr_decoder_embed(dec, pre.data(), prefix_len, embeds))) return rc;
+    if ((rc = cuda_status(cudaMemcpyAsync(embeds + (size_t)prefix_len * H, enc_out, (size_t)T * H * 4,
+                                          cudaMemcpyDeviceToDevice, st),
+                          "qasr_transcribe_batch: audio rows")))
+      return rc;
+    if ((rc = qasr_decoder_embed(dec, post.data(), (int)post.size(), embeds + (size_t)(prefix_len + T) * H)))
+      return rc;
+    // prefill all but the last row; the first decode step feeds the last
+    // prompt token at position total - 1 (transcribe.rs:172-190)
+    if ((rc = qasr_decoder_prefill(dec, i, embeds, total - 1, 0))) return rc;
+    tok0[i] = post.back();
+    for (int s = 0; s < max_new; ++s) pos[(size_t)s * M + i] = total - 1 + s;
+  }
+  if ((rc = cuda_status(cudaMemcpyAsync(d_tok0, tok0.data(), (size_t)M * 4, cudaMemcpyHostToDevice, st),
+                        "qasr_transcribe_batch: tokens")))
+    return rc;
+  if ((rc = cuda_status(cudaMemcpyAsync(d_pos, pos.data(), pos.size() * 4, cudaMemcpyHostToDevice, st),
+                        "qasr_transcribe_batch: positions")))
+    return rc;
+  // greedy decode (transcribe.rs:192-222)
+  std::vector<int32_t> out((size_t)max_new * M);
+  std::vector<int> count(M, 0);
+  std::vector<char> done(M, 0);
+  int steps_run = 0;
+  while (steps_run < max_new) {
+    const int upto = std::min(max_new, steps_run + (stop_at_eos ? kCheckEvery : max_new));
+    for (int s = steps_run; s < upto; ++s) {
+      const int32_t *tok = s == 0 ? d_tok0 : d_ids + (size_t)(s - 1) * M;
+      if ((rc = qasr_decoder_step_device(dec, tok, d_pos + (size_t)s * M, M, d_ids + (size_t)s * M))) return rc;
+    }
+    if ((rc = cuda_status(cudaMemcpyAsync(out.data() + (size_t)steps_run * M, d_ids + (size_t)steps_run * M,
+                                          (size_t)(upto - steps_run) * M * 4, cudaMemcpyDeviceToHost, st),
+                          "qasr_transcribe_batch: ids")))
+      return rc;
+    if ((rc = cuda_status(cudaStreamSynchronize(st), "qasr_transcribe_batch: decode"))) return rc;
+    for (int s = steps_run; s < upto; ++s)
+      for (int i = 0; i < M; ++i) {
+        if (done[i]) continue;
+        const int32_t t = out[(size_t)s * M + i];
+        ids[(size_t)i * ids_stride + count[i]++] = t;
+        if (stop_at_eos && is_stop(t)) done[i] = 1;
+      }
+    steps_run = upto;
+    if (std::all_of(done.begin(), done.end(), [](char c) { return c != 0; })) break;
+  }
+  std::memcpy(n_ids, count.data(), (size_t)M * sizeof(int));
+  return QASR_OK;
+}

@@ -124,6 +124,13 @@ class Decoder:
             view = torch.as_tensor(_DevArray(ptr, (seq, self.cfg["hidden"])), device=f"cuda:{self.device}")
             return view.clone()
 
+    def embed(self, ids) -> torch.Tensor:
+        """QwenCtx::tok_embed_to_f32 for host ids: [n, hidden] rows on the device."""
+        a = np.ascontiguousarray(ids, dtype=np.int32)
+        out = torch.empty(a.size, self.cfg["hidden"], dtype=torch.float32, device=f"cuda:{self.device}")
+        _lib.call("qasr_decoder_embed", self._h, a.ctypes.data_as(C.c_void_p), a.size, C.c_void_p(out.data_ptr()))
+        return out
+
     def step_device(self, tokens: torch.Tensor, positions: torch.Tensor, out: torch.Tensor) -> None:
         """Same step on device int32 tensors, enqueued on the engine stream."""
         _lib.call("qasr_decoder_step_device", self._h, C.c_void_p(tokens.data_ptr()),

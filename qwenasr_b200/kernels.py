@@ -173,6 +173,18 @@ def bidirectional_attention(out, q, k, v, seq, n_heads, head_dim, scale, window_
               _ptr(window_starts, i32, "window_starts", n_windows + 1), n_windows, _stream())
 
 
+def mel_frames(n_samples: int) -> int:
+    """Frames audio::mel_spectrogram produces for n_samples (0 = too short)."""
+    return int(_lib.load().qasr_mel_frames(int(n_samples)))
+
+
+def mel_spectrogram(mel, samples, n_samples):
+    """audio::mel_spectrogram (audio.rs:271): mel [128, n_frames] from 16 kHz samples, both on the device."""
+    n_frames = mel_frames(n_samples)
+    _lib.call("qasr_mel_spectrogram", _ptr(mel, f32, "mel", 128 * max(n_frames, 1)),
+              _ptr(samples, f32, "samples", n_samples), n_samples, _stream())
+
+
 def causal_attention(out, q, k, v, seq_q, seq_k, n_heads, n_kv_heads, head_dim, scale, q_offset):
     """kernels::causal_attention (mod.rs:1174)."""
     _lib.call("qasr_causal_attention", _ptr(out, f32, "out", seq_q * n_heads * head_dim),

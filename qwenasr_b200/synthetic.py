@@ -124,3 +124,52 @@ def encoder_weights_np(cfg: dict, seed: int) -> dict:
                             "bo": mat(D), "ffn_norm_w": ones(D), "ffn_norm_b": mat(D), "fc1_w": mat(F, D),
                             "fc1_b": mat(F), "fc2_w": mat(D, F), "fc2_b": mat(D)})
     return w
+
+
+ENC_1_7B = dict(ENC_0_6B, d_model=1024, n_layers=24, n_heads=16, ffn_dim=4096, output_dim=2048)
+
+SAMPLE_RATE = 16000
+
+
+def synthetic_audio(seconds: float, seed: int) -> np.ndarray:
+    """16 kHz mono test signal: pink noise at -20 dBFS RMS plus three
+    sinusoids of random frequency in [200, 3000] Hz (amplitude 0.05 each,
+    random phase), float32 in [-1, 1].  Stands in for speech recordings,
+    which do not exist on these machines."""
+    rng = np.random.default_rng(seed)
+    n = int(round(seconds * SAMPLE_RATE))
+    if n == 0:
+        return np.zeros(0, np.float32)
+    spec = np.fft.rfft(rng.standard_normal(n))
+    f = np.arange(len(spec), dtype=np.float64)
+    f[0] = 1.0
+    pink = np.fft.irfft(spec / np.sqrt(f), n)
+    pink *= 0.1 / max(np.sqrt(np.mean(pink * pink)), 1e-12)
+    t = np.arange(n, dtype=np.float64) / SAMPLE_RATE
+    for hz, ph in zip(rng.uniform(200.0, 3000.0, 3), rng.uniform(0.0, 2 * np.pi, 3)):
+        pink += 0.05 * np.sin(2 * np.pi * hz * t + ph)
+    return np.clip(pink, -1.0, 1.0).astype(np.float32)
+
+
+def encoder_weights_gpu(cfg: dict, gen, device) -> dict:
+    """encoder_weights_np's distributions drawn on the GPU with torch (for
+    benchmarks at full size; the values differ from the numpy draw)."""
+    import torch
+    D, F, O, CH = cfg["d_model"], cfg["ffn_dim"], cfg["output_dim"], CONV_HIDDEN
+
+    def mat(*shape, s=0.02):
+        return torch.randn(*shape, generator=gen, device=device) * s
+
+    def ones(n):
+        return 1.0 + 0.02 * torch.randn(n, generator=gen, device=device)
+
+    w = {"conv1_w": mat(CH, 1, 3, 3, s=0.05), "conv1_b": mat(CH), "conv2_w": mat(CH, CH, 3, 3, s=0.05),
+         "conv2_b": mat(CH), "conv3_w": mat(CH, CH, 3, 3, s=0.05), "conv3_b": mat(CH), "conv_out_w": mat(D, CH * 16),
+         "ln_post_w": ones(D), "ln_post_b": mat(D), "proj1_w": mat(D, D), "proj1_b": mat(D), "proj2_w": mat(O, D),
+         "proj2_b": mat(O), "layers": []}
+    for _ in range(cfg["n_layers"]):
+        w["layers"].append({"attn_norm_w": ones(D), "attn_norm_b": mat(D), "wq": mat(D, D), "bq": mat(D),
+                            "wk": mat(D, D), "bk": mat(D), "wv": mat(D, D), "bv": mat(D), "wo": mat(D, D),
+                            "bo": mat(D), "ffn_norm_w": ones(D), "ffn_norm_b": mat(D), "fc1_w": mat(F, D),
+                            "fc1_b": mat(F), "fc2_w": mat(D, F), "fc2_b": mat(D)})
+    return w

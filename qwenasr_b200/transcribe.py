@@ -1,0 +1,65 @@
+"""Python face of qasr_transcribe_batch: transcribe_segment
+(crates/qwen-asr/src/transcribe.rs:67-244) on one GPU, token ids out.
+
+Audio -> log-mel -> encoder -> prompt embeddings (the reference's special
+tokens, transcribe.rs:11-13) -> prefill -> greedy decode, for up to
+`dec.max_batch` independent segments decoded together.  Text decoding stays
+with the caller's tokenizer, as in the reference's host.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from typing import Sequence
+
+import numpy as np
+import torch
+
+from . import _lib
+
+PREFIX_HEAD = (151644, 8948, 198)
+PREFIX_TAIL = (151645, 198, 151644, 872, 198, 151669)
+SUFFIX_BASE = (151670, 151645, 198, 151644, 77091, 198)
+TOKEN_ENDOFTEXT, TOKEN_IM_END = 151643, 151645
+
+
+def prompt_len(n_audio_tokens: int, n_prompt: int = 0, n_force: int = 0) -> int:
+    return int(_lib.load().qasr_transcribe_prompt_len(int(n_audio_tokens), int(n_prompt), int(n_force)))
+
+
+def _ids_arg(ids):
+    if ids is None or len(ids) == 0:
+        return None, 0, None
+    a = np.ascontiguousarray(ids, dtype=np.int32)
+    return C.c_void_p(a.ctypes.data), len(a), a
+
+
+def transcribe_ids(dec, enc, segments: Sequence, max_new: int, stop_at_eos: bool = False, prompt_tokens=None,
+                   force_tokens=None) -> list[list[int]]:
+    """Greedy token ids of each segment (16 kHz f32 samples: numpy arrays or
+    CUDA tensors).  With stop_at_eos the ids end at the first end-of-text /
+    im_end token (included), as the reference's decode loop stops there."""
+    n = len(segments)
+    if n == 0:
+        return []
+    keep = []
+    ptrs = (C.c_void_p * n)()
+    lens = (C.c_int * n)()
+    for i, s in enumerate(segments):
+        if isinstance(s, torch.Tensor):
+            s = s.detach().float().contiguous()
+            ptrs[i] = s.data_ptr()
+        else:
+            s = np.ascontiguousarray(s, dtype=np.float32)
+            ptrs[i] = s.ctypes.data
+        keep.append(s)
+        lens[i] = s.numel() if isinstance(s, torch.Tensor) else s.size
+    if any(isinstance(s, torch.Tensor) for s in keep):
+        torch.cuda.synchronize()  # the engine reads them on its own stream
+    pp, npr, pa = _ids_arg(prompt_tokens)
+    fp, nfr, fa = _ids_arg(force_tokens)
+    ids = np.zeros((n, max_new), np.int32)
+    counts = (C.c_int * n)()
+    _lib.call("qasr_transcribe_batch", dec._h, ptrs, lens, n, pp, npr, fp, nfr, int(max_new), 1 if stop_at_eos else 0,
+              C.c_void_p(ids.ctypes.data), int(max_new), counts)
+    del pa, fa, keep
+    return [ids[i, :counts[i]].tolist() for i in range(n)]

@@ -199,3 +199,40 @@ def test_segment_batch_greedy_matches_oracle(orc):
             ids.append(tok)
         assert got[i] == ids, (i, got[i], ids)
     dec.close()
+
+
+SMALL_1P7B = dict(synthetic.DEC_1_7B, n_layers=2, vocab=4096)
+
+
+@pytest.mark.parametrize("M", [1, 8])
+def test_decode_step_1p7b_shapes(orc, M):
+    """The 1.7B decoder shapes (hidden 2048, intermediate 6144): every
+    contraction has K = 2048 or 6144 and the planner's cluster / stage
+    choices differ from 0.6B.  Prefill a prompt per slot, then two greedy
+    steps: ids, logits and K/V rows against the oracle."""
+    orc.set_threads(8)
+    w, od, dec = build_pair(orc, SMALL_1P7B, seed=70 + M, max_seq=128, max_batch=M)
+    rng = np.random.default_rng(70 + M)
+    P = [int(p) for p in rng.integers(1, 60, M)]
+    caches, toks = [], rng.integers(0, SMALL_1P7B["vocab"], M).astype(np.int32)
+    for m in range(M):
+        kh, vh = od.new_kv(128)
+        emb = w["embed"][rng.integers(0, SMALL_1P7B["vocab"], P[m])]
+        od.prefill(kh, vh, 0, emb)
+        dec.prefill(m, emb, 0)
+        caches.append((kh, vh))
+    dec.keep_logits(True)
+    pos = np.array(P, np.int32)
+    for _ in range(2):
+        nxt = dec.step(toks, pos)
+        logits = dec.logits(M).cpu().numpy()
+        for m in range(M):
+            kh, vh = caches[m]
+            tok, ref_logits, _ = od.forward(kh, vh, int(pos[m]), w["embed"][toks[m]], want_logits=True)
+            assert int(nxt[m]) == tok
+            assert rel_err(logits[m], ref_logits) < 2e-3
+            kg, _ = dec.kv(m)
+            assert rel_err(kg[:, :pos[m] + 1].cpu().numpy(), kh[:, :pos[m] + 1]) < 2e-3
+        toks = nxt.astype(np.int32)
+        pos = pos + 1
+    dec.close()

@@ -1,0 +1,148 @@
+"""GPU parity of the transcription path (transcribe_segment,
+transcribe.rs:67-244): samples -> log-mel -> encoder -> prompt -> prefill ->
+greedy decode, through qasr_transcribe_batch.
+
+Two checks per case:
+  * decoder stage, exact: the oracle decoder (decoder.rs:751-965) fed the
+    same prompt rows -- the reference's special tokens around the GPU
+    encoder's rows -- gives the identical greedy ids;
+  * whole chain: oracle log-mel, oracle encoder composition and oracle
+    decoder give the same ids up to the first step whose oracle top-2 logit
+    margin is below 1e-3 of the logits' RMS (the encoder is only within 2e-3
+    relative of its oracle, so a near-tie may break either way after that).
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+from qwenasr_b200 import kernels as K  # noqa: E402
+from qwenasr_b200 import synthetic  # noqa: E402
+from qwenasr_b200.decoder import Decoder  # noqa: E402
+from qwenasr_b200.encoder import Encoder  # noqa: E402
+from qwenasr_b200.transcribe import (PREFIX_HEAD, PREFIX_TAIL, SUFFIX_BASE, TOKEN_IM_END, prompt_len,  # noqa: E402
+                                     transcribe_ids)
+from oracle.pyoracle import encoder_forward as encoder_forward_ref  # noqa: E402
+
+DEC = dict(synthetic.DEC_0_6B, n_layers=2)  # full vocabulary: the prompt uses the special ids
+ENC = dict(d_model=128, n_layers=2, n_heads=2, head_dim=64, ffn_dim=256, output_dim=1024, chunk_size=100,
+           n_window_infer=800)
+MAX_SEQ = 160
+
+
+@pytest.fixture(scope="module")
+def engines(orc):
+    orc.set_threads(8)
+    wd = synthetic.decoder_weights_np(DEC, seed=21)
+    we = synthetic.encoder_weights_np(ENC, seed=22)
+    dec = Decoder(DEC, device=0, max_batch=4, max_seq=MAX_SEQ)
+    for i, lw in enumerate(wd["layers"]):
+        dec.set_layer(i, lw)
+    dec.set_globals(wd["embed"], wd["norm"], wd["lm_head"], wd["lm_head_s"])
+    enc = Encoder(ENC, device=0)
+    enc.set_weights(we)
+    yield wd, we, orc.OracleDecoder(wd), dec, enc
+    dec.close()
+    enc.close()
+
+
+def oracle_decode(od, wd, rows, max_new, prompt=(), force=()):
+    pre = list(PREFIX_HEAD) + list(prompt) + list(PREFIX_TAIL)
+    post = list(SUFFIX_BASE) + list(force)
+    emb = np.concatenate([wd["embed"][pre], rows, wd["embed"][post]]).astype(np.float32)
+    kh, vh = od.new_kv(MAX_SEQ)
+    od.prefill(kh, vh, 0, emb[:-1])
+    tok, pos, ids, margins = post[-1], len(emb) - 1, [], []
+    for _ in range(max_new):
+        tok, logits, _ = od.forward(kh, vh, pos, wd["embed"][tok], want_logits=True)
+        top2 = np.sort(logits)[-2:]
+        margins.append(float(top2[1] - top2[0]) / math.sqrt(float(np.mean(logits.astype(np.float64) ** 2))))
+        ids.append(tok)
+        pos += 1
+    return ids, margins
+
+
+def _gpu_rows(enc, audio):
+    s = torch.from_numpy(audio).cuda()
+    mel = torch.empty(128, K.mel_frames(len(audio)), device="cuda")
+    K.mel_spectrogram(mel, s, len(audio))
+    torch.cuda.synchronize()  # the encoder runs on its own stream
+    return enc.forward(mel).cpu().numpy()
+
+
+@pytest.mark.parametrize("seconds,prompt,force", [
+    ((2.0,), (), ()),
+    ((2.0, 1.3, 0.7), (), ()),
+    ((1.0, 0.5), (1000, 2000), (3000, 4000)),
+])
+def test_transcribe_matches_oracle(orc, engines, seconds, prompt, force):
+    wd, we, od, dec, enc = engines
+    max_new = 12
+    audio = [synthetic.synthetic_audio(s, seed=100 + i) for i, s in enumerate(seconds)]
+    got = transcribe_ids(dec, enc, audio, max_new, prompt_tokens=prompt, force_tokens=force)
+    assert [len(g) for g in got] == [max_new] * len(audio)
+    for a, ids in zip(audio, got):
+        rows = _gpu_rows(enc, a)
+        assert prompt_len(len(rows), len(prompt), len(force)) == 15 + len(rows) + len(prompt) + len(force)
+        ref, _ = oracle_decode(od, wd, rows, max_new, prompt, force)
+        assert ids == ref
+        # the whole chain on the CPU
+        rows_o = encoder_forward_ref(we, ENC, orc.mel_spectrogram(a))
+        ref_o, margins = oracle_decode(od, wd, rows_o, max_new, prompt, force)
+        for s in range(max_new):
+            if ids[s] != ref_o[s]:
+                assert min(margins[:s + 1]) < 1e-3, (s, ids, ref_o, margins)
+                break
+
+
+def test_transcribe_device_samples_and_repeat(engines):
+    """Device-resident samples give the host result; a second call reuses the slots."""
+    wd, we, od, dec, enc = engines
+    a = synthetic.synthetic_audio(1.5, seed=7)
+    h = transcribe_ids(dec, enc, [a], 8)
+    d = transcribe_ids(dec, enc, [torch.from_numpy(a).cuda()], 8)
+    assert h == d
+
+
+def test_transcribe_stops_at_end_of_text(orc):
+    """With <|im_end|>'s lm-head scale raised, it wins early; the ids end there."""
+    orc.set_threads(8)
+    wd = synthetic.decoder_weights_np(DEC, seed=31)
+    wd["lm_head_s"] = wd["lm_head_s"].copy()
+    wd["lm_head_s"][TOKEN_IM_END] *= 1000.0
+    we = synthetic.encoder_weights_np(ENC, seed=32)
+    dec = Decoder(DEC, device=0, max_batch=2, max_seq=MAX_SEQ)
+    for i, lw in enumerate(wd["layers"]):
+        dec.set_layer(i, lw)
+    dec.set_globals(wd["embed"], wd["norm"], wd["lm_head"], wd["lm_head_s"])
+    enc = Encoder(ENC, device=0)
+    enc.set_weights(we)
+    od = orc.OracleDecoder(wd)
+    audio = [synthetic.synthetic_audio(1.0, seed=s) for s in (1, 2)]
+    got = transcribe_ids(dec, enc, audio, 40, stop_at_eos=True)
+    full = transcribe_ids(dec, enc, audio, 40, stop_at_eos=False)
+    for a, ids, f in zip(audio, got, full):
+        ref, _ = oracle_decode(od, wd, _gpu_rows(enc, a), 40)
+        assert f == ref
+        if TOKEN_IM_END in ref:
+            cut = ref.index(TOKEN_IM_END) + 1
+            assert ids == ref[:cut]
+        else:
+            assert ids == ref
+    assert any(TOKEN_IM_END in g for g in got)
+    dec.close()
+    enc.close()
+
+
+def test_transcribe_rejects_bad_requests(engines):
+    from qwenasr_b200._lib import QasrError
+    wd, we, od, dec, enc = engines
+    with pytest.raises(QasrError):
+        transcribe_ids(dec, enc, [np.zeros(100, np.float32)], 4)  # shorter than one frame
+    with pytest.raises(QasrError):
+        transcribe_ids(dec, enc, [synthetic.synthetic_audio(1.0, 0)] * 5, 4)  # more than max_batch
+    with pytest.raises(QasrError):
+        transcribe_ids(dec, enc, [synthetic.synthetic_audio(1.0, 0)], MAX_SEQ)  # positions past the cache

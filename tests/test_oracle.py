@@ -243,3 +243,127 @@ def test_embed_and_interleave(orc):
     f, fs = orc.interleave_gate_up(g, np.arange(3, dtype=np.float32), u, np.arange(3, 6, dtype=np.float32))
     assert np.array_equal(f[0::2], g) and np.array_equal(f[1::2], u)
     assert fs.tolist() == [0, 3, 1, 4, 2, 5]
+
+
+# ------------------------------------------------------- log-mel front end --
+# crates/qwen-asr/tests/audio.rs, then float64 and loop-level cross-checks.
+
+def test_ref_mel_spectrogram_short_audio(orc):  # audio.rs tests:47-60
+    n = 8000
+    i = np.arange(n, dtype=np.float32)
+    s = (np.sin(np.float32(2.0) * np.float32(np.pi) * np.float32(440.0) * i / np.float32(16000.0)) *
+         np.float32(0.5)).astype(np.float32)
+    mel = orc.mel_spectrogram(s)
+    assert mel is not None
+    assert 20 < mel.shape[1] < 80 and mel.shape == (128, 50)
+    # 440 Hz is 6.6 on the Slaney scale: filter 17 or 18 (centres 0.35 mel apart) peaks
+    assert int(np.argmax(mel[:, 25])) in (17, 18)
+
+
+def test_ref_mel_spectrogram_shape_and_range(orc):  # audio.rs tests:22-45 (11 s of synthetic audio for jfk.wav)
+    from qwenasr_b200.synthetic import synthetic_audio
+    s = synthetic_audio(11.0, seed=3)
+    mel = orc.mel_spectrogram(s)
+    assert mel.shape == (128, 1100)
+    assert mel.min() >= -1.0 and mel.max() <= 2.0
+    # the clamp: nothing below max - 8 in log10 units, i.e. 2 in normalised units
+    assert mel.max() - mel.min() <= 2.0 + 1e-6
+
+
+def test_mel_frame_count_and_too_short(orc):
+    assert orc.mel_spectrogram(np.zeros(159, np.float32)) is None
+    assert orc.mel_spectrogram(np.zeros(0, np.float32)) is None
+    for n in (160, 170, 399, 401, 5287):
+        assert orc.mel_spectrogram(np.ones(n, np.float32)).shape == (128, n // 160)
+
+
+def test_mel_filters_slaney(orc):
+    f = orc.mel_filters().astype(np.float64)
+    assert f.shape == (128, 201) and (f >= 0).all()
+    # each filter is a triangle over its two neighbours' centres, height 2/(width in Hz)
+    hz = np.arange(201) * 8000.0 / 200.0
+
+    def to_mel(h):
+        return np.where(h >= 1000, 15 + np.log(np.maximum(h, 1e-9) / 1000) * 27 / np.log(6.4), 3 * h / 200)
+
+    def to_hz(m):
+        return np.where(m >= 15, 1000 * np.exp(np.log(6.4) / 27 * (m - 15)), 200 * m / 3)
+
+    edges = to_hz(np.linspace(0, to_mel(np.array(8000.0)), 130))
+    for m in (0, 40, 90, 127):
+        lo, c, hi = edges[m], edges[m + 1], edges[m + 2]
+        tri = np.maximum(np.minimum((hz - lo) / (c - lo), (hi - hz) / (hi - c)), 0) * 2 / (hi - lo)
+        # f32 edges: near the triangle's feet the rise/fall terms cancel, hence the atol
+        np.testing.assert_allclose(f[m], tri, rtol=2e-5, atol=1e-4 * tri.max())
+
+
+def _mel_loop(orc, s):
+    """Pure-Python loop restatement of audio.rs:271-385 on the oracle's tables
+    (f32 scalar arithmetic, sequential sums), for a couple of frames."""
+    win, ct, st = orc.mel_tables()
+    filt = orc.mel_filters()
+    n = len(s)
+    frames = n // 160
+    padded = np.zeros(n + 400, np.float32)
+    for i in range(200):
+        padded[i] = s[200 - i] if 200 - i < n else 0.0
+        src = n - 2 - i
+        padded[200 + n + i] = s[src] if src >= 0 else 0.0
+    padded[200:200 + n] = s
+    out = np.empty((frames, 128), np.float32)
+    for t in range(frames):
+        w = [padded[t * 160 + i] * win[i] for i in range(400)]
+        power = []
+        for k in range(201):
+            re = np.float32(0)
+            im = np.float32(0)
+            for i in range(400):
+                re = np.float32(re + w[i] * ct[k, i])
+                im = np.float32(im + w[i] * st[k, i])
+            power.append(np.float32(re * re + im * im))
+        for m in range(128):
+            acc = np.float32(0)
+            for k in range(201):
+                acc = np.float32(acc + filt[m, k] * power[k])
+            out[t, m] = np.float32(math.log10(max(float(acc), float(np.float32(1e-10)))))
+    top = out.max()
+    return ((np.maximum(out, np.float32(top - np.float32(8))) + np.float32(4)) / np.float32(4)).T
+
+
+@pytest.mark.parametrize("n", [170, 330])
+def test_mel_matches_loop_restatement(orc, n):
+    """Short inputs whose reflect padding runs off the signal (zeros)."""
+    s = np.random.default_rng(n).standard_normal(n).astype(np.float32) * 0.1
+    got = orc.mel_spectrogram(s)
+    ref = _mel_loop(orc, s)
+    # log10 in the loop is correctly rounded; the oracle calls glibc log10f (<= 1 ulp apart)
+    assert np.max(np.abs(got - ref)) <= 2.5e-7
+
+
+def test_mel_matches_float64(orc):
+    """Whole pipeline against a float64 numpy derivation (numpy's reflect pad,
+    rfft, the same filter bank): f32 DFT rounding only."""
+    from qwenasr_b200.synthetic import synthetic_audio
+    s = synthetic_audio(2.0, seed=11)
+    got = orc.mel_spectrogram(s)
+    n = len(s)
+    x = np.pad(s.astype(np.float64), 200, mode="reflect")
+    win = 0.5 * (1 - np.cos(2 * np.pi * np.arange(400) / 400))
+    fr = np.stack([x[t * 160:t * 160 + 400] * win for t in range(n // 160)])
+    p = np.abs(np.fft.rfft(fr, axis=1)) ** 2
+    lm = np.log10(np.maximum(p @ orc.mel_filters().astype(np.float64).T, 1e-10))
+    ref = ((np.maximum(lm, lm.max() - 8) + 4) / 4).T
+    assert np.max(np.abs(got - ref)) < 2e-4
+
+
+def test_encoder_composition_runs(orc):
+    """The oracle's Encoder::forward composition (the encoder parity checker
+    and CPU baseline): 13 tokens per full 100-frame chunk, the tail chunk's
+    three stride-2 convs, finite rows of output_dim."""
+    from qwenasr_b200 import synthetic
+    cfg = dict(d_model=128, n_layers=1, n_heads=2, head_dim=64, ffn_dim=256, output_dim=96, chunk_size=100,
+               n_window_infer=800)
+    w = synthetic.encoder_weights_np(cfg, seed=5)
+    mel = np.random.default_rng(5).standard_normal((128, 137)).astype(np.float32)
+    out = orc.encoder_forward(w, cfg, mel)
+    assert out.shape == (13 + 5, 96) and np.isfinite(out).all()
