@@ -59,7 +59,7 @@ def transcribe_ids(dec, enc, segments: Sequence, max_new: int, stop_at_eos: bool
     fp, nfr, fa = _ids_arg(force_tokens)
     ids = np.zeros((n, max_new), np.int32)
     counts = (C.c_int * n)()
-    _lib.call("qasr_transcribe_batch", dec._h, ptrs, lens, n, pp, npr, fp, nfr, int(max_new), 1 if stop_at_eos else 0,
+    _lib.call("qasr_transcribe_batch", dec._h, enc._h, ptrs, lens, n, pp, npr, fp, nfr, int(max_new), 1 if stop_at_eos else 0,
               C.c_void_p(ids.ctypes.data), int(max_new), counts)
     del pa, fa, keep
     return [ids[i, :counts[i]].tolist() for i in range(n)]

@@ -108,31 +108,34 @@ def test_transcribe_device_samples_and_repeat(engines):
 
 
 def test_transcribe_stops_at_end_of_text(orc):
-    """With <|im_end|>'s lm-head scale raised, it wins early; the ids end there."""
+    """<|im_end|>'s lm-head row is made a 1.5x copy of the row that wins step 2
+    of the unmodified model, so it wins by step 2; the ids end there."""
     orc.set_threads(8)
     wd = synthetic.decoder_weights_np(DEC, seed=31)
-    wd["lm_head_s"] = wd["lm_head_s"].copy()
-    wd["lm_head_s"][TOKEN_IM_END] *= 1000.0
     we = synthetic.encoder_weights_np(ENC, seed=32)
+    enc = Encoder(ENC, device=0)
+    enc.set_weights(we)
+    audio = [synthetic.synthetic_audio(1.0, seed=s) for s in (1, 2)]
+    rows = [_gpu_rows(enc, a) for a in audio]
+    plain, _ = oracle_decode(orc.OracleDecoder(wd), wd, rows[0], 3)
+    t2 = plain[2]
+    wd["lm_head"] = wd["lm_head"].copy()
+    wd["lm_head_s"] = wd["lm_head_s"].copy()
+    wd["lm_head"][TOKEN_IM_END] = wd["lm_head"][t2]
+    wd["lm_head_s"][TOKEN_IM_END] = np.float32(1.5) * wd["lm_head_s"][t2]
     dec = Decoder(DEC, device=0, max_batch=2, max_seq=MAX_SEQ)
     for i, lw in enumerate(wd["layers"]):
         dec.set_layer(i, lw)
     dec.set_globals(wd["embed"], wd["norm"], wd["lm_head"], wd["lm_head_s"])
-    enc = Encoder(ENC, device=0)
-    enc.set_weights(we)
     od = orc.OracleDecoder(wd)
-    audio = [synthetic.synthetic_audio(1.0, seed=s) for s in (1, 2)]
     got = transcribe_ids(dec, enc, audio, 40, stop_at_eos=True)
     full = transcribe_ids(dec, enc, audio, 40, stop_at_eos=False)
-    for a, ids, f in zip(audio, got, full):
-        ref, _ = oracle_decode(od, wd, _gpu_rows(enc, a), 40)
+    for r, ids, f in zip(rows, got, full):
+        ref, _ = oracle_decode(od, wd, r, 40)
         assert f == ref
-        if TOKEN_IM_END in ref:
-            cut = ref.index(TOKEN_IM_END) + 1
-            assert ids == ref[:cut]
-        else:
-            assert ids == ref
-    assert any(TOKEN_IM_END in g for g in got)
+        cut = ref.index(TOKEN_IM_END) + 1 if TOKEN_IM_END in ref else len(ref)
+        assert ids == ref[:cut]
+    assert TOKEN_IM_END in got[0][:3] and got[0][-1] == TOKEN_IM_END
     dec.close()
     enc.close()
 
