@@ -291,6 +291,12 @@ void qasr_decoder_free(qasr_decoder *dec);
 
 /* Upload weights (host or device pointers; copied). */
 int qasr_decoder_set_layer(qasr_decoder *dec, int layer, const qasr_dec_layer_weights *w);
+/* DecoderInt8::load's gate/up fusion (decoder.rs:699-719) on the device:
+ * gate and up [inter, hidden] INT8 (host or device) with their scales,
+ * interleaved g0,u0,g1,u1,... into layer `layer`'s fused matrix.  For this,
+ * qasr_decoder_set_layer may be given gate_up = gate_up_s = NULL. */
+int qasr_decoder_set_gate_up(qasr_decoder *dec, int layer, const int8_t *gate, const float *gate_s, const int8_t *up,
+                             const float *up_s);
 /* embed: f32 [vocab, hidden] or int8 [vocab, hidden] (+ embed_scales);
  * final norm [hidden]; lm_head int8 [vocab, hidden] + scales.  When lm_head
  * is NULL the lm head is tied to the INT8 embedding table (decoder.rs:950-963). */
@@ -398,6 +404,31 @@ int qasr_encoder_set_layer(qasr_encoder *enc, int layer, const qasr_enc_layer_we
 int qasr_encoder_set_post(qasr_encoder *enc, const float *ln_post_w, const float *ln_post_b, const float *proj1_w,
                           const float *proj1_b, const float *proj2_w, const float *proj2_b);
 
+/* EncLayerInt8 (encoder.rs:424-444): the projection matrices INT8 [out, in]
+ * with f32 per-row scales (the qwen-asr-quantize format), biases and norms f32. */
+typedef struct {
+  const float *attn_norm_w, *attn_norm_b;
+  const int8_t *wq; const float *wq_s, *bq;
+  const int8_t *wk; const float *wk_s, *bk;
+  const int8_t *wv; const float *wv_s, *bv;
+  const int8_t *wo; const float *wo_s, *bo;
+  const float *ffn_norm_w, *ffn_norm_b;
+  const int8_t *fc1; const float *fc1_s, *fc1_b;
+  const int8_t *fc2; const float *fc2_s, *fc2_b;
+} qasr_enc_layer_weights_int8;
+
+/* EncoderInt8 (encoder.rs:446-520, the encoder of a V2 .qint8 file): the
+ * same engine with INT8 projections, run through qasr_linear_int8 /
+ * qasr_linear_nobias_int8 as EncoderInt8::forward does.  Each matrix keeps
+ * whichever form its latest setter supplied. */
+int qasr_encoder_set_conv_int8(qasr_encoder *enc, const float *conv1_w, const float *conv1_b, const float *conv2_w,
+                               const float *conv2_b, const float *conv3_w, const float *conv3_b,
+                               const int8_t *conv_out, const float *conv_out_s);
+int qasr_encoder_set_layer_int8(qasr_encoder *enc, int layer, const qasr_enc_layer_weights_int8 *w);
+int qasr_encoder_set_post_int8(qasr_encoder *enc, const float *ln_post_w, const float *ln_post_b,
+                               const int8_t *proj1, const float *proj1_s, const float *proj1_b, const int8_t *proj2,
+                               const float *proj2_s, const float *proj2_b);
+
 /* Encoder tokens produced for mel_frames frames (13 per full 100-frame chunk). */
 int qasr_encoder_tokens(const qasr_encoder *enc, int mel_frames);
 const qasr_encoder_config *qasr_encoder_get_config(const qasr_encoder *enc);
@@ -408,6 +439,33 @@ int qasr_encoder_device(const qasr_encoder *enc);
  * Synchronous. */
 int qasr_encoder_forward(qasr_encoder *enc, const float *mel, int mel_frames, float *out, int out_rows,
                          int *n_tokens);
+
+/* ======================================================================
+ * .qint8 model files (quantize.rs) and the V2 load path (context.rs:341-420)
+ * ==================================================================== */
+
+typedef struct qasr_qint8 qasr_qint8;
+
+/* QuantFile::open (quantize.rs:130-280): mmap a V1 or V2 .qint8 file and
+ * parse its tensor table.  Truncated tables and tensors whose bytes run past
+ * the end of the file are rejected.  NULL on failure.  Needs no GPU. */
+qasr_qint8 *qasr_qint8_open(const char *path);
+void qasr_qint8_close(qasr_qint8 *f);
+int qasr_qint8_version(const qasr_qint8 *f); /* 1 or 2 */
+int qasr_qint8_count(const qasr_qint8 *f);
+int qasr_qint8_find(const qasr_qint8 *f, const char *name); /* index, -1 if absent */
+/* Tensor i: name, dtype (0 INT8, 1 F32, 2 BF16), dims and shape (up to 8),
+ * pointers into the mapping (scales NULL unless INT8; F32/BF16 data may be
+ * unaligned).  Any output pointer may be NULL. */
+int qasr_qint8_tensor(const qasr_qint8 *f, int i, const char **name, int *dtype, int *n_dims, int64_t *shape,
+                      const void **data, const float **scales);
+/* QwenConfig::detect (config.rs:110-156) from the tensor shapes; either
+ * output may be NULL.  max_batch / max_seq of dec are left unchanged. */
+int qasr_qint8_detect(const qasr_qint8 *f, qasr_decoder_config *dec, qasr_encoder_config *enc);
+/* DecoderInt8::load (decoder.rs:680-748) / EncoderInt8::load_from_qint8
+ * (encoder.rs:466-520) into engines created with the detected configs. */
+int qasr_qint8_load_decoder(const qasr_qint8 *f, qasr_decoder *dec);
+int qasr_qint8_load_encoder(const qasr_qint8 *f, qasr_encoder *enc);
 
 /* ======================================================================
  * Transcription (transcribe.rs), token ids out

@@ -72,6 +72,24 @@ pub struct QasrEncLayerWeights {
     pub fc1_w: *const f32, pub fc1_b: *const f32, pub fc2_w: *const f32, pub fc2_b: *const f32,
 }
 
+#[repr(C)]
+#[derive(Clone, Copy)]
+pub struct QasrEncLayerWeightsInt8 {
+    pub attn_norm_w: *const f32, pub attn_norm_b: *const f32,
+    pub wq: *const i8, pub wq_s: *const f32, pub bq: *const f32,
+    pub wk: *const i8, pub wk_s: *const f32, pub bk: *const f32,
+    pub wv: *const i8, pub wv_s: *const f32, pub bv: *const f32,
+    pub wo: *const i8, pub wo_s: *const f32, pub bo: *const f32,
+    pub ffn_norm_w: *const f32, pub ffn_norm_b: *const f32,
+    pub fc1: *const i8, pub fc1_s: *const f32, pub fc1_b: *const f32,
+    pub fc2: *const i8, pub fc2_s: *const f32, pub fc2_b: *const f32,
+}
+
+#[repr(C)]
+pub struct QasrQint8 {
+    _private: [u8; 0],
+}
+
 #[link(name = "qwenasr_b200")]
 extern "C" {
     pub fn qasr_last_error() -> *const c_char;
@@ -111,6 +129,7 @@ extern "C" {
     pub fn qasr_decoder_create(cfg: *const QasrDecoderConfig, device: c_int) -> *mut QasrDecoder;
     pub fn qasr_decoder_free(dec: *mut QasrDecoder);
     pub fn qasr_decoder_set_layer(dec: *mut QasrDecoder, layer: c_int, w: *const QasrDecLayerWeights) -> c_int;
+    pub fn qasr_decoder_set_gate_up(dec: *mut QasrDecoder, layer: c_int, gate: *const i8, gate_s: *const f32, up: *const i8, up_s: *const f32) -> c_int;
     pub fn qasr_decoder_set_globals(dec: *mut QasrDecoder, embed: *const c_void, embed_scales: *const f32, norm: *const f32, lm_head: *const i8, lm_head_s: *const f32) -> c_int;
     pub fn qasr_decoder_kv(dec: *mut QasrDecoder, slot: c_int, k_cache: *mut *mut f32, v_cache: *mut *mut f32) -> c_int;
     pub fn qasr_decoder_step(dec: *mut QasrDecoder, tokens: *const i32, positions: *const i32, M: c_int, next_tokens: *mut i32) -> c_int;
@@ -130,10 +149,22 @@ extern "C" {
     pub fn qasr_encoder_set_conv(enc: *mut QasrEncoder, conv1_w: *const f32, conv1_b: *const f32, conv2_w: *const f32, conv2_b: *const f32, conv3_w: *const f32, conv3_b: *const f32, conv_out_w: *const f32) -> c_int;
     pub fn qasr_encoder_set_layer(enc: *mut QasrEncoder, layer: c_int, w: *const QasrEncLayerWeights) -> c_int;
     pub fn qasr_encoder_set_post(enc: *mut QasrEncoder, ln_post_w: *const f32, ln_post_b: *const f32, proj1_w: *const f32, proj1_b: *const f32, proj2_w: *const f32, proj2_b: *const f32) -> c_int;
+    pub fn qasr_encoder_set_conv_int8(enc: *mut QasrEncoder, conv1_w: *const f32, conv1_b: *const f32, conv2_w: *const f32, conv2_b: *const f32, conv3_w: *const f32, conv3_b: *const f32, conv_out: *const i8, conv_out_s: *const f32) -> c_int;
+    pub fn qasr_encoder_set_layer_int8(enc: *mut QasrEncoder, layer: c_int, w: *const QasrEncLayerWeightsInt8) -> c_int;
+    pub fn qasr_encoder_set_post_int8(enc: *mut QasrEncoder, ln_post_w: *const f32, ln_post_b: *const f32, proj1: *const i8, proj1_s: *const f32, proj1_b: *const f32, proj2: *const i8, proj2_s: *const f32, proj2_b: *const f32) -> c_int;
     pub fn qasr_encoder_tokens(enc: *const QasrEncoder, mel_frames: c_int) -> c_int;
     pub fn qasr_encoder_get_config(enc: *const QasrEncoder) -> *const QasrEncoderConfig;
     pub fn qasr_encoder_device(enc: *const QasrEncoder) -> c_int;
     pub fn qasr_encoder_forward(enc: *mut QasrEncoder, mel: *const f32, mel_frames: c_int, out: *mut f32, out_rows: c_int, n_tokens: *mut c_int) -> c_int;
+    pub fn qasr_qint8_open(path: *const c_char) -> *mut QasrQint8;
+    pub fn qasr_qint8_close(f: *mut QasrQint8);
+    pub fn qasr_qint8_version(f: *const QasrQint8) -> c_int;
+    pub fn qasr_qint8_count(f: *const QasrQint8) -> c_int;
+    pub fn qasr_qint8_find(f: *const QasrQint8, name: *const c_char) -> c_int;
+    pub fn qasr_qint8_tensor(f: *const QasrQint8, i: c_int, name: *mut *const c_char, dtype: *mut c_int, n_dims: *mut c_int, shape: *mut i64, data: *mut *const c_void, scales: *mut *const f32) -> c_int;
+    pub fn qasr_qint8_detect(f: *const QasrQint8, dec: *mut QasrDecoderConfig, enc: *mut QasrEncoderConfig) -> c_int;
+    pub fn qasr_qint8_load_decoder(f: *const QasrQint8, dec: *mut QasrDecoder) -> c_int;
+    pub fn qasr_qint8_load_encoder(f: *const QasrQint8, enc: *mut QasrEncoder) -> c_int;
     pub fn qasr_transcribe_prompt_len(n_audio_tokens: c_int, n_prompt: c_int, n_force: c_int) -> c_int;
     pub fn qasr_transcribe_batch(dec: *mut QasrDecoder, enc: *mut QasrEncoder, samples: *mut *const f32, n_samples: *const c_int, n_segments: c_int, prompt_tokens: *const i32, n_prompt: c_int, force_tokens: *const i32, n_force: c_int, max_new: c_int, stop_at_eos: c_int, ids: *mut i32, ids_stride: c_int, n_ids: *mut c_int) -> c_int;
 }

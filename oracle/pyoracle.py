@@ -437,11 +437,22 @@ def _conv3x3s2(x, w, b, c_in, c_out, h, wd):
     return ((w.reshape(c_out, -1).astype(np.float64) @ cols) + b[:, None]).astype(np.float32), ho, wo
 
 
+def _enc_proj(x, d, name, bias_key):
+    """kernels::linear (f32 "<name>" or "<name>_w") or linear_int8 ("<name>" + "<name>_s")."""
+    b = d[bias_key] if bias_key else None
+    if name + "_s" in d:
+        return linear_int8(x, d[name], d[name + "_s"], b) if b is not None else linear_nobias_int8(
+            x, d[name], d[name + "_s"])
+    return linear(x, d[name] if name in d else d[name + "_w"], b)
+
+
 def encoder_forward(w, cfg, mel):
     """Encoder::forward (encoder.rs:243-415) composed from the restated
     kernels: per 100-frame chunk the conv stem (3 x conv + GELU), conv_out
     and the sinusoidal positions; windowed layers; post LayerNorm and the two
-    projections.  mel [128, frames] -> [tokens, output_dim]."""
+    projections.  mel [128, frames] -> [tokens, output_dim].  Matrices given
+    with scales ("<m>", "<m>_s") run as EncoderInt8::forward does
+    (encoder.rs:562-667: linear_int8 / linear_nobias_int8)."""
     D, CH, cs = cfg["d_model"], _CONV_HIDDEN, cfg["chunk_size"]
     frames = mel.shape[1]
     xs = []
@@ -454,7 +465,7 @@ def encoder_forward(w, cfg, mel):
         c3, h3, w3 = _conv3x3s2(c2, w["conv3_w"], w["conv3_b"], CH, CH, h2, w2)
         c3 = gelu(c3.ravel()).reshape(CH, h3, w3)
         reshaped = np.ascontiguousarray(c3.transpose(2, 0, 1).reshape(w3, CH * h3))
-        xs.append(linear(reshaped, w["conv_out_w"]) + sinusoidal_pe(w3, D))
+        xs.append(_enc_proj(reshaped, w, "conv_out", None) + sinusoidal_pe(w3, D))
     x = np.concatenate(xs).astype(np.float32)
     T = x.shape[0]
     tpc = 13
@@ -463,14 +474,14 @@ def encoder_forward(w, cfg, mel):
     scale = np.float32(1.0 / math.sqrt(cfg["head_dim"]))
     for L in w["layers"]:
         xn = layer_norm(x, L["attn_norm_w"], L["attn_norm_b"], 1e-5)
-        q = linear(xn, L["wq"], L["bq"])
-        k = linear(xn, L["wk"], L["bk"])
-        v = linear(xn, L["wv"], L["bv"])
+        q = _enc_proj(xn, L, "wq", "bq")
+        k = _enc_proj(xn, L, "wk", "bk")
+        v = _enc_proj(xn, L, "wv", "bv")
         a = bidirectional_attention(q, k, v, T, cfg["n_heads"], cfg["head_dim"], starts, scale)
-        x = (x + linear(a, L["wo"], L["bo"])).astype(np.float32)
+        x = (x + _enc_proj(a, L, "wo", "bo")).astype(np.float32)
         xn = layer_norm(x, L["ffn_norm_w"], L["ffn_norm_b"], 1e-5)
-        mid = gelu(linear(xn, L["fc1_w"], L["fc1_b"]).ravel()).reshape(T, -1)
-        x = (x + linear(mid, L["fc2_w"], L["fc2_b"])).astype(np.float32)
+        mid = gelu(_enc_proj(xn, L, "fc1", "fc1_b").ravel()).reshape(T, -1)
+        x = (x + _enc_proj(mid, L, "fc2", "fc2_b")).astype(np.float32)
     xn = layer_norm(x, w["ln_post_w"], w["ln_post_b"], 1e-5)
-    p1 = gelu(linear(xn, w["proj1_w"], w["proj1_b"]).ravel()).reshape(T, -1)
-    return linear(p1, w["proj2_w"], w["proj2_b"])
+    p1 = gelu(_enc_proj(xn, w, "proj1", "proj1_b").ravel()).reshape(T, -1)
+    return _enc_proj(p1, w, "proj2", "proj2_b")

@@ -90,6 +90,7 @@ _SIGS = {
     "qasr_decoder_prefill_hidden": (P, [P]),
     "qasr_decoder_step_device": (I, [P, P, P, I, P]),
     "qasr_decoder_stream": (P, [P]),
+    "qasr_decoder_set_gate_up": (I, [P, I, P, P, P, P]),
     "qasr_decoder_get_config": (P, [P]),
     "qasr_decoder_device": (I, [P]),
     "qasr_decoder_embed": (I, [P, P, I, P]),
@@ -110,6 +111,12 @@ class EncLayerWeights(C.Structure):
         "fc1_w", "fc1_b", "fc2_w", "fc2_b")]
 
 
+class EncLayerWeightsInt8(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in (
+        "attn_norm_w", "attn_norm_b", "wq", "wq_s", "bq", "wk", "wk_s", "bk", "wv", "wv_s", "bv", "wo", "wo_s", "bo",
+        "ffn_norm_w", "ffn_norm_b", "fc1", "fc1_s", "fc1_b", "fc2", "fc2_s", "fc2_b")]
+
+
 _SIGS.update({
     "qasr_encoder_create": (P, [C.POINTER(EncoderConfig), I]),
     "qasr_encoder_free": (None, [P]),
@@ -119,6 +126,19 @@ _SIGS.update({
     "qasr_encoder_tokens": (I, [P, I]),
     "qasr_encoder_forward": (I, [P, P, I, P, I, C.POINTER(C.c_int)]),
     "qasr_encoder_get_config": (P, [P]),
+    "qasr_encoder_set_conv_int8": (I, [P, P, P, P, P, P, P, P, P]),
+    "qasr_encoder_set_layer_int8": (I, [P, I, C.POINTER(EncLayerWeightsInt8)]),
+    "qasr_encoder_set_post_int8": (I, [P, P, P, P, P, P, P, P, P]),
+    "qasr_qint8_open": (P, [C.c_char_p]),
+    "qasr_qint8_close": (None, [P]),
+    "qasr_qint8_version": (I, [P]),
+    "qasr_qint8_count": (I, [P]),
+    "qasr_qint8_find": (I, [P, C.c_char_p]),
+    "qasr_qint8_tensor": (I, [P, I, C.POINTER(C.c_char_p), C.POINTER(C.c_int), C.POINTER(C.c_int),
+                              C.POINTER(C.c_int64), C.POINTER(C.c_void_p), C.POINTER(C.c_void_p)]),
+    "qasr_qint8_detect": (I, [P, C.POINTER(DecoderConfig), C.POINTER(EncoderConfig)]),
+    "qasr_qint8_load_decoder": (I, [P, P]),
+    "qasr_qint8_load_encoder": (I, [P, P]),
     "qasr_encoder_device": (I, [P]),
     "qasr_transcribe_prompt_len": (I, [I, I, I]),
     "qasr_transcribe_batch": (I, [P, P, P, P, I, P, I, P, I, I, I, P, I, P]),

@@ -257,8 +257,10 @@ extern "C" int qasr_decoder_set_layer(qasr_decoder *d, int layer, const qasr_dec
   if (!rc) rc = copy_in(d, ld.sqkv + q_dim + kv, w->wv_s, kv * 4, "wv_s");
   if (!rc) rc = copy_in(d, ld.wo, w->wo, H * q_dim, "wo");
   if (!rc) rc = copy_in(d, ld.so, w->wo_s, H * 4, "wo_s");
-  if (!rc) rc = copy_in(d, ld.gate_up, w->gate_up, 2 * I * H, "gate_up");
-  if (!rc) rc = copy_in(d, ld.sgu, w->gate_up_s, 2 * I * 4, "gate_up_s");
+  if (w->gate_up || w->gate_up_s) {  // both NULL: qasr_decoder_set_gate_up supplies them
+    if (!rc) rc = copy_in(d, ld.gate_up, w->gate_up, 2 * I * H, "gate_up");
+    if (!rc) rc = copy_in(d, ld.sgu, w->gate_up_s, 2 * I * 4, "gate_up_s");
+  }
   if (!rc) rc = copy_in(d, ld.down, w->down, H * I, "down");
   if (!rc) rc = copy_in(d, ld.sdown, w->down_s, H * 4, "down_s");
   if (!rc) rc = copy_in(d, ld.q_norm, w->q_norm, c.head_dim * 4, "q_norm");
@@ -267,6 +269,56 @@ extern "C" int qasr_decoder_set_layer(qasr_decoder *d, int layer, const qasr_dec
   if (!rc) rc = copy_in(d, ld.post_norm, w->post_attn_norm, H * 4, "post_attn_norm");
   if (!rc) rc = cuda_status(cudaStreamSynchronize(d->stream), "qasr_decoder_set_layer");
   return rc;
+}
+
+namespace qasr {
+// fused[2r] = gate[r], fused[2r+1] = up[r] (rows of `cols` bytes), and the scales alike.
+__global__ void __launch_bounds__(256) interleave_rows_kernel(int8_t *__restrict__ fused, float *__restrict__ fused_s,
+                                                              const int8_t *__restrict__ gate,
+                                                              const float *__restrict__ gate_s,
+                                                              const int8_t *__restrict__ up,
+                                                              const float *__restrict__ up_s, int rows, int cols) {
+  const int vec = cols / 16;  // uint4 per row
+  const long total = (long)2 * rows * vec;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const long r2 = i / vec, c = i % vec;
+    const long r = r2 >> 1;
+    const int8_t *src = (r2 & 1) ? up : gate;
+    reinterpret_cast<uint4 *>(fused + r2 * cols)[c] = reinterpret_cast<const uint4 *>(src + r * cols)[c];
+    if (c == 0) fused_s[r2] = (r2 & 1) ? up_s[r] : gate_s[r];
+  }
+}
+}  // namespace qasr
+
+// DecoderInt8::load's gate/up fusion (decoder.rs:699-719) on the device.
+extern "C" int qasr_decoder_set_gate_up(qasr_decoder *d, int layer, const int8_t *gate, const float *gate_s,
+                                        const int8_t *up, const float *up_s) {
+  if (!d || layer < 0 || layer >= d->cfg.n_layers || !gate || !gate_s || !up || !up_s) {
+    set_error("qasr_decoder_set_gate_up: invalid arguments");
+    return QASR_ERR_INVALID;
+  }
+  cudaSetDevice(d->device);
+  const qasr_decoder_config &c = d->cfg;
+  const size_t H = c.hidden, I = c.inter;
+  LayerDev &ld = d->layers[layer];
+  void *tmp = nullptr;
+  int rc = cuda_status(cudaMalloc(&tmp, 2 * I * H + 2 * I * 4), "qasr_decoder_set_gate_up: staging");
+  if (rc) return rc;
+  int8_t *g = static_cast<int8_t *>(tmp), *u = g + I * H;
+  float *gs = reinterpret_cast<float *>(u + I * H), *us = gs + I;
+  rc = copy_in(d, g, gate, I * H, "gate");
+  if (!rc) rc = copy_in(d, u, up, I * H, "up");
+  if (!rc) rc = copy_in(d, gs, gate_s, I * 4, "gate_s");
+  if (!rc) rc = copy_in(d, us, up_s, I * 4, "up_s");
+  if (!rc) {
+    const long total = (long)2 * I * (H / 16);
+    interleave_rows_kernel<<<(int)std::min((total + 255) / 256, 148l * 8), 256, 0, d->stream>>>(
+        ld.gate_up, ld.sgu, g, gs, u, us, (int)I, (int)H);
+    rc = launch_status("qasr_decoder_set_gate_up");
+  }
+  const int rc2 = cuda_status(cudaStreamSynchronize(d->stream), "qasr_decoder_set_gate_up");
+  cudaFree(tmp);
+  return rc ? rc : rc2;
 }
 
 extern "C" int qasr_decoder_set_globals(qasr_decoder *d, const void *embed, const float *embed_scales,

@@ -1,6 +1,10 @@
 // encoder_engine.cu -- the audio encoder on one GPU: Encoder::forward
-// (crates/qwen-asr/src/encoder.rs:243-415) for f32 weights, composed from
-// the kernel-level entries in the reference's order.
+// (crates/qwen-asr/src/encoder.rs:243-415, f32 weights) and
+// EncoderInt8::forward (encoder.rs:562-667, INT8 projection weights with f32
+// scales, as a V2 .qint8 file stores them), composed from the kernel-level
+// entries in the reference's order.  Each projection matrix is held either as
+// f32 or as INT8 + per-row scales, whichever its setter supplied, and runs
+// through qasr_linear / qasr_linear_int8 accordingly.
 //
 // Per mel chunk of chunk_size frames (encoder.rs:281-348): three stride-2
 // 3x3 convolutions (480 channels) each followed by the tanh GELU, the
@@ -34,9 +38,27 @@ __global__ void __launch_bounds__(256) conv_reshape_kernel(float *__restrict__ o
   }
 }
 
+// One projection matrix [rows, cols]: f32, or INT8 with f32 row scales.
+struct EncMat {
+  int rows = 0, cols = 0;
+  float *f = nullptr;
+  int8_t *q = nullptr;
+  float *s = nullptr;
+  bool ready() const { return f || q; }
+  void release() {
+    if (f) cudaFree(f);
+    if (q) cudaFree(q);
+    if (s) cudaFree(s);
+    f = nullptr;
+    q = nullptr;
+    s = nullptr;
+  }
+};
+
 struct EncLayerDev {
-  float *attn_norm_w, *attn_norm_b, *wq, *bq, *wk, *bk, *wv, *bv, *wo, *bo;
-  float *ffn_norm_w, *ffn_norm_b, *fc1_w, *fc1_b, *fc2_w, *fc2_b;
+  float *attn_norm_w, *attn_norm_b, *bq, *bk, *bv, *bo;
+  float *ffn_norm_w, *ffn_norm_b, *fc1_b, *fc2_b;
+  EncMat wq, wk, wv, wo, fc1, fc2;
 };
 
 }  // namespace qasr
@@ -46,9 +68,9 @@ struct qasr_encoder {
   int device = 0;
   cudaStream_t stream = nullptr;
   std::vector<qasr::EncLayerDev> layers;
-  float *conv_w[3] = {nullptr, nullptr, nullptr}, *conv_b[3] = {nullptr, nullptr, nullptr}, *conv_out_w = nullptr;
-  float *ln_post_w = nullptr, *ln_post_b = nullptr, *proj1_w = nullptr, *proj1_b = nullptr, *proj2_w = nullptr,
-        *proj2_b = nullptr;
+  float *conv_w[3] = {nullptr, nullptr, nullptr}, *conv_b[3] = {nullptr, nullptr, nullptr};
+  qasr::EncMat conv_out, proj1, proj2;
+  float *ln_post_w = nullptr, *ln_post_b = nullptr, *proj1_b = nullptr, *proj2_b = nullptr;
   std::vector<void *> allocs;
   // activations, grown on demand
   int tok_cap = 0, frames_cap = 0;
@@ -80,10 +102,68 @@ static int enc_copy(qasr_encoder *e, float *dst, const float *src, size_t n, con
   return cuda_status(cudaMemcpyAsync(dst, src, n * 4, cudaMemcpyDefault, e->stream), what);
 }
 
+// f32 weights into m (replacing an INT8 copy).
+static int mat_set_f32(qasr_encoder *e, EncMat &m, const float *src, const char *what) {
+  if (!src) {
+    set_error("qasr_encoder: %s is NULL", what);
+    return QASR_ERR_INVALID;
+  }
+  const size_t n = (size_t)m.rows * m.cols;
+  if (m.q) {
+    int rc = cuda_status(cudaStreamSynchronize(e->stream), what);
+    if (rc) return rc;
+    m.release();
+  }
+  if (!m.f) {
+    int rc = cuda_status(cudaMalloc(&m.f, n * 4), "qasr_encoder: cudaMalloc");
+    if (rc) return rc;
+  }
+  return cuda_status(cudaMemcpyAsync(m.f, src, n * 4, cudaMemcpyDefault, e->stream), what);
+}
+
+// INT8 weights + row scales into m (replacing an f32 copy).
+static int mat_set_i8(qasr_encoder *e, EncMat &m, const int8_t *src, const float *scales, const char *what) {
+  if (!src || !scales) {
+    set_error("qasr_encoder: %s (or its scales) is NULL", what);
+    return QASR_ERR_INVALID;
+  }
+  const size_t n = (size_t)m.rows * m.cols;
+  if (m.f) {
+    int rc = cuda_status(cudaStreamSynchronize(e->stream), what);
+    if (rc) return rc;
+    m.release();
+  }
+  if (!m.q) {
+    int rc = cuda_status(cudaMalloc(&m.q, n), "qasr_encoder: cudaMalloc");
+    if (!rc) rc = cuda_status(cudaMalloc(&m.s, (size_t)m.rows * 4), "qasr_encoder: cudaMalloc");
+    if (rc) return rc;
+  }
+  int rc = cuda_status(cudaMemcpyAsync(m.q, src, n, cudaMemcpyDefault, e->stream), what);
+  if (!rc) rc = cuda_status(cudaMemcpyAsync(m.s, scales, (size_t)m.rows * 4, cudaMemcpyDefault, e->stream), what);
+  return rc;
+}
+
+// y [T, rows] = x [T, cols] m^T (+ bias): kernels::linear or linear_int8.
+static int mat_apply(float *y, const float *x, const EncMat &m, const float *bias, int T, cudaStream_t st) {
+  if (m.q)
+    return bias ? qasr_linear_int8(y, x, m.q, m.s, bias, T, m.cols, m.rows, st)
+                : qasr_linear_nobias_int8(y, x, m.q, m.s, T, m.cols, m.rows, st);
+  return bias ? qasr_linear(y, x, m.f, bias, T, m.cols, m.rows, st)
+              : qasr_linear_nobias(y, x, m.f, T, m.cols, m.rows, st);
+}
+
+static std::vector<EncMat *> enc_mats(qasr_encoder *e) {
+  std::vector<EncMat *> v = {&e->conv_out, &e->proj1, &e->proj2};
+  for (auto &L : e->layers)
+    for (EncMat *m : {&L.wq, &L.wk, &L.wv, &L.wo, &L.fc1, &L.fc2}) v.push_back(m);
+  return v;
+}
+
 extern "C" void qasr_encoder_free(qasr_encoder *e) {
   if (!e) return;
   cudaSetDevice(e->device);
   if (e->stream) cudaStreamSynchronize(e->stream);
+  for (EncMat *m : enc_mats(e)) m->release();
   for (void *p : e->allocs) cudaFree(p);
   if (e->act) cudaFree(e->act);
   if (e->conv_buf) cudaFree(e->conv_buf);
@@ -124,24 +204,31 @@ extern "C" qasr_encoder *qasr_encoder_create(const qasr_encoder_config *cfg, int
     rc = enc_alloc(e, &e->conv_w[i], (size_t)CH * cin[i] * 9);
     if (!rc) rc = enc_alloc(e, &e->conv_b[i], CH);
   }
-  if (!rc) rc = enc_alloc(e, &e->conv_out_w, (size_t)D * CH * h3);
+  // projection matrices: shapes now, storage when a setter supplies f32 or INT8
+  e->conv_out.rows = D;
+  e->conv_out.cols = CH * h3;
+  e->proj1.rows = D;
+  e->proj1.cols = D;
+  e->proj2.rows = O;
+  e->proj2.cols = D;
   for (auto &L : e->layers) {
     float **pp[] = {&L.attn_norm_w, &L.attn_norm_b, &L.bq, &L.bk, &L.bv, &L.bo, &L.ffn_norm_w, &L.ffn_norm_b,
                     &L.fc2_b};
     for (float **p : pp)
       if (!rc) rc = enc_alloc(e, p, D);
-    float **mm[] = {&L.wq, &L.wk, &L.wv, &L.wo};
-    for (float **p : mm)
-      if (!rc) rc = enc_alloc(e, p, (size_t)D * D);
-    if (!rc) rc = enc_alloc(e, &L.fc1_w, (size_t)F * D);
     if (!rc) rc = enc_alloc(e, &L.fc1_b, F);
-    if (!rc) rc = enc_alloc(e, &L.fc2_w, (size_t)D * F);
+    for (EncMat *m : {&L.wq, &L.wk, &L.wv, &L.wo}) {
+      m->rows = D;
+      m->cols = D;
+    }
+    L.fc1.rows = F;
+    L.fc1.cols = D;
+    L.fc2.rows = D;
+    L.fc2.cols = F;
   }
   if (!rc) rc = enc_alloc(e, &e->ln_post_w, D);
   if (!rc) rc = enc_alloc(e, &e->ln_post_b, D);
-  if (!rc) rc = enc_alloc(e, &e->proj1_w, (size_t)D * D);
   if (!rc) rc = enc_alloc(e, &e->proj1_b, D);
-  if (!rc) rc = enc_alloc(e, &e->proj2_w, (size_t)O * D);
   if (!rc) rc = enc_alloc(e, &e->proj2_b, O);
   if (rc) {
     qasr_encoder_free(e);
@@ -166,8 +253,31 @@ extern "C" int qasr_encoder_set_conv(qasr_encoder *e, const float *conv1_w, cons
     rc = enc_copy(e, e->conv_w[i], w[i], (size_t)CH * cin[i] * 9, "conv weight");
     if (!rc) rc = enc_copy(e, e->conv_b[i], b[i], CH, "conv bias");
   }
-  if (!rc) rc = enc_copy(e, e->conv_out_w, conv_out_w, (size_t)e->cfg.d_model * CH * h3, "conv_out weight");
+  if (!rc) rc = mat_set_f32(e, e->conv_out, conv_out_w, "conv_out weight");
   if (!rc) rc = cuda_status(cudaStreamSynchronize(e->stream), "qasr_encoder_set_conv");
+  (void)h3;
+  return rc;
+}
+
+// EncoderInt8 (encoder.rs:446-520): the convolutions stay f32, conv_out is INT8.
+extern "C" int qasr_encoder_set_conv_int8(qasr_encoder *e, const float *conv1_w, const float *conv1_b,
+                                          const float *conv2_w, const float *conv2_b, const float *conv3_w,
+                                          const float *conv3_b, const int8_t *conv_out, const float *conv_out_s) {
+  if (!e) {
+    set_error("qasr_encoder_set_conv_int8: null encoder");
+    return QASR_ERR_INVALID;
+  }
+  cudaSetDevice(e->device);
+  const int CH = kConvHidden;
+  const float *w[3] = {conv1_w, conv2_w, conv3_w}, *b[3] = {conv1_b, conv2_b, conv3_b};
+  const int cin[3] = {1, CH, CH};
+  int rc = QASR_OK;
+  for (int i = 0; i < 3 && !rc; ++i) {
+    rc = enc_copy(e, e->conv_w[i], w[i], (size_t)CH * cin[i] * 9, "conv weight");
+    if (!rc) rc = enc_copy(e, e->conv_b[i], b[i], CH, "conv bias");
+  }
+  if (!rc) rc = mat_set_i8(e, e->conv_out, conv_out, conv_out_s, "conv_out weight");
+  if (!rc) rc = cuda_status(cudaStreamSynchronize(e->stream), "qasr_encoder_set_conv_int8");
   return rc;
 }
 
@@ -186,14 +296,49 @@ extern "C" int qasr_encoder_set_layer(qasr_encoder *e, int layer, const qasr_enc
     size_t n;
     const char *what;
   } items[] = {{L.attn_norm_w, w->attn_norm_w, D, "attn_norm_w"}, {L.attn_norm_b, w->attn_norm_b, D, "attn_norm_b"},
-               {L.wq, w->wq, D * D, "wq"}, {L.bq, w->bq, D, "bq"}, {L.wk, w->wk, D * D, "wk"},
-               {L.bk, w->bk, D, "bk"}, {L.wv, w->wv, D * D, "wv"}, {L.bv, w->bv, D, "bv"},
-               {L.wo, w->wo, D * D, "wo"}, {L.bo, w->bo, D, "bo"}, {L.ffn_norm_w, w->ffn_norm_w, D, "ffn_norm_w"},
-               {L.ffn_norm_b, w->ffn_norm_b, D, "ffn_norm_b"}, {L.fc1_w, w->fc1_w, F * D, "fc1_w"},
-               {L.fc1_b, w->fc1_b, F, "fc1_b"}, {L.fc2_w, w->fc2_w, D * F, "fc2_w"}, {L.fc2_b, w->fc2_b, D, "fc2_b"}};
+               {L.bq, w->bq, D, "bq"}, {L.bk, w->bk, D, "bk"}, {L.bv, w->bv, D, "bv"}, {L.bo, w->bo, D, "bo"},
+               {L.ffn_norm_w, w->ffn_norm_w, D, "ffn_norm_w"}, {L.ffn_norm_b, w->ffn_norm_b, D, "ffn_norm_b"},
+               {L.fc1_b, w->fc1_b, F, "fc1_b"}, {L.fc2_b, w->fc2_b, D, "fc2_b"}};
   for (auto &it : items)
     if (!rc) rc = enc_copy(e, it.dst, it.src, it.n, it.what);
+  if (!rc) rc = mat_set_f32(e, L.wq, w->wq, "wq");
+  if (!rc) rc = mat_set_f32(e, L.wk, w->wk, "wk");
+  if (!rc) rc = mat_set_f32(e, L.wv, w->wv, "wv");
+  if (!rc) rc = mat_set_f32(e, L.wo, w->wo, "wo");
+  if (!rc) rc = mat_set_f32(e, L.fc1, w->fc1_w, "fc1_w");
+  if (!rc) rc = mat_set_f32(e, L.fc2, w->fc2_w, "fc2_w");
   if (!rc) rc = cuda_status(cudaStreamSynchronize(e->stream), "qasr_encoder_set_layer");
+  return rc;
+}
+
+// EncLayerInt8 (encoder.rs:424-444): INT8 projections, f32 biases and norms.
+extern "C" int qasr_encoder_set_layer_int8(qasr_encoder *e, int layer, const qasr_enc_layer_weights_int8 *w) {
+  if (!e || !w || layer < 0 || layer >= e->cfg.n_layers) {
+    set_error("qasr_encoder_set_layer_int8: invalid arguments");
+    return QASR_ERR_INVALID;
+  }
+  cudaSetDevice(e->device);
+  const size_t D = e->cfg.d_model, F = e->cfg.ffn_dim;
+  EncLayerDev &L = e->layers[layer];
+  int rc = QASR_OK;
+  struct {
+    float *dst;
+    const float *src;
+    size_t n;
+    const char *what;
+  } items[] = {{L.attn_norm_w, w->attn_norm_w, D, "attn_norm_w"}, {L.attn_norm_b, w->attn_norm_b, D, "attn_norm_b"},
+               {L.bq, w->bq, D, "bq"}, {L.bk, w->bk, D, "bk"}, {L.bv, w->bv, D, "bv"}, {L.bo, w->bo, D, "bo"},
+               {L.ffn_norm_w, w->ffn_norm_w, D, "ffn_norm_w"}, {L.ffn_norm_b, w->ffn_norm_b, D, "ffn_norm_b"},
+               {L.fc1_b, w->fc1_b, F, "fc1_b"}, {L.fc2_b, w->fc2_b, D, "fc2_b"}};
+  for (auto &it : items)
+    if (!rc) rc = enc_copy(e, it.dst, it.src, it.n, it.what);
+  if (!rc) rc = mat_set_i8(e, L.wq, w->wq, w->wq_s, "wq");
+  if (!rc) rc = mat_set_i8(e, L.wk, w->wk, w->wk_s, "wk");
+  if (!rc) rc = mat_set_i8(e, L.wv, w->wv, w->wv_s, "wv");
+  if (!rc) rc = mat_set_i8(e, L.wo, w->wo, w->wo_s, "wo");
+  if (!rc) rc = mat_set_i8(e, L.fc1, w->fc1, w->fc1_s, "fc1");
+  if (!rc) rc = mat_set_i8(e, L.fc2, w->fc2, w->fc2_s, "fc2");
+  if (!rc) rc = cuda_status(cudaStreamSynchronize(e->stream), "qasr_encoder_set_layer_int8");
   return rc;
 }
 
@@ -208,11 +353,30 @@ extern "C" int qasr_encoder_set_post(qasr_encoder *e, const float *ln_post_w, co
   const size_t D = e->cfg.d_model, O = e->cfg.output_dim;
   int rc = enc_copy(e, e->ln_post_w, ln_post_w, D, "ln_post_w");
   if (!rc) rc = enc_copy(e, e->ln_post_b, ln_post_b, D, "ln_post_b");
-  if (!rc) rc = enc_copy(e, e->proj1_w, proj1_w, D * D, "proj1_w");
+  if (!rc) rc = mat_set_f32(e, e->proj1, proj1_w, "proj1_w");
   if (!rc) rc = enc_copy(e, e->proj1_b, proj1_b, D, "proj1_b");
-  if (!rc) rc = enc_copy(e, e->proj2_w, proj2_w, O * D, "proj2_w");
+  if (!rc) rc = mat_set_f32(e, e->proj2, proj2_w, "proj2_w");
   if (!rc) rc = enc_copy(e, e->proj2_b, proj2_b, O, "proj2_b");
   if (!rc) rc = cuda_status(cudaStreamSynchronize(e->stream), "qasr_encoder_set_post");
+  return rc;
+}
+
+extern "C" int qasr_encoder_set_post_int8(qasr_encoder *e, const float *ln_post_w, const float *ln_post_b,
+                                          const int8_t *proj1, const float *proj1_s, const float *proj1_b,
+                                          const int8_t *proj2, const float *proj2_s, const float *proj2_b) {
+  if (!e) {
+    set_error("qasr_encoder_set_post_int8: null encoder");
+    return QASR_ERR_INVALID;
+  }
+  cudaSetDevice(e->device);
+  const size_t D = e->cfg.d_model, O = e->cfg.output_dim;
+  int rc = enc_copy(e, e->ln_post_w, ln_post_w, D, "ln_post_w");
+  if (!rc) rc = enc_copy(e, e->ln_post_b, ln_post_b, D, "ln_post_b");
+  if (!rc) rc = mat_set_i8(e, e->proj1, proj1, proj1_s, "proj1");
+  if (!rc) rc = enc_copy(e, e->proj1_b, proj1_b, D, "proj1_b");
+  if (!rc) rc = mat_set_i8(e, e->proj2, proj2, proj2_s, "proj2");
+  if (!rc) rc = enc_copy(e, e->proj2_b, proj2_b, O, "proj2_b");
+  if (!rc) rc = cuda_status(cudaStreamSynchronize(e->stream), "qasr_encoder_set_post_int8");
   return rc;
 }
 
@@ -234,6 +398,11 @@ extern "C" int qasr_encoder_forward(qasr_encoder *e, const float *mel, int mel_f
     return QASR_ERR_INVALID;
   }
   cudaSetDevice(e->device);
+  for (EncMat *m : enc_mats(e))
+    if (!m->ready()) {
+      set_error("qasr_encoder_forward: weights not set (call the qasr_encoder_set_* functions first)");
+      return QASR_ERR_INVALID;
+    }
   const qasr_encoder_config &c = e->cfg;
   const int D = c.d_model, F = c.ffn_dim, O = c.output_dim, CH = kConvHidden, cs = c.chunk_size;
   const int T = qasr_encoder_tokens(e, mel_frames);
@@ -301,7 +470,7 @@ extern "C" int qasr_encoder_forward(qasr_encoder *e, const float *mel, int mel_f
       conv_reshape_kernel<<<(int)std::min((n + 255) / 256, 4096l), 256, 0, st>>>(e->reshaped, e->c3, CH * h3, w3);
       rc = launch_status("qasr_encoder_forward: reshape");
     }
-    if (!rc) rc = qasr_linear_nobias(e->x + (size_t)tok * D, e->reshaped, e->conv_out_w, w3, CH * h3, D, st);
+    if (!rc) rc = mat_apply(e->x + (size_t)tok * D, e->reshaped, e->conv_out, nullptr, w3, st);
     if (!rc) rc = qasr_sinusoidal_pe(e->pe, w3, D, st);
     if (!rc) rc = qasr_add_inplace(e->x + (size_t)tok * D, e->pe, (int64_t)w3 * D, st);
     tok += w3;
@@ -329,23 +498,23 @@ extern "C" int qasr_encoder_forward(qasr_encoder *e, const float *mel, int mel_f
   for (int l = 0; l < c.n_layers && !rc; ++l) {
     const EncLayerDev &L = e->layers[l];
     rc = qasr_layer_norm(e->xn, e->x, L.attn_norm_w, L.attn_norm_b, T, D, 1e-5f, st);
-    if (!rc) rc = qasr_linear(e->q, e->xn, L.wq, L.bq, T, D, D, st);
-    if (!rc) rc = qasr_linear(e->k, e->xn, L.wk, L.bk, T, D, D, st);
-    if (!rc) rc = qasr_linear(e->v, e->xn, L.wv, L.bv, T, D, D, st);
+    if (!rc) rc = mat_apply(e->q, e->xn, L.wq, L.bq, T, st);
+    if (!rc) rc = mat_apply(e->k, e->xn, L.wk, L.bk, T, st);
+    if (!rc) rc = mat_apply(e->v, e->xn, L.wv, L.bv, T, st);
     if (!rc) rc = qasr_bidirectional_attention(e->attn, e->q, e->k, e->v, T, c.n_heads, c.head_dim, scale, e->win, nw, st);
-    if (!rc) rc = qasr_linear(e->proj, e->attn, L.wo, L.bo, T, D, D, st);
+    if (!rc) rc = mat_apply(e->proj, e->attn, L.wo, L.bo, T, st);
     if (!rc) rc = qasr_add_inplace(e->x, e->proj, td, st);
     if (!rc) rc = qasr_layer_norm(e->xn, e->x, L.ffn_norm_w, L.ffn_norm_b, T, D, 1e-5f, st);
-    if (!rc) rc = qasr_linear(e->mid, e->xn, L.fc1_w, L.fc1_b, T, D, F, st);
+    if (!rc) rc = mat_apply(e->mid, e->xn, L.fc1, L.fc1_b, T, st);
     if (!rc) rc = qasr_gelu(e->mid, (int64_t)T * F, st);
-    if (!rc) rc = qasr_linear(e->proj, e->mid, L.fc2_w, L.fc2_b, T, F, D, st);
+    if (!rc) rc = mat_apply(e->proj, e->mid, L.fc2, L.fc2_b, T, st);
     if (!rc) rc = qasr_add_inplace(e->x, e->proj, td, st);
   }
   // ---- post LayerNorm and projections (encoder.rs:405-415)
   if (!rc) rc = qasr_layer_norm(e->xn, e->x, e->ln_post_w, e->ln_post_b, T, D, 1e-5f, st);
-  if (!rc) rc = qasr_linear(e->q, e->xn, e->proj1_w, e->proj1_b, T, D, D, st);
+  if (!rc) rc = mat_apply(e->q, e->xn, e->proj1, e->proj1_b, T, st);
   if (!rc) rc = qasr_gelu(e->q, td, st);
-  if (!rc) rc = qasr_linear(e->out, e->q, e->proj2_w, e->proj2_b, T, D, O, st);
+  if (!rc) rc = mat_apply(e->out, e->q, e->proj2, e->proj2_b, T, st);
   if (!rc) rc = cuda_status(cudaMemcpyAsync(out, e->out, (size_t)T * O * 4, cudaMemcpyDefault, st), "encoder output");
   if (!rc) rc = cuda_status(cudaStreamSynchronize(st), "qasr_encoder_forward");
   if (!rc && n_tokens) *n_tokens = T;

@@ -12,10 +12,12 @@ from . import _lib
 
 def _ptr(a, keep):
     if isinstance(a, torch.Tensor):
-        a = a.detach().float().contiguous()
+        a = a.detach().contiguous()
+        if a.dtype != torch.int8:
+            a = a.float()
         keep.append(a)
         return C.c_void_p(a.data_ptr())
-    arr = np.ascontiguousarray(a, dtype=np.float32)
+    arr = np.ascontiguousarray(a, dtype=np.int8 if np.asarray(a).dtype == np.int8 else np.float32)
     keep.append(arr)
     return C.c_void_p(arr.ctypes.data)
 
@@ -31,14 +33,30 @@ class Encoder:
             raise _lib.QasrError(_lib.QASR_ERR_INVALID, "qasr_encoder_create", _lib.last_error())
 
     def set_weights(self, w: dict) -> None:
+        """f32 weights (encoder_weights_np keys), or the INT8 form of
+        EncoderInt8 when the dict carries scales ("wq_s", "conv_out_s", ...;
+        see synthetic.quantize_encoder)."""
         keep = []
-        _lib.call("qasr_encoder_set_conv", self._h, *[_ptr(w[k], keep) for k in (
-            "conv1_w", "conv1_b", "conv2_w", "conv2_b", "conv3_w", "conv3_b", "conv_out_w")])
+        if "conv_out_s" in w:
+            _lib.call("qasr_encoder_set_conv_int8", self._h, *[_ptr(w[k], keep) for k in (
+                "conv1_w", "conv1_b", "conv2_w", "conv2_b", "conv3_w", "conv3_b")],
+                _ptr(w["conv_out"], keep), _ptr(w["conv_out_s"], keep))
+        else:
+            _lib.call("qasr_encoder_set_conv", self._h, *[_ptr(w[k], keep) for k in (
+                "conv1_w", "conv1_b", "conv2_w", "conv2_b", "conv3_w", "conv3_b", "conv_out_w")])
         for i, lw in enumerate(w["layers"]):
-            s = _lib.EncLayerWeights(*[_ptr(lw[n], keep) for n, _ in _lib.EncLayerWeights._fields_])
-            _lib.call("qasr_encoder_set_layer", self._h, i, C.byref(s))
-        _lib.call("qasr_encoder_set_post", self._h, *[_ptr(w[k], keep) for k in (
-            "ln_post_w", "ln_post_b", "proj1_w", "proj1_b", "proj2_w", "proj2_b")])
+            if "wq_s" in lw:
+                s = _lib.EncLayerWeightsInt8(*[_ptr(lw[n], keep) for n, _ in _lib.EncLayerWeightsInt8._fields_])
+                _lib.call("qasr_encoder_set_layer_int8", self._h, i, C.byref(s))
+            else:
+                s = _lib.EncLayerWeights(*[_ptr(lw[n], keep) for n, _ in _lib.EncLayerWeights._fields_])
+                _lib.call("qasr_encoder_set_layer", self._h, i, C.byref(s))
+        if "proj1_s" in w:
+            _lib.call("qasr_encoder_set_post_int8", self._h, *[_ptr(w[k], keep) for k in (
+                "ln_post_w", "ln_post_b", "proj1", "proj1_s", "proj1_b", "proj2", "proj2_s", "proj2_b")])
+        else:
+            _lib.call("qasr_encoder_set_post", self._h, *[_ptr(w[k], keep) for k in (
+                "ln_post_w", "ln_post_b", "proj1_w", "proj1_b", "proj2_w", "proj2_b")])
 
     def tokens(self, mel_frames: int) -> int:
         return _lib.load().qasr_encoder_tokens(self._h, int(mel_frames))

@@ -173,3 +173,22 @@ def encoder_weights_gpu(cfg: dict, gen, device) -> dict:
                             "bo": mat(D), "ffn_norm_w": ones(D), "ffn_norm_b": mat(D), "fc1_w": mat(F, D),
                             "fc1_b": mat(F), "fc2_w": mat(D, F), "fc2_b": mat(D)})
     return w
+
+
+def quantize_encoder(w: dict, quantize=quantize_np) -> dict:
+    """The EncoderInt8 form of f32 encoder weights (what qwen-asr-quantize
+    writes to a V2 file): conv_out, q/k/v/o, fc1, fc2, proj1, proj2 as INT8
+    with per-row scales (keys "<m>" + "<m>_s"); convolutions, biases and norms
+    stay f32."""
+    out = {k: w[k] for k in ("conv1_w", "conv1_b", "conv2_w", "conv2_b", "conv3_w", "conv3_b", "ln_post_w",
+                             "ln_post_b", "proj1_b", "proj2_b")}
+    for dst, src in (("conv_out", "conv_out_w"), ("proj1", "proj1_w"), ("proj2", "proj2_w")):
+        out[dst], out[dst + "_s"] = quantize(np.asarray(w[src], np.float32))
+    out["layers"] = []
+    for L in w["layers"]:
+        q = {k: L[k] for k in ("attn_norm_w", "attn_norm_b", "bq", "bk", "bv", "bo", "ffn_norm_w", "ffn_norm_b",
+                               "fc1_b", "fc2_b")}
+        for dst, src in (("wq", "wq"), ("wk", "wk"), ("wv", "wv"), ("wo", "wo"), ("fc1", "fc1_w"), ("fc2", "fc2_w")):
+            q[dst], q[dst + "_s"] = quantize(np.asarray(L[src], np.float32))
+        out["layers"].append(q)
+    return out
