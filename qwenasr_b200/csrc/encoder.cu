@@ -4,10 +4,16 @@
 //    into a [spatial, patch] matrix, then the tensor-core f32 GEMM
 //    (umma_gemm.cu) with the conv weights as the row operand, which writes
 //    the reference's [c_out, spatial] layout directly, then the bias;
-//  * kernels::bidirectional_attention (mod.rs:1038-1122): windowed
-//    full attention, one warp per (query, head), keys of the query's window,
-//    the reference's per-key online-softmax update.
+//  * kernels::bidirectional_attention (mod.rs:1038-1122): windowed full
+//    attention.  The main kernel stages one window's K and V rows of one
+//    head in shared memory; each warp then takes a query: one key per lane
+//    for the scores, the window max, exp and sum, then the weighted sum of V
+//    rows (lanes over dimensions).  This is the softmax in two passes rather
+//    than the reference's per-key running update (same value up to f32
+//    rounding, and no per-key dependency chain).  Windows longer than the
+//    shared-memory budget use the per-key kernel, which keeps K/V in L2.
 #include <algorithm>
+#include <vector>
 
 #include "common.cuh"
 #include "matvec.cuh"
@@ -90,6 +96,73 @@ bidir_attention_kernel(float *__restrict__ out, const float *__restrict__ q, con
     out[i * hidden + (long)h * hd + lane * EPL + e] = sum_exp > 0.0f ? __fmul_rn(o[e], inv) : o[e];
 }
 
+// Window [starts[w], starts[w+1]) of head h, queries z*8+warp, z*8+warp+8*gridDim.z, ...
+// Shared memory: K [kt][HD+1] (padded: lane-per-key reads are conflict-free),
+// V [kt][HD], per-warp q [HD] and scores [kt].
+template <int EPL>
+__global__ void __launch_bounds__(256)
+bidir_attention_staged_kernel(float *__restrict__ out, const float *__restrict__ q, const float *__restrict__ k,
+                              const float *__restrict__ v, int seq, int n_heads, float scale,
+                              const int32_t *__restrict__ window_starts, int kt) {
+  constexpr int HD = EPL * 32;
+  extern __shared__ float4 bidir_smem[];
+  float *sK = reinterpret_cast<float *>(bidir_smem);
+  float *sV = sK + (size_t)kt * (HD + 1);
+  float *sQ = sV + (size_t)kt * HD;
+  float *sP = sQ + 8 * HD;
+  const int w = blockIdx.x, h = blockIdx.y;
+  const int ws = max(0, window_starts[w]), we = min(seq, window_starts[w + 1]);
+  const int n = we - ws;
+  if (n <= 0 || n > kt) return;  // block-uniform; the host sizes kt to the longest window
+  const long hidden = (long)n_heads * HD;
+  for (int idx = threadIdx.x; idx < n * HD; idx += blockDim.x) {
+    const int j = idx / HD, d = idx - j * HD;
+    const long g = (long)(ws + j) * hidden + (long)h * HD + d;
+    sK[j * (HD + 1) + d] = k[g];
+    sV[j * HD + d] = v[g];
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float *qs = sQ + warp * HD, *ps = sP + (size_t)warp * kt;
+  for (int qi = blockIdx.z * 8 + warp; qi < n; qi += gridDim.z * 8) {
+    const long row = (long)(ws + qi) * hidden + (long)h * HD;
+    for (int d = lane; d < HD; d += 32) qs[d] = q[row + d];
+    __syncwarp();
+    float mx = -INFINITY;
+    for (int j = lane; j < n; j += 32) {
+      const float *kr = sK + j * (HD + 1);
+      float sc = 0.0f;
+#pragma unroll 16
+      for (int d = 0; d < HD; ++d) sc = fmaf(qs[d], kr[d], sc);
+      sc = __fmul_rn(sc, scale);
+      ps[j] = sc;
+      mx = fmaxf(mx, sc);
+    }
+    mx = warp_max(mx);
+    float l = 0.0f;
+    for (int j = lane; j < n; j += 32) {
+      const float pj = expf(__fsub_rn(ps[j], mx));
+      ps[j] = pj;
+      l = __fadd_rn(l, pj);
+    }
+    l = warp_sum(l);
+    __syncwarp();
+    float o[EPL];
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) o[e] = 0.0f;
+    for (int j = 0; j < n; ++j) {
+      const float pj = ps[j];
+      const float *vr = sV + j * HD + lane * EPL;
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) o[e] = fmaf(pj, vr[e], o[e]);
+    }
+    const float inv = __fdiv_rn(1.0f, l);  // l >= 1: the max key contributes exp(0)
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) out[row + lane * EPL + e] = __fmul_rn(o[e], inv);
+    __syncwarp();  // qs / ps are rewritten by the next query
+  }
+}
+
 static int grid_for(long n) { return (int)std::max(1l, std::min((n + 255) / 256, 148l * 16)); }
 
 }  // namespace qasr
@@ -124,6 +197,56 @@ extern "C" int qasr_conv2d(float *out, const float *input, const float *weight, 
   return QASR_OK;
 }
 
+namespace qasr {
+constexpr int kBidirMaxSmem = 200 * 1024;
+
+size_t bidir_smem_bytes(int head_dim, int kt) {
+  return ((size_t)kt * (head_dim + 1) + (size_t)kt * head_dim + 8 * head_dim + 8 * (size_t)kt) * 4;
+}
+
+// Windowed attention with the longest window known (max_window keys).
+int bidir_attention_launch(float *out, const float *q, const float *k, const float *v, int seq, int n_heads,
+                           int head_dim, float scale, const int32_t *window_starts, int n_windows, int max_window,
+                           cudaStream_t st) {
+  const size_t smem = bidir_smem_bytes(head_dim, max_window);
+  if (max_window > 0 && smem <= (size_t)kBidirMaxSmem) {
+    static bool attr_set[64][2] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int which = head_dim == 64 ? 0 : 1;
+    if (dev >= 0 && dev < 64 && !attr_set[dev][which]) {
+      cudaError_t e = head_dim == 64
+                          ? cudaFuncSetAttribute(bidir_attention_staged_kernel<2>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, kBidirMaxSmem)
+                          : cudaFuncSetAttribute(bidir_attention_staged_kernel<4>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, kBidirMaxSmem);
+      if (int rc = cuda_status(e, "qasr_bidirectional_attention: smem attribute")) return rc;
+      attr_set[dev][which] = true;
+    }
+    // about two queries per warp of each (window, head)
+    const int qz = std::max(1, (max_window + 15) / 16);
+    const dim3 grid((unsigned)n_windows, (unsigned)n_heads, (unsigned)qz);
+    if (head_dim == 64)
+      bidir_attention_staged_kernel<2><<<grid, 256, smem, st>>>(out, q, k, v, seq, n_heads, scale, window_starts,
+                                                                 max_window);
+    else
+      bidir_attention_staged_kernel<4><<<grid, 256, smem, st>>>(out, q, k, v, seq, n_heads, scale, window_starts,
+                                                                 max_window);
+    return launch_status("qasr_bidirectional_attention");
+  }
+  const long tasks = (long)seq * n_heads;
+  const int grid = (int)((tasks + 7) / 8);
+  if (head_dim == 64)
+    bidir_attention_kernel<2><<<grid, 256, 0, st>>>(out, q, k, v, seq, n_heads, scale, window_starts, n_windows);
+  else
+    bidir_attention_kernel<4><<<grid, 256, 0, st>>>(out, q, k, v, seq, n_heads, scale, window_starts, n_windows);
+  return launch_status("qasr_bidirectional_attention");
+}
+}  // namespace qasr
+
+// The window bounds are device data: they are read back once per call to size
+// the shared-memory window (the encoder engine, which knows its windows, calls
+// bidir_attention_launch directly).
 extern "C" int qasr_bidirectional_attention(float *out, const float *q, const float *k, const float *v, int seq,
                                             int n_heads, int head_dim, float scale, const int32_t *window_starts,
                                             int n_windows, void *stream) {
@@ -136,12 +259,15 @@ extern "C" int qasr_bidirectional_attention(float *out, const float *q, const fl
     return QASR_ERR_UNSUPPORTED;
   }
   if (seq == 0) return QASR_OK;
-  const long tasks = (long)seq * n_heads;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const int grid = (int)((tasks + 7) / 8);
-  if (head_dim == 64)
-    bidir_attention_kernel<2><<<grid, 256, 0, st>>>(out, q, k, v, seq, n_heads, scale, window_starts, n_windows);
-  else
-    bidir_attention_kernel<4><<<grid, 256, 0, st>>>(out, q, k, v, seq, n_heads, scale, window_starts, n_windows);
-  return launch_status("qasr_bidirectional_attention");
+  std::vector<int32_t> starts(n_windows + 1);
+  int rc = cuda_status(cudaMemcpyAsync(starts.data(), window_starts, starts.size() * 4, cudaMemcpyDefault, st),
+                       "qasr_bidirectional_attention: window starts");
+  if (!rc) rc = cuda_status(cudaStreamSynchronize(st), "qasr_bidirectional_attention");
+  if (rc) return rc;
+  int max_window = 0;
+  for (int w = 0; w < n_windows; ++w)
+    max_window = std::max(max_window, std::min(seq, starts[w + 1]) - std::max(0, starts[w]));
+  return bidir_attention_launch(out, q, k, v, seq, n_heads, head_dim, scale, window_starts, n_windows, max_window,
+                                st);
 }

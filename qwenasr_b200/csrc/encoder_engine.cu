@@ -22,20 +22,75 @@
 #include <vector>
 
 #include "common.cuh"
+#include "umma.cuh"
 
 namespace qasr {
 
 constexpr int kConvHidden = 480;  // CONV_HIDDEN (config.rs:23)
 constexpr int kMelBins = 128;
+constexpr int kStemGroup = 32;  // chunks per conv-stem pass (bounds the patch buffers on long audio)
 
-// reshaped[t, ch*h3 + f] = c3[ch, f, t]
-__global__ void __launch_bounds__(256) conv_reshape_kernel(float *__restrict__ out, const float *__restrict__ c3,
-                                                           int ch_f, int w3) {
-  const long total = (long)ch_f * w3;
+inline int grid_of(long n) { return (int)std::max(1l, std::min((n + 255) / 256, 148l * 16)); }
+
+// The conv stem runs on B chunks at once in channel-last layout: the
+// activation of chunk b at (row h, column w), channel c is act[((b*H + h)*W +
+// w)*C + c].  Each convolution is then one GEMM over all B*h_out*w_out output
+// positions: colsT[(b*h_out + oh)*w_out + ow, (ic*3 + ki)*3 + kj] (3x3
+// kernel, stride 2, padding 1, every chunk padded on its own as in the
+// reference's per-chunk kernels::conv2d) times the [c_out, c_in*9] weights.
+
+// conv1's patches straight from the mel [128, mel_frames]: chunk b covers
+// frames first + b*cs .. + cw (one input channel).
+__global__ void __launch_bounds__(256) im2col_mel_kernel(float *__restrict__ colsT, const float *__restrict__ mel,
+                                                         int mel_frames, int first, int cs, int cw, int B, int h_out,
+                                                         int w_out) {
+  const long total = (long)B * h_out * w_out * 9;
   for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
-    const int t = (int)(i / ch_f), cf = (int)(i % ch_f);
-    out[i] = c3[(long)cf * w3 + t];
+    const long r = i / 9;
+    const int p = (int)(i - r * 9), ki = p / 3, kj = p % 3;
+    const int ow = (int)(r % w_out), oh = (int)((r / w_out) % h_out), b = (int)(r / ((long)w_out * h_out));
+    const int ih = oh * 2 + ki - 1, iw = ow * 2 + kj - 1;
+    colsT[i] = (ih >= 0 && ih < kMelBins && iw >= 0 && iw < cw)
+                   ? mel[(long)ih * mel_frames + first + (long)b * cs + iw]
+                   : 0.0f;
   }
+}
+
+// patches of a channel-last activation [B, h_in, w_in, C]
+__global__ void __launch_bounds__(256) im2col_cl_kernel(float *__restrict__ colsT, const float *__restrict__ act,
+                                                        int C, int h_in, int w_in, int B, int h_out, int w_out) {
+  const long patch = (long)C * 9;
+  const long total = (long)B * h_out * w_out * patch;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const long r = i / patch;
+    const int p = (int)(i - r * patch), ic = p / 9, kk = p % 9, ki = kk / 3, kj = kk % 3;
+    const int ow = (int)(r % w_out), oh = (int)((r / w_out) % h_out), b = (int)(r / ((long)w_out * h_out));
+    const int ih = oh * 2 + ki - 1, iw = ow * 2 + kj - 1;
+    colsT[i] = (ih >= 0 && ih < h_in && iw >= 0 && iw < w_in) ? act[(((long)b * h_in + ih) * w_in + iw) * C + ic]
+                                                               : 0.0f;
+  }
+}
+
+// the encoder.rs:322-331 reshape per chunk, from channel-last c3 [B, h3, w3, C]:
+// reshaped[b*w3 + t, c*h3 + f] = c3[b, f, t, c]
+__global__ void __launch_bounds__(256) conv_reshape_cl_kernel(float *__restrict__ out, const float *__restrict__ c3,
+                                                              int C, int h3, int w3, int B) {
+  const long row = (long)C * h3;
+  const long total = (long)B * w3 * row;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const long bt = i / row;
+    const int cf = (int)(i - bt * row), c = cf / h3, f = cf % h3;
+    const int t = (int)(bt % w3), b = (int)(bt / w3);
+    out[i] = c3[(((long)b * h3 + f) * w3 + t) * C + c];
+  }
+}
+
+// x[b*w3 + t, :] += pe[t, :] (every chunk restarts its positions, encoder.rs:339-343)
+__global__ void __launch_bounds__(256) add_chunk_pe_kernel(float *__restrict__ x, const float *__restrict__ pe, int B,
+                                                           int w3, int D) {
+  const long total = (long)B * w3 * D;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x)
+    x[i] = __fadd_rn(x[i], pe[i % ((long)w3 * D)]);
 }
 
 // One projection matrix [rows, cols]: f32, or INT8 with f32 row scales.
@@ -44,8 +99,10 @@ struct EncMat {
   float *f = nullptr;
   int8_t *q = nullptr;
   float *s = nullptr;
+  F32Weight pw;  // digit planes of f (when the tensor-core GEMM takes the shape)
   bool ready() const { return f || q; }
   void release() {
+    f32_weight_free(&pw);
     if (f) cudaFree(f);
     if (q) cudaFree(q);
     if (s) cudaFree(s);
@@ -73,12 +130,15 @@ struct qasr_encoder {
   float *ln_post_w = nullptr, *ln_post_b = nullptr, *proj1_b = nullptr, *proj2_b = nullptr;
   std::vector<void *> allocs;
   // activations, grown on demand
-  int tok_cap = 0, frames_cap = 0;
+  int tok_cap = 0, stem_cap = 0;
+  qasr::F32Weight conv_pw[3];  // conv2 / conv3 weights as digit planes (conv1 has K = 9: CUDA cores)
   void *act = nullptr;
   float *x = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr, *proj = nullptr,
         *mid = nullptr, *out = nullptr, *pe = nullptr;
   void *conv_buf = nullptr;
-  float *mel_chunk = nullptr, *c1 = nullptr, *c2 = nullptr, *c3 = nullptr, *reshaped = nullptr;
+  float *cols = nullptr, *act_a = nullptr, *act_b = nullptr;  // stem patches, ping-pong activations
+  float *mel_dev = nullptr;  // device copy of a host mel input
+  size_t mel_cap = 0;
   int32_t *win = nullptr;
   int win_cap = 0;
 };
@@ -118,7 +178,13 @@ static int mat_set_f32(qasr_encoder *e, EncMat &m, const float *src, const char 
     int rc = cuda_status(cudaMalloc(&m.f, n * 4), "qasr_encoder: cudaMalloc");
     if (rc) return rc;
   }
-  return cuda_status(cudaMemcpyAsync(m.f, src, n * 4, cudaMemcpyDefault, e->stream), what);
+  int rc = cuda_status(cudaMemcpyAsync(m.f, src, n * 4, cudaMemcpyDefault, e->stream), what);
+  if (rc) return rc;
+  // the constant operand's digit planes, once (unsupported shapes stay on qasr_linear)
+  if ((rc = cuda_status(cudaStreamSynchronize(e->stream), what))) return rc;
+  f32_weight_free(&m.pw);
+  rc = f32_weight_prepare(&m.pw, m.f, m.rows, m.cols, e->stream);
+  return rc == QASR_ERR_UNSUPPORTED ? QASR_OK : rc;
 }
 
 // INT8 weights + row scales into m (replacing an f32 copy).
@@ -148,8 +214,34 @@ static int mat_apply(float *y, const float *x, const EncMat &m, const float *bia
   if (m.q)
     return bias ? qasr_linear_int8(y, x, m.q, m.s, bias, T, m.cols, m.rows, st)
                 : qasr_linear_nobias_int8(y, x, m.q, m.s, T, m.cols, m.rows, st);
+  if (m.pw.planes) {
+    const int rc = f32_gemm_prepared(y, m.rows, x, m.cols, m.pw, bias, T, st);
+    if (rc != QASR_ERR_UNSUPPORTED) return rc;
+  }
   return bias ? qasr_linear(y, x, m.f, bias, T, m.cols, m.rows, st)
               : qasr_linear_nobias(y, x, m.f, T, m.cols, m.rows, st);
+}
+
+// conv i (1 or 2) of the stem over `rows` patch rows: y [rows, 480] =
+// cols [rows, 480*9] W_i^T + b_i.
+static int conv_gemm(qasr_encoder *e, int i, float *y, const float *cols, int rows, cudaStream_t st) {
+  const int CH = kConvHidden;
+  if (e->conv_pw[i].planes) {
+    const int rc = f32_gemm_prepared(y, CH, cols, (long)CH * 9, e->conv_pw[i], e->conv_b[i], rows, st);
+    if (rc != QASR_ERR_UNSUPPORTED) return rc;
+  }
+  return f32_gemm_fallback(y, cols, e->conv_w[i], e->conv_b[i], rows, CH * 9, CH, st);
+}
+
+// digit planes of conv2 / conv3 after their weights change
+static int prepare_convs(qasr_encoder *e) {
+  int rc = cuda_status(cudaStreamSynchronize(e->stream), "qasr_encoder: conv weights");
+  for (int i = 1; i < 3 && !rc; ++i) {
+    f32_weight_free(&e->conv_pw[i]);
+    rc = f32_weight_prepare(&e->conv_pw[i], e->conv_w[i], kConvHidden, kConvHidden * 9, e->stream);
+    if (rc == QASR_ERR_UNSUPPORTED) rc = QASR_OK;
+  }
+  return rc;
 }
 
 static std::vector<EncMat *> enc_mats(qasr_encoder *e) {
@@ -164,10 +256,12 @@ extern "C" void qasr_encoder_free(qasr_encoder *e) {
   cudaSetDevice(e->device);
   if (e->stream) cudaStreamSynchronize(e->stream);
   for (EncMat *m : enc_mats(e)) m->release();
+  for (auto &pw : e->conv_pw) f32_weight_free(&pw);
   for (void *p : e->allocs) cudaFree(p);
   if (e->act) cudaFree(e->act);
   if (e->conv_buf) cudaFree(e->conv_buf);
   if (e->win) cudaFree(e->win);
+  if (e->mel_dev) cudaFree(e->mel_dev);
   if (e->stream) cudaStreamDestroy(e->stream);
   delete e;
 }
@@ -254,6 +348,7 @@ extern "C" int qasr_encoder_set_conv(qasr_encoder *e, const float *conv1_w, cons
     if (!rc) rc = enc_copy(e, e->conv_b[i], b[i], CH, "conv bias");
   }
   if (!rc) rc = mat_set_f32(e, e->conv_out, conv_out_w, "conv_out weight");
+  if (!rc) rc = prepare_convs(e);
   if (!rc) rc = cuda_status(cudaStreamSynchronize(e->stream), "qasr_encoder_set_conv");
   (void)h3;
   return rc;
@@ -277,6 +372,7 @@ extern "C" int qasr_encoder_set_conv_int8(qasr_encoder *e, const float *conv1_w,
     if (!rc) rc = enc_copy(e, e->conv_b[i], b[i], CH, "conv bias");
   }
   if (!rc) rc = mat_set_i8(e, e->conv_out, conv_out, conv_out_s, "conv_out weight");
+  if (!rc) rc = prepare_convs(e);
   if (!rc) rc = cuda_status(cudaStreamSynchronize(e->stream), "qasr_encoder_set_conv_int8");
   return rc;
 }
@@ -412,14 +508,16 @@ extern "C" int qasr_encoder_forward(qasr_encoder *e, const float *mel, int mel_f
   }
   cudaStream_t st = e->stream;
   int rc = QASR_OK;
-  // buffers
+  // buffers: per-token activations, and the conv stem of up to kStemGroup chunks
   const int h1 = (kMelBins + 2 - 3) / 2 + 1, h2 = (h1 + 2 - 3) / 2 + 1, h3 = (h2 + 2 - 3) / 2 + 1;
   const int w1m = (cs + 2 - 3) / 2 + 1, w2m = (w1m + 2 - 3) / 2 + 1, w3m = (w2m + 2 - 3) / 2 + 1;
-  if (T > e->tok_cap || mel_frames > e->frames_cap) {
+  const int n_full = mel_frames / cs, tail = mel_frames % cs;
+  const int gmax = std::max(1, std::min(n_full, kStemGroup));
+  if (T > e->tok_cap) {
     if ((rc = cuda_status(cudaStreamSynchronize(st), "qasr_encoder_forward"))) return rc;
     if (e->act) cudaFree(e->act);
-    if (e->conv_buf) cudaFree(e->conv_buf);
-    e->act = e->conv_buf = nullptr;
+    e->act = nullptr;
+    e->tok_cap = 0;
     const size_t per_tok = (size_t)7 * D + F + O + D;  // x xn q k v attn proj | mid | out | pe
     if ((rc = cuda_status(cudaMalloc(&e->act, per_tok * T * 4), "qasr_encoder_forward: buffers"))) return rc;
     float *f = static_cast<float *>(e->act);
@@ -434,46 +532,80 @@ extern "C" int qasr_encoder_forward(qasr_encoder *e, const float *mel, int mel_f
     e->mid = take(F);
     e->out = take(O);
     e->pe = take(D);
-    const size_t conv_elems = (size_t)kMelBins * cs + (size_t)CH * h1 * w1m + (size_t)CH * h2 * w2m +
-                              (size_t)CH * h3 * w3m + (size_t)w3m * CH * h3;
-    if ((rc = cuda_status(cudaMalloc(&e->conv_buf, conv_elems * 4), "qasr_encoder_forward: conv buffers"))) return rc;
-    f = static_cast<float *>(e->conv_buf);
-    e->mel_chunk = f;
-    f += (size_t)kMelBins * cs;
-    e->c1 = f;
-    f += (size_t)CH * h1 * w1m;
-    e->c2 = f;
-    f += (size_t)CH * h2 * w2m;
-    e->c3 = f;
-    f += (size_t)CH * h3 * w3m;
-    e->reshaped = f;
     e->tok_cap = T;
-    e->frames_cap = mel_frames;
   }
-  // ---- conv stem per chunk (encoder.rs:281-348)
+  if (gmax > e->stem_cap) {
+    if ((rc = cuda_status(cudaStreamSynchronize(st), "qasr_encoder_forward"))) return rc;
+    if (e->conv_buf) cudaFree(e->conv_buf);
+    e->conv_buf = nullptr;
+    e->stem_cap = 0;
+    const size_t pos1 = (size_t)gmax * h1 * w1m, pos2 = (size_t)gmax * h2 * w2m, pos3 = (size_t)gmax * h3 * w3m;
+    const size_t cols = std::max({pos1 * 9, pos2 * CH * 9, pos3 * CH * 9});
+    if ((rc = cuda_status(cudaMalloc(&e->conv_buf, (cols + pos1 * CH + pos2 * CH) * 4),
+                          "qasr_encoder_forward: conv buffers")))
+      return rc;
+    e->cols = static_cast<float *>(e->conv_buf);
+    e->act_a = e->cols + cols;
+    e->act_b = e->act_a + pos1 * CH;
+    e->stem_cap = gmax;
+  }
+  // the stem kernels read the mel directly: a host mel is copied to the device first
+  {
+    cudaPointerAttributes pa{};
+    const bool on_dev = cudaPointerGetAttributes(&pa, mel) == cudaSuccess &&
+                        (pa.type == cudaMemoryTypeDevice || pa.type == cudaMemoryTypeManaged);
+    cudaGetLastError();  // an unknown pointer is not an error here
+    if (!on_dev) {
+      const size_t bytes = (size_t)kMelBins * mel_frames * 4;
+      if (bytes > e->mel_cap) {
+        if ((rc = cuda_status(cudaStreamSynchronize(st), "qasr_encoder_forward"))) return rc;
+        if (e->mel_dev) cudaFree(e->mel_dev);
+        e->mel_dev = nullptr;
+        e->mel_cap = 0;
+        if ((rc = cuda_status(cudaMalloc(&e->mel_dev, bytes), "qasr_encoder_forward: mel buffer"))) return rc;
+        e->mel_cap = bytes;
+      }
+      if ((rc = cuda_status(cudaMemcpyAsync(e->mel_dev, mel, bytes, cudaMemcpyDefault, st), "qasr_encoder_forward: mel")))
+        return rc;
+      mel = e->mel_dev;
+    }
+  }
+  // ---- conv stem (encoder.rs:281-348): groups of full chunks, then the tail chunk
   int tok = 0;
-  for (int s = 0; s < mel_frames && !rc; s += cs) {
-    const int cw = std::min(cs, mel_frames - s);
+  for (int first = 0; first < mel_frames && !rc;) {
+    const bool full = first + cs <= mel_frames;
+    const int B = full ? std::min(kStemGroup, (mel_frames - first) / cs) : 1;
+    const int cw = full ? cs : tail;
     const int w1 = (cw + 2 - 3) / 2 + 1, w2 = (w1 + 2 - 3) / 2 + 1, w3 = (w2 + 2 - 3) / 2 + 1;
-    // chunk_mel [128, cw] from mel [128, mel_frames]
-    rc = cuda_status(cudaMemcpy2DAsync(e->mel_chunk, (size_t)cw * 4, mel + s, (size_t)mel_frames * 4, (size_t)cw * 4,
-                                       kMelBins, cudaMemcpyDefault, st),
-                     "qasr_encoder_forward: mel chunk");
-    if (!rc) rc = qasr_conv2d(e->c1, e->mel_chunk, e->conv_w[0], e->conv_b[0], 1, CH, kMelBins, cw, 3, 3, 2, 1, st);
-    if (!rc) rc = qasr_gelu(e->c1, (int64_t)CH * h1 * w1, st);
-    if (!rc) rc = qasr_conv2d(e->c2, e->c1, e->conv_w[1], e->conv_b[1], CH, CH, h1, w1, 3, 3, 2, 1, st);
-    if (!rc) rc = qasr_gelu(e->c2, (int64_t)CH * h2 * w2, st);
-    if (!rc) rc = qasr_conv2d(e->c3, e->c2, e->conv_w[2], e->conv_b[2], CH, CH, h2, w2, 3, 3, 2, 1, st);
-    if (!rc) rc = qasr_gelu(e->c3, (int64_t)CH * h3 * w3, st);
+    const long r1 = (long)B * h1 * w1, r2 = (long)B * h2 * w2, r3 = (long)B * h3 * w3;
+    im2col_mel_kernel<<<grid_of(r1 * 9), 256, 0, st>>>(e->cols, mel, mel_frames, first, cs, cw, B, h1, w1);
+    rc = launch_status("qasr_encoder_forward: conv1 patches");
+    if (!rc) rc = f32_gemm_fallback(e->act_a, e->cols, e->conv_w[0], e->conv_b[0], (int)r1, 9, CH, st);
+    if (!rc) rc = qasr_gelu(e->act_a, (int64_t)r1 * CH, st);
     if (!rc) {
-      const long n = (long)CH * h3 * w3;
-      conv_reshape_kernel<<<(int)std::min((n + 255) / 256, 4096l), 256, 0, st>>>(e->reshaped, e->c3, CH * h3, w3);
+      im2col_cl_kernel<<<grid_of(r2 * CH * 9), 256, 0, st>>>(e->cols, e->act_a, CH, h1, w1, B, h2, w2);
+      rc = launch_status("qasr_encoder_forward: conv2 patches");
+    }
+    if (!rc) rc = conv_gemm(e, 1, e->act_b, e->cols, (int)r2, st);
+    if (!rc) rc = qasr_gelu(e->act_b, (int64_t)r2 * CH, st);
+    if (!rc) {
+      im2col_cl_kernel<<<grid_of(r3 * CH * 9), 256, 0, st>>>(e->cols, e->act_b, CH, h2, w2, B, h3, w3);
+      rc = launch_status("qasr_encoder_forward: conv3 patches");
+    }
+    if (!rc) rc = conv_gemm(e, 2, e->act_a, e->cols, (int)r3, st);
+    if (!rc) rc = qasr_gelu(e->act_a, (int64_t)r3 * CH, st);
+    if (!rc) {
+      conv_reshape_cl_kernel<<<grid_of(r3 * CH), 256, 0, st>>>(e->cols, e->act_a, CH, h3, w3, B);
       rc = launch_status("qasr_encoder_forward: reshape");
     }
-    if (!rc) rc = mat_apply(e->x + (size_t)tok * D, e->reshaped, e->conv_out, nullptr, w3, st);
+    if (!rc) rc = mat_apply(e->x + (size_t)tok * D, e->cols, e->conv_out, nullptr, B * w3, st);
     if (!rc) rc = qasr_sinusoidal_pe(e->pe, w3, D, st);
-    if (!rc) rc = qasr_add_inplace(e->x + (size_t)tok * D, e->pe, (int64_t)w3 * D, st);
-    tok += w3;
+    if (!rc) {
+      add_chunk_pe_kernel<<<grid_of((long)B * w3 * D), 256, 0, st>>>(e->x + (size_t)tok * D, e->pe, B, w3, D);
+      rc = launch_status("qasr_encoder_forward: positions");
+    }
+    tok += B * w3;
+    first += B * cw;
   }
   if (rc) return rc;
   // ---- attention windows (encoder.rs:350-357)
@@ -501,7 +633,9 @@ extern "C" int qasr_encoder_forward(qasr_encoder *e, const float *mel, int mel_f
     if (!rc) rc = mat_apply(e->q, e->xn, L.wq, L.bq, T, st);
     if (!rc) rc = mat_apply(e->k, e->xn, L.wk, L.bk, T, st);
     if (!rc) rc = mat_apply(e->v, e->xn, L.wv, L.bv, T, st);
-    if (!rc) rc = qasr_bidirectional_attention(e->attn, e->q, e->k, e->v, T, c.n_heads, c.head_dim, scale, e->win, nw, st);
+    if (!rc)
+      rc = bidir_attention_launch(e->attn, e->q, e->k, e->v, T, c.n_heads, c.head_dim, scale, e->win, nw,
+                                  std::min(wsize, T), st);
     if (!rc) rc = mat_apply(e->proj, e->attn, L.wo, L.bo, T, st);
     if (!rc) rc = qasr_add_inplace(e->x, e->proj, td, st);
     if (!rc) rc = qasr_layer_norm(e->xn, e->x, L.ffn_norm_w, L.ffn_norm_b, T, D, 1e-5f, st);

@@ -47,11 +47,29 @@ int int8_gemm(float *y, long y_stride, const float *x, long x_stride, const int8
 // cores (three digit planes per operand); QASR_ERR_UNSUPPORTED as above.
 int f32_gemm(float *y, long y_stride, const float *x, long x_stride, const float *w, const float *bias, int T, int K,
              int N, cudaStream_t st);
+// f32 weights [N, K] held as their digit planes (built once).
+struct F32Weight {
+  int8_t *planes = nullptr;  // [3N, K]
+  float *factors = nullptr;  // [N]
+  int N = 0, K = 0;
+  CUtensorMap tm;
+};
+// QASR_ERR_UNSUPPORTED for shapes the tensor-core GEMM does not take.
+int f32_weight_prepare(F32Weight *pw, const float *w, int N, int K, cudaStream_t st);
+void f32_weight_free(F32Weight *pw);
+int f32_gemm_prepared(float *y, long y_stride, const float *x, long x_stride, const F32Weight &w, const float *bias,
+                      int T, cudaStream_t st);
 // The same on CUDA cores, any shape.
 int f32_gemm_fallback(float *y, const float *x, const float *w, const float *bias, int T, int K, int N,
                       cudaStream_t st);
 
 // Driver entry point cuTensorMapEncodeTiled (resolved once).
 void *tensor_map_encoder();
+
+// kernels::bidirectional_attention with the longest window (keys) known on
+// the host (encoder.cu).
+int bidir_attention_launch(float *out, const float *q, const float *k, const float *v, int seq, int n_heads,
+                           int head_dim, float scale, const int32_t *window_starts, int n_windows, int max_window,
+                           cudaStream_t st);
 
 }  // namespace qasr

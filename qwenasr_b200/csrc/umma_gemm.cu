@@ -392,6 +392,57 @@ int f32_gemm(float *y, long y_stride, const float *x, long x_stride, const float
   return gemm_launch<3>(p, st);
 }
 
+// f32 weights [N, K] converted once into their three digit planes (rows of
+// plane a at a*N) and per-row factors, with the tensor map: the constant
+// operand of f32_gemm_prepared.
+int f32_weight_prepare(F32Weight *pw, const float *w, int N, int K, cudaStream_t st) {
+  *pw = F32Weight{};
+  if (!w || N < 128 || K < 128 || K % 16 || (reinterpret_cast<uintptr_t>(w) & 15)) return QASR_ERR_UNSUPPORTED;
+  int rc = cuda_status(cudaMalloc(&pw->planes, (size_t)3 * N * K), "f32 weight digits");
+  if (!rc) rc = cuda_status(cudaMalloc(&pw->factors, (size_t)N * 4), "f32 weight factors");
+  if (!rc) rc = int8_map(&pw->tm, pw->planes, 3l * N, K, 128);
+  if (!rc) rc = digit_rows(pw->planes, pw->factors, w, K, N, N, K, N, st);
+  if (rc) {
+    f32_weight_free(pw);
+    return rc;
+  }
+  pw->N = N;
+  pw->K = K;
+  return QASR_OK;
+}
+
+void f32_weight_free(F32Weight *pw) {
+  if (pw->planes) cudaFree(pw->planes);
+  if (pw->factors) cudaFree(pw->factors);
+  *pw = F32Weight{};
+}
+
+// f32_gemm with the weight operand prepared: only the activation rows are
+// converted per call.
+int f32_gemm_prepared(float *y, long y_stride, const float *x, long x_stride, const F32Weight &w, const float *bias,
+                      int T, cudaStream_t st) {
+  if (!w.planes || !gemm_shape_ok(x, x_stride, T, w.K, w.N)) return QASR_ERR_UNSUPPORTED;
+  const int K = w.K, NB = (T + kGTok - 1) / kGTok, T_pad = NB * kGTok;
+  void *dbuf = nullptr, *qbuf = nullptr;
+  int rc;
+  if ((rc = dev_scratch(kScratchDigits, (size_t)NB * kGRows * K, &dbuf))) return rc;
+  if ((rc = dev_scratch(kScratchDigitScale, (size_t)T_pad * 4, &qbuf))) return rc;
+  GemmParams p{};
+  p.tm_w = w.tm;
+  if ((rc = int8_map(&p.tm_d, static_cast<int8_t *>(dbuf), (long)NB * kGRows, K, kGRows))) return rc;
+  p.dq = static_cast<float *>(qbuf);
+  p.scales = w.factors;
+  p.bias = bias;
+  p.y = y;
+  p.y_stride = y_stride;
+  p.T = T;
+  p.K = K;
+  p.N = w.N;
+  if ((rc = digit_rows(static_cast<int8_t *>(dbuf), static_cast<float *>(qbuf), x, x_stride, T, T_pad, K, kGTok, st)))
+    return rc;
+  return gemm_launch<3>(p, st);
+}
+
 // ------------------------------------------------- CUDA-core fallback SGEMM --
 // y[t, o] = sum_k x[t, k] w[o, k] (+ b[o]) for shapes the tensor-core GEMM
 // does not take (K not a multiple of 16, unaligned rows): 32x32 output tiles,

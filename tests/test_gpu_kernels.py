@@ -464,11 +464,17 @@ def test_conv2d_encoder_stem(c_in, c_out, h, w, bias):
     assert ok, err
 
 
-@pytest.mark.parametrize("seq,n_heads,hd,win", [(390, 14, 64, 104), (37, 2, 128, 37), (50, 3, 64, 7)])
+@pytest.mark.parametrize("seq,n_heads,hd,win", [(390, 14, 64, 104), (37, 2, 128, 37), (50, 3, 64, 7),
+                                                (1000, 2, 128, 1000), (300, 2, 64, "ragged")])
 def test_bidirectional_attention(orc, seq, n_heads, hd, win):
-    rng = np.random.default_rng(seq + win)
+    """Windows held in shared memory, a window too long for it (1000 keys of
+    128 dims: the L2 kernel), and ragged windows including one-key ones."""
+    rng = np.random.default_rng(seq + (win if win != "ragged" else 1))
     q, k, v = (rng.standard_normal((seq, n_heads * hd)).astype(np.float32) for _ in range(3))
-    starts = np.array(list(range(0, seq, win)) + [seq], np.int32)
+    if win == "ragged":
+        starts = np.array([0, 1, 2, 40, 41, 170, 299, seq], np.int32)
+    else:
+        starts = np.array(list(range(0, seq, win)) + [seq], np.int32)
     scale = 1.0 / math.sqrt(hd)
     out = torch.empty(seq, n_heads * hd, device=DEV)
     K.bidirectional_attention(out, T(q), T(k), T(v), seq, n_heads, hd, scale, T(starts), len(starts) - 1)
