@@ -490,6 +490,55 @@ int qasr_transcribe_batch(qasr_decoder *dec, qasr_encoder *enc, const float *con
                           int n_segments, const int32_t *prompt_tokens, int n_prompt, const int32_t *force_tokens,
                           int n_force, int max_new, int stop_at_eos, int32_t *ids, int ids_stride, int *n_ids);
 
+/* ======================================================================
+ * Streaming transcription (transcribe.rs:445-1495), token ids out
+ * ==================================================================== */
+
+typedef struct qasr_stream qasr_stream;
+
+typedef struct {
+  float chunk_sec;            /* stream_chunk_sec: audio per step (2.0) */
+  int rollback;               /* stream_rollback: uncommitted tail tokens (5) */
+  int unfixed_chunks;         /* stream_unfixed_chunks: chunks before commits start (2) */
+  int max_new_tokens;         /* stream_max_new_tokens per chunk (32; <= 0 means 32) */
+  int past_text_conditioning; /* feed the committed tokens back as prompt (0) */
+  int incremental;            /* 1: stream_push_audio / StreamState semantics; 0: transcribe_stream */
+} qasr_stream_config;
+
+/* The QwenCtx defaults (context.rs:499-512), incremental. */
+void qasr_stream_default_config(qasr_stream_config *cfg);
+/* A stream over an encoder and a decoder on one device; it decodes in the
+ * decoder's KV slot 0 (batch of one).  NULL on failure. */
+qasr_stream *qasr_stream_create(qasr_decoder *dec, qasr_encoder *enc, const qasr_stream_config *cfg);
+void qasr_stream_free(qasr_stream *s);
+/* Prompt / forced-language token ids (placed as in transcribe_segment). */
+int qasr_stream_set_prompt(qasr_stream *s, const int32_t *prompt, int n_prompt, const int32_t *force, int n_force);
+/* Byte length of every token's text (tokenizer.decode_bytes(t).len()), used by
+ * the byte-level realignment of committed tokens after a re-anchor. */
+int qasr_stream_set_token_bytes(qasr_stream *s, const int32_t *bytes, int n);
+/* stream_push_audio (transcribe.rs:960-1495): samples = all audio received
+ * so far (16 kHz f32, host or device); processes every complete chunk after
+ * the cursor (and the rest when finalize).  emitted (host, cap entries)
+ * receives the token ids committed by this call.  With incremental = 0, one
+ * call with the whole buffer and finalize = 1 is transcribe_stream. */
+int qasr_stream_push(qasr_stream *s, const float *samples, int64_t n_samples, int finalize, int32_t *emitted, int cap,
+                     int *n_emitted);
+/* StreamState::reset / audio_cursor / audio_trim_request / apply_audio_trim. */
+int qasr_stream_reset(qasr_stream *s);
+int64_t qasr_stream_audio_cursor(const qasr_stream *s);
+int64_t qasr_stream_trim_request(const qasr_stream *s);
+int qasr_stream_apply_trim(qasr_stream *s, int64_t trim);
+/* All committed ids so far (StreamState::text) and the decoded but not yet
+ * committed ones (unfixed_text); *n = the full count, up to cap copied. */
+int qasr_stream_emitted(const qasr_stream *s, int32_t *ids, int cap, int *n);
+int qasr_stream_unfixed(const qasr_stream *s, int32_t *ids, int cap, int *n);
+
+/* Host helpers of the transcription drivers (no GPU):
+ * stream_tail_repeat_blocks (transcribe.rs:42-59) and find_split_point
+ * (transcribe.rs:250-275). */
+int qasr_stream_tail_repeat(const int32_t *tokens, int n, int max_period, int *best_reps, int *best_period);
+int64_t qasr_find_split_point(const float *samples, int64_t n, int64_t target_sample, float search_sec);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

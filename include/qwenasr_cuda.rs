@@ -90,6 +90,22 @@ pub struct QasrQint8 {
     _private: [u8; 0],
 }
 
+#[repr(C)]
+pub struct QasrStream {
+    _private: [u8; 0],
+}
+
+#[repr(C)]
+#[derive(Clone, Copy)]
+pub struct QasrStreamConfig {
+    pub chunk_sec: f32,
+    pub rollback: c_int,
+    pub unfixed_chunks: c_int,
+    pub max_new_tokens: c_int,
+    pub past_text_conditioning: c_int,
+    pub incremental: c_int,
+}
+
 #[link(name = "qwenasr_b200")]
 extern "C" {
     pub fn qasr_last_error() -> *const c_char;
@@ -167,4 +183,18 @@ extern "C" {
     pub fn qasr_qint8_load_encoder(f: *const QasrQint8, enc: *mut QasrEncoder) -> c_int;
     pub fn qasr_transcribe_prompt_len(n_audio_tokens: c_int, n_prompt: c_int, n_force: c_int) -> c_int;
     pub fn qasr_transcribe_batch(dec: *mut QasrDecoder, enc: *mut QasrEncoder, samples: *mut *const f32, n_samples: *const c_int, n_segments: c_int, prompt_tokens: *const i32, n_prompt: c_int, force_tokens: *const i32, n_force: c_int, max_new: c_int, stop_at_eos: c_int, ids: *mut i32, ids_stride: c_int, n_ids: *mut c_int) -> c_int;
+    pub fn qasr_stream_default_config(cfg: *mut QasrStreamConfig);
+    pub fn qasr_stream_create(dec: *mut QasrDecoder, enc: *mut QasrEncoder, cfg: *const QasrStreamConfig) -> *mut QasrStream;
+    pub fn qasr_stream_free(s: *mut QasrStream);
+    pub fn qasr_stream_set_prompt(s: *mut QasrStream, prompt: *const i32, n_prompt: c_int, force: *const i32, n_force: c_int) -> c_int;
+    pub fn qasr_stream_set_token_bytes(s: *mut QasrStream, bytes: *const i32, n: c_int) -> c_int;
+    pub fn qasr_stream_push(s: *mut QasrStream, samples: *const f32, n_samples: i64, finalize: c_int, emitted: *mut i32, cap: c_int, n_emitted: *mut c_int) -> c_int;
+    pub fn qasr_stream_reset(s: *mut QasrStream) -> c_int;
+    pub fn qasr_stream_audio_cursor(s: *const QasrStream) -> i64;
+    pub fn qasr_stream_trim_request(s: *const QasrStream) -> i64;
+    pub fn qasr_stream_apply_trim(s: *mut QasrStream, trim: i64) -> c_int;
+    pub fn qasr_stream_emitted(s: *const QasrStream, ids: *mut i32, cap: c_int, n: *mut c_int) -> c_int;
+    pub fn qasr_stream_unfixed(s: *const QasrStream, ids: *mut i32, cap: c_int, n: *mut c_int) -> c_int;
+    pub fn qasr_stream_tail_repeat(tokens: *const i32, n: c_int, max_period: c_int, best_reps: *mut c_int, best_period: *mut c_int) -> c_int;
+    pub fn qasr_find_split_point(samples: *const f32, n: i64, target_sample: i64, search_sec: f32) -> i64;
 }

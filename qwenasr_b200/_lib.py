@@ -111,6 +111,11 @@ class EncLayerWeights(C.Structure):
         "fc1_w", "fc1_b", "fc2_w", "fc2_b")]
 
 
+class StreamConfig(C.Structure):
+    _fields_ = [("chunk_sec", C.c_float), ("rollback", C.c_int), ("unfixed_chunks", C.c_int),
+                ("max_new_tokens", C.c_int), ("past_text_conditioning", C.c_int), ("incremental", C.c_int)]
+
+
 class EncLayerWeightsInt8(C.Structure):
     _fields_ = [(n, C.c_void_p) for n in (
         "attn_norm_w", "attn_norm_b", "wq", "wq_s", "bq", "wk", "wk_s", "bk", "wv", "wv_s", "bv", "wo", "wo_s", "bo",
@@ -139,6 +144,20 @@ _SIGS.update({
     "qasr_qint8_detect": (I, [P, C.POINTER(DecoderConfig), C.POINTER(EncoderConfig)]),
     "qasr_qint8_load_decoder": (I, [P, P]),
     "qasr_qint8_load_encoder": (I, [P, P]),
+    "qasr_stream_default_config": (None, [C.POINTER(StreamConfig)]),
+    "qasr_stream_create": (P, [P, P, C.POINTER(StreamConfig)]),
+    "qasr_stream_free": (None, [P]),
+    "qasr_stream_set_prompt": (I, [P, P, I, P, I]),
+    "qasr_stream_set_token_bytes": (I, [P, P, I]),
+    "qasr_stream_push": (I, [P, P, I64, I, P, I, C.POINTER(C.c_int)]),
+    "qasr_stream_reset": (I, [P]),
+    "qasr_stream_audio_cursor": (I64, [P]),
+    "qasr_stream_trim_request": (I64, [P]),
+    "qasr_stream_apply_trim": (I, [P, I64]),
+    "qasr_stream_emitted": (I, [P, P, I, C.POINTER(C.c_int)]),
+    "qasr_stream_unfixed": (I, [P, P, I, C.POINTER(C.c_int)]),
+    "qasr_stream_tail_repeat": (I, [P, I, I, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
+    "qasr_find_split_point": (I64, [P, I64, I64, F]),
     "qasr_encoder_device": (I, [P]),
     "qasr_transcribe_prompt_len": (I, [I, I, I]),
     "qasr_transcribe_batch": (I, [P, P, P, P, I, P, I, P, I, I, I, P, I, P]),

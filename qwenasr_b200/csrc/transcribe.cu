@@ -18,23 +18,94 @@
 #include <vector>
 
 #include "common.cuh"
+#include "engine.cuh"
 #include "matvec.cuh"
 #include "qwenasr_cuda.h"
 
 namespace qasr {
-namespace {
 
 // transcribe.rs:11-13
-const int32_t kPrefixHead[] = {151644, 8948, 198};
-const int32_t kPrefixTail[] = {151645, 198, 151644, 872, 198, 151669};
-const int32_t kSuffixBase[] = {151670, 151645, 198, 151644, 77091, 198};
-constexpr int32_t kEndOfText = 151643, kImEnd = 151645;  // config.rs:14-15
+const int32_t kPrefixHead[3] = {151644, 8948, 198};
+const int32_t kPrefixTail[6] = {151645, 198, 151644, 872, 198, 151669};
+const int32_t kSuffixBase[6] = {151670, 151645, 198, 151644, 77091, 198};
+
+namespace {
 constexpr int kHead = 3, kTail = 6, kSuffix = 6;
 constexpr int kCheckEvery = 32;
-
-bool is_stop(int32_t t) { return t == kEndOfText || t == kImEnd; }
-
 }  // namespace
+
+bool is_stop_token(int32_t t) { return t == kTokEndOfText || t == kTokImEnd; }
+
+int encode_samples(qasr_encoder *enc, int device, cudaStream_t st, const float *samples, int n_samples, float *rows,
+                   int rows_cap, int *T) {
+  const int frames = qasr_mel_frames(n_samples);
+  if (frames <= 0) {
+    set_error("encode: %d samples (at least 160 needed)", n_samples);
+    return QASR_ERR_INVALID;
+  }
+  void *audio = nullptr, *mel = nullptr;
+  int rc;
+  if ((rc = dev_scratch(kScratchAudio, (size_t)n_samples * 4, &audio))) return rc;
+  if ((rc = dev_scratch(kScratchMelOut, (size_t)128 * frames * 4, &mel))) return rc;
+  if ((rc = cuda_status(cudaMemcpyAsync(audio, samples, (size_t)n_samples * 4, cudaMemcpyDefault, st),
+                        "encode: samples")))
+    return rc;
+  if ((rc = qasr_mel_spectrogram(static_cast<float *>(mel), static_cast<const float *>(audio), n_samples, st)))
+    return rc;
+  if ((rc = cuda_status(cudaStreamSynchronize(st), "encode: mel"))) return rc;
+  rc = qasr_encoder_forward(enc, static_cast<const float *>(mel), frames, rows, rows_cap, T);
+  cudaSetDevice(device);
+  return rc;
+}
+
+// Greedy decode of M sequences (KV slots 0..M-1) from token tok0[i] at
+// position pos0[i]: the ids stay on the device, step s reading step s-1's
+// argmax, so steps are enqueued back to back; the host reads the ids every
+// check_every steps when stopping at end-of-text (the stop token is kept).
+int greedy_decode(qasr_decoder *dec, int M, const int32_t *tok0, const int32_t *pos0, int max_new, int stop_at_eos,
+                  int check_every, int32_t *ids, int ids_stride, int *n_ids) {
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(qasr_decoder_stream(dec));
+  void *steps = nullptr;
+  int rc = dev_scratch(kScratchDecode, (size_t)(M + 2 * (size_t)max_new * M) * 4, &steps);
+  if (rc) return rc;
+  int32_t *d_tok0 = static_cast<int32_t *>(steps), *d_pos = d_tok0 + M, *d_ids = d_pos + (size_t)max_new * M;
+  std::vector<int32_t> pos((size_t)max_new * M);
+  for (int s = 0; s < max_new; ++s)
+    for (int i = 0; i < M; ++i) pos[(size_t)s * M + i] = pos0[i] + s;
+  if ((rc = cuda_status(cudaMemcpyAsync(d_tok0, tok0, (size_t)M * 4, cudaMemcpyHostToDevice, st), "decode: tokens")))
+    return rc;
+  if ((rc = cuda_status(cudaMemcpyAsync(d_pos, pos.data(), pos.size() * 4, cudaMemcpyHostToDevice, st),
+                        "decode: positions")))
+    return rc;
+  std::vector<int32_t> out((size_t)max_new * M);
+  std::vector<int> count(M, 0);
+  std::vector<char> done(M, 0);
+  int steps_run = 0;
+  while (steps_run < max_new) {
+    const int upto = std::min(max_new, steps_run + (stop_at_eos ? check_every : max_new));
+    for (int s = steps_run; s < upto; ++s) {
+      const int32_t *tok = s == 0 ? d_tok0 : d_ids + (size_t)(s - 1) * M;
+      if ((rc = qasr_decoder_step_device(dec, tok, d_pos + (size_t)s * M, M, d_ids + (size_t)s * M))) return rc;
+    }
+    if ((rc = cuda_status(cudaMemcpyAsync(out.data() + (size_t)steps_run * M, d_ids + (size_t)steps_run * M,
+                                          (size_t)(upto - steps_run) * M * 4, cudaMemcpyDeviceToHost, st),
+                          "decode: ids")))
+      return rc;
+    if ((rc = cuda_status(cudaStreamSynchronize(st), "decode"))) return rc;
+    for (int s = steps_run; s < upto; ++s)
+      for (int i = 0; i < M; ++i) {
+        if (done[i]) continue;
+        const int32_t t = out[(size_t)s * M + i];
+        ids[(size_t)i * ids_stride + count[i]++] = t;
+        if (stop_at_eos && is_stop_token(t)) done[i] = 1;
+      }
+    steps_run = upto;
+    if (std::all_of(done.begin(), done.end(), [](char c) { return c != 0; })) break;
+  }
+  std::memcpy(n_ids, count.data(), (size_t)M * sizeof(int));
+  return QASR_OK;
+}
+
 }  // namespace qasr
 
 using namespace qasr;
@@ -86,32 +157,18 @@ extern "C" int qasr_transcribe_batch(qasr_decoder *dec, qasr_encoder *enc, const
   const int max_prompt = qasr_transcribe_prompt_len(max_tokens, n_prompt, n_force);
   const int max_frames = qasr_mel_frames(max_samples);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(qasr_decoder_stream(dec));
-  void *audio = nullptr, *mel = nullptr, *enc_out = nullptr, *prompt = nullptr, *steps = nullptr;
+  void *enc_out = nullptr, *prompt = nullptr;
   int rc;
-  if ((rc = dev_scratch(kScratchAudio, (size_t)max_samples * 4, &audio))) return rc;
-  if ((rc = dev_scratch(kScratchMelOut, (size_t)128 * max_frames * 4, &mel))) return rc;
+  (void)max_frames;
   if ((rc = dev_scratch(kScratchEncOut, (size_t)max_tokens * H * 4, &enc_out))) return rc;
   if ((rc = dev_scratch(kScratchPrompt, (size_t)max_prompt * H * 4, &prompt))) return rc;
-  // decode rows: tokens of step 0, then positions and ids of every step
-  if ((rc = dev_scratch(kScratchDecode, (size_t)(M + 2 * (size_t)max_new * M) * 4, &steps))) return rc;
-  int32_t *d_tok0 = static_cast<int32_t *>(steps), *d_pos = d_tok0 + M, *d_ids = d_pos + (size_t)max_new * M;
-
-  std::vector<int32_t> tok0(M), pos((size_t)max_new * M), pre;
+  std::vector<int32_t> tok0(M), pos0(M), pre;
   float *embeds = static_cast<float *>(prompt);
   for (int i = 0; i < M; ++i) {
     // mel + encoder (transcribe.rs:78-96)
-    const int frames = qasr_mel_frames(n_samples[i]);
-    if ((rc = cuda_status(cudaMemcpyAsync(audio, samples[i], (size_t)n_samples[i] * 4, cudaMemcpyDefault, st),
-                          "qasr_transcribe_batch: samples")))
-      return rc;
-    if ((rc = qasr_mel_spectrogram(static_cast<float *>(mel), static_cast<const float *>(audio), n_samples[i], st)))
-      return rc;
-    if ((rc = cuda_status(cudaStreamSynchronize(st), "qasr_transcribe_batch: mel"))) return rc;
     int T = 0;
-    if ((rc = qasr_encoder_forward(enc, static_cast<const float *>(mel), frames, static_cast<float *>(enc_out),
-                                   max_tokens, &T)))
+    if ((rc = encode_samples(enc, dev, st, samples[i], n_samples[i], static_cast<float *>(enc_out), max_tokens, &T)))
       return rc;
-    cudaSetDevice(dev);
     // prompt embeddings (transcribe.rs:98-170): token rows around the audio rows
     pre.assign(kPrefixHead, kPrefixHead + kHead);
     pre.insert(pre.end(), prompt_tokens, prompt_tokens + n_prompt);
@@ -131,40 +188,9 @@ extern "C" int qasr_transcribe_batch(qasr_decoder *dec, qasr_encoder *enc, const
     // prompt token at position total - 1 (transcribe.rs:172-190)
     if ((rc = qasr_decoder_prefill(dec, i, embeds, total - 1, 0))) return rc;
     tok0[i] = post.back();
-    for (int s = 0; s < max_new; ++s) pos[(size_t)s * M + i] = total - 1 + s;
+    pos0[i] = total - 1;
   }
-  if ((rc = cuda_status(cudaMemcpyAsync(d_tok0, tok0.data(), (size_t)M * 4, cudaMemcpyHostToDevice, st),
-                        "qasr_transcribe_batch: tokens")))
-    return rc;
-  if ((rc = cuda_status(cudaMemcpyAsync(d_pos, pos.data(), pos.size() * 4, cudaMemcpyHostToDevice, st),
-                        "qasr_transcribe_batch: positions")))
-    return rc;
   // greedy decode (transcribe.rs:192-222)
-  std::vector<int32_t> out((size_t)max_new * M);
-  std::vector<int> count(M, 0);
-  std::vector<char> done(M, 0);
-  int steps_run = 0;
-  while (steps_run < max_new) {
-    const int upto = std::min(max_new, steps_run + (stop_at_eos ? kCheckEvery : max_new));
-    for (int s = steps_run; s < upto; ++s) {
-      const int32_t *tok = s == 0 ? d_tok0 : d_ids + (size_t)(s - 1) * M;
-      if ((rc = qasr_decoder_step_device(dec, tok, d_pos + (size_t)s * M, M, d_ids + (size_t)s * M))) return rc;
-    }
-    if ((rc = cuda_status(cudaMemcpyAsync(out.data() + (size_t)steps_run * M, d_ids + (size_t)steps_run * M,
-                                          (size_t)(upto - steps_run) * M * 4, cudaMemcpyDeviceToHost, st),
-                          "qasr_transcribe_batch: ids")))
-      return rc;
-    if ((rc = cuda_status(cudaStreamSynchronize(st), "qasr_transcribe_batch: decode"))) return rc;
-    for (int s = steps_run; s < upto; ++s)
-      for (int i = 0; i < M; ++i) {
-        if (done[i]) continue;
-        const int32_t t = out[(size_t)s * M + i];
-        ids[(size_t)i * ids_stride + count[i]++] = t;
-        if (stop_at_eos && is_stop(t)) done[i] = 1;
-      }
-    steps_run = upto;
-    if (std::all_of(done.begin(), done.end(), [](char c) { return c != 0; })) break;
-  }
-  std::memcpy(n_ids, count.data(), (size_t)M * sizeof(int));
-  return QASR_OK;
+  return greedy_decode(dec, M, tok0.data(), pos0.data(), max_new, stop_at_eos, kCheckEvery, ids, ids_stride, n_ids);
 }
+
