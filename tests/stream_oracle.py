@@ -67,12 +67,14 @@ class OracleStream:
         self.snapshot, self.stale = [], 0
         self.last_partial_cursor, self.last_partial = 0, None
         self.cursor, self.chunk_idx, self.trim_request = 0, 0, 0
+        self.max_prefix, self.resets, self.max_reused = 0, 0, 0  # coverage counters for the tests
         self.k, self.v = od.new_kv(max_seq)
 
     def _bytes(self, t):
         return int(self.tok_bytes[t]) if self.tok_bytes is not None and 0 <= t < len(self.tok_bytes) else 1
 
     def _reset_tokens(self, keep_windows):
+        self.resets += 1
         carry = min(len(self.stable), CARRY)
         carried = self.stable[len(self.stable) - carry:]
         self.raw = ([ASR_TEXT] + carried) if carry else []
@@ -127,6 +129,7 @@ class OracleStream:
                 continue
             n_prefix = (max(len(self.raw) - self.rollback, 0)
                         if self.past and self.chunk_idx >= self.unfixed and self.raw else 0)
+            self.max_prefix = max(self.max_prefix, n_prefix)
             pre = list(PREFIX_HEAD) + self.prompt + list(PREFIX_TAIL)
             post = list(SUFFIX_BASE) + self.force + self.raw[:n_prefix]
             parts = [self.embed(pre)] + self.enc_cache + ([partial] if n_partial else []) + [self.embed(post)]
@@ -137,6 +140,7 @@ class OracleStream:
                 cmp = min(prefill_len, self.prev_len)
                 while reused < cmp and np.array_equal(self.prev_rows[reused], rows[reused]):
                     reused += 1
+            self.max_reused = max(self.max_reused, reused)
             if prefill_len > reused:
                 self.od.prefill(self.k, self.v, reused, rows[reused:prefill_len])
             tok = post[-1]
