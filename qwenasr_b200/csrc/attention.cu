@@ -3,14 +3,19 @@
 //
 // Two kernels:
 //  * causal_attention_kernel: the general kernel-level entry (any seq_q,
-//    e.g. prefill).  One warp per (query, head), lanes over head dims, the
-//    reference's per-key online softmax update (mod.rs:1154-1164).
+//    e.g. prefill, kernels::causal_attention mod.rs:1124-1207).  K/V tiles of
+//    32 keys staged in shared memory serve the block's queries and every
+//    query head of their GQA group; scores one key per lane, merged tile by
+//    tile (flash-style) instead of the reference's per-key update -- the same
+//    softmax up to f32 rounding.
 //  * attn_decode_kernel: the decode step of the engine.  Flash-decoding over
 //    the f32 KV cache: the keys of one (sequence, kv head) are split across
 //    CTAs, each CTA serves both query heads of the GQA group so every K/V row
 //    is read from HBM exactly once, and the last CTA of a (sequence, kv head)
 //    merges the partial softmax states (counter + threadfence, no spin).
 #include <cudaTypedefs.h>
+
+#include <algorithm>
 
 #include "attention.cuh"
 #include "common.cuh"
@@ -19,49 +24,94 @@
 namespace qasr {
 
 // ------------------------------------------------------------------ general
+constexpr int kCaTile = 32;   // keys per shared-memory tile (one per lane for the scores)
+constexpr int kCaTasks = 16;  // (query, head) tasks per block: two per warp
+
+// Block (query block qb, kv head kvh): queries qb*QB .. +QB, every query head of
+// the GQA group (task = query * G + head-in-group).  K/V tiles of kCaTile keys
+// are staged in shared memory (K rows padded to HD+1 floats: the lane-per-key
+// score loop is conflict-free) and shared by all tasks; each task keeps a
+// running (max, sum, o) merged tile by tile (flash-style), its causal limit
+// masking the keys after q_offset + query.
 template <int EPL>  // elements per lane: head_dim / 32
 __global__ void __launch_bounds__(256)
 causal_attention_kernel(float *__restrict__ out, const float *__restrict__ q, const float *__restrict__ k,
                         const float *__restrict__ v, int seq_q, int seq_k, int n_heads, int n_kv_heads, float scale,
                         int q_offset) {
+  constexpr int HD = EPL * 32;
+  __shared__ float sK[kCaTile][HD + 1];
+  __shared__ float sV[kCaTile][HD];
+  __shared__ float sQ[kCaTasks][HD];
+  __shared__ float sP[8][kCaTile];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const long task = (long)blockIdx.x * 8 + warp;
-  if (task >= (long)seq_q * n_heads) return;
-  const int i = (int)(task / n_heads), h = (int)(task % n_heads);
-  const int hd = EPL * 32;
-  const int kv_h = h / (n_heads / n_kv_heads);
-  const long q_hidden = (long)n_heads * hd, kv_hidden = (long)n_kv_heads * hd;
-  float qv[EPL], o[EPL];
-#pragma unroll
-  for (int e = 0; e < EPL; ++e) {
-    qv[e] = q[i * q_hidden + (long)h * hd + lane * EPL + e];
-    o[e] = 0.0f;
+  const int G = n_heads / n_kv_heads, QB = max(1, kCaTasks / G), n_tasks = QB * G;
+  const int kvh = blockIdx.y, i0 = blockIdx.x * QB;
+  const long q_hidden = (long)n_heads * HD, kv_hidden = (long)n_kv_heads * HD;
+  const int i_last = min(seq_q, i0 + QB) - 1;
+  const int k_end = min(q_offset + i_last + 1, seq_k);  // keys any task of the block needs
+  // q rows of the block's tasks
+  for (int idx = threadIdx.x; idx < n_tasks * HD; idx += blockDim.x) {
+    const int t = idx / HD, d = idx % HD, i = i0 + t / G, h = kvh * G + t % G;
+    sQ[t][d] = i < seq_q ? q[(long)i * q_hidden + (long)h * HD + d] : 0.0f;
   }
-  const int k_end = min(q_offset + i + 1, seq_k);
-  float max_score = -1e30f, sum_exp = 0.0f;
-  for (int j = 0; j < k_end; ++j) {
-    const float *kr = k + j * kv_hidden + (long)kv_h * hd + lane * EPL;
-    const float *vr = v + j * kv_hidden + (long)kv_h * hd + lane * EPL;
-    float d = 0.0f;
+  float m[2], l[2], o[2][EPL];
 #pragma unroll
-    for (int e = 0; e < EPL; ++e) d = fmaf(qv[e], kr[e], d);
-    const float score = __fmul_rn(warp_sum(d), scale);
-    if (score > max_score) {
-      const float corr = expf(__fsub_rn(max_score, score));
-      sum_exp = __fadd_rn(__fmul_rn(sum_exp, corr), 1.0f);
+  for (int u = 0; u < 2; ++u) {
+    m[u] = -INFINITY;
+    l[u] = 0.0f;
 #pragma unroll
-      for (int e = 0; e < EPL; ++e) o[e] = fmaf(o[e], corr, vr[e]);
-      max_score = score;
-    } else {
-      const float wt = expf(__fsub_rn(score, max_score));
-      sum_exp = __fadd_rn(sum_exp, wt);
+    for (int e = 0; e < EPL; ++e) o[u][e] = 0.0f;
+  }
+  for (int t0 = 0; t0 < k_end; t0 += kCaTile) {
+    const int nk = min(kCaTile, k_end - t0);
+    __syncthreads();  // the previous tile is consumed (and sQ written, first time)
+    stage_kv_rows<HD, 1>(&sK[0][0], &sV[0][0], k, v, t0, kv_hidden, (long)kvh * HD, nk);
+    __syncthreads();
 #pragma unroll
-      for (int e = 0; e < EPL; ++e) o[e] = fmaf(vr[e], wt, o[e]);
+    for (int u = 0; u < 2; ++u) {
+      const int t = warp + 8 * u;
+      if (t >= n_tasks) continue;  // warp-uniform
+      const int i = i0 + t / G;
+      if (i >= seq_q) continue;
+      const int lim = min(q_offset + i + 1, seq_k);  // keys < lim are visible
+      // scores: lane j takes key t0 + j
+      float sc = -INFINITY;
+      if (lane < nk && t0 + lane < lim) {
+        float d = 0.0f;
+#pragma unroll 16
+        for (int e = 0; e < HD; ++e) d = fmaf(sQ[t][e], sK[lane][e], d);
+        sc = __fmul_rn(d, scale);
+      }
+      const float mt = warp_max(sc);
+      const float mn = fmaxf(m[u], mt);
+      if (mn == -INFINITY) continue;  // no visible key yet (only before the first tile)
+      const float corr = m[u] == -INFINITY ? 0.0f : expf(__fsub_rn(m[u], mn));
+      const float pj = sc == -INFINITY ? 0.0f : expf(__fsub_rn(sc, mn));
+      l[u] = __fadd_rn(__fmul_rn(l[u], corr), warp_sum(pj));
+      m[u] = mn;
+      sP[warp][lane] = pj;
+      __syncwarp();
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) o[u][e] = __fmul_rn(o[u][e], corr);
+      for (int j = 0; j < nk; ++j) {
+        const float w = sP[warp][j];
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) o[u][e] = fmaf(w, sV[j][lane * EPL + e], o[u][e]);
+      }
+      __syncwarp();  // sP is rewritten by the next task
     }
   }
-  const float inv = sum_exp > 0.0f ? __fdiv_rn(1.0f, sum_exp) : 0.0f;
 #pragma unroll
-  for (int e = 0; e < EPL; ++e) out[i * q_hidden + (long)h * hd + lane * EPL + e] = sum_exp > 0.0f ? __fmul_rn(o[e], inv) : o[e];
+  for (int u = 0; u < 2; ++u) {
+    const int t = warp + 8 * u;
+    if (t >= n_tasks) continue;
+    const int i = i0 + t / G, h = kvh * G + t % G;
+    if (i >= seq_q) continue;
+    const float inv = l[u] > 0.0f ? __fdiv_rn(1.0f, l[u]) : 0.0f;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e)
+      out[(long)i * q_hidden + (long)h * HD + lane * EPL + e] = l[u] > 0.0f ? __fmul_rn(o[u][e], inv) : o[u][e];
+  }
 }
 
 // ------------------------------------------------------------------- decode
@@ -129,10 +179,11 @@ attn_decode_kernel(const __grid_constant__ AttnDecodeParams p) {
   }
   __syncthreads();
   const long long Tk = sm.off[n_pairs];
-  // Virtual grid: with fewer keys than CTAs, only the first Tk CTAs take part,
-  // so every participating CTA owns at least one key and the CTAs covering a
-  // pair are exactly c_of(first key) .. c_of(last key).
-  const long long Gd = min((long long)gridDim.x, Tk), c = blockIdx.x;
+  // Virtual grid: only the first Gd CTAs take part, each owning at least
+  // kAttnMinKeys keys (one when Tk is smaller), so the CTAs covering a pair
+  // are exactly c_of(first key) .. c_of(last key) and short histories are
+  // split into few partials.
+  const long long Gd = max(1ll, min((long long)gridDim.x, Tk / kAttnMinKeys)), c = blockIdx.x;
   if (c >= Gd) return;
   const long long t0 = c * Tk / Gd, t1 = (c + 1) * Tk / Gd;
 
@@ -358,21 +409,36 @@ attn_decode_kernel(const __grid_constant__ AttnDecodeParams p) {
         const int s = g0 + task / G, g = task % G;
         const int prs = sm.seg_pair[s], ms = prs / n_kv, kvs = prs % n_kv;
         const long long cf = c_first(s), cl = c_last(s);
+        auto part = [&](long long c2) { return p.partials + ((size_t)(c2 + prs) * G + g) * kAttnPartStride; };
+        // max and sum: one partial per lane, then a warp reduction
         float Mx = -INFINITY;
-        for (long long c2 = cf; c2 <= cl; ++c2)
-          Mx = fmaxf(Mx, __ldcg(p.partials + ((size_t)(c2 + prs) * G + g) * kAttnPartStride + 128));
+        for (long long c2 = cf + lane; c2 <= cl; c2 += 32) Mx = fmaxf(Mx, __ldcg(part(c2) + 128));
+        Mx = warp_max(Mx);
         float L = 0.0f;
+        for (long long c2 = cf + lane; c2 <= cl; c2 += 32) {
+          const float ms2 = __ldcg(part(c2) + 128);
+          L = __fadd_rn(L, __fmul_rn(__ldcg(part(c2) + 129), ms2 == -INFINITY ? 0.0f : expf(__fsub_rn(ms2, Mx))));
+        }
+        L = warp_sum(L);
+        // the vectors: independent loads, four partials per round
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (long long c2 = cf; c2 <= cl; ++c2) {
-          const float *ps2 = p.partials + ((size_t)(c2 + prs) * G + g) * kAttnPartStride;
-          const float ms2 = __ldcg(ps2 + 128);
-          const float f = ms2 == -INFINITY ? 0.0f : expf(__fsub_rn(ms2, Mx));
-          L = __fadd_rn(L, __fmul_rn(__ldcg(ps2 + 129), f));
-          const float4 ov = __ldcg(reinterpret_cast<const float4 *>(ps2) + lane);
-          acc.x = fmaf(ov.x, f, acc.x);
-          acc.y = fmaf(ov.y, f, acc.y);
-          acc.z = fmaf(ov.z, f, acc.z);
-          acc.w = fmaf(ov.w, f, acc.w);
+        for (long long c0 = cf; c0 <= cl; c0 += 4) {
+          float4 ov[4];
+          float f[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const long long c2 = min(c0 + u, cl);
+            ov[u] = __ldcg(reinterpret_cast<const float4 *>(part(c2)) + lane);
+            const float ms2 = __ldcg(part(c2) + 128);
+            f[u] = (c0 + u > cl || ms2 == -INFINITY) ? 0.0f : expf(__fsub_rn(ms2, Mx));
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            acc.x = fmaf(ov[u].x, f[u], acc.x);
+            acc.y = fmaf(ov[u].y, f[u], acc.y);
+            acc.z = fmaf(ov[u].z, f[u], acc.z);
+            acc.w = fmaf(ov[u].w, f[u], acc.w);
+          }
         }
         const float inv = __fdiv_rn(1.0f, L);
         *reinterpret_cast<float4 *>(p.out + (size_t)ms * p.out_stride + (kvs * G + g) * 128 + 4 * lane) =
@@ -488,13 +554,19 @@ extern "C" int qasr_causal_attention(float *out, const float *q, const float *k,
     return QASR_ERR_UNSUPPORTED;
   }
   if (seq_q == 0) return QASR_OK;
-  const long tasks = (long)seq_q * n_heads;
+  const int G = n_heads / n_kv_heads;
+  if (G > kCaTasks) {
+    set_error("qasr_causal_attention: %d query heads per kv head unsupported (at most %d)", G, kCaTasks);
+    return QASR_ERR_UNSUPPORTED;
+  }
+  const int QB = std::max(1, kCaTasks / G);
+  const dim3 grid((unsigned)((seq_q + QB - 1) / QB), (unsigned)n_kv_heads);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (head_dim == 128)
-    causal_attention_kernel<4><<<ceil_div(tasks, 8), 256, 0, st>>>(out, q, k, v, seq_q, seq_k, n_heads, n_kv_heads,
-                                                                   scale, q_offset);
+    causal_attention_kernel<4><<<grid, 256, 0, st>>>(out, q, k, v, seq_q, seq_k, n_heads, n_kv_heads, scale,
+                                                     q_offset);
   else
-    causal_attention_kernel<2><<<ceil_div(tasks, 8), 256, 0, st>>>(out, q, k, v, seq_q, seq_k, n_heads, n_kv_heads,
-                                                                   scale, q_offset);
+    causal_attention_kernel<2><<<grid, 256, 0, st>>>(out, q, k, v, seq_q, seq_k, n_heads, n_kv_heads, scale,
+                                                     q_offset);
   return launch_status("qasr_causal_attention");
 }

@@ -10,6 +10,7 @@ constexpr int kAttnWarps = 8;
 constexpr int kAttnTile = 8;          // keys per TMA tile (one warp's pipeline stage)
 constexpr int kAttnStages = 2;        // K+V tiles in flight per warp
 constexpr int kAttnPartStride = 132;  // floats per (segment, head) partial: o[128], max, sum, pad
+constexpr int kAttnMinKeys = 128;     // keys per CTA at least: short histories use fewer CTAs (fewer partials)
 
 struct AttnDecodeParams {
   CUtensorMap tm_k;      // 2D tensor maps over the whole cache: [rows = B*L*max_seq, kv_dim] f32,

@@ -64,6 +64,15 @@ QASR_DEV float fast_exp_ref(float x) {
   return __fmul_rn(exp_i, p);
 }
 
+// tanh GELU of avx::gelu_inplace (avx.rs:536-555), one lane.
+QASR_DEV float gelu_tanh_ref(float v) {
+  const float v2 = __fmul_rn(v, v), v3 = __fmul_rn(v2, v);
+  const float inner = __fmul_rn(0.7978845608028654f, fmaf(0.044715f, v3, v));
+  const float e = fast_exp_ref(__fmul_rn(2.0f, inner));
+  const float t = __fsub_rn(1.0f, __fdiv_rn(2.0f, __fadd_rn(e, 1.0f)));
+  return __fmul_rn(0.5f, __fmul_rn(v, __fadd_rn(1.0f, t)));
+}
+
 // Four int8 values packed in a 32-bit word -> four exact floats.  Each byte
 // (sign-flipped to excess-128) is placed in the mantissa of 2^23 with one
 // byte permute; subtracting 2^23+128 recovers the signed value exactly.
@@ -148,5 +157,36 @@ QASR_DEV int reduce_index(int lane) {
 }
 
 inline int ceil_div(long a, long b) { return (int)((a + b - 1) / b); }
+
+// Copies rows row0 .. row0+n-1, columns col0 .. col0+HD-1 of two row-major
+// matrices (row stride `stride`) into shared memory (K rows padded by PADK
+// floats, V rows dense).  Each thread issues eight independent loads before
+// its stores, so a block has 8 x blockDim loads in flight instead of one.
+template <int HD, int PADK>
+QASR_DEV void stage_kv_rows(float *sK, float *sV, const float *__restrict__ k, const float *__restrict__ v, long row0,
+                            long stride, long col0, int n) {
+  const int total = n * HD;
+  for (int base = threadIdx.x; base < total; base += blockDim.x * 8) {
+    float kr[8], vr[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int idx = base + u * (int)blockDim.x;
+      if (idx < total) {
+        const long g = (row0 + idx / HD) * stride + col0 + idx % HD;
+        kr[u] = k[g];
+        vr[u] = v[g];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int idx = base + u * (int)blockDim.x;
+      if (idx < total) {
+        const int j = idx / HD, d = idx % HD;
+        sK[j * (HD + PADK) + d] = kr[u];
+        sV[j * HD + d] = vr[u];
+      }
+    }
+  }
+}
 
 }  // namespace qasr

@@ -648,14 +648,22 @@ extern "C" int qasr_decoder_prefill(qasr_decoder *d, int slot, const float *embe
     const LayerDev &L = d->layers[l];
     const size_t kv_rows = (size_t)kv_dim * H;
     if ((rc = qasr_rms_norm(d->pf_xn, d->pf_x, L.in_norm, seq, H, c.eps, st))) break;
-    // q, k, v: the three row ranges of the fused q|k|v matrix
-    if ((rc = qasr_linear_nobias_int8(d->pf_q, d->pf_xn, L.wqkv, L.sqkv, seq, H, q_dim, st))) break;
-    if ((rc = qasr_linear_nobias_int8(d->pf_k, d->pf_xn, L.wqkv + (size_t)q_dim * H, L.sqkv + q_dim, seq, H, kv_dim,
-                                      st)))
+    // q, k, v: the three row ranges of the fused q|k|v matrix, one GEMM when
+    // the tensor-core path takes it (seq > 8), else three matvec calls
+    rc = seq > 8 ? int8_gemm_split3(d->pf_q, q_dim, d->pf_k, kv_dim, q_dim, d->pf_v, kv_dim, q_dim + kv_dim, d->pf_xn,
+                                    H, L.wqkv, L.sqkv, seq, H, q_dim + 2 * kv_dim, st)
+                 : QASR_ERR_UNSUPPORTED;
+    if (rc == QASR_ERR_UNSUPPORTED) {
+      if ((rc = qasr_linear_nobias_int8(d->pf_q, d->pf_xn, L.wqkv, L.sqkv, seq, H, q_dim, st))) break;
+      if ((rc = qasr_linear_nobias_int8(d->pf_k, d->pf_xn, L.wqkv + (size_t)q_dim * H, L.sqkv + q_dim, seq, H,
+                                        kv_dim, st)))
+        break;
+      if ((rc = qasr_linear_nobias_int8(d->pf_v, d->pf_xn, L.wqkv + (size_t)q_dim * H + kv_rows,
+                                        L.sqkv + q_dim + kv_dim, seq, H, kv_dim, st)))
+        break;
+    } else if (rc) {
       break;
-    if ((rc = qasr_linear_nobias_int8(d->pf_v, d->pf_xn, L.wqkv + (size_t)q_dim * H + kv_rows, L.sqkv + q_dim + kv_dim,
-                                      seq, H, kv_dim, st)))
-      break;
+    }
     if ((rc = qasr_rms_norm_per_head(d->pf_q, L.q_norm, seq, c.n_heads, hd, c.eps, st))) break;
     if ((rc = qasr_rms_norm_per_head(d->pf_k, L.k_norm, seq, c.n_kv_heads, hd, c.eps, st))) break;
     if ((rc = qasr_apply_rope_neox(d->pf_q, cos_r, sin_r, seq, c.n_heads, hd, st))) break;

@@ -20,14 +20,6 @@ static int stream_grid(long n_vec, int threads) {
   return (int)(want < cap ? (want > 0 ? want : 1) : cap);
 }
 
-// tanh GELU of avx::gelu_inplace (avx.rs:536-555), one lane.
-QASR_DEV float gelu_tanh_ref(float v) {
-  const float v2 = __fmul_rn(v, v), v3 = __fmul_rn(v2, v);
-  const float inner = __fmul_rn(0.7978845608028654f, fmaf(0.044715f, v3, v));
-  const float e = fast_exp_ref(__fmul_rn(2.0f, inner));
-  const float t = __fsub_rn(1.0f, __fdiv_rn(2.0f, __fadd_rn(e, 1.0f)));
-  return __fmul_rn(0.5f, __fmul_rn(v, __fadd_rn(1.0f, t)));
-}
 // Scalar tail of the same function (avx.rs:557-562), libm tanh.
 QASR_DEV float gelu_tanh_tail(float val) {
   const float x3 = __fmul_rn(__fmul_rn(val, val), val);

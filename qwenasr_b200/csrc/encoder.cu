@@ -115,12 +115,7 @@ bidir_attention_staged_kernel(float *__restrict__ out, const float *__restrict__
   const int n = we - ws;
   if (n <= 0 || n > kt) return;  // block-uniform; the host sizes kt to the longest window
   const long hidden = (long)n_heads * HD;
-  for (int idx = threadIdx.x; idx < n * HD; idx += blockDim.x) {
-    const int j = idx / HD, d = idx - j * HD;
-    const long g = (long)(ws + j) * hidden + (long)h * HD + d;
-    sK[j * (HD + 1) + d] = k[g];
-    sV[j * HD + d] = v[g];
-  }
+  stage_kv_rows<HD, 1>(sK, sV, k, v, ws, hidden, (long)h * HD, n);
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float *qs = sQ + warp * HD, *ps = sP + (size_t)warp * kt;

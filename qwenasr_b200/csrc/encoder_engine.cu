@@ -39,35 +39,62 @@ inline int grid_of(long n) { return (int)std::max(1l, std::min((n + 255) / 256, 
 // kernel, stride 2, padding 1, every chunk padded on its own as in the
 // reference's per-chunk kernels::conv2d) times the [c_out, c_in*9] weights.
 
-// conv1's patches straight from the mel [128, mel_frames]: chunk b covers
-// frames first + b*cs .. + cw (one input channel).
-__global__ void __launch_bounds__(256) im2col_mel_kernel(float *__restrict__ colsT, const float *__restrict__ mel,
+// conv1 (one input channel) + bias + tanh GELU straight from the mel
+// [128, mel_frames]: chunk b covers frames first + b*cs .. + cw; out[r, o]
+// channel-last.  The GELU is the gelu_kernel body (the 480-channel rows keep
+// every element in the 8-lane body of avx::gelu_inplace).
+__global__ void __launch_bounds__(256) conv1_gelu_kernel(float *__restrict__ out, const float *__restrict__ mel,
                                                          int mel_frames, int first, int cs, int cw, int B, int h_out,
-                                                         int w_out) {
-  const long total = (long)B * h_out * w_out * 9;
+                                                         int w_out, const float *__restrict__ w,
+                                                         const float *__restrict__ bias, int C) {
+  const long total = (long)B * h_out * w_out * C;
   for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
-    const long r = i / 9;
-    const int p = (int)(i - r * 9), ki = p / 3, kj = p % 3;
+    const long r = i / C;
+    const int o = (int)(i - r * C);
     const int ow = (int)(r % w_out), oh = (int)((r / w_out) % h_out), b = (int)(r / ((long)w_out * h_out));
-    const int ih = oh * 2 + ki - 1, iw = ow * 2 + kj - 1;
-    colsT[i] = (ih >= 0 && ih < kMelBins && iw >= 0 && iw < cw)
-                   ? mel[(long)ih * mel_frames + first + (long)b * cs + iw]
-                   : 0.0f;
+    float acc = 0.0f;
+#pragma unroll
+    for (int kk = 0; kk < 9; ++kk) {
+      const int ih = oh * 2 + kk / 3 - 1, iw = ow * 2 + kk % 3 - 1;
+      const float x = (ih >= 0 && ih < kMelBins && iw >= 0 && iw < cw)
+                          ? __ldg(mel + (long)ih * mel_frames + first + (long)b * cs + iw)
+                          : 0.0f;
+      acc = fmaf(__ldg(w + o * 9 + kk), x, acc);
+    }
+    out[i] = gelu_tanh_ref(__fadd_rn(acc, __ldg(bias + o)));
   }
 }
 
-// patches of a channel-last activation [B, h_in, w_in, C]
+// Patches of a channel-last activation [B, h_in, w_in, C] in channel-fastest
+// order: colsT[r, (ki*3 + kj)*C + ic] (the conv weights are permuted to match
+// once, conv_weight_cl_kernel), so every (position, ki, kj) copies C
+// contiguous floats: float4 loads and stores.
 __global__ void __launch_bounds__(256) im2col_cl_kernel(float *__restrict__ colsT, const float *__restrict__ act,
                                                         int C, int h_in, int w_in, int B, int h_out, int w_out) {
-  const long patch = (long)C * 9;
-  const long total = (long)B * h_out * w_out * patch;
+  const int C4 = C / 4;
+  const long per_row = 9l * C4;
+  const long total = (long)B * h_out * w_out * per_row;
+  float4 *dst = reinterpret_cast<float4 *>(colsT);
+  const float4 *src = reinterpret_cast<const float4 *>(act);
   for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
-    const long r = i / patch;
-    const int p = (int)(i - r * patch), ic = p / 9, kk = p % 9, ki = kk / 3, kj = kk % 3;
+    const long r = i / per_row;
+    const int rem = (int)(i - r * per_row), kk = rem / C4, c4 = rem % C4;
     const int ow = (int)(r % w_out), oh = (int)((r / w_out) % h_out), b = (int)(r / ((long)w_out * h_out));
-    const int ih = oh * 2 + ki - 1, iw = ow * 2 + kj - 1;
-    colsT[i] = (ih >= 0 && ih < h_in && iw >= 0 && iw < w_in) ? act[(((long)b * h_in + ih) * w_in + iw) * C + ic]
-                                                               : 0.0f;
+    const int ih = oh * 2 + kk / 3 - 1, iw = ow * 2 + kk % 3 - 1;
+    dst[i] = (ih >= 0 && ih < h_in && iw >= 0 && iw < w_in) ? src[(((long)b * h_in + ih) * w_in + iw) * C4 + c4]
+                                                             : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+}
+
+// dst[o, kk*C + ic] = src[o, ic*9 + kk]: the [c_out, c_in, 3, 3] weights in
+// the channel-fastest patch order of im2col_cl_kernel.
+__global__ void __launch_bounds__(256) conv_weight_cl_kernel(float *__restrict__ dst, const float *__restrict__ src,
+                                                             int c_out, int C) {
+  const long total = (long)c_out * C * 9;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const long o = i / (9l * C);
+    const int rem = (int)(i - o * 9l * C), kk = rem / C, ic = rem % C;
+    dst[i] = src[(o * C + ic) * 9 + kk];
   }
 }
 
@@ -233,9 +260,22 @@ static int conv_gemm(qasr_encoder *e, int i, float *y, const float *cols, int ro
   return f32_gemm_fallback(y, cols, e->conv_w[i], e->conv_b[i], rows, CH * 9, CH, st);
 }
 
-// digit planes of conv2 / conv3 after their weights change
+// conv2 / conv3 after their weights change: the weights into the
+// channel-fastest patch order, then their digit planes
 static int prepare_convs(qasr_encoder *e) {
-  int rc = cuda_status(cudaStreamSynchronize(e->stream), "qasr_encoder: conv weights");
+  const int CH = kConvHidden;
+  float *tmp = nullptr;
+  int rc = cuda_status(cudaMalloc(&tmp, (size_t)CH * CH * 9 * 4), "qasr_encoder: conv weights");
+  for (int i = 1; i < 3 && !rc; ++i) {
+    conv_weight_cl_kernel<<<grid_of((long)CH * CH * 9), 256, 0, e->stream>>>(tmp, e->conv_w[i], CH, CH);
+    rc = launch_status("qasr_encoder: conv weight order");
+    if (!rc)
+      rc = cuda_status(cudaMemcpyAsync(e->conv_w[i], tmp, (size_t)CH * CH * 9 * 4, cudaMemcpyDeviceToDevice,
+                                       e->stream),
+                       "qasr_encoder: conv weight order");
+  }
+  if (!rc) rc = cuda_status(cudaStreamSynchronize(e->stream), "qasr_encoder: conv weights");
+  if (tmp) cudaFree(tmp);
   for (int i = 1; i < 3 && !rc; ++i) {
     f32_weight_free(&e->conv_pw[i]);
     rc = f32_weight_prepare(&e->conv_pw[i], e->conv_w[i], kConvHidden, kConvHidden * 9, e->stream);
@@ -578,18 +618,17 @@ extern "C" int qasr_encoder_forward(qasr_encoder *e, const float *mel, int mel_f
     const int cw = full ? cs : tail;
     const int w1 = (cw + 2 - 3) / 2 + 1, w2 = (w1 + 2 - 3) / 2 + 1, w3 = (w2 + 2 - 3) / 2 + 1;
     const long r1 = (long)B * h1 * w1, r2 = (long)B * h2 * w2, r3 = (long)B * h3 * w3;
-    im2col_mel_kernel<<<grid_of(r1 * 9), 256, 0, st>>>(e->cols, mel, mel_frames, first, cs, cw, B, h1, w1);
-    rc = launch_status("qasr_encoder_forward: conv1 patches");
-    if (!rc) rc = f32_gemm_fallback(e->act_a, e->cols, e->conv_w[0], e->conv_b[0], (int)r1, 9, CH, st);
-    if (!rc) rc = qasr_gelu(e->act_a, (int64_t)r1 * CH, st);
+    conv1_gelu_kernel<<<grid_of(r1 * CH), 256, 0, st>>>(e->act_a, mel, mel_frames, first, cs, cw, B, h1, w1,
+                                                        e->conv_w[0], e->conv_b[0], CH);
+    rc = launch_status("qasr_encoder_forward: conv1");
     if (!rc) {
-      im2col_cl_kernel<<<grid_of(r2 * CH * 9), 256, 0, st>>>(e->cols, e->act_a, CH, h1, w1, B, h2, w2);
+      im2col_cl_kernel<<<grid_of(r2 * CH * 9 / 4), 256, 0, st>>>(e->cols, e->act_a, CH, h1, w1, B, h2, w2);
       rc = launch_status("qasr_encoder_forward: conv2 patches");
     }
     if (!rc) rc = conv_gemm(e, 1, e->act_b, e->cols, (int)r2, st);
     if (!rc) rc = qasr_gelu(e->act_b, (int64_t)r2 * CH, st);
     if (!rc) {
-      im2col_cl_kernel<<<grid_of(r3 * CH * 9), 256, 0, st>>>(e->cols, e->act_b, CH, h2, w2, B, h3, w3);
+      im2col_cl_kernel<<<grid_of(r3 * CH * 9 / 4), 256, 0, st>>>(e->cols, e->act_b, CH, h2, w2, B, h3, w3);
       rc = launch_status("qasr_encoder_forward: conv3 patches");
     }
     if (!rc) rc = conv_gemm(e, 2, e->act_a, e->cols, (int)r3, st);

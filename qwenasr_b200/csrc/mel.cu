@@ -135,10 +135,25 @@ __global__ void __launch_bounds__(256)
   extern __shared__ float4 mel_smem[];
   float *frames = reinterpret_cast<float *>(mel_smem);  // [32][kFramePitch]
   const int t0 = blockIdx.x * kFramesPerBlock;
-  for (int i = threadIdx.x; i < kFramesPerBlock * kFft; i += blockDim.x) {
-    const int f = i / kFft, j = i - f * kFft, t = t0 + f;
-    frames[f * kFramePitch + j] =
-        t < n_frames ? __fmul_rn(padded_sample(samples, n_samples, (long)t * kHop + j), window[j]) : 0.0f;
+  // eight independent loads per thread before the stores
+  for (int base = threadIdx.x; base < kFramesPerBlock * kFft; base += blockDim.x * 8) {
+    float val[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = base + u * (int)blockDim.x;
+      const int f = i / kFft, j = i - f * kFft, t = t0 + f;
+      val[u] = (i < kFramesPerBlock * kFft && t < n_frames)
+                   ? __fmul_rn(padded_sample(samples, n_samples, (long)t * kHop + j), window[j])
+                   : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = base + u * (int)blockDim.x;
+      if (i < kFramesPerBlock * kFft) {
+        const int f = i / kFft, j = i - f * kFft;
+        frames[f * kFramePitch + j] = val[u];
+      }
+    }
   }
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;

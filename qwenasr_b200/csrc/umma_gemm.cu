@@ -109,6 +109,11 @@ struct GemmParams {
   const float *scales, *bias;  // per weight row: INT8 scales, or the f32 weights' factors
   float *y;          // [T, N], row stride y_stride
   long y_stride;
+  // optional split of the output by weight row: rows >= n1 go to y1 (column
+  // row - n1, stride y1_stride), rows >= n2 to y2 (n1, n2 multiples of 128)
+  float *y1, *y2;
+  long y1_stride, y2_stride;
+  int n1, n2;
   int T, K, N;
   int *err;
 };
@@ -249,7 +254,12 @@ __global__ void __launch_bounds__(256, 1) gemm_kernel(const __grid_constant__ Ge
           if (t < p.T) {
             float v = __fmul_rn(__fmul_rn(__ll2float_rn(V[tl]), __ldg(p.dq + t)), sc);
             if (p.bias) v = __fadd_rn(v, b);
-            p.y[(size_t)t * p.y_stride + row] = v;
+            if (row >= p.n2)
+              p.y2[(size_t)t * p.y2_stride + (row - p.n2)] = v;
+            else if (row >= p.n1)
+              p.y1[(size_t)t * p.y1_stride + (row - p.n1)] = v;
+            else
+              p.y[(size_t)t * p.y_stride + row] = v;
           }
         }
       }
@@ -315,6 +325,7 @@ static int digit_rows(int8_t *D, float *dq, const float *x, long x_stride, int r
 
 template <int PLANES>
 static int gemm_launch(GemmParams &p, cudaStream_t st) {
+  if (!p.y1) p.n1 = p.n2 = 0x7fffffff;  // no split
   static int attr_mask = 0;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -356,6 +367,40 @@ int int8_gemm(float *y, long y_stride, const float *x, long x_stride, const int8
   p.bias = bias;
   p.y = y;
   p.y_stride = y_stride;
+  p.T = T;
+  p.K = K;
+  p.N = N;
+  if ((rc = digit_rows(static_cast<int8_t *>(dbuf), static_cast<float *>(qbuf), x, x_stride, T, T_pad, K, kGTok, st)))
+    return rc;
+  return gemm_launch<1>(p, st);
+}
+
+// int8_gemm over one weight matrix whose row ranges [0, n1), [n1, n2),
+// [n2, N) are written to three outputs (the fused q|k|v projection of the
+// prefill: the activation digits are made once).
+int int8_gemm_split3(float *y0, long s0, float *y1, long s1, int n1, float *y2, long s2, int n2, const float *x,
+                     long x_stride, const int8_t *w, const float *scales, int T, int K, int N, cudaStream_t st) {
+  if (!gemm_shape_ok(x, x_stride, T, K, N) || (reinterpret_cast<uintptr_t>(w) & 15) || n1 % 128 || n2 % 128 ||
+      !(0 < n1 && n1 <= n2 && n2 <= N))
+    return QASR_ERR_UNSUPPORTED;
+  const int NB = (T + kGTok - 1) / kGTok, T_pad = NB * kGTok;
+  void *dbuf = nullptr, *qbuf = nullptr;
+  int rc;
+  if ((rc = dev_scratch(kScratchDigits, (size_t)NB * kGRows * K, &dbuf))) return rc;
+  if ((rc = dev_scratch(kScratchDigitScale, (size_t)T_pad * 4, &qbuf))) return rc;
+  GemmParams p{};
+  if ((rc = int8_map(&p.tm_w, w, N, K, 128))) return rc;
+  if ((rc = int8_map(&p.tm_d, static_cast<int8_t *>(dbuf), (long)NB * kGRows, K, kGRows))) return rc;
+  p.dq = static_cast<float *>(qbuf);
+  p.scales = scales;
+  p.y = y0;
+  p.y_stride = s0;
+  p.y1 = y1;
+  p.y1_stride = s1;
+  p.n1 = n1;
+  p.y2 = y2;
+  p.y2_stride = s2;
+  p.n2 = n2;
   p.T = T;
   p.K = K;
   p.N = N;

@@ -418,10 +418,12 @@ def test_argmax_first_max_tie_rule():
 
 
 # ------------------------------------------------------------ attention ----
-@pytest.mark.parametrize("seq_q,seq_k,off", [(37, 37, 0), (1, 1024, 1023), (4, 200, 196)])
-def test_causal_attention(orc, seq_q, seq_k, off):
+@pytest.mark.parametrize("seq_q,seq_k,off,nh,nkv,hd", [
+    (37, 37, 0, 16, 8, 128), (1, 1024, 1023, 16, 8, 128), (4, 200, 196, 16, 8, 128), (404, 404, 0, 16, 8, 128),
+    (33, 100, 67, 16, 8, 128), (50, 50, 0, 8, 8, 64), (29, 70, 41, 6, 2, 64), (9, 40, 31, 16, 1, 128)])
+def test_causal_attention(orc, seq_q, seq_k, off, nh, nkv, hd):
+    """Prefill shapes, key tiles crossed at offsets, GQA groups of 1, 2, 3, 16."""
     rng = np.random.default_rng(seq_q + seq_k)
-    nh, nkv, hd = 16, 8, 128
     q = rng.standard_normal((seq_q, nh * hd)).astype(np.float32)
     k = rng.standard_normal((seq_k, nkv * hd)).astype(np.float32)
     v = rng.standard_normal((seq_k, nkv * hd)).astype(np.float32)
