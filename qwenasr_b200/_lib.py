@@ -10,7 +10,9 @@ import os
 import re
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libqwenasr_b200.so")
+# QASR_LIB selects another build of the library (e.g. one compiled with other
+# tuning constants); by default the in-tree one.
+LIB_PATH = os.environ.get("QASR_LIB") or os.path.join(HERE, "libqwenasr_b200.so")
 HEADER = os.path.join(os.path.dirname(HERE), "include", "qwenasr_cuda.h")
 
 QASR_OK = 0

@@ -131,12 +131,12 @@ causal_attention_kernel(float *__restrict__ out, const float *__restrict__ q, co
 // the previous kernel) waits for it.  More than 8 segments (very short
 // pairs) are taken 8 at a time.
 struct AttnSmall {
-  uint64_t bar[kAttnWarps][kAttnStages];
+  uint64_t bar[kAttnMaxWarps][kAttnStages];
   int nseg;
   int seg_pair[128], seg_a[128], seg_b[128];
   long long off[129];  // prefix sums of the pair lengths (off[n_pairs] = total keys)
-  int wseg[kAttnWarps], wa[kAttnWarps], wb[kAttnWarps];  // per group: warp -> segment, key range
-  int last[kAttnWarps];
+  int wseg[kAttnMaxWarps], wa[kAttnMaxWarps], wb[kAttnMaxWarps];  // per group: warp -> segment, key range
+  int last[kAttnMaxWarps];
 };
 
 QASR_DEV void tma_load_2d(float *dst, const CUtensorMap *tm, int x, int y, uint64_t *bar) {
@@ -147,13 +147,13 @@ QASR_DEV void tma_load_2d(float *dst, const CUtensorMap *tm, int x, int y, uint6
       : "memory");
 }
 
-template <int G>
-__global__ void __launch_bounds__(kAttnWarps * 32, 1)
+template <int G, int W>
+__global__ void __launch_bounds__(W * 32, 1)
 attn_decode_kernel(const __grid_constant__ AttnDecodeParams p) {
+  static_assert(W <= kAttnMaxWarps, "warps per CTA");
   extern __shared__ __align__(128) unsigned char smem_raw[];
   constexpr int TILE_F = kAttnTile * 128;  // floats per K (or V) tile
   constexpr int KPW = kAttnTile;           // keys per tile
-  constexpr int W = kAttnWarps;
   float *tiles = reinterpret_cast<float *>(smem_raw);
   float *slots = tiles + (size_t)W * kAttnStages * 2 * TILE_F;  // [warp][G][kAttnPartStride]
   AttnSmall &sm = *reinterpret_cast<AttnSmall *>(slots + (size_t)W * G * kAttnPartStride);
@@ -495,32 +495,34 @@ int attn_make_tensor_map(CUtensorMap *tm, const float *base, long rows, int kv_d
   return QASR_OK;
 }
 
-static size_t attn_smem(int G) {
-  return (size_t)kAttnWarps * kAttnStages * 2 * kAttnTile * 128 * 4 + (size_t)kAttnWarps * G * kAttnPartStride * 4 +
-         sizeof(AttnSmall);
+static size_t attn_smem(int G, int W) {
+  return (size_t)W * kAttnStages * 2 * kAttnTile * 128 * 4 + (size_t)W * G * kAttnPartStride * 4 + sizeof(AttnSmall);
 }
 
-template <int G>
+template <int G, int W>
 static int attn_launch_t(const AttnDecodeParams &p, cudaStream_t st, bool pdl) {
-  static bool attr_done = false;
-  if (!attr_done) {
-    int rc = cuda_status(cudaFuncSetAttribute(attn_decode_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              (int)attn_smem(G)),
+  static bool attr_done[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return QASR_ERR_INVALID;
+  if (!attr_done[dev]) {
+    int rc = cuda_status(cudaFuncSetAttribute(attn_decode_kernel<G, W>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              (int)attn_smem(G, W)),
                          "attention: shared memory opt-in");
     if (rc) return rc;
-    attr_done = true;
+    attr_done[dev] = true;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)attn_grid());
-  cfg.blockDim = dim3(kAttnWarps * 32);
-  cfg.dynamicSmemBytes = attn_smem(G);
+  cfg.blockDim = dim3(W * 32);
+  cfg.dynamicSmemBytes = attn_smem(G, W);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cuda_status(cudaLaunchKernelEx(&cfg, attn_decode_kernel<G>, p), "attention launch");
+  return cuda_status(cudaLaunchKernelEx(&cfg, attn_decode_kernel<G, W>, p), "attention launch");
 }
 
 int attn_decode_launch(const AttnDecodeParams &p, int group, cudaStream_t st, bool pdl) {
@@ -528,9 +530,10 @@ int attn_decode_launch(const AttnDecodeParams &p, int group, cudaStream_t st, bo
     set_error("attention: M*n_kv_heads = %d > 128", p.M * p.n_kv_heads);
     return QASR_ERR_UNSUPPORTED;
   }
+  const bool wide = p.M >= kAttnWideFromM;
   switch (group) {
-    case 1: return attn_launch_t<1>(p, st, pdl);
-    case 2: return attn_launch_t<2>(p, st, pdl);
+    case 1: return wide ? attn_launch_t<1, kAttnWideWarps>(p, st, pdl) : attn_launch_t<1, kAttnMaxWarps>(p, st, pdl);
+    case 2: return wide ? attn_launch_t<2, kAttnWideWarps>(p, st, pdl) : attn_launch_t<2, kAttnMaxWarps>(p, st, pdl);
     default:
       set_error("attention: GQA group size %d unsupported (1 or 2)", group);
       return QASR_ERR_UNSUPPORTED;

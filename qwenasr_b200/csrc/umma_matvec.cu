@@ -52,6 +52,24 @@ namespace qasr {
 
 constexpr int kUWarps = 8;
 constexpr int kUMaxStages = 8;
+// Ring depth of the gate/up kernel (the largest shared-memory user of the
+// step): a shallower ring lets it share SMs with its neighbours in the step.
+#ifndef QASR_SWIGLU_STAGES
+#define QASR_SWIGLU_STAGES 3
+#endif
+constexpr int kUSwigluStages = QASR_SWIGLU_STAGES;
+// Cluster sizes the planner must use per epilogue kind (0: its cost model).
+#ifndef QASR_FORCE_C_RESIDUAL
+#define QASR_FORCE_C_RESIDUAL 0
+#endif
+#ifndef QASR_FORCE_C_QKV
+#define QASR_FORCE_C_QKV 0
+#endif
+#ifndef QASR_FORCE_C_SWIGLU
+#define QASR_FORCE_C_SWIGLU 0
+#endif
+constexpr int kUForceCResidual = QASR_FORCE_C_RESIDUAL, kUForceCQkv = QASR_FORCE_C_QKV,
+              kUForceCSwiglu = QASR_FORCE_C_SWIGLU;
 constexpr int kUMaxCluster = 16;
 constexpr int kUTile = 128 * 128;        // bytes of one weight tile
 constexpr int kUBSlot = 32 * 128;        // bytes of the digit rows of one K tile
@@ -603,7 +621,7 @@ static int umma_max_clusters(int dev, int C, size_t smem) {
 // ranks of a cluster.  Cost model in units of one 16 KB weight tile streamed
 // by one SM: the busiest cluster's row tiles x K tiles per rank, plus the
 // exchange of partials when C > 1 (about three tiles' time, then one per
-// further row tile).
+// further row tile); on a tie the larger cluster (more CTAs) wins.
 template <MvEpi E, bool NORM>
 static UmmaPlan umma_plan(const UmmaParams &p, bool norm) {
   UmmaPlan best;
@@ -613,9 +631,13 @@ static UmmaPlan umma_plan(const UmmaParams &p, bool norm) {
   if (state < 0) return best;
   const int KT = p.K / 128, NT = (p.N + 127) / 128;
   double best_cost = 1e30;
+  const int forced = E == MvEpi::Residual ? kUForceCResidual : E == MvEpi::QkvPost ? kUForceCQkv
+                     : E == MvEpi::SwiGLU   ? kUForceCSwiglu
+                                            : 0;
   for (int C = 1; C <= kUMaxCluster && C <= KT; ++C) {
     if (KT % C || (C > 8 && state < 2) || 128 % (2 * C) && C > 1) continue;  // even row shares
-    int stages = kUMaxStages;
+    if (forced && C != forced) continue;
+    int stages = std::min(kUMaxStages, E == MvEpi::SwiGLU ? kUSwigluStages : kUMaxStages);
     while (stages > 2 && umma_smem_bytes(stages, C, norm, p.M, p.K) > 227 * 1024) --stages;
     const size_t smem = umma_smem_bytes(stages, C, norm, p.M, p.K);
     if (smem > 227 * 1024) continue;
@@ -624,7 +646,7 @@ static UmmaPlan umma_plan(const UmmaParams &p, bool norm) {
     const int clusters = std::min(NT, resident);
     const int tiles = (NT + clusters - 1) / clusters;
     const double cost = (double)tiles * (KT / C) + (C > 1 ? 3.0 + tiles : 0.0);
-    if (cost < best_cost - 1e-9) {
+    if (cost < best_cost + 1e-9) {  // ties go to the larger cluster: more SMs stream the weights
       best_cost = cost;
       best.C = C;
       best.clusters = clusters;
