@@ -538,6 +538,10 @@ int qasr_stream_unfixed(const qasr_stream *s, int32_t *ids, int cap, int *n);
  * (transcribe.rs:250-275). */
 int qasr_stream_tail_repeat(const int32_t *tokens, int n, int max_period, int *best_reps, int *best_period);
 int64_t qasr_find_split_point(const float *samples, int64_t n, int64_t target_sample, float search_sec);
+/* transcribe_audio's segment plan (transcribe.rs:317-345): starts[i] = the
+ * first sample of segment i, *n_segments their count (up to 127). */
+int qasr_plan_segments(const float *samples, int64_t n, float segment_sec, float search_sec, int64_t *starts, int cap,
+                       int *n_segments);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

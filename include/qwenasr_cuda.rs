@@ -197,4 +197,5 @@ extern "C" {
     pub fn qasr_stream_unfixed(s: *const QasrStream, ids: *mut i32, cap: c_int, n: *mut c_int) -> c_int;
     pub fn qasr_stream_tail_repeat(tokens: *const i32, n: c_int, max_period: c_int, best_reps: *mut c_int, best_period: *mut c_int) -> c_int;
     pub fn qasr_find_split_point(samples: *const f32, n: i64, target_sample: i64, search_sec: f32) -> i64;
+    pub fn qasr_plan_segments(samples: *const f32, n: i64, segment_sec: f32, search_sec: f32, starts: *mut i64, cap: c_int, n_segments: *mut c_int) -> c_int;
 }

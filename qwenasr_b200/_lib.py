@@ -160,6 +160,7 @@ _SIGS.update({
     "qasr_stream_unfixed": (I, [P, P, I, C.POINTER(C.c_int)]),
     "qasr_stream_tail_repeat": (I, [P, I, I, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
     "qasr_find_split_point": (I64, [P, I64, I64, F]),
+    "qasr_plan_segments": (I, [P, I64, F, F, P, I, C.POINTER(C.c_int)]),
     "qasr_encoder_device": (I, [P]),
     "qasr_transcribe_prompt_len": (I, [I, I, I]),
     "qasr_transcribe_batch": (I, [P, P, P, P, I, P, I, P, I, I, I, P, I, P]),

@@ -526,3 +526,33 @@ extern "C" int qasr_stream_push(qasr_stream *s, const float *samples, int64_t n_
   if (!delta.empty()) std::memcpy(emitted, delta.data(), delta.size() * 4);
   return QASR_OK;
 }
+
+// The segment plan of transcribe_audio (transcribe.rs:317-345): with
+// segment_sec > 0 and more than segment_sec + the search margin of audio,
+// split points every ~segment_sec at the quietest 100 ms within +-search of
+// the target (search = min(search_sec, segment_sec / 2)), at most 127
+// points.  starts[i] is the first sample of segment i (segment i ends at
+// starts[i+1], the last at n); *n_segments their count (starts holds cap).
+extern "C" int qasr_plan_segments(const float *samples, int64_t n, float segment_sec, float search_sec,
+                                  int64_t *starts, int cap, int *n_segments) {
+  if ((n > 0 && !samples) || n < 0 || !n_segments || (cap > 0 && !starts)) {
+    set_error("qasr_plan_segments: invalid arguments");
+    return QASR_ERR_INVALID;
+  }
+  const int64_t target = (int64_t)(segment_sec * 16000.0f);
+  const float search = std::min(search_sec, segment_sec / 2.0f);
+  const int64_t margin = (int64_t)(search * 16000.0f);
+  std::vector<int64_t> splits = {0};
+  if (segment_sec > 0.0f && n > target + margin) {
+    int64_t pos = 0;
+    while (pos + target + margin < n) {
+      const int64_t split = qasr_find_split_point(samples, n, pos + target, search);
+      splits.push_back(split);
+      pos = split;
+      if (splits.size() >= 127) break;
+    }
+  }
+  *n_segments = (int)splits.size();
+  std::memcpy(starts, splits.data(), sizeof(int64_t) * std::min<size_t>(cap, splits.size()));
+  return QASR_OK;
+}

@@ -63,3 +63,35 @@ def transcribe_ids(dec, enc, segments: Sequence, max_new: int, stop_at_eos: bool
               C.c_void_p(ids.ctypes.data), int(max_new), counts)
     del pa, fa, keep
     return [ids[i, :counts[i]].tolist() for i in range(n)]
+
+
+def plan_segments(samples, segment_sec: float, search_sec: float = 3.0) -> list[tuple[int, int]]:
+    """transcribe_audio's split of long audio (transcribe.rs:317-345):
+    [(start, end)] per segment, cut at the quietest 100 ms near every
+    segment_sec (no split when segment_sec <= 0)."""
+    s = np.ascontiguousarray(samples, dtype=np.float32)
+    starts = np.zeros(128, np.int64)
+    n = C.c_int(0)
+    _lib.call("qasr_plan_segments", C.c_void_p(s.ctypes.data) if s.size else None, s.size, C.c_float(segment_sec),
+              C.c_float(search_sec), C.c_void_p(starts.ctypes.data), starts.size, C.byref(n))
+    st = starts[:n.value].tolist()
+    return [(a, b) for a, b in zip(st, st[1:] + [s.size])]
+
+
+def transcribe_audio(dec, enc, samples, max_new: int, segment_sec: float = 0.0, search_sec: float = 3.0,
+                     stop_at_eos: bool = True, prompt_tokens=None, force_tokens=None) -> list[list[int]]:
+    """transcribe_audio (transcribe.rs:294-420) without past-text
+    conditioning: the planned segments (each shorter than 0.5 s zero-padded
+    to 0.5 s, as the reference does) transcribed independently, up to
+    dec.max_batch at a time; the ids of every segment in order."""
+    s = np.ascontiguousarray(samples, dtype=np.float32)
+    segs = []
+    for a, b in plan_segments(s, segment_sec, search_sec):
+        seg = s[a:b]
+        if seg.size < 8000:
+            seg = np.concatenate([seg, np.zeros(8000 - seg.size, np.float32)])
+        segs.append(seg)
+    out = []
+    for i in range(0, len(segs), dec.max_batch):
+        out += transcribe_ids(dec, enc, segs[i:i + dec.max_batch], max_new, stop_at_eos, prompt_tokens, force_tokens)
+    return out

@@ -149,3 +149,20 @@ def test_transcribe_rejects_bad_requests(engines):
         transcribe_ids(dec, enc, [synthetic.synthetic_audio(1.0, 0)] * 5, 4)  # more than max_batch
     with pytest.raises(QasrError):
         transcribe_ids(dec, enc, [synthetic.synthetic_audio(1.0, 0)], MAX_SEQ)  # positions past the cache
+
+
+def test_transcribe_audio_segments(engines):
+    """transcribe_audio (transcribe.rs:294-420, no past text): the planned
+    segments, a short tail padded to 0.5 s, batched; equal to transcribing
+    each planned segment alone."""
+    from qwenasr_b200.transcribe import plan_segments, transcribe_audio
+    wd, we, od, dec, enc = engines
+    a = synthetic.synthetic_audio(5.2, seed=41)
+    segs = plan_segments(a, 2.0, 0.5)
+    assert len(segs) >= 2
+    got = transcribe_audio(dec, enc, a, 6, segment_sec=2.0, search_sec=0.5, stop_at_eos=False)
+    for (s0, s1), ids in zip(segs, got):
+        seg = a[s0:s1]
+        if seg.size < 8000:
+            seg = np.concatenate([seg, np.zeros(8000 - seg.size, np.float32)])
+        assert transcribe_ids(dec, enc, [seg], 6) == [ids]
