@@ -74,6 +74,8 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="bounded CPU-baseline sample length")
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--workload", choices=("decode", "gemm", "encoder", "e2e", "segments"), default="decode")
+    ap.add_argument("--model", choices=("0.6b", "1.7b"), default="0.6b",
+                    help="decoder shapes of the decode workload (0.6b = BASELINE configs[2])")
     ap.add_argument("--layers", type=int, default=28,
                     help="decoder layers (28 = the configured workload; fewer only for profiler captures)")
     a = ap.parse_args()
@@ -264,7 +266,7 @@ def run_ours(a):
     from qwenasr_b200 import synthetic
     from qwenasr_b200.decoder import Decoder
 
-    cfg = dict(synthetic.DEC_0_6B, n_layers=a.layers)
+    cfg = dict(synthetic.DEC_0_6B if a.model == "0.6b" else synthetic.DEC_1_7B, n_layers=a.layers)
     M, L = a.batch, a.kv_len
     dev = torch.device(f"cuda:{local}")
     dec = Decoder(cfg, device=local, max_batch=M, max_seq=L)
@@ -356,7 +358,8 @@ def run_ours(a):
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
             "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8xf32",
             "data": "synthetic (seeded random-init weights, random KV history)",
-            "config": {"workload": "INT8 decode step, Qwen3-ASR-0.6B decoder shapes (BASELINE configs[2])",
+            "config": {"workload": ("INT8 decode step, Qwen3-ASR-0.6B decoder shapes (BASELINE configs[2])"
+                                    if a.model == "0.6b" else "INT8 decode step, Qwen3-ASR-1.7B decoder shapes"),
                        "batch_per_gpu": M, "kv_len": L, "layers": cfg["n_layers"], "vocab": cfg["vocab"],
                        "parallelism": f"replicas x{world} (no collective)",
                        "l2": f"inputs larger than L2: {step_bytes / 1e9:.2f} GB read per step"},
@@ -365,7 +368,8 @@ def run_ours(a):
             "gpu_launches": launches_per_step * a.steps,
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak,
-                         "traffic": NCU_TRAFFIC_M8.get(dom) if (M, L, cfg["n_layers"]) == (8, 1024, 28) else None,
+                         "traffic": (NCU_TRAFFIC_M8.get(dom)
+                                     if (M, L, cfg["n_layers"], a.model) == (8, 1024, 28, "0.6b") else None),
                          "traffic_source": "ncu capture of this workload (profiles/)", "peak_kind": peak_kind,
                          "bytes_per_launch": cb[dom], "us_per_launch": per_launch_s * 1e6},
             "step_roofline": {"bytes": step_bytes, "achieved_gbs": step_bytes / (ms / 1e3) / 1e9,
