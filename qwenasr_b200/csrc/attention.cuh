@@ -10,7 +10,10 @@ namespace qasr {
 // where the smaller shared-memory footprint lets an attention CTA share an SM
 // with the q/k/v kernel before it (measured: -3.5% step time at M=8, +2.5% at
 // M=1, hence the split).
-constexpr int kAttnMaxWarps = 8, kAttnWideWarps = 6, kAttnWideFromM = 4;
+#ifndef QASR_ATTN_WIDE_WARPS
+#define QASR_ATTN_WIDE_WARPS 6
+#endif
+constexpr int kAttnMaxWarps = 8, kAttnWideWarps = QASR_ATTN_WIDE_WARPS, kAttnWideFromM = 4;
 constexpr int kAttnTile = 8;          // keys per TMA tile (one warp's pipeline stage)
 constexpr int kAttnStages = 2;        // K+V tiles in flight per warp
 constexpr int kAttnPartStride = 132;  // floats per (segment, head) partial: o[128], max, sum, pad
