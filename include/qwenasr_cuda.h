@@ -439,6 +439,12 @@ int qasr_encoder_device(const qasr_encoder *enc);
  * Synchronous. */
 int qasr_encoder_forward(qasr_encoder *enc, const float *mel, int mel_frames, float *out, int out_rows,
                          int *n_tokens);
+/* qasr_encoder_forward over n independent segments at once (their tokens
+ * concatenated on the device, attention windows restarting per segment):
+ * outs[i] receives segment i's rows exactly as a forward of it alone would,
+ * n_tokens[i] their count.  Synchronous. */
+int qasr_encoder_forward_batch(qasr_encoder *enc, const float *const *mels, const int *mel_frames, int n,
+                               float *const *outs, const int *out_rows, int *n_tokens);
 
 /* ======================================================================
  * .qint8 model files (quantize.rs) and the V2 load path (context.rs:341-420)

@@ -132,6 +132,7 @@ _SIGS.update({
     "qasr_encoder_set_post": (I, [P, P, P, P, P, P, P]),
     "qasr_encoder_tokens": (I, [P, I]),
     "qasr_encoder_forward": (I, [P, P, I, P, I, C.POINTER(C.c_int)]),
+    "qasr_encoder_forward_batch": (I, [P, P, P, I, P, P, P]),
     "qasr_encoder_get_config": (P, [P]),
     "qasr_encoder_set_conv_int8": (I, [P, P, P, P, P, P, P, P, P]),
     "qasr_encoder_set_layer_int8": (I, [P, I, C.POINTER(EncLayerWeightsInt8)]),

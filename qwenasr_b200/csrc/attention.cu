@@ -28,85 +28,118 @@ constexpr int kCaTile = 32;   // keys per shared-memory tile (one per lane for t
 constexpr int kCaTasks = 16;  // (query, head) tasks per block: two per warp
 
 // Block (query block qb, kv head kvh): queries qb*QB .. +QB, every query head of
-// the GQA group (task = query * G + head-in-group).  K/V tiles of kCaTile keys
-// are staged in shared memory (K rows padded to HD+1 floats: the lane-per-key
-// score loop is conflict-free) and shared by all tasks; each task keeps a
-// running (max, sum, o) merged tile by tile (flash-style), its causal limit
-// masking the keys after q_offset + query.
+// the GQA group (task = query * G + head-in-group); warp w takes tasks w and
+// w + 8 together, so every K and V value it reads from shared memory serves
+// both.  K/V tiles of kCaTile keys are staged in shared memory (K rows padded
+// by 4 floats: 16-byte rows whose float4 reads, one key per lane, are
+// conflict-free) and shared by all tasks; each task keeps a running (max, sum,
+// o) merged tile by tile (flash-style), its causal limit masking the keys
+// after q_offset + query.
 template <int EPL>  // elements per lane: head_dim / 32
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 2)
 causal_attention_kernel(float *__restrict__ out, const float *__restrict__ q, const float *__restrict__ k,
                         const float *__restrict__ v, int seq_q, int seq_k, int n_heads, int n_kv_heads, float scale,
                         int q_offset) {
-  constexpr int HD = EPL * 32;
-  __shared__ float sK[kCaTile][HD + 1];
-  __shared__ float sV[kCaTile][HD];
-  __shared__ float sQ[kCaTasks][HD];
-  __shared__ float sP[8][kCaTile];
+  constexpr int HD = EPL * 32, KP = HD + 4;
+  __shared__ __align__(16) float sK[kCaTile][KP];
+  __shared__ __align__(16) float sV[kCaTile][HD];
+  __shared__ __align__(16) float sQ[kCaTasks][HD];
+  __shared__ float sP[8][2][kCaTile];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = n_heads / n_kv_heads, QB = max(1, kCaTasks / G), n_tasks = QB * G;
   const int kvh = blockIdx.y, i0 = blockIdx.x * QB;
   const long q_hidden = (long)n_heads * HD, kv_hidden = (long)n_kv_heads * HD;
   const int i_last = min(seq_q, i0 + QB) - 1;
   const int k_end = min(q_offset + i_last + 1, seq_k);  // keys any task of the block needs
-  // q rows of the block's tasks
-  for (int idx = threadIdx.x; idx < n_tasks * HD; idx += blockDim.x) {
+  // q rows of the block's tasks (zero for the unused ones)
+  for (int idx = threadIdx.x; idx < kCaTasks * HD; idx += blockDim.x) {
     const int t = idx / HD, d = idx % HD, i = i0 + t / G, h = kvh * G + t % G;
-    sQ[t][d] = i < seq_q ? q[(long)i * q_hidden + (long)h * HD + d] : 0.0f;
+    sQ[t][d] = (t < n_tasks && i < seq_q) ? q[(long)i * q_hidden + (long)h * HD + d] : 0.0f;
   }
+  bool act[2];
+  int lim[2];
   float m[2], l[2], o[2][EPL];
 #pragma unroll
   for (int u = 0; u < 2; ++u) {
+    const int t = warp + 8 * u, i = i0 + t / G;
+    act[u] = t < n_tasks && i < seq_q;
+    lim[u] = act[u] ? min(q_offset + i + 1, seq_k) : 0;  // keys < lim are visible
     m[u] = -INFINITY;
     l[u] = 0.0f;
 #pragma unroll
     for (int e = 0; e < EPL; ++e) o[u][e] = 0.0f;
   }
+  const float4 *q0 = reinterpret_cast<const float4 *>(sQ[warp]), *q1 = reinterpret_cast<const float4 *>(sQ[warp + 8]);
   for (int t0 = 0; t0 < k_end; t0 += kCaTile) {
     const int nk = min(kCaTile, k_end - t0);
     __syncthreads();  // the previous tile is consumed (and sQ written, first time)
-    stage_kv_rows<HD, 1>(&sK[0][0], &sV[0][0], k, v, t0, kv_hidden, (long)kvh * HD, nk);
+    stage_kv_rows<HD, 4>(&sK[0][0], &sV[0][0], k, v, t0, kv_hidden, (long)kvh * HD, nk);
     __syncthreads();
+    if (!act[0] && !act[1]) continue;  // warp-uniform, no barrier before the next tile
+    // scores of both tasks, one key per lane, two partial sums each
+    float sc[2] = {-INFINITY, -INFINITY};
+    if (lane < nk) {
+      const float4 *kr = reinterpret_cast<const float4 *>(sK[lane]);
+      float a0 = 0.0f, a1 = 0.0f, b0 = 0.0f, b1 = 0.0f;
+#pragma unroll 8
+      for (int e4 = 0; e4 < HD / 4; ++e4) {
+        const float4 kk = kr[e4], x = q0[e4], y = q1[e4];
+        a0 = fmaf(x.x, kk.x, a0);
+        a1 = fmaf(x.y, kk.y, a1);
+        b0 = fmaf(y.x, kk.x, b0);
+        b1 = fmaf(y.y, kk.y, b1);
+        a0 = fmaf(x.z, kk.z, a0);
+        a1 = fmaf(x.w, kk.w, a1);
+        b0 = fmaf(y.z, kk.z, b0);
+        b1 = fmaf(y.w, kk.w, b1);
+      }
+      const int key = t0 + lane;
+      if (key < lim[0]) sc[0] = __fmul_rn(__fadd_rn(a0, a1), scale);
+      if (key < lim[1]) sc[1] = __fmul_rn(__fadd_rn(b0, b1), scale);
+    }
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
-      const int t = warp + 8 * u;
-      if (t >= n_tasks) continue;  // warp-uniform
-      const int i = i0 + t / G;
-      if (i >= seq_q) continue;
-      const int lim = min(q_offset + i + 1, seq_k);  // keys < lim are visible
-      // scores: lane j takes key t0 + j
-      float sc = -INFINITY;
-      if (lane < nk && t0 + lane < lim) {
-        float d = 0.0f;
-#pragma unroll 16
-        for (int e = 0; e < HD; ++e) d = fmaf(sQ[t][e], sK[lane][e], d);
-        sc = __fmul_rn(d, scale);
+      float pj = 0.0f, corr = 1.0f;
+      if (act[u]) {  // warp-uniform
+        const float mn = fmaxf(m[u], warp_max(sc[u]));
+        if (mn != -INFINITY) {  // some key of this task visible so far
+          corr = m[u] == -INFINITY ? 0.0f : expf(__fsub_rn(m[u], mn));
+          pj = sc[u] == -INFINITY ? 0.0f : expf(__fsub_rn(sc[u], mn));
+          l[u] = __fadd_rn(__fmul_rn(l[u], corr), warp_sum(pj));
+          m[u] = mn;
+        }
       }
-      const float mt = warp_max(sc);
-      const float mn = fmaxf(m[u], mt);
-      if (mn == -INFINITY) continue;  // no visible key yet (only before the first tile)
-      const float corr = m[u] == -INFINITY ? 0.0f : expf(__fsub_rn(m[u], mn));
-      const float pj = sc == -INFINITY ? 0.0f : expf(__fsub_rn(sc, mn));
-      l[u] = __fadd_rn(__fmul_rn(l[u], corr), warp_sum(pj));
-      m[u] = mn;
-      sP[warp][lane] = pj;
-      __syncwarp();
+      sP[warp][u][lane] = pj;  // zero for masked keys, skipped and unused tasks
 #pragma unroll
       for (int e = 0; e < EPL; ++e) o[u][e] = __fmul_rn(o[u][e], corr);
-      for (int j = 0; j < nk; ++j) {
-        const float w = sP[warp][j];
-#pragma unroll
-        for (int e = 0; e < EPL; ++e) o[u][e] = fmaf(w, sV[j][lane * EPL + e], o[u][e]);
-      }
-      __syncwarp();  // sP is rewritten by the next task
     }
+    __syncwarp();
+    for (int j = 0; j < nk; ++j) {
+      const float p0 = sP[warp][0][j], p1 = sP[warp][1][j];
+      float vv[EPL];
+      if constexpr (EPL == 4) {
+        const float4 t4 = *reinterpret_cast<const float4 *>(&sV[j][lane * 4]);
+        vv[0] = t4.x;
+        vv[1] = t4.y;
+        vv[2] = t4.z;
+        vv[3] = t4.w;
+      } else {
+        const float2 t2 = *reinterpret_cast<const float2 *>(&sV[j][lane * 2]);
+        vv[0] = t2.x;
+        vv[1] = t2.y;
+      }
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) {
+        o[0][e] = fmaf(p0, vv[e], o[0][e]);
+        o[1][e] = fmaf(p1, vv[e], o[1][e]);
+      }
+    }
+    __syncwarp();  // sP is rewritten by the next tile
   }
 #pragma unroll
   for (int u = 0; u < 2; ++u) {
-    const int t = warp + 8 * u;
-    if (t >= n_tasks) continue;
-    const int i = i0 + t / G, h = kvh * G + t % G;
-    if (i >= seq_q) continue;
+    if (!act[u]) continue;
+    const int t = warp + 8 * u, i = i0 + t / G, h = kvh * G + t % G;
     const float inv = l[u] > 0.0f ? __fdiv_rn(1.0f, l[u]) : 0.0f;
 #pragma unroll
     for (int e = 0; e < EPL; ++e)

@@ -14,8 +14,14 @@ namespace qasr {
 #define QASR_ATTN_WIDE_WARPS 6
 #endif
 constexpr int kAttnMaxWarps = 8, kAttnWideWarps = QASR_ATTN_WIDE_WARPS, kAttnWideFromM = 4;
-constexpr int kAttnTile = 8;          // keys per TMA tile (one warp's pipeline stage)
-constexpr int kAttnStages = 2;        // K+V tiles in flight per warp
+#ifndef QASR_ATTN_TILE
+#define QASR_ATTN_TILE 8
+#endif
+#ifndef QASR_ATTN_STAGES
+#define QASR_ATTN_STAGES 2
+#endif
+constexpr int kAttnTile = QASR_ATTN_TILE;      // keys per TMA tile (one warp's pipeline stage)
+constexpr int kAttnStages = QASR_ATTN_STAGES;  // K+V tiles in flight per warp
 constexpr int kAttnPartStride = 132;  // floats per (segment, head) partial: o[128], max, sum, pad
 #ifndef QASR_ATTN_MIN_KEYS
 #define QASR_ATTN_MIN_KEYS 256

@@ -673,13 +673,31 @@ extern "C" int qasr_decoder_prefill(qasr_decoder *d, int slot, const float *embe
     if ((rc = qasr_causal_attention(d->pf_attn, d->pf_q, kc + lay, vc + lay, seq, total, c.n_heads, c.n_kv_heads, hd,
                                     scale, start_pos, st)))
       break;
-    if ((rc = qasr_linear_nobias_int8(d->pf_proj, d->pf_attn, L.wo, L.so, seq, q_dim, H, st))) break;
-    if ((rc = qasr_add_inplace(d->pf_x, d->pf_proj, (int64_t)seq * H, st))) break;
+    // o-proj + residual, gate/up + SwiGLU, down + residual: fused GEMM
+    // epilogues when the tensor-core GEMM takes the shape (seq > 8)
+    const bool fused = seq > 8;
+    rc = fused ? int8_gemm_epi(d->pf_x, H, d->pf_attn, q_dim, L.wo, L.so, seq, q_dim, H, 1, st) : QASR_ERR_UNSUPPORTED;
+    if (rc == QASR_ERR_UNSUPPORTED) {
+      if ((rc = qasr_linear_nobias_int8(d->pf_proj, d->pf_attn, L.wo, L.so, seq, q_dim, H, st))) break;
+      if ((rc = qasr_add_inplace(d->pf_x, d->pf_proj, (int64_t)seq * H, st))) break;
+    } else if (rc) {
+      break;
+    }
     if ((rc = qasr_rms_norm(d->pf_xn, d->pf_x, L.post_norm, seq, H, c.eps, st))) break;
-    if ((rc = qasr_linear_nobias_int8(d->pf_gu, d->pf_xn, L.gate_up, L.sgu, seq, H, 2 * I, st))) break;
-    if ((rc = qasr_swiglu_multiply(d->pf_h, d->pf_gu, seq, I, st))) break;
-    if ((rc = qasr_linear_nobias_int8(d->pf_proj, d->pf_h, L.down, L.sdown, seq, I, H, st))) break;
-    if ((rc = qasr_add_inplace(d->pf_x, d->pf_proj, (int64_t)seq * H, st))) break;
+    rc = fused ? int8_gemm_epi(d->pf_h, I, d->pf_xn, H, L.gate_up, L.sgu, seq, H, 2 * I, 2, st) : QASR_ERR_UNSUPPORTED;
+    if (rc == QASR_ERR_UNSUPPORTED) {
+      if ((rc = qasr_linear_nobias_int8(d->pf_gu, d->pf_xn, L.gate_up, L.sgu, seq, H, 2 * I, st))) break;
+      if ((rc = qasr_swiglu_multiply(d->pf_h, d->pf_gu, seq, I, st))) break;
+    } else if (rc) {
+      break;
+    }
+    rc = fused ? int8_gemm_epi(d->pf_x, H, d->pf_h, I, L.down, L.sdown, seq, I, H, 1, st) : QASR_ERR_UNSUPPORTED;
+    if (rc == QASR_ERR_UNSUPPORTED) {
+      if ((rc = qasr_linear_nobias_int8(d->pf_proj, d->pf_h, L.down, L.sdown, seq, I, H, st))) break;
+      if ((rc = qasr_add_inplace(d->pf_x, d->pf_proj, (int64_t)seq * H, st))) break;
+    } else if (rc) {
+      break;
+    }
   }
   if (!rc) rc = cuda_status(cudaStreamSynchronize(st), "qasr_decoder_prefill");
   return rc;

@@ -527,12 +527,13 @@ extern "C" int qasr_encoder_tokens(const qasr_encoder *e, int mel_frames) {
   return total;
 }
 
-extern "C" int qasr_encoder_forward(qasr_encoder *e, const float *mel, int mel_frames, float *out, int out_rows,
-                                    int *n_tokens) {
-  if (!e || !mel || !out || mel_frames <= 0) {
-    set_error("qasr_encoder_forward: invalid arguments");
-    return QASR_ERR_INVALID;
-  }
+// Encoder::forward over n independent segments at once: their tokens are
+// concatenated (segment s at rows off_s ..), every per-token operation runs
+// once over all rows, the attention windows restart at every segment and
+// each segment's conv chunks are padded on their own, so segment s's rows
+// equal a forward of that segment alone.
+static int encoder_run(qasr_encoder *e, int n, const float *const *mels, const int *frames, float *const *outs,
+                       const int *out_rows, int *n_tokens) {
   cudaSetDevice(e->device);
   for (EncMat *m : enc_mats(e))
     if (!m->ready()) {
@@ -541,18 +542,29 @@ extern "C" int qasr_encoder_forward(qasr_encoder *e, const float *mel, int mel_f
     }
   const qasr_encoder_config &c = e->cfg;
   const int D = c.d_model, F = c.ffn_dim, O = c.output_dim, CH = kConvHidden, cs = c.chunk_size;
-  const int T = qasr_encoder_tokens(e, mel_frames);
-  if (out_rows < T) {
-    set_error("qasr_encoder_forward: output has %d rows, %d tokens needed", out_rows, T);
-    return QASR_ERR_INVALID;
+  std::vector<int> seg_T(n), seg_off(n + 1, 0);
+  int max_frames = 0, max_full = 0;
+  for (int i = 0; i < n; ++i) {
+    if (!mels[i] || !outs[i] || frames[i] <= 0) {
+      set_error("qasr_encoder_forward: invalid arguments (segment %d)", i);
+      return QASR_ERR_INVALID;
+    }
+    seg_T[i] = qasr_encoder_tokens(e, frames[i]);
+    if (out_rows[i] < seg_T[i]) {
+      set_error("qasr_encoder_forward: output %d has %d rows, %d tokens needed", i, out_rows[i], seg_T[i]);
+      return QASR_ERR_INVALID;
+    }
+    seg_off[i + 1] = seg_off[i] + seg_T[i];
+    max_frames = std::max(max_frames, frames[i]);
+    max_full = std::max(max_full, frames[i] / cs);
   }
+  const int T = seg_off[n];
   cudaStream_t st = e->stream;
   int rc = QASR_OK;
   // buffers: per-token activations, and the conv stem of up to kStemGroup chunks
   const int h1 = (kMelBins + 2 - 3) / 2 + 1, h2 = (h1 + 2 - 3) / 2 + 1, h3 = (h2 + 2 - 3) / 2 + 1;
   const int w1m = (cs + 2 - 3) / 2 + 1, w2m = (w1m + 2 - 3) / 2 + 1, w3m = (w2m + 2 - 3) / 2 + 1;
-  const int n_full = mel_frames / cs, tail = mel_frames % cs;
-  const int gmax = std::max(1, std::min(n_full, kStemGroup));
+  const int gmax = std::max(1, std::min(max_full, kStemGroup));
   if (T > e->tok_cap) {
     if ((rc = cuda_status(cudaStreamSynchronize(st), "qasr_encoder_forward"))) return rc;
     if (e->act) cudaFree(e->act);
@@ -589,14 +601,18 @@ extern "C" int qasr_encoder_forward(qasr_encoder *e, const float *mel, int mel_f
     e->act_b = e->act_a + pos1 * CH;
     e->stem_cap = gmax;
   }
-  // the stem kernels read the mel directly: a host mel is copied to the device first
-  {
+  // ---- conv stem (encoder.rs:281-348) per segment: groups of full chunks, then the tail chunk
+  int tok = 0;
+  for (int sg = 0; sg < n && !rc; ++sg) {
+    const float *mel = mels[sg];
+    const int mel_frames = frames[sg], tail = mel_frames % cs;
+    // the stem kernels read the mel directly: a host mel is copied to the device first
     cudaPointerAttributes pa{};
     const bool on_dev = cudaPointerGetAttributes(&pa, mel) == cudaSuccess &&
                         (pa.type == cudaMemoryTypeDevice || pa.type == cudaMemoryTypeManaged);
     cudaGetLastError();  // an unknown pointer is not an error here
     if (!on_dev) {
-      const size_t bytes = (size_t)kMelBins * mel_frames * 4;
+      const size_t bytes = (size_t)kMelBins * max_frames * 4;
       if (bytes > e->mel_cap) {
         if ((rc = cuda_status(cudaStreamSynchronize(st), "qasr_encoder_forward"))) return rc;
         if (e->mel_dev) cudaFree(e->mel_dev);
@@ -605,55 +621,60 @@ extern "C" int qasr_encoder_forward(qasr_encoder *e, const float *mel, int mel_f
         if ((rc = cuda_status(cudaMalloc(&e->mel_dev, bytes), "qasr_encoder_forward: mel buffer"))) return rc;
         e->mel_cap = bytes;
       }
-      if ((rc = cuda_status(cudaMemcpyAsync(e->mel_dev, mel, bytes, cudaMemcpyDefault, st), "qasr_encoder_forward: mel")))
+      // the previous segment's stem must be done with the buffer
+      if ((rc = cuda_status(cudaMemcpyAsync(e->mel_dev, mel, (size_t)kMelBins * mel_frames * 4, cudaMemcpyDefault, st),
+                            "qasr_encoder_forward: mel")))
         return rc;
       mel = e->mel_dev;
     }
-  }
-  // ---- conv stem (encoder.rs:281-348): groups of full chunks, then the tail chunk
-  int tok = 0;
-  for (int first = 0; first < mel_frames && !rc;) {
-    const bool full = first + cs <= mel_frames;
-    const int B = full ? std::min(kStemGroup, (mel_frames - first) / cs) : 1;
-    const int cw = full ? cs : tail;
-    const int w1 = (cw + 2 - 3) / 2 + 1, w2 = (w1 + 2 - 3) / 2 + 1, w3 = (w2 + 2 - 3) / 2 + 1;
-    const long r1 = (long)B * h1 * w1, r2 = (long)B * h2 * w2, r3 = (long)B * h3 * w3;
-    conv1_gelu_kernel<<<grid_of(r1 * CH), 256, 0, st>>>(e->act_a, mel, mel_frames, first, cs, cw, B, h1, w1,
-                                                        e->conv_w[0], e->conv_b[0], CH);
-    rc = launch_status("qasr_encoder_forward: conv1");
-    if (!rc) {
-      im2col_cl_kernel<<<grid_of(r2 * CH * 9 / 4), 256, 0, st>>>(e->cols, e->act_a, CH, h1, w1, B, h2, w2);
-      rc = launch_status("qasr_encoder_forward: conv2 patches");
+    for (int first = 0; first < mel_frames && !rc;) {
+      const bool full = first + cs <= mel_frames;
+      const int B = full ? std::min(kStemGroup, (mel_frames - first) / cs) : 1;
+      const int cw = full ? cs : tail;
+      const int w1 = (cw + 2 - 3) / 2 + 1, w2 = (w1 + 2 - 3) / 2 + 1, w3 = (w2 + 2 - 3) / 2 + 1;
+      const long r1 = (long)B * h1 * w1, r2 = (long)B * h2 * w2, r3 = (long)B * h3 * w3;
+      conv1_gelu_kernel<<<grid_of(r1 * CH), 256, 0, st>>>(e->act_a, mel, mel_frames, first, cs, cw, B, h1, w1,
+                                                          e->conv_w[0], e->conv_b[0], CH);
+      rc = launch_status("qasr_encoder_forward: conv1");
+      if (!rc) {
+        im2col_cl_kernel<<<grid_of(r2 * CH * 9 / 4), 256, 0, st>>>(e->cols, e->act_a, CH, h1, w1, B, h2, w2);
+        rc = launch_status("qasr_encoder_forward: conv2 patches");
+      }
+      if (!rc) rc = conv_gemm(e, 1, e->act_b, e->cols, (int)r2, st);
+      if (!rc) rc = qasr_gelu(e->act_b, (int64_t)r2 * CH, st);
+      if (!rc) {
+        im2col_cl_kernel<<<grid_of(r3 * CH * 9 / 4), 256, 0, st>>>(e->cols, e->act_b, CH, h2, w2, B, h3, w3);
+        rc = launch_status("qasr_encoder_forward: conv3 patches");
+      }
+      if (!rc) rc = conv_gemm(e, 2, e->act_a, e->cols, (int)r3, st);
+      if (!rc) rc = qasr_gelu(e->act_a, (int64_t)r3 * CH, st);
+      if (!rc) {
+        conv_reshape_cl_kernel<<<grid_of(r3 * CH), 256, 0, st>>>(e->cols, e->act_a, CH, h3, w3, B);
+        rc = launch_status("qasr_encoder_forward: reshape");
+      }
+      if (!rc) rc = mat_apply(e->x + (size_t)tok * D, e->cols, e->conv_out, nullptr, B * w3, st);
+      if (!rc) rc = qasr_sinusoidal_pe(e->pe, w3, D, st);
+      if (!rc) {
+        add_chunk_pe_kernel<<<grid_of((long)B * w3 * D), 256, 0, st>>>(e->x + (size_t)tok * D, e->pe, B, w3, D);
+        rc = launch_status("qasr_encoder_forward: positions");
+      }
+      tok += B * w3;
+      first += B * cw;
     }
-    if (!rc) rc = conv_gemm(e, 1, e->act_b, e->cols, (int)r2, st);
-    if (!rc) rc = qasr_gelu(e->act_b, (int64_t)r2 * CH, st);
-    if (!rc) {
-      im2col_cl_kernel<<<grid_of(r3 * CH * 9 / 4), 256, 0, st>>>(e->cols, e->act_b, CH, h2, w2, B, h3, w3);
-      rc = launch_status("qasr_encoder_forward: conv3 patches");
-    }
-    if (!rc) rc = conv_gemm(e, 2, e->act_a, e->cols, (int)r3, st);
-    if (!rc) rc = qasr_gelu(e->act_a, (int64_t)r3 * CH, st);
-    if (!rc) {
-      conv_reshape_cl_kernel<<<grid_of(r3 * CH), 256, 0, st>>>(e->cols, e->act_a, CH, h3, w3, B);
-      rc = launch_status("qasr_encoder_forward: reshape");
-    }
-    if (!rc) rc = mat_apply(e->x + (size_t)tok * D, e->cols, e->conv_out, nullptr, B * w3, st);
-    if (!rc) rc = qasr_sinusoidal_pe(e->pe, w3, D, st);
-    if (!rc) {
-      add_chunk_pe_kernel<<<grid_of((long)B * w3 * D), 256, 0, st>>>(e->x + (size_t)tok * D, e->pe, B, w3, D);
-      rc = launch_status("qasr_encoder_forward: positions");
-    }
-    tok += B * w3;
-    first += B * cw;
   }
   if (rc) return rc;
   // ---- attention windows (encoder.rs:350-357)
   const int tpc = chunk_tokens(cs);
   const int wsize = tpc * (c.n_window_infer / cs);
-  const int nw = (T + wsize - 1) / wsize;
-  std::vector<int32_t> starts(nw + 1);
-  for (int w = 0; w < nw; ++w) starts[w] = w * wsize;
-  starts[nw] = T;
+  std::vector<int32_t> starts;
+  int max_window = 0;
+  for (int i = 0; i < n; ++i)
+    for (int w0 = 0; w0 < seg_T[i]; w0 += wsize) {
+      starts.push_back(seg_off[i] + w0);
+      max_window = std::max(max_window, std::min(wsize, seg_T[i] - w0));
+    }
+  const int nw = (int)starts.size();
+  starts.push_back(T);
   if (nw + 1 > e->win_cap) {
     if (e->win) cudaFree(e->win);
     e->win = nullptr;
@@ -674,7 +695,7 @@ extern "C" int qasr_encoder_forward(qasr_encoder *e, const float *mel, int mel_f
     if (!rc) rc = mat_apply(e->v, e->xn, L.wv, L.bv, T, st);
     if (!rc)
       rc = bidir_attention_launch(e->attn, e->q, e->k, e->v, T, c.n_heads, c.head_dim, scale, e->win, nw,
-                                  std::min(wsize, T), st);
+                                  max_window, st);
     if (!rc) rc = mat_apply(e->proj, e->attn, L.wo, L.bo, T, st);
     if (!rc) rc = qasr_add_inplace(e->x, e->proj, td, st);
     if (!rc) rc = qasr_layer_norm(e->xn, e->x, L.ffn_norm_w, L.ffn_norm_b, T, D, 1e-5f, st);
@@ -688,8 +709,34 @@ extern "C" int qasr_encoder_forward(qasr_encoder *e, const float *mel, int mel_f
   if (!rc) rc = mat_apply(e->q, e->xn, e->proj1, e->proj1_b, T, st);
   if (!rc) rc = qasr_gelu(e->q, td, st);
   if (!rc) rc = mat_apply(e->out, e->q, e->proj2, e->proj2_b, T, st);
-  if (!rc) rc = cuda_status(cudaMemcpyAsync(out, e->out, (size_t)T * O * 4, cudaMemcpyDefault, st), "encoder output");
+  for (int i = 0; i < n && !rc; ++i)
+    rc = cuda_status(cudaMemcpyAsync(outs[i], e->out + (size_t)seg_off[i] * O, (size_t)seg_T[i] * O * 4,
+                                     cudaMemcpyDefault, st),
+                     "encoder output");
   if (!rc) rc = cuda_status(cudaStreamSynchronize(st), "qasr_encoder_forward");
+  if (!rc && n_tokens)
+    for (int i = 0; i < n; ++i) n_tokens[i] = seg_T[i];
+  return rc;
+}
+
+extern "C" int qasr_encoder_forward(qasr_encoder *e, const float *mel, int mel_frames, float *out, int out_rows,
+                                    int *n_tokens) {
+  if (!e || !mel || !out || mel_frames <= 0) {
+    set_error("qasr_encoder_forward: invalid arguments");
+    return QASR_ERR_INVALID;
+  }
+  float *outs[1] = {out};
+  int T = 0;
+  const int rc = encoder_run(e, 1, &mel, &mel_frames, outs, &out_rows, &T);
   if (!rc && n_tokens) *n_tokens = T;
   return rc;
+}
+
+extern "C" int qasr_encoder_forward_batch(qasr_encoder *e, const float *const *mels, const int *mel_frames, int n,
+                                          float *const *outs, const int *out_rows, int *n_tokens) {
+  if (!e || !mels || !mel_frames || !outs || !out_rows || n <= 0) {
+    set_error("qasr_encoder_forward_batch: invalid arguments");
+    return QASR_ERR_INVALID;
+  }
+  return encoder_run(e, n, mels, mel_frames, outs, out_rows, n_tokens);
 }

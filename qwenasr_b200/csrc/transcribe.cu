@@ -155,20 +155,43 @@ extern "C" int qasr_transcribe_batch(qasr_decoder *dec, qasr_encoder *enc, const
     }
   }
   const int max_prompt = qasr_transcribe_prompt_len(max_tokens, n_prompt, n_force);
-  const int max_frames = qasr_mel_frames(max_samples);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(qasr_decoder_stream(dec));
-  void *enc_out = nullptr, *prompt = nullptr;
+  // every segment's log-mel, then one encoder pass over all of them (transcribe.rs:78-96)
+  std::vector<int> frames(M), tokens(M), tok_off(M + 1, 0);
+  std::vector<size_t> mel_off(M + 1, 0);
+  for (int i = 0; i < M; ++i) {
+    frames[i] = qasr_mel_frames(n_samples[i]);
+    mel_off[i + 1] = mel_off[i] + (size_t)128 * frames[i];
+    tokens[i] = qasr_encoder_tokens(enc, frames[i]);
+    tok_off[i + 1] = tok_off[i] + tokens[i];
+  }
+  void *audio = nullptr, *mel = nullptr, *enc_out = nullptr, *prompt = nullptr;
   int rc;
-  (void)max_frames;
-  if ((rc = dev_scratch(kScratchEncOut, (size_t)max_tokens * H * 4, &enc_out))) return rc;
+  if ((rc = dev_scratch(kScratchAudio, (size_t)max_samples * 4, &audio))) return rc;
+  if ((rc = dev_scratch(kScratchMelOut, mel_off[M] * 4, &mel))) return rc;
+  if ((rc = dev_scratch(kScratchEncOut, (size_t)tok_off[M] * H * 4, &enc_out))) return rc;
   if ((rc = dev_scratch(kScratchPrompt, (size_t)max_prompt * H * 4, &prompt))) return rc;
+  std::vector<const float *> mels(M);
+  std::vector<float *> outs(M);
+  for (int i = 0; i < M; ++i) {
+    float *m = static_cast<float *>(mel) + mel_off[i];
+    if ((rc = cuda_status(cudaMemcpyAsync(audio, samples[i], (size_t)n_samples[i] * 4, cudaMemcpyDefault, st),
+                          "qasr_transcribe_batch: samples")))
+      return rc;
+    if ((rc = qasr_mel_spectrogram(m, static_cast<const float *>(audio), n_samples[i], st))) return rc;
+    mels[i] = m;
+    outs[i] = static_cast<float *>(enc_out) + (size_t)tok_off[i] * H;
+  }
+  if ((rc = cuda_status(cudaStreamSynchronize(st), "qasr_transcribe_batch: mel"))) return rc;
+  std::vector<int> got(M);
+  if ((rc = qasr_encoder_forward_batch(enc, mels.data(), frames.data(), M, outs.data(), tokens.data(), got.data())))
+    return rc;
+  cudaSetDevice(dev);
   std::vector<int32_t> tok0(M), pos0(M), pre;
   float *embeds = static_cast<float *>(prompt);
   for (int i = 0; i < M; ++i) {
-    // mel + encoder (transcribe.rs:78-96)
-    int T = 0;
-    if ((rc = encode_samples(enc, dev, st, samples[i], n_samples[i], static_cast<float *>(enc_out), max_tokens, &T)))
-      return rc;
+    const int T = got[i];
+    const float *rows_i = outs[i];
     // prompt embeddings (transcribe.rs:98-170): token rows around the audio rows
     pre.assign(kPrefixHead, kPrefixHead + kHead);
     pre.insert(pre.end(), prompt_tokens, prompt_tokens + n_prompt);
@@ -178,7 +201,7 @@ extern "C" int qasr_transcribe_batch(qasr_decoder *dec, qasr_encoder *enc, const
     post.insert(post.end(), force_tokens, force_tokens + n_force);
     const int total = prefix_len + T + (int)post.size();
     if ((rc = qasr_decoder_embed(dec, pre.data(), prefix_len, embeds))) return rc;
-    if ((rc = cuda_status(cudaMemcpyAsync(embeds + (size_t)prefix_len * H, enc_out, (size_t)T * H * 4,
+    if ((rc = cuda_status(cudaMemcpyAsync(embeds + (size_t)prefix_len * H, rows_i, (size_t)T * H * 4,
                                           cudaMemcpyDeviceToDevice, st),
                           "qasr_transcribe_batch: audio rows")))
       return rc;

@@ -47,6 +47,10 @@ int int8_gemm(float *y, long y_stride, const float *x, long x_stride, const int8
 // cores (three digit planes per operand); QASR_ERR_UNSUPPORTED as above.
 int f32_gemm(float *y, long y_stride, const float *x, long x_stride, const float *w, const float *bias, int T, int K,
              int N, cudaStream_t st);
+// int8_gemm with a fused epilogue: 1 = add into y (residual), 2 = SwiGLU of
+// interleaved (gate, up) row pairs into y [T, N/2].
+int int8_gemm_epi(float *y, long y_stride, const float *x, long x_stride, const int8_t *w, const float *scales, int T,
+                  int K, int N, int epi, cudaStream_t st);
 // int8_gemm with the output rows split at n1 and n2 into three matrices.
 int int8_gemm_split3(float *y0, long s0, float *y1, long s1, int n1, float *y2, long s2, int n2, const float *x,
                      long x_stride, const int8_t *w, const float *scales, int T, int K, int N, cudaStream_t st);

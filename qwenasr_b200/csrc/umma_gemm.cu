@@ -53,6 +53,7 @@ constexpr int kGATile = 128 * 128;        // weight tile bytes
 constexpr int kGBTile = kGRows * 128;     // digit tile bytes
 constexpr int kGTmemCols = 256;           // two 96-column accumulators
 constexpr uint32_t kGIdesc = umma_idesc_s8(128, kGRows);
+constexpr int kGemmStore = 0, kGemmResidual = 1, kGemmSwiGLU = 2;
 
 // ---------------------------------------------------------------- digits --
 __global__ void __launch_bounds__(256) digit_rows_kernel(int8_t *__restrict__ D, float *__restrict__ dq,
@@ -114,6 +115,7 @@ struct GemmParams {
   float *y1, *y2;
   long y1_stride, y2_stride;
   int n1, n2;
+  int epi;  // kGemmStore, kGemmResidual (y += result), kGemmSwiGLU (rows g,u interleaved -> y[t, row/2])
   int T, K, N;
   int *err;
 };
@@ -244,23 +246,33 @@ __global__ void __launch_bounds__(256, 1) gemm_kernel(const __grid_constant__ Ge
         V[tl] += (((long long)(int)a0[tl] << 16) + ((long long)(int)a1[tl] << 8) + (long long)(int)a2[tl]) << wshift;
       if (a != PLANES - 1) continue;
       const int row = rt * 128 + ri;
-      if (row < p.N) {
-        const float sc = p.scales[row];
-        const float b = p.bias ? p.bias[row] : 0.0f;
-        const int t0 = tb * kGTok;
+      const bool row_ok = row < p.N;
+      const float sc = row_ok ? p.scales[row] : 0.0f;
+      const float b = (row_ok && p.bias) ? p.bias[row] : 0.0f;
+      const int t0 = tb * kGTok;
 #pragma unroll
-        for (int tl = 0; tl < kGTok; ++tl) {
-          const int t = t0 + tl;
-          if (t < p.T) {
-            float v = __fmul_rn(__fmul_rn(__ll2float_rn(V[tl]), __ldg(p.dq + t)), sc);
-            if (p.bias) v = __fadd_rn(v, b);
-            if (row >= p.n2)
-              p.y2[(size_t)t * p.y2_stride + (row - p.n2)] = v;
-            else if (row >= p.n1)
-              p.y1[(size_t)t * p.y1_stride + (row - p.n1)] = v;
-            else
-              p.y[(size_t)t * p.y_stride + row] = v;
+      for (int tl = 0; tl < kGTok; ++tl) {
+        const int t = t0 + tl;  // dq holds the padded block: defined past T
+        float v = __fmul_rn(__fmul_rn(__ll2float_rn(V[tl]), __ldg(p.dq + t)), sc);
+        if (p.bias) v = __fadd_rn(v, b);
+        if (p.epi == kGemmSwiGLU) {
+          // avx::swiglu_interleaved (avx.rs:568-599) on the (gate, up) row pair
+          const float u = __shfl_xor_sync(0xffffffffu, v, 1);
+          if (t < p.T && row_ok && !(ri & 1)) {
+            const int j = row >> 1, body = (p.N >> 1) - (p.N >> 1) % 8;
+            const float silu = j < body ? __fdiv_rn(v, __fadd_rn(1.0f, fast_exp_ref(__fsub_rn(0.0f, v))))
+                                        : __fdiv_rn(v, __fadd_rn(1.0f, expf(-v)));
+            p.y[(size_t)t * p.y_stride + j] = __fmul_rn(silu, u);
           }
+        } else if (t < p.T && row_ok) {
+          float *dst;
+          if (row >= p.n2)
+            dst = p.y2 + (size_t)t * p.y2_stride + (row - p.n2);
+          else if (row >= p.n1)
+            dst = p.y1 + (size_t)t * p.y1_stride + (row - p.n1);
+          else
+            dst = p.y + (size_t)t * p.y_stride + row;
+          *dst = p.epi == kGemmResidual ? __fadd_rn(*dst, v) : v;
         }
       }
 #pragma unroll
@@ -370,6 +382,34 @@ int int8_gemm(float *y, long y_stride, const float *x, long x_stride, const int8
   p.T = T;
   p.K = K;
   p.N = N;
+  if ((rc = digit_rows(static_cast<int8_t *>(dbuf), static_cast<float *>(qbuf), x, x_stride, T, T_pad, K, kGTok, st)))
+    return rc;
+  return gemm_launch<1>(p, st);
+}
+
+// int8_gemm with a fused epilogue: kGemmResidual adds the result to y (the
+// residual stream: add_inplace of the projection), kGemmSwiGLU turns each
+// interleaved (gate, up) row pair into silu(g) * u at y[t, row / 2].
+int int8_gemm_epi(float *y, long y_stride, const float *x, long x_stride, const int8_t *w, const float *scales, int T,
+                  int K, int N, int epi, cudaStream_t st) {
+  if (!gemm_shape_ok(x, x_stride, T, K, N) || (reinterpret_cast<uintptr_t>(w) & 15) || (epi == kGemmSwiGLU && N % 128))
+    return QASR_ERR_UNSUPPORTED;
+  const int NB = (T + kGTok - 1) / kGTok, T_pad = NB * kGTok;
+  void *dbuf = nullptr, *qbuf = nullptr;
+  int rc;
+  if ((rc = dev_scratch(kScratchDigits, (size_t)NB * kGRows * K, &dbuf))) return rc;
+  if ((rc = dev_scratch(kScratchDigitScale, (size_t)T_pad * 4, &qbuf))) return rc;
+  GemmParams p{};
+  if ((rc = int8_map(&p.tm_w, w, N, K, 128))) return rc;
+  if ((rc = int8_map(&p.tm_d, static_cast<int8_t *>(dbuf), (long)NB * kGRows, K, kGRows))) return rc;
+  p.dq = static_cast<float *>(qbuf);
+  p.scales = scales;
+  p.y = y;
+  p.y_stride = y_stride;
+  p.T = T;
+  p.K = K;
+  p.N = N;
+  p.epi = epi;
   if ((rc = digit_rows(static_cast<int8_t *>(dbuf), static_cast<float *>(qbuf), x, x_stride, T, T_pad, K, kGTok, st)))
     return rc;
   return gemm_launch<1>(p, st);

@@ -72,6 +72,20 @@ class Encoder:
                   C.byref(n))
         return out
 
+    def forward_batch(self, mels) -> list[torch.Tensor]:
+        """Several mels [128, frames_i] in one pass -> [tokens_i, output_dim] each."""
+        keep = []
+        n = len(mels)
+        ptrs = (C.c_void_p * n)(*[_ptr(m, keep) for m in mels])
+        frames = (C.c_int * n)(*[int(m.shape[1]) for m in mels])
+        outs = [torch.empty(self.tokens(f), self.cfg["output_dim"], dtype=torch.float32,
+                            device=f"cuda:{self.device}") for f in frames]
+        optr = (C.c_void_p * n)(*[o.data_ptr() for o in outs])
+        rows = (C.c_int * n)(*[o.shape[0] for o in outs])
+        got = (C.c_int * n)()
+        _lib.call("qasr_encoder_forward_batch", self._h, ptrs, frames, n, optr, rows, got)
+        return outs
+
     def close(self) -> None:
         if self._h:
             _lib.load().qasr_encoder_free(self._h)

@@ -35,3 +35,19 @@ def test_encoder_forward_matches_oracle(orc, frames):
     out2 = enc.forward(torch.from_numpy(mel).cuda()).cpu().numpy()
     assert np.array_equal(out, out2)
     enc.close()
+
+
+def test_encoder_forward_batch_equals_single(orc):
+    """qasr_encoder_forward_batch: ragged segments (a tail chunk, a sub-chunk
+    one, several windows) in one pass give each segment's single-forward rows
+    bit for bit; host and device mels mixed."""
+    w = synthetic.encoder_weights_np(SMALL, seed=7)
+    rng = np.random.default_rng(7)
+    mels = [rng.standard_normal((128, f)).astype(np.float32) for f in (250, 37, 1000, 100)]
+    enc = Encoder(SMALL, device=0)
+    enc.set_weights(w)
+    single = [enc.forward(m).cpu().numpy() for m in mels]
+    batch = enc.forward_batch([mels[0], torch.from_numpy(mels[1]).cuda(), mels[2], torch.from_numpy(mels[3]).cuda()])
+    for a, b in zip(single, batch):
+        assert np.array_equal(a, b.cpu().numpy())
+    enc.close()
