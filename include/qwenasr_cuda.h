@@ -318,6 +318,12 @@ int qasr_decoder_step(qasr_decoder *dec, const int32_t *tokens, const int32_t *p
  * are written to the slot's cache (KvCache with len = start_pos).  The next
  * decode step for the slot is at position start_pos + seq.  Synchronous. */
 int qasr_decoder_prefill(qasr_decoder *dec, int slot, const float *embeds, int seq, int start_pos);
+/* decoder_prefill_int8 for n sequences at once (distinct slots): their rows
+ * go through the layers together, each with its own positions, slot and
+ * causal attention; every slot's cache ends up as a prefill of it alone
+ * would leave it.  embeds[i] [seqs[i], hidden] host or device.  Synchronous. */
+int qasr_decoder_prefill_batch(qasr_decoder *dec, const int *slots, const float *const *embeds, const int *seqs,
+                               const int *start_pos, int n);
 
 /* Device pointer to the residual stream [seq, hidden] left by the last
  * prefill (the reference's bufs.pref_x); NULL before the first prefill. */

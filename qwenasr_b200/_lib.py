@@ -89,6 +89,7 @@ _SIGS = {
     "qasr_decoder_kv": (I, [P, I, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p)]),
     "qasr_decoder_step": (I, [P, P, P, I, P]),
     "qasr_decoder_prefill": (I, [P, I, P, I, I]),
+    "qasr_decoder_prefill_batch": (I, [P, P, P, P, P, I]),
     "qasr_decoder_prefill_hidden": (P, [P]),
     "qasr_decoder_step_device": (I, [P, P, P, I, P]),
     "qasr_decoder_stream": (P, [P]),

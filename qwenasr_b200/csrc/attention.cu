@@ -38,8 +38,15 @@ constexpr int kCaTasks = 16;  // (query, head) tasks per block: two per warp
 template <int EPL>  // elements per lane: head_dim / 32
 __global__ void __launch_bounds__(256, 2)
 causal_attention_kernel(float *__restrict__ out, const float *__restrict__ q, const float *__restrict__ k,
-                        const float *__restrict__ v, int seq_q, int seq_k, int n_heads, int n_kv_heads, float scale,
-                        int q_offset) {
+                        const float *__restrict__ v, CaSeg one, const CaSeg *__restrict__ many, int n_heads,
+                        int n_kv_heads, float scale) {
+  // segment blockIdx.z: its query rows, its keys / values and causal offset
+  const CaSeg sg = many ? many[blockIdx.z] : one;
+  const int seq_q = sg.seq_q, seq_k = sg.seq_k, q_offset = sg.q_offset;
+  q += sg.q_row0 * (long)n_heads * (EPL * 32);
+  out += sg.q_row0 * (long)n_heads * (EPL * 32);
+  k += sg.kv_off;
+  v += sg.kv_off;
   constexpr int HD = EPL * 32, KP = HD + 4;
   __shared__ __align__(16) float sK[kCaTile][KP];
   __shared__ __align__(16) float sV[kCaTile][HD];
@@ -48,6 +55,7 @@ causal_attention_kernel(float *__restrict__ out, const float *__restrict__ q, co
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = n_heads / n_kv_heads, QB = max(1, kCaTasks / G), n_tasks = QB * G;
   const int kvh = blockIdx.y, i0 = blockIdx.x * QB;
+  if (i0 >= seq_q) return;  // block-uniform: the grid covers the longest segment
   const long q_hidden = (long)n_heads * HD, kv_hidden = (long)n_kv_heads * HD;
   const int i_last = min(seq_q, i0 + QB) - 1;
   const int k_end = min(q_offset + i_last + 1, seq_k);  // keys any task of the block needs
@@ -487,6 +495,27 @@ attn_decode_kernel(const __grid_constant__ AttnDecodeParams p) {
     mbar_wait(&sm.bar[warp][k2 % kAttnStages], (unsigned)((k2 / kAttnStages) & 1));
 }
 
+// kernels::causal_attention for n segments in one launch (blockIdx.z):
+// segs (device) give each segment's query rows in q/out, its key/value
+// offset into k/v, its lengths and causal offset.
+int causal_attention_segments(float *out, const float *q, const float *k, const float *v, const CaSeg *segs, int n,
+                              int max_seq_q, int n_heads, int n_kv_heads, int head_dim, float scale,
+                              cudaStream_t st) {
+  const int G = n_heads / n_kv_heads;
+  if (G > kCaTasks || n_heads % n_kv_heads || (head_dim != 64 && head_dim != 128) || n <= 0 || n > 65535) {
+    set_error("causal attention: unsupported shape");
+    return QASR_ERR_UNSUPPORTED;
+  }
+  const int QB = std::max(1, kCaTasks / G);
+  const dim3 grid((unsigned)((max_seq_q + QB - 1) / QB), (unsigned)n_kv_heads, (unsigned)n);
+  const CaSeg none{};
+  if (head_dim == 128)
+    causal_attention_kernel<4><<<grid, 256, 0, st>>>(out, q, k, v, none, segs, n_heads, n_kv_heads, scale);
+  else
+    causal_attention_kernel<2><<<grid, 256, 0, st>>>(out, q, k, v, none, segs, n_heads, n_kv_heads, scale);
+  return launch_status("causal attention (segments)");
+}
+
 int attn_grid() {
   static int sms = 0;
   if (!sms) {
@@ -598,11 +627,10 @@ extern "C" int qasr_causal_attention(float *out, const float *q, const float *k,
   const int QB = std::max(1, kCaTasks / G);
   const dim3 grid((unsigned)((seq_q + QB - 1) / QB), (unsigned)n_kv_heads);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const CaSeg one{0, seq_q, seq_k, q_offset, 0};
   if (head_dim == 128)
-    causal_attention_kernel<4><<<grid, 256, 0, st>>>(out, q, k, v, seq_q, seq_k, n_heads, n_kv_heads, scale,
-                                                     q_offset);
+    causal_attention_kernel<4><<<grid, 256, 0, st>>>(out, q, k, v, one, nullptr, n_heads, n_kv_heads, scale);
   else
-    causal_attention_kernel<2><<<grid, 256, 0, st>>>(out, q, k, v, seq_q, seq_k, n_heads, n_kv_heads, scale,
-                                                     q_offset);
+    causal_attention_kernel<2><<<grid, 256, 0, st>>>(out, q, k, v, one, nullptr, n_heads, n_kv_heads, scale);
   return launch_status("qasr_causal_attention");
 }

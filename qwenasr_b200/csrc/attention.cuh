@@ -44,6 +44,17 @@ struct AttnDecodeParams {
   int *err;              // -QASR_ERR_TIMEOUT on a bounded-wait timeout
 };
 
+// One segment of a batched causal attention: query rows q_row0 .. q_row0 +
+// seq_q of q/out, keys/values at k/v + kv_off (floats), seq_k keys, the
+// first query at position q_offset.
+struct CaSeg {
+  long q_row0;
+  int seq_q, seq_k, q_offset;
+  long kv_off;
+};
+int causal_attention_segments(float *out, const float *q, const float *k, const float *v, const CaSeg *segs, int n,
+                              int max_seq_q, int n_heads, int n_kv_heads, int head_dim, float scale, cudaStream_t st);
+
 // 2D tensor map over a KV cache [rows, kv_dim] f32 with box [kAttnTile, 128].
 int attn_make_tensor_map(CUtensorMap *tm, const float *base, long rows, int kv_dim);
 int attn_decode_launch(const AttnDecodeParams &p, int group, cudaStream_t st, bool pdl);

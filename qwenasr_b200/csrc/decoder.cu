@@ -72,6 +72,8 @@ struct qasr_decoder {
   float *pf_x = nullptr, *pf_xn = nullptr, *pf_q = nullptr, *pf_k = nullptr, *pf_v = nullptr, *pf_attn = nullptr,
         *pf_proj = nullptr, *pf_gu = nullptr, *pf_h = nullptr;
   void *pf_block = nullptr;
+  unsigned char *pf_meta = nullptr;  // row positions / slots and attention segments of a prefill
+  size_t pf_meta_cap = 0;
   int32_t *emb_ids = nullptr;  // device ids of qasr_decoder_embed, grown on demand
   int emb_cap = 0;
   std::vector<cudaGraphExec_t> graphs;  // per M (index M), built lazily
@@ -601,32 +603,91 @@ extern "C" int qasr_decoder_profile_step(qasr_decoder *d, const int32_t *tokens,
 // slot's cache.  The projections run as tensor-core GEMMs over all rows
 // (the reference: seq_len matvecs), the norms, RoPE, attention and SwiGLU
 // are the kernel-level entries, in the reference's order.
-extern "C" int qasr_decoder_prefill(qasr_decoder *d, int slot, const float *embeds, int seq, int start_pos) {
-  if (!d || !embeds || slot < 0 || slot >= (d ? d->cfg.max_batch : 0) || seq <= 0 || start_pos < 0) {
+namespace qasr {
+// apply_rope_neox with a position per row: x[r, head, :] rotated by the
+// table row pos[r] (the arithmetic of apply_rope_kernel).
+__global__ void rope_rows_kernel(float *__restrict__ x, const float *__restrict__ cos_tab,
+                                 const float *__restrict__ sin_tab, const int32_t *__restrict__ pos, int rows,
+                                 int n_heads, int head_dim) {
+  const int half = head_dim / 2;
+  const long t = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= (long)rows * n_heads * half) return;
+  const int dd = (int)(t % half);
+  const long sh = t / half;
+  const int r = (int)(sh / n_heads);
+  float *vec = x + sh * head_dim;
+  const float *c = cos_tab + (size_t)pos[r] * head_dim, *sn = sin_tab + (size_t)pos[r] * head_dim;
+  const float x1 = vec[dd], x2 = vec[half + dd];
+  vec[dd] = __fadd_rn(__fmul_rn(x1, c[dd]), __fmul_rn(-x2, sn[dd]));
+  vec[half + dd] = __fadd_rn(__fmul_rn(x2, c[half + dd]), __fmul_rn(x1, sn[half + dd]));
+}
+
+// KV append with a destination per row: row r of k/v goes to cache row
+// (layer * max_seq + pos[r]) of sequence slot[r].
+__global__ void kv_append_rows_kernel(float *__restrict__ k_cache, float *__restrict__ v_cache,
+                                      const float *__restrict__ k_new, const float *__restrict__ v_new,
+                                      const int32_t *__restrict__ slot, const int32_t *__restrict__ pos, int rows,
+                                      int layer, int max_seq, int kv_dim, long seq_stride) {
+  const long t = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  const int per_row = kv_dim / 4;
+  if (t >= (long)rows * per_row) return;
+  const int r = (int)(t / per_row), c = (int)(t % per_row);
+  const size_t dst = (size_t)slot[r] * seq_stride + ((size_t)layer * max_seq + pos[r]) * kv_dim;
+  reinterpret_cast<float4 *>(k_cache + dst)[c] = reinterpret_cast<const float4 *>(k_new + (size_t)r * kv_dim)[c];
+  reinterpret_cast<float4 *>(v_cache + dst)[c] = reinterpret_cast<const float4 *>(v_new + (size_t)r * kv_dim)[c];
+}
+}  // namespace qasr
+
+// decoder_prefill_int8 (decoder.rs:751-842) for n sequences at once: their
+// prompt rows are concatenated, every per-row operation (norms, the q|k|v,
+// o, gate/up and down GEMMs with their fused epilogues, SwiGLU) runs once over
+// all rows, RoPE and the KV append take each row's position and slot, and
+// one causal-attention launch covers every sequence (grid z).  Sequence i's
+// cache ends up exactly as a prefill of it alone would leave it.
+extern "C" int qasr_decoder_prefill_batch(qasr_decoder *d, const int *slots, const float *const *embeds,
+                                          const int *seqs, const int *start_pos, int n) {
+  if (!d || !slots || !embeds || !seqs || !start_pos || n <= 0 || n > d->cfg.max_batch) {
     set_error("qasr_decoder_prefill: invalid arguments");
     return QASR_ERR_INVALID;
   }
   const qasr_decoder_config &c = d->cfg;
-  if (start_pos + seq > c.max_seq) {
-    set_error("qasr_decoder_prefill: positions %d..%d outside the cache (max_seq %d)", start_pos,
-              start_pos + seq - 1, c.max_seq);
-    return QASR_ERR_INVALID;
+  int R = 0, max_seq_q = 0;
+  for (int i = 0; i < n; ++i) {
+    if (!embeds[i] || slots[i] < 0 || slots[i] >= c.max_batch || seqs[i] <= 0 || start_pos[i] < 0) {
+      set_error("qasr_decoder_prefill: invalid arguments (sequence %d)", i);
+      return QASR_ERR_INVALID;
+    }
+    if (start_pos[i] + seqs[i] > c.max_seq) {
+      set_error("qasr_decoder_prefill: positions %d..%d outside the cache (max_seq %d)", start_pos[i],
+                start_pos[i] + seqs[i] - 1, c.max_seq);
+      return QASR_ERR_INVALID;
+    }
+    for (int j = 0; j < i; ++j)
+      if (slots[j] == slots[i]) {
+        set_error("qasr_decoder_prefill: slot %d given twice", slots[i]);
+        return QASR_ERR_INVALID;
+      }
+    R += seqs[i];
+    max_seq_q = std::max(max_seq_q, seqs[i]);
   }
   cudaSetDevice(d->device);
   cudaStream_t st = d->stream;
   const int H = c.hidden, I = c.inter, hd = c.head_dim;
   const int q_dim = c.n_heads * hd, kv_dim = c.n_kv_heads * hd;
   int rc = QASR_OK;
-  if (seq > d->pf_cap) {
-    const int cap = std::max(seq, 64);
-    const size_t per_row = (size_t)2 * H + 2 * q_dim + 2 * kv_dim + H + 2 * I + I;
+  // buffers: activations for R rows, then per-row positions / slots and the segment table
+  const size_t per_row = (size_t)2 * H + 2 * q_dim + 2 * kv_dim + H + 2 * I + I;
+  const size_t meta_bytes = (size_t)2 * R * 4 + (size_t)n * sizeof(CaSeg) + 256;
+  if (R > d->pf_cap || meta_bytes > d->pf_meta_cap) {
+    const int cap = std::max(R, 64);
     void *blk = nullptr;
     if ((rc = cuda_status(cudaStreamSynchronize(st), "qasr_decoder_prefill"))) return rc;
-    if ((rc = cuda_status(cudaMalloc(&blk, per_row * cap * 4), "qasr_decoder_prefill: buffers"))) return rc;
+    const size_t meta = std::max(meta_bytes, (size_t)2 * cap * 4 + (size_t)c.max_batch * sizeof(CaSeg) + 256);
+    if ((rc = cuda_status(cudaMalloc(&blk, per_row * cap * 4 + meta), "qasr_decoder_prefill: buffers"))) return rc;
     if (d->pf_block) cudaFree(d->pf_block);
     d->pf_block = blk;
     float *f = static_cast<float *>(blk);
-    auto take = [&](size_t n) { float *r = f; f += n * cap; return r; };
+    auto take = [&](size_t k) { float *r = f; f += k * cap; return r; };
     d->pf_x = take(H);
     d->pf_xn = take(H);
     d->pf_q = take(q_dim);
@@ -636,71 +697,104 @@ extern "C" int qasr_decoder_prefill(qasr_decoder *d, int slot, const float *embe
     d->pf_proj = take(H);
     d->pf_gu = take(2 * I);
     d->pf_h = take(I);
+    d->pf_meta = reinterpret_cast<unsigned char *>(f);
     d->pf_cap = cap;
+    d->pf_meta_cap = meta;
   }
-  if ((rc = cuda_status(cudaMemcpyAsync(d->pf_x, embeds, (size_t)seq * H * 4, cudaMemcpyDefault, st), "prefill embeds")))
-    return rc;
-  const float *cos_r = d->rope_cos + (size_t)start_pos * hd, *sin_r = d->rope_sin + (size_t)start_pos * hd;
-  float *kc = d->k_cache + (size_t)slot * d->seq_stride(), *vc = d->v_cache + (size_t)slot * d->seq_stride();
+  // host tables -> device: row positions and slots, then the attention segments
+  std::vector<int32_t> row_pos(R), row_slot(R);
+  std::vector<CaSeg> segs(n);
+  const long seq_stride = d->seq_stride();
+  for (int i = 0, r0 = 0; i < n; r0 += seqs[i], ++i) {
+    for (int j = 0; j < seqs[i]; ++j) {
+      row_pos[r0 + j] = start_pos[i] + j;
+      row_slot[r0 + j] = slots[i];
+    }
+    segs[i] = CaSeg{r0, seqs[i], start_pos[i] + seqs[i], start_pos[i], (long)slots[i] * seq_stride};
+  }
+  int32_t *d_pos = reinterpret_cast<int32_t *>(d->pf_meta), *d_slot = d_pos + R;
+  CaSeg *d_segs = reinterpret_cast<CaSeg *>(d->pf_meta + ((2 * (size_t)R * 4 + 15) & ~(size_t)15));
+  rc = cuda_status(cudaMemcpyAsync(d_pos, row_pos.data(), (size_t)R * 4, cudaMemcpyHostToDevice, st), "prefill meta");
+  if (!rc)
+    rc = cuda_status(cudaMemcpyAsync(d_slot, row_slot.data(), (size_t)R * 4, cudaMemcpyHostToDevice, st),
+                     "prefill meta");
+  if (!rc)
+    rc = cuda_status(cudaMemcpyAsync(d_segs, segs.data(), (size_t)n * sizeof(CaSeg), cudaMemcpyHostToDevice, st),
+                     "prefill meta");
+  for (int i = 0, r0 = 0; i < n && !rc; r0 += seqs[i], ++i)
+    rc = cuda_status(cudaMemcpyAsync(d->pf_x + (size_t)r0 * H, embeds[i], (size_t)seqs[i] * H * 4, cudaMemcpyDefault,
+                                     st),
+                     "prefill embeds");
+  if (rc) return rc;
   const float scale = 1.0f / sqrtf((float)hd);
-  const int total = start_pos + seq;
+  const long nq = (long)R * c.n_heads * (hd / 2), nk = (long)R * c.n_kv_heads * (hd / 2);
+  const long nkv = (long)R * (kv_dim / 4);
   for (int l = 0; l < c.n_layers && !rc; ++l) {
     const LayerDev &L = d->layers[l];
     const size_t kv_rows = (size_t)kv_dim * H;
-    if ((rc = qasr_rms_norm(d->pf_xn, d->pf_x, L.in_norm, seq, H, c.eps, st))) break;
+    if ((rc = qasr_rms_norm(d->pf_xn, d->pf_x, L.in_norm, R, H, c.eps, st))) break;
     // q, k, v: the three row ranges of the fused q|k|v matrix, one GEMM when
-    // the tensor-core path takes it (seq > 8), else three matvec calls
-    rc = seq > 8 ? int8_gemm_split3(d->pf_q, q_dim, d->pf_k, kv_dim, q_dim, d->pf_v, kv_dim, q_dim + kv_dim, d->pf_xn,
-                                    H, L.wqkv, L.sqkv, seq, H, q_dim + 2 * kv_dim, st)
-                 : QASR_ERR_UNSUPPORTED;
+    // the tensor-core path takes it (more than 8 rows), else three matvec calls
+    rc = R > 8 ? int8_gemm_split3(d->pf_q, q_dim, d->pf_k, kv_dim, q_dim, d->pf_v, kv_dim, q_dim + kv_dim, d->pf_xn, H,
+                                  L.wqkv, L.sqkv, R, H, q_dim + 2 * kv_dim, st)
+               : QASR_ERR_UNSUPPORTED;
     if (rc == QASR_ERR_UNSUPPORTED) {
-      if ((rc = qasr_linear_nobias_int8(d->pf_q, d->pf_xn, L.wqkv, L.sqkv, seq, H, q_dim, st))) break;
-      if ((rc = qasr_linear_nobias_int8(d->pf_k, d->pf_xn, L.wqkv + (size_t)q_dim * H, L.sqkv + q_dim, seq, H,
-                                        kv_dim, st)))
+      if ((rc = qasr_linear_nobias_int8(d->pf_q, d->pf_xn, L.wqkv, L.sqkv, R, H, q_dim, st))) break;
+      if ((rc = qasr_linear_nobias_int8(d->pf_k, d->pf_xn, L.wqkv + (size_t)q_dim * H, L.sqkv + q_dim, R, H, kv_dim,
+                                        st)))
         break;
       if ((rc = qasr_linear_nobias_int8(d->pf_v, d->pf_xn, L.wqkv + (size_t)q_dim * H + kv_rows,
-                                        L.sqkv + q_dim + kv_dim, seq, H, kv_dim, st)))
+                                        L.sqkv + q_dim + kv_dim, R, H, kv_dim, st)))
         break;
     } else if (rc) {
       break;
     }
-    if ((rc = qasr_rms_norm_per_head(d->pf_q, L.q_norm, seq, c.n_heads, hd, c.eps, st))) break;
-    if ((rc = qasr_rms_norm_per_head(d->pf_k, L.k_norm, seq, c.n_kv_heads, hd, c.eps, st))) break;
-    if ((rc = qasr_apply_rope_neox(d->pf_q, cos_r, sin_r, seq, c.n_heads, hd, st))) break;
-    if ((rc = qasr_apply_rope_neox(d->pf_k, cos_r, sin_r, seq, c.n_kv_heads, hd, st))) break;
-    if ((rc = qasr_kv_append(kc, vc, d->pf_k, d->pf_v, l, c.max_seq, kv_dim, start_pos, seq, st))) break;
+    if ((rc = qasr_rms_norm_per_head(d->pf_q, L.q_norm, R, c.n_heads, hd, c.eps, st))) break;
+    if ((rc = qasr_rms_norm_per_head(d->pf_k, L.k_norm, R, c.n_kv_heads, hd, c.eps, st))) break;
+    rope_rows_kernel<<<(int)((nq + 255) / 256), 256, 0, st>>>(d->pf_q, d->rope_cos, d->rope_sin, d_pos, R, c.n_heads,
+                                                              hd);
+    rope_rows_kernel<<<(int)((nk + 255) / 256), 256, 0, st>>>(d->pf_k, d->rope_cos, d->rope_sin, d_pos, R,
+                                                              c.n_kv_heads, hd);
+    kv_append_rows_kernel<<<(int)((nkv + 255) / 256), 256, 0, st>>>(d->k_cache, d->v_cache, d->pf_k, d->pf_v, d_slot,
+                                                                    d_pos, R, l, c.max_seq, kv_dim, seq_stride);
+    if ((rc = launch_status("qasr_decoder_prefill: rope / kv append"))) break;
+    // causal attention of every sequence over its cache (layer l)
     const size_t lay = (size_t)l * c.max_seq * kv_dim;
-    if ((rc = qasr_causal_attention(d->pf_attn, d->pf_q, kc + lay, vc + lay, seq, total, c.n_heads, c.n_kv_heads, hd,
-                                    scale, start_pos, st)))
+    if ((rc = causal_attention_segments(d->pf_attn, d->pf_q, d->k_cache + lay, d->v_cache + lay, d_segs, n, max_seq_q,
+                                        c.n_heads, c.n_kv_heads, hd, scale, st)))
       break;
     // o-proj + residual, gate/up + SwiGLU, down + residual: fused GEMM
-    // epilogues when the tensor-core GEMM takes the shape (seq > 8)
-    const bool fused = seq > 8;
-    rc = fused ? int8_gemm_epi(d->pf_x, H, d->pf_attn, q_dim, L.wo, L.so, seq, q_dim, H, 1, st) : QASR_ERR_UNSUPPORTED;
+    // epilogues when the tensor-core GEMM takes the shape (more than 8 rows)
+    const bool fused = R > 8;
+    rc = fused ? int8_gemm_epi(d->pf_x, H, d->pf_attn, q_dim, L.wo, L.so, R, q_dim, H, 1, st) : QASR_ERR_UNSUPPORTED;
     if (rc == QASR_ERR_UNSUPPORTED) {
-      if ((rc = qasr_linear_nobias_int8(d->pf_proj, d->pf_attn, L.wo, L.so, seq, q_dim, H, st))) break;
-      if ((rc = qasr_add_inplace(d->pf_x, d->pf_proj, (int64_t)seq * H, st))) break;
+      if ((rc = qasr_linear_nobias_int8(d->pf_proj, d->pf_attn, L.wo, L.so, R, q_dim, H, st))) break;
+      if ((rc = qasr_add_inplace(d->pf_x, d->pf_proj, (int64_t)R * H, st))) break;
     } else if (rc) {
       break;
     }
-    if ((rc = qasr_rms_norm(d->pf_xn, d->pf_x, L.post_norm, seq, H, c.eps, st))) break;
-    rc = fused ? int8_gemm_epi(d->pf_h, I, d->pf_xn, H, L.gate_up, L.sgu, seq, H, 2 * I, 2, st) : QASR_ERR_UNSUPPORTED;
+    if ((rc = qasr_rms_norm(d->pf_xn, d->pf_x, L.post_norm, R, H, c.eps, st))) break;
+    rc = fused ? int8_gemm_epi(d->pf_h, I, d->pf_xn, H, L.gate_up, L.sgu, R, H, 2 * I, 2, st) : QASR_ERR_UNSUPPORTED;
     if (rc == QASR_ERR_UNSUPPORTED) {
-      if ((rc = qasr_linear_nobias_int8(d->pf_gu, d->pf_xn, L.gate_up, L.sgu, seq, H, 2 * I, st))) break;
-      if ((rc = qasr_swiglu_multiply(d->pf_h, d->pf_gu, seq, I, st))) break;
+      if ((rc = qasr_linear_nobias_int8(d->pf_gu, d->pf_xn, L.gate_up, L.sgu, R, H, 2 * I, st))) break;
+      if ((rc = qasr_swiglu_multiply(d->pf_h, d->pf_gu, R, I, st))) break;
     } else if (rc) {
       break;
     }
-    rc = fused ? int8_gemm_epi(d->pf_x, H, d->pf_h, I, L.down, L.sdown, seq, I, H, 1, st) : QASR_ERR_UNSUPPORTED;
+    rc = fused ? int8_gemm_epi(d->pf_x, H, d->pf_h, I, L.down, L.sdown, R, I, H, 1, st) : QASR_ERR_UNSUPPORTED;
     if (rc == QASR_ERR_UNSUPPORTED) {
-      if ((rc = qasr_linear_nobias_int8(d->pf_proj, d->pf_h, L.down, L.sdown, seq, I, H, st))) break;
-      if ((rc = qasr_add_inplace(d->pf_x, d->pf_proj, (int64_t)seq * H, st))) break;
+      if ((rc = qasr_linear_nobias_int8(d->pf_proj, d->pf_h, L.down, L.sdown, R, I, H, st))) break;
+      if ((rc = qasr_add_inplace(d->pf_x, d->pf_proj, (int64_t)R * H, st))) break;
     } else if (rc) {
       break;
     }
   }
   if (!rc) rc = cuda_status(cudaStreamSynchronize(st), "qasr_decoder_prefill");
   return rc;
+}
+
+extern "C" int qasr_decoder_prefill(qasr_decoder *d, int slot, const float *embeds, int seq, int start_pos) {
+  return qasr_decoder_prefill_batch(d, &slot, &embeds, &seq, &start_pos, 1);
 }
 
 extern "C" const qasr_decoder_config *qasr_decoder_get_config(const qasr_decoder *d) { return d ? &d->cfg : nullptr; }

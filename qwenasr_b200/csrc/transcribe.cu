@@ -170,7 +170,8 @@ extern "C" int qasr_transcribe_batch(qasr_decoder *dec, qasr_encoder *enc, const
   if ((rc = dev_scratch(kScratchAudio, (size_t)max_samples * 4, &audio))) return rc;
   if ((rc = dev_scratch(kScratchMelOut, mel_off[M] * 4, &mel))) return rc;
   if ((rc = dev_scratch(kScratchEncOut, (size_t)tok_off[M] * H * 4, &enc_out))) return rc;
-  if ((rc = dev_scratch(kScratchPrompt, (size_t)max_prompt * H * 4, &prompt))) return rc;
+  // prompt rows of every segment, side by side (one batched prefill)
+  if ((rc = dev_scratch(kScratchPrompt, (size_t)M * max_prompt * H * 4, &prompt))) return rc;
   std::vector<const float *> mels(M);
   std::vector<float *> outs(M);
   for (int i = 0; i < M; ++i) {
@@ -188,8 +189,10 @@ extern "C" int qasr_transcribe_batch(qasr_decoder *dec, qasr_encoder *enc, const
     return rc;
   cudaSetDevice(dev);
   std::vector<int32_t> tok0(M), pos0(M), pre;
-  float *embeds = static_cast<float *>(prompt);
+  std::vector<int> slots(M), lens(M), starts(M, 0);
+  std::vector<const float *> rows_of(M);
   for (int i = 0; i < M; ++i) {
+    float *embeds = static_cast<float *>(prompt) + (size_t)i * max_prompt * H;
     const int T = got[i];
     const float *rows_i = outs[i];
     // prompt embeddings (transcribe.rs:98-170): token rows around the audio rows
@@ -209,10 +212,13 @@ extern "C" int qasr_transcribe_batch(qasr_decoder *dec, qasr_encoder *enc, const
       return rc;
     // prefill all but the last row; the first decode step feeds the last
     // prompt token at position total - 1 (transcribe.rs:172-190)
-    if ((rc = qasr_decoder_prefill(dec, i, embeds, total - 1, 0))) return rc;
+    slots[i] = i;
+    lens[i] = total - 1;
+    rows_of[i] = embeds;
     tok0[i] = post.back();
     pos0[i] = total - 1;
   }
+  if ((rc = qasr_decoder_prefill_batch(dec, slots.data(), rows_of.data(), lens.data(), starts.data(), M))) return rc;
   // greedy decode (transcribe.rs:192-222)
   return greedy_decode(dec, M, tok0.data(), pos0.data(), max_new, stop_at_eos, kCheckEvery, ids, ids_stride, n_ids);
 }

@@ -115,6 +115,17 @@ class Decoder:
             ptr, seq = e.ctypes.data, e.shape[0]
         _lib.call("qasr_decoder_prefill", self._h, int(slot), C.c_void_p(ptr), int(seq), int(start_pos))
 
+    def prefill_batch(self, slots, embeds, start_pos=None) -> None:
+        """decoder_prefill_int8 of several sequences at once (distinct slots)."""
+        keep = []
+        n = len(slots)
+        sl = (C.c_int * n)(*[int(x) for x in slots])
+        embeds = [e.float() if isinstance(e, torch.Tensor) else np.asarray(e, np.float32) for e in embeds]
+        ptrs = (C.c_void_p * n)(*[_host_or_dev_ptr(e, keep) for e in embeds])
+        lens = (C.c_int * n)(*[int(e.shape[0]) for e in embeds])
+        st = (C.c_int * n)(*([int(x) for x in start_pos] if start_pos is not None else [0] * n))
+        _lib.call("qasr_decoder_prefill_batch", self._h, sl, ptrs, lens, st, n)
+
     def prefill_hidden(self, seq: int) -> torch.Tensor:
         """Residual stream [seq, hidden] left by the last prefill (a copy)."""
         ptr = _lib.load().qasr_decoder_prefill_hidden(self._h)

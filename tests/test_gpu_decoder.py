@@ -236,3 +236,45 @@ def test_decode_step_1p7b_shapes(orc, M):
         toks = nxt.astype(np.int32)
         pos = pos + 1
     dec.close()
+
+
+def test_prefill_batch_equals_single(orc):
+    """qasr_decoder_prefill_batch: ragged prompts (one of a single row, one
+    after 10 history rows) prefilled together leave each slot's K/V exactly as
+    one prefill per slot does, and the next greedy step agrees with the oracle."""
+    orc.set_threads(8)
+    w, od, a = build_pair(orc, SMALL, seed=33, max_seq=256, max_batch=4)
+    b = Decoder(SMALL, device=0, max_batch=4, max_seq=256)
+    for i, lw in enumerate(w["layers"]):
+        b.set_layer(i, lw)
+    b.set_globals(w["embed"], w["norm"], w["lm_head"], w["lm_head_s"])
+    rng = np.random.default_rng(33)
+    lens, starts, slots = [37, 1, 120, 12], [0, 0, 10, 0], [2, 0, 3, 1]
+    rows = [w["embed"][rng.integers(0, SMALL["vocab"], n)] for n in lens]
+    hist = w["embed"][rng.integers(0, SMALL["vocab"], 10)]
+    for dec in (a, b):
+        dec.prefill(3, hist, 0)  # slot 3's first 10 rows
+    a.prefill_batch(slots, rows, starts)
+    for s, r, p0 in zip(slots, rows, starts):
+        b.prefill(s, r, p0)
+    for s in slots:
+        ka, va = a.kv(s)
+        kb, vb = b.kv(s)
+        assert torch.equal(ka, kb) and torch.equal(va, vb)
+    toks = rng.integers(0, SMALL["vocab"], 4).astype(np.int32)
+    pos = np.array([lens[slots.index(s)] + starts[slots.index(s)] for s in range(4)], np.int32)
+    assert np.array_equal(a.step(toks, pos), b.step(toks, pos))
+    # slot 3 (10 history rows + 120) against the oracle: row 3 of a fresh 4-row step
+    kh, vh = od.new_kv(256)
+    od.prefill(kh, vh, 0, np.concatenate([hist, rows[2]]))
+    tok, _, _ = od.forward(kh, vh, 130, w["embed"][toks[3]])
+    c = Decoder(SMALL, device=0, max_batch=4, max_seq=256)
+    for i, lw in enumerate(w["layers"]):
+        c.set_layer(i, lw)
+    c.set_globals(w["embed"], w["norm"], w["lm_head"], w["lm_head_s"])
+    c.prefill(3, hist, 0)
+    c.prefill_batch(slots, rows, starts)
+    assert int(c.step(toks, pos)[3]) == tok
+    c.close()
+    a.close()
+    b.close()
