@@ -19,11 +19,12 @@ Prints one JSON line on rank 0.
     python bench.py --workload e2e [--gpus N]
     python bench.py --workload segments [--gpus N]
 
-run the whole transcription path through qasr_transcribe_batch: 30 s of
+run the whole transcription path through qasr_transcribe_lanes: 30 s of
 synthetic audio per segment -> log-mel -> encoder -> prompt -> prefill ->
 greedy decode (e2e: Qwen3-ASR-0.6B shapes, one segment per GPU, 256 tokens;
 segments: 1.7B shapes, 64 segments split evenly over the GPUs and decoded 8
-at a time, 128 tokens each).  Metric: audio seconds per second (whole job).
+at a time, 128 tokens each, over --lanes engine lanes per GPU that overlap
+one another).  Metric: audio seconds per second (whole job).
 
     python bench.py --workload gemm [--steps K] [--warmup W]
 
@@ -73,6 +74,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="bounded CPU-baseline sample length")
     ap.add_argument("--seed", type=int, default=1234)
+    ap.add_argument("--lanes", type=int, default=None,
+                    help="engine lanes (decoder + encoder pairs) per GPU for the transcription workloads "
+                         "(default 1 for e2e, 2 for segments)")
     ap.add_argument("--workload", choices=("decode", "gemm", "encoder", "e2e", "segments"), default="decode")
     ap.add_argument("--model", choices=("0.6b", "1.7b"), default="0.6b",
                     help="decoder shapes of the decode workload (0.6b = BASELINE configs[2])")
@@ -562,10 +566,10 @@ def run_encoder(a):
 
 # ----------------------------------------------------------- transcription --
 TRANSCRIBE = {
-    "e2e": dict(dec="DEC_0_6B", enc="ENC_0_6B", segments_per_rank=1, seconds=30.0, new=256, batch=1,
+    "e2e": dict(dec="DEC_0_6B", enc="ENC_0_6B", segments_per_rank=1, seconds=30.0, new=256, batch=1, lanes=1,
                 scaling="weak", desc="BASELINE configs[3]: one 30 s segment per GPU, Qwen3-ASR-0.6B shapes "
                                      "(INT8 decoder, f32 encoder), 256 greedy tokens"),
-    "segments": dict(dec="DEC_1_7B", enc="ENC_1_7B", segments=64, seconds=30.0, new=128, batch=8,
+    "segments": dict(dec="DEC_1_7B", enc="ENC_1_7B", segments=64, seconds=30.0, new=128, batch=8, lanes=2,
                      scaling="strong", desc="BASELINE configs[4]: 64 segments of 30 s split evenly over the GPUs, "
                                             "Qwen3-ASR-1.7B shapes (INT8 decoder, f32 encoder), 128 greedy tokens "
                                             "each, 8 segments per decode batch"),
@@ -629,7 +633,7 @@ def run_transcribe(a):
     from qwenasr_b200.decoder import Decoder
     from qwenasr_b200.encoder import Encoder
     from qwenasr_b200.segments import segment_range
-    from qwenasr_b200.transcribe import prompt_len, transcribe_ids
+    from qwenasr_b200.transcribe import prompt_len, transcribe_lanes
 
     spec = TRANSCRIBE[a.workload]
     dcfg = dict(getattr(synthetic, spec["dec"]), n_layers=a.layers)
@@ -638,10 +642,11 @@ def run_transcribe(a):
     mine = list(segment_range(n_seg, rank, world))
     new, batch, secs = spec["new"], spec["batch"], spec["seconds"]
     dev = torch.device(f"cuda:{local}")
-    enc = Encoder(ecfg, device=local)
-    enc_tokens = enc.tokens(K.mel_frames(int(secs * 16000)))
+    n_lanes = a.lanes or spec["lanes"]
+    encs = [Encoder(ecfg, device=local) for _ in range(n_lanes)]
+    enc_tokens = encs[0].tokens(K.mel_frames(int(secs * 16000)))
     max_seq = ((prompt_len(enc_tokens) - 1 + new + 63) // 64) * 64
-    dec = Decoder(dcfg, device=local, max_batch=batch, max_seq=max_seq)
+    decs = [Decoder(dcfg, device=local, max_batch=batch, max_seq=max_seq) for _ in range(n_lanes)]
     gen = torch.Generator(device=dev)
     gen.manual_seed(a.seed + 17 * rank)
 
@@ -651,24 +656,31 @@ def run_transcribe(a):
         K.quantize_f32_to_int8(w, w.shape[0], w.shape[1], q, s)
         return q, s
 
+    # every lane holds the same weights (its own copy)
     for i in range(dcfg["n_layers"]):
-        dec.set_layer(i, synthetic.layer_weights_gpu(dcfg, gen, dev, qz))
+        lw = synthetic.layer_weights_gpu(dcfg, gen, dev, qz)
+        for d in decs:
+            d.set_layer(i, lw)
+        del lw
     emb = torch.randn(dcfg["vocab"], dcfg["hidden"], generator=gen, device=dev) * 0.02
     lm, lms = qz(emb)
     norm = 1.0 + 0.02 * torch.randn(dcfg["hidden"], generator=gen, device=dev)
-    dec.set_globals(emb, norm, lm, lms)
+    for d in decs:
+        d.set_globals(emb, norm, lm, lms)
     del lm, lms, emb
-    enc.set_weights(synthetic.encoder_weights_gpu(ecfg, gen, dev))
+    we = synthetic.encoder_weights_gpu(ecfg, gen, dev)
+    for e in encs:
+        e.set_weights(we)
+    del we
+    lanes = list(zip(decs, encs))
+    dec = decs[0]
     torch.cuda.synchronize()
     audio_h = [synthetic.synthetic_audio(secs, a.seed + s) for s in mine]
     audio_d = [torch.from_numpy(x).to(dev) for x in audio_h]
     torch.cuda.synchronize()
 
-    def one_pass(src):
-        out = []
-        for b in range(0, len(src), batch):
-            out += transcribe_ids(dec, enc, src[b:b + batch], new)
-        return out
+    def one_pass(src, n_new=new):
+        return transcribe_lanes(lanes, src, n_new)
 
     def barrier():
         if dist:
@@ -698,13 +710,13 @@ def run_transcribe(a):
     barrier()
     # phase split on this rank: everything but the decode loop (one token)
     t0 = time.perf_counter()
-    for b in range(0, len(audio_d), batch):
-        transcribe_ids(dec, enc, audio_d[b:b + batch], 1)
+    one_pass(audio_d, 1)
     front_ms = (time.perf_counter() - t0) * 1e3
     t = torch.tensor([ms, e2e_ms], device=dev)
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, e2e_ms = float(t[0]), float(t[1])
+    batch = min(batch, -(-len(mine) // n_lanes))  # as qasr_transcribe_lanes sizes its batches
     n_batches = (len(mine) + batch - 1) // batch
     dec_step_ms = max(ms - front_ms, 1e-6) / max(1, n_batches * (new - 1))
     mid_pos = np.full(min(batch, len(mine)), prompt_len(enc_tokens) - 1 + new // 2, np.int32)
@@ -726,7 +738,9 @@ def run_transcribe(a):
             "config": {"workload": spec["desc"], "segments": n_seg, "seconds_per_segment": secs,
                        "tokens_per_segment": new, "decode_batch": batch, "decoder_layers": dcfg["n_layers"],
                        "hidden": dcfg["hidden"], "encoder_layers": ecfg["n_layers"],
-                       "parallelism": f"segments split over {world} GPU(s), no collective",
+                       "parallelism": f"segments split over {world} GPU(s), no collective; {n_lanes} engine "
+                                      f"lane(s) per GPU",
+                       "lanes_per_gpu": n_lanes,
                        "l2": "decode steps read weights + KV above L2 size; no flush"},
             "decode_tokens_per_s": n_seg * new / (ms / 1e3),
             "phase_ms_rank0": {"audio_encoder_prefill_first_token": front_ms,
@@ -734,7 +748,9 @@ def run_transcribe(a):
             "e2e": {"value": audio_s / (e2e_ms / 1e3), "unit": "audio-s/s",
                     "h2d_bytes_per_step": int(sum(x.nbytes for x in audio_h)) * world,
                     "d2h_bytes_per_step": n_seg * new * 4},
-            "roofline": {"bound": "hbm", "kernel": "decode step (whole graph), estimated from the phase split",
+            "roofline": {"bound": "hbm", "kernel": "decode step (whole graph), estimated from the phase split: "
+                                                   "decode-step bytes of all batches over the decode phase "
+                                                   "(lanes overlap, so this is the aggregate rate)",
                          "achieved": step_bytes / (dec_step_ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
                          "frac": step_bytes / (dec_step_ms / 1e3) / 1e9 / peak, "traffic": None,
                          "peak_kind": peak_kind, "bytes_per_step": step_bytes, "ms_per_decode_step": dec_step_ms},
@@ -746,8 +762,9 @@ def run_transcribe(a):
         }
     if dist:
         dist.barrier()
-    dec.close()
-    enc.close()
+    for d, e in lanes:
+        d.close()
+        e.close()
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         line["cpu_baseline"] = cpu_transcribe_baseline(dcfg, ecfg, secs, new, a.seed, a.cpu_seconds)
     if rank == 0:

@@ -502,6 +502,23 @@ int qasr_transcribe_batch(qasr_decoder *dec, qasr_encoder *enc, const float *con
                           int n_segments, const int32_t *prompt_tokens, int n_prompt, const int32_t *force_tokens,
                           int n_force, int max_new, int stop_at_eos, int32_t *ids, int ids_stride, int *n_ids);
 
+/* The segment loop of transcribe_audio (transcribe.rs:354-420, past-text
+ * conditioning off) over n_segments independent segments, spread over
+ * n_lanes engine lanes (decs[l], encs[l]: one decoder + encoder pair per
+ * lane, no engine in two lanes, each pair on one device).  Segments go in
+ * batches of the smallest lane's max_batch (fewer when that leaves a lane
+ * idle: ceil(n_segments / n_lanes)) to whichever lane is free; lane 0
+ * runs on the calling thread, the others on threads of their own, so lanes on
+ * one GPU overlap their work and lanes on several GPUs run side by side.
+ * Outputs as qasr_transcribe_batch, indexed by segment; the ids of a segment
+ * do not depend on the lane or batch it ran in.  Synchronous; on an error the
+ * first failing lane's message is reported and the other lanes stop after
+ * their current batch. */
+int qasr_transcribe_lanes(qasr_decoder *const *decs, qasr_encoder *const *encs, int n_lanes,
+                          const float *const *samples, const int *n_samples, int n_segments,
+                          const int32_t *prompt_tokens, int n_prompt, const int32_t *force_tokens, int n_force,
+                          int max_new, int stop_at_eos, int32_t *ids, int ids_stride, int *n_ids);
+
 /* ======================================================================
  * Streaming transcription (transcribe.rs:445-1495), token ids out
  * ==================================================================== */

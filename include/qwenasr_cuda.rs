@@ -150,7 +150,7 @@ extern "C" {
     pub fn qasr_decoder_kv(dec: *mut QasrDecoder, slot: c_int, k_cache: *mut *mut f32, v_cache: *mut *mut f32) -> c_int;
     pub fn qasr_decoder_step(dec: *mut QasrDecoder, tokens: *const i32, positions: *const i32, M: c_int, next_tokens: *mut i32) -> c_int;
     pub fn qasr_decoder_prefill(dec: *mut QasrDecoder, slot: c_int, embeds: *const f32, seq: c_int, start_pos: c_int) -> c_int;
-    pub fn qasr_decoder_prefill_batch(dec: *mut QasrDecoder, slots: *const c_int, embeds: *mut *const f32, seqs: *const c_int, start_pos: *const c_int, n: c_int) -> c_int;
+    pub fn qasr_decoder_prefill_batch(dec: *mut QasrDecoder, slots: *const c_int, embeds: *const *const f32, seqs: *const c_int, start_pos: *const c_int, n: c_int) -> c_int;
     pub fn qasr_decoder_prefill_hidden(dec: *mut QasrDecoder) -> *const f32;
     pub fn qasr_decoder_step_device(dec: *mut QasrDecoder, tokens: *const i32, positions: *const i32, M: c_int, next_tokens: *mut i32) -> c_int;
     pub fn qasr_decoder_stream(dec: *mut QasrDecoder) -> *mut c_void;
@@ -173,7 +173,7 @@ extern "C" {
     pub fn qasr_encoder_get_config(enc: *const QasrEncoder) -> *const QasrEncoderConfig;
     pub fn qasr_encoder_device(enc: *const QasrEncoder) -> c_int;
     pub fn qasr_encoder_forward(enc: *mut QasrEncoder, mel: *const f32, mel_frames: c_int, out: *mut f32, out_rows: c_int, n_tokens: *mut c_int) -> c_int;
-    pub fn qasr_encoder_forward_batch(enc: *mut QasrEncoder, mels: *mut *const f32, mel_frames: *const c_int, n: c_int, outs: *mut *mut f32, out_rows: *const c_int, n_tokens: *mut c_int) -> c_int;
+    pub fn qasr_encoder_forward_batch(enc: *mut QasrEncoder, mels: *const *const f32, mel_frames: *const c_int, n: c_int, outs: *const *mut f32, out_rows: *const c_int, n_tokens: *mut c_int) -> c_int;
     pub fn qasr_qint8_open(path: *const c_char) -> *mut QasrQint8;
     pub fn qasr_qint8_close(f: *mut QasrQint8);
     pub fn qasr_qint8_version(f: *const QasrQint8) -> c_int;
@@ -184,7 +184,8 @@ extern "C" {
     pub fn qasr_qint8_load_decoder(f: *const QasrQint8, dec: *mut QasrDecoder) -> c_int;
     pub fn qasr_qint8_load_encoder(f: *const QasrQint8, enc: *mut QasrEncoder) -> c_int;
     pub fn qasr_transcribe_prompt_len(n_audio_tokens: c_int, n_prompt: c_int, n_force: c_int) -> c_int;
-    pub fn qasr_transcribe_batch(dec: *mut QasrDecoder, enc: *mut QasrEncoder, samples: *mut *const f32, n_samples: *const c_int, n_segments: c_int, prompt_tokens: *const i32, n_prompt: c_int, force_tokens: *const i32, n_force: c_int, max_new: c_int, stop_at_eos: c_int, ids: *mut i32, ids_stride: c_int, n_ids: *mut c_int) -> c_int;
+    pub fn qasr_transcribe_batch(dec: *mut QasrDecoder, enc: *mut QasrEncoder, samples: *const *const f32, n_samples: *const c_int, n_segments: c_int, prompt_tokens: *const i32, n_prompt: c_int, force_tokens: *const i32, n_force: c_int, max_new: c_int, stop_at_eos: c_int, ids: *mut i32, ids_stride: c_int, n_ids: *mut c_int) -> c_int;
+    pub fn qasr_transcribe_lanes(decs: *const *mut QasrDecoder, encs: *const *mut QasrEncoder, n_lanes: c_int, samples: *const *const f32, n_samples: *const c_int, n_segments: c_int, prompt_tokens: *const i32, n_prompt: c_int, force_tokens: *const i32, n_force: c_int, max_new: c_int, stop_at_eos: c_int, ids: *mut i32, ids_stride: c_int, n_ids: *mut c_int) -> c_int;
     pub fn qasr_stream_default_config(cfg: *mut QasrStreamConfig);
     pub fn qasr_stream_create(dec: *mut QasrDecoder, enc: *mut QasrEncoder, cfg: *const QasrStreamConfig) -> *mut QasrStream;
     pub fn qasr_stream_free(s: *mut QasrStream);

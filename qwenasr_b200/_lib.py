@@ -166,6 +166,7 @@ _SIGS.update({
     "qasr_encoder_device": (I, [P]),
     "qasr_transcribe_prompt_len": (I, [I, I, I]),
     "qasr_transcribe_batch": (I, [P, P, P, P, I, P, I, P, I, I, I, P, I, P]),
+    "qasr_transcribe_lanes": (I, [P, P, I, P, P, I, P, I, P, I, I, I, P, I, P]),
 })
 
 KERNEL_CLASSES = ("embed", "norm", "qkv", "qkv_post", "attn", "oproj", "gateup", "down", "lmhead")

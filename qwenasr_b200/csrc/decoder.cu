@@ -49,6 +49,7 @@ struct qasr_decoder {
   qasr_decoder_config cfg;
   int device = 0;
   cudaStream_t stream = nullptr;
+  qasr::ScratchArena *arena = nullptr;  // this engine's kernel-level scratch
   std::vector<qasr::LayerDev> layers;
   void *embed = nullptr;
   float *embed_s = nullptr, *norm = nullptr, *lm_s = nullptr;
@@ -140,6 +141,7 @@ extern "C" void qasr_decoder_free(qasr_decoder *d) {
   if (d->emb_ids) cudaFree(d->emb_ids);
   if (d->h_tok) cudaFreeHost(d->h_tok);
   if (d->stream) cudaStreamDestroy(d->stream);
+  arena_free(d->arena);
   delete d;
 }
 
@@ -162,6 +164,10 @@ extern "C" qasr_decoder *qasr_decoder_create(const qasr_decoder_config *cfg, int
   d->cfg = *cfg;
   d->device = device;
   int rc = cuda_status(cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking), "qasr_decoder_create");
+  if (!rc && !(d->arena = arena_create(device))) {
+    set_error("qasr_decoder_create: scratch arena");
+    rc = QASR_ERR_ALLOC;
+  }
   const int H = cfg->hidden, I = cfg->inter, L = cfg->n_layers, hd = cfg->head_dim;
   const int q_dim = cfg->n_heads * hd, kv_dim = cfg->n_kv_heads * hd, qkv_rows = q_dim + 2 * kv_dim;
   const int B = cfg->max_batch;
@@ -247,6 +253,7 @@ extern "C" int qasr_decoder_set_layer(qasr_decoder *d, int layer, const qasr_dec
     return QASR_ERR_INVALID;
   }
   cudaSetDevice(d->device);
+  qasr::ArenaScope arena_scope(d->arena);
   const qasr_decoder_config &c = d->cfg;
   const size_t H = c.hidden, I = c.inter, q_dim = (size_t)c.n_heads * c.head_dim, kv = (size_t)c.n_kv_heads * c.head_dim;
   LayerDev &ld = d->layers[layer];
@@ -300,6 +307,7 @@ extern "C" int qasr_decoder_set_gate_up(qasr_decoder *d, int layer, const int8_t
     return QASR_ERR_INVALID;
   }
   cudaSetDevice(d->device);
+  qasr::ArenaScope arena_scope(d->arena);
   const qasr_decoder_config &c = d->cfg;
   const size_t H = c.hidden, I = c.inter;
   LayerDev &ld = d->layers[layer];
@@ -330,6 +338,7 @@ extern "C" int qasr_decoder_set_globals(qasr_decoder *d, const void *embed, cons
     return QASR_ERR_INVALID;
   }
   cudaSetDevice(d->device);
+  qasr::ArenaScope arena_scope(d->arena);
   const qasr_decoder_config &c = d->cfg;
   const size_t VH = (size_t)c.vocab * c.hidden;
   int rc = QASR_OK;
@@ -380,6 +389,7 @@ extern "C" int qasr_decoder_keep_logits(qasr_decoder *d, int enable) {
   if (enable && !d->logits) {
     int rc = 0;
     cudaSetDevice(d->device);
+    qasr::ArenaScope arena_scope(d->arena);
     d->logits = (float *)dalloc(d, (size_t)d->cfg.max_batch * d->cfg.vocab * 4, &rc);
     if (rc) return rc;
   }
@@ -507,6 +517,7 @@ extern "C" int qasr_decoder_step_device(qasr_decoder *d, const int32_t *tokens, 
     return QASR_ERR_INVALID;
   }
   cudaSetDevice(d->device);
+  qasr::ArenaScope arena_scope(d->arena);
   int rc = cuda_status(cudaMemcpyAsync(d->tok, tokens, M * 4, cudaMemcpyDeviceToDevice, d->stream), "tokens");
   if (!rc) rc = cuda_status(cudaMemcpyAsync(d->pos, positions, M * 4, cudaMemcpyDeviceToDevice, d->stream), "pos");
   if (!rc) rc = run_graph(d, M);
@@ -531,6 +542,7 @@ extern "C" int qasr_decoder_step(qasr_decoder *d, const int32_t *tokens, const i
     }
   }
   cudaSetDevice(d->device);
+  qasr::ArenaScope arena_scope(d->arena);
   std::memcpy(d->h_tok, tokens, M * 4);
   std::memcpy(d->h_pos, positions, M * 4);
   int rc = cuda_status(cudaMemcpyAsync(d->tok, d->h_tok, M * 4, cudaMemcpyHostToDevice, d->stream), "tokens H2D");
@@ -571,6 +583,7 @@ extern "C" int qasr_decoder_profile_step(qasr_decoder *d, const int32_t *tokens,
     return QASR_ERR_INVALID;
   }
   cudaSetDevice(d->device);
+  qasr::ArenaScope arena_scope(d->arena);
   std::memcpy(d->h_tok, tokens, M * 4);
   std::memcpy(d->h_pos, positions, M * 4);
   int rc = cuda_status(cudaMemcpyAsync(d->tok, d->h_tok, M * 4, cudaMemcpyHostToDevice, d->stream), "tokens H2D");
@@ -671,6 +684,7 @@ extern "C" int qasr_decoder_prefill_batch(qasr_decoder *d, const int *slots, con
     max_seq_q = std::max(max_seq_q, seqs[i]);
   }
   cudaSetDevice(d->device);
+  qasr::ArenaScope arena_scope(d->arena);
   cudaStream_t st = d->stream;
   const int H = c.hidden, I = c.inter, hd = c.head_dim;
   const int q_dim = c.n_heads * hd, kv_dim = c.n_kv_heads * hd;
@@ -800,6 +814,8 @@ extern "C" int qasr_decoder_prefill(qasr_decoder *d, int slot, const float *embe
 extern "C" const qasr_decoder_config *qasr_decoder_get_config(const qasr_decoder *d) { return d ? &d->cfg : nullptr; }
 extern "C" int qasr_decoder_device(const qasr_decoder *d) { return d ? d->device : -1; }
 
+qasr::ScratchArena *qasr::decoder_arena(qasr_decoder *d) { return d ? d->arena : nullptr; }
+
 // QwenCtx::tok_embed_to_f32 (context.rs:115-124) for n host ids: rows of the
 // engine's embedding table (dequantised when INT8) into out [n, hidden].
 extern "C" int qasr_decoder_embed(qasr_decoder *d, const int32_t *ids, int n, float *out) {
@@ -818,6 +834,7 @@ extern "C" int qasr_decoder_embed(qasr_decoder *d, const int32_t *ids, int n, fl
       return QASR_ERR_INVALID;
     }
   cudaSetDevice(d->device);
+  qasr::ArenaScope arena_scope(d->arena);
   cudaStream_t st = d->stream;
   int rc = QASR_OK;
   if (n > d->emb_cap) {

@@ -22,6 +22,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "matvec.cuh"
 #include "umma.cuh"
 
 namespace qasr {
@@ -151,6 +152,7 @@ struct qasr_encoder {
   qasr_encoder_config cfg;
   int device = 0;
   cudaStream_t stream = nullptr;
+  qasr::ScratchArena *arena = nullptr;  // this engine's kernel-level scratch
   std::vector<qasr::EncLayerDev> layers;
   float *conv_w[3] = {nullptr, nullptr, nullptr}, *conv_b[3] = {nullptr, nullptr, nullptr};
   qasr::EncMat conv_out, proj1, proj2;
@@ -303,6 +305,7 @@ extern "C" void qasr_encoder_free(qasr_encoder *e) {
   if (e->win) cudaFree(e->win);
   if (e->mel_dev) cudaFree(e->mel_dev);
   if (e->stream) cudaStreamDestroy(e->stream);
+  arena_free(e->arena);
   delete e;
 }
 
@@ -330,6 +333,10 @@ extern "C" qasr_encoder *qasr_encoder_create(const qasr_encoder_config *cfg, int
   e->cfg = *cfg;
   e->device = device;
   int rc = cuda_status(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking), "qasr_encoder_create");
+  if (!rc && !(e->arena = arena_create(device))) {
+    set_error("qasr_encoder_create: scratch arena");
+    rc = QASR_ERR_ALLOC;
+  }
   const int D = cfg->d_model, F = cfg->ffn_dim, O = cfg->output_dim, CH = kConvHidden;
   const int h3 = chunk_tokens(kMelBins);  // frequency rows after the stem: 16
   e->layers.resize(cfg->n_layers);
@@ -379,6 +386,7 @@ extern "C" int qasr_encoder_set_conv(qasr_encoder *e, const float *conv1_w, cons
     return QASR_ERR_INVALID;
   }
   cudaSetDevice(e->device);
+  qasr::ArenaScope arena_scope(e->arena);
   const int CH = kConvHidden, h3 = chunk_tokens(kMelBins);
   const float *w[3] = {conv1_w, conv2_w, conv3_w}, *b[3] = {conv1_b, conv2_b, conv3_b};
   const int cin[3] = {1, CH, CH};
@@ -403,6 +411,7 @@ extern "C" int qasr_encoder_set_conv_int8(qasr_encoder *e, const float *conv1_w,
     return QASR_ERR_INVALID;
   }
   cudaSetDevice(e->device);
+  qasr::ArenaScope arena_scope(e->arena);
   const int CH = kConvHidden;
   const float *w[3] = {conv1_w, conv2_w, conv3_w}, *b[3] = {conv1_b, conv2_b, conv3_b};
   const int cin[3] = {1, CH, CH};
@@ -423,6 +432,7 @@ extern "C" int qasr_encoder_set_layer(qasr_encoder *e, int layer, const qasr_enc
     return QASR_ERR_INVALID;
   }
   cudaSetDevice(e->device);
+  qasr::ArenaScope arena_scope(e->arena);
   const size_t D = e->cfg.d_model, F = e->cfg.ffn_dim;
   EncLayerDev &L = e->layers[layer];
   int rc = QASR_OK;
@@ -454,6 +464,7 @@ extern "C" int qasr_encoder_set_layer_int8(qasr_encoder *e, int layer, const qas
     return QASR_ERR_INVALID;
   }
   cudaSetDevice(e->device);
+  qasr::ArenaScope arena_scope(e->arena);
   const size_t D = e->cfg.d_model, F = e->cfg.ffn_dim;
   EncLayerDev &L = e->layers[layer];
   int rc = QASR_OK;
@@ -486,6 +497,7 @@ extern "C" int qasr_encoder_set_post(qasr_encoder *e, const float *ln_post_w, co
     return QASR_ERR_INVALID;
   }
   cudaSetDevice(e->device);
+  qasr::ArenaScope arena_scope(e->arena);
   const size_t D = e->cfg.d_model, O = e->cfg.output_dim;
   int rc = enc_copy(e, e->ln_post_w, ln_post_w, D, "ln_post_w");
   if (!rc) rc = enc_copy(e, e->ln_post_b, ln_post_b, D, "ln_post_b");
@@ -505,6 +517,7 @@ extern "C" int qasr_encoder_set_post_int8(qasr_encoder *e, const float *ln_post_
     return QASR_ERR_INVALID;
   }
   cudaSetDevice(e->device);
+  qasr::ArenaScope arena_scope(e->arena);
   const size_t D = e->cfg.d_model, O = e->cfg.output_dim;
   int rc = enc_copy(e, e->ln_post_w, ln_post_w, D, "ln_post_w");
   if (!rc) rc = enc_copy(e, e->ln_post_b, ln_post_b, D, "ln_post_b");
@@ -518,6 +531,8 @@ extern "C" int qasr_encoder_set_post_int8(qasr_encoder *e, const float *ln_post_
 
 extern "C" const qasr_encoder_config *qasr_encoder_get_config(const qasr_encoder *e) { return e ? &e->cfg : nullptr; }
 extern "C" int qasr_encoder_device(const qasr_encoder *e) { return e ? e->device : -1; }
+
+qasr::ScratchArena *qasr::encoder_arena(qasr_encoder *e) { return e ? e->arena : nullptr; }
 
 extern "C" int qasr_encoder_tokens(const qasr_encoder *e, int mel_frames) {
   if (!e || mel_frames <= 0) return 0;
@@ -535,6 +550,7 @@ extern "C" int qasr_encoder_tokens(const qasr_encoder *e, int mel_frames) {
 static int encoder_run(qasr_encoder *e, int n, const float *const *mels, const int *frames, float *const *outs,
                        const int *out_rows, int *n_tokens) {
   cudaSetDevice(e->device);
+  qasr::ArenaScope arena_scope(e->arena);
   for (EncMat *m : enc_mats(e))
     if (!m->ready()) {
       set_error("qasr_encoder_forward: weights not set (call the qasr_encoder_set_* functions first)");

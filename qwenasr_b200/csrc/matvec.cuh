@@ -2,6 +2,9 @@
 #pragma once
 #include "common.cuh"
 
+struct qasr_decoder;
+struct qasr_encoder;
+
 namespace qasr {
 
 constexpr int kMvWarps = 4;  // warps per CTA
@@ -95,5 +98,21 @@ constexpr int kScratchPartial = 0, kScratchCounter = 1, kScratchDigits = 2, kScr
               kScratchMelMax = 8, kScratchAudio = 9, kScratchMelOut = 10, kScratchEncOut = 11,
               kScratchPrompt = 12, kScratchDecode = 13, kScratchSlots = 14;
 int dev_scratch(int slot, size_t bytes, void **out);
+
+// Engine-owned scratch: while an ArenaScope is alive on a thread, dev_scratch
+// calls on the arena's device use the arena's buffers.
+struct ScratchArena;
+ScratchArena *arena_create(int device);
+void arena_free(ScratchArena *a);
+struct ArenaScope {
+  explicit ArenaScope(ScratchArena *a);
+  ~ArenaScope();
+  ArenaScope(const ArenaScope &) = delete;
+  ArenaScope &operator=(const ArenaScope &) = delete;
+  ScratchArena *prev;
+};
+// The engines' own arenas.
+ScratchArena *decoder_arena(qasr_decoder *d);
+ScratchArena *encoder_arena(qasr_encoder *e);
 
 }  // namespace qasr

@@ -3,6 +3,8 @@
 #include <cstdarg>
 #include <cstdio>
 #include <mutex>
+#include <new>
+#include <vector>
 
 #include "common.cuh"
 #include "matvec.cuh"
@@ -66,10 +68,75 @@ struct DevScratch {
 };
 static DevScratch g_dev_scratch[64][kScratchSlots];
 
+// Scratch owned by one engine.  While an ArenaScope of the engine is active
+// on the calling thread, dev_scratch hands out the engine's buffers instead
+// of the per-device ones, so engines driven from different host threads
+// (the transcription lanes) never share a buffer.  A buffer that grows is
+// retired, not freed: kernels still in flight on the engine's streams may
+// read it, and freeing would synchronise the whole device under another
+// thread's graph capture.  Retired buffers go with the arena.
+struct ScratchArena {
+  int device = 0;
+  DevScratch slot[kScratchSlots];
+  std::vector<void *> retired;
+};
+
+static thread_local ScratchArena *t_arena = nullptr;
+
+ScratchArena *arena_create(int device) {
+  ScratchArena *a = new (std::nothrow) ScratchArena;
+  if (a) a->device = device;
+  return a;
+}
+
+void arena_free(ScratchArena *a) {
+  if (!a) return;
+  for (auto &s : a->slot)
+    if (s.buf) cudaFree(s.buf);
+  for (void *p : a->retired) cudaFree(p);
+  delete a;
+}
+
+ArenaScope::ArenaScope(ScratchArena *a) : prev(t_arena) {
+  if (a) t_arena = a;
+}
+ArenaScope::~ArenaScope() { t_arena = prev; }
+
+static int scratch_fill(void *buf, size_t bytes) {
+  // zero on the legacy stream and wait for it: the engines' streams are
+  // non-blocking and would not order behind it
+  if (cudaMemset(buf, 0, bytes) != cudaSuccess || cudaStreamSynchronize(cudaStreamLegacy) != cudaSuccess) {
+    set_error("kernel-level scratch: zero fill failed");
+    return QASR_ERR_CUDA;
+  }
+  return QASR_OK;
+}
+
 int dev_scratch(int slot, size_t bytes, void **out) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || slot < 0 || slot >= kScratchSlots) return QASR_ERR_INVALID;
+  if (ScratchArena *a = t_arena; a && a->device == dev) {
+    DevScratch &s = a->slot[slot];
+    if (s.cap < bytes) {
+      size_t want = bytes < 4096 ? 4096 : bytes;
+      if (want < s.cap + s.cap / 2) want = s.cap + s.cap / 2;
+      void *buf = nullptr;
+      if (cudaMalloc(&buf, want) != cudaSuccess) {
+        set_error("engine scratch: cudaMalloc(%zu) failed", want);
+        return QASR_ERR_ALLOC;
+      }
+      if (int rc = scratch_fill(buf, want)) {
+        cudaFree(buf);
+        return rc;
+      }
+      if (s.buf) a->retired.push_back(s.buf);
+      s.buf = buf;
+      s.cap = want;
+    }
+    *out = s.buf;
+    return QASR_OK;
+  }
   std::lock_guard<std::mutex> lk(g_scratch_mu);
   DevScratch &s = g_dev_scratch[dev][slot];
   if (s.cap < bytes) {
@@ -84,10 +151,7 @@ int dev_scratch(int slot, size_t bytes, void **out) {
       set_error("kernel-level scratch: cudaMalloc(%zu) failed", want);
       return QASR_ERR_ALLOC;
     }
-    if (cudaMemset(s.buf, 0, want) != cudaSuccess) {
-      set_error("kernel-level scratch: cudaMemset failed");
-      return QASR_ERR_CUDA;
-    }
+    if (int rc = scratch_fill(s.buf, want)) return rc;
     s.cap = want;
   }
   *out = s.buf;

@@ -503,6 +503,7 @@ extern "C" int qasr_stream_push(qasr_stream *s, const float *samples, int64_t n_
   }
   *n_emitted = 0;
   if (cudaSetDevice(s->device) != cudaSuccess) return QASR_ERR_CUDA;
+  ArenaScope arena_scope(decoder_arena(s->dec));
   std::vector<int32_t> delta;
   int rc = QASR_OK;
   const long avail = n_samples > s->cursor ? n_samples - s->cursor : 0;

@@ -14,7 +14,11 @@
 // are enqueued back to back with no host round trip; the host looks at the
 // ids only every kCheckEvery steps, when stopping at end-of-text.
 #include <algorithm>
+#include <atomic>
 #include <cstring>
+#include <mutex>
+#include <string>
+#include <thread>
 #include <vector>
 
 #include "common.cuh"
@@ -137,6 +141,7 @@ extern "C" int qasr_transcribe_batch(qasr_decoder *dec, qasr_encoder *enc, const
     return QASR_ERR_INVALID;
   }
   if (int rc = cuda_status(cudaSetDevice(dev), "qasr_transcribe_batch")) return rc;
+  ArenaScope arena_scope(decoder_arena(dec));
   const int H = dc->hidden, M = n_segments;
   int max_samples = 0, max_tokens = 0;
   for (int i = 0; i < M; ++i) {
@@ -223,3 +228,80 @@ extern "C" int qasr_transcribe_batch(qasr_decoder *dec, qasr_encoder *enc, const
   return greedy_decode(dec, M, tok0.data(), pos0.data(), max_new, stop_at_eos, kCheckEvery, ids, ids_stride, n_ids);
 }
 
+
+// Independent segments over several engine lanes: transcribe_audio's
+// segment loop (transcribe.rs:354-420, past_text_conditioning off, so no
+// segment depends on another) with the segments taken in batches by
+// whichever lane is free.  Each lane is one decoder + encoder pair driven by
+// its own host thread (the first by the caller's): the engines have their
+// own streams, graphs and scratch, so one lane's encoder and prefill overlap
+// another lane's latency-bound decode steps on the same GPU, and lanes on
+// different GPUs run side by side.  A batch is the smallest lane's
+// max_batch, or fewer so that every lane gets one; per-segment results equal qasr_transcribe_batch's, as every
+// kernel on the path is row-independent.
+extern "C" int qasr_transcribe_lanes(qasr_decoder *const *decs, qasr_encoder *const *encs, int n_lanes,
+                                     const float *const *samples, const int *n_samples, int n_segments,
+                                     const int32_t *prompt_tokens, int n_prompt, const int32_t *force_tokens,
+                                     int n_force, int max_new, int stop_at_eos, int32_t *ids, int ids_stride,
+                                     int *n_ids) {
+  if (!decs || !encs || n_lanes <= 0 || n_lanes > 64 || n_segments < 0 || (n_segments && (!samples || !n_samples)) ||
+      !ids || !n_ids || max_new <= 0 || ids_stride < max_new) {
+    set_error("qasr_transcribe_lanes: invalid arguments (%d lanes, %d segments)", n_lanes, n_segments);
+    return QASR_ERR_INVALID;
+  }
+  int batch = 1 << 30;
+  for (int l = 0; l < n_lanes; ++l) {
+    const qasr_decoder_config *dc = qasr_decoder_get_config(decs[l]);
+    if (!dc || !qasr_encoder_get_config(encs[l])) {
+      set_error("qasr_transcribe_lanes: lane %d has no decoder or encoder", l);
+      return QASR_ERR_INVALID;
+    }
+    for (int j = 0; j < l; ++j)
+      if (decs[j] == decs[l] || encs[j] == encs[l]) {
+        set_error("qasr_transcribe_lanes: lanes %d and %d share an engine", j, l);
+        return QASR_ERR_INVALID;
+      }
+    batch = std::min(batch, dc->max_batch);
+  }
+  if (n_segments == 0) return QASR_OK;
+  batch = std::min(batch, (n_segments + n_lanes - 1) / n_lanes);  // every lane gets work
+  const int n_batches = (n_segments + batch - 1) / batch;
+  std::atomic<int> next{0};
+  std::atomic<bool> failed{false};
+  std::mutex mu;
+  int first_rc = QASR_OK;
+  std::string first_msg;
+  auto lane = [&](int l) {
+    for (;;) {
+      if (failed.load()) return;
+      const int b = next.fetch_add(1);
+      if (b >= n_batches) return;
+      const int lo = b * batch, cnt = std::min(batch, n_segments - lo);
+      const int rc = qasr_transcribe_batch(decs[l], encs[l], samples + lo, n_samples + lo, cnt, prompt_tokens,
+                                           n_prompt, force_tokens, n_force, max_new, stop_at_eos,
+                                           ids + (size_t)lo * ids_stride, ids_stride, n_ids + lo);
+      if (rc) {
+        std::lock_guard<std::mutex> lk(mu);
+        if (!first_rc) {
+          first_rc = rc;
+          first_msg = std::string("lane ") + std::to_string(l) + ": " + qasr_last_error();
+        }
+        failed.store(true);
+        return;
+      }
+    }
+  };
+  std::vector<std::thread> threads;
+  const int use = std::min(n_lanes, n_batches);
+  for (int l = 1; l < use; ++l) {
+    try {
+      threads.emplace_back(lane, l);
+    } catch (...) {
+      break;  // fewer threads: the running lanes take the remaining batches
+    }
+  }
+  lane(0);
+  for (auto &t : threads) t.join();
+  if (first_rc) set_error("qasr_transcribe_lanes: %s", first_msg.c_str());
+  return first_rc;
+}

@@ -34,6 +34,7 @@
 //    coalesced over rows.
 // Every wait is bounded; a timeout sets *err, stops the roles, drains the
 // copies and MMAs in flight and frees TMEM.
+#include <atomic>
 #include <cuda.h>
 
 #include <algorithm>
@@ -338,16 +339,16 @@ static int digit_rows(int8_t *D, float *dq, const float *x, long x_stride, int r
 template <int PLANES>
 static int gemm_launch(GemmParams &p, cudaStream_t st) {
   if (!p.y1) p.n1 = p.n2 = 0x7fffffff;  // no split
-  static int attr_mask = 0;
+  static std::atomic<unsigned> attr_mask{0};  // engines on several host threads reach here
   int dev = 0;
   cudaGetDevice(&dev);
   const size_t smem = 1024 + (size_t)kGStages * (kGATile + kGBTile) + sizeof(GSmem);
-  if (dev < 31 && !(attr_mask & (1 << dev))) {
+  if (dev < 31 && !(attr_mask.load() & (1u << dev))) {
     int rc = cuda_status(cudaFuncSetAttribute(gemm_kernel<PLANES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               (int)smem),
                          "tensor-core GEMM: shared memory opt-in");
     if (rc) return rc;
-    attr_mask |= 1 << dev;
+    attr_mask.fetch_or(1u << dev);
   }
   const long tiles = (long)((p.N + 127) / 128) * ((p.T + kGTok - 1) / kGTok);
   const int grid = (int)std::min<long>(gemm_sms(), tiles);

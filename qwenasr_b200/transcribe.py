@@ -1,10 +1,12 @@
-"""Python face of qasr_transcribe_batch: transcribe_segment
-(crates/qwen-asr/src/transcribe.rs:67-244) on one GPU, token ids out.
+"""Python face of qasr_transcribe_batch / qasr_transcribe_lanes:
+transcribe_segment (crates/qwen-asr/src/transcribe.rs:67-244) and the
+segmented transcribe_audio (transcribe.rs:294-420), token ids out.
 
 Audio -> log-mel -> encoder -> prompt embeddings (the reference's special
 tokens, transcribe.rs:11-13) -> prefill -> greedy decode, for up to
-`dec.max_batch` independent segments decoded together.  Text decoding stays
-with the caller's tokenizer, as in the reference's host.
+`dec.max_batch` independent segments decoded together; any number of
+segments over one or more engine lanes.  Text decoding stays with the
+caller's tokenizer, as in the reference's host.
 """
 from __future__ import annotations
 
@@ -33,6 +35,28 @@ def _ids_arg(ids):
     return C.c_void_p(a.ctypes.data), len(a), a
 
 
+def _segment_args(segments):
+    """ctypes arrays of the segments' sample pointers and lengths, and the
+    arrays that keep them alive."""
+    n = len(segments)
+    keep = []
+    ptrs = (C.c_void_p * n)()
+    lens = (C.c_int * n)()
+    for i, s in enumerate(segments):
+        if isinstance(s, torch.Tensor):
+            s = s.detach().float().contiguous()
+            ptrs[i] = s.data_ptr()
+            lens[i] = s.numel()
+        else:
+            s = np.ascontiguousarray(s, dtype=np.float32)
+            ptrs[i] = s.ctypes.data
+            lens[i] = s.size
+        keep.append(s)
+    if any(isinstance(s, torch.Tensor) for s in keep):
+        torch.cuda.synchronize()  # the engines read them on their own streams
+    return ptrs, lens, keep
+
+
 def transcribe_ids(dec, enc, segments: Sequence, max_new: int, stop_at_eos: bool = False, prompt_tokens=None,
                    force_tokens=None) -> list[list[int]]:
     """Greedy token ids of each segment (16 kHz f32 samples: numpy arrays or
@@ -41,26 +65,36 @@ def transcribe_ids(dec, enc, segments: Sequence, max_new: int, stop_at_eos: bool
     n = len(segments)
     if n == 0:
         return []
-    keep = []
-    ptrs = (C.c_void_p * n)()
-    lens = (C.c_int * n)()
-    for i, s in enumerate(segments):
-        if isinstance(s, torch.Tensor):
-            s = s.detach().float().contiguous()
-            ptrs[i] = s.data_ptr()
-        else:
-            s = np.ascontiguousarray(s, dtype=np.float32)
-            ptrs[i] = s.ctypes.data
-        keep.append(s)
-        lens[i] = s.numel() if isinstance(s, torch.Tensor) else s.size
-    if any(isinstance(s, torch.Tensor) for s in keep):
-        torch.cuda.synchronize()  # the engine reads them on its own stream
+    ptrs, lens, keep = _segment_args(segments)
     pp, npr, pa = _ids_arg(prompt_tokens)
     fp, nfr, fa = _ids_arg(force_tokens)
     ids = np.zeros((n, max_new), np.int32)
     counts = (C.c_int * n)()
     _lib.call("qasr_transcribe_batch", dec._h, enc._h, ptrs, lens, n, pp, npr, fp, nfr, int(max_new), 1 if stop_at_eos else 0,
               C.c_void_p(ids.ctypes.data), int(max_new), counts)
+    del pa, fa, keep
+    return [ids[i, :counts[i]].tolist() for i in range(n)]
+
+
+def transcribe_lanes(lanes: Sequence, segments: Sequence, max_new: int, stop_at_eos: bool = False,
+                     prompt_tokens=None, force_tokens=None) -> list[list[int]]:
+    """transcribe_ids over any number of independent segments, spread over
+    engine lanes: lanes = [(dec, enc), ...], one decoder + encoder pair each
+    (qasr_transcribe_lanes).  Lanes on one GPU overlap one another's work;
+    the ids of a segment do not depend on the lane that ran it."""
+    n = len(segments)
+    if n == 0:
+        return []
+    L = len(lanes)
+    decs = (C.c_void_p * L)(*[d._h for d, _ in lanes])
+    encs = (C.c_void_p * L)(*[e._h for _, e in lanes])
+    ptrs, lens, keep = _segment_args(segments)
+    pp, npr, pa = _ids_arg(prompt_tokens)
+    fp, nfr, fa = _ids_arg(force_tokens)
+    ids = np.zeros((n, max_new), np.int32)
+    counts = (C.c_int * n)()
+    _lib.call("qasr_transcribe_lanes", decs, encs, L, ptrs, lens, n, pp, npr, fp, nfr, int(max_new),
+              1 if stop_at_eos else 0, C.c_void_p(ids.ctypes.data), int(max_new), counts)
     del pa, fa, keep
     return [ids[i, :counts[i]].tolist() for i in range(n)]
 
@@ -79,11 +113,12 @@ def plan_segments(samples, segment_sec: float, search_sec: float = 3.0) -> list[
 
 
 def transcribe_audio(dec, enc, samples, max_new: int, segment_sec: float = 0.0, search_sec: float = 3.0,
-                     stop_at_eos: bool = True, prompt_tokens=None, force_tokens=None) -> list[list[int]]:
+                     stop_at_eos: bool = True, prompt_tokens=None, force_tokens=None, lanes=None) -> list[list[int]]:
     """transcribe_audio (transcribe.rs:294-420) without past-text
     conditioning: the planned segments (each shorter than 0.5 s zero-padded
     to 0.5 s, as the reference does) transcribed independently, up to
-    dec.max_batch at a time; the ids of every segment in order."""
+    dec.max_batch at a time, or over `lanes` ([(dec, enc), ...], dec and enc
+    then unused) when given; the ids of every segment in order."""
     s = np.ascontiguousarray(samples, dtype=np.float32)
     segs = []
     for a, b in plan_segments(s, segment_sec, search_sec):
@@ -91,7 +126,4 @@ def transcribe_audio(dec, enc, samples, max_new: int, segment_sec: float = 0.0, 
         if seg.size < 8000:
             seg = np.concatenate([seg, np.zeros(8000 - seg.size, np.float32)])
         segs.append(seg)
-    out = []
-    for i in range(0, len(segs), dec.max_batch):
-        out += transcribe_ids(dec, enc, segs[i:i + dec.max_batch], max_new, stop_at_eos, prompt_tokens, force_tokens)
-    return out
+    return transcribe_lanes(lanes or [(dec, enc)], segs, max_new, stop_at_eos, prompt_tokens, force_tokens)

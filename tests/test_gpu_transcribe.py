@@ -166,3 +166,28 @@ def test_transcribe_audio_segments(engines):
         if seg.size < 8000:
             seg = np.concatenate([seg, np.zeros(8000 - seg.size, np.float32)])
         assert transcribe_ids(dec, enc, [seg], 6) == [ids]
+
+
+def test_transcribe_lanes_match_single(engines):
+    """qasr_transcribe_lanes: nine segments over two lanes (batches of the
+    smaller lane's max_batch, taken by whichever lane is free) give each
+    segment the ids it gets transcribed alone; lanes may not share an
+    engine."""
+    from qwenasr_b200._lib import QasrError
+    from qwenasr_b200.transcribe import transcribe_lanes
+    wd, we, od, dec, enc = engines
+    dec2 = Decoder(DEC, device=0, max_batch=3, max_seq=MAX_SEQ)
+    for i, lw in enumerate(wd["layers"]):
+        dec2.set_layer(i, lw)
+    dec2.set_globals(wd["embed"], wd["norm"], wd["lm_head"], wd["lm_head_s"])
+    enc2 = Encoder(ENC, device=0)
+    enc2.set_weights(we)
+    segs = [synthetic.synthetic_audio(s, seed=60 + i) for i, s in enumerate((2.0, 0.5, 1.3, 0.7, 1.9, 1.0, 0.6, 1.6, 1.1))]
+    want = [transcribe_ids(dec, enc, [s], 6)[0] for s in segs]
+    assert transcribe_lanes([(dec, enc), (dec2, enc2)], segs, 6) == want
+    assert transcribe_lanes([(dec2, enc2)], segs, 6) == want
+    assert transcribe_lanes([(dec, enc), (dec2, enc2)], [], 6) == []
+    with pytest.raises(QasrError):
+        transcribe_lanes([(dec, enc), (dec, enc2)], segs, 6)
+    dec2.close()
+    enc2.close()
