@@ -74,6 +74,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="bounded CPU-baseline sample length")
     ap.add_argument("--seed", type=int, default=1234)
+    ap.add_argument("--segments", type=int, default=None,
+                    help="segments of the whole job for --workload segments (default 64, the configuration's)")
     ap.add_argument("--lanes", type=int, default=None,
                     help="engine lanes (decoder + encoder pairs) per GPU for the transcription workloads "
                          "(default 1 for e2e, 2 for segments)")
@@ -639,6 +641,8 @@ def run_transcribe(a):
     dcfg = dict(getattr(synthetic, spec["dec"]), n_layers=a.layers)
     ecfg = getattr(synthetic, spec["enc"])
     n_seg = spec.get("segments", spec.get("segments_per_rank", 1) * world)
+    if a.segments and a.workload == "segments":
+        n_seg = a.segments
     mine = list(segment_range(n_seg, rank, world))
     new, batch, secs = spec["new"], spec["batch"], spec["seconds"]
     dev = torch.device(f"cuda:{local}")
