@@ -42,6 +42,8 @@ def test_version(lib):
     ("qasr_pre_attn_block", (None,) * 3 + (1, 1024) + (None,) * 6 + (16, 8, 128, C.c_float(1e-6), None, None, 0,
                                                                       None, None, 0, 16, None)),
     ("qasr_final_norm_lmhead_argmax", (None,) * 6 + (1, 1024, 151936, C.c_float(1e-6), None)),
+    ("qasr_transcribe_lanes", (None, None, 1, None, None, 1, None, 0, None, 0, 8, 0, None, 8, None)),
+    ("qasr_transcribe_batch", (None, None, None, None, 1, None, 0, None, 0, 8, 0, None, 8, None)),
 ])
 def test_null_pointers_rejected(lib, name, args):
     rc = getattr(lib, name)(*args)
@@ -60,6 +62,20 @@ def test_shape_errors(lib):
     assert lib.qasr_linear_nobias_int8(p, p, p, p, 1, 100, 8, None) == _lib.QASR_ERR_UNSUPPORTED
     assert lib.qasr_causal_attention(p, p, p, p, 1, 1, 16, 8, 96, C.c_float(0.1), 0, None) == \
         _lib.QASR_ERR_UNSUPPORTED
+
+
+def test_transcribe_lanes_validates_lanes(lib):
+    """Lane arrays are checked before any engine is touched: no lanes, more
+    than 64, or a lane without engines."""
+    ids = (C.c_int * 8)()
+    n = (C.c_int * 1)()
+    nulls = (C.c_void_p * 2)()
+    for lanes in (0, 65):
+        assert lib.qasr_transcribe_lanes(nulls, nulls, lanes, None, None, 0, None, 0, None, 0, 8, 0, ids, 8,
+                                         n) == _lib.QASR_ERR_INVALID
+    assert lib.qasr_transcribe_lanes(nulls, nulls, 2, None, None, 0, None, 0, None, 0, 8, 0, ids, 8,
+                                     n) == _lib.QASR_ERR_INVALID
+    assert "lane 0" in _lib.last_error()
 
 
 def test_decoder_create_rejects_bad_config(lib):
