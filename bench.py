@@ -78,7 +78,7 @@ def parse():
                     help="segments of the whole job for --workload segments (default 64, the configuration's)")
     ap.add_argument("--lanes", type=int, default=None,
                     help="engine lanes (decoder + encoder pairs) per GPU for the transcription workloads "
-                         "(default 1 for e2e, 2 for segments)")
+                         "(default 1 for e2e, 4 for segments)")
     ap.add_argument("--workload", choices=("decode", "gemm", "encoder", "e2e", "segments"), default="decode")
     ap.add_argument("--model", choices=("0.6b", "1.7b"), default="0.6b",
                     help="decoder shapes of the decode workload (0.6b = BASELINE configs[2])")
@@ -571,7 +571,7 @@ TRANSCRIBE = {
     "e2e": dict(dec="DEC_0_6B", enc="ENC_0_6B", segments_per_rank=1, seconds=30.0, new=256, batch=1, lanes=1,
                 scaling="weak", desc="BASELINE configs[3]: one 30 s segment per GPU, Qwen3-ASR-0.6B shapes "
                                      "(INT8 decoder, f32 encoder), 256 greedy tokens"),
-    "segments": dict(dec="DEC_1_7B", enc="ENC_1_7B", segments=64, seconds=30.0, new=128, batch=8, lanes=2,
+    "segments": dict(dec="DEC_1_7B", enc="ENC_1_7B", segments=64, seconds=30.0, new=128, batch=8, lanes=4,
                      scaling="strong", desc="BASELINE configs[4]: 64 segments of 30 s split evenly over the GPUs, "
                                             "Qwen3-ASR-1.7B shapes (INT8 decoder, f32 encoder), 128 greedy tokens "
                                             "each, 8 segments per decode batch"),
@@ -720,7 +720,6 @@ def run_transcribe(a):
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, e2e_ms = float(t[0]), float(t[1])
-    batch = min(batch, -(-len(mine) // n_lanes))  # as qasr_transcribe_lanes sizes its batches
     n_batches = (len(mine) + batch - 1) // batch
     dec_step_ms = max(ms - front_ms, 1e-6) / max(1, n_batches * (new - 1))
     mid_pos = np.full(min(batch, len(mine)), prompt_len(enc_tokens) - 1 + new // 2, np.int32)

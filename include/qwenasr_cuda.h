@@ -506,8 +506,8 @@ int qasr_transcribe_batch(qasr_decoder *dec, qasr_encoder *enc, const float *con
  * conditioning off) over n_segments independent segments, spread over
  * n_lanes engine lanes (decs[l], encs[l]: one decoder + encoder pair per
  * lane, no engine in two lanes, each pair on one device).  Segments go in
- * batches of the smallest lane's max_batch (fewer when that leaves a lane
- * idle: ceil(n_segments / n_lanes)) to whichever lane is free; lane 0
+ * full batches of the smallest lane's max_batch to whichever lane is free
+ * (so lanes beyond ceil(n_segments / max_batch) stay idle); lane 0
  * runs on the calling thread, the others on threads of their own, so lanes on
  * one GPU overlap their work and lanes on several GPUs run side by side.
  * Outputs as qasr_transcribe_batch, indexed by segment; the ids of a segment

@@ -221,10 +221,12 @@ attn_decode_kernel(const __grid_constant__ AttnDecodeParams p) {
   __syncthreads();
   const long long Tk = sm.off[n_pairs];
   // Virtual grid: only the first Gd CTAs take part, each owning at least
-  // kAttnMinKeys keys (one when Tk is smaller), so the CTAs covering a pair
-  // are exactly c_of(first key) .. c_of(last key) and short histories are
-  // split into few partials.
-  const long long Gd = max(1ll, min((long long)gridDim.x, Tk / kAttnMinKeys)), c = blockIdx.x;
+  // kAttnMinKeys keys -- or, when that would leave CTAs of the grid idle,
+  // at least p.floor_keys -- (one when Tk is smaller), so the CTAs covering
+  // a pair are exactly c_of(first key) .. c_of(last key) and short histories
+  // are split into few partials.
+  const long long per_cta = max((long long)max(1, p.floor_keys), min((long long)kAttnMinKeys, Tk / gridDim.x));
+  const long long Gd = max(1ll, min((long long)gridDim.x, Tk / per_cta)), c = blockIdx.x;
   if (c >= Gd) return;
   const long long t0 = c * Tk / Gd, t1 = (c + 1) * Tk / Gd;
 
@@ -593,9 +595,11 @@ int attn_decode_launch(const AttnDecodeParams &p, int group, cudaStream_t st, bo
     return QASR_ERR_UNSUPPORTED;
   }
   const bool wide = p.M >= kAttnWideFromM;
+  AttnDecodeParams q = p;
+  q.floor_keys = wide ? kAttnFloorKeys : kAttnMinKeys;
   switch (group) {
-    case 1: return wide ? attn_launch_t<1, kAttnWideWarps>(p, st, pdl) : attn_launch_t<1, kAttnMaxWarps>(p, st, pdl);
-    case 2: return wide ? attn_launch_t<2, kAttnWideWarps>(p, st, pdl) : attn_launch_t<2, kAttnMaxWarps>(p, st, pdl);
+    case 1: return wide ? attn_launch_t<1, kAttnWideWarps>(q, st, pdl) : attn_launch_t<1, kAttnMaxWarps>(q, st, pdl);
+    case 2: return wide ? attn_launch_t<2, kAttnWideWarps>(q, st, pdl) : attn_launch_t<2, kAttnMaxWarps>(q, st, pdl);
     default:
       set_error("attention: GQA group size %d unsupported (1 or 2)", group);
       return QASR_ERR_UNSUPPORTED;

@@ -27,6 +27,15 @@ constexpr int kAttnPartStride = 132;  // floats per (segment, head) partial: o[1
 #define QASR_ATTN_MIN_KEYS 256
 #endif
 constexpr int kAttnMinKeys = QASR_ATTN_MIN_KEYS;  // keys per CTA at least: short histories use fewer CTAs (fewer partials)
+#ifndef QASR_ATTN_FLOOR_KEYS
+#define QASR_ATTN_FLOOR_KEYS 64
+#endif
+// From kAttnWideFromM sequences on, when kAttnMinKeys keys per CTA would
+// leave CTAs of the grid idle, down to kAttnFloorKeys keys per CTA (about one
+// 8-key tile per warp).  Measured: -1.6 % step time at M=8 / KV 480, -2.7 %
+// at M=4 / KV 700, unchanged at M=8 / KV 1024; at M=1 it costs +3.8 %, hence
+// the batch threshold.
+constexpr int kAttnFloorKeys = QASR_ATTN_FLOOR_KEYS;
 
 struct AttnDecodeParams {
   CUtensorMap tm_k;      // 2D tensor maps over the whole cache: [rows = B*L*max_seq, kv_dim] f32,
@@ -37,6 +46,7 @@ struct AttnDecodeParams {
   const int32_t *positions;  // [M]: attend over rows 0..positions[m]
   float scale;
   int M;
+  int floor_keys;        // keys per CTA at least when kAttnMinKeys leaves CTAs idle (set by attn_decode_launch)
   float *partials;       // [gridDim + M*n_kv, G, kAttnPartStride]
   unsigned *counters;    // [M*n_kv], zero on entry, re-armed by the kernel
   float *out;            // [M, n_heads*128]

@@ -97,8 +97,9 @@ bidir_attention_kernel(float *__restrict__ out, const float *__restrict__ q, con
 }
 
 // Window [starts[w], starts[w+1]) of head h, queries z*8+warp, z*8+warp+8*gridDim.z, ...
-// Shared memory: K [kt][HD+1] (padded: lane-per-key reads are conflict-free),
-// V [kt][HD], per-warp q [HD] and scores [kt].
+// Shared memory: K [kt][HD+4] (padded: lane-per-key float4 reads are
+// conflict-free), V [kt][HD], per-warp q [HD] and scores [kt].
+constexpr int kBidirPadK = 4;
 template <int EPL>
 __global__ void __launch_bounds__(256)
 bidir_attention_staged_kernel(float *__restrict__ out, const float *__restrict__ q, const float *__restrict__ k,
@@ -107,7 +108,7 @@ bidir_attention_staged_kernel(float *__restrict__ out, const float *__restrict__
   constexpr int HD = EPL * 32;
   extern __shared__ float4 bidir_smem[];
   float *sK = reinterpret_cast<float *>(bidir_smem);
-  float *sV = sK + (size_t)kt * (HD + 1);
+  float *sV = sK + (size_t)kt * (HD + kBidirPadK);
   float *sQ = sV + (size_t)kt * HD;
   float *sP = sQ + 8 * HD;
   const int w = blockIdx.x, h = blockIdx.y;
@@ -115,7 +116,7 @@ bidir_attention_staged_kernel(float *__restrict__ out, const float *__restrict__
   const int n = we - ws;
   if (n <= 0 || n > kt) return;  // block-uniform; the host sizes kt to the longest window
   const long hidden = (long)n_heads * HD;
-  stage_kv_rows<HD, 1>(sK, sV, k, v, ws, hidden, (long)h * HD, n);
+  stage_kv_rows<HD, kBidirPadK>(sK, sV, k, v, ws, hidden, (long)h * HD, n);
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float *qs = sQ + warp * HD, *ps = sP + (size_t)warp * kt;
@@ -125,10 +126,19 @@ bidir_attention_staged_kernel(float *__restrict__ out, const float *__restrict__
     __syncwarp();
     float mx = -INFINITY;
     for (int j = lane; j < n; j += 32) {
-      const float *kr = sK + j * (HD + 1);
+      // K rows padded to HD + 4 floats: the float4 reads of 8 consecutive
+      // lanes cover all 32 banks; q is a broadcast read
+      const float4 *kr = reinterpret_cast<const float4 *>(sK + j * (HD + kBidirPadK));
+      const float4 *q4 = reinterpret_cast<const float4 *>(qs);
       float sc = 0.0f;
-#pragma unroll 16
-      for (int d = 0; d < HD; ++d) sc = fmaf(qs[d], kr[d], sc);
+#pragma unroll 4
+      for (int d4 = 0; d4 < HD / 4; ++d4) {
+        const float4 kk = kr[d4], qq = q4[d4];
+        sc = fmaf(qq.x, kk.x, sc);
+        sc = fmaf(qq.y, kk.y, sc);
+        sc = fmaf(qq.z, kk.z, sc);
+        sc = fmaf(qq.w, kk.w, sc);
+      }
       sc = __fmul_rn(sc, scale);
       ps[j] = sc;
       mx = fmaxf(mx, sc);
@@ -145,15 +155,15 @@ bidir_attention_staged_kernel(float *__restrict__ out, const float *__restrict__
     float o[EPL];
 #pragma unroll
     for (int e = 0; e < EPL; ++e) o[e] = 0.0f;
-    for (int j = 0; j < n; ++j) {
+    for (int j = 0; j < n; ++j) {  // lane owns elements lane + 32 e: conflict-free V reads
       const float pj = ps[j];
-      const float *vr = sV + j * HD + lane * EPL;
+      const float *vr = sV + j * HD + lane;
 #pragma unroll
-      for (int e = 0; e < EPL; ++e) o[e] = fmaf(pj, vr[e], o[e]);
+      for (int e = 0; e < EPL; ++e) o[e] = fmaf(pj, vr[32 * e], o[e]);
     }
     const float inv = __fdiv_rn(1.0f, l);  // l >= 1: the max key contributes exp(0)
 #pragma unroll
-    for (int e = 0; e < EPL; ++e) out[row + lane * EPL + e] = __fmul_rn(o[e], inv);
+    for (int e = 0; e < EPL; ++e) out[row + lane + 32 * e] = __fmul_rn(o[e], inv);
     __syncwarp();  // qs / ps are rewritten by the next query
   }
 }
@@ -196,7 +206,7 @@ namespace qasr {
 constexpr int kBidirMaxSmem = 200 * 1024;
 
 size_t bidir_smem_bytes(int head_dim, int kt) {
-  return ((size_t)kt * (head_dim + 1) + (size_t)kt * head_dim + 8 * head_dim + 8 * (size_t)kt) * 4;
+  return ((size_t)kt * (head_dim + kBidirPadK) + (size_t)kt * head_dim + 8 * head_dim + 8 * (size_t)kt) * 4;
 }
 
 // Windowed attention with the longest window known (max_window keys).
