@@ -47,22 +47,33 @@ inline int grid_of(long n) { return (int)std::max(1l, std::min((n + 255) / 256, 
 __global__ void __launch_bounds__(256) conv1_gelu_kernel(float *__restrict__ out, const float *__restrict__ mel,
                                                          int mel_frames, int first, int cs, int cw, int B, int h_out,
                                                          int w_out, const float *__restrict__ w,
-                                                         const float *__restrict__ bias, int C) {
-  const long total = (long)B * h_out * w_out * C;
-  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
-    const long r = i / C;
-    const int o = (int)(i - r * C);
-    const int ow = (int)(r % w_out), oh = (int)((r / w_out) % h_out), b = (int)(r / ((long)w_out * h_out));
-    float acc = 0.0f;
+                                                         const float *__restrict__ bias) {
+  // one warp per output position (b, oh, ow): its 9 inputs are read once,
+  // the lanes cover the kConvHidden channels (weights in shared memory,
+  // stride 9 across lanes: conflict-free), stores are coalesced rows
+  __shared__ float sw[kConvHidden * 9], sb[kConvHidden];
+  for (int i = threadIdx.x; i < kConvHidden * 9; i += blockDim.x) sw[i] = w[i];
+  for (int i = threadIdx.x; i < kConvHidden; i += blockDim.x) sb[i] = bias[i];
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int positions = B * h_out * w_out;  // < 2^31: B <= kStemGroup
+  for (int r = blockIdx.x * 8 + warp; r < positions; r += gridDim.x * 8) {
+    const int ow = r % w_out, t = r / w_out, oh = t % h_out, b = t / h_out;
+    float x[9];
 #pragma unroll
     for (int kk = 0; kk < 9; ++kk) {
       const int ih = oh * 2 + kk / 3 - 1, iw = ow * 2 + kk % 3 - 1;
-      const float x = (ih >= 0 && ih < kMelBins && iw >= 0 && iw < cw)
-                          ? __ldg(mel + (long)ih * mel_frames + first + (long)b * cs + iw)
-                          : 0.0f;
-      acc = fmaf(__ldg(w + o * 9 + kk), x, acc);
+      x[kk] = (ih >= 0 && ih < kMelBins && iw >= 0 && iw < cw)
+                  ? __ldg(mel + (long)ih * mel_frames + first + (long)b * cs + iw)
+                  : 0.0f;
     }
-    out[i] = gelu_tanh_ref(__fadd_rn(acc, __ldg(bias + o)));
+    float *row = out + (long)r * kConvHidden;
+    for (int o = lane; o < kConvHidden; o += 32) {
+      float acc = 0.0f;
+#pragma unroll
+      for (int kk = 0; kk < 9; ++kk) acc = fmaf(sw[o * 9 + kk], x[kk], acc);
+      row[o] = gelu_tanh_ref(__fadd_rn(acc, sb[o]));
+    }
   }
 }
 
@@ -72,15 +83,16 @@ __global__ void __launch_bounds__(256) conv1_gelu_kernel(float *__restrict__ out
 // contiguous floats: float4 loads and stores.
 __global__ void __launch_bounds__(256) im2col_cl_kernel(float *__restrict__ colsT, const float *__restrict__ act,
                                                         int C, int h_in, int w_in, int B, int h_out, int w_out) {
+  // 32-bit index math: B <= kStemGroup keeps every index below 2^31
   const int C4 = C / 4;
-  const long per_row = 9l * C4;
-  const long total = (long)B * h_out * w_out * per_row;
+  const int per_row = 9 * C4;
+  const int total = B * h_out * w_out * per_row;
   float4 *dst = reinterpret_cast<float4 *>(colsT);
   const float4 *src = reinterpret_cast<const float4 *>(act);
-  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
-    const long r = i / per_row;
-    const int rem = (int)(i - r * per_row), kk = rem / C4, c4 = rem % C4;
-    const int ow = (int)(r % w_out), oh = (int)((r / w_out) % h_out), b = (int)(r / ((long)w_out * h_out));
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const int r = i / per_row;
+    const int rem = i - r * per_row, kk = rem / C4, c4 = rem % C4;
+    const int ow = r % w_out, t = r / w_out, oh = t % h_out, b = t / h_out;
     const int ih = oh * 2 + kk / 3 - 1, iw = ow * 2 + kk % 3 - 1;
     dst[i] = (ih >= 0 && ih < h_in && iw >= 0 && iw < w_in) ? src[(((long)b * h_in + ih) * w_in + iw) * C4 + c4]
                                                              : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -649,8 +661,8 @@ static int encoder_run(qasr_encoder *e, int n, const float *const *mels, const i
       const int cw = full ? cs : tail;
       const int w1 = (cw + 2 - 3) / 2 + 1, w2 = (w1 + 2 - 3) / 2 + 1, w3 = (w2 + 2 - 3) / 2 + 1;
       const long r1 = (long)B * h1 * w1, r2 = (long)B * h2 * w2, r3 = (long)B * h3 * w3;
-      conv1_gelu_kernel<<<grid_of(r1 * CH), 256, 0, st>>>(e->act_a, mel, mel_frames, first, cs, cw, B, h1, w1,
-                                                          e->conv_w[0], e->conv_b[0], CH);
+      conv1_gelu_kernel<<<(int)std::min<long>((r1 + 7) / 8, 148l * 8), 256, 0, st>>>(
+          e->act_a, mel, mel_frames, first, cs, cw, B, h1, w1, e->conv_w[0], e->conv_b[0]);
       rc = launch_status("qasr_encoder_forward: conv1");
       if (!rc) {
         im2col_cl_kernel<<<grid_of(r2 * CH * 9 / 4), 256, 0, st>>>(e->cols, e->act_a, CH, h1, w1, B, h2, w2);

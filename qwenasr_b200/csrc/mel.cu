@@ -216,9 +216,13 @@ __global__ void __launch_bounds__(256)
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, t = t0 + lane;
   float top = -1e30f;
-  for (int m = warp; m < kBins; m += 8) {
+  // blockIdx.y takes kBins / gridDim.y mel bins, two per warp; the loads of
+  // the sequential sum are independent of it, so unrolling runs them ahead
+  const int per = kBins / gridDim.y, m0 = blockIdx.y * per;
+  for (int m = m0 + warp; m < m0 + per; m += 8) {
     const float *fr = filters + (size_t)m * kFreqs;
     float acc = 0.0f;
+#pragma unroll 8
     for (int k = 0; k < kFreqs; ++k) acc = __fadd_rn(acc, __fmul_rn(__ldg(fr + k), p[k][lane]));
     if (acc < 1e-10f) acc = 1e-10f;
     const float v = (float)log10((double)acc);
@@ -276,7 +280,7 @@ extern "C" int qasr_mel_spectrogram(float *mel, const float *samples, int n_samp
       power, samples, n_samples, n_frames, tab->window, tab->cos_t, tab->sin_t);
   if ((rc = launch_status("qasr_mel_spectrogram: power"))) return rc;
   if ((rc = cuda_status(cudaMemsetAsync(max_key, 0, 4, st), "qasr_mel_spectrogram: reset max"))) return rc;
-  mel_log_kernel<<<fb, 256, 0, st>>>(mel, max_key, power, n_frames, tab->filters);
+  mel_log_kernel<<<dim3(fb, kBins / 16), 256, 0, st>>>(mel, max_key, power, n_frames, tab->filters);
   if ((rc = launch_status("qasr_mel_spectrogram: log"))) return rc;
   const long total = (long)kBins * n_frames;
   mel_norm_kernel<<<(int)std::min((total + 255) / 256, 148l * 8), 256, 0, st>>>(mel, max_key, total);

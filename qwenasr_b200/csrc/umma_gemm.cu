@@ -47,13 +47,25 @@
 
 namespace qasr {
 
-constexpr int kGTok = 32;                 // tokens per block
+constexpr int kGTok = 32;                 // tokens per block (the f32 three-plane GEMM; small INT8 grids)
 constexpr int kGRows = 3 * kGTok;         // digit rows per block (MMA N)
 constexpr int kGStages = 4;
 constexpr int kGATile = 128 * 128;        // weight tile bytes
-constexpr int kGBTile = kGRows * 128;     // digit tile bytes
-constexpr int kGTmemCols = 256;           // two 96-column accumulators
-constexpr uint32_t kGIdesc = umma_idesc_s8(128, kGRows);
+
+// Token block of TOK tokens: 3*TOK digit rows (the MMA's N), a digit tile of
+// 3*TOK x 128 bytes per stage, two TMEM accumulators of 3*TOK columns (at
+// column 0 and kBufCols).  TOK = 64 (N = 192) halves the MMA instructions
+// and the weight-tile reads per token against TOK = 32.
+template <int TOK>
+struct GTile {
+  static_assert(TOK == 32 || TOK == 64, "token block");
+  static constexpr int kRows = 3 * TOK;
+  static constexpr int kBTile = kRows * 128;
+  static constexpr int kBufCols = TOK == 32 ? 128 : 256;
+  static constexpr int kTmemCols = 2 * kBufCols;
+  static constexpr uint32_t kIdesc = umma_idesc_s8(128, kRows);
+  static constexpr size_t kSmem = 1024 + (size_t)kGStages * (kGATile + kBTile);
+};
 constexpr int kGemmStore = 0, kGemmResidual = 1, kGemmSwiGLU = 2;
 
 // ---------------------------------------------------------------- digits --
@@ -135,17 +147,20 @@ QASR_DEV void g_fail(GSmem &sm, int *err) {
   if (err) atomicExch(err, -QASR_ERR_TIMEOUT);
 }
 
-template <int PLANES>
+template <int PLANES, int TOK>
 __global__ void __launch_bounds__(256, 1) gemm_kernel(const __grid_constant__ GemmParams p) {
+  using G = GTile<TOK>;
+  static_assert(PLANES == 1 || TOK == 32, "the plane sums of the f32 GEMM stay in registers: 32-token blocks");
+  constexpr int kHalves = TOK / 32;  // the epilogue reads TMEM 32 tokens at a time
   extern __shared__ unsigned char smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   unsigned char *base = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
   unsigned char *a_ring = base;
   unsigned char *b_ring = a_ring + (size_t)kGStages * kGATile;
-  GSmem &sm = *reinterpret_cast<GSmem *>(b_ring + (size_t)kGStages * kGBTile);
+  GSmem &sm = *reinterpret_cast<GSmem *>(b_ring + (size_t)kGStages * G::kBTile);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int KT = (p.K + 127) / 128, NT = (p.N + 127) / 128, NB = (p.T + kGTok - 1) / kGTok;
+  const int KT = (p.K + 127) / 128, NT = (p.N + 127) / 128, NB = (p.T + TOK - 1) / TOK;
   const int tiles = NT * NB;
   const int my_tiles = (int)blockIdx.x < tiles ? (tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
   // pipeline items: (output tile j, weight plane a, K step kt); one accumulator per (j, a) "piece"
@@ -166,7 +181,7 @@ __global__ void __launch_bounds__(256, 1) gemm_kernel(const __grid_constant__ Ge
     sm.abort = 0;
     mbar_fence_init();
   }
-  if (warp == 5) tmem_alloc(&sm.tmem, kGTmemCols);
+  if (warp == 5) tmem_alloc(&sm.tmem, G::kTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -178,9 +193,9 @@ __global__ void __launch_bounds__(256, 1) gemm_kernel(const __grid_constant__ Ge
   auto produce = [&](int i) {
     const int st = i % kGStages, tile = tile_of(i / per_tile), a = (i / KT) % PLANES, kt = i % KT;
     const int rt = tile / NB, tb = tile % NB;
-    mbar_arrive_expect_tx(&sm.full[st], kGATile + kGBTile);
+    mbar_arrive_expect_tx(&sm.full[st], kGATile + G::kBTile);
     tma_load_2d_u8(a_ring + (size_t)st * kGATile, &p.tm_w, kt * 128, a * p.N + rt * 128, &sm.full[st]);
-    tma_load_2d_u8(b_ring + (size_t)st * kGBTile, &p.tm_d, kt * 128, tb * kGRows, &sm.full[st]);
+    tma_load_2d_u8(b_ring + (size_t)st * G::kBTile, &p.tm_d, kt * 128, tb * G::kRows, &sm.full[st]);
   };
   const bool producer = warp == 4 && lane == 0;
   if (producer) {
@@ -208,11 +223,11 @@ __global__ void __launch_bounds__(256, 1) gemm_kernel(const __grid_constant__ Ge
         if (g_aborted(sm)) break;
         tc_fence_after();
         const uint32_t a_addr = smem_u32(a_ring + (size_t)st * kGATile);
-        const uint32_t b_addr = smem_u32(b_ring + (size_t)st * kGBTile);
-        const uint32_t d_addr = tmem + (uint32_t)(buf * 128);
+        const uint32_t b_addr = smem_u32(b_ring + (size_t)st * G::kBTile);
+        const uint32_t d_addr = tmem + (uint32_t)(buf * G::kBufCols);
 #pragma unroll
         for (int s = 0; s < 4; ++s)
-          umma_s8(d_addr, umma_desc_sw128(a_addr + 32 * s), umma_desc_sw128(b_addr + 32 * s), kGIdesc,
+          umma_s8(d_addr, umma_desc_sw128(a_addr + 32 * s), umma_desc_sw128(b_addr + 32 * s), G::kIdesc,
                   (kt == 0 && s == 0) ? 0u : 1u);
         umma_commit(&sm.empty[st]);
         if (kt == KT - 1) umma_commit(&sm.accfull[buf]);
@@ -232,52 +247,58 @@ __global__ void __launch_bounds__(256, 1) gemm_kernel(const __grid_constant__ Ge
       named_bar(1, 128);  // the four epilogue warps decide together
       if (g_aborted(sm)) break;
       tc_fence_after();
-      uint32_t a0[32], a1[32], a2[32];
-      const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(buf * 128);
-      tmem_ld32(taddr, a0);
-      tmem_ld32(taddr + 32, a1);
-      tmem_ld32(taddr + 64, a2);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&sm.accempty[buf])) : "memory");
       // plane a carries weight digit a: weight 2^(8*(PLANES-1-a)) within the plane sum
       const int wshift = 8 * (PLANES - 1 - a);
-#pragma unroll
-      for (int tl = 0; tl < kGTok; ++tl)
-        V[tl] += (((long long)(int)a0[tl] << 16) + ((long long)(int)a1[tl] << 8) + (long long)(int)a2[tl]) << wshift;
-      if (a != PLANES - 1) continue;
       const int row = rt * 128 + ri;
       const bool row_ok = row < p.N;
-      const float sc = row_ok ? p.scales[row] : 0.0f;
-      const float b = (row_ok && p.bias) ? p.bias[row] : 0.0f;
-      const int t0 = tb * kGTok;
-#pragma unroll
-      for (int tl = 0; tl < kGTok; ++tl) {
-        const int t = t0 + tl;  // dq holds the padded block: defined past T
-        float v = __fmul_rn(__fmul_rn(__ll2float_rn(V[tl]), __ldg(p.dq + t)), sc);
-        if (p.bias) v = __fadd_rn(v, b);
-        if (p.epi == kGemmSwiGLU) {
-          // avx::swiglu_interleaved (avx.rs:568-599) on the (gate, up) row pair
-          const float u = __shfl_xor_sync(0xffffffffu, v, 1);
-          if (t < p.T && row_ok && !(ri & 1)) {
-            const int j = row >> 1, body = (p.N >> 1) - (p.N >> 1) % 8;
-            const float silu = j < body ? __fdiv_rn(v, __fadd_rn(1.0f, fast_exp_ref(__fsub_rn(0.0f, v))))
-                                        : __fdiv_rn(v, __fadd_rn(1.0f, expf(-v)));
-            p.y[(size_t)t * p.y_stride + j] = __fmul_rn(silu, u);
-          }
-        } else if (t < p.T && row_ok) {
-          float *dst;
-          if (row >= p.n2)
-            dst = p.y2 + (size_t)t * p.y2_stride + (row - p.n2);
-          else if (row >= p.n1)
-            dst = p.y1 + (size_t)t * p.y1_stride + (row - p.n1);
-          else
-            dst = p.y + (size_t)t * p.y_stride + row;
-          *dst = p.epi == kGemmResidual ? __fadd_rn(*dst, v) : v;
+      for (int h = 0; h < kHalves; ++h) {
+        uint32_t a0[32], a1[32], a2[32];
+        // digit d of token tl sits in column d*TOK + tl of the accumulator
+        const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(buf * G::kBufCols + 32 * h);
+        tmem_ld32(taddr, a0);
+        tmem_ld32(taddr + TOK, a1);
+        tmem_ld32(taddr + 2 * TOK, a2);
+        if (h == kHalves - 1) {  // the accumulator is free for the MMA warp
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0)
+            asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&sm.accempty[buf])) : "memory");
         }
-      }
 #pragma unroll
-      for (int t = 0; t < kGTok; ++t) V[t] = 0;
+        for (int tl = 0; tl < kGTok; ++tl)
+          V[tl] += (((long long)(int)a0[tl] << 16) + ((long long)(int)a1[tl] << 8) + (long long)(int)a2[tl]) << wshift;
+        if (a != PLANES - 1) continue;  // PLANES > 1 implies one half: on to the next plane
+        const float sc = row_ok ? p.scales[row] : 0.0f;
+        const float b = (row_ok && p.bias) ? p.bias[row] : 0.0f;
+        const int t0 = tb * TOK + 32 * h;
+#pragma unroll
+        for (int tl = 0; tl < kGTok; ++tl) {
+          const int t = t0 + tl;  // dq holds the padded block: defined past T
+          float v = __fmul_rn(__fmul_rn(__ll2float_rn(V[tl]), __ldg(p.dq + t)), sc);
+          if (p.bias) v = __fadd_rn(v, b);
+          if (p.epi == kGemmSwiGLU) {
+            // avx::swiglu_interleaved (avx.rs:568-599) on the (gate, up) row pair
+            const float u = __shfl_xor_sync(0xffffffffu, v, 1);
+            if (t < p.T && row_ok && !(ri & 1)) {
+              const int j = row >> 1, body = (p.N >> 1) - (p.N >> 1) % 8;
+              const float silu = j < body ? __fdiv_rn(v, __fadd_rn(1.0f, fast_exp_ref(__fsub_rn(0.0f, v))))
+                                          : __fdiv_rn(v, __fadd_rn(1.0f, expf(-v)));
+              p.y[(size_t)t * p.y_stride + j] = __fmul_rn(silu, u);
+            }
+          } else if (t < p.T && row_ok) {
+            float *dst;
+            if (row >= p.n2)
+              dst = p.y2 + (size_t)t * p.y2_stride + (row - p.n2);
+            else if (row >= p.n1)
+              dst = p.y1 + (size_t)t * p.y1_stride + (row - p.n1);
+            else
+              dst = p.y + (size_t)t * p.y_stride + row;
+            *dst = p.epi == kGemmResidual ? __fadd_rn(*dst, v) : v;
+          }
+        }
+#pragma unroll
+        for (int t = 0; t < kGTok; ++t) V[t] = 0;
+      }
     }
   }
   __syncthreads();
@@ -289,7 +310,7 @@ __global__ void __launch_bounds__(256, 1) gemm_kernel(const __grid_constant__ Ge
   __syncthreads();
   if (warp == 5) {
     tc_fence_after();
-    tmem_dealloc(tmem, kGTmemCols);
+    tmem_dealloc(tmem, G::kTmemCols);
   }
 }
 
@@ -336,24 +357,54 @@ static int digit_rows(int8_t *D, float *dq, const float *x, long x_stride, int r
   return launch_status("tensor-core GEMM: digit rows");
 }
 
-template <int PLANES>
+template <int PLANES, int TOK>
 static int gemm_launch(GemmParams &p, cudaStream_t st) {
+  using G = GTile<TOK>;
   if (!p.y1) p.n1 = p.n2 = 0x7fffffff;  // no split
   static std::atomic<unsigned> attr_mask{0};  // engines on several host threads reach here
   int dev = 0;
   cudaGetDevice(&dev);
-  const size_t smem = 1024 + (size_t)kGStages * (kGATile + kGBTile) + sizeof(GSmem);
+  const size_t smem = G::kSmem + sizeof(GSmem);
   if (dev < 31 && !(attr_mask.load() & (1u << dev))) {
-    int rc = cuda_status(cudaFuncSetAttribute(gemm_kernel<PLANES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    int rc = cuda_status(cudaFuncSetAttribute(gemm_kernel<PLANES, TOK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               (int)smem),
                          "tensor-core GEMM: shared memory opt-in");
     if (rc) return rc;
     attr_mask.fetch_or(1u << dev);
   }
-  const long tiles = (long)((p.N + 127) / 128) * ((p.T + kGTok - 1) / kGTok);
+  const long tiles = (long)((p.N + 127) / 128) * ((p.T + TOK - 1) / TOK);
   const int grid = (int)std::min<long>(gemm_sms(), tiles);
-  gemm_kernel<PLANES><<<grid, 256, smem, st>>>(p);
+  gemm_kernel<PLANES, TOK><<<grid, 256, smem, st>>>(p);
   return launch_status("tensor-core GEMM");
+}
+
+// Token block of an INT8 GEMM: the one with fewer rounds of tiles over the
+// SMs, a 64-token tile counted as kGTok64Cost / 10 of a 32-token one (fewer
+// MMA instructions and weight-tile reads per token, more work per tile).
+#ifndef QASR_GEMM_TOK64_COST
+#define QASR_GEMM_TOK64_COST 16
+#endif
+constexpr int kGTok64Cost = QASR_GEMM_TOK64_COST;
+static int int8_gemm_tok(int T, int N) {
+  const long sms = gemm_sms(), nt = (N + 127) / 128;
+  const long waves32 = (nt * ((T + 31) / 32) + sms - 1) / sms, waves64 = (nt * ((T + 63) / 64) + sms - 1) / sms;
+  return waves64 * kGTok64Cost < waves32 * 10 ? 64 : 32;
+}
+
+// The activation digits of x (token blocks of TOK) and the launch, for an
+// INT8 GEMM whose weight map, scales and outputs p already holds.
+static int int8_gemm_run(GemmParams &p, const float *x, long x_stride, cudaStream_t st) {
+  const int T = p.T, K = p.K, TOK = int8_gemm_tok(T, p.N);
+  const int NB = (T + TOK - 1) / TOK, T_pad = NB * TOK, rows = 3 * TOK;
+  void *dbuf = nullptr, *qbuf = nullptr;
+  int rc;
+  if ((rc = dev_scratch(kScratchDigits, (size_t)NB * rows * K, &dbuf))) return rc;
+  if ((rc = dev_scratch(kScratchDigitScale, (size_t)T_pad * 4, &qbuf))) return rc;
+  if ((rc = int8_map(&p.tm_d, static_cast<int8_t *>(dbuf), (long)NB * rows, K, rows))) return rc;
+  p.dq = static_cast<float *>(qbuf);
+  if ((rc = digit_rows(static_cast<int8_t *>(dbuf), static_cast<float *>(qbuf), x, x_stride, T, T_pad, K, TOK, st)))
+    return rc;
+  return TOK == 64 ? gemm_launch<1, 64>(p, st) : gemm_launch<1, 32>(p, st);
 }
 
 // Shapes the tensor-core GEMMs take: K a multiple of 16 (TMA row pitch) and
@@ -367,15 +418,8 @@ static bool gemm_shape_ok(const float *x, long x_stride, int T, int K, int N) {
 int int8_gemm(float *y, long y_stride, const float *x, long x_stride, const int8_t *w, const float *scales,
               const float *bias, int T, int K, int N, cudaStream_t st) {
   if (!gemm_shape_ok(x, x_stride, T, K, N) || (reinterpret_cast<uintptr_t>(w) & 15)) return QASR_ERR_UNSUPPORTED;
-  const int NB = (T + kGTok - 1) / kGTok, T_pad = NB * kGTok;
-  void *dbuf = nullptr, *qbuf = nullptr;
-  int rc;
-  if ((rc = dev_scratch(kScratchDigits, (size_t)NB * kGRows * K, &dbuf))) return rc;
-  if ((rc = dev_scratch(kScratchDigitScale, (size_t)T_pad * 4, &qbuf))) return rc;
   GemmParams p{};
-  if ((rc = int8_map(&p.tm_w, w, N, K, 128))) return rc;
-  if ((rc = int8_map(&p.tm_d, static_cast<int8_t *>(dbuf), (long)NB * kGRows, K, kGRows))) return rc;
-  p.dq = static_cast<float *>(qbuf);
+  if (int rc = int8_map(&p.tm_w, w, N, K, 128)) return rc;
   p.scales = scales;
   p.bias = bias;
   p.y = y;
@@ -383,9 +427,7 @@ int int8_gemm(float *y, long y_stride, const float *x, long x_stride, const int8
   p.T = T;
   p.K = K;
   p.N = N;
-  if ((rc = digit_rows(static_cast<int8_t *>(dbuf), static_cast<float *>(qbuf), x, x_stride, T, T_pad, K, kGTok, st)))
-    return rc;
-  return gemm_launch<1>(p, st);
+  return int8_gemm_run(p, x, x_stride, st);
 }
 
 // int8_gemm with a fused epilogue: kGemmResidual adds the result to y (the
@@ -395,15 +437,8 @@ int int8_gemm_epi(float *y, long y_stride, const float *x, long x_stride, const 
                   int K, int N, int epi, cudaStream_t st) {
   if (!gemm_shape_ok(x, x_stride, T, K, N) || (reinterpret_cast<uintptr_t>(w) & 15) || (epi == kGemmSwiGLU && N % 128))
     return QASR_ERR_UNSUPPORTED;
-  const int NB = (T + kGTok - 1) / kGTok, T_pad = NB * kGTok;
-  void *dbuf = nullptr, *qbuf = nullptr;
-  int rc;
-  if ((rc = dev_scratch(kScratchDigits, (size_t)NB * kGRows * K, &dbuf))) return rc;
-  if ((rc = dev_scratch(kScratchDigitScale, (size_t)T_pad * 4, &qbuf))) return rc;
   GemmParams p{};
-  if ((rc = int8_map(&p.tm_w, w, N, K, 128))) return rc;
-  if ((rc = int8_map(&p.tm_d, static_cast<int8_t *>(dbuf), (long)NB * kGRows, K, kGRows))) return rc;
-  p.dq = static_cast<float *>(qbuf);
+  if (int rc = int8_map(&p.tm_w, w, N, K, 128)) return rc;
   p.scales = scales;
   p.y = y;
   p.y_stride = y_stride;
@@ -411,9 +446,7 @@ int int8_gemm_epi(float *y, long y_stride, const float *x, long x_stride, const 
   p.K = K;
   p.N = N;
   p.epi = epi;
-  if ((rc = digit_rows(static_cast<int8_t *>(dbuf), static_cast<float *>(qbuf), x, x_stride, T, T_pad, K, kGTok, st)))
-    return rc;
-  return gemm_launch<1>(p, st);
+  return int8_gemm_run(p, x, x_stride, st);
 }
 
 // int8_gemm over one weight matrix whose row ranges [0, n1), [n1, n2),
@@ -424,15 +457,8 @@ int int8_gemm_split3(float *y0, long s0, float *y1, long s1, int n1, float *y2, 
   if (!gemm_shape_ok(x, x_stride, T, K, N) || (reinterpret_cast<uintptr_t>(w) & 15) || n1 % 128 || n2 % 128 ||
       !(0 < n1 && n1 <= n2 && n2 <= N))
     return QASR_ERR_UNSUPPORTED;
-  const int NB = (T + kGTok - 1) / kGTok, T_pad = NB * kGTok;
-  void *dbuf = nullptr, *qbuf = nullptr;
-  int rc;
-  if ((rc = dev_scratch(kScratchDigits, (size_t)NB * kGRows * K, &dbuf))) return rc;
-  if ((rc = dev_scratch(kScratchDigitScale, (size_t)T_pad * 4, &qbuf))) return rc;
   GemmParams p{};
-  if ((rc = int8_map(&p.tm_w, w, N, K, 128))) return rc;
-  if ((rc = int8_map(&p.tm_d, static_cast<int8_t *>(dbuf), (long)NB * kGRows, K, kGRows))) return rc;
-  p.dq = static_cast<float *>(qbuf);
+  if (int rc = int8_map(&p.tm_w, w, N, K, 128)) return rc;
   p.scales = scales;
   p.y = y0;
   p.y_stride = s0;
@@ -445,9 +471,7 @@ int int8_gemm_split3(float *y0, long s0, float *y1, long s1, int n1, float *y2, 
   p.T = T;
   p.K = K;
   p.N = N;
-  if ((rc = digit_rows(static_cast<int8_t *>(dbuf), static_cast<float *>(qbuf), x, x_stride, T, T_pad, K, kGTok, st)))
-    return rc;
-  return gemm_launch<1>(p, st);
+  return int8_gemm_run(p, x, x_stride, st);
 }
 
 int f32_gemm(float *y, long y_stride, const float *x, long x_stride, const float *w, const float *bias, int T, int K,
@@ -475,7 +499,7 @@ int f32_gemm(float *y, long y_stride, const float *x, long x_stride, const float
   if ((rc = digit_rows(static_cast<int8_t *>(wbuf), static_cast<float *>(wq), w, K, N, N, K, N, st))) return rc;
   if ((rc = digit_rows(static_cast<int8_t *>(dbuf), static_cast<float *>(qbuf), x, x_stride, T, T_pad, K, kGTok, st)))
     return rc;
-  return gemm_launch<3>(p, st);
+  return gemm_launch<3, kGTok>(p, st);
 }
 
 // f32 weights [N, K] converted once into their three digit planes (rows of
@@ -526,7 +550,7 @@ int f32_gemm_prepared(float *y, long y_stride, const float *x, long x_stride, co
   p.N = w.N;
   if ((rc = digit_rows(static_cast<int8_t *>(dbuf), static_cast<float *>(qbuf), x, x_stride, T, T_pad, K, kGTok, st)))
     return rc;
-  return gemm_launch<3>(p, st);
+  return gemm_launch<3, kGTok>(p, st);
 }
 
 // ------------------------------------------------- CUDA-core fallback SGEMM --

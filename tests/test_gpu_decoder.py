@@ -238,6 +238,25 @@ def test_decode_step_1p7b_shapes(orc, M):
     dec.close()
 
 
+def test_long_prefill_matches_oracle(orc):
+    """A 1000-row prompt in one prefill: every projection (split q|k|v,
+    o-proj + residual, gate/up + SwiGLU, down + residual) runs with 64-token
+    blocks; K/V rows and the residual stream against the oracle's prefill."""
+    orc.set_threads(16)
+    P = 1000
+    w, od, dec = build_pair(orc, SMALL, seed=77, max_seq=1024, max_batch=1)
+    rng = np.random.default_rng(77)
+    emb = w["embed"][rng.integers(0, SMALL["vocab"], P)]
+    kh, vh = od.new_kv(1024)
+    ref_x = od.prefill(kh, vh, 0, emb)
+    dec.prefill(0, emb, 0)
+    kg, vg = dec.kv(0)
+    assert rel_err(kg[:, :P].cpu().numpy(), kh[:, :P]) < 2e-3
+    assert rel_err(vg[:, :P].cpu().numpy(), vh[:, :P]) < 2e-3
+    assert rel_err(dec.prefill_hidden(P).cpu().numpy(), ref_x) < 2e-3
+    dec.close()
+
+
 def test_prefill_batch_equals_single(orc):
     """qasr_decoder_prefill_batch: ragged prompts (one of a single row, one
     after 10 history rows) prefilled together leave each slot's K/V exactly as

@@ -299,6 +299,8 @@ def test_linear_int8_bias(orc):
     (200, 4096, 1024, False),   # decoder prefill q|k|v rows
     (390, 896, 896, True),      # encoder projection, one 30 s window of tokens
     (100, 1000, 3072, True),    # rows not a multiple of the 128-row tile
+    (1000, 4096, 1024, False),  # 64-token blocks (N = 192 MMAs), ragged last block
+    (3000, 1000, 1024, True),   # 64-token blocks with a partial last weight tile
 ])
 def test_int8_gemm_prefill_shapes(orc, seq, out_dim, in_dim, bias):
     """seq_len > 8 runs as one tensor-core GEMM (the reference: seq_len matvecs,
