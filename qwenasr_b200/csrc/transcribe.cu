@@ -16,6 +16,7 @@
 #include <algorithm>
 #include <atomic>
 #include <cstring>
+#include <exception>
 #include <mutex>
 #include <string>
 #include <thread>
@@ -279,9 +280,18 @@ extern "C" int qasr_transcribe_lanes(qasr_decoder *const *decs, qasr_encoder *co
       const int b = next.fetch_add(1);
       if (b >= n_batches) return;
       const int lo = b * batch, cnt = std::min(batch, n_segments - lo);
-      const int rc = qasr_transcribe_batch(decs[l], encs[l], samples + lo, n_samples + lo, cnt, prompt_tokens,
-                                           n_prompt, force_tokens, n_force, max_new, stop_at_eos,
-                                           ids + (size_t)lo * ids_stride, ids_stride, n_ids + lo);
+      int rc;
+      try {  // an exception must not leave a lane thread (std::terminate)
+        rc = qasr_transcribe_batch(decs[l], encs[l], samples + lo, n_samples + lo, cnt, prompt_tokens, n_prompt,
+                                   force_tokens, n_force, max_new, stop_at_eos, ids + (size_t)lo * ids_stride,
+                                   ids_stride, n_ids + lo);
+      } catch (const std::exception &ex) {
+        set_error("host exception: %s", ex.what());
+        rc = QASR_ERR_ALLOC;
+      } catch (...) {
+        set_error("host exception");
+        rc = QASR_ERR_INVALID;
+      }
       if (rc) {
         std::lock_guard<std::mutex> lk(mu);
         if (!first_rc) {
