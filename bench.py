@@ -646,7 +646,8 @@ def run_transcribe(a):
     mine = list(segment_range(n_seg, rank, world))
     new, batch, secs = spec["new"], spec["batch"], spec["seconds"]
     dev = torch.device(f"cuda:{local}")
-    n_lanes = a.lanes or spec["lanes"]
+    # lanes take full batches (qasr_transcribe_lanes): more lanes than batches would idle
+    n_lanes = max(1, min(a.lanes or spec["lanes"], -(-len(mine) // batch)))
     encs = [Encoder(ecfg, device=local) for _ in range(n_lanes)]
     enc_tokens = encs[0].tokens(K.mel_frames(int(secs * 16000)))
     max_seq = ((prompt_len(enc_tokens) - 1 + new + 63) // 64) * 64
