@@ -153,9 +153,10 @@ struct EncMat {
 };
 
 struct EncLayerDev {
-  float *attn_norm_w, *attn_norm_b, *bq, *bk, *bv, *bo;
+  float *attn_norm_w, *attn_norm_b, *bq, *bk, *bv, *bo;  // bk, bv follow bq in one [3D] buffer
   float *ffn_norm_w, *ffn_norm_b, *fc1_b, *fc2_b;
   EncMat wq, wk, wv, wo, fc1, fc2;
+  F32Weight qkv;  // f32 q|k|v as one [3D, D] digit-plane operand (d_model a multiple of 128)
 };
 
 }  // namespace qasr
@@ -263,6 +264,30 @@ static int mat_apply(float *y, const float *x, const EncMat &m, const float *bia
               : qasr_linear_nobias(y, x, m.f, T, m.cols, m.rows, st);
 }
 
+// The f32 q|k|v weights of a layer as one [3D, D] digit-plane operand, so
+// the three projections run as one GEMM with a split output; the separate
+// planes are then dropped.  d_model not a multiple of 128 keeps three GEMMs.
+static int prepare_qkv(qasr_encoder *e, EncLayerDev &L) {
+  f32_weight_free(&L.qkv);  // callers synchronised e->stream
+  const int D = e->cfg.d_model;
+  if (D % 128 || !L.wq.f || !L.wk.f || !L.wv.f) return QASR_OK;
+  const size_t n = (size_t)D * D;
+  float *tmp = nullptr;
+  int rc = cuda_status(cudaMalloc(&tmp, 3 * n * 4), "qasr_encoder: q|k|v weights");
+  if (rc) return rc;
+  const float *src[3] = {L.wq.f, L.wk.f, L.wv.f};
+  for (int i = 0; i < 3 && !rc; ++i)
+    rc = cuda_status(cudaMemcpyAsync(tmp + i * n, src[i], n * 4, cudaMemcpyDeviceToDevice, e->stream),
+                     "qasr_encoder: q|k|v weights");
+  if (!rc) rc = f32_weight_prepare(&L.qkv, tmp, 3 * D, D, e->stream);
+  if (rc == QASR_ERR_UNSUPPORTED) rc = QASR_OK;
+  const int rs = cuda_status(cudaStreamSynchronize(e->stream), "qasr_encoder: q|k|v weights");
+  cudaFree(tmp);
+  if (!rc && !rs && L.qkv.planes)
+    for (EncMat *m : {&L.wq, &L.wk, &L.wv}) f32_weight_free(&m->pw);
+  return rc ? rc : rs;
+}
+
 // conv i (1 or 2) of the stem over `rows` patch rows: y [rows, 480] =
 // cols [rows, 480*9] W_i^T + b_i.
 static int conv_gemm(qasr_encoder *e, int i, float *y, const float *cols, int rows, cudaStream_t st) {
@@ -310,6 +335,7 @@ extern "C" void qasr_encoder_free(qasr_encoder *e) {
   cudaSetDevice(e->device);
   if (e->stream) cudaStreamSynchronize(e->stream);
   for (EncMat *m : enc_mats(e)) m->release();
+  for (auto &L : e->layers) f32_weight_free(&L.qkv);
   for (auto &pw : e->conv_pw) f32_weight_free(&pw);
   for (void *p : e->allocs) cudaFree(p);
   if (e->act) cudaFree(e->act);
@@ -365,10 +391,14 @@ extern "C" qasr_encoder *qasr_encoder_create(const qasr_encoder_config *cfg, int
   e->proj2.rows = O;
   e->proj2.cols = D;
   for (auto &L : e->layers) {
-    float **pp[] = {&L.attn_norm_w, &L.attn_norm_b, &L.bq, &L.bk, &L.bv, &L.bo, &L.ffn_norm_w, &L.ffn_norm_b,
-                    &L.fc2_b};
+    float **pp[] = {&L.attn_norm_w, &L.attn_norm_b, &L.bo, &L.ffn_norm_w, &L.ffn_norm_b, &L.fc2_b};
     for (float **p : pp)
       if (!rc) rc = enc_alloc(e, p, D);
+    if (!rc) rc = enc_alloc(e, &L.bq, 3 * (size_t)D);
+    if (!rc) {
+      L.bk = L.bq + D;
+      L.bv = L.bq + 2 * (size_t)D;
+    }
     if (!rc) rc = enc_alloc(e, &L.fc1_b, F);
     for (EncMat *m : {&L.wq, &L.wk, &L.wv, &L.wo}) {
       m->rows = D;
@@ -462,6 +492,7 @@ extern "C" int qasr_encoder_set_layer(qasr_encoder *e, int layer, const qasr_enc
   if (!rc) rc = mat_set_f32(e, L.wq, w->wq, "wq");
   if (!rc) rc = mat_set_f32(e, L.wk, w->wk, "wk");
   if (!rc) rc = mat_set_f32(e, L.wv, w->wv, "wv");
+  if (!rc) rc = prepare_qkv(e, L);
   if (!rc) rc = mat_set_f32(e, L.wo, w->wo, "wo");
   if (!rc) rc = mat_set_f32(e, L.fc1, w->fc1_w, "fc1_w");
   if (!rc) rc = mat_set_f32(e, L.fc2, w->fc2_w, "fc2_w");
@@ -489,6 +520,10 @@ extern "C" int qasr_encoder_set_layer_int8(qasr_encoder *e, int layer, const qas
                {L.bq, w->bq, D, "bq"}, {L.bk, w->bk, D, "bk"}, {L.bv, w->bv, D, "bv"}, {L.bo, w->bo, D, "bo"},
                {L.ffn_norm_w, w->ffn_norm_w, D, "ffn_norm_w"}, {L.ffn_norm_b, w->ffn_norm_b, D, "ffn_norm_b"},
                {L.fc1_b, w->fc1_b, F, "fc1_b"}, {L.fc2_b, w->fc2_b, D, "fc2_b"}};
+  if (L.qkv.planes) {  // the f32 q|k|v operand goes with the f32 weights
+    rc = cuda_status(cudaStreamSynchronize(e->stream), "qasr_encoder_set_layer_int8");
+    f32_weight_free(&L.qkv);
+  }
   for (auto &it : items)
     if (!rc) rc = enc_copy(e, it.dst, it.src, it.n, it.what);
   if (!rc) rc = mat_set_i8(e, L.wq, w->wq, w->wq_s, "wq");
@@ -718,9 +753,19 @@ static int encoder_run(qasr_encoder *e, int n, const float *const *mels, const i
   for (int l = 0; l < c.n_layers && !rc; ++l) {
     const EncLayerDev &L = e->layers[l];
     rc = qasr_layer_norm(e->xn, e->x, L.attn_norm_w, L.attn_norm_b, T, D, 1e-5f, st);
-    if (!rc) rc = mat_apply(e->q, e->xn, L.wq, L.bq, T, st);
-    if (!rc) rc = mat_apply(e->k, e->xn, L.wk, L.bk, T, st);
-    if (!rc) rc = mat_apply(e->v, e->xn, L.wv, L.bv, T, st);
+    bool fused = false;
+    if (!rc && L.qkv.planes) {  // one digit pass and one launch for q, k and v
+      const int r = f32_gemm_prepared_split3(e->q, D, e->k, D, D, e->v, D, 2 * D, e->xn, D, L.qkv, L.bq, T, st);
+      if (r != QASR_ERR_UNSUPPORTED) {
+        rc = r;
+        fused = true;
+      }
+    }
+    if (!fused) {
+      if (!rc) rc = mat_apply(e->q, e->xn, L.wq, L.bq, T, st);
+      if (!rc) rc = mat_apply(e->k, e->xn, L.wk, L.bk, T, st);
+      if (!rc) rc = mat_apply(e->v, e->xn, L.wv, L.bv, T, st);
+    }
     if (!rc)
       rc = bidir_attention_launch(e->attn, e->q, e->k, e->v, T, c.n_heads, c.head_dim, scale, e->win, nw,
                                   max_window, st);

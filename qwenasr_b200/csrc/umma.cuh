@@ -66,6 +66,9 @@ int f32_weight_prepare(F32Weight *pw, const float *w, int N, int K, cudaStream_t
 void f32_weight_free(F32Weight *pw);
 int f32_gemm_prepared(float *y, long y_stride, const float *x, long x_stride, const F32Weight &w, const float *bias,
                       int T, cudaStream_t st);
+int f32_gemm_prepared_split3(float *y0, long s0, float *y1, long s1, int n1, float *y2, long s2, int n2,
+                             const float *x, long x_stride, const F32Weight &w, const float *bias, int T,
+                             cudaStream_t st);
 // The same on CUDA cores, any shape.
 int f32_gemm_fallback(float *y, const float *x, const float *w, const float *bias, int T, int K, int N,
                       cudaStream_t st);

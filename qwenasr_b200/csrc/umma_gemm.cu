@@ -553,6 +553,41 @@ int f32_gemm_prepared(float *y, long y_stride, const float *x, long x_stride, co
   return gemm_launch<3, kGTok>(p, st);
 }
 
+// f32_gemm_prepared over a weight whose row ranges [0, n1), [n1, n2),
+// [n2, N) go to three outputs (the encoder's fused q|k|v projection: one
+// activation digit pass and one launch for the three).
+int f32_gemm_prepared_split3(float *y0, long s0, float *y1, long s1, int n1, float *y2, long s2, int n2,
+                             const float *x, long x_stride, const F32Weight &w, const float *bias, int T,
+                             cudaStream_t st) {
+  if (!w.planes || !gemm_shape_ok(x, x_stride, T, w.K, w.N) || n1 % 128 || n2 % 128 || !(0 < n1 && n1 <= n2 && n2 <= w.N))
+    return QASR_ERR_UNSUPPORTED;
+  const int K = w.K, NB = (T + kGTok - 1) / kGTok, T_pad = NB * kGTok;
+  void *dbuf = nullptr, *qbuf = nullptr;
+  int rc;
+  if ((rc = dev_scratch(kScratchDigits, (size_t)NB * kGRows * K, &dbuf))) return rc;
+  if ((rc = dev_scratch(kScratchDigitScale, (size_t)T_pad * 4, &qbuf))) return rc;
+  GemmParams p{};
+  p.tm_w = w.tm;
+  if ((rc = int8_map(&p.tm_d, static_cast<int8_t *>(dbuf), (long)NB * kGRows, K, kGRows))) return rc;
+  p.dq = static_cast<float *>(qbuf);
+  p.scales = w.factors;
+  p.bias = bias;
+  p.y = y0;
+  p.y_stride = s0;
+  p.y1 = y1;
+  p.y1_stride = s1;
+  p.n1 = n1;
+  p.y2 = y2;
+  p.y2_stride = s2;
+  p.n2 = n2;
+  p.T = T;
+  p.K = K;
+  p.N = w.N;
+  if ((rc = digit_rows(static_cast<int8_t *>(dbuf), static_cast<float *>(qbuf), x, x_stride, T, T_pad, K, kGTok, st)))
+    return rc;
+  return gemm_launch<3, kGTok>(p, st);
+}
+
 // ------------------------------------------------- CUDA-core fallback SGEMM --
 // y[t, o] = sum_k x[t, k] w[o, k] (+ b[o]) for shapes the tensor-core GEMM
 // does not take (K not a multiple of 16, unaligned rows): 32x32 output tiles,
