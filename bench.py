@@ -79,7 +79,8 @@ def parse():
     ap.add_argument("--lanes", type=int, default=None,
                     help="engine lanes (decoder + encoder pairs) per GPU for the transcription workloads "
                          "(default 1 for e2e, 4 for segments)")
-    ap.add_argument("--workload", choices=("decode", "gemm", "encoder", "e2e", "segments"), default="decode")
+    ap.add_argument("--workload", choices=("decode", "gemm", "encoder", "e2e", "segments", "pre_attn",
+                                           "enc_elementwise"), default="decode")
     ap.add_argument("--model", choices=("0.6b", "1.7b"), default="0.6b",
                     help="decoder shapes of the decode workload (0.6b = BASELINE configs[2])")
     ap.add_argument("--layers", type=int, default=28,
@@ -87,7 +88,7 @@ def parse():
     a = ap.parse_args()
     long_run = a.workload in ("e2e", "segments")
     if a.steps is None:
-        a.steps = {"e2e": 5, "segments": 3}.get(a.workload, 50)
+        a.steps = {"e2e": 5, "segments": 3, "pre_attn": 400, "enc_elementwise": 120}.get(a.workload, 50)
     if a.warmup is None:
         a.warmup = 3 if long_run else 5
     return a
@@ -505,6 +506,283 @@ def run_gemm(a):
     return 0
 
 
+# ------------------------------------------------ fused row kernels (cfg1/2) --
+# the decoder pre-attention block at 0.6B shapes.
+PRE_ATTN = dict(seq=512, hidden=1024, n_heads=16, n_kv=8, head_dim=128, capacity=4096, eps=1e-6, theta=1e6)
+# the encoder elementwise steps, batch 8 x 375 frames.
+ENC_ELEM = dict(rows=3000, d=896, n_pos=375, ffn=3584, eps=1e-5)
+
+
+def pre_attn_bytes(c):
+    """Algorithmic bytes of one config-1 block: x read, x_norm written, q read
+    and written, k and v read, their cache rows written (norm weights and the
+    RoPE rows are below 0.1 % and not counted)."""
+    S, H, q, kv = c["seq"], c["hidden"], c["n_heads"] * c["head_dim"], c["n_kv"] * c["head_dim"]
+    return 4 * S * (2 * H + 2 * q + 2 * kv + 2 * kv)
+
+
+def enc_elem_bytes(c):
+    """LN+PE: x read, out written; GELU: the FFN activation read and written."""
+    return 4 * c["rows"] * c["d"] * 2 + 4 * c["rows"] * c["ffn"] * 2
+
+
+class _Graph:
+    """A CUDA graph of `fn` called once per input set (the sets together
+    exceed L2, so every launch reads cold data)."""
+
+    def __init__(self, torch, fn, n_sets):
+        self.torch = torch
+        st = torch.cuda.Stream()
+        st.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(st):
+            for i in range(n_sets):  # warm-up outside the capture (attribute opt-ins)
+                fn(i)
+        torch.cuda.current_stream().wait_stream(st)
+        torch.cuda.synchronize()
+        self.g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.g):
+            for i in range(n_sets):
+                fn(i)
+        self.n = n_sets
+
+    def time_ms(self, reps):
+        """Device time per launch: CUDA events around `reps` replays."""
+        torch = self.torch
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            self.g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / (reps * self.n)
+
+
+def _row_kernel_line(a, metric, workload_cfg, bytes_step, ms, kernels, e2e_ms, h2d, d2h, cpu, clk, n_sets, set_bytes):
+    peak, peak_kind = peaks()
+    gbs = bytes_step / (ms / 1e3) / 1e9
+    dom = max(kernels, key=lambda k: kernels[k]["us"])
+    kd = kernels[dom]
+    return {
+        "metric": metric, "value": gbs, "unit": "GB/s", "n_gpus": 1, "steps": a.steps, "warmup": a.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "none", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1) activations, N(1,0.02) / N(0,0.02) norm weights)",
+        "config": dict(workload_cfg, l2=f"{n_sets} input sets of {set_bytes / 1e6:.1f} MB used in turn "
+                                        f"({n_sets * set_bytes / 1e6:.0f} MB > 126 MB L2): every launch reads "
+                                        f"cold data"),
+        "e2e": {"value": bytes_step / (e2e_ms / 1e3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+        "gpu_launches": sum(k["launches_per_step"] for k in kernels.values()) * a.steps,
+        "roofline": {"bound": "hbm", "kernel": dom, "achieved": kd["gbs"], "peak": peak, "unit": "GB/s",
+                     "frac": kd["gbs"] / peak, "traffic": None,
+                     "traffic_note": "dram bytes of one launch are in profiles/ (ncu)", "peak_kind": peak_kind,
+                     "bytes_per_launch": kd["bytes"], "us_per_launch": kd["us"]},
+        "kernels": kernels,
+        "cpu_baseline": cpu,
+        "timing": "CUDA events around replays of a CUDA graph holding one launch per input set",
+        "clocks": clk.summary(),
+    }
+
+
+def run_pre_attn(a):
+    """BASELINE configs[0] through qasr_pre_attn_block (kernels.pre_attn_block)."""
+    import torch
+    from qwenasr_b200 import kernels as K
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda:0")
+    c = PRE_ATTN
+    S, H, nh, nkv, hd, cap = c["seq"], c["hidden"], c["n_heads"], c["n_kv"], c["head_dim"], c["capacity"]
+    q_dim, kv = nh * hd, nkv * hd
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(a.seed)
+    cos = torch.empty(cap, hd, device=dev)
+    sin = torch.empty(cap, hd, device=dev)
+    K.rope_cache_table(cos, sin, cap, hd, c["theta"])
+    w_in = 1 + 0.02 * torch.randn(H, generator=gen, device=dev)
+    qw = 1 + 0.02 * torch.randn(hd, generator=gen, device=dev)
+    kw = 1 + 0.02 * torch.randn(hd, generator=gen, device=dev)
+    set_bytes = pre_attn_bytes(c)
+    n_sets = 8
+    sets = []
+    for _ in range(n_sets):
+        sets.append(dict(x=torch.randn(S, H, generator=gen, device=dev), xn=torch.empty(S, H, device=dev),
+                         q=torch.randn(S, q_dim, generator=gen, device=dev),
+                         k=torch.randn(S, kv, generator=gen, device=dev),
+                         v=torch.randn(S, kv, generator=gen, device=dev),
+                         kc=torch.zeros(cap, kv, device=dev), vc=torch.zeros(cap, kv, device=dev)))
+
+    def call(i, s=None):
+        s = s or sets[i]
+        K.pre_attn_block(s["xn"], s["x"], w_in, S, H, s["q"], s["k"], s["v"], None, qw, kw, nh, nkv, hd, c["eps"],
+                         cos, sin, 0, s["kc"], s["vc"], 0, cap)
+
+    g = _Graph(torch, call, n_sets)
+    reps = max(1, -(-a.steps // n_sets))
+    for _ in range(max(a.warmup, 3)):
+        g.time_ms(1)
+    with ClockSampler(0) as clk:
+        ms = g.time_ms(reps)
+    kernels = {"pre_attn_block_kernel": {"us": ms * 1e3, "bytes": set_bytes, "gbs": set_bytes / (ms / 1e3) / 1e9,
+                                         "launches_per_step": 1}}
+    # e2e: pinned host inputs -> device, the C-ABI call, results -> pinned host
+    hx = torch.randn(S, H).pin_memory()
+    hq = torch.randn(S, q_dim).pin_memory()
+    hk = torch.randn(S, kv).pin_memory()
+    hv = torch.randn(S, kv).pin_memory()
+    hxn = torch.empty(S, H).pin_memory()
+    hqo = torch.empty(S, q_dim).pin_memory()
+    hkc = torch.empty(S, kv).pin_memory()
+    hvc = torch.empty(S, kv).pin_memory()
+    s0 = sets[0]
+
+    def e2e_step():
+        s0["x"].copy_(hx, non_blocking=True)
+        s0["q"].copy_(hq, non_blocking=True)
+        s0["k"].copy_(hk, non_blocking=True)
+        s0["v"].copy_(hv, non_blocking=True)
+        call(0)
+        hxn.copy_(s0["xn"], non_blocking=True)
+        hqo.copy_(s0["q"], non_blocking=True)
+        hkc.copy_(s0["kc"][:S], non_blocking=True)
+        hvc.copy_(s0["vc"][:S], non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / a.steps
+    h2d = 4 * S * (H + q_dim + 2 * kv)
+    d2h = 4 * S * (H + q_dim + 2 * kv)
+    cpu = None
+    if not a.no_cpu_baseline:
+        from oracle import pyoracle as orc
+        xs = [t.cpu().numpy() for t in (sets[0]["x"], w_in, sets[0]["q"], sets[0]["k"], sets[0]["v"], qw, kw)]
+        ch, sh = cos.cpu().numpy(), sin.cpu().numpy()
+        kc = np.zeros((cap, kv), np.float32)
+        vc = np.zeros((cap, kv), np.float32)
+        n, t_cpu = 0, 0.0
+        while t_cpu < min(a.cpu_seconds, 10.0) or n < 3:
+            t0 = time.perf_counter()
+            orc.pre_attn_block(xs[0], xs[1], xs[2], xs[3], xs[4], xs[5], xs[6], nh, nkv, hd, c["eps"], ch, sh, 0,
+                               kc, vc)
+            t_cpu += time.perf_counter() - t0
+            n += 1
+        cpu = {"value": set_bytes * n / t_cpu / 1e9, "unit": "GB/s", "cores": 1, "kind": "port",
+               "sample": f"{n} whole config-1 blocks of the oracle restatement (rms_norm, rms_norm_per_head, "
+                         f"apply_rope_neox, KV append in the reference's order), 1 thread like the reference's "
+                         f"norm kernels"}
+    line = _row_kernel_line(
+        a, "decoder pre-attention block HBM throughput (RMSNorm + q/k per-head norm + RoPE + KV append)",
+        {"workload": "BASELINE configs[0]: S=512 rows at Qwen3-0.6B shapes, positions 0..511, KV capacity 4096",
+         "seq": S, "hidden": H, "heads": [nh, nkv], "head_dim": hd}, set_bytes, ms, kernels, e2e_ms, h2d, d2h, cpu,
+        clk, n_sets, set_bytes)
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_enc_elementwise(a):
+    """BASELINE configs[1] through qasr_ln_pe_gelu_erf (one launch), with the
+    two separate entries qasr_ln_pe + qasr_gelu_erf timed beside it."""
+    import torch
+    from qwenasr_b200 import kernels as K
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda:0")
+    c = ENC_ELEM
+    R, D, P, F = c["rows"], c["d"], c["n_pos"], c["ffn"]
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(a.seed)
+    g_ = 1 + 0.02 * torch.randn(D, generator=gen, device=dev)
+    b_ = 0.02 * torch.randn(D, generator=gen, device=dev)
+    pe = torch.empty(P, D, device=dev)
+    K.sinusoidal_pe(pe, P, D)
+    set_bytes = enc_elem_bytes(c)
+    n_sets = 3
+    sets = [dict(x=torch.randn(R, D, generator=gen, device=dev), out=torch.empty(R, D, device=dev),
+                 act=torch.randn(R * F, generator=gen, device=dev)) for _ in range(n_sets)]
+
+    def fused(i):
+        s = sets[i]
+        K.ln_pe_gelu_erf(s["out"], s["x"], g_, b_, pe, R, D, P, c["eps"], s["act"], R * F)
+
+    def ln_only(i):
+        s = sets[i]
+        K.ln_pe(s["out"], s["x"], g_, b_, pe, R, D, P, c["eps"])
+
+    def gelu_only(i):
+        K.gelu_erf(sets[i]["act"], R * F)
+
+    graphs = {n: _Graph(torch, f, n_sets) for n, f in (("ln_pe_gelu_kernel", fused), ("layer_norm_kernel", ln_only),
+                                                       ("gelu_erf_kernel", gelu_only))}
+    reps = max(1, -(-a.steps // n_sets))
+    for g in graphs.values():
+        for _ in range(max(a.warmup, 3)):
+            g.time_ms(1)
+    with ClockSampler(0) as clk:
+        ms = graphs["ln_pe_gelu_kernel"].time_ms(reps)
+        ms_ln = graphs["layer_norm_kernel"].time_ms(reps)
+        ms_ge = graphs["gelu_erf_kernel"].time_ms(reps)
+    ln_b, ge_b = 4 * R * D * 2, 4 * R * F * 2
+    kernels = {"ln_pe_gelu_kernel": {"us": ms * 1e3, "bytes": set_bytes, "gbs": set_bytes / (ms / 1e3) / 1e9,
+                                     "launches_per_step": 1},
+               "separate: layer_norm_kernel (qasr_ln_pe)": {"us": ms_ln * 1e3, "bytes": ln_b,
+                                                            "gbs": ln_b / (ms_ln / 1e3) / 1e9,
+                                                            "launches_per_step": 0},
+               "separate: gelu_erf_kernel (qasr_gelu_erf)": {"us": ms_ge * 1e3, "bytes": ge_b,
+                                                             "gbs": ge_b / (ms_ge / 1e3) / 1e9,
+                                                             "launches_per_step": 0}}
+    hx = torch.randn(R, D).pin_memory()
+    ha = torch.randn(R * F).pin_memory()
+    ho = torch.empty(R, D).pin_memory()
+    hao = torch.empty(R * F).pin_memory()
+    s0 = sets[0]
+
+    def e2e_step():
+        s0["x"].copy_(hx, non_blocking=True)
+        s0["act"].copy_(ha, non_blocking=True)
+        fused(0)
+        ho.copy_(s0["out"], non_blocking=True)
+        hao.copy_(s0["act"], non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / a.steps
+    h2d = d2h = 4 * (R * D + R * F)
+    cpu = None
+    if not a.no_cpu_baseline:
+        from oracle import pyoracle as orc
+        x_h, g_h, b_h, pe_h = (t.cpu().numpy() for t in (s0["x"], g_, b_, pe))
+        act_h = s0["act"].cpu().numpy()
+        pe_rows = pe_h[np.arange(R) % P]
+        n, t_cpu = 0, 0.0
+        while t_cpu < min(a.cpu_seconds, 10.0) or n < 2:
+            t0 = time.perf_counter()
+            _ = orc.layer_norm(x_h, g_h, b_h, c["eps"]) + pe_rows
+            _ = orc.gelu_erf(act_h)
+            t_cpu += time.perf_counter() - t0
+            n += 1
+        cpu = {"value": set_bytes * n / t_cpu / 1e9, "unit": "GB/s", "cores": 1, "kind": "port",
+               "sample": f"{n} whole config-2 passes of the oracle restatement (layer_norm_row AVX order + PE "
+                         f"add + erff GELU), 1 thread like the reference's row kernels"}
+    line = _row_kernel_line(
+        a, "encoder elementwise HBM throughput (LayerNorm + sinusoidal PE, exact-erf GELU)",
+        {"workload": "BASELINE configs[1]: LN + PE on [3000, 896] (8 items x 375 frames), erf GELU on "
+                     "[3000, 3584]", "rows": R, "d_model": D, "ffn": F}, set_bytes, ms, kernels, e2e_ms, h2d, d2h,
+        cpu, clk, n_sets, set_bytes)
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 # ---------------------------------------------------------------- encoder --
 def encoder_flops(cfg, frames):
     """f32-equivalent multiply-adds x 2 of Encoder::forward for `frames` mel frames."""
@@ -784,6 +1062,10 @@ def main():
         return run_reference(a)
     if a.workload == "gemm":
         return run_gemm(a)
+    if a.workload == "pre_attn":
+        return run_pre_attn(a)
+    if a.workload == "enc_elementwise":
+        return run_enc_elementwise(a)
     if a.workload == "encoder":
         return run_encoder(a)
     if a.workload in TRANSCRIBE:

@@ -218,6 +218,15 @@ int qasr_pre_attn_block(float *x_norm, const float *x, const float *w_in, int se
 int qasr_ln_pe(float *out, const float *x, const float *w, const float *b, const float *pe, int rows, int hidden,
                int n_pos, float eps, void *stream);
 
+/* The encoder's elementwise steps in one launch (the ln_pe_gelu entry of the
+ * fused family): out = qasr_ln_pe(x) as above, and exact-erf GELU in place on
+ * act [n_act] (the FFN activation; qasr_gelu_erf's arithmetic).  Replaces
+ * layer_norm (mod.rs:866) + the PE add (encoder.rs:341-343) + gelu
+ * (mod.rs:948) of a config-2 pass; both results are bit-identical to the
+ * separate entries.  act 16-byte aligned; n_act may be 0. */
+int qasr_ln_pe_gelu_erf(float *out, const float *x, const float *w, const float *b, const float *pe, int rows,
+                        int hidden, int n_pos, float eps, float *act, int64_t n_act, void *stream);
+
 /* Post-attention RMSNorm + fused gate/up INT8 matvec + SwiGLU for M tokens
  * (decoder.rs:911-921): h[m,j] = silu(g)*u with g,u the interleaved rows
  * 2j, 2j+1 of w_gate_up applied to rms_norm(x[m]).  M <= 8. */
@@ -242,9 +251,11 @@ int qasr_final_norm_lmhead_argmax(int32_t *ids_out, float *logits_out, const flo
  * started: a runtime with its own pool or a hard memory budget.  The argmax
  * scratch is a fixed 256-byte array in the library; its device address is
  * looked up on the first call on each device (make that first call before any
- * stream capture).  Limits: M <= 8, hidden a multiple of 512 and <= 3072,
- * x / w / norm_w 16-byte aligned; larger M returns QASR_ERR_INVALID, other
- * shapes QASR_ERR_UNSUPPORTED.  The scratch is shared by all calls on one
+ * stream capture), and every call clears it with a 256-byte memset on
+ * `stream` before its kernel.  Limits: M <= 8, hidden a multiple of 512 and
+ * <= 3072, x / w / norm_w 16-byte aligned; larger M returns QASR_ERR_INVALID,
+ * other shapes QASR_ERR_UNSUPPORTED.  If a bounded device-side wait gives
+ * up, every id of the call is -1.  The scratch is shared by all calls on one
  * device, so calls that overlap in time on one device race and must be
  * serialised. */
 int qasr_final_norm_lmhead_argmax_noalloc(int32_t *ids_out, float *logits_out, const float *x, const float *norm_w,

@@ -138,6 +138,7 @@ extern "C" {
     pub fn qasr_embed_gather_int8(dst: *mut f32, table: *const i8, scales: *const f32, ids: *const i32, n: c_int, dim: c_int, vocab: i64, bad_id_flag: *mut c_int, stream: *mut c_void) -> c_int;
     pub fn qasr_pre_attn_block(x_norm: *mut f32, x: *const f32, w_in: *const f32, seq: c_int, hidden: c_int, q: *mut f32, k: *const f32, v: *const f32, k_out: *mut f32, q_norm_w: *const f32, k_norm_w: *const f32, n_heads: c_int, n_kv_heads: c_int, head_dim: c_int, eps: f32, cos_tab: *const f32, sin_tab: *const f32, start_pos: c_int, k_cache: *mut f32, v_cache: *mut f32, layer: c_int, max_seq: c_int, stream: *mut c_void) -> c_int;
     pub fn qasr_ln_pe(out: *mut f32, x: *const f32, w: *const f32, b: *const f32, pe: *const f32, rows: c_int, hidden: c_int, n_pos: c_int, eps: f32, stream: *mut c_void) -> c_int;
+    pub fn qasr_ln_pe_gelu_erf(out: *mut f32, x: *const f32, w: *const f32, b: *const f32, pe: *const f32, rows: c_int, hidden: c_int, n_pos: c_int, eps: f32, act: *mut f32, n_act: i64, stream: *mut c_void) -> c_int;
     pub fn qasr_int8_norm_gateup_swiglu(h: *mut f32, x: *const f32, norm_w: *const f32, w_gate_up: *const i8, scales: *const f32, M: c_int, hidden: c_int, inter: c_int, eps: f32, stream: *mut c_void) -> c_int;
     pub fn qasr_int8_matvec_residual(x: *mut f32, a: *const f32, w: *const i8, scales: *const f32, M: c_int, in_dim: c_int, out_dim: c_int, stream: *mut c_void) -> c_int;
     pub fn qasr_final_norm_lmhead_argmax(ids_out: *mut i32, logits_out: *mut f32, x: *const f32, norm_w: *const f32, w: *const i8, scales: *const f32, M: c_int, hidden: c_int, vocab: c_int, eps: f32, stream: *mut c_void) -> c_int;

@@ -10,9 +10,7 @@ import os
 import re
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-# QASR_LIB selects another build of the library (e.g. one compiled with other
-# tuning constants); by default the in-tree one.
-LIB_PATH = os.environ.get("QASR_LIB") or os.path.join(HERE, "libqwenasr_b200.so")
+LIB_PATH = os.path.join(HERE, "libqwenasr_b200.so")
 HEADER = os.path.join(os.path.dirname(HERE), "include", "qwenasr_cuda.h")
 
 QASR_OK = 0
@@ -78,6 +76,7 @@ _SIGS = {
     "qasr_embed_gather_int8": (I, [P, P, P, P, I, I, I64, P, P]),
     "qasr_pre_attn_block": (I, [P, P, P, I, I, P, P, P, P, P, P, I, I, I, F, P, P, I, P, P, I, I, P]),
     "qasr_ln_pe": (I, [P, P, P, P, P, I, I, I, F, P]),
+    "qasr_ln_pe_gelu_erf": (I, [P, P, P, P, P, I, I, I, F, P, I64, P]),
     "qasr_int8_norm_gateup_swiglu": (I, [P, P, P, P, P, I, I, I, F, P]),
     "qasr_int8_matvec_residual": (I, [P, P, P, P, I, I, I, P]),
     "qasr_final_norm_lmhead_argmax": (I, [P, P, P, P, P, P, I, I, I, F, P]),

@@ -73,6 +73,35 @@ QASR_DEV float gelu_tanh_ref(float v) {
   return __fmul_rn(0.5f, __fmul_rn(v, __fadd_rn(1.0f, t)));
 }
 
+// Exact-erf GELU 0.5*x*(1+erf(x/sqrt(2))) (the Metal encoder's activation,
+// encoder_gpu.rs:470), one lane.
+QASR_DEV float gelu_erf_f(float v) {
+  return __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, erff(__fmul_rn(v, 0.70710678118654752f))));
+}
+
+// Exact-erf GELU over n floats in place, for the CTAs [0, n_ctas) of a
+// grid-stride pass: four 16-byte vectors per thread per round, all loaded
+// before any is computed, so each thread keeps 64 bytes in flight.
+QASR_DEV void gelu_erf_pass(float *__restrict__ x, long n, long cta, long n_ctas) {
+  const long nv = n / 4;
+  float4 *x4 = reinterpret_cast<float4 *>(x);
+  const long step = n_ctas * blockDim.x * 4;
+  for (long base = cta * blockDim.x * 4 + threadIdx.x; base < nv; base += step) {
+    float4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (base + (long)u * blockDim.x < nv) v[u] = x4[base + (long)u * blockDim.x];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (base + (long)u * blockDim.x < nv) {
+        float4 w = v[u];
+        w.x = gelu_erf_f(w.x); w.y = gelu_erf_f(w.y); w.z = gelu_erf_f(w.z); w.w = gelu_erf_f(w.w);
+        x4[base + (long)u * blockDim.x] = w;
+      }
+  }
+  if (cta == 0 && threadIdx.x < n - nv * 4) x[nv * 4 + threadIdx.x] = gelu_erf_f(x[nv * 4 + threadIdx.x]);
+}
+
 // Four int8 values packed in a 32-bit word -> four exact floats.  Each byte
 // (sign-flipped to excess-128) is placed in the mantissa of 2^23 with one
 // byte permute; subtracting 2^23+128 recovers the signed value exactly.

@@ -26,10 +26,6 @@ QASR_DEV float gelu_tanh_tail(float val) {
   const float inner = __fmul_rn(0.7978845608028654f, __fadd_rn(val, __fmul_rn(0.044715f, x3)));
   return __fmul_rn(__fmul_rn(0.5f, val), __fadd_rn(1.0f, tanhf(inner)));
 }
-QASR_DEV float gelu_erf_f(float v) {
-  return __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, erff(__fmul_rn(v, 0.70710678118654752f))));
-}
-
 __global__ void gelu_kernel(float *__restrict__ x, long n) {
   const long body = n - n % 8;
   const long nv = body / 4;
@@ -42,15 +38,8 @@ __global__ void gelu_kernel(float *__restrict__ x, long n) {
   if (blockIdx.x == 0 && threadIdx.x < n - body) x[body + threadIdx.x] = gelu_tanh_tail(x[body + threadIdx.x]);
 }
 
-__global__ void gelu_erf_kernel(float *__restrict__ x, long n) {
-  const long nv = n / 4;
-  float4 *x4 = reinterpret_cast<float4 *>(x);
-  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < nv; i += (long)gridDim.x * blockDim.x) {
-    float4 v = x4[i];
-    v.x = gelu_erf_f(v.x); v.y = gelu_erf_f(v.y); v.z = gelu_erf_f(v.z); v.w = gelu_erf_f(v.w);
-    x4[i] = v;
-  }
-  if (blockIdx.x == 0 && threadIdx.x < n - nv * 4) x[nv * 4 + threadIdx.x] = gelu_erf_f(x[nv * 4 + threadIdx.x]);
+__global__ void __launch_bounds__(256) gelu_erf_kernel(float *__restrict__ x, long n) {
+  gelu_erf_pass(x, n, blockIdx.x, gridDim.x);
 }
 
 __global__ void silu_kernel(float *__restrict__ x, long n) {
@@ -165,7 +154,7 @@ extern "C" int qasr_gelu_erf(float *x, int64_t n, void *stream) {
     return QASR_ERR_INVALID;
   }
   if (n == 0) return QASR_OK;
-  gelu_erf_kernel<<<stream_grid(n / 4, 256), 256, 0, S(stream)>>>(x, n);
+  gelu_erf_kernel<<<stream_grid((n / 4 + 3) / 4, 256), 256, 0, S(stream)>>>(x, n);  // 4 vectors per thread
   return launch_status("qasr_gelu_erf");
 }
 

@@ -27,6 +27,8 @@
 //  * the weight prefetch is issued before griddepcontrol.wait.
 // Every mbarrier wait is bounded (tma.cuh); a timeout sets *err and the kernel
 // drains its copies and returns.
+#include <atomic>
+
 #include "common.cuh"
 #include "matvec.cuh"
 #include "qkvpost.cuh"
@@ -404,7 +406,10 @@ int8_mv2_kernel(const __grid_constant__ Mv2Params p) {
     if (last && threadIdx.x < M) {
       __threadfence();
       const unsigned long long k = atomicExch(p.keys + threadIdx.x, 0ull);
-      p.ids[threadIdx.x] = (int32_t)(0xffffffffu - (uint32_t)(k & 0xffffffffull));
+      // a bounded wait that gave up anywhere in the grid leaves the keys
+      // incomplete: report -1 (no token has that id) rather than a plausible id
+      const bool timed_out = p.err && *reinterpret_cast<volatile int *>(p.err) != 0;
+      p.ids[threadIdx.x] = timed_out ? -1 : (int32_t)(0xffffffffu - (uint32_t)(k & 0xffffffffull));
     }
     if (last && threadIdx.x == 0) atomicExch(p.counter, 0u);
   }
@@ -478,13 +483,19 @@ static int launch_t(const Mv2Params &p, cudaStream_t st, bool pdl) {
   while (G > 1 && (U + G - 1) / G > n_rg) --G;
   const int nsl = p.S == 1 ? 1 : 2;
   const size_t smem = mv2_smem_bytes(MT, p.KS, nsl, NORM ? p.K : 0);
-  static bool attr_done = false;
-  if (!attr_done) {
+  // The shared-memory opt-in is a per-device property of the function: track
+  // it per device (bit `dev` of a mask), so a call on a second device of the
+  // same process opts in there too; concurrent first calls both set it.
+  static std::atomic<unsigned long long> attr_done{0ull};
+  int dev = 0;
+  if (int rc = cuda_status(cudaGetDevice(&dev), "int8 matvec: cudaGetDevice")) return rc;
+  const unsigned long long bit = dev >= 0 && dev < 64 ? 1ull << dev : 0ull;
+  if (!bit || !(attr_done.load(std::memory_order_acquire) & bit)) {
     int rc = cuda_status(cudaFuncSetAttribute(int8_mv2_kernel<MT, R, E, NORM, TILED>,
                                               cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024),
                          "int8 matvec: shared memory opt-in");
     if (rc) return rc;
-    attr_done = true;
+    attr_done.fetch_or(bit, std::memory_order_release);
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)G);

@@ -10,12 +10,14 @@
 // scratch in a fixed file-scope __device__ array instead, so a call performs
 // no allocation of any kind.
 //
-// The array holds the keys of at most kNoAllocMaxRows token rows plus one
-// counter.  It is zero when the module loads, the one-time set-up zeroes it
-// again, and every call leaves it at zero when its last CTA finishes, so the
-// next call starts from zero.  Because there is one array per device, calls
-// that overlap in time on one device (two streams, two host threads) race on
-// it and may return wrong ids: serialise them.
+// The array holds the keys of at most kNoAllocMaxRows token rows, one
+// arrival counter and one error word.  Every call first clears it with a
+// 256-byte cudaMemsetAsync on the caller's stream (ordered before the
+// kernel; a memset allocates nothing), so a call never depends on what the
+// previous one left there.  If a bounded wait inside the kernel gives up, the
+// kernel sets the error word and writes -1 as every id.  Because there is one
+// array per device, calls that overlap in time on one device (two streams,
+// two host threads) race on it and may return wrong ids: serialise them.
 #include <cstdint>
 #include <mutex>
 
@@ -26,6 +28,7 @@ namespace qasr {
 
 constexpr int kNoAllocMaxRows = 8;
 constexpr int kNoAllocCounterWord = 16;  // counter at byte 128, after 8 keys (64 B) and padding
+constexpr int kNoAllocErrWord = 17;      // error word at byte 136
 constexpr int kNoAllocWords = 32;        // 256 bytes
 
 static __device__ __align__(256) unsigned long long g_noalloc_scratch[kNoAllocWords];
@@ -36,8 +39,10 @@ struct NoAllocSlot {
 static NoAllocSlot g_noalloc_slots[64];
 static std::mutex g_noalloc_mu;
 
-// Resolve the device address of the array for the current device, once.
-static int noalloc_scratch(unsigned long long **keys, unsigned **counter) {
+// Resolve the device address of the array for the current device, once.  In
+// host code `g_noalloc_scratch` names a host-side stand-in, not device
+// memory, so only the address returned here may be handed to a kernel.
+static int noalloc_scratch(unsigned long long **base) {
   int dev = 0;
   int rc = cuda_status(cudaGetDevice(&dev), "qasr_final_norm_lmhead_argmax_noalloc: cudaGetDevice");
   if (rc) return rc;
@@ -52,12 +57,9 @@ static int noalloc_scratch(unsigned long long **keys, unsigned **counter) {
     rc = cuda_status(cudaGetSymbolAddress(&p, g_noalloc_scratch),
                      "qasr_final_norm_lmhead_argmax_noalloc: cudaGetSymbolAddress");
     if (rc) return rc;
-    rc = cuda_status(cudaMemset(p, 0, sizeof(g_noalloc_scratch)), "qasr_final_norm_lmhead_argmax_noalloc: zero scratch");
-    if (rc) return rc;
     s.base = static_cast<unsigned long long *>(p);
   }
-  *keys = s.base;
-  *counter = reinterpret_cast<unsigned *>(s.base + kNoAllocCounterWord);
+  *base = s.base;
   return QASR_OK;
 }
 
@@ -104,8 +106,15 @@ extern "C" int qasr_final_norm_lmhead_argmax_noalloc(int32_t *ids_out, float *lo
   p.KS = hidden;
   p.KC = 512;
   p.ids = ids_out;
-  int rc = noalloc_scratch(&p.keys, &p.counter);
+  unsigned long long *base = nullptr;
+  int rc = noalloc_scratch(&base);
   if (rc) return rc;
-  rc = mv2_launch(p, MvEpi::Argmax, reinterpret_cast<cudaStream_t>(stream), false);
+  p.keys = base;
+  p.counter = reinterpret_cast<unsigned *>(base + kNoAllocCounterWord);
+  p.err = reinterpret_cast<int *>(base + kNoAllocErrWord);
+  const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  rc = cuda_status(cudaMemsetAsync(base, 0, sizeof(g_noalloc_scratch), st), "qasr_final_norm_lmhead_argmax_noalloc: clear scratch");
+  if (rc) return rc;
+  rc = mv2_launch(p, MvEpi::Argmax, st, false);
   return rc ? rc : launch_status(fn);
 }

@@ -6,6 +6,8 @@
 // All of these are HBM-bound row kernels: each row is read once with 16-byte
 // vector loads into shared memory, reduced in the reference's order by one
 // warp, and written once.
+#include <algorithm>
+
 #include "common.cuh"
 #include "rowops.cuh"
 
@@ -75,6 +77,40 @@ layer_norm_kernel(float *__restrict__ out, const float *__restrict__ x, const fl
     float y = i < body ? fmaf(c, w[i], b[i]) : __fadd_rn(__fmul_rn(c, w[i]), b[i]);
     if (p) y = __fadd_rn(y, p[i]);
     o[i] = y;
+  }
+}
+
+// --------------------------------------------------- LayerNorm+PE and GELU
+// The encoder's elementwise steps in one launch: CTAs [0, ln_ctas) run
+// out = layer_norm(x) + pe[row % n_pos] (one warp per row, the arithmetic of
+// layer_norm_kernel), the remaining CTAs apply exact-erf GELU in place to the
+// FFN activation `act`.  The LayerNorm CTAs are dispatched first, so their
+// per-row reduction latency overlaps the GELU stream instead of forming a
+// launch of its own.
+constexpr int kLnGeluWarps = 8;
+__global__ void __launch_bounds__(kLnGeluWarps * 32)
+ln_pe_gelu_kernel(float *__restrict__ out, const float *__restrict__ x, const float *__restrict__ w,
+                  const float *__restrict__ b, const float *__restrict__ pe, int rows, int hidden, int n_pos,
+                  float eps, float *__restrict__ act, long n_act, int ln_ctas) {
+  if ((int)blockIdx.x >= ln_ctas) {
+    gelu_erf_pass(act, n_act, (long)blockIdx.x - ln_ctas, (long)gridDim.x - ln_ctas);
+    return;
+  }
+  extern __shared__ float smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kLnGeluWarps + warp;
+  if (row >= rows) return;
+  float *xs = smem + (size_t)warp * hidden;
+  warp_load_row(xs, x + (size_t)row * hidden, hidden);
+  float mean, inv;
+  ln_stats_ref(xs, hidden, eps, mean, inv);
+  const int body = hidden - hidden % 8;
+  float *o = out + (size_t)row * hidden;
+  const float *p = pe + (size_t)(row % n_pos) * hidden;
+  for (int i = lane; i < hidden; i += 32) {
+    const float c = __fmul_rn(__fsub_rn(xs[i], mean), inv);
+    const float y = i < body ? fmaf(c, w[i], b[i]) : __fadd_rn(__fmul_rn(c, w[i]), b[i]);
+    o[i] = __fadd_rn(y, p[i]);
   }
 }
 
@@ -329,6 +365,37 @@ extern "C" int qasr_ln_pe(float *out, const float *x, const float *w, const floa
   layer_norm_kernel<<<ceil_div(rows, kRowWarps), kRowWarps * 32, smem, S(stream)>>>(out, x, w, b, pe, rows, hidden,
                                                                                     n_pos, eps);
   return launch_status("qasr_ln_pe");
+}
+
+extern "C" int qasr_ln_pe_gelu_erf(float *out, const float *x, const float *w, const float *b, const float *pe,
+                                   int rows, int hidden, int n_pos, float eps, float *act, int64_t n_act,
+                                   void *stream) {
+  if (!out || !x || !w || !b || !pe || rows < 0 || hidden <= 0 || n_pos <= 0 || n_act < 0 || (n_act > 0 && !act) ||
+      (act && !al16(act))) {
+    set_error("qasr_ln_pe_gelu_erf: invalid arguments (act must be 16-byte aligned)");
+    return QASR_ERR_INVALID;
+  }
+  const size_t smem = (size_t)kLnGeluWarps * hidden * sizeof(float);
+  if (smem > 200 * 1024) {
+    set_error("qasr_ln_pe_gelu_erf: hidden=%d too large", hidden);
+    return QASR_ERR_UNSUPPORTED;
+  }
+  if (rows == 0 && n_act == 0) return QASR_OK;
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0, v = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    sms = v > 0 ? v : 148;
+  }
+  const int ln_ctas = ceil_div(rows, kLnGeluWarps);
+  const long gelu_items = (n_act / 4 + 4 * 256 - 1) / (4 * 256);  // 4 vectors per thread per round
+  const long gelu_ctas = n_act > 0 ? std::max(1l, std::min(gelu_items, (long)sms * 8)) : 0;
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(ln_pe_gelu_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  ln_pe_gelu_kernel<<<(unsigned)(ln_ctas + gelu_ctas), kLnGeluWarps * 32, smem, S(stream)>>>(
+      out, x, w, b, pe, rows, hidden, n_pos, eps, act, n_act, ln_ctas);
+  return launch_status("qasr_ln_pe_gelu_erf");
 }
 
 extern "C" int qasr_compute_rope_neox(float *cos_out, float *sin_out, const int32_t *positions, int seq,

@@ -20,7 +20,7 @@ __all__ = [
     "rms_norm", "rms_norm_per_head", "layer_norm", "compute_rope_neox", "rope_cache_table", "apply_rope_neox",
     "kv_append", "sinusoidal_pe", "gelu", "gelu_erf", "silu", "swiglu_multiply", "add_inplace",
     "linear_nobias_int8", "linear_int8", "causal_attention", "quantize_f32_to_int8", "embed_gather",
-    "pre_attn_block", "ln_pe", "int8_norm_gateup_swiglu", "int8_matvec_residual", "final_norm_lmhead_argmax",
+    "pre_attn_block", "ln_pe", "ln_pe_gelu_erf", "int8_norm_gateup_swiglu", "int8_matvec_residual", "final_norm_lmhead_argmax",
 ]
 
 
@@ -233,6 +233,14 @@ def ln_pe(out, x, weight, bias, pe, rows, hidden, n_pos, eps):
     _lib.call("qasr_ln_pe", _ptr(out, f32, "out", rows * hidden), _ptr(x, f32, "x", rows * hidden),
               _ptr(weight, f32, "weight", hidden), _ptr(bias, f32, "bias", hidden), _ptr(pe, f32, "pe", n_pos * hidden),
               rows, hidden, n_pos, C.c_float(eps), _stream())
+
+
+def ln_pe_gelu_erf(out, x, weight, bias, pe, rows, hidden, n_pos, eps, act, n_act):
+    """LayerNorm + sinusoidal position add (mod.rs:866 + encoder.rs:341-343)
+    and exact-erf GELU in place on the FFN activation, one launch."""
+    _lib.call("qasr_ln_pe_gelu_erf", _ptr(out, f32, "out", rows * hidden), _ptr(x, f32, "x", rows * hidden),
+              _ptr(weight, f32, "weight", hidden), _ptr(bias, f32, "bias", hidden), _ptr(pe, f32, "pe", n_pos * hidden),
+              rows, hidden, n_pos, C.c_float(eps), _ptr(act, f32, "act", n_act), C.c_int64(n_act), _stream())
 
 
 def int8_norm_gateup_swiglu(h, x, norm_w, w_gate_up, scales, M, hidden, inter, eps):

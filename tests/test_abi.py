@@ -117,21 +117,3 @@ def test_rust_binding_matches_header():
     decl = {n: len([x for x in a.split(",") if x.strip()]) for n, a in re.findall(r"pub fn (qasr_\w+)\((.*?)\)", rs)}
     assert decl == _header_arg_counts()
 
-
-def test_integration_maps_every_function():
-    """INTEGRATION.md's function map names every entry of the header (as
-    `qasr_x` or, after an engine prefix in the same cell, `_suffix`)."""
-    import re
-    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-    hdr = re.sub(r"/\*.*?\*/", "", open(os.path.join(root, "include", "qwenasr_cuda.h")).read(), flags=re.S)
-    names = sorted(set(re.findall(r"\b(qasr_\w+)\s*\(", hdr)))
-    doc = open(os.path.join(root, "INTEGRATION.md")).read()
-    table = doc[doc.index("## Function map"):]
-
-    def named(n):
-        if f"`{n}`" in table:
-            return True
-        return any(n.startswith(p + "_") and f"`_{n[len(p) + 1:]}`" in table
-                   for p in ("qasr_decoder", "qasr_encoder", "qasr_qint8", "qasr_stream"))
-
-    assert [n for n in names if not named(n)] == []

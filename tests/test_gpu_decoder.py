@@ -124,25 +124,47 @@ def test_device_step_matches_host_step(orc):
     dec.close()
 
 
+FULL_CASES = {
+    # the benchmarked configuration (0.6B, 28 layers, full vocab, KV 1024) at
+    # the batch sizes whose kernel choices differ (attention CTA width from
+    # M = 4, cluster sizes per M), and the 1.7B decode shape of the
+    # segmented workload (KV around 480)
+    "0.6b_m2": ("DEC_0_6B", 1024, [1023, 600]),
+    "0.6b_m4": ("DEC_0_6B", 1024, [1023, 17, 1023, 700]),
+    "0.6b_m8": ("DEC_0_6B", 1024, [1023, 1023, 600, 1023, 17, 900, 1023, 512]),
+    "1.7b_m8": ("DEC_1_7B", 480, [479, 479, 300, 479, 100, 479, 479, 5]),
+}
+
+
 @pytest.mark.slow
-def test_decode_step_full_0_6b(orc):
-    """All 28 layers and the 151936-row lm head at 0.6B shapes, KV length 1024."""
+@pytest.mark.parametrize("case", list(FULL_CASES))
+def test_decode_step_full_depth(orc, case):
+    """All 28 layers and the 151936-row lm head, sequences at mixed positions:
+    ids identical to the oracle's, logits and the new K/V rows within 2e-3."""
     orc.set_threads(16)
-    cfg = synthetic.DEC_0_6B
-    w, od, dec = build_pair(orc, cfg, seed=2026, max_seq=1024, max_batch=2)
-    rng = np.random.default_rng(5)
-    M = 2
-    positions = np.array([1023, 600], np.int32)
+    name, max_seq, pos = FULL_CASES[case]
+    cfg = getattr(synthetic, name)
+    M = len(pos)
+    w, od, dec = build_pair(orc, cfg, seed=2026 + M, max_seq=max_seq, max_batch=M)
+    rng = np.random.default_rng(5 + M)
+    positions = np.array(pos, np.int32)
     tokens = rng.integers(0, cfg["vocab"], M).astype(np.int32)
-    hist = [prefill_random_kv(dec, od, m, int(positions[m]), rng) for m in range(M)]
     dec.keep_logits(True)
+    hist = []
+    for m in range(M):
+        hist.append(prefill_random_kv(dec, od, m, int(positions[m]), rng))
     nxt = dec.step(tokens, positions)
     logits = dec.logits(M).cpu().numpy()
     for m in range(M):
         kh, vh = hist[m]
-        tok, ref_logits, _ = od.forward(kh, vh, int(positions[m]), w["embed"][tokens[m]], want_logits=True)
-        assert int(nxt[m]) == tok
+        p = int(positions[m])
+        tok, ref_logits, _ = od.forward(kh, vh, p, w["embed"][tokens[m]], want_logits=True)
+        assert int(nxt[m]) == tok, (m, int(nxt[m]), tok)
         assert rel_err(logits[m], ref_logits) < 2e-3
+        kg, vg = dec.kv(m)
+        assert rel_err(kg[:, p].cpu().numpy(), kh[:, p]) < 2e-3
+        assert rel_err(vg[:, p].cpu().numpy(), vh[:, p]) < 2e-3
+        hist[m] = None
     dec.close()
 
 

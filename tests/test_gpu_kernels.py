@@ -189,6 +189,31 @@ def test_ln_pe_config2(orc):
     assert np.array_equal(H(out), ref)
 
 
+@pytest.mark.parametrize("rows,n_act", [(3000, 3000 * 3584), (37, 1001), (0, 4099), (13, 0)])
+def test_ln_pe_gelu_erf_config2(orc, rows, n_act):
+    """The one-launch config-2 pass: LN + PE bit-exact with the oracle, the
+    GELU part bit-identical to qasr_gelu_erf and within 1e-5 of the oracle."""
+    rng = np.random.default_rng(78 + rows)
+    d, npos = 896, 375
+    x = rng.standard_normal((max(rows, 1), d)).astype(np.float32)
+    g = (1 + 0.02 * rng.standard_normal(d)).astype(np.float32)
+    b = (0.02 * rng.standard_normal(d)).astype(np.float32)
+    pe = orc.sinusoidal_pe(npos, d)
+    a = (rng.standard_normal(max(n_act, 1)) * 3).astype(np.float32)
+    out = torch.zeros(max(rows, 1), d, device=DEV)
+    act = T(a)
+    act_sep = T(a)
+    K.ln_pe_gelu_erf(out, T(x), T(g), T(b), T(pe), rows, d, npos, 1e-5, act, n_act)
+    if n_act:
+        K.gelu_erf(act_sep, n_act)
+        assert np.array_equal(H(act)[:n_act], H(act_sep)[:n_act])
+        ok, err = rel_close(H(act)[:n_act], orc.gelu_erf(a[:n_act]), 1e-5)
+        assert ok, err
+    if rows:
+        pe_rows = pe[np.arange(rows) % npos]
+        assert np.array_equal(H(out)[:rows], orc.layer_norm(x[:rows], g, b, 1e-5) + pe_rows)
+
+
 @pytest.mark.parametrize("n", [3000 * 3584, 1003, 8])
 def test_gelu_tanh_reference_form(orc, n):
     rng = np.random.default_rng(n)

@@ -92,8 +92,13 @@ def test_transcribe_matches_oracle(orc, engines, seconds, prompt, force):
         # the whole chain on the CPU
         rows_o = encoder_forward_ref(we, ENC, orc.mel_spectrogram(a))
         ref_o, margins = oracle_decode(od, wd, rows_o, max_new, prompt, force)
+        # The GPU encoder differs from the oracle's by up to 2e-3 relative, so
+        # a step whose oracle top-2 margin is that small may flip; every such
+        # divergence is reported with its margin, never passed silently.
         for s in range(max_new):
             if ids[s] != ref_o[s]:
+                print(f"near-tie divergence at step {s}: gpu id {ids[s]} vs oracle {ref_o[s]}, "
+                      f"smallest top-2 margin so far {min(margins[:s + 1]):.3e} of the logit RMS")
                 assert min(margins[:s + 1]) < 1e-3, (s, ids, ref_o, margins)
                 break
 
