@@ -72,6 +72,8 @@ def parse():
     ap.add_argument("--kv-len", type=int, default=1024)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="decode workload only: skip the configs[4]/[3] transcription objects of the line")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="bounded CPU-baseline sample length")
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--segments", type=int, default=None,
@@ -244,12 +246,14 @@ def run_reference(a):
     value = per_step_seqs / step_s
     sample = (f"{per_step_seqs} of {a.batch} sequences per step, decoded sequentially like transcribe_segment; "
               f"oracle restatement of decoder_forward_int8 on {th} threads of {os.cpu_count()} host cores")
-    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
             "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "int8xf32", "data": "synthetic (seeded random-init weights, random KV history)",
             "impl": "reference",
-            "config": {"workload": "INT8 decode step, 0.6B decoder shapes", "batch_per_gpu": a.batch,
-                       "kv_len": a.kv_len, "parallelism": f"replicas x{a.gpus}"},
+            "hardware": (f"host CPU only: one process (rank 0 of {world}) on {th} threads; the reference has no "
+                         f"GPU path, so this value does not grow with n_gpus"),
+            "config": decode_config(a, cfg, world),
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": th, "kind": "port", "sample": sample},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -259,16 +263,7 @@ def run_reference(a):
 # ------------------------------------------------------------------- ours ----
 def run_ours(a):
     import torch
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    torch.cuda.set_device(local)
-    dist = None
-    if world > 1:
-        import datetime
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
-                                device_id=torch.device(f"cuda:{local}"))
+    rank, local, world, dist = init_dist(600)
     from qwenasr_b200 import kernels as K
     from qwenasr_b200 import synthetic
     from qwenasr_b200.decoder import Decoder
@@ -365,11 +360,7 @@ def run_ours(a):
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
             "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8xf32",
             "data": "synthetic (seeded random-init weights, random KV history)",
-            "config": {"workload": ("INT8 decode step, Qwen3-ASR-0.6B decoder shapes (BASELINE configs[2])"
-                                    if a.model == "0.6b" else "INT8 decode step, Qwen3-ASR-1.7B decoder shapes"),
-                       "batch_per_gpu": M, "kv_len": L, "layers": cfg["n_layers"], "vocab": cfg["vocab"],
-                       "parallelism": f"replicas x{world} (no collective)",
-                       "l2": f"inputs larger than L2: {step_bytes / 1e9:.2f} GB read per step"},
+            "config": decode_config(a, cfg, world),
             "e2e": {"value": world * M / e2e_s, "unit": UNIT, "h2d_bytes_per_step": 2 * 4 * M,
                     "d2h_bytes_per_step": 4 * M + 4},
             "gpu_launches": launches_per_step * a.steps,
@@ -377,7 +368,8 @@ def run_ours(a):
                          "frac": achieved / peak,
                          "traffic": (NCU_TRAFFIC_M8.get(dom)
                                      if (M, L, cfg["n_layers"], a.model) == (8, 1024, 28, "0.6b") else None),
-                         "traffic_source": "ncu capture of this workload (profiles/)", "peak_kind": peak_kind,
+                         "traffic_source": "committed constant (NCU_TRAFFIC_M8) copied from one earlier ncu capture of this "
+                                           "workload (profiles/); not measured by this run", "peak_kind": peak_kind,
                          "bytes_per_launch": cb[dom], "us_per_launch": per_launch_s * 1e6},
             "step_roofline": {"bytes": step_bytes, "achieved_gbs": step_bytes / (ms / 1e3) / 1e9,
                               "frac": step_bytes / (ms / 1e3) / 1e9 / peak},
@@ -387,6 +379,18 @@ def run_ours(a):
     if dist:
         dist.barrier()
     dec.close()
+    del dec
+    torch.cuda.synchronize()
+    if not a.no_extras and a.model == "0.6b" and a.layers == 28:
+        # the transcription configurations, measured in the same run so that
+        # every n_gpus of a scaling run records them
+        # (64 segments split over the GPUs, the partitioned mode) and
+        # configs[3] (one 30 s segment per GPU)
+        seg = measure_transcribe(a, "segments", rank, local, world, dist, 2, 2, None, None, False)
+        e2e4 = measure_transcribe(a, "e2e", rank, local, world, dist, 2, 2, None, None, False)
+        if rank == 0:
+            line["segments_cfg5"] = _sub_line(seg)
+            line["e2e_cfg4"] = _sub_line(e2e4)
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(cfg, L, a.seed, a.cpu_seconds)
     if rank == 0:
@@ -394,6 +398,34 @@ def run_ours(a):
     if dist:
         dist.destroy_process_group()
     return 0
+
+
+def _sub_line(line):
+    keep = ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "scaling", "config",
+            "decode_tokens_per_s", "phase_ms_rank0", "e2e", "roofline", "gpu_launches", "clocks")
+    return {k: line[k] for k in keep if k in line}
+
+
+def decode_config(a, cfg, world):
+    """The `config` of the decode line, shared by both arms."""
+    return {"workload": ("INT8 decode step, Qwen3-ASR-0.6B decoder shapes (BASELINE configs[2])"
+                         if a.model == "0.6b" else "INT8 decode step, Qwen3-ASR-1.7B decoder shapes"),
+            "batch_per_gpu": a.batch, "kv_len": a.kv_len, "layers": cfg["n_layers"], "vocab": cfg["vocab"],
+            "parallelism": f"replicas x{world} (no collective)",
+            "l2": f"inputs larger than L2: "
+                  f"{decode_step_bytes(cfg, [a.kv_len - 1] * a.batch) / 1e9:.2f} GB read per step"}
+
+
+def decode_step_bytes(cfg, positions):
+    """Algorithmic bytes of one decode step (qasr_decoder_step_bytes): every
+    weight, scale and norm once, the lm head, K/V rows 0..pos per sequence."""
+    H, I, hd, L = cfg["hidden"], cfg["inter"], cfg["head_dim"], cfg["n_layers"]
+    q, kv = cfg["n_heads"] * hd, cfg["n_kv_heads"] * hd
+    w_layer = (q + 2 * kv) * H + H * q + 2 * I * H + H * I
+    s_layer = 4 * ((q + 2 * kv) + H + 2 * I + H)
+    n_layer = 4 * (2 * hd + 2 * H)
+    b = L * (w_layer + s_layer + n_layer) + cfg["vocab"] * H + 4 * cfg["vocab"]
+    return b + sum(L * 2 * (p + 1) * kv * 4 for p in positions)
 
 
 # ------------------------------------------------------------ prefill GEMM --
@@ -896,7 +928,9 @@ def cpu_transcribe_baseline(dcfg, ecfg, seconds, new, seed, budget_s):
             "phase_s": {"mel": t_mel, "encoder": t_enc, "prefill_est": t_pre, "decode_est": t_dec}}
 
 
-def run_transcribe(a):
+def init_dist(timeout_s):
+    """One process per GPU (torchrun env); NCCL group for the timing barriers
+    and max-over-ranks reductions only."""
     import torch
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -906,8 +940,26 @@ def run_transcribe(a):
     if world > 1:
         import datetime
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=timeout_s),
                                 device_id=torch.device(f"cuda:{local}"))
+    return rank, local, world, dist
+
+
+def run_transcribe(a):
+    rank, local, world, dist = init_dist(600)
+    line = measure_transcribe(a, a.workload, rank, local, world, dist, a.steps, a.warmup, a.lanes,
+                              a.segments if a.workload == "segments" else None, not a.no_cpu_baseline)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.destroy_process_group()
+    return 0
+
+
+def measure_transcribe(a, workload, rank, local, world, dist, steps, warmup, lanes_opt, segments_opt, with_cpu):
+    """One transcription workload (TRANSCRIBE[workload]) on this rank's share
+    of the segments; returns the JSON line on rank 0 (None elsewhere)."""
+    import torch
     from qwenasr_b200 import kernels as K
     from qwenasr_b200 import synthetic
     from qwenasr_b200.decoder import Decoder
@@ -915,17 +967,15 @@ def run_transcribe(a):
     from qwenasr_b200.segments import segment_range
     from qwenasr_b200.transcribe import prompt_len, transcribe_lanes
 
-    spec = TRANSCRIBE[a.workload]
+    spec = TRANSCRIBE[workload]
     dcfg = dict(getattr(synthetic, spec["dec"]), n_layers=a.layers)
     ecfg = getattr(synthetic, spec["enc"])
-    n_seg = spec.get("segments", spec.get("segments_per_rank", 1) * world)
-    if a.segments and a.workload == "segments":
-        n_seg = a.segments
+    n_seg = segments_opt or spec.get("segments", spec.get("segments_per_rank", 1) * world)
     mine = list(segment_range(n_seg, rank, world))
     new, batch, secs = spec["new"], spec["batch"], spec["seconds"]
     dev = torch.device(f"cuda:{local}")
     # lanes take full batches (qasr_transcribe_lanes): more lanes than batches would idle
-    n_lanes = max(1, min(a.lanes or spec["lanes"], -(-len(mine) // batch)))
+    n_lanes = max(1, min(lanes_opt or spec["lanes"], -(-len(mine) // batch)))
     encs = [Encoder(ecfg, device=local) for _ in range(n_lanes)]
     enc_tokens = encs[0].tokens(K.mel_frames(int(secs * 16000)))
     max_seq = ((prompt_len(enc_tokens) - 1 + new + 63) // 64) * 64
@@ -969,7 +1019,7 @@ def run_transcribe(a):
         if dist:
             dist.barrier()
 
-    for _ in range(max(a.warmup, 3)):
+    for _ in range(max(warmup, 1)):
         one_pass(audio_d)
     st = dec.stream
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -977,19 +1027,19 @@ def run_transcribe(a):
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
         ev0.record(st)
-        for _ in range(a.steps):
+        for _ in range(steps):
             ids = one_pass(audio_d)
         ev1.record(st)
         st.synchronize()
     torch.cuda.synchronize()
     barrier()
-    ms = ev0.elapsed_time(ev1) / a.steps
+    ms = ev0.elapsed_time(ev1) / steps
     # e2e: host samples in (H2D inside the call), host ids out
     barrier()
     t0 = time.perf_counter()
-    for _ in range(a.steps):
+    for _ in range(steps):
         one_pass(audio_h)
-    e2e_ms = (time.perf_counter() - t0) / a.steps * 1e3
+    e2e_ms = (time.perf_counter() - t0) / steps * 1e3
     barrier()
     # phase split on this rank: everything but the decode loop (one token)
     t0 = time.perf_counter()
@@ -1006,15 +1056,15 @@ def run_transcribe(a):
     prof = None
     for _ in range(2):
         prof = dec.profile_step(np.full(len(mid_pos), 198, np.int32), mid_pos)
-    launches = sum(n for _, n in prof.values()) * n_batches * new * a.steps
+    launches = sum(n for _, n in prof.values()) * n_batches * new * steps
     peak, peak_kind = peaks()
     line = None
     if rank == 0:
         audio_s = n_seg * secs
         line = {
             "metric": "audio seconds per second (transcription: log-mel, encoder, prefill, greedy decode)",
-            "value": audio_s / (ms / 1e3), "unit": "audio-s/s", "n_gpus": world, "steps": a.steps,
-            "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": spec["scaling"],
+            "value": audio_s / (ms / 1e3), "unit": "audio-s/s", "n_gpus": world, "steps": steps,
+            "warmup": warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": spec["scaling"],
             "vs_baseline": None, "dtype": "int8xf32 decoder, f32 encoder (int8 digit planes on tcgen05)",
             "data": "synthetic (pink noise + 3 sinusoids at 16 kHz; seeded random-init weights)",
             "config": {"workload": spec["desc"], "segments": n_seg, "seconds_per_segment": secs,
@@ -1047,13 +1097,9 @@ def run_transcribe(a):
     for d, e in lanes:
         d.close()
         e.close()
-    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+    if rank == 0 and world == 1 and with_cpu:
         line["cpu_baseline"] = cpu_transcribe_baseline(dcfg, ecfg, secs, new, a.seed, a.cpu_seconds)
-    if rank == 0:
-        print(json.dumps(line), flush=True)
-    if dist:
-        dist.destroy_process_group()
-    return 0
+    return line
 
 
 def main():

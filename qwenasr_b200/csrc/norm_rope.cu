@@ -181,58 +181,20 @@ __global__ void kv_append_kernel(float *__restrict__ k_cache, float *__restrict_
 }
 
 // --------------------------------------------------- fused pre-attn block
-// One CTA per token row, 16 warps.  Work items: the rms_norm of x (item 0),
-// one item per Q/K head (per-head norm + RoPE, K also appended to the cache),
-// and 8 slices of the V row copy.  head_dim is 128: lane L holds elements
-// 4L..4L+3, lanes 0-15 the first half and lanes 16-31 the second, so the
-// RoPE partner of a lane is lane^16.
-constexpr int kPreWarps = 16;
+// One CTA per token row, 8 warps.  The row's x, q and k are staged in shared
+// memory (q and k as n_heads + n_kv heads of 128 floats, each padded to 129
+// so that lane h of a warp walking head h element by element hits bank
+// (h + d) % 32: the 24 sequential sums run side by side without conflicts)
+// and the V row goes straight to the cache.  Then warp 0 computes the x row's
+// 1/rms in the reference's AVX order (rms_inv_ref) while warp 1 runs one
+// per-head sequential sum per lane (mod.rs:926-929), and finally all threads
+// write x_norm and the normalised, rotated q and k heads (4 elements and
+// their RoPE partners per thread).  Every rounding step is the reference's,
+// so all outputs are bit-exact.
+constexpr int kPreThreads = 256;
+constexpr int kHeadPad = 129;
 
-QASR_DEV void head_norm_rope_128(float *dst, float *dst2, const float *src,
-                                 const float *__restrict__ nw, const float *__restrict__ crow,
-                                 const float *__restrict__ srow, float eps, float *hs) {
-  const int lane = threadIdx.x & 31;
-  float4 v = reinterpret_cast<const float4 *>(src)[lane];
-  reinterpret_cast<float4 *>(hs)[lane] = v;
-  __syncwarp();
-  float inv = 0.0f;
-  if (lane == 0) {
-    float s = 0.0f;
-#pragma unroll 16
-    for (int d = 0; d < 128; ++d) s = __fadd_rn(s, __fmul_rn(hs[d], hs[d]));
-    inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, 128.0f), eps)));
-  }
-  inv = __shfl_sync(0xffffffffu, inv, 0);
-  const float4 w4 = reinterpret_cast<const float4 *>(nw)[lane];
-  v.x = __fmul_rn(__fmul_rn(v.x, inv), w4.x);
-  v.y = __fmul_rn(__fmul_rn(v.y, inv), w4.y);
-  v.z = __fmul_rn(__fmul_rn(v.z, inv), w4.z);
-  v.w = __fmul_rn(__fmul_rn(v.w, inv), w4.w);
-  float4 p;
-  p.x = __shfl_xor_sync(0xffffffffu, v.x, 16);
-  p.y = __shfl_xor_sync(0xffffffffu, v.y, 16);
-  p.z = __shfl_xor_sync(0xffffffffu, v.z, 16);
-  p.w = __shfl_xor_sync(0xffffffffu, v.w, 16);
-  const float4 c = reinterpret_cast<const float4 *>(crow)[lane];
-  const float4 s = reinterpret_cast<const float4 *>(srow)[lane];
-  float4 o;
-  if (lane < 16) {  // x1 = own, x2 = partner: x1*c + (-x2)*s
-    o.x = __fadd_rn(__fmul_rn(v.x, c.x), __fmul_rn(-p.x, s.x));
-    o.y = __fadd_rn(__fmul_rn(v.y, c.y), __fmul_rn(-p.y, s.y));
-    o.z = __fadd_rn(__fmul_rn(v.z, c.z), __fmul_rn(-p.z, s.z));
-    o.w = __fadd_rn(__fmul_rn(v.w, c.w), __fmul_rn(-p.w, s.w));
-  } else {          // x2 = own, x1 = partner: x2*c + x1*s
-    o.x = __fadd_rn(__fmul_rn(v.x, c.x), __fmul_rn(p.x, s.x));
-    o.y = __fadd_rn(__fmul_rn(v.y, c.y), __fmul_rn(p.y, s.y));
-    o.z = __fadd_rn(__fmul_rn(v.z, c.z), __fmul_rn(p.z, s.z));
-    o.w = __fadd_rn(__fmul_rn(v.w, c.w), __fmul_rn(p.w, s.w));
-  }
-  reinterpret_cast<float4 *>(dst)[lane] = o;
-  if (dst2) reinterpret_cast<float4 *>(dst2)[lane] = o;
-  __syncwarp();
-}
-
-__global__ void __launch_bounds__(kPreWarps * 32)
+__global__ void __launch_bounds__(kPreThreads)
 pre_attn_block_kernel(float *__restrict__ x_norm, const float *__restrict__ x, const float *__restrict__ w_in,
                       int hidden, float *__restrict__ q, const float *__restrict__ k, const float *__restrict__ v,
                       float *__restrict__ k_out, const float *__restrict__ q_norm_w,
@@ -240,37 +202,79 @@ pre_attn_block_kernel(float *__restrict__ x_norm, const float *__restrict__ x, c
                       const float *__restrict__ cos_tab, const float *__restrict__ sin_tab, int start_pos,
                       float *__restrict__ k_cache, float *__restrict__ v_cache, int layer, int max_seq) {
   extern __shared__ float smem[];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int s = blockIdx.x;
-  const int pos = start_pos + s;
-  const int q_dim = n_heads * 128, kv_dim = n_kv_heads * 128;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int s = blockIdx.x, pos = start_pos + s;
+  const int q_dim = n_heads * 128, kv_dim = n_kv_heads * 128, n_h = n_heads + n_kv_heads;
+  float *xs = smem;                              // [hidden]
+  float *hs = xs + hidden;                       // [n_h][kHeadPad]
+  float *inv = hs + (size_t)n_h * kHeadPad;      // [0]: x row, [1 + h]: head h
+  const size_t cache_row = ((size_t)layer * max_seq + pos) * kv_dim;
+
+  const float4 *x4 = reinterpret_cast<const float4 *>(x + (size_t)s * hidden);
+  for (int i = tid; i < hidden / 4; i += kPreThreads) reinterpret_cast<float4 *>(xs)[i] = x4[i];
+  const float4 *q4 = reinterpret_cast<const float4 *>(q + (size_t)s * q_dim);
+  const float4 *k4 = reinterpret_cast<const float4 *>(k + (size_t)s * kv_dim);
+  for (int i = tid; i < (q_dim + kv_dim) / 4; i += kPreThreads) {
+    const float4 t = i < q_dim / 4 ? q4[i] : k4[i - q_dim / 4];
+    float *dst = hs + (size_t)(i >> 5) * kHeadPad + ((i & 31) << 2);  // head i/32, element 4*(i%32)
+    dst[0] = t.x;
+    dst[1] = t.y;
+    dst[2] = t.z;
+    dst[3] = t.w;
+  }
+  const float4 *v4 = reinterpret_cast<const float4 *>(v + (size_t)s * kv_dim);
+  float4 *vc4 = reinterpret_cast<float4 *>(v_cache + cache_row);
+  for (int i = tid; i < kv_dim / 4; i += kPreThreads) vc4[i] = v4[i];
+  __syncthreads();
+
+  if (warp == 0) {
+    const float r = rms_inv_ref(xs, hidden, eps);
+    if (lane == 0) inv[0] = r;
+  } else if (warp == 1 && lane < n_h) {
+    const float *hp = hs + (size_t)lane * kHeadPad;
+    float acc = 0.0f;
+#pragma unroll 16
+    for (int d = 0; d < 128; ++d) acc = __fadd_rn(acc, __fmul_rn(hp[d], hp[d]));
+    inv[1 + lane] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(acc, 128.0f), eps)));
+  }
+  __syncthreads();
+
+  const float ix = inv[0];
+  float4 *xo4 = reinterpret_cast<float4 *>(x_norm + (size_t)s * hidden);
+  const float4 *w4 = reinterpret_cast<const float4 *>(w_in);
+  for (int i = tid; i < hidden / 4; i += kPreThreads) {
+    const float4 a = reinterpret_cast<const float4 *>(xs)[i], b = w4[i];
+    xo4[i] = make_float4(__fmul_rn(__fmul_rn(a.x, ix), b.x), __fmul_rn(__fmul_rn(a.y, ix), b.y),
+                         __fmul_rn(__fmul_rn(a.z, ix), b.z), __fmul_rn(__fmul_rn(a.w, ix), b.w));
+  }
   const float *crow = cos_tab + (size_t)pos * 128, *srow = sin_tab + (size_t)pos * 128;
-  float *cache_row_k = k_cache + ((size_t)layer * max_seq + pos) * kv_dim;
-  float *cache_row_v = v_cache + ((size_t)layer * max_seq + pos) * kv_dim;
-  float *hs = smem + hidden + warp * 128;
-  const int n_items = 1 + n_heads + n_kv_heads + 8;
-  for (int it = warp; it < n_items; it += kPreWarps) {
-    if (it == 0) {
-      warp_load_row(smem, x + (size_t)s * hidden, hidden);
-      const float inv = rms_inv_ref(smem, hidden, eps);
-      float *o = x_norm + (size_t)s * hidden;
-      for (int i = lane; i < hidden; i += 32) o[i] = __fmul_rn(__fmul_rn(smem[i], inv), w_in[i]);
-    } else if (it <= n_heads) {
-      const int h = it - 1;
-      float *qh = q + (size_t)s * q_dim + h * 128;
-      head_norm_rope_128(qh, nullptr, qh, q_norm_w, crow, srow, eps, hs);
-    } else if (it <= n_heads + n_kv_heads) {
-      const int h = it - 1 - n_heads;
-      const float *kh = k + (size_t)s * kv_dim + h * 128;
-      float *ko = k_out ? k_out + (size_t)s * kv_dim + h * 128 : nullptr;
-      head_norm_rope_128(cache_row_k + h * 128, ko, kh, k_norm_w, crow, srow, eps, hs);
-    } else {
-      const int part = it - 1 - n_heads - n_kv_heads;  // 8 slices of the V row
-      const int per = kv_dim / 8;                       // floats per slice (multiple of 4)
-      const float4 *src = reinterpret_cast<const float4 *>(v + (size_t)s * kv_dim + part * per);
-      float4 *dst = reinterpret_cast<float4 *>(cache_row_v + part * per);
-      for (int i = lane; i < per / 4; i += 32) dst[i] = src[i];
+  for (int it = tid; it < n_h * 16; it += kPreThreads) {
+    const int h = it >> 4, d = (it & 15) << 2;  // elements d..d+3 and their partners d+64..d+67
+    const float *hp = hs + (size_t)h * kHeadPad;
+    const float ih = inv[1 + h];
+    const float *nw = h < n_heads ? q_norm_w : k_norm_w;
+    float lo[4], hi[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float x1 = __fmul_rn(__fmul_rn(hp[d + j], ih), nw[d + j]);
+      const float x2 = __fmul_rn(__fmul_rn(hp[64 + d + j], ih), nw[64 + d + j]);
+      lo[j] = __fadd_rn(__fmul_rn(x1, crow[d + j]), __fmul_rn(-x2, srow[d + j]));
+      hi[j] = __fadd_rn(__fmul_rn(x2, crow[64 + d + j]), __fmul_rn(x1, srow[64 + d + j]));
     }
+    const float4 l4 = make_float4(lo[0], lo[1], lo[2], lo[3]), h4 = make_float4(hi[0], hi[1], hi[2], hi[3]);
+    float *dst;
+    if (h < n_heads) {
+      dst = q + (size_t)s * q_dim + h * 128;
+    } else {
+      dst = k_cache + cache_row + (h - n_heads) * 128;
+      if (k_out) {
+        float *ko = k_out + (size_t)s * kv_dim + (h - n_heads) * 128;
+        *reinterpret_cast<float4 *>(ko + d) = l4;
+        *reinterpret_cast<float4 *>(ko + 64 + d) = h4;
+      }
+    }
+    *reinterpret_cast<float4 *>(dst + d) = l4;
+    *reinterpret_cast<float4 *>(dst + 64 + d) = h4;
   }
 }
 
@@ -468,15 +472,20 @@ extern "C" int qasr_pre_attn_block(float *x_norm, const float *x, const float *w
     set_error("qasr_pre_attn_block: all vector operands must be 16-byte aligned");
     return QASR_ERR_INVALID;
   }
-  if (head_dim != 128 || (hidden & 3) || ((n_kv_heads * 128 / 8) & 3)) {
-    set_error("qasr_pre_attn_block: head_dim must be 128 (got %d)", head_dim);
+  if (head_dim != 128 || (hidden & 3) || n_heads + n_kv_heads > 32) {
+    set_error("qasr_pre_attn_block: head_dim must be 128 (got %d), hidden a multiple of 4 and at most 32 q+k heads",
+              head_dim);
     return QASR_ERR_UNSUPPORTED;
   }
   if (seq == 0) return QASR_OK;
-  const size_t smem = ((size_t)hidden + kPreWarps * 128) * sizeof(float);
+  const size_t smem = ((size_t)hidden + (size_t)(n_heads + n_kv_heads) * kHeadPad + 33) * sizeof(float);
+  if (smem > 200 * 1024) {
+    set_error("qasr_pre_attn_block: hidden=%d too large", hidden);
+    return QASR_ERR_UNSUPPORTED;
+  }
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(pre_attn_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  pre_attn_block_kernel<<<seq, kPreWarps * 32, smem, S(stream)>>>(x_norm, x, w_in, hidden, q, k, v, k_out, q_norm_w,
+  pre_attn_block_kernel<<<seq, kPreThreads, smem, S(stream)>>>(x_norm, x, w_in, hidden, q, k, v, k_out, q_norm_w,
                                                                   k_norm_w, n_heads, n_kv_heads, eps, cos_tab,
                                                                   sin_tab, start_pos, k_cache, v_cache, layer,
                                                                   max_seq);
