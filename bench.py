@@ -72,6 +72,8 @@ def parse():
     ap.add_argument("--kv-len", type=int, default=1024)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--step-kernel", type=int, choices=(0, 1), default=1,
+                    help="decode step as one persistent kernel (0) or per-layer kernels (1, the default)")
     ap.add_argument("--no-extras", action="store_true",
                     help="decode workload only: skip the configs[4]/[3] transcription objects of the line")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="bounded CPU-baseline sample length")
@@ -172,6 +174,8 @@ def class_bytes(cfg, M, kv_len):
         "gateup": 2 * I * H + 2 * I * f + M * H * f + M * I * f,
         "down": H * I + H * f + M * I * f + 2 * M * H * f,
         "lmhead": cfg["vocab"] * H + cfg["vocab"] * f + M * H * f,
+        # the persistent kernel: the whole step but the embedding gather
+        "step": decode_step_bytes(cfg, [kv_len - 1] * M),
     }
 
 
@@ -272,6 +276,7 @@ def run_ours(a):
     M, L = a.batch, a.kv_len
     dev = torch.device(f"cuda:{local}")
     dec = Decoder(cfg, device=local, max_batch=M, max_seq=L)
+    dec.set_step_kernel(a.step_kernel)
     gen = torch.Generator(device=dev)
     gen.manual_seed(a.seed)
 
@@ -412,6 +417,8 @@ def decode_config(a, cfg, world):
                          if a.model == "0.6b" else "INT8 decode step, Qwen3-ASR-1.7B decoder shapes"),
             "batch_per_gpu": a.batch, "kv_len": a.kv_len, "layers": cfg["n_layers"], "vocab": cfg["vocab"],
             "parallelism": f"replicas x{world} (no collective)",
+            "decode_step": ("one persistent kernel per step" if a.step_kernel == 0
+                            else "per-layer kernels (5 launches per layer)"),
             "l2": f"inputs larger than L2: "
                   f"{decode_step_bytes(cfg, [a.kv_len - 1] * a.batch) / 1e9:.2f} GB read per step"}
 

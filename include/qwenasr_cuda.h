@@ -358,6 +358,27 @@ int qasr_decoder_embed(qasr_decoder *dec, const int32_t *ids, int n, float *out)
 int qasr_decoder_keep_logits(qasr_decoder *dec, int enable);
 const float *qasr_decoder_logits(qasr_decoder *dec);
 
+/* How the engine runs a decode step.  mode 1 (the default): per-layer
+ * kernels (5 launches per layer, replayed as one CUDA graph with
+ * programmatic dependent launch); mode 0: one persistent kernel for the whole
+ * step (every layer, the lm head and the argmax) on every SM, wherever it
+ * covers the shape (up to 8 sequences, 2 query heads per kv head, hidden <=
+ * 2048), else the per-layer kernels.  Same results within the parity bars.
+ * No counterpart in the reference (a CPU engine has no launches to fuse). */
+int qasr_decoder_set_step_kernel(qasr_decoder *dec, int mode);
+/* 0 if a step of M sequences runs as the persistent kernel, 1 if it runs as
+ * per-layer kernels, -1 for bad arguments. */
+int qasr_decoder_step_kernel(const qasr_decoder *dec, int M);
+/* Phase timeline of the persistent kernel: while `stamps` (device memory,
+ * n >= SMs x qasr_decoder_trace_stride values) is set, every step writes
+ * %globaltimer stamps, CTA c at stamps[c * stride + layer * 20 + phase * 4 +
+ * e] for phase 0..4 (q|k|v, attention, o-proj, gate/up, down) and e 0..3
+ * (entry, dependency met, input staged, results published), the lm head as
+ * layer n_layers.  n = 0 turns it off.  For profiling; no counterpart in the
+ * reference. */
+int qasr_decoder_trace(qasr_decoder *dec, unsigned long long *stamps, int64_t n);
+int qasr_decoder_trace_stride(const qasr_decoder *dec);
+
 /* Kernel classes of a decode step, for qasr_decoder_profile_step. */
 #define QASR_K_EMBED 0     /* token embedding gather */
 #define QASR_K_NORM 1      /* input / post-attention / final RMSNorm */
@@ -368,7 +389,8 @@ const float *qasr_decoder_logits(qasr_decoder *dec);
 #define QASR_K_GATEUP 6    /* gate/up INT8 matvec + SwiGLU */
 #define QASR_K_DOWN 7      /* down INT8 matvec + residual */
 #define QASR_K_LMHEAD 8    /* lm head INT8 matvec + argmax */
-#define QASR_K_COUNT 9
+#define QASR_K_STEP 9      /* the persistent kernel: all of the above but the embedding gather */
+#define QASR_K_COUNT 10
 
 /* Run one decode step eagerly (no graph) with CUDA events around every
  * kernel; class_ms[c] receives the summed device time of class c and

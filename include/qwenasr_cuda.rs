@@ -159,6 +159,10 @@ extern "C" {
     pub fn qasr_decoder_device(dec: *const QasrDecoder) -> c_int;
     pub fn qasr_decoder_embed(dec: *mut QasrDecoder, ids: *const i32, n: c_int, out: *mut f32) -> c_int;
     pub fn qasr_decoder_keep_logits(dec: *mut QasrDecoder, enable: c_int) -> c_int;
+    pub fn qasr_decoder_set_step_kernel(dec: *mut QasrDecoder, mode: c_int) -> c_int;
+    pub fn qasr_decoder_step_kernel(dec: *const QasrDecoder, M: c_int) -> c_int;
+    pub fn qasr_decoder_trace(dec: *mut QasrDecoder, stamps: *mut u64, n: i64) -> c_int;
+    pub fn qasr_decoder_trace_stride(dec: *const QasrDecoder) -> c_int;
     pub fn qasr_decoder_logits(dec: *mut QasrDecoder) -> *const f32;
     pub fn qasr_decoder_profile_step(dec: *mut QasrDecoder, tokens: *const i32, positions: *const i32, M: c_int, class_ms: *mut f32, class_launches: *mut c_int, n_classes: c_int) -> c_int;
     pub fn qasr_decoder_step_bytes(dec: *const QasrDecoder, positions: *const i32, M: c_int) -> i64;

@@ -97,6 +97,10 @@ _SIGS = {
     "qasr_decoder_device": (I, [P]),
     "qasr_decoder_embed": (I, [P, P, I, P]),
     "qasr_decoder_keep_logits": (I, [P, I]),
+    "qasr_decoder_set_step_kernel": (I, [P, I]),
+    "qasr_decoder_step_kernel": (I, [P, I]),
+    "qasr_decoder_trace": (I, [P, P, I64]),
+    "qasr_decoder_trace_stride": (I, [P]),
     "qasr_decoder_logits": (P, [P]),
     "qasr_decoder_step_bytes": (I64, [P, P, I]),
     "qasr_decoder_profile_step": (I, [P, P, P, I, P, P, I]),
@@ -168,7 +172,7 @@ _SIGS.update({
     "qasr_transcribe_lanes": (I, [P, P, I, P, P, I, P, I, P, I, I, I, P, I, P]),
 })
 
-KERNEL_CLASSES = ("embed", "norm", "qkv", "qkv_post", "attn", "oproj", "gateup", "down", "lmhead")
+KERNEL_CLASSES = ("embed", "norm", "qkv", "qkv_post", "attn", "oproj", "gateup", "down", "lmhead", "step")
 
 _lib = None
 

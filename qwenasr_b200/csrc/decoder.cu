@@ -32,6 +32,7 @@
 #include "attention.cuh"
 #include "common.cuh"
 #include "matvec.cuh"
+#include "step.cuh"
 #include "umma.cuh"
 
 namespace qasr {
@@ -78,6 +79,18 @@ struct qasr_decoder {
   int32_t *emb_ids = nullptr;  // device ids of qasr_decoder_embed, grown on demand
   int emb_cap = 0;
   std::vector<cudaGraphExec_t> graphs;  // per M (index M), built lazily
+  // the persistent decode-step kernel (decode_step.cu): tensor maps and layer
+  // pointers in device memory, its zeroed scratch block and attention partials
+  int step_kernel = 1;  // 0: the persistent kernel where it covers the shape; 1: per-layer kernels (default)
+  CUtensorMap *step_maps = nullptr;
+  qasr::StepLayerPtrs *step_layers = nullptr;
+  unsigned char *step_scratch = nullptr;
+  qasr::StepScratch step_layout{};
+  float *step_part = nullptr;
+  bool step_dirty = true;  // weights changed since the device tables were written
+  unsigned long long *step_trace = nullptr;  // caller's phase-timeline buffer (qasr_decoder_trace) or null
+  int64_t step_trace_n = 0;
+  CUtensorMap tm_k16, tm_v16;
   std::vector<void *> allocs;
   long seq_stride() const { return (long)cfg.n_layers * cfg.max_seq * cfg.n_kv_heads * cfg.head_dim; }
 };
@@ -212,6 +225,11 @@ extern "C" qasr_decoder *qasr_decoder_create(const qasr_decoder_config *cfg, int
   d->pos = (int32_t *)dalloc(d, 8 * 4, &rc);
   d->next = (int32_t *)dalloc(d, 8 * 4, &rc);
   d->err = (int *)dalloc(d, 16, &rc);
+  d->step_maps = (CUtensorMap *)dalloc(d, (size_t)(3 + 4 * L) * sizeof(CUtensorMap), &rc);
+  d->step_layers = (qasr::StepLayerPtrs *)dalloc(d, (size_t)L * sizeof(qasr::StepLayerPtrs), &rc);
+  d->step_layout = qasr::step_scratch_layout(L, std::max({(long)qkv_rows, (long)H, 2l * I}));
+  d->step_scratch = (unsigned char *)dalloc(d, d->step_layout.total, &rc);
+  d->step_part = (float *)dalloc(d, (size_t)(attn_grid() + qasr::kStepMaxPairs) * 2 * 132 * 4, &rc);
   if (!rc) rc = cuda_status(cudaHostAlloc((void **)&d->h_tok, 4 * 64, cudaHostAllocDefault), "cudaHostAlloc");
   if (rc) {
     qasr_decoder_free(d);
@@ -226,6 +244,9 @@ extern "C" qasr_decoder *qasr_decoder_create(const qasr_decoder_config *cfg, int
   if (!rc) rc = cuda_status(cudaMemsetAsync(d->attn_ctr, 0, (size_t)B * cfg->n_kv_heads * 4, st), "memset");
   if (!rc) rc = attn_make_tensor_map(&d->tm_k, d->k_cache, (long)B * L * cfg->max_seq, kv_dim);
   if (!rc) rc = attn_make_tensor_map(&d->tm_v, d->v_cache, (long)B * L * cfg->max_seq, kv_dim);
+  if (!rc) rc = step_kv_map(&d->tm_k16, d->k_cache, (long)B * L * cfg->max_seq, kv_dim);
+  if (!rc) rc = step_kv_map(&d->tm_v16, d->v_cache, (long)B * L * cfg->max_seq, kv_dim);
+  if (!rc) rc = cuda_status(cudaMemsetAsync(d->step_scratch, 0, d->step_layout.total, st), "memset");
   if (!rc) rc = cuda_status(cudaMemsetAsync(d->am_keys, 0, 64, st), "memset");
   if (!rc) rc = cuda_status(cudaMemsetAsync(d->am_ctr, 0, 16, st), "memset");
   if (!rc) rc = cuda_status(cudaMemsetAsync(d->err, 0, 16, st), "memset");
@@ -277,6 +298,7 @@ extern "C" int qasr_decoder_set_layer(qasr_decoder *d, int layer, const qasr_dec
   if (!rc) rc = copy_in(d, ld.in_norm, w->input_norm, H * 4, "input_norm");
   if (!rc) rc = copy_in(d, ld.post_norm, w->post_attn_norm, H * 4, "post_attn_norm");
   if (!rc) rc = cuda_status(cudaStreamSynchronize(d->stream), "qasr_decoder_set_layer");
+  d->step_dirty = true;
   return rc;
 }
 
@@ -328,6 +350,7 @@ extern "C" int qasr_decoder_set_gate_up(qasr_decoder *d, int layer, const int8_t
   }
   const int rc2 = cuda_status(cudaStreamSynchronize(d->stream), "qasr_decoder_set_gate_up");
   cudaFree(tmp);
+  d->step_dirty = true;
   return rc ? rc : rc2;
 }
 
@@ -369,6 +392,7 @@ extern "C" int qasr_decoder_set_globals(qasr_decoder *d, const void *embed, cons
     rc = umma_weight_map(&d->tm_lm, d->lm_tied ? static_cast<const int8_t *>(d->embed) : d->lm, c.vocab, c.hidden);
   if (!rc) rc = cuda_status(cudaStreamSynchronize(d->stream), "qasr_decoder_set_globals");
   d->globals_ready = rc == QASR_OK;
+  d->step_dirty = true;
   return rc;
 }
 
@@ -406,6 +430,51 @@ extern "C" int qasr_decoder_keep_logits(qasr_decoder *d, int enable) {
 
 extern "C" const float *qasr_decoder_logits(qasr_decoder *d) { return d && d->keep_logits ? d->logits : nullptr; }
 
+static bool step_params(qasr_decoder *d, int M, StepParams *out);
+
+extern "C" int qasr_decoder_set_step_kernel(qasr_decoder *d, int mode) {
+  if (!d || mode < 0 || mode > 1) {
+    set_error("qasr_decoder_set_step_kernel: invalid arguments (mode 0 or 1)");
+    return QASR_ERR_INVALID;
+  }
+  if (mode != d->step_kernel) {
+    cudaSetDevice(d->device);
+    for (auto &g : d->graphs)
+      if (g) {
+        cudaGraphExecDestroy(g);
+        g = nullptr;
+      }
+  }
+  d->step_kernel = mode;
+  return QASR_OK;
+}
+
+extern "C" int qasr_decoder_trace(qasr_decoder *d, unsigned long long *stamps, int64_t n) {
+  if (!d || n < 0) {
+    set_error("qasr_decoder_trace: invalid arguments");
+    return QASR_ERR_INVALID;
+  }
+  cudaSetDevice(d->device);
+  for (auto &g : d->graphs)
+    if (g) {
+      cudaGraphExecDestroy(g);
+      g = nullptr;
+    }
+  d->step_trace = n ? stamps : nullptr;
+  d->step_trace_n = n;
+  return QASR_OK;
+}
+
+extern "C" int qasr_decoder_trace_stride(const qasr_decoder *d) {
+  return d ? step_trace_stride(d->cfg.n_layers) : -1;
+}
+
+extern "C" int qasr_decoder_step_kernel(const qasr_decoder *d, int M) {
+  if (!d || M < 1 || M > d->cfg.max_batch) return -1;
+  StepParams q{};
+  return step_params(const_cast<qasr_decoder *>(d), M, &q) ? 0 : 1;
+}
+
 // Optional per-kernel-class timing of an eager step: events recorded before
 // the first and after every kernel, durations summed per class.
 struct StepMarks {
@@ -426,6 +495,83 @@ struct StepMarks {
 #define MARK(c) \
   if (marks) marks->mark(c)
 
+// Write the persistent kernel's tables (tensor maps, layer pointers) to the
+// device when the weights changed; never inside a stream capture.
+static int step_upload(qasr_decoder *d) {
+  if (!d->step_dirty) return QASR_OK;
+  const qasr_decoder_config &c = d->cfg;
+  std::vector<CUtensorMap> maps((size_t)3 + 4 * c.n_layers);
+  std::vector<StepLayerPtrs> lp((size_t)c.n_layers);
+  maps[0] = d->tm_k16;
+  maps[1] = d->tm_v16;
+  maps[2] = d->tm_lm;
+  for (int l = 0; l < c.n_layers; ++l) {
+    const LayerDev &L = d->layers[l];
+    maps[3 + 4 * l] = L.tm_qkv;
+    maps[4 + 4 * l] = L.tm_o;
+    maps[5 + 4 * l] = L.tm_gu;
+    maps[6 + 4 * l] = L.tm_down;
+    lp[l] = StepLayerPtrs{L.sqkv, L.so, L.sgu, L.sdown, L.q_norm, L.k_norm, L.in_norm, L.post_norm};
+  }
+  int rc = cuda_status(cudaMemcpy(d->step_maps, maps.data(), maps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice),
+                       "decode step tables");
+  if (!rc)
+    rc = cuda_status(cudaMemcpy(d->step_layers, lp.data(), lp.size() * sizeof(StepLayerPtrs), cudaMemcpyHostToDevice),
+                     "decode step tables");
+  if (!rc) d->step_dirty = false;
+  return rc;
+}
+
+// Parameters of the persistent kernel for a step of M sequences; false when
+// the engine uses the per-layer kernels (by choice or because the kernel does
+// not cover the shape).
+static bool step_params(qasr_decoder *d, int M, StepParams *out) {
+  if (d->step_kernel != 0) return false;
+  const qasr_decoder_config &c = d->cfg;
+  StepParams q{};
+  q.maps = d->step_maps;
+  q.layers = d->step_layers;
+  q.final_norm = d->norm;
+  q.lm_s = d->lm_tied ? d->embed_s : d->lm_s;
+  q.x = d->x;
+  q.q_out = d->q_out;
+  q.attn = d->attn;
+  q.h = d->h;
+  q.k_cache = d->k_cache;
+  q.v_cache = d->v_cache;
+  q.seq_stride = d->seq_stride();
+  q.rope_cos = d->rope_cos;
+  q.rope_sin = d->rope_sin;
+  q.pos = d->pos;
+  unsigned char *b = d->step_scratch;
+  const StepScratch &o = d->step_layout;
+  q.sync = reinterpret_cast<unsigned *>(b + o.sync);
+  q.tile_ctr = reinterpret_cast<unsigned *>(b + o.tile_ctr);
+  q.pair_ctr = reinterpret_cast<unsigned *>(b + o.pair_ctr);
+  q.keys = reinterpret_cast<unsigned long long *>(b + o.keys);
+  q.am_ctr = reinterpret_cast<unsigned *>(b + o.am_ctr);
+  q.acc = reinterpret_cast<long long *>(b + o.acc);
+  q.part = d->step_part;
+  q.logits = d->keep_logits ? d->logits : nullptr;
+  q.next = d->next;
+  q.err = d->err;
+  q.trace = d->step_trace && d->step_trace_n >= (int64_t)attn_grid() * step_trace_stride(c.n_layers) ? d->step_trace
+                                                                                                      : nullptr;
+  q.M = M;
+  q.H = c.hidden;
+  q.I = c.inter;
+  q.NQ = c.n_heads;
+  q.NKV = c.n_kv_heads;
+  q.L = c.n_layers;
+  q.V = c.vocab;
+  q.max_seq = c.max_seq;
+  q.eps = c.eps;
+  q.scale = 1.0f / sqrtf((float)c.head_dim);
+  if (step_plan(q, attn_grid()) != QASR_OK) return false;
+  *out = q;
+  return true;
+}
+
 // Enqueue the kernels of one decode step for M sequences on d->stream.
 static int enqueue_step(qasr_decoder *d, int M, StepMarks *marks = nullptr) {
   const qasr_decoder_config &c = d->cfg;
@@ -442,6 +588,14 @@ static int enqueue_step(qasr_decoder *d, int M, StepMarks *marks = nullptr) {
   step_embed_kernel<<<M, 256, 0, st>>>(d->x, emb_tab, d->embed_s, c.embed_is_int8, d->tok, H, c.vocab, d->err);
   MARK(QASR_K_EMBED);
   int rc = launch_status("decode step: embed");
+  StepParams sp;
+  if (!rc && step_params(d, M, &sp)) {
+    // the whole step as one persistent kernel after its scratch is zeroed
+    rc = cuda_status(cudaMemsetAsync(d->step_scratch, 0, d->step_layout.total, st), "decode step: scratch");
+    if (!rc) rc = step_launch(sp, attn_grid(), st);
+    MARK(QASR_K_STEP);
+    return rc;
+  }
   auto mvp = [&](const CUtensorMap &tm, const float *x, long xs, const float *nw, const float *sc, float *y, long ys,
                  int K, int N) {
     UmmaParams p{};
@@ -490,6 +644,7 @@ static int enqueue_step(qasr_decoder *d, int M, StepMarks *marks = nullptr) {
 }
 
 static int run_graph(qasr_decoder *d, int M) {
+  if (int rc = step_upload(d)) return rc;
   if (!d->graphs[M]) {
     cudaGraph_t graph = nullptr;
     int rc = cuda_status(cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
@@ -589,6 +744,7 @@ extern "C" int qasr_decoder_profile_step(qasr_decoder *d, const int32_t *tokens,
   int rc = cuda_status(cudaMemcpyAsync(d->tok, d->h_tok, M * 4, cudaMemcpyHostToDevice, d->stream), "tokens H2D");
   if (!rc) rc = cuda_status(cudaMemcpyAsync(d->pos, d->h_pos, M * 4, cudaMemcpyHostToDevice, d->stream), "pos H2D");
   if (rc) return rc;
+  if ((rc = step_upload(d))) return rc;
   StepMarks marks;
   marks.st = d->stream;
   rc = enqueue_step(d, M, &marks);

@@ -85,6 +85,35 @@ class Decoder:
     def stream(self) -> torch.cuda.ExternalStream:
         return torch.cuda.ExternalStream(_lib.load().qasr_decoder_stream(self._h), device=f"cuda:{self.device}")
 
+    def set_step_kernel(self, mode: int) -> None:
+        """0: the whole step as one persistent kernel where it covers the shape;
+        1: per-layer kernels (the default)."""
+        _lib.call("qasr_decoder_set_step_kernel", self._h, int(mode))
+
+    def step_kernel(self, M: int) -> int:
+        """0 if a step of M sequences runs as the persistent kernel, 1 if per layer."""
+        return int(_lib.load().qasr_decoder_step_kernel(self._h, int(M)))
+
+    def trace_step(self, tokens, positions) -> np.ndarray:
+        """One step through the persistent kernel with its phase timeline on:
+        int64 %globaltimer stamps [CTAs, n_layers + 1, 5 phases, 4 events]
+        (0 where a CTA had no part in a phase); see qasr_decoder_trace."""
+        lib = _lib.load()
+        stride = int(lib.qasr_decoder_trace_stride(self._h))
+        sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+        buf = torch.zeros(sms * stride, dtype=torch.int64, device=f"cuda:{self.device}")
+        _lib.call("qasr_decoder_trace", self._h, C.c_void_p(buf.data_ptr()), C.c_int64(buf.numel()))
+        try:
+            self.step(tokens, positions)
+        finally:
+            _lib.call("qasr_decoder_trace", self._h, None, C.c_int64(0))
+        L = self.cfg["n_layers"]
+        t = buf.cpu().numpy().reshape(sms, stride)
+        out = np.zeros((sms, L + 1, 5, 4), np.int64)
+        out[:, :L] = t[:, :L * 20].reshape(sms, L, 5, 4)
+        out[:, L, 0] = t[:, L * 20:L * 20 + 4]
+        return out
+
     def keep_logits(self, enable: bool = True) -> None:
         _lib.call("qasr_decoder_keep_logits", self._h, 1 if enable else 0)
 

@@ -73,6 +73,34 @@ def test_decode_step_small(orc, M):
     dec.close()
 
 
+@pytest.mark.parametrize("M,positions", [(1, [0]), (2, [0, 1]), (5, [3, 64, 200, 1023, 65]), (8, [1023] * 8)])
+def test_persistent_and_per_layer_steps_agree(orc, M, positions):
+    """The persistent step kernel and the per-layer kernels (the default) give
+    the oracle's ids and logits within 2e-3, at histories from empty to full."""
+    orc.set_threads(8)
+    w, od, dec = build_pair(orc, SMALL, seed=300 + M, max_seq=1100, max_batch=8)
+    assert dec.step_kernel(M) == 1  # the default path is the per-layer kernels
+    rng = np.random.default_rng(40 + M)
+    pos = np.array(positions, np.int32)
+    tokens = rng.integers(0, SMALL["vocab"], M).astype(np.int32)
+    hist = [prefill_random_kv(dec, od, m, int(pos[m]), rng) for m in range(M)]
+    dec.keep_logits(True)
+    results = {}
+    for mode in (0, 1):
+        dec.set_step_kernel(mode)
+        assert dec.step_kernel(M) == mode
+        nxt = dec.step(tokens, pos)
+        results[mode] = (nxt.copy(), dec.logits(M).cpu().numpy().copy())
+    for m in range(M):
+        kh, vh = hist[m]
+        tok, ref_logits, _ = od.forward(kh, vh, int(pos[m]), w["embed"][tokens[m]], want_logits=True)
+        for mode in (0, 1):
+            ids, logits = results[mode]
+            assert int(ids[m]) == tok, (mode, m, int(ids[m]), tok)
+            assert rel_err(logits[m], ref_logits) < 2e-3, mode
+    dec.close()
+
+
 def test_greedy_loop_matches_oracle(orc):
     """Five greedy steps fed back through both engines give the same ids."""
     orc.set_threads(8)
@@ -137,15 +165,18 @@ FULL_CASES = {
 
 
 @pytest.mark.slow
-@pytest.mark.parametrize("case", list(FULL_CASES))
-def test_decode_step_full_depth(orc, case):
+@pytest.mark.parametrize("case,mode", [(c, 1) for c in FULL_CASES] + [("0.6b_m8", 0), ("1.7b_m8", 0)])
+def test_decode_step_full_depth(orc, case, mode):
     """All 28 layers and the 151936-row lm head, sequences at mixed positions:
-    ids identical to the oracle's, logits and the new K/V rows within 2e-3."""
+    ids identical to the oracle's, logits and the new K/V rows within 2e-3
+    (mode 1: the per-layer kernels, mode 0: the persistent step kernel)."""
     orc.set_threads(16)
     name, max_seq, pos = FULL_CASES[case]
     cfg = getattr(synthetic, name)
     M = len(pos)
     w, od, dec = build_pair(orc, cfg, seed=2026 + M, max_seq=max_seq, max_batch=M)
+    dec.set_step_kernel(mode)
+    assert dec.step_kernel(M) == mode
     rng = np.random.default_rng(5 + M)
     positions = np.array(pos, np.int32)
     tokens = rng.integers(0, cfg["vocab"], M).astype(np.int32)
