@@ -205,7 +205,10 @@ int qasr_embed_gather_int8(float *dst, const int8_t *table, const float *scales,
  *   q, k   = apply_rope_neox(q|k, cos/sin rows start_pos..) (mod.rs:1247)
  *   cache rows start_pos.. of layer `layer` <- k, v         (decoder.rs:805-810)
  * q is rotated in place; k_out (may be NULL) receives the rotated k.
- * cos_tab/sin_tab are full RopeCache tables (row = position).  Bit-exact. */
+ * cos_tab/sin_tab are full RopeCache tables (row = position).  Bit-exact.
+ * Shapes: head_dim 128, hidden <= 2048, n_heads + n_kv_heads <= 24 with
+ * n_kv_heads <= 8 (the published models); others return
+ * QASR_ERR_UNSUPPORTED. */
 int qasr_pre_attn_block(float *x_norm, const float *x, const float *w_in, int seq, int hidden, float *q,
                         const float *k, const float *v, float *k_out, const float *q_norm_w, const float *k_norm_w,
                         int n_heads, int n_kv_heads, int head_dim, float eps, const float *cos_tab,

@@ -189,7 +189,7 @@ QASR_DEV void tma_load_2d(float *dst, const CUtensorMap *tm, int x, int y, uint6
 }
 
 template <int G, int W>
-__global__ void __launch_bounds__(W * 32, 1)
+__global__ void __launch_bounds__(W * 32, kAttnCtasPerSm)
 attn_decode_kernel(const __grid_constant__ AttnDecodeParams p) {
   static_assert(W <= kAttnMaxWarps, "warps per CTA");
   extern __shared__ __align__(128) unsigned char smem_raw[];
@@ -518,6 +518,8 @@ int causal_attention_segments(float *out, const float *q, const float *k, const 
   return launch_status("causal attention (segments)");
 }
 
+int attn_decode_grid() { return attn_grid() * kAttnCtasPerSm; }
+
 int attn_grid() {
   static int sms = 0;
   if (!sms) {
@@ -577,7 +579,7 @@ static int attn_launch_t(const AttnDecodeParams &p, cudaStream_t st, bool pdl) {
     attr_done[dev] = true;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)attn_grid());
+  cfg.gridDim = dim3((unsigned)attn_decode_grid());
   cfg.blockDim = dim3(W * 32);
   cfg.dynamicSmemBytes = attn_smem(G, W);
   cfg.stream = st;

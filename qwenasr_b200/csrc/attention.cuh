@@ -14,6 +14,11 @@ namespace qasr {
 #define QASR_ATTN_WIDE_WARPS 6
 #endif
 constexpr int kAttnMaxWarps = 8, kAttnWideWarps = QASR_ATTN_WIDE_WARPS, kAttnWideFromM = 4;
+// Decode-attention CTAs per SM (the grid is this many times the SM count).
+#ifndef QASR_ATTN_CTAS_PER_SM
+#define QASR_ATTN_CTAS_PER_SM 1
+#endif
+constexpr int kAttnCtasPerSm = QASR_ATTN_CTAS_PER_SM;
 #ifndef QASR_ATTN_TILE
 #define QASR_ATTN_TILE 8
 #endif
@@ -68,6 +73,7 @@ int causal_attention_segments(float *out, const float *q, const float *k, const 
 // 2D tensor map over a KV cache [rows, kv_dim] f32 with box [kAttnTile, 128].
 int attn_make_tensor_map(CUtensorMap *tm, const float *base, long rows, int kv_dim);
 int attn_decode_launch(const AttnDecodeParams &p, int group, cudaStream_t st, bool pdl);
-int attn_grid();
+int attn_grid();         // SMs of the current device
+int attn_decode_grid();  // CTAs of one decode-attention launch (size of the partials buffer)
 
 }  // namespace qasr

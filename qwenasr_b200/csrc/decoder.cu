@@ -217,7 +217,8 @@ extern "C" qasr_decoder *qasr_decoder_create(const qasr_decoder_config *cfg, int
   d->attn = (float *)dalloc(d, (size_t)B * q_dim * 4, &rc);
   d->h = (float *)dalloc(d, (size_t)B * I * 4, &rc);
   const int G = cfg->n_heads / cfg->n_kv_heads;
-  d->partials = (float *)dalloc(d, (size_t)(attn_grid() + B * cfg->n_kv_heads) * G * kAttnPartStride * 4, &rc);
+  d->partials =
+      (float *)dalloc(d, (size_t)(attn_decode_grid() + B * cfg->n_kv_heads) * G * kAttnPartStride * 4, &rc);
   d->attn_ctr = (unsigned *)dalloc(d, (size_t)B * cfg->n_kv_heads * 4, &rc);
   d->am_keys = (unsigned long long *)dalloc(d, 8 * 8, &rc);
   d->am_ctr = (unsigned *)dalloc(d, 16, &rc);

@@ -194,6 +194,14 @@ __global__ void kv_append_kernel(float *__restrict__ k_cache, float *__restrict_
 constexpr int kPreThreads = 256;
 constexpr int kHeadPad = 129;
 
+// 16-byte global -> shared copy that completes asynchronously (waited for with
+// cp_async_wait_all before a barrier).
+QASR_DEV void cp_async16(void *dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
+QASR_DEV void cp_async_wait_all() { asm volatile("cp.async.commit_group;\n\tcp.async.wait_all;" ::: "memory"); }
+
 __global__ void __launch_bounds__(kPreThreads)
 pre_attn_block_kernel(float *__restrict__ x_norm, const float *__restrict__ x, const float *__restrict__ w_in,
                       int hidden, float *__restrict__ q, const float *__restrict__ k, const float *__restrict__ v,
@@ -201,32 +209,70 @@ pre_attn_block_kernel(float *__restrict__ x_norm, const float *__restrict__ x, c
                       const float *__restrict__ k_norm_w, int n_heads, int n_kv_heads, float eps,
                       const float *__restrict__ cos_tab, const float *__restrict__ sin_tab, int start_pos,
                       float *__restrict__ k_cache, float *__restrict__ v_cache, int layer, int max_seq) {
-  extern __shared__ float smem[];
+  extern __shared__ __align__(16) float smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int s = blockIdx.x, pos = start_pos + s;
   const int q_dim = n_heads * 128, kv_dim = n_kv_heads * 128, n_h = n_heads + n_kv_heads;
-  float *xs = smem;                              // [hidden]
-  float *hs = xs + hidden;                       // [n_h][kHeadPad]
-  float *inv = hs + (size_t)n_h * kHeadPad;      // [0]: x row, [1 + h]: head h
+  // shared layout: x row | RoPE rows and norm weights (cp.async) | q|k heads (padded) | 1/rms values
+  float *xs = smem;                                // [hidden]
+  float *tab = xs + hidden;                        // cos[128] sin[128] qn[128] kn[128] w_in[hidden]
+  float *hs = tab + 512 + hidden;                  // [n_h][kHeadPad]
+  float *inv = hs + (size_t)n_h * kHeadPad;        // [0]: x row, [1 + h]: head h
   const size_t cache_row = ((size_t)layer * max_seq + pos) * kv_dim;
 
+  // ---- every global read of the row is issued before any of it is used: the
+  // constant rows by cp.async straight into shared memory, the activations
+  // into registers
+  {
+    const float *srcs[4] = {cos_tab + (size_t)pos * 128, sin_tab + (size_t)pos * 128, q_norm_w, k_norm_w};
+    for (int i = tid; i < 128 + hidden / 4; i += kPreThreads) {
+      if (i < 128)
+        cp_async16(tab + 4 * i, srcs[i >> 5] + 4 * (i & 31));
+      else
+        cp_async16(tab + 512 + 4 * (i - 128), w_in + 4 * (i - 128));
+    }
+  }
   const float4 *x4 = reinterpret_cast<const float4 *>(x + (size_t)s * hidden);
-  for (int i = tid; i < hidden / 4; i += kPreThreads) reinterpret_cast<float4 *>(xs)[i] = x4[i];
   const float4 *q4 = reinterpret_cast<const float4 *>(q + (size_t)s * q_dim);
   const float4 *k4 = reinterpret_cast<const float4 *>(k + (size_t)s * kv_dim);
-  for (int i = tid; i < (q_dim + kv_dim) / 4; i += kPreThreads) {
-    const float4 t = i < q_dim / 4 ? q4[i] : k4[i - q_dim / 4];
-    float *dst = hs + (size_t)(i >> 5) * kHeadPad + ((i & 31) << 2);  // head i/32, element 4*(i%32)
-    dst[0] = t.x;
-    dst[1] = t.y;
-    dst[2] = t.z;
-    dst[3] = t.w;
-  }
   const float4 *v4 = reinterpret_cast<const float4 *>(v + (size_t)s * kv_dim);
+  // float4 per thread: x (hidden <= 2048), q|k (<= 3072 floats), v (<= 1024)
+  constexpr int kVx = 2, kVqk = 3;
+  float4 rx[kVx], rqk[kVqk], rv;
+#pragma unroll
+  for (int j = 0; j < kVx; ++j) {
+    const int i = tid + j * kPreThreads;
+    if (i < hidden / 4) rx[j] = x4[i];
+  }
+  if (tid < kv_dim / 4) rv = v4[tid];
+#pragma unroll
+  for (int j = 0; j < kVqk; ++j) {
+    const int i = tid + j * kPreThreads;
+    if (i < (q_dim + kv_dim) / 4) rqk[j] = i < q_dim / 4 ? q4[i] : k4[i - q_dim / 4];
+  }
   float4 *vc4 = reinterpret_cast<float4 *>(v_cache + cache_row);
-  for (int i = tid; i < kv_dim / 4; i += kPreThreads) vc4[i] = v4[i];
+#pragma unroll
+  for (int j = 0; j < kVx; ++j) {
+    const int i = tid + j * kPreThreads;
+    if (i < hidden / 4) reinterpret_cast<float4 *>(xs)[i] = rx[j];
+  }
+  if (tid < kv_dim / 4) vc4[tid] = rv;
+#pragma unroll
+  for (int j = 0; j < kVqk; ++j) {
+    const int i = tid + j * kPreThreads;
+    if (i < (q_dim + kv_dim) / 4) {
+      float *dst = hs + (size_t)(i >> 5) * kHeadPad + ((i & 31) << 2);  // head i/32, element 4*(i%32)
+      dst[0] = rqk[j].x;
+      dst[1] = rqk[j].y;
+      dst[2] = rqk[j].z;
+      dst[3] = rqk[j].w;
+    }
+  }
+  cp_async_wait_all();
   __syncthreads();
 
+  // ---- the sequential sums: warp 0 the x row (rms_inv_ref order), warp 1 one
+  // head per lane (mod.rs:926-929)
   if (warp == 0) {
     const float r = rms_inv_ref(xs, hidden, eps);
     if (lane == 0) inv[0] = r;
@@ -239,20 +285,21 @@ pre_attn_block_kernel(float *__restrict__ x_norm, const float *__restrict__ x, c
   }
   __syncthreads();
 
+  // ---- outputs: x_norm, then the normalised and rotated q and k heads
   const float ix = inv[0];
   float4 *xo4 = reinterpret_cast<float4 *>(x_norm + (size_t)s * hidden);
-  const float4 *w4 = reinterpret_cast<const float4 *>(w_in);
+  const float4 *w4 = reinterpret_cast<const float4 *>(tab + 512);
   for (int i = tid; i < hidden / 4; i += kPreThreads) {
     const float4 a = reinterpret_cast<const float4 *>(xs)[i], b = w4[i];
     xo4[i] = make_float4(__fmul_rn(__fmul_rn(a.x, ix), b.x), __fmul_rn(__fmul_rn(a.y, ix), b.y),
                          __fmul_rn(__fmul_rn(a.z, ix), b.z), __fmul_rn(__fmul_rn(a.w, ix), b.w));
   }
-  const float *crow = cos_tab + (size_t)pos * 128, *srow = sin_tab + (size_t)pos * 128;
+  const float *crow = tab, *srow = tab + 128;
   for (int it = tid; it < n_h * 16; it += kPreThreads) {
     const int h = it >> 4, d = (it & 15) << 2;  // elements d..d+3 and their partners d+64..d+67
     const float *hp = hs + (size_t)h * kHeadPad;
     const float ih = inv[1 + h];
-    const float *nw = h < n_heads ? q_norm_w : k_norm_w;
+    const float *nw = tab + (h < n_heads ? 256 : 384);
     float lo[4], hi[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -472,13 +519,15 @@ extern "C" int qasr_pre_attn_block(float *x_norm, const float *x, const float *w
     set_error("qasr_pre_attn_block: all vector operands must be 16-byte aligned");
     return QASR_ERR_INVALID;
   }
-  if (head_dim != 128 || (hidden & 3) || n_heads + n_kv_heads > 32) {
-    set_error("qasr_pre_attn_block: head_dim must be 128 (got %d), hidden a multiple of 4 and at most 32 q+k heads",
-              head_dim);
+  if (head_dim != 128 || (hidden & 3) || hidden > 2048 || (n_heads + n_kv_heads) * 128 > 3072 ||
+      n_kv_heads * 128 > 1024 || !al16(w_in)) {
+    set_error("qasr_pre_attn_block: head_dim must be 128 (got %d), hidden a multiple of 4 and <= 2048, q+k heads "
+              "<= 24, kv heads <= 8, w_in 16-byte aligned", head_dim);
     return QASR_ERR_UNSUPPORTED;
   }
   if (seq == 0) return QASR_OK;
-  const size_t smem = ((size_t)hidden + (size_t)(n_heads + n_kv_heads) * kHeadPad + 33) * sizeof(float);
+  const size_t smem =
+      ((size_t)2 * hidden + 512 + (size_t)(n_heads + n_kv_heads) * kHeadPad + 33) * sizeof(float);
   if (smem > 200 * 1024) {
     set_error("qasr_pre_attn_block: hidden=%d too large", hidden);
     return QASR_ERR_UNSUPPORTED;
