@@ -54,8 +54,8 @@
 
 namespace qasr {
 
-constexpr int kSWorkerWarps = 8, kSProducerWarp = 8, kSMmaWarp = 9, kSThreads = 320;
-constexpr int kSStage = 16384;     // bytes of a ring stage: one 128x128 weight tile or 16 K + 16 V rows
+constexpr int kSWorkerWarps = 8, kSProducerWarp = 8, kSMmaWarp = 9, kSKvWarp = 10, kSThreads = 352;
+constexpr int kSStage = 16384;     // bytes of a ring stage: one 128x128 weight tile, or 16 K + 16 V rows
 constexpr int kSMaxStages = 12;
 constexpr int kSKeys = 16;         // keys per attention stage
 constexpr int kSSlot = 32 * 128;   // bytes of the digit rows of one K tile
@@ -68,7 +68,9 @@ enum { kQKV = 0, kO = 1, kGU = 2, kDOWN = 3, kLM = 4 };
 constexpr int kBarWorkers = 1, kBarEpi = 2, kBarHead = 3;
 
 struct alignas(16) StepSmem {
-  uint64_t full[kSMaxStages], empty[kSMaxStages];
+  uint64_t full[kSMaxStages], empty[kSMaxStages];    // weight ring
+  uint64_t kfull[kSMaxStages], kempty[kSMaxStages];  // K/V ring
+  int kv_issued;  // K/V ring items issued so far (written by the K/V producer only)
   uint64_t accfull[2], accempty[2];
   uint64_t dready, dfree, mdone;
   uint32_t tmem;
@@ -170,6 +172,20 @@ QASR_DEV bool bar_any(int id, int count, bool pred) {
       : "r"((uint32_t)pred), "r"(id), "r"(count)
       : "memory");
   return r != 0;
+}
+// Bounded wait until the K/V producer has issued ring item `item`.
+QASR_DEV bool s_wait_issued(StepSmem &sm, int item, int *err) {
+  const volatile int *v = reinterpret_cast<const volatile int *>(&sm.kv_issued);
+  if (*v > item) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  while (*v <= item) {
+    if (s_aborted(sm)) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      s_fail(sm, err);
+      return false;
+    }
+  }
+  return true;
 }
 QASR_DEV unsigned ld_acquire(const unsigned *p) {
   unsigned v;
@@ -281,11 +297,6 @@ QASR_DEV const CUtensorMap *phase_map(const StepParams &p, int k, int l) {
   return k == kLM ? p.maps + 2 : p.maps + 3 + 4 * l + k;
 }
 
-// Ring items of one layer for this CTA, by phase.
-QASR_DEV int phase_tiles(const StepParams &p, int k, int c, int G) {
-  const Geo g = step_geo(p, k, G);
-  return unit_count(g, first_unit(g, c, G), G) * g.KC;
-}
 
 // The q|k|v finisher's per-head epilogue (decoder.rs:888-895): q/k per-head
 // RMSNorm (warp-tree sum) + NeoX RoPE at the token's position into q_out or
@@ -423,9 +434,10 @@ __global__ void __launch_bounds__(kSThreads, 1) decode_step_kernel(const __grid_
   extern __shared__ unsigned char smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   unsigned char *base = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
-  const int STG = p.stages;
-  unsigned char *ring = base;
-  unsigned char *dig = ring + (size_t)STG * kSStage;
+  const int STG = p.stages, KSTG = p.kstages;
+  unsigned char *ring = base;                              // weight tiles
+  unsigned char *kring = ring + (size_t)STG * kSStage;     // K/V history tiles
+  unsigned char *dig = kring + (size_t)KSTG * kSStage;
   StepSmem &sm = *reinterpret_cast<StepSmem *>(dig + (size_t)p.slots * kSSlot);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
   const int c = blockIdx.x, G = gridDim.x;
@@ -436,6 +448,8 @@ __global__ void __launch_bounds__(kSThreads, 1) decode_step_kernel(const __grid_
     for (int s = 0; s < kSMaxStages; ++s) {
       mbar_init(&sm.full[s], 1);
       mbar_init(&sm.empty[s], 1);
+      mbar_init(&sm.kfull[s], 1);
+      mbar_init(&sm.kempty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&sm.accfull[b], 1);
@@ -445,6 +459,7 @@ __global__ void __launch_bounds__(kSThreads, 1) decode_step_kernel(const __grid_
     mbar_init(&sm.dfree, 1);
     mbar_init(&sm.mdone, 1);
     sm.abort = 0;
+    sm.kv_issued = 0;
     mbar_fence_init();
     build_att_plan(p, sm, c, G);
   }
@@ -460,10 +475,7 @@ __global__ void __launch_bounds__(kSThreads, 1) decode_step_kernel(const __grid_
   tc_fence_after();
   const uint32_t tmem = sm.tmem;
   // items of one layer in the ring, by phase (the same for every layer)
-  const int n_qkv = phase_tiles(p, kQKV, c, G), n_o = phase_tiles(p, kO, c, G), n_gu = phase_tiles(p, kGU, c, G),
-            n_down = phase_tiles(p, kDOWN, c, G);
-  const int n_att = sm.att_items;
-  const int per_layer = n_qkv + n_att + n_o + n_gu + n_down;
+  const int n_att = sm.att_items;  // K/V stages of one layer
 
   if (warp == kSProducerWarp) {
     // ------------------------------------------------------------ producer
@@ -494,8 +506,21 @@ __global__ void __launch_bounds__(kSThreads, 1) decode_step_kernel(const __grid_
         }
         return true;
       };
-      for (int l = 0; l < p.L && ok; ++l) {
-        ok = push_phase(kQKV, l);
+      for (int l = 0; l < p.L && ok; ++l)
+        ok = push_phase(kQKV, l) && push_phase(kO, l) && push_phase(kGU, l) && push_phase(kDOWN, l);
+      if (ok) push_phase(kLM, 0);
+      // copies still in flight (only after an abort) land before the CTA exits
+      for (int i = max(0, it - STG); i < it; ++i) mbar_wait(&sm.full[i % STG], (unsigned)((i / STG) & 1));
+    }
+  } else if (warp == kSKvWarp) {
+    // ------------------------------------------- K/V history producer
+    // the attention stages of every layer, in the order the workers take them
+    // (round-robin over the warps of each group); its own ring, so the weight
+    // tiles of the phases after attention stream in while attention runs
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int l = 0; l < p.L && ok; ++l)
         for (int gi = 0; gi < sm.ngroups && ok; ++gi) {
           int maxT = 0;
           for (int w = 0; w < kSWorkerWarps; ++w) maxT = max(maxT, sm.wt[gi][w]);
@@ -504,20 +529,21 @@ __global__ void __launch_bounds__(kSThreads, 1) decode_step_kernel(const __grid_
               if (r >= sm.wt[gi][w]) continue;
               const int pr = sm.seg_pair[sm.wseg[gi][w]], m = pr / p.NKV, kvh = pr % p.NKV;
               const int row = (m * p.L + l) * p.max_seq + sm.wa[gi][w] + r * kSKeys;
-              int st;
-              if (!(ok = slot_for(st))) break;
-              unsigned char *dst = ring + (size_t)st * kSStage;
-              mbar_arrive_expect_tx(&sm.full[st], kSStage);
-              s_tma_f32(dst, p.maps + 0, kvh * 128, row, &sm.full[st]);
-              s_tma_f32(dst + kSStage / 2, p.maps + 1, kvh * 128, row, &sm.full[st]);
+              const int st = it % KSTG;
+              if (it >= KSTG && !s_wait(sm, &sm.kempty[st], (unsigned)(((it / KSTG) - 1) & 1), p.err)) ok = false;
+              if (!ok || s_aborted(sm)) {
+                ok = false;
+                break;
+              }
+              unsigned char *dst = kring + (size_t)st * kSStage;
+              mbar_arrive_expect_tx(&sm.kfull[st], kSStage);
+              s_tma_f32(dst, p.maps + 0, kvh * 128, row, &sm.kfull[st]);
+              s_tma_f32(dst + kSStage / 2, p.maps + 1, kvh * 128, row, &sm.kfull[st]);
               ++it;
+              *reinterpret_cast<volatile int *>(&sm.kv_issued) = it;
             }
         }
-        ok = ok && push_phase(kO, l) && push_phase(kGU, l) && push_phase(kDOWN, l);
-      }
-      if (ok) push_phase(kLM, 0);
-      // copies still in flight (only after an abort) land before the CTA exits
-      for (int i = max(0, it - STG); i < it; ++i) mbar_wait(&sm.full[i % STG], (unsigned)((i / STG) & 1));
+      for (int i = max(0, it - KSTG); i < it; ++i) mbar_wait(&sm.kfull[i % KSTG], (unsigned)((i / KSTG) & 1));
     }
   } else if (warp == kSMmaWarp) {
     // ---------------------------------------------------------- MMA issuer
@@ -557,9 +583,7 @@ __global__ void __launch_bounds__(kSThreads, 1) decode_step_kernel(const __grid_
         return true;
       };
       for (int l = 0; l < p.L && ok; ++l) {
-        ok = run_phase(kQKV, l);
-        it += n_att;  // attention stages are the workers'
-        ok = ok && run_phase(kO, l) && run_phase(kGU, l) && run_phase(kDOWN, l);
+        ok = run_phase(kQKV, l) && run_phase(kO, l) && run_phase(kGU, l) && run_phase(kDOWN, l);
       }
       if (ok) run_phase(kLM, 0);
       umma_commit(&sm.mdone);
@@ -567,7 +591,7 @@ __global__ void __launch_bounds__(kSThreads, 1) decode_step_kernel(const __grid_
     }
   } else {
     // -------------------------------------------------------------- workers
-    int it_base = 0, j = 0, sp = 0;
+    int j = 0, sp = 0;
     bool ok = true;
     unsigned long long best[8];
 #pragma unroll
@@ -778,7 +802,7 @@ __global__ void __launch_bounds__(kSThreads, 1) decode_step_kernel(const __grid_
 
     // One layer's attention for this CTA's segments.
     auto attention = [&](int l) -> bool {
-      const int att0 = it_base + n_qkv;  // ring index of this layer's first attention stage
+      const int att0 = l * n_att;  // K/V ring index of this layer's first stage
       s_stamp(p, l, 1, 0);
       for (int gi = 0; gi < sm.ngroups; ++gi) {
         const int seg = sm.wseg[gi][warp];
@@ -817,13 +841,18 @@ __global__ void __launch_bounds__(kSThreads, 1) decode_step_kernel(const __grid_
               }
             const int item = rbase + before;
             rbase += in_round;
-            const int st = item % STG;
-            const bool ready = s_wait(sm, &sm.full[st], (unsigned)((item / STG) & 1), p.err);
+            const int st = item % KSTG;
+            // The warps take the stages round-robin and a warp's next item can
+            // lie more than one lap of the ring ahead; waiting for the item to
+            // be issued first keeps the parity wait within one lap (an mbarrier
+            // parity cannot tell phase n from phase n + 2).
+            const bool ready = s_wait_issued(sm, item, p.err) &&
+                               s_wait(sm, &sm.kfull[st], (unsigned)((item / KSTG) & 1), p.err);
             if (!__all_sync(0xffffffffu, ready)) {
               fail = true;
               break;
             }
-            const float *kt = reinterpret_cast<const float *>(ring + (size_t)st * kSStage);
+            const float *kt = reinterpret_cast<const float *>(kring + (size_t)st * kSStage);
             const float *vt = kt + kSKeys * 128;
             const int nk = min(kSKeys, wb - wa - r * kSKeys);
             float part[32];
@@ -868,7 +897,7 @@ __global__ void __launch_bounds__(kSThreads, 1) decode_step_kernel(const __grid_
               }
             }
             __syncwarp();  // the stage and sp are free
-            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&sm.empty[st])) : "memory");
+            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&sm.kempty[st])) : "memory");
           }
           if (fail) break;
           if (has_new) {
@@ -1019,7 +1048,6 @@ __global__ void __launch_bounds__(kSThreads, 1) decode_step_kernel(const __grid_
         ok = attention(l);
       } else {
         ok = contraction(ph == 0 ? kQKV : ph - 1, l);
-        if (ph == 4) it_base += per_layer;
       }
     }
     if (ok && warp < 4) {
@@ -1090,7 +1118,7 @@ StepScratch step_scratch_layout(int n_layers, long acc_rows) {
 #endif
 constexpr double kStepSplitCost = QASR_STEP_SPLIT_COST;
 
-static size_t step_smem_bytes(int stages, int slots) {
+static size_t step_smem_bytes(int stages, int slots) {  // stages: both rings together
   return 1024 + (size_t)stages * kSStage + (size_t)slots * kSSlot + sizeof(StepSmem);
 }
 
@@ -1136,7 +1164,13 @@ int step_plan(StepParams &p, int grid) {
     set_error("decode step kernel: shared memory");
     return QASR_ERR_UNSUPPORTED;
   }
-  p.stages = stages;
+  // the K/V ring takes up to half of the stages (at least 2 each)
+  if (stages < 4) {
+    set_error("decode step kernel: shared memory");
+    return QASR_ERR_UNSUPPORTED;
+  }
+  p.kstages = std::min(5, stages / 2);
+  p.stages = stages - p.kstages;
   return QASR_OK;
 }
 
@@ -1172,7 +1206,7 @@ int step_launch(const StepParams &p, int grid, cudaStream_t st) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return QASR_ERR_INVALID;
-  const size_t smem = step_smem_bytes(p.stages, p.slots);
+  const size_t smem = step_smem_bytes(p.stages + p.kstages, p.slots);
   if (!attr_done[dev]) {
     int rc = cuda_status(cudaFuncSetAttribute(decode_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               227 * 1024),

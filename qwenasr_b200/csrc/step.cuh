@@ -55,7 +55,7 @@ struct StepParams {
   int M, H, I, NQ, NKV, L, V, max_seq;
   float eps, scale;
   int S[4];                  // K chunks per row tile: q|k|v, o, gate/up, down
-  int stages, slots;         // ring stages of 16 KB, digit tiles of 4 KB
+  int stages, kstages, slots;  // 16 KB stages of the weight and the K/V rings, digit tiles of 4 KB
 };
 
 // Stamps per CTA of the phase timeline: per layer five phases (q|k|v,
