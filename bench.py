@@ -350,8 +350,13 @@ def run_ours(a):
     for _ in range(3):
         prof = dec.profile_step(host_tok, host_pos)
     cb = class_bytes(cfg, M, L)
-    dom = max(prof, key=lambda k: prof[k][0])
-    dom_ms, dom_n = prof[dom]
+    # ---- in-step timing: the graph-replayed step with %globaltimer stamps
+    # (first CTA past its dependency wait .. last CTA exit per launch), the
+    # kernels as they overlap inside the timed region ----
+    in_step = in_step_classes(dec, host_tok, host_pos, cfg["n_layers"]) if a.step_kernel != 0 else None
+    src = in_step if in_step else prof
+    dom = max(src, key=lambda k: src[k][0])
+    dom_ms, dom_n = src[dom]
     per_launch_s = dom_ms / 1e3 / dom_n
     peak, peak_kind = peaks()
     achieved = cb[dom] / per_launch_s / 1e9
@@ -375,10 +380,14 @@ def run_ours(a):
                                      if (M, L, cfg["n_layers"], a.model) == (8, 1024, 28, "0.6b") else None),
                          "traffic_source": "committed constant (NCU_TRAFFIC_M8) copied from one earlier ncu capture of this "
                                            "workload (profiles/); not measured by this run", "peak_kind": peak_kind,
-                         "bytes_per_launch": cb[dom], "us_per_launch": per_launch_s * 1e6},
+                         "bytes_per_launch": cb[dom], "us_per_launch": per_launch_s * 1e6,
+                         "timing": ("in-step: %globaltimer stamps in the graph-replayed step, first CTA past its "
+                                    "dependency wait to last CTA exit, mean over the class's launches"
+                                    if in_step else "eager step, CUDA events around each launch")},
             "step_roofline": {"bytes": step_bytes, "achieved_gbs": step_bytes / (ms / 1e3) / 1e9,
                               "frac": step_bytes / (ms / 1e3) / 1e9 / peak},
             "kernel_ms_per_step": {k: round(v[0], 4) for k, v in prof.items()},
+            "kernel_ms_in_step": ({k: round(v[0], 4) for k, v in in_step.items()} if in_step else None),
             "clocks": clk.summary(),
         }
     if dist:
@@ -403,6 +412,25 @@ def run_ours(a):
     if dist:
         dist.destroy_process_group()
     return 0
+
+
+def in_step_classes(dec, tokens, positions, n_layers, reps=3):
+    """{class: (ms summed over the step's launches, launches)} from the
+    per-launch stamps of a graph-replayed step (Decoder.trace_step); the last
+    of `reps` traced steps (the first re-captures the graph)."""
+    t = None
+    for _ in range(reps):
+        t = dec.trace_step(tokens, positions)
+    names = ("qkv", "attn", "oproj", "gateup", "down")
+    out = {}
+    for i in range(t.shape[0]):
+        k = "lmhead" if i == 5 * n_layers else names[i % 5]
+        s, e = int(t[i, 0]), int(t[i, 1])
+        if e <= s or s == (1 << 64) - 1:
+            return None  # a launch wrote no stamps
+        ms, n = out.get(k, (0.0, 0))
+        out[k] = (ms + (e - s) / 1e6, n + 1)
+    return out
 
 
 def _sub_line(line):

@@ -372,13 +372,19 @@ int qasr_decoder_set_step_kernel(qasr_decoder *dec, int mode);
 /* 0 if a step of M sequences runs as the persistent kernel, 1 if it runs as
  * per-layer kernels, -1 for bad arguments. */
 int qasr_decoder_step_kernel(const qasr_decoder *dec, int M);
-/* Phase timeline of the persistent kernel: while `stamps` (device memory,
- * n >= SMs x qasr_decoder_trace_stride values) is set, every step writes
- * %globaltimer stamps, CTA c at stamps[c * stride + layer * 20 + phase * 4 +
- * e] for phase 0..4 (q|k|v, attention, o-proj, gate/up, down) and e 0..3
- * (entry, dependency met, input staged, results published), the lm head as
- * layer n_layers.  n = 0 turns it off.  For profiling; no counterpart in the
- * reference. */
+/* In-step timeline of the decode step (for profiling; no counterpart in the
+ * reference).  While `stamps` (device memory, n values) is set, every step
+ * writes %globaltimer stamps (ns):
+ *  - per-layer kernels (step kernel mode 1): launch i = 5*layer + {0 q|k|v,
+ *    1 attention, 2 o-proj, 3 gate/up, 4 down}, i = 5*n_layers the lm head;
+ *    stamps[2i] = the earliest CTA past its dependency wait (atomic min: set
+ *    it to all ones first), stamps[2i+1] = the last CTA's exit (atomic max:
+ *    set it to 0 first); needs n >= 2*(5*n_layers + 1);
+ *  - the persistent kernel (mode 0): CTA c writes stamps[c * stride +
+ *    layer * 20 + phase * 4 + e], phase 0..4 as above, e 0..3 (entry,
+ *    dependency met, input staged, results published), the lm head as layer
+ *    n_layers; stride = qasr_decoder_trace_stride, n >= SMs x stride.
+ * n = 0 turns it off.  Changing it re-captures the step graphs. */
 int qasr_decoder_trace(qasr_decoder *dec, unsigned long long *stamps, int64_t n);
 int qasr_decoder_trace_stride(const qasr_decoder *dec);
 

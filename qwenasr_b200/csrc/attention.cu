@@ -309,6 +309,7 @@ attn_decode_kernel(const __grid_constant__ AttnDecodeParams p) {
       // q and the newest K/V rows come from the previous kernel
       pdl_wait();
       pdl_launch_dependents();
+      if (p.tstamp && threadIdx.x == 0) atomicMin(p.tstamp, globaltimer_ns());
     }
     if (lane == 0)
       while (next_issue < T && next_issue < kAttnStages) issue(next_issue++);
@@ -495,6 +496,10 @@ attn_decode_kernel(const __grid_constant__ AttnDecodeParams p) {
   // copies still in flight (only after a timeout) land before the CTA exits
   for (int k2 = waited; k2 < issued; ++k2)
     mbar_wait(&sm.bar[warp][k2 % kAttnStages], (unsigned)((k2 / kAttnStages) & 1));
+  if (p.tstamp) {
+    __syncthreads();
+    if (threadIdx.x == 0) atomicMax(p.tstamp + 1, globaltimer_ns());
+  }
 }
 
 // kernels::causal_attention for n segments in one launch (blockIdx.z):

@@ -57,6 +57,7 @@ struct AttnDecodeParams {
   float *out;            // [M, n_heads*128]
   long out_stride;
   int *err;              // -QASR_ERR_TIMEOUT on a bounded-wait timeout
+  unsigned long long *tstamp;  // optional [2]: first dependency-met and last exit %globaltimer (null = off)
 };
 
 // One segment of a batched causal attention: query rows q_row0 .. q_row0 +

@@ -597,6 +597,11 @@ static int enqueue_step(qasr_decoder *d, int M, StepMarks *marks = nullptr) {
     MARK(QASR_K_STEP);
     return rc;
   }
+  // in-step timeline of the per-layer kernels (qasr_decoder_trace): launch
+  // 5*l + {0 q|k|v, 1 attention, 2 o-proj, 3 gate/up, 4 down}, 5*L the lm head
+  unsigned long long *ts =
+      d->step_trace && d->step_trace_n >= 2 * (5 * (int64_t)c.n_layers + 1) ? d->step_trace : nullptr;
+  auto tslot = [&](int launch) { return ts ? ts + 2 * launch : nullptr; };
   auto mvp = [&](const CUtensorMap &tm, const float *x, long xs, const float *nw, const float *sc, float *y, long ys,
                  int K, int N) {
     UmmaParams p{};
@@ -607,7 +612,11 @@ static int enqueue_step(qasr_decoder *d, int M, StepMarks *marks = nullptr) {
     return p;
   };
   auto mv = [&](const CUtensorMap &tm, const float *x, long xs, const float *nw, const float *sc, float *y, long ys,
-                int K, int N, MvEpi e) { return umma_launch(mvp(tm, x, xs, nw, sc, y, ys, K, N), e, st, true); };
+                int K, int N, MvEpi e, int launch) {
+    UmmaParams p = mvp(tm, x, xs, nw, sc, y, ys, K, N);
+    p.tstamp = tslot(launch);
+    return umma_launch(p, e, st, true);
+  };
   for (int l = 0; l < c.n_layers && !rc; ++l) {
     const LayerDev &L = d->layers[l];
     // input RMSNorm fused into the q|k|v matvec; its epilogue applies the q/k
@@ -618,6 +627,7 @@ static int enqueue_step(qasr_decoder *d, int M, StepMarks *marks = nullptr) {
       p.post.seq_stride = d->seq_stride(); p.post.layer = l; p.post.max_seq = c.max_seq;
       p.post.n_heads = c.n_heads; p.post.n_kv = c.n_kv_heads; p.post.positions = d->pos;
       p.post.q_norm = L.q_norm; p.post.k_norm = L.k_norm; p.post.cos_tab = d->rope_cos; p.post.sin_tab = d->rope_sin;
+      p.tstamp = tslot(5 * l);
       if ((rc = umma_launch(p, MvEpi::QkvPost, st, true))) break;
     }
     MARK(QASR_K_QKV);
@@ -626,20 +636,21 @@ static int enqueue_step(qasr_decoder *d, int M, StepMarks *marks = nullptr) {
     a.q = d->q_out; a.q_stride = q_dim; a.layer = l; a.n_layers = c.n_layers; a.max_seq = c.max_seq;
     a.n_kv_heads = c.n_kv_heads; a.positions = d->pos; a.scale = 1.0f / sqrtf((float)hd); a.M = M;
     a.partials = d->partials; a.counters = d->attn_ctr; a.out = d->attn; a.out_stride = q_dim; a.err = d->err;
+    a.tstamp = tslot(5 * l + 1);
     if ((rc = attn_decode_launch(a, G, st, true))) break;
     MARK(QASR_K_ATTN);
-    if ((rc = mv(L.tm_o, d->attn, q_dim, nullptr, L.so, d->x, H, q_dim, H, MvEpi::Residual))) break;
+    if ((rc = mv(L.tm_o, d->attn, q_dim, nullptr, L.so, d->x, H, q_dim, H, MvEpi::Residual, 5 * l + 2))) break;
     MARK(QASR_K_OPROJ);
     // post-attention RMSNorm fused into the gate/up matvec, SwiGLU in its epilogue
-    if ((rc = mv(L.tm_gu, d->x, H, L.post_norm, L.sgu, d->h, I, H, 2 * I, MvEpi::SwiGLU))) break;
+    if ((rc = mv(L.tm_gu, d->x, H, L.post_norm, L.sgu, d->h, I, H, 2 * I, MvEpi::SwiGLU, 5 * l + 3))) break;
     MARK(QASR_K_GATEUP);
-    if ((rc = mv(L.tm_down, d->h, I, nullptr, L.sdown, d->x, H, I, H, MvEpi::Residual))) break;
+    if ((rc = mv(L.tm_down, d->h, I, nullptr, L.sdown, d->x, H, I, H, MvEpi::Residual, 5 * l + 4))) break;
     MARK(QASR_K_DOWN);
   }
   if (rc) return rc;
   // final RMSNorm fused into the lm head, argmax in its epilogue
   rc = mv(d->tm_lm, d->x, H, d->norm, d->lm_tied ? d->embed_s : d->lm_s, d->keep_logits ? d->logits : nullptr, c.vocab,
-          H, c.vocab, MvEpi::Argmax);
+          H, c.vocab, MvEpi::Argmax, 5 * c.n_layers);
   MARK(QASR_K_LMHEAD);
   return rc;
 }

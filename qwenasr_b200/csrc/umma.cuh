@@ -27,6 +27,8 @@ struct UmmaParams {
   unsigned *counter;         // Argmax: CTA counter, zero on entry, re-armed
   int32_t *ids;              // Argmax: [M]
   int *err;                  // -QASR_ERR_TIMEOUT if a bounded wait gives up (may be null)
+  unsigned long long *tstamp;  // optional [2]: min over CTAs of %globaltimer after the dependency wait,
+                               // max at exit (in-step timing of a graph-replayed step; null = off)
   QkvPostParams post;        // MvEpi::QkvPost (head_ctr unused)
   // filled in by umma_launch
   int stages, csize;

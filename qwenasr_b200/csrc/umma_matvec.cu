@@ -179,6 +179,7 @@ __global__ void __launch_bounds__(kUWarps * 32, 1) int8_umma_kernel(const __grid
 
   pdl_wait();
   pdl_launch_dependents();
+  if (p.tstamp && threadIdx.x == 0) atomicMin(p.tstamp, globaltimer_ns());
 
   // ---- stage x.  Warp m owns token row m: its exponent (after the RMSNorm
   // when NORM), then its three digit rows for every K tile this CTA uses.
@@ -501,6 +502,7 @@ __global__ void __launch_bounds__(kUWarps * 32, 1) int8_umma_kernel(const __grid
     tc_fence_after();
     tmem_dealloc(tmem, kUTmemCols);
   }
+  if (p.tstamp && threadIdx.x == 0) atomicMax(p.tstamp + 1, globaltimer_ns());
 }
 
 // ------------------------------------------------------------------- host --

@@ -95,10 +95,23 @@ class Decoder:
         return int(_lib.load().qasr_decoder_step_kernel(self._h, int(M)))
 
     def trace_step(self, tokens, positions) -> np.ndarray:
-        """One step through the persistent kernel with its phase timeline on:
-        int64 %globaltimer stamps [CTAs, n_layers + 1, 5 phases, 4 events]
-        (0 where a CTA had no part in a phase); see qasr_decoder_trace."""
+        """One step with the in-step timeline on (qasr_decoder_trace).  Per-layer
+        kernels: uint64 [5*n_layers + 1, 2] (first CTA past its dependency
+        wait, last CTA exit) per launch.  Persistent kernel: int64 %globaltimer
+        stamps [CTAs, n_layers + 1, 5 phases, 4 events] (0 where a CTA had no
+        part in a phase)."""
         lib = _lib.load()
+        L = self.cfg["n_layers"]
+        if self.step_kernel(len(tokens)) != 0:
+            n = 2 * (5 * L + 1)
+            buf = torch.zeros(n, dtype=torch.int64, device=f"cuda:{self.device}")
+            buf[0::2] = -1  # all ones: atomic-min slots
+            _lib.call("qasr_decoder_trace", self._h, C.c_void_p(buf.data_ptr()), C.c_int64(n))
+            try:
+                self.step(tokens, positions)
+            finally:
+                _lib.call("qasr_decoder_trace", self._h, None, C.c_int64(0))
+            return buf.cpu().numpy().view(np.uint64).reshape(5 * L + 1, 2)
         stride = int(lib.qasr_decoder_trace_stride(self._h))
         sms = torch.cuda.get_device_properties(self.device).multi_processor_count
         buf = torch.zeros(sms * stride, dtype=torch.int64, device=f"cuda:{self.device}")
@@ -107,7 +120,6 @@ class Decoder:
             self.step(tokens, positions)
         finally:
             _lib.call("qasr_decoder_trace", self._h, None, C.c_int64(0))
-        L = self.cfg["n_layers"]
         t = buf.cpu().numpy().reshape(sms, stride)
         out = np.zeros((sms, L + 1, 5, 4), np.int64)
         out[:, :L] = t[:, :L * 20].reshape(sms, L, 5, 4)

@@ -101,6 +101,35 @@ def test_persistent_and_per_layer_steps_agree(orc, M, positions):
     dec.close()
 
 
+def test_step_timeline_in_both_modes(orc):
+    """qasr_decoder_trace: a traced step gives the untraced step's ids, every
+    per-layer launch stamps a start before its end in launch order, and the
+    persistent kernel stamps every phase of every layer on some CTA."""
+    orc.set_threads(8)
+    w, od, dec = build_pair(orc, SMALL, seed=77, max_seq=300, max_batch=4)
+    rng = np.random.default_rng(77)
+    pos = np.array([5, 120, 250], np.int32)
+    tokens = rng.integers(0, SMALL["vocab"], 3).astype(np.int32)
+    for m in range(3):
+        prefill_random_kv(dec, od, m, int(pos[m]), rng)
+    L = SMALL["n_layers"]
+    ref = dec.step(tokens, pos).copy()
+    t = dec.trace_step(tokens, pos)
+    assert t.shape == (5 * L + 1, 2)
+    start, end = t[:, 0].astype(np.int64), t[:, 1].astype(np.int64)
+    assert (t[:, 0] != np.uint64(2**64 - 1)).all() and (end > start).all()
+    assert (np.diff(start) > 0).all()  # PDL lets a launch start early, never before its predecessor
+    assert (dec.step(tokens, pos) == ref).all()
+    dec.set_step_kernel(0)
+    if dec.step_kernel(3) == 0:
+        p = dec.trace_step(tokens, pos)
+        assert p.shape[1:] == (L + 1, 5, 4)
+        assert (p[:, :L, :, 0].max(axis=0) > 0).all()  # every phase entered by some CTA
+        assert (p[:, L, 0, 0] > 0).any()  # the lm head
+        assert (dec.step(tokens, pos) == ref).all()
+    dec.close()
+
+
 def test_greedy_loop_matches_oracle(orc):
     """Five greedy steps fed back through both engines give the same ids."""
     orc.set_threads(8)
