@@ -353,20 +353,34 @@ attn_decode_kernel(const __grid_constant__ AttnDecodeParams p) {
         const float tot = warp_reduce_scatter<V>(part);
         const bool live = my_key < nk;
         const float sc = live ? __fmul_rn(tot, p.scale) : -INFINITY;
+        // Each lane carries one (head, key) score, the key in lane bits KB ..
+        // KB+LOGK-1, so one xor butterfly over those bits gives every head's
+        // tile maximum and exp-sum at once.  Bits are taken high to low: the
+        // pairing (and so the rounding) of a full-warp butterfly sum.
+        constexpr int LOGK = Log2<KPW>::value, KB = 5 - Log2<V>::value;
+        float hm = sc;
+#pragma unroll
+        for (int b = LOGK - 1; b >= 0; --b) hm = fmaxf(hm, __shfl_xor_sync(0xffffffffu, hm, 1 << (KB + b)));
+        float nmax[G], corr[G], mine = -INFINITY;
 #pragma unroll
         for (int g = 0; g < G; ++g) {
-          // lanes of head g carry its scores; the rest contribute neutral values
-          const float scg = my_g == g ? sc : -INFINITY;
-          const float nmax = fmaxf(mx[g], warp_max(scg));
-          const float corr = mx[g] == -INFINITY ? 0.0f : __expf(__fsub_rn(mx[g], nmax));
-          const float pj = (my_g == g && live) ? __expf(__fsub_rn(sc, nmax)) : 0.0f;
-          sum[g] = __fadd_rn(__fmul_rn(sum[g], corr), warp_sum(writer ? pj : 0.0f));
-          mx[g] = nmax;
-          if (writer && my_g == g) sp[warp][g][my_key] = pj;
-          o[g].x = __fmul_rn(o[g].x, corr);
-          o[g].y = __fmul_rn(o[g].y, corr);
-          o[g].z = __fmul_rn(o[g].z, corr);
-          o[g].w = __fmul_rn(o[g].w, corr);
+          nmax[g] = fmaxf(mx[g], __shfl_sync(0xffffffffu, hm, g << (KB + LOGK)));
+          corr[g] = mx[g] == -INFINITY ? 0.0f : __expf(__fsub_rn(mx[g], nmax[g]));
+          if (my_g == g) mine = nmax[g];
+        }
+        const float pj = live ? __expf(__fsub_rn(sc, mine)) : 0.0f;
+        float ps = pj;
+#pragma unroll
+        for (int b = LOGK - 1; b >= 0; --b) ps = __fadd_rn(ps, __shfl_xor_sync(0xffffffffu, ps, 1 << (KB + b)));
+        if (writer) sp[warp][my_g][my_key] = pj;
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          sum[g] = __fadd_rn(__fmul_rn(sum[g], corr[g]), __shfl_sync(0xffffffffu, ps, g << (KB + LOGK)));
+          mx[g] = nmax[g];
+          o[g].x = __fmul_rn(o[g].x, corr[g]);
+          o[g].y = __fmul_rn(o[g].y, corr[g]);
+          o[g].z = __fmul_rn(o[g].z, corr[g]);
+          o[g].w = __fmul_rn(o[g].w, corr[g]);
         }
         __syncwarp();
 #pragma unroll

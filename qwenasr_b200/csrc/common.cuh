@@ -142,6 +142,28 @@ QASR_DEV uint4 ldg_stream(const void *p) {
 QASR_DEV void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 QASR_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+// Launch with programmatic stream serialization: the grid may be scheduled
+// while the previous kernel of the stream is still running, so its launch
+// and CTA set-up overlap that kernel's tail.  The kernel must call pdl_wait()
+// before its first global-memory access (read or write): that wait returns
+// once the previous grid has completed and its writes are visible, so the
+// stream order of memory effects is unchanged.
+template <typename... Params, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Params>(args)...);
+}
+
 // Warp reduce-scatter: V per-lane partial sums -> one full sum per lane group.
 template <int V>
 struct Log2 {

@@ -92,6 +92,9 @@ __global__ void __launch_bounds__(kLnGeluWarps * 32)
 ln_pe_gelu_kernel(float *__restrict__ out, const float *__restrict__ x, const float *__restrict__ w,
                   const float *__restrict__ b, const float *__restrict__ pe, int rows, int hidden, int n_pos,
                   float eps, float *__restrict__ act, long n_act, int ln_ctas) {
+  // launched with launch_pdl: no memory access before the previous kernel completed
+  pdl_wait();
+  pdl_launch_dependents();
   if ((int)blockIdx.x >= ln_ctas) {
     gelu_erf_pass(act, n_act, (long)blockIdx.x - ln_ctas, (long)gridDim.x - ln_ctas);
     return;
@@ -219,6 +222,10 @@ pre_attn_block_kernel(float *__restrict__ x_norm, const float *__restrict__ x, c
   float *hs = tab + 512 + hidden;                  // [n_h][kHeadPad]
   float *inv = hs + (size_t)n_h * kHeadPad;        // [0]: x row, [1 + h]: head h
   const size_t cache_row = ((size_t)layer * max_seq + pos) * kv_dim;
+  // launched with launch_pdl: nothing is read or written before the previous
+  // kernel of the stream has completed
+  pdl_wait();
+  pdl_launch_dependents();
 
   // ---- every global read of the row is issued before any of it is used: the
   // constant rows by cp.async straight into shared memory, the activations
@@ -444,9 +451,9 @@ extern "C" int qasr_ln_pe_gelu_erf(float *out, const float *x, const float *w, c
   const long gelu_ctas = n_act > 0 ? std::max(1l, std::min(gelu_items, (long)sms * 8)) : 0;
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(ln_pe_gelu_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  ln_pe_gelu_kernel<<<(unsigned)(ln_ctas + gelu_ctas), kLnGeluWarps * 32, smem, S(stream)>>>(
-      out, x, w, b, pe, rows, hidden, n_pos, eps, act, n_act, ln_ctas);
-  return launch_status("qasr_ln_pe_gelu_erf");
+  return cuda_status(launch_pdl(ln_pe_gelu_kernel, dim3((unsigned)(ln_ctas + gelu_ctas)), dim3(kLnGeluWarps * 32), smem,
+                                S(stream), out, x, w, b, pe, rows, hidden, n_pos, eps, act, n_act, ln_ctas),
+                     "qasr_ln_pe_gelu_erf");
 }
 
 extern "C" int qasr_compute_rope_neox(float *cos_out, float *sin_out, const int32_t *positions, int seq,
@@ -534,11 +541,10 @@ extern "C" int qasr_pre_attn_block(float *x_norm, const float *x, const float *w
   }
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(pre_attn_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  pre_attn_block_kernel<<<seq, kPreThreads, smem, S(stream)>>>(x_norm, x, w_in, hidden, q, k, v, k_out, q_norm_w,
-                                                                  k_norm_w, n_heads, n_kv_heads, eps, cos_tab,
-                                                                  sin_tab, start_pos, k_cache, v_cache, layer,
-                                                                  max_seq);
-  return launch_status("qasr_pre_attn_block");
+  return cuda_status(launch_pdl(pre_attn_block_kernel, dim3(seq), dim3(kPreThreads), smem, S(stream), x_norm, x, w_in,
+                                hidden, q, k, v, k_out, q_norm_w, k_norm_w, n_heads, n_kv_heads, eps, cos_tab,
+                                sin_tab, start_pos, k_cache, v_cache, layer, max_seq),
+                     "qasr_pre_attn_block");
 }
 
 extern "C" int qasr_sinusoidal_pe(float *pe, int n_pos, int d_model, void *stream) {
