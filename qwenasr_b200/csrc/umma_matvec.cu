@@ -177,9 +177,28 @@ __global__ void __launch_bounds__(kUWarps * 32, 1) int8_umma_kernel(const __grid
     }
   }
 
+  // Epilogue operands of this thread's first row (warps 0..3: thread = row of
+  // the tile), loaded now so that no dependent load is left on the path from
+  // the accumulator to the output: the row's scale (a constant, fetched before
+  // the dependency wait) and, for the residual epilogue, the residual values.
+  const int ri0 = (warp & 3) * 32 + lane;
+  float sc_next = 0.0f;
+  if (warp < 4 && ntiles > 0 && cid * 128 + ri0 < N) sc_next = __ldg(p.scales + cid * 128 + ri0);
+
   pdl_wait();
   pdl_launch_dependents();
   if (p.tstamp && threadIdx.x == 0) atomicMin(p.tstamp, globaltimer_ns());
+  float res0[8];
+#pragma unroll
+  for (int m = 0; m < 8; ++m) res0[m] = 0.0f;
+  if constexpr (E == MvEpi::Residual) {
+    const int row = cid * 128 + ri0;
+    if (warp < 4 && ntiles > 0 && ri0 / (128 / C) == rank && row < N) {
+#pragma unroll
+      for (int m = 0; m < 8; ++m)
+        if (m < M) res0[m] = p.y[(size_t)m * p.y_stride + row];
+    }
+  }
 
   // ---- stage x.  Warp m owns token row m: its exponent (after the RMSNorm
   // when NORM), then its three digit rows for every K tile this CTA uses.
@@ -403,7 +422,11 @@ __global__ void __launch_bounds__(kUWarps * 32, 1) int8_umma_kernel(const __grid
 
       const int row = t * 128 + ri;
       const bool valid = mine && row < N;
-      const float sc = valid ? p.scales[row] : 0.0f;
+      const float sc = valid ? sc_next : 0.0f;
+      {  // the next tile's scale, in flight during this tile's epilogue
+        const int nrow = (t + ncl) * 128 + ri;
+        sc_next = j + 1 < ntiles && nrow < N ? __ldg(p.scales + nrow) : 0.0f;
+      }
       float yv[8];
 #pragma unroll
       for (int m = 0; m < 8; ++m) yv[m] = m < M ? __fmul_rn(__fmul_rn(__ll2float_rn(V[m]), sm.dq[m]), sc) : 0.0f;
@@ -418,7 +441,7 @@ __global__ void __launch_bounds__(kUWarps * 32, 1) int8_umma_kernel(const __grid
         for (int m = 0; m < 8; ++m)
           if (valid && m < M) {
             float *dst = p.y + (size_t)m * p.y_stride + row;
-            *dst = __fadd_rn(*dst, yv[m]);
+            *dst = __fadd_rn(j == 0 ? res0[m] : *dst, yv[m]);
           }
       } else if constexpr (E == MvEpi::SwiGLU) {
 #pragma unroll
