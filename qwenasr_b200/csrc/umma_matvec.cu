@@ -92,6 +92,16 @@ struct alignas(16) USmem {
   alignas(16) float hs[8][128];  // QkvPost: one head of every token (read as float4)
 };
 
+// QkvPost: the first tile's RoPE rows and norm weights, copied into shared
+// memory (cp.async) before the dependency wait; dynamic shared memory after USmem.
+struct alignas(16) QkvStage {
+  float c[8][128], s[8][128], w[128];
+};
+
+QASR_DEV void cp_async16_g2s(void *dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+
 QASR_DEV bool u_aborted(const USmem &sm) { return *reinterpret_cast<const volatile int *>(&sm.abort) != 0; }
 
 QASR_DEV void u_fail(USmem &sm, int *err) {
@@ -184,6 +194,29 @@ __global__ void __launch_bounds__(kUWarps * 32, 1) int8_umma_kernel(const __grid
   const int ri0 = (warp & 3) * 32 + lane;
   float sc_next = 0.0f;
   if (warp < 4 && ntiles > 0 && cid * 128 + ri0 < N) sc_next = __ldg(p.scales + cid * 128 + ri0);
+  // QkvPost: the first tile's head operands for the two tokens this warp
+  // finishes: positions (uploaded before the step) in registers, RoPE rows and
+  // norm weights copied into shared memory
+  int qpos[2] = {0, 0};
+  QkvStage *qst = reinterpret_cast<QkvStage *>(reinterpret_cast<unsigned char *>(&sm) + sizeof(USmem));
+  if constexpr (E == MvEpi::QkvPost) {
+    const QkvPostParams &q = p.post;
+    const bool rot = cid < q.n_heads + q.n_kv;  // a q or k head: normalised and rotated
+    if (warp < 4 && ntiles > 0 && cid % C == rank) {
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int m = warp + 4 * i;
+        if (m >= M) break;
+        qpos[i] = q.positions[m];
+        if (rot && qpos[i] >= 0 && qpos[i] < q.max_seq) {
+          cp_async16_g2s(&qst->c[m][4 * lane], q.cos_tab + (size_t)qpos[i] * 128 + 4 * lane);
+          cp_async16_g2s(&qst->s[m][4 * lane], q.sin_tab + (size_t)qpos[i] * 128 + 4 * lane);
+        }
+      }
+      if (warp == 0 && rot) cp_async16_g2s(&qst->w[4 * lane], (cid < q.n_heads ? q.q_norm : q.k_norm) + 4 * lane);
+      asm volatile("cp.async.commit_group;" ::: "memory");
+    }
+  }
 
   pdl_wait();
   pdl_launch_dependents();
@@ -466,10 +499,22 @@ __global__ void __launch_bounds__(kUWarps * 32, 1) int8_umma_kernel(const __grid
         if (fin_rank == rank) {
 #pragma unroll
           for (int m = 0; m < 8; ++m) sm.hs[m][ri] = yv[m];
+          if (j == 0) asm volatile("cp.async.wait_all;" ::: "memory");  // this thread's operand copies
           named_bar(2, kUEpiThreads);
-          for (int m = warp; m < M; m += 4) {
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            const int m = warp + 4 * i;
+            if (m >= M) break;
             const float4 hv = reinterpret_cast<const float4 *>(sm.hs[m])[lane];
-            qkv_head_post(p.post, p.eps, t, m, hv, p.err);
+            if (j == 0) {
+              QkvPostOperands op;
+              op.pos = qpos[i];
+              op.c = reinterpret_cast<const float4 *>(qst->c[m])[lane];
+              op.s = reinterpret_cast<const float4 *>(qst->s[m])[lane];
+              op.w = reinterpret_cast<const float4 *>(qst->w)[lane];
+              qkv_head_post(p.post, p.eps, t, m, hv, op, p.err);
+            } else
+              qkv_head_post(p.post, p.eps, t, m, hv, p.err);
           }
           named_bar(2, kUEpiThreads);
         }
@@ -581,10 +626,10 @@ static int umma_sms() {
   return sms[dev];
 }
 
-static size_t umma_smem_bytes(int stages, int C, bool norm, int M, int K) {
+static size_t umma_smem_bytes(int stages, int C, bool norm, int M, int K, bool qkv) {
   const int KC = K / 128 / C;
   return 1024 + (size_t)stages * kUTile + (size_t)KC * kUBSlot + (C > 1 ? 2 * kURed : 0) +
-         (norm ? (size_t)(M + 1) * K * 4 : 0) + sizeof(USmem);
+         (norm ? (size_t)(M + 1) * K * 4 : 0) + sizeof(USmem) + (qkv ? sizeof(QkvStage) : 0);
 }
 
 struct UmmaPlan {
@@ -666,8 +711,8 @@ static UmmaPlan umma_plan(const UmmaParams &p, bool norm) {
     if (KT % C || (C > 8 && state < 2) || 128 % (2 * C) && C > 1) continue;  // even row shares
     if (forced && C != forced) continue;
     int stages = std::min(kUMaxStages, E == MvEpi::SwiGLU ? kUSwigluStages : kUMaxStages);
-    while (stages > 2 && umma_smem_bytes(stages, C, norm, p.M, p.K) > 227 * 1024) --stages;
-    const size_t smem = umma_smem_bytes(stages, C, norm, p.M, p.K);
+    while (stages > 2 && umma_smem_bytes(stages, C, norm, p.M, p.K, E == MvEpi::QkvPost) > 227 * 1024) --stages;
+    const size_t smem = umma_smem_bytes(stages, C, norm, p.M, p.K, E == MvEpi::QkvPost);
     if (smem > 227 * 1024) continue;
     const int resident = C == 1 ? umma_max_clusters<E, NORM>(dev, 1, smem) * 1 : umma_max_clusters<E, NORM>(dev, C, smem);
     if (resident < 1) continue;
@@ -694,7 +739,7 @@ static int umma_launch_t(UmmaParams p, cudaStream_t st, bool pdl) {
   }
   p.csize = plan.C;
   p.stages = plan.stages;
-  const size_t smem = umma_smem_bytes(p.stages, plan.C, NORM, p.M, p.K);
+  const size_t smem = umma_smem_bytes(p.stages, plan.C, NORM, p.M, p.K, E == MvEpi::QkvPost);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(plan.clusters * plan.C));
   cfg.blockDim = dim3(kUWarps * 32);
