@@ -188,6 +188,8 @@ QASR_DEV void tma_load_2d(float *dst, const CUtensorMap *tm, int x, int y, uint6
       : "memory");
 }
 
+constexpr int kMergeRegs = 4;  // partials a cross-CTA merge takes in one round of loads
+
 template <int G, int W>
 __global__ void __launch_bounds__(W * 32, kAttnCtasPerSm)
 attn_decode_kernel(const __grid_constant__ AttnDecodeParams p) {
@@ -468,34 +470,63 @@ attn_decode_kernel(const __grid_constant__ AttnDecodeParams p) {
         const int prs = sm.seg_pair[s], ms = prs / n_kv, kvs = prs % n_kv;
         const long long cf = c_first(s), cl = c_last(s);
         auto part = [&](long long c2) { return p.partials + ((size_t)(c2 + prs) * G + g) * kAttnPartStride; };
-        // max and sum: one partial per lane, then a warp reduction
-        float Mx = -INFINITY;
-        for (long long c2 = cf + lane; c2 <= cl; c2 += 32) Mx = fmaxf(Mx, __ldcg(part(c2) + 128));
-        Mx = warp_max(Mx);
-        float L = 0.0f;
-        for (long long c2 = cf + lane; c2 <= cl; c2 += 32) {
-          const float ms2 = __ldcg(part(c2) + 128);
-          L = __fadd_rn(L, __fmul_rn(__ldcg(part(c2) + 129), ms2 == -INFINITY ? 0.0f : expf(__fsub_rn(ms2, Mx))));
-        }
-        L = warp_sum(L);
-        // the vectors: independent loads, four partials per round
+        float Mx = -INFINITY, L = 0.0f;
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (long long c0 = cf; c0 <= cl; c0 += 4) {
-          float4 ov[4];
-          float f[4];
+        if (cl - cf < kMergeRegs) {
+          // up to kMergeRegs partials (the usual case): every load of the
+          // merge in one round, then max, weights, sum and vector on registers
+          float4 ov[kMergeRegs];
+          float mp[kMergeRegs], lp[kMergeRegs];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const long long c2 = min(c0 + u, cl);
-            ov[u] = __ldcg(reinterpret_cast<const float4 *>(part(c2)) + lane);
-            const float ms2 = __ldcg(part(c2) + 128);
-            f[u] = (c0 + u > cl || ms2 == -INFINITY) ? 0.0f : expf(__fsub_rn(ms2, Mx));
+          for (int u = 0; u < kMergeRegs; ++u) {
+            ov[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+            mp[u] = -INFINITY;
+            lp[u] = 0.0f;
+            if (cf + u <= cl) {
+              ov[u] = __ldcg(reinterpret_cast<const float4 *>(part(cf + u)) + lane);
+              mp[u] = __ldcg(part(cf + u) + 128);
+              lp[u] = __ldcg(part(cf + u) + 129);
+            }
           }
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            acc.x = fmaf(ov[u].x, f[u], acc.x);
-            acc.y = fmaf(ov[u].y, f[u], acc.y);
-            acc.z = fmaf(ov[u].z, f[u], acc.z);
-            acc.w = fmaf(ov[u].w, f[u], acc.w);
+          for (int u = 0; u < kMergeRegs; ++u)
+            if (cf + u <= cl) Mx = fmaxf(Mx, mp[u]);
+#pragma unroll
+          for (int u = 0; u < kMergeRegs; ++u) {
+            const float f = (cf + u > cl || mp[u] == -INFINITY) ? 0.0f : expf(__fsub_rn(mp[u], Mx));
+            L = __fadd_rn(L, __fmul_rn(lp[u], f));
+            acc.x = fmaf(ov[u].x, f, acc.x);
+            acc.y = fmaf(ov[u].y, f, acc.y);
+            acc.z = fmaf(ov[u].z, f, acc.z);
+            acc.w = fmaf(ov[u].w, f, acc.w);
+          }
+        } else {
+          // max and sum: one partial per lane, then a warp reduction
+          for (long long c2 = cf + lane; c2 <= cl; c2 += 32) Mx = fmaxf(Mx, __ldcg(part(c2) + 128));
+          Mx = warp_max(Mx);
+          for (long long c2 = cf + lane; c2 <= cl; c2 += 32) {
+            const float ms2 = __ldcg(part(c2) + 128);
+            L = __fadd_rn(L, __fmul_rn(__ldcg(part(c2) + 129), ms2 == -INFINITY ? 0.0f : expf(__fsub_rn(ms2, Mx))));
+          }
+          L = warp_sum(L);
+          // the vectors: independent loads, four partials per round
+          for (long long c0 = cf; c0 <= cl; c0 += 4) {
+            float4 ov[4];
+            float f[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const long long c2 = min(c0 + u, cl);
+              ov[u] = __ldcg(reinterpret_cast<const float4 *>(part(c2)) + lane);
+              const float ms2 = __ldcg(part(c2) + 128);
+              f[u] = (c0 + u > cl || ms2 == -INFINITY) ? 0.0f : expf(__fsub_rn(ms2, Mx));
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              acc.x = fmaf(ov[u].x, f[u], acc.x);
+              acc.y = fmaf(ov[u].y, f[u], acc.y);
+              acc.z = fmaf(ov[u].z, f[u], acc.z);
+              acc.w = fmaf(ov[u].w, f[u], acc.w);
+            }
           }
         }
         const float inv = __fdiv_rn(1.0f, L);
