@@ -165,7 +165,9 @@ causal_attention_kernel(float *__restrict__ out, const float *__restrict__ q, co
 // ring of 8-key K and V tiles (2D TMA, box 8 rows x one 128-float head slice,
 // no multicast), scores its keys for both query heads of the GQA group (each
 // K/V byte is read from HBM once and used twice) and keeps an online-softmax
-// state.  The CTA then merges the warps of each segment; a pair split over
+// state whose maximum is raised only when a score exceeds it by more than 8
+// (the common tile pays no rescale), with the tile's V rows loaded while its
+// scores are reduced.  The CTA then merges the warps of each segment; a pair split over
 // several CTAs is merged by the last one to finish (counter + threadfence,
 // partials in CTA order: deterministic).  History tiles are fetched before
 // griddepcontrol.wait; only a tile holding the pair's newest row (appended by
@@ -200,7 +202,6 @@ attn_decode_kernel(const __grid_constant__ AttnDecodeParams p) {
   float *tiles = reinterpret_cast<float *>(smem_raw);
   float *slots = tiles + (size_t)W * kAttnStages * 2 * TILE_F;  // [warp][G][kAttnPartStride]
   AttnSmall &sm = *reinterpret_cast<AttnSmall *>(slots + (size_t)W * G * kAttnPartStride);
-  __shared__ float sp[W][G][KPW];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_kv = p.n_kv_heads, n_pairs = p.M * n_kv;
@@ -352,61 +353,70 @@ attn_decode_kernel(const __grid_constant__ AttnDecodeParams p) {
             part[g * KPW + j] = d;
           }
         }
+        // the V rows do not depend on the scores: in flight during the softmax
+        float4 vr[KPW];
+#pragma unroll
+        for (int j = 0; j < KPW; ++j) {
+          vr[j] = *reinterpret_cast<const float4 *>(vt + (size_t)j * 128 + 4 * lane);
+          if (j >= nk) vr[j] = make_float4(0.f, 0.f, 0.f, 0.f);  // rows past the range may hold anything
+        }
         const float tot = warp_reduce_scatter<V>(part);
         const bool live = my_key < nk;
         const float sc = live ? __fmul_rn(tot, p.scale) : -INFINITY;
         // Each lane carries one (head, key) score, the key in lane bits KB ..
-        // KB+LOGK-1, so one xor butterfly over those bits gives every head's
-        // tile maximum and exp-sum at once.  Bits are taken high to low: the
-        // pairing (and so the rounding) of a full-warp butterfly sum.
+        // KB+LOGK-1 (lane (g*KPW + j) << KB holds head g, key j).
         constexpr int LOGK = Log2<KPW>::value, KB = 5 - Log2<V>::value;
-        float hm = sc;
+        float mine = -INFINITY;
 #pragma unroll
-        for (int b = LOGK - 1; b >= 0; --b) hm = fmaxf(hm, __shfl_xor_sync(0xffffffffu, hm, 1 << (KB + b)));
-        float nmax[G], corr[G], mine = -INFINITY;
+        for (int g = 0; g < G; ++g)
+          if (my_g == g) mine = mx[g];
+        // Online softmax with a lazy maximum: while no score exceeds its
+        // head's running maximum by more than 8 (e^8 bounds the terms), the
+        // maximum, the sums and the output keep their scale; only a tile that
+        // does raise it pays for the tile maximum and the rescale.
+        if (__any_sync(0xffffffffu, live && sc > __fadd_rn(mine, 8.0f))) {
+          float hm = sc;
 #pragma unroll
-        for (int g = 0; g < G; ++g) {
-          nmax[g] = fmaxf(mx[g], __shfl_sync(0xffffffffu, hm, g << (KB + LOGK)));
-          corr[g] = mx[g] == -INFINITY ? 0.0f : __expf(__fsub_rn(mx[g], nmax[g]));
-          if (my_g == g) mine = nmax[g];
+          for (int b = LOGK - 1; b >= 0; --b) hm = fmaxf(hm, __shfl_xor_sync(0xffffffffu, hm, 1 << (KB + b)));
+#pragma unroll
+          for (int g = 0; g < G; ++g) {
+            const float nmax = fmaxf(mx[g], __shfl_sync(0xffffffffu, hm, g << (KB + LOGK)));
+            const float corr = mx[g] == -INFINITY ? 0.0f : __expf(__fsub_rn(mx[g], nmax));
+            mx[g] = nmax;
+            sum[g] = __fmul_rn(sum[g], corr);
+            o[g].x = __fmul_rn(o[g].x, corr);
+            o[g].y = __fmul_rn(o[g].y, corr);
+            o[g].z = __fmul_rn(o[g].z, corr);
+            o[g].w = __fmul_rn(o[g].w, corr);
+            if (my_g == g) mine = nmax;
+          }
         }
         const float pj = live ? __expf(__fsub_rn(sc, mine)) : 0.0f;
-        float ps = pj;
+        // per-lane exp-sums (one lane per (head, key)), reduced after the loop
 #pragma unroll
-        for (int b = LOGK - 1; b >= 0; --b) ps = __fadd_rn(ps, __shfl_xor_sync(0xffffffffu, ps, 1 << (KB + b)));
-        if (writer) sp[warp][my_g][my_key] = pj;
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-          sum[g] = __fadd_rn(__fmul_rn(sum[g], corr[g]), __shfl_sync(0xffffffffu, ps, g << (KB + LOGK)));
-          mx[g] = nmax[g];
-          o[g].x = __fmul_rn(o[g].x, corr[g]);
-          o[g].y = __fmul_rn(o[g].y, corr[g]);
-          o[g].z = __fmul_rn(o[g].z, corr[g]);
-          o[g].w = __fmul_rn(o[g].w, corr[g]);
-        }
-        __syncwarp();
+        for (int g = 0; g < G; ++g) sum[g] = __fadd_rn(sum[g], (writer && my_g == g) ? pj : 0.0f);
+        // o += p_j * V_j with p_j broadcast from the lane that holds it
 #pragma unroll
         for (int j = 0; j < KPW; ++j) {
-          if (j < nk) {
-            const float4 vv = *reinterpret_cast<const float4 *>(vt + (size_t)j * 128 + 4 * lane);
 #pragma unroll
-            for (int g = 0; g < G; ++g) {
-              const float w = sp[warp][g][j];
-              o[g].x = fmaf(w, vv.x, o[g].x);
-              o[g].y = fmaf(w, vv.y, o[g].y);
-              o[g].z = fmaf(w, vv.z, o[g].z);
-              o[g].w = fmaf(w, vv.w, o[g].w);
-            }
+          for (int g = 0; g < G; ++g) {
+            const float w = __shfl_sync(0xffffffffu, pj, (g * KPW + j) << KB);
+            o[g].x = fmaf(w, vr[j].x, o[g].x);
+            o[g].y = fmaf(w, vr[j].y, o[g].y);
+            o[g].z = fmaf(w, vr[j].z, o[g].z);
+            o[g].w = fmaf(w, vr[j].w, o[g].w);
           }
         }
       }
-      __syncwarp();  // every lane is done with stage st and with sp
+      __syncwarp();  // every lane is done with stage st
       if (lane == 0 && !failed && next_issue < T) {
         fence_proxy_async();
         issue(next_issue++);
       }
       issued = __shfl_sync(0xffffffffu, issued, 0);
     }
+#pragma unroll
+    for (int g = 0; g < G; ++g) sum[g] = warp_sum(sum[g]);  // the per-lane exp-sums
     // park this warp's state (an empty range leaves max = -inf, sum = 0)
     float *sl = slots + (size_t)warp * G * kAttnPartStride;
 #pragma unroll
