@@ -194,7 +194,10 @@ __global__ void kv_append_kernel(float *__restrict__ k_cache, float *__restrict_
 // write x_norm and the normalised, rotated q and k heads (4 elements and
 // their RoPE partners per thread).  Every rounding step is the reference's,
 // so all outputs are bit-exact.
-constexpr int kPreThreads = 256;
+#ifndef QASR_PRE_THREADS
+#define QASR_PRE_THREADS 128
+#endif
+constexpr int kPreThreads = QASR_PRE_THREADS;  // threads per row of the configuration-1 block
 constexpr int kHeadPad = 129;
 
 // 16-byte global -> shared copy that completes asynchronously (waited for with
@@ -244,14 +247,17 @@ pre_attn_block_kernel(float *__restrict__ x_norm, const float *__restrict__ x, c
   const float4 *k4 = reinterpret_cast<const float4 *>(k + (size_t)s * kv_dim);
   const float4 *v4 = reinterpret_cast<const float4 *>(v + (size_t)s * kv_dim);
   // float4 per thread: x (hidden <= 2048), q|k (<= 3072 floats), v (<= 1024)
-  constexpr int kVx = 2, kVqk = 3;
-  float4 rx[kVx], rqk[kVqk], rv;
+  constexpr int kVx = (512 + kPreThreads - 1) / kPreThreads, kVqk = (768 + kPreThreads - 1) / kPreThreads,
+                kVv = (256 + kPreThreads - 1) / kPreThreads;
+  float4 rx[kVx], rqk[kVqk], rv[kVv];
 #pragma unroll
   for (int j = 0; j < kVx; ++j) {
     const int i = tid + j * kPreThreads;
     if (i < hidden / 4) rx[j] = x4[i];
   }
-  if (tid < kv_dim / 4) rv = v4[tid];
+#pragma unroll
+  for (int j = 0; j < kVv; ++j)
+    if (tid + j * kPreThreads < kv_dim / 4) rv[j] = v4[tid + j * kPreThreads];
 #pragma unroll
   for (int j = 0; j < kVqk; ++j) {
     const int i = tid + j * kPreThreads;
@@ -263,7 +269,9 @@ pre_attn_block_kernel(float *__restrict__ x_norm, const float *__restrict__ x, c
     const int i = tid + j * kPreThreads;
     if (i < hidden / 4) reinterpret_cast<float4 *>(xs)[i] = rx[j];
   }
-  if (tid < kv_dim / 4) vc4[tid] = rv;
+#pragma unroll
+  for (int j = 0; j < kVv; ++j)
+    if (tid + j * kPreThreads < kv_dim / 4) vc4[tid + j * kPreThreads] = rv[j];
 #pragma unroll
   for (int j = 0; j < kVqk; ++j) {
     const int i = tid + j * kPreThreads;
