@@ -299,6 +299,24 @@ static int conv_gemm(qasr_encoder *e, int i, float *y, const float *cols, int ro
   return f32_gemm_fallback(y, cols, e->conv_w[i], e->conv_b[i], rows, CH * 9, CH, st);
 }
 
+// conv2 / conv3 (3x3, stride 2, padding 1, CH -> CH channels) of the
+// channel-last activation act [B, h_in, w_in, CH] into y [B*h_out*w_out, CH]:
+// an implicit GEMM (patch digits straight from act) when the weights have
+// their digit planes, else patches into e->cols and the CUDA-core GEMM.
+static int conv_stage(qasr_encoder *e, int i, float *y, const float *act, int h_in, int w_in, int B, int h_out,
+                      int w_out, cudaStream_t st) {
+  const int CH = kConvHidden;
+  const long rows = (long)B * h_out * w_out;
+  if (e->conv_pw[i].planes) {
+    const int rc = f32_gemm_prepared_conv(y, CH, act, CH, h_in, w_in, B, h_out, w_out, e->conv_pw[i], e->conv_b[i],
+                                          st);
+    if (rc != QASR_ERR_UNSUPPORTED) return rc;
+  }
+  im2col_cl_kernel<<<grid_of(rows * CH * 9 / 4), 256, 0, st>>>(e->cols, act, CH, h_in, w_in, B, h_out, w_out);
+  if (int rc = launch_status("qasr_encoder_forward: conv patches")) return rc;
+  return conv_gemm(e, i, y, e->cols, (int)rows, st);
+}
+
 // conv2 / conv3 after their weights change: the weights into the
 // channel-fastest patch order, then their digit planes
 static int prepare_convs(qasr_encoder *e) {
@@ -699,17 +717,9 @@ static int encoder_run(qasr_encoder *e, int n, const float *const *mels, const i
       conv1_gelu_kernel<<<(int)std::min<long>((r1 + 7) / 8, 148l * 8), 256, 0, st>>>(
           e->act_a, mel, mel_frames, first, cs, cw, B, h1, w1, e->conv_w[0], e->conv_b[0]);
       rc = launch_status("qasr_encoder_forward: conv1");
-      if (!rc) {
-        im2col_cl_kernel<<<grid_of(r2 * CH * 9 / 4), 256, 0, st>>>(e->cols, e->act_a, CH, h1, w1, B, h2, w2);
-        rc = launch_status("qasr_encoder_forward: conv2 patches");
-      }
-      if (!rc) rc = conv_gemm(e, 1, e->act_b, e->cols, (int)r2, st);
+      if (!rc) rc = conv_stage(e, 1, e->act_b, e->act_a, h1, w1, B, h2, w2, st);
       if (!rc) rc = qasr_gelu(e->act_b, (int64_t)r2 * CH, st);
-      if (!rc) {
-        im2col_cl_kernel<<<grid_of(r3 * CH * 9 / 4), 256, 0, st>>>(e->cols, e->act_b, CH, h2, w2, B, h3, w3);
-        rc = launch_status("qasr_encoder_forward: conv3 patches");
-      }
-      if (!rc) rc = conv_gemm(e, 2, e->act_a, e->cols, (int)r3, st);
+      if (!rc) rc = conv_stage(e, 2, e->act_a, e->act_b, h2, w2, B, h3, w3, st);
       if (!rc) rc = qasr_gelu(e->act_a, (int64_t)r3 * CH, st);
       if (!rc) {
         conv_reshape_cl_kernel<<<grid_of(r3 * CH), 256, 0, st>>>(e->cols, e->act_a, CH, h3, w3, B);

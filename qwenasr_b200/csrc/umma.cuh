@@ -68,6 +68,11 @@ int f32_weight_prepare(F32Weight *pw, const float *w, int N, int K, cudaStream_t
 void f32_weight_free(F32Weight *pw);
 int f32_gemm_prepared(float *y, long y_stride, const float *x, long x_stride, const F32Weight &w, const float *bias,
                       int T, cudaStream_t st);
+// A 3x3 / stride 2 / padding 1 convolution of a channel-last activation
+// [B, h_in, w_in, C] as an implicit GEMM over w (channel-fastest patch order,
+// K = 9*C): no im2col matrix is written.  QASR_ERR_UNSUPPORTED as above.
+int f32_gemm_prepared_conv(float *y, long y_stride, const float *act, int C, int h_in, int w_in, int B, int h_out,
+                           int w_out, const F32Weight &w, const float *bias, cudaStream_t st);
 int f32_gemm_prepared_split3(float *y0, long s0, float *y1, long s1, int n1, float *y2, long s2, int n2,
                              const float *x, long x_stride, const F32Weight &w, const float *bias, int T,
                              cudaStream_t st);

@@ -69,6 +69,84 @@ struct GTile {
 constexpr int kGemmStore = 0, kGemmResidual = 1, kGemmSwiGLU = 2;
 
 // ---------------------------------------------------------------- digits --
+// Four values of a row -> their balanced base-256 digits (X = rint(v*qm),
+// |X| <= 2^22, X = 65536*d0 + 256*d1 + d2), written as bytes k..k+3 of the
+// three digit rows at row0, row0 + dstep, row0 + 2*dstep.
+QASR_DEV void put_digits4(int8_t *row0, size_t dstep, int k, float4 v, float qm) {
+  // X = rint(v*qm) via the 1.5*2^23 magic constant; balanced base-256 digits
+  int X[4] = {__float_as_int(fmaf(v.x, qm, 12582912.0f)) - 0x4B400000,
+              __float_as_int(fmaf(v.y, qm, 12582912.0f)) - 0x4B400000,
+              __float_as_int(fmaf(v.z, qm, 12582912.0f)) - 0x4B400000,
+              __float_as_int(fmaf(v.w, qm, 12582912.0f)) - 0x4B400000};
+  uint32_t w[3];
+  w[2] = __byte_perm(__byte_perm(X[0], X[1], 0x0040), __byte_perm(X[2], X[3], 0x0040), 0x5410);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) X[q] = (X[q] + 128) >> 8;
+  w[1] = __byte_perm(__byte_perm(X[0], X[1], 0x0040), __byte_perm(X[2], X[3], 0x0040), 0x5410);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) X[q] = (X[q] + 128) >> 8;
+  w[0] = __byte_perm(__byte_perm(X[0], X[1], 0x0040), __byte_perm(X[2], X[3], 0x0040), 0x5410);
+#pragma unroll
+  for (int d = 0; d < 3; ++d) *reinterpret_cast<uint32_t *>(row0 + d * dstep + k) = w[d];
+}
+
+// Exponent of a row from its largest magnitude: returns the scale qm that
+// maps the row to |X| <= 2^22 and writes the row's factor 2^(e-22).
+QASR_DEV float row_exponent(float mx, float *dq_slot, bool write) {
+  int e = 0;
+  if (mx > 0.0f && mx <= 3.0e38f) frexpf(mx, &e);  // mx < 2^e
+  e = max(-100, min(e, 127));
+  if (write) *dq_slot = __int_as_float((127 + e - 22) << 23);
+  return __int_as_float((127 + 22 - e) << 23);
+}
+
+// The digit rows of a 3x3, stride-2, padding-1 convolution's patch matrix,
+// read straight from the channel-last activation act [B, h_in, w_in, C]:
+// row r = (b, oh, ow), column (ki*3 + kj)*C + ic = act[b, 2oh+ki-1, 2ow+kj-1,
+// ic] (0 outside) -- the channel-fastest order the conv weights are permuted
+// to.  The GEMM then reads the patches without a materialised im2col matrix;
+// the digits equal digit_rows_kernel's on that matrix.  One warp per row.
+__global__ void __launch_bounds__(256) conv_digit_rows_kernel(int8_t *__restrict__ D, float *__restrict__ dq,
+                                                              const float *__restrict__ act, int C, int h_in,
+                                                              int w_in, int h_out, int w_out, int rows, int rows_pad,
+                                                              int B) {
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (t >= rows_pad) return;
+  const int K = 9 * C, C4 = C / 4;
+  int8_t *row0 = D + ((size_t)(t / B) * 3 * B + t % B) * K;  // digit d at row0 + d*B*K
+  const size_t dstep = (size_t)B * K;
+  if (t >= rows) {  // rows past the end of the last block: zero digits
+    for (int k = 4 * lane; k < K; k += 128)
+      for (int d = 0; d < 3; ++d) *reinterpret_cast<uint32_t *>(row0 + d * dstep + k) = 0u;
+    if (lane == 0) dq[t] = 0.0f;
+    return;
+  }
+  // 32-bit index math: the engine's stem passes keep B * h_in * w_in * C below 2^31
+  const int ow = t % w_out, bt = t / w_out, oh = bt % h_out, b = bt / h_out;
+  const float4 *src = reinterpret_cast<const float4 *>(act);
+  auto tap = [&](int kk) -> const float4 * {  // the tap's C channels, or null in the padding
+    const int ih = 2 * oh + kk / 3 - 1, iw = 2 * ow + kk % 3 - 1;
+    return (ih >= 0 && ih < h_in && iw >= 0 && iw < w_in) ? src + ((b * h_in + ih) * w_in + iw) * C4 : nullptr;
+  };
+  float mx = 0.0f;
+  for (int kk = 0; kk < 9; ++kk) {
+    const float4 *tp = tap(kk);
+    if (!tp) continue;
+    for (int c4 = lane; c4 < C4; c4 += 32) {
+      const float4 v = tp[c4];
+      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    }
+  }
+  mx = warp_max(mx);
+  const float qm = row_exponent(mx, dq + t, lane == 0);
+  for (int kk = 0; kk < 9; ++kk) {
+    const float4 *tp = tap(kk);
+    for (int c4 = lane; c4 < C4; c4 += 32)
+      put_digits4(row0, dstep, kk * C + 4 * c4, tp ? tp[c4] : make_float4(0.f, 0.f, 0.f, 0.f), qm);
+  }
+}
+
 __global__ void __launch_bounds__(256) digit_rows_kernel(int8_t *__restrict__ D, float *__restrict__ dq,
                                                          const float *__restrict__ x, long x_stride, int rows, int K,
                                                          int rows_pad, int B) {
@@ -90,29 +168,8 @@ __global__ void __launch_bounds__(256) digit_rows_kernel(int8_t *__restrict__ D,
     mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
   }
   mx = warp_max(mx);
-  int e = 0;
-  if (mx > 0.0f && mx <= 3.0e38f) frexpf(mx, &e);  // mx < 2^e
-  e = max(-100, min(e, 127));
-  const float qm = __int_as_float((127 + 22 - e) << 23);
-  if (lane == 0) dq[t] = __int_as_float((127 + e - 22) << 23);
-  for (int k4 = lane; k4 < K / 4; k4 += 32) {
-    const float4 v = xr[k4];  // L1 hit: read just above
-    // X = rint(v*qm) via the 1.5*2^23 magic constant; balanced base-256 digits
-    int X[4] = {__float_as_int(fmaf(v.x, qm, 12582912.0f)) - 0x4B400000,
-                __float_as_int(fmaf(v.y, qm, 12582912.0f)) - 0x4B400000,
-                __float_as_int(fmaf(v.z, qm, 12582912.0f)) - 0x4B400000,
-                __float_as_int(fmaf(v.w, qm, 12582912.0f)) - 0x4B400000};
-    uint32_t w[3];
-    w[2] = __byte_perm(__byte_perm(X[0], X[1], 0x0040), __byte_perm(X[2], X[3], 0x0040), 0x5410);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) X[q] = (X[q] + 128) >> 8;
-    w[1] = __byte_perm(__byte_perm(X[0], X[1], 0x0040), __byte_perm(X[2], X[3], 0x0040), 0x5410);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) X[q] = (X[q] + 128) >> 8;
-    w[0] = __byte_perm(__byte_perm(X[0], X[1], 0x0040), __byte_perm(X[2], X[3], 0x0040), 0x5410);
-#pragma unroll
-    for (int d = 0; d < 3; ++d) *reinterpret_cast<uint32_t *>(row0 + d * dstep + 4 * k4) = w[d];
-  }
+  const float qm = row_exponent(mx, dq + t, lane == 0);
+  for (int k4 = lane; k4 < K / 4; k4 += 32) put_digits4(row0, dstep, 4 * k4, xr[k4], qm);  // L1 hit: read above
 }
 
 // ------------------------------------------------------------------ GEMM --
@@ -550,6 +607,39 @@ int f32_gemm_prepared(float *y, long y_stride, const float *x, long x_stride, co
   p.N = w.N;
   if ((rc = digit_rows(static_cast<int8_t *>(dbuf), static_cast<float *>(qbuf), x, x_stride, T, T_pad, K, kGTok, st)))
     return rc;
+  return gemm_launch<3, kGTok>(p, st);
+}
+
+// A 3x3, stride-2, padding-1 convolution of the channel-last activation act
+// [B, h_in, w_in, C] as an implicit GEMM: the digit rows of its patches come
+// straight from act (conv_digit_rows_kernel), y [B*h_out*w_out, w.N] = patches
+// x w^T (+ bias), with w the weights in the channel-fastest patch order.
+int f32_gemm_prepared_conv(float *y, long y_stride, const float *act, int C, int h_in, int w_in, int B, int h_out,
+                           int w_out, const F32Weight &w, const float *bias, cudaStream_t st) {
+  const long T = (long)B * h_out * w_out;
+  if (!w.planes || C % 4 || w.K != 9 * C || T <= 0 || T >= (1l << 30) || (long)B * h_in * w_in * C >= (1l << 31) ||
+      (reinterpret_cast<uintptr_t>(act) & 15) || !gemm_shape_ok(act, w.K, (int)T, w.K, w.N))
+    return QASR_ERR_UNSUPPORTED;
+  const int K = w.K, NB = (int)((T + kGTok - 1) / kGTok), T_pad = NB * kGTok;
+  void *dbuf = nullptr, *qbuf = nullptr;
+  int rc;
+  if ((rc = dev_scratch(kScratchDigits, (size_t)NB * kGRows * K, &dbuf))) return rc;
+  if ((rc = dev_scratch(kScratchDigitScale, (size_t)T_pad * 4, &qbuf))) return rc;
+  GemmParams p{};
+  p.tm_w = w.tm;
+  if ((rc = int8_map(&p.tm_d, static_cast<int8_t *>(dbuf), (long)NB * kGRows, K, kGRows))) return rc;
+  p.dq = static_cast<float *>(qbuf);
+  p.scales = w.factors;
+  p.bias = bias;
+  p.y = y;
+  p.y_stride = y_stride;
+  p.T = (int)T;
+  p.K = K;
+  p.N = w.N;
+  conv_digit_rows_kernel<<<(T_pad + 7) / 8, 256, 0, st>>>(static_cast<int8_t *>(dbuf), static_cast<float *>(qbuf), act,
+                                                          C, h_in, w_in, h_out,
+                                                          w_out, (int)T, T_pad, kGTok);
+  if ((rc = launch_status("tensor-core GEMM: conv digit rows"))) return rc;
   return gemm_launch<3, kGTok>(p, st);
 }
 
