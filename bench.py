@@ -154,8 +154,8 @@ class ClockSampler:
 # kernel class from one ncu capture of the 0.6B, M=8, KV-1024 step; see
 # profiles/attn_decode_0p6b_m8_kv1024.md and
 # profiles/int8_contraction_tcgen05_decode_0p6b_m8.md for the commands.
-NCU_TRAFFIC_M8 = {"attn": 67643904 + 1371392, "qkv": 4309504, "oproj": 2244608, "gateup": 6413824,
-                  "down": 3325952, "lmhead": 156296448 + 4083456}
+NCU_TRAFFIC_M8 = {"attn": 67960832 + 1236736, "qkv": 4317440, "oproj": 2247168, "gateup": 6412544,
+                  "down": 3328512, "lmhead": 156295680 + 5308928}
 
 
 def class_bytes(cfg, M, kv_len):
